@@ -1,0 +1,186 @@
+/*
+ * kino.h - C ABI of libkino_b200.so, the sm_100a (B200) kernels behind the denoise-step path of
+ * KinoMLX (the Flux2-style MMDiT, the LTX-2 video DiT block and the tiled conv VAE decoder).
+ *
+ * Conventions
+ *   - All tensors are caller-owned device pointers; nothing here allocates device memory.
+ *   - bf16 activations and weights, fp32 rope tables; "ld" is a row stride and "bs" a batch
+ *     stride, both in elements. Row strides of TMA-read operands must be multiples of 8.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is asynchronous.
+ *   - Every entry point returns a kino_status. KINO_ENOTSUPPORTED mirrors the reference's
+ *     `applies()` refusals; there is no fallback path, so callers treat it as an error.
+ *     kino_last_error() gives a one-line reason for the last failure on this thread.
+ *
+ * Each entry point names the reference interface (path:line inside the KinoMLX project) that it
+ * replaces.
+ */
+#ifndef KINO_H
+#define KINO_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int kino_status;
+#define KINO_OK 0
+#define KINO_EINVAL 1
+#define KINO_ENOTSUPPORTED 2
+#define KINO_ECUDA 3
+#define KINO_ETIMEOUT 4
+
+/* ABI version of this header; bumped on any signature change. */
+int kino_abi_version(void);
+
+/* One-line description of the last error on the calling thread ("" if none). */
+const char* kino_last_error(void);
+
+/* Synchronises `stream`, then reads and clears the device-side error word that bounded waits in
+ * the kernels set (KINO_ETIMEOUT if a wait gave up). Host-side counterpart of the reference's
+ * per-step finiteness/status checks (kinomlx/models/flux2/sampling.py:241-244). */
+kino_status kino_device_status(void* stream);
+
+/* Number of SMs of the current device (the persistent kernels size their grids by it). */
+int kino_num_sms(void);
+
+/* ------------------------------------------------------------------ linear (GEMM) */
+#define KINO_EPI_NONE 0           /* out = bf16(acc + bias) */
+#define KINO_EPI_GELU 1           /* out = gelu_tanh(bf16(acc + bias)) for columns >= act_col_begin */
+#define KINO_EPI_GATED_RESIDUAL 2 /* out = residual + bf16(gate[b] * bf16(acc + bias)) */
+#define KINO_EPI_EULER 3          /* out = aux + bf16(bf16(scalar) * bf16(acc + bias)), fp32 add */
+#define KINO_EPI_SIGMOID2 4       /* out = 2 * sigmoid(bf16(acc + bias)) */
+
+typedef struct kino_epilogue {
+  int kind;                /* KINO_EPI_* */
+  const void* bias;        /* [n] bf16 or NULL */
+  const void* residual;    /* GATED_RESIDUAL: bf16, may alias out */
+  int64_t ld_residual;
+  int64_t bs_residual;
+  const void* gate;        /* GATED_RESIDUAL: [batch][n] bf16 at batch stride bs_gate */
+  int64_t bs_gate;
+  int64_t act_col_begin;   /* GELU: first column the activation applies to */
+  float scalar;            /* EULER: dt = sigma_next - sigma (fp32) */
+  const void* aux;         /* EULER: current sample, bf16, geometry of out */
+  int64_t ld_aux;
+  int64_t bs_aux;
+} kino_epilogue;
+
+/* out[b, i, j] = epilogue(sum_k x[b, i, k] * w[j, k]) on tcgen05 tensor cores.
+ * x: batch x m x k (row stride ldx, batch stride bsx); w: n x k, row stride ldw ((out, in) layout);
+ * out: batch x m x n (ldo, bso). Requires k % 8 == 0, n % 8 == 0, strides % 8 == 0.
+ * Replaces kinomlx.kernels.mpp_linear.linear (kinomlx/kernels/mpp_linear.py:469-506) and the
+ * MLX addmm/matmul projections of kinomlx/modeling/layers.py:8-31 and
+ * kinomlx/models/ltx2/transformer/attention.py:41-51. `epi` may be NULL (plain product). */
+kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, int64_t m,
+                        int64_t n, int64_t k, int64_t ldx, int64_t bsx, int64_t ldw, int64_t ldo,
+                        int64_t bso, const kino_epilogue* epi, void* stream);
+
+/* Small-batch product (batch <= 4 rows): y[b, j] = sum_k act(x[b, k]) * w[j, k] + bias[j],
+ * act = identity (0) or SiLU (1). Replaces the M=1 modulation/timestep projections
+ * (kinomlx/models/flux2/transformer.py:223-258, kinomlx/models/ltx2/transformer/timestep.py:31-85). */
+kino_status kino_gemv(const void* x, int64_t ldx, const void* w, const void* bias, void* y,
+                      int64_t ldy, int64_t batch, int64_t n, int64_t k, int act, void* stream);
+
+/* ------------------------------------------------------------------ attention */
+typedef struct kino_attention_args {
+  int64_t batch;
+  int64_t heads;
+  int64_t head_dim;        /* 128 */
+  float scale;             /* softmax scale, head_dim^-0.5 in the reference */
+  int n_q;                 /* 1 or 2 query segments (logically concatenated) */
+  const void* q[2];
+  void* out[2];            /* output of segment s, token-major, may alias q[s] */
+  int64_t q_tokens[2];
+  int64_t ld_q[2], bs_q[2], ld_out[2], bs_out[2];
+  int n_kv;                /* 1 or 2 key/value segments */
+  const void* k[2];
+  const void* v[2];
+  int64_t kv_tokens[2];
+  int64_t ld_k[2], bs_k[2], ld_v[2], bs_v[2];
+} kino_attention_args;
+
+/* softmax(q k^T * scale) v over all key segments, per head, token-major operands.
+ * Replaces MLX SDPA in the joint attention (kinomlx/models/flux2/kv.py:48-54,
+ * kinomlx/models/flux2/transformer.py:35-53) and unmasked LTX attention
+ * (kinomlx/models/ltx2/transformer/attention.py:144-161). */
+kino_status kino_attention(const kino_attention_args* args, void* stream);
+
+/* The reference dense kernel's contract: q (tq, heads*dim), k and v (tk, heads*dim), out like q.
+ * Replaces kinomlx.models.ltx2.kernels.dense_attention.dense_attention
+ * (kinomlx/models/ltx2/kernels/dense_attention.py:107-151); dim must be 128 here. */
+kino_status kino_dense_attention(const void* q, const void* k, const void* v, void* out,
+                                 int64_t tq, int64_t tk, int64_t heads, int64_t dim, void* stream);
+
+/* ------------------------------------------------------------------ norms and rotary */
+#define KINO_NORM_RMS 0
+#define KINO_NORM_LAYER 1
+
+/* out = norm(x) * (1 + scale[b]) + shift[b], norm without affine, fp32 statistics.
+ * x: batch x rows x dim (ldx, bsx); shift/scale: [batch][dim] at batch stride bs_mod.
+ * Replaces kinomlx/models/flux2/transformer.py:56-60 (`normalized`, LayerNorm) and
+ * kinomlx/models/ltx2/transformer/transformer.py:16-23 (`_adaln`, RMSNorm). dim <= 8192. */
+kino_status kino_adaln(const void* x, int64_t ldx, int64_t bsx, const void* shift,
+                       const void* scale, int64_t bs_mod, void* out, int64_t ldo, int64_t bso,
+                       int64_t batch, int64_t rows, int64_t dim, int norm_kind, float eps,
+                       void* stream);
+
+/* RMSNorm over the last dimension; weight may be NULL (unweighted).
+ * Replaces kinomlx.kernels.rms_norm (kinomlx/kernels/fused_ops.py:412-457). dim <= 8192. */
+kino_status kino_rms_norm(const void* x, const void* weight, void* out, int64_t rows, int64_t dim,
+                          float eps, float weight_offset, void* stream);
+
+#define KINO_QKNORM_NONE 0
+#define KINO_QKNORM_PER_HEAD 1
+#define KINO_QKNORM_FULL_ROW 2
+#define KINO_ROPE_NONE 0
+#define KINO_ROPE_PAIRS 1   /* adjacent pairs, tables [table_batch][table_tokens][128] */
+#define KINO_ROPE_SPLIT 2   /* split halves, tables [table_batch][heads][table_tokens][64] */
+
+/* In place on token-major q or k (batch x tokens x heads*128, ld, bs): RMSNorm (per head or over
+ * the whole row) with weight, rounded to bf16, then RoPE from fp32 tables. Token t reads table
+ * row table_offset + t. Replaces QKNorm + rotate (kinomlx/models/flux2/transformer.py:17-32,
+ * 68-75) and q_norm/k_norm + apply_rotary_emb
+ * (kinomlx/models/ltx2/transformer/attention.py:330-342). */
+kino_status kino_qk_norm_rope(void* x, int64_t ld, int64_t bs, int64_t batch, int64_t tokens,
+                              int64_t heads, const void* weight, int norm_kind, int rope_kind,
+                              const float* cos_table, const float* sin_table, int table_batched,
+                              int64_t table_tokens, int64_t table_offset, float eps, void* stream);
+
+/* value (batch, tokens, heads*2*half) bf16, tables (table_batch, heads, tokens, half) fp32.
+ * Replaces kinomlx.kernels.split_rope.rotate (kinomlx/kernels/split_rope.py:159-163) with the
+ * same rounding (bit-identical to the reference graph). */
+kino_status kino_split_rope(const void* x, const float* cos_table, const float* sin_table,
+                            void* out, int64_t batch, int64_t tokens, int64_t heads, int64_t half,
+                            int table_batched, void* stream);
+
+/* ------------------------------------------------------------------ elementwise and sampler */
+/* tanh-GELU / SiLU with fp32 opmath (kinomlx/kernels/fused_ops.py:327-372). n % 8 == 0. */
+kino_status kino_gelu_tanh(const void* x, void* out, int64_t n, void* stream);
+kino_status kino_silu(const void* x, void* out, int64_t n, void* stream);
+
+/* out = uncond + guidance * (cond - uncond) in bf16 (kinomlx/models/flux2/sampling.py:264-280). */
+kino_status kino_cfg_combine(const void* cond, const void* uncond, float guidance, void* out,
+                             int64_t n, void* stream);
+
+/* Klein Euler: out = bf16(f32(x) + f32(bf16(bf16(dt) * v))) (kinomlx/models/flux2/sampling.py:109-113). */
+kino_status kino_euler_velocity(const void* x, const void* v, float dt, void* out, int64_t n,
+                                void* stream);
+
+/* LTX X0 + Euler: x0 = bf16(x - sigma * v) (fp32), out = bf16(x0 + ratio * (x - x0)) (fp32),
+ * ratio = fp32(sigma_next / sigma) (kinomlx/models/ltx2/transformer/wrappers.py:49-65,
+ * kinomlx/samplers/steps.py:36-70). */
+kino_status kino_euler_x0(const void* x, const void* v, float sigma, float ratio, void* out,
+                          int64_t n, void* stream);
+
+/* [cos(t f_i), sin(t f_i)] features, f_i = exp(-ln(10000) i / (dim/2)); t: fp32 device [batch].
+ * Replaces kinomlx/models/flux2/transformer.py:238-241 and
+ * kinomlx/models/ltx2/transformer/timestep.py:13-28. */
+kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, int64_t dim,
+                                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KINO_H */

@@ -1,0 +1,152 @@
+"""ctypes binding of libkino_b200.so (the C ABI in include/kino.h).
+
+The library is loaded from this package directory. There is no fallback: if it is missing or a
+call returns a non-OK status, a RuntimeError names the reason from kino_last_error().
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_float, c_int, c_int64, c_void_p
+from pathlib import Path
+
+LIBRARY_PATH = Path(__file__).with_name("libkino_b200.so")
+
+KINO_OK = 0
+KINO_EINVAL = 1
+KINO_ENOTSUPPORTED = 2
+KINO_ECUDA = 3
+KINO_ETIMEOUT = 4
+
+STATUS_NAMES = {
+    KINO_OK: "KINO_OK",
+    KINO_EINVAL: "KINO_EINVAL",
+    KINO_ENOTSUPPORTED: "KINO_ENOTSUPPORTED",
+    KINO_ECUDA: "KINO_ECUDA",
+    KINO_ETIMEOUT: "KINO_ETIMEOUT",
+}
+
+EPI_NONE = 0
+EPI_GELU = 1
+EPI_GATED_RESIDUAL = 2
+EPI_EULER = 3
+EPI_SIGMOID2 = 4
+
+NORM_RMS = 0
+NORM_LAYER = 1
+
+QKNORM_NONE = 0
+QKNORM_PER_HEAD = 1
+QKNORM_FULL_ROW = 2
+ROPE_NONE = 0
+ROPE_PAIRS = 1
+ROPE_SPLIT = 2
+
+
+class Epilogue(ctypes.Structure):
+    _fields_ = [
+        ("kind", c_int),
+        ("bias", c_void_p),
+        ("residual", c_void_p),
+        ("ld_residual", c_int64),
+        ("bs_residual", c_int64),
+        ("gate", c_void_p),
+        ("bs_gate", c_int64),
+        ("act_col_begin", c_int64),
+        ("scalar", c_float),
+        ("aux", c_void_p),
+        ("ld_aux", c_int64),
+        ("bs_aux", c_int64),
+    ]
+
+
+class AttentionArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int64),
+        ("heads", c_int64),
+        ("head_dim", c_int64),
+        ("scale", c_float),
+        ("n_q", c_int),
+        ("q", c_void_p * 2),
+        ("out", c_void_p * 2),
+        ("q_tokens", c_int64 * 2),
+        ("ld_q", c_int64 * 2),
+        ("bs_q", c_int64 * 2),
+        ("ld_out", c_int64 * 2),
+        ("bs_out", c_int64 * 2),
+        ("n_kv", c_int),
+        ("k", c_void_p * 2),
+        ("v", c_void_p * 2),
+        ("kv_tokens", c_int64 * 2),
+        ("ld_k", c_int64 * 2),
+        ("bs_k", c_int64 * 2),
+        ("ld_v", c_int64 * 2),
+        ("bs_v", c_int64 * 2),
+    ]
+
+
+I64 = c_int64
+P = c_void_p
+F = c_float
+
+# Every exported entry point with its argument types, in include/kino.h order.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "kino_abi_version": (c_int, []),
+    "kino_last_error": (ctypes.c_char_p, []),
+    "kino_device_status": (c_int, [P]),
+    "kino_num_sms": (c_int, []),
+    "kino_linear": (
+        c_int,
+        [P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, POINTER(Epilogue), P],
+    ),
+    "kino_gemv": (c_int, [P, I64, P, P, P, I64, I64, I64, I64, c_int, P]),
+    "kino_attention": (c_int, [POINTER(AttentionArgs), P]),
+    "kino_dense_attention": (c_int, [P, P, P, P, I64, I64, I64, I64, P]),
+    "kino_adaln": (c_int, [P, I64, I64, P, P, I64, P, I64, I64, I64, I64, I64, c_int, F, P]),
+    "kino_rms_norm": (c_int, [P, P, P, I64, I64, F, F, P]),
+    "kino_qk_norm_rope": (
+        c_int,
+        [P, I64, I64, I64, I64, I64, P, c_int, c_int, P, P, c_int, I64, I64, F, P],
+    ),
+    "kino_split_rope": (c_int, [P, P, P, P, I64, I64, I64, I64, c_int, P]),
+    "kino_gelu_tanh": (c_int, [P, P, I64, P]),
+    "kino_silu": (c_int, [P, P, I64, P]),
+    "kino_cfg_combine": (c_int, [P, P, F, P, I64, P]),
+    "kino_euler_velocity": (c_int, [P, P, F, P, I64, P]),
+    "kino_euler_x0": (c_int, [P, P, F, F, P, I64, P]),
+    "kino_timestep_embedding": (c_int, [P, P, I64, I64, P]),
+}
+
+_LIB: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once and declare every signature; raise if it is not built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIBRARY_PATH.exists():
+        raise RuntimeError(
+            f"{LIBRARY_PATH.name} is not built; run `python -m kinomlx_b200.build` "
+            "(the sm_100a kernels have no fallback)"
+        )
+    lib = ctypes.CDLL(str(LIBRARY_PATH))
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _LIB = lib
+    return lib
+
+
+def last_error() -> str:
+    raw = load().kino_last_error()
+    return raw.decode() if raw else ""
+
+
+def call(name: str, *args: object) -> None:
+    """Call one kino_* entry point and raise RuntimeError on a non-OK status."""
+    status = getattr(load(), name)(*args)
+    if status != KINO_OK:
+        label = STATUS_NAMES.get(status, str(status))
+        raise RuntimeError(f"{name} failed with {label}: {last_error()}")

@@ -1,0 +1,463 @@
+// Host side of libkino_b200.so: argument checks, TMA descriptor encoding and launches for the
+// extern "C" entry points declared in include/kino.h. One translation unit holds every kernel so
+// the device error word is a single symbol without relocatable device code.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/kino.h"
+#include "kino_attention.cuh"
+#include "kino_common.cuh"
+#include "kino_gemm.cuh"
+#include "kino_ops.cuh"
+
+namespace {
+
+thread_local char g_err[512] = {0};
+
+kino_status fail(kino_status code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+kino_status check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(KINO_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  return KINO_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------- driver entry point for TMA
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map, dims innermost first, strides in elements for dims 1.., box sizes.
+kino_status make_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                     const uint64_t* strides_elems, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(KINO_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if (!aligned16(base)) return fail(KINO_EINVAL, "TMA base address not 16-byte aligned");
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5];
+  cuuint32_t e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    s[i] = strides_elems[i] * 2;
+    if (s[i] % 16 != 0) return fail(KINO_EINVAL, "TMA stride %llu bytes not a multiple of 16",
+                                    static_cast<unsigned long long>(s[i]));
+  }
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s,
+                        b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KINO_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return KINO_OK;
+}
+
+int device_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// Opt a kernel into its dynamic shared memory once per device.
+template <typename K>
+kino_status ensure_smem(K kernel, int bytes, int slot) {
+  static bool done[16][64] = {{false}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[slot][dev]) return KINO_OK;
+  const cudaError_t e =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return fail(KINO_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64) done[slot][dev] = true;
+  return KINO_OK;
+}
+
+template <int BN, int STAGES>
+kino_status launch_gemm(const void* x, const void* w, void* out, const kino::GemmShape& s0,
+                        int64_t ldx, int64_t bsx, int64_t ldw, const kino::GemmEpi& e,
+                        cudaStream_t stream, int slot) {
+  using L = kino::GemmSmem<BN, STAGES>;
+  CUtensorMap ma, mb;
+  const uint64_t da[3] = {static_cast<uint64_t>(s0.k), static_cast<uint64_t>(s0.m),
+                          static_cast<uint64_t>(s0.batch)};
+  const uint64_t sa[2] = {static_cast<uint64_t>(ldx),
+                          static_cast<uint64_t>(s0.batch > 1 ? bsx : ldx * s0.m)};
+  const uint32_t ba[3] = {64, 128, 1};
+  kino_status st = make_map(&ma, x, 3, da, sa, ba);
+  if (st != KINO_OK) return st;
+  const uint64_t db[2] = {static_cast<uint64_t>(s0.k), static_cast<uint64_t>(s0.n)};
+  const uint64_t sb[1] = {static_cast<uint64_t>(ldw)};
+  const uint32_t bb[2] = {64, static_cast<uint32_t>(BN)};
+  st = make_map(&mb, w, 2, db, sb, bb);
+  if (st != KINO_OK) return st;
+  kino::GemmShape s = s0;
+  s.tiles_m = (s.m + kino::GEMM_BM - 1) / kino::GEMM_BM;
+  s.tiles_n = (s.n + BN - 1) / BN;
+  s.num_tiles = s.tiles_m * s.tiles_n * s.batch;
+  s.kblocks = (s.k + kino::GEMM_BK - 1) / kino::GEMM_BK;
+  auto kernel = kino::gemm_bf16_tc_kernel<BN, STAGES>;
+  st = ensure_smem(kernel, L::TOTAL, slot);
+  if (st != KINO_OK) return st;
+  const int grid = s.num_tiles < device_sms() ? s.num_tiles : device_sms();
+  kernel<<<grid, kino::GEMM_THREADS, L::TOTAL, stream>>>(
+      ma, mb, reinterpret_cast<__nv_bfloat16*>(out), s, e);
+  return check_launch("kino_linear");
+}
+
+}  // namespace
+
+extern "C" {
+
+int kino_abi_version(void) { return 1; }
+
+const char* kino_last_error(void) { return g_err; }
+
+int kino_num_sms(void) { return device_sms(); }
+
+kino_status kino_device_status(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(KINO_ECUDA, "stream sync: %s", cudaGetErrorString(e));
+  int flag = 0;
+  e = cudaMemcpyFromSymbol(&flag, kino::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return fail(KINO_ECUDA, "device status: %s", cudaGetErrorString(e));
+  if (flag != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(kino::g_device_error, &zero, sizeof(int));
+    return fail(flag, "a kernel wait timed out (device status %d)", flag);
+  }
+  return KINO_OK;
+}
+
+kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, int64_t m,
+                        int64_t n, int64_t k, int64_t ldx, int64_t bsx, int64_t ldw, int64_t ldo,
+                        int64_t bso, const kino_epilogue* epi, void* stream) {
+  if (x == nullptr || w == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_linear: null operand");
+  if (batch < 1 || m < 1 || n < 1 || k < 1) return fail(KINO_EINVAL, "kino_linear: empty shape");
+  if (k % 8 || n % 8 || ldx % 8 || ldw % 8 || ldo % 8 || (batch > 1 && (bsx % 8 || bso % 8)))
+    return fail(KINO_ENOTSUPPORTED,
+                "kino_linear: k, n and strides must be multiples of 8 (k=%lld n=%lld)",
+                (long long)k, (long long)n);
+  if (ldx < k || ldw < k || ldo < n) return fail(KINO_EINVAL, "kino_linear: stride below width");
+  if (m > (1 << 30) || n > (1 << 30) || k > (1 << 30) || batch > 65535)
+    return fail(KINO_ENOTSUPPORTED, "kino_linear: shape too large");
+  if (!aligned16(out)) return fail(KINO_EINVAL, "kino_linear: out not 16-byte aligned");
+  kino::GemmEpi e;
+  std::memset(&e, 0, sizeof(e));
+  e.kind = kino::EPI_NONE;
+  e.act_col_begin = 0;
+  if (epi != nullptr) {
+    e.kind = epi->kind;
+    e.bias = static_cast<const __nv_bfloat16*>(epi->bias);
+    e.residual = static_cast<const __nv_bfloat16*>(epi->residual);
+    e.ld_res = epi->ld_residual;
+    e.bs_res = epi->bs_residual;
+    e.gate = static_cast<const __nv_bfloat16*>(epi->gate);
+    e.bs_gate = epi->bs_gate;
+    e.act_col_begin = epi->act_col_begin;
+    e.scalar = epi->scalar;
+    e.aux = static_cast<const __nv_bfloat16*>(epi->aux);
+    e.ld_aux = epi->ld_aux;
+    e.bs_aux = epi->bs_aux;
+    if (e.kind < 0 || e.kind > 4) return fail(KINO_EINVAL, "kino_linear: unknown epilogue");
+    if (e.bias != nullptr && !aligned16(e.bias))
+      return fail(KINO_EINVAL, "kino_linear: bias not 16-byte aligned");
+    if (e.kind == kino::EPI_GATED_RESIDUAL &&
+        (e.residual == nullptr || e.gate == nullptr || !aligned16(e.residual) ||
+         !aligned16(e.gate) || e.ld_res % 8 || e.bs_res % 8 || e.bs_gate % 8))
+      return fail(KINO_EINVAL, "kino_linear: gated residual needs aligned residual and gate");
+    if (e.kind == kino::EPI_EULER &&
+        (e.aux == nullptr || !aligned16(e.aux) || e.ld_aux % 8 || e.bs_aux % 8))
+      return fail(KINO_EINVAL, "kino_linear: Euler epilogue needs an aligned sample");
+  }
+  kino::GemmShape s;
+  std::memset(&s, 0, sizeof(s));
+  s.batch = static_cast<int>(batch);
+  s.m = static_cast<int>(m);
+  s.n = static_cast<int>(n);
+  s.k = static_cast<int>(k);
+  s.ldo = ldo;
+  s.bs_out = batch > 1 ? bso : 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n <= 128) return launch_gemm<128, 6>(x, w, out, s, ldx, bsx, ldw, e, st, 0);
+  return launch_gemm<256, 4>(x, w, out, s, ldx, bsx, ldw, e, st, 1);
+}
+
+kino_status kino_gemv(const void* x, int64_t ldx, const void* w, const void* bias, void* y,
+                      int64_t ldy, int64_t batch, int64_t n, int64_t k, int act, void* stream) {
+  if (x == nullptr || w == nullptr || y == nullptr) return fail(KINO_EINVAL, "kino_gemv: null");
+  if (batch < 1 || batch > kino::GEMV_MAXB)
+    return fail(KINO_ENOTSUPPORTED, "kino_gemv: batch must be 1..%d", kino::GEMV_MAXB);
+  if (k % 8 || !aligned16(w) || n < 1 || k < 8)
+    return fail(KINO_ENOTSUPPORTED, "kino_gemv: k %% 8 and aligned weight required");
+  const int smem = static_cast<int>(batch * k * sizeof(float));
+  if (smem > 200 * 1024) return fail(KINO_ENOTSUPPORTED, "kino_gemv: k too large");
+  kino_status s = ensure_smem(kino::gemv_kernel, 200 * 1024, 2);
+  if (s != KINO_OK) return s;
+  const int per = kino::GEMV_THREADS / 32;
+  const int grid = static_cast<int>((n + per - 1) / per);
+  kino::gemv_kernel<<<grid, kino::GEMV_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
+      static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y), ldy,
+      static_cast<int>(batch), static_cast<int>(n), static_cast<int>(k), act);
+  return check_launch("kino_gemv");
+}
+
+kino_status kino_attention(const kino_attention_args* a, void* stream) {
+  if (a == nullptr) return fail(KINO_EINVAL, "kino_attention: null args");
+  if (a->head_dim != 128)
+    return fail(KINO_ENOTSUPPORTED, "kino_attention: head_dim %lld (only 128)",
+                (long long)a->head_dim);
+  if (a->n_q < 1 || a->n_q > 2 || a->n_kv < 1 || a->n_kv > 2)
+    return fail(KINO_EINVAL, "kino_attention: 1 or 2 segments");
+  if (a->batch < 1 || a->heads < 1 || a->batch > 65535 || a->heads > 65535)
+    return fail(KINO_EINVAL, "kino_attention: batch/heads");
+  kino::AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.batch = static_cast<int>(a->batch);
+  p.heads = static_cast<int>(a->heads);
+  p.nq_seg = a->n_q;
+  p.nkv_seg = a->n_kv;
+  p.scale_log2 = a->scale * 1.4426950408889634f;
+  CUtensorMap mq[2], mk[2], mv[2];
+  const uint32_t box[4] = {64, 128, 1, 1};
+  int tiles = 0;
+  for (int s = 0; s < 2; ++s) {
+    const int qs = s < a->n_q ? s : 0;
+    if (s < a->n_q && (a->q_tokens[s] < 1 || a->q[s] == nullptr || a->out[s] == nullptr))
+      return fail(KINO_EINVAL, "kino_attention: empty query segment");
+    if (a->ld_q[qs] % 8 || a->ld_out[qs] % 8 || (a->batch > 1 && (a->bs_q[qs] % 8)))
+      return fail(KINO_ENOTSUPPORTED, "kino_attention: strides must be multiples of 8");
+    const uint64_t dq[4] = {128, static_cast<uint64_t>(a->q_tokens[qs]),
+                            static_cast<uint64_t>(a->heads), static_cast<uint64_t>(a->batch)};
+    const uint64_t sq[3] = {static_cast<uint64_t>(a->ld_q[qs]), 128,
+                            static_cast<uint64_t>(a->batch > 1 ? a->bs_q[qs] : 8)};
+    kino_status st = make_map(&mq[s], a->q[qs], 4, dq, sq, box);
+    if (st != KINO_OK) return st;
+    if (!aligned16(a->out[qs])) return fail(KINO_EINVAL, "kino_attention: out alignment");
+    if (s < a->n_q) {
+      p.q_tokens[s] = static_cast<int>(a->q_tokens[s]);
+      p.q_tiles[s] = (p.q_tokens[s] + 127) / 128;
+      p.out[s] = static_cast<__nv_bfloat16*>(a->out[s]);
+      p.ld_out[s] = a->ld_out[s];
+      p.bs_out[s] = a->bs_out[s];
+      tiles += p.q_tiles[s];
+    }
+    const int ks = s < a->n_kv ? s : 0;
+    if (s < a->n_kv && (a->kv_tokens[s] < 1 || a->k[s] == nullptr || a->v[s] == nullptr))
+      return fail(KINO_EINVAL, "kino_attention: empty key segment");
+    if (a->ld_k[ks] % 8 || a->ld_v[ks] % 8 ||
+        (a->batch > 1 && (a->bs_k[ks] % 8 || a->bs_v[ks] % 8)))
+      return fail(KINO_ENOTSUPPORTED, "kino_attention: strides must be multiples of 8");
+    const uint64_t dk[4] = {128, static_cast<uint64_t>(a->kv_tokens[ks]),
+                            static_cast<uint64_t>(a->heads), static_cast<uint64_t>(a->batch)};
+    const uint64_t sk[3] = {static_cast<uint64_t>(a->ld_k[ks]), 128,
+                            static_cast<uint64_t>(a->batch > 1 ? a->bs_k[ks] : 8)};
+    const uint64_t sv[3] = {static_cast<uint64_t>(a->ld_v[ks]), 128,
+                            static_cast<uint64_t>(a->batch > 1 ? a->bs_v[ks] : 8)};
+    st = make_map(&mk[s], a->k[ks], 4, dk, sk, box);
+    if (st != KINO_OK) return st;
+    st = make_map(&mv[s], a->v[ks], 4, dk, sv, box);
+    if (st != KINO_OK) return st;
+    if (s < a->n_kv) {
+      p.kv_tokens[s] = static_cast<int>(a->kv_tokens[s]);
+      p.kv_blocks[s] = (p.kv_tokens[s] + 127) / 128;
+    }
+  }
+  kino_status st = ensure_smem(kino::attention_tc_kernel, kino::AttnSmem::TOTAL, 3);
+  if (st != KINO_OK) return st;
+  dim3 grid(tiles, p.heads, p.batch);
+  kino::attention_tc_kernel<<<grid, kino::ATT_THREADS, kino::AttnSmem::TOTAL,
+                              static_cast<cudaStream_t>(stream)>>>(mq[0], mq[1], mk[0], mk[1],
+                                                                   mv[0], mv[1], p);
+  return check_launch("kino_attention");
+}
+
+kino_status kino_dense_attention(const void* q, const void* k, const void* v, void* out,
+                                 int64_t tq, int64_t tk, int64_t heads, int64_t dim,
+                                 void* stream) {
+  if (dim != 128) return fail(KINO_ENOTSUPPORTED, "kino_dense_attention: dim %lld", (long long)dim);
+  kino_attention_args a;
+  std::memset(&a, 0, sizeof(a));
+  a.batch = 1;
+  a.heads = heads;
+  a.head_dim = dim;
+  a.scale = 1.0f / sqrtf(static_cast<float>(dim));
+  a.n_q = 1;
+  a.q[0] = q;
+  a.out[0] = out;
+  a.q_tokens[0] = tq;
+  a.ld_q[0] = a.ld_out[0] = heads * dim;
+  a.n_kv = 1;
+  a.k[0] = k;
+  a.v[0] = v;
+  a.kv_tokens[0] = tk;
+  a.ld_k[0] = a.ld_v[0] = heads * dim;
+  return kino_attention(&a, stream);
+}
+
+kino_status kino_adaln(const void* x, int64_t ldx, int64_t bsx, const void* shift,
+                       const void* scale, int64_t bs_mod, void* out, int64_t ldo, int64_t bso,
+                       int64_t batch, int64_t rows, int64_t dim, int norm_kind, float eps,
+                       void* stream) {
+  if (x == nullptr || shift == nullptr || scale == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_adaln: null");
+  if (dim % 8 || dim > 8192 || ldx % 8 || ldo % 8 || bs_mod % 8 || !aligned16(x) ||
+      !aligned16(out) || !aligned16(shift) || !aligned16(scale))
+    return fail(KINO_ENOTSUPPORTED, "kino_adaln: dim %% 8, dim <= 8192, aligned operands");
+  if (rows < 1 || batch < 1 || rows > 0x7fffffff || batch > 65535)
+    return fail(KINO_EINVAL, "kino_adaln: rows/batch");
+  dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(batch));
+  kino::adaln_kernel<<<grid, kino::ADALN_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, bsx, static_cast<const __nv_bfloat16*>(shift),
+      static_cast<const __nv_bfloat16*>(scale), bs_mod, static_cast<__nv_bfloat16*>(out), ldo,
+      bso, static_cast<int>(rows), static_cast<int>(dim), norm_kind == KINO_NORM_LAYER, eps);
+  return check_launch("kino_adaln");
+}
+
+kino_status kino_rms_norm(const void* x, const void* weight, void* out, int64_t rows, int64_t dim,
+                          float eps, float weight_offset, void* stream) {
+  if (x == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_rms_norm: null");
+  if (dim % 8 || dim > 8192 || !aligned16(x) || !aligned16(out) ||
+      (weight != nullptr && !aligned16(weight)))
+    return fail(KINO_ENOTSUPPORTED, "kino_rms_norm: dim %% 8, dim <= 8192, aligned operands");
+  if (rows < 1 || rows > 0x7fffffff) return fail(KINO_EINVAL, "kino_rms_norm: rows");
+  kino::rms_norm_kernel<<<static_cast<unsigned>(rows), kino::ADALN_THREADS, 0,
+                          static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
+      static_cast<__nv_bfloat16*>(out), static_cast<int>(dim), eps, weight_offset);
+  return check_launch("kino_rms_norm");
+}
+
+kino_status kino_qk_norm_rope(void* x, int64_t ld, int64_t bs, int64_t batch, int64_t tokens,
+                              int64_t heads, const void* weight, int norm_kind, int rope_kind,
+                              const float* cos_table, const float* sin_table, int table_batched,
+                              int64_t table_tokens, int64_t table_offset, float eps,
+                              void* stream) {
+  if (x == nullptr) return fail(KINO_EINVAL, "kino_qk_norm_rope: null");
+  if (norm_kind < 0 || norm_kind > 2 || rope_kind < 0 || rope_kind > 2)
+    return fail(KINO_EINVAL, "kino_qk_norm_rope: bad kind");
+  if (norm_kind != 0 && (weight == nullptr || !aligned16(weight)))
+    return fail(KINO_EINVAL, "kino_qk_norm_rope: norm needs an aligned weight");
+  if (rope_kind != 0 && (cos_table == nullptr || sin_table == nullptr))
+    return fail(KINO_EINVAL, "kino_qk_norm_rope: rope needs tables");
+  if (heads < 1 || heads > 128 || ld % 8 || (batch > 1 && bs % 8) || !aligned16(x))
+    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope: heads <= 128, aligned rows");
+  if (tokens < 1 || batch < 1) return fail(KINO_EINVAL, "kino_qk_norm_rope: empty");
+  if (rope_kind != 0 && table_offset + tokens > table_tokens)
+    return fail(KINO_EINVAL, "kino_qk_norm_rope: table too short");
+  dim3 grid(static_cast<unsigned>(tokens), static_cast<unsigned>(batch));
+  kino::qk_norm_rope_kernel<<<grid, static_cast<unsigned>(heads * 8), 0,
+                              static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(x), ld, bs, static_cast<int>(heads),
+      static_cast<const __nv_bfloat16*>(weight), norm_kind, rope_kind, cos_table, sin_table,
+      table_batched, static_cast<int>(table_tokens), static_cast<int>(table_offset), eps);
+  return check_launch("kino_qk_norm_rope");
+}
+
+kino_status kino_split_rope(const void* x, const float* cos_table, const float* sin_table,
+                            void* out, int64_t batch, int64_t tokens, int64_t heads, int64_t half,
+                            int table_batched, void* stream) {
+  if (x == nullptr || cos_table == nullptr || sin_table == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_split_rope: null");
+  if (batch < 1 || tokens < 1 || heads < 1 || half < 1)
+    return fail(KINO_EINVAL, "kino_split_rope: empty");
+  const int64_t n = batch * tokens * heads * half;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 65535 * 8) blocks = 65535 * 8;
+  kino::split_rope_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                            static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), cos_table, sin_table,
+      static_cast<__nv_bfloat16*>(out), static_cast<int>(batch), static_cast<int>(tokens),
+      static_cast<int>(heads), static_cast<int>(half), table_batched);
+  return check_launch("kino_split_rope");
+}
+
+static kino_status launch_elem(int kind, const void* a, const void* b, void* out, int64_t n,
+                               float s0, float s1, void* stream, const char* name) {
+  if (a == nullptr || out == nullptr) return fail(KINO_EINVAL, "%s: null", name);
+  if (n % 8 || !aligned16(a) || !aligned16(out) || (b != nullptr && !aligned16(b)))
+    return fail(KINO_ENOTSUPPORTED, "%s: n %% 8 == 0 and 16-byte alignment required", name);
+  if (n == 0) return KINO_OK;
+  int64_t blocks = (n / 8 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  kino::elementwise_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                             static_cast<cudaStream_t>(stream)>>>(
+      kind, static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
+      static_cast<__nv_bfloat16*>(out), n, s0, s1);
+  return check_launch(name);
+}
+
+kino_status kino_gelu_tanh(const void* x, void* out, int64_t n, void* stream) {
+  return launch_elem(kino::ELEM_GELU, x, nullptr, out, n, 0.f, 0.f, stream, "kino_gelu_tanh");
+}
+
+kino_status kino_silu(const void* x, void* out, int64_t n, void* stream) {
+  return launch_elem(kino::ELEM_SILU, x, nullptr, out, n, 0.f, 0.f, stream, "kino_silu");
+}
+
+kino_status kino_cfg_combine(const void* cond, const void* uncond, float guidance, void* out,
+                             int64_t n, void* stream) {
+  if (uncond == nullptr) return fail(KINO_EINVAL, "kino_cfg_combine: null");
+  return launch_elem(kino::ELEM_CFG, cond, uncond, out, n, guidance, 0.f, stream,
+                     "kino_cfg_combine");
+}
+
+kino_status kino_euler_velocity(const void* x, const void* v, float dt, void* out, int64_t n,
+                                void* stream) {
+  if (v == nullptr) return fail(KINO_EINVAL, "kino_euler_velocity: null");
+  return launch_elem(kino::ELEM_EULER_V, x, v, out, n, dt, 0.f, stream, "kino_euler_velocity");
+}
+
+kino_status kino_euler_x0(const void* x, const void* v, float sigma, float ratio, void* out,
+                          int64_t n, void* stream) {
+  if (v == nullptr) return fail(KINO_EINVAL, "kino_euler_x0: null");
+  return launch_elem(kino::ELEM_EULER_X0, x, v, out, n, sigma, ratio, stream, "kino_euler_x0");
+}
+
+kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, int64_t dim,
+                                    void* stream) {
+  if (t == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_timestep_embedding: null");
+  if (batch < 1 || dim < 2 || dim % 2 || batch > 65535)
+    return fail(KINO_EINVAL, "kino_timestep_embedding: shape");
+  kino::timestep_embedding_kernel<<<static_cast<unsigned>(batch), 128, 0,
+                                    static_cast<cudaStream_t>(stream)>>>(
+      t, static_cast<__nv_bfloat16*>(out), static_cast<int>(batch), static_cast<int>(dim));
+  return check_launch("kino_timestep_embedding");
+}
+
+}  // extern "C"

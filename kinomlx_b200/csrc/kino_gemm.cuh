@@ -1,0 +1,323 @@
+// bf16 GEMM on the 5th-generation tensor cores (tcgen05) with fused epilogues.
+//
+//   out[b, m, n] = epilogue( sum_k x[b, m, k] * w[n, k] )
+//
+// x rows are K-contiguous (activations), w is an nn.Linear-style (out, in) weight, so both
+// operands are K-major and TMA loads them straight into 128-byte-swizzled shared memory.
+// One CTA per SM runs a persistent loop over 128 x BN output tiles:
+//   warp 0      TMA producer (A and B tiles, STAGES-deep ring of mbarriers)
+//   warp 1      allocates tensor memory and issues tcgen05.mma (one elected thread)
+//   warps 2..5  epilogue: tcgen05.ld the fp32 accumulator, apply the fused op, store bf16
+// Two accumulator buffers in tensor memory let the epilogue of tile i overlap the MMAs of
+// tile i+1. Nothing here uses cluster multicast.
+//
+// The epilogue ops restate, in one pass, the reference's separate MLX operations with their
+// rounding points (kinomlx/models/flux2/transformer.py:162-164 gated residuals,
+// kinomlx/kernels/fused_ops.py:27-35 tanh-GELU, kinomlx/models/flux2/sampling.py:109-113 Euler,
+// kinomlx/models/ltx2/transformer/attention.py:308-315 head gates).
+#pragma once
+#include "kino_common.cuh"
+
+namespace kino {
+
+enum EpiKind : int {
+  EPI_NONE = 0,
+  EPI_GELU = 1,
+  EPI_GATED_RESIDUAL = 2,
+  EPI_EULER = 3,
+  EPI_SIGMOID2 = 4,
+};
+
+struct GemmEpi {
+  int kind;
+  const __nv_bfloat16* bias;      // [n] or null
+  const __nv_bfloat16* residual;  // gated residual source, geometry of out
+  int64_t ld_res, bs_res;
+  const __nv_bfloat16* gate;      // [batch, n] (batch stride bs_gate)
+  int64_t bs_gate;
+  int64_t act_col_begin;          // GELU only for columns >= this
+  float scalar;                   // Euler dt (fp32, rounded to bf16 as the reference does)
+  const __nv_bfloat16* aux;       // Euler current sample
+  int64_t ld_aux, bs_aux;
+};
+
+struct GemmShape {
+  int batch, m, n, k;
+  int64_t ldo, bs_out;
+  int tiles_m, tiles_n, num_tiles, kblocks;
+};
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  // barriers: full[S], empty[S], tmem_full[2], tmem_empty[2], drain; then tmem base + abort
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int TOTAL = TILE_BYTES + BAR_BYTES + 1024;  // + alignment slack
+};
+
+__device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int t, int& b, int& mt,
+                                                 int& nt) {
+  const int per_n = s.batch * s.tiles_m;
+  nt = t / per_n;
+  const int rem = t - nt * per_n;
+  b = rem / s.tiles_m;
+  mt = rem - b * s.tiles_m;
+}
+
+// Apply the epilogue to 32 consecutive columns [col0, col0 + 32) of one output row and store.
+__device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const GemmEpi& e,
+                                                    __nv_bfloat16* out, int b, int row,
+                                                    int col0, const uint32_t (&acc)[32]) {
+  if (row >= s.m || col0 >= s.n) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]);
+  if (e.bias != nullptr) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (col0 + g * 8 < s.n) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(e.bias + col0 + g * 8);
+        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = unpack_bf16x2(w4[q]);
+          v[g * 8 + q * 2] += f.x;
+          v[g * 8 + q * 2 + 1] += f.y;
+        }
+      }
+    }
+  }
+  // Every reference path rounds the projection to the activation dtype first.
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
+
+  const int64_t out_off = static_cast<int64_t>(b) * s.bs_out + static_cast<int64_t>(row) * s.ldo;
+  if (e.kind == EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j >= e.act_col_begin) v[j] = gelu_tanh_f32(v[j]);
+  } else if (e.kind == EPI_SIGMOID2) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = 2.0f * bf16_round(1.0f / (1.0f + expf(-v[j])));
+  } else if (e.kind == EPI_GATED_RESIDUAL) {
+    const __nv_bfloat16* res = e.residual + static_cast<int64_t>(b) * e.bs_res +
+                               static_cast<int64_t>(row) * e.ld_res + col0;
+    const __nv_bfloat16* gte = e.gate + static_cast<int64_t>(b) * e.bs_gate + col0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (col0 + g * 8 < s.n) {
+        const uint4 rr = *reinterpret_cast<const uint4*>(res + g * 8);
+        const uint4 gg = *reinterpret_cast<const uint4*>(gte + g * 8);
+        const uint32_t r4[4] = {rr.x, rr.y, rr.z, rr.w};
+        const uint32_t g4[4] = {gg.x, gg.y, gg.z, gg.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 rf = unpack_bf16x2(r4[q]);
+          const float2 gf = unpack_bf16x2(g4[q]);
+          float& a0 = v[g * 8 + q * 2];
+          float& a1 = v[g * 8 + q * 2 + 1];
+          a0 = rf.x + bf16_round(gf.x * a0);
+          a1 = rf.y + bf16_round(gf.y * a1);
+        }
+      }
+    }
+  } else if (e.kind == EPI_EULER) {
+    const __nv_bfloat16* xs = e.aux + static_cast<int64_t>(b) * e.bs_aux +
+                              static_cast<int64_t>(row) * e.ld_aux + col0;
+    const float dt = bf16_round(e.scalar);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (col0 + g * 8 < s.n) {
+        const uint4 xx = *reinterpret_cast<const uint4*>(xs + g * 8);
+        const uint32_t x4[4] = {xx.x, xx.y, xx.z, xx.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 xf = unpack_bf16x2(x4[q]);
+          float& a0 = v[g * 8 + q * 2];
+          float& a1 = v[g * 8 + q * 2 + 1];
+          a0 = xf.x + bf16_round(dt * a0);
+          a1 = xf.y + bf16_round(dt * a1);
+        }
+      }
+    }
+  }
+  __nv_bfloat16* dst = out + out_off + col0;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    if (col0 + g * 8 < s.n) {
+      uint4 w;
+      w.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
+      w.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
+      w.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
+      w.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
+      *reinterpret_cast<uint4*>(dst + g * 8) = w;
+    }
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_b, __nv_bfloat16* __restrict__ out,
+                        const GemmShape s, const GemmEpi e) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = warp_id();
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&map_a);
+    tma_prefetch(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x) {
+        int b, mt, nt;
+        gemm_tile_coords(s, t, b, mt, nt);
+        for (int kb = 0; kb < s.kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+          uint8_t* sa = smem + stage * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          mbar_expect_tx(&full[stage], L::STAGE_BYTES);
+          tma_load_3d(sa, &map_a, &full[stage], kb * GEMM_BK, mt * GEMM_BM, b);
+          tma_load_2d(sb, &map_b, &full[stage], kb * GEMM_BK, nt * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      // Copies still in flight must land before the CTA exits: wait (bounded) on the last
+      // phase armed on each stage. In a normal run these phases completed long ago.
+      if (*abort_flag) {
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--stage < 0) {
+            stage = STAGES - 1;
+            phase ^= 1u;
+          }
+          const uint64_t t0 = global_ns();
+          while (!mbar_try_wait(&full[stage], phase) && global_ns() - t0 < 200000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(GEMM_BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < s.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            umma_bf16(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32), idesc,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      // All issued MMAs must finish before tensor memory is released.
+      umma_commit(drain);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 200000000ull) {
+      }
+    }
+  } else {
+    // Epilogue warps 2..5. Tensor-memory lane quarter is fixed by warp id % 4.
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + static_cast<int>(lane);
+    int local = 0;
+    for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
+      int b, mt, nt;
+      gemm_tile_coords(s, t, b, mt, nt);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int row = mt * GEMM_BM + row_in_tile;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((quarter * 32) << 16) + acc * BN + c * 32, r);
+        tmem_wait_ld();
+        gemm_epilogue_store(s, e, out, b, row, nt * BN + c * 32, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+}  // namespace kino

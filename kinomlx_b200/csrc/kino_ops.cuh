@@ -1,0 +1,412 @@
+// Bandwidth-bound kernels of the denoise step. Each restates one reference operation with its
+// rounding points, reading and writing every element once.
+#pragma once
+#include "kino_common.cuh"
+
+namespace kino {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Block-wide sum; `red` holds one float per warp. All threads get the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5;
+  const int l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = (l < nw) ? red[l] : 0.0f;
+  t = warp_sum(t);
+  return t;
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 r = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = unpack_bf16x2(w[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 r;
+  r.x = pack_bf16x2(f[0], f[1]);
+  r.y = pack_bf16x2(f[2], f[3]);
+  r.z = pack_bf16x2(f[4], f[5]);
+  r.w = pack_bf16x2(f[6], f[7]);
+  *reinterpret_cast<uint4*>(p) = r;
+}
+
+// ----------------------------------------------------------------------------- AdaLN
+// out = norm(x) * (1 + scale[b]) + shift[b], norm = LayerNorm (no affine) or RMSNorm (no
+// affine), statistics in fp32, the normalised row rounded to bf16, then the modulation in bf16
+// arithmetic one operation at a time:
+//   kinomlx/models/flux2/transformer.py:56-60 (layer_norm, eps 1e-6)
+//   kinomlx/models/ltx2/transformer/transformer.py:16-23 (rms_norm)
+//   kinomlx/models/ltx2/transformer/model.py:577-592 (output LayerNorm + shift/scale)
+constexpr int ADALN_THREADS = 128;
+constexpr int ADALN_MAXV = 8;  // dim <= 128 threads * 8 vectors * 8 = 8192
+
+__global__ void __launch_bounds__(ADALN_THREADS)
+    adaln_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x, int64_t bs_x,
+                 const __nv_bfloat16* __restrict__ shift, const __nv_bfloat16* __restrict__ scale,
+                 int64_t bs_mod, __nv_bfloat16* __restrict__ out, int64_t ld_out, int64_t bs_out,
+                 int rows, int dim, int layer_norm, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int b = blockIdx.y;
+  const __nv_bfloat16* xr = x + b * bs_x + static_cast<int64_t>(row) * ld_x;
+  __nv_bfloat16* orow = out + b * bs_out + static_cast<int64_t>(row) * ld_out;
+  const int nvec = dim >> 3;
+  float v[ADALN_MAXV][8];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < ADALN_MAXV; ++i) {
+    const int c = threadIdx.x + i * ADALN_THREADS;
+    if (c < nvec) {
+      load8(xr + c * 8, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += v[i][j];
+    }
+  }
+  float mean = 0.0f;
+  if (layer_norm) mean = block_sum(s, red) / static_cast<float>(dim);
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < ADALN_MAXV; ++i) {
+    const int c = threadIdx.x + i * ADALN_THREADS;
+    if (c < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[i][j] - mean;
+        q += d * d;
+      }
+    }
+  }
+  const float var = block_sum(q, red) / static_cast<float>(dim);
+  const float rstd = rsqrtf(var + eps);
+  const __nv_bfloat16* sh = shift + b * bs_mod;
+  const __nv_bfloat16* sc = scale + b * bs_mod;
+#pragma unroll
+  for (int i = 0; i < ADALN_MAXV; ++i) {
+    const int c = threadIdx.x + i * ADALN_THREADS;
+    if (c < nvec) {
+      float fs[8], fc[8], o[8];
+      load8(sh + c * 8, fs);
+      load8(sc + c * 8, fc);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float n = bf16_round((v[i][j] - mean) * rstd);
+        const float one_plus = bf16_round(1.0f + fc[j]);
+        o[j] = bf16_round(n * one_plus) + fs[j];
+      }
+      store8(orow + c * 8, o);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- RMSNorm
+// Weighted RMSNorm with fp32 reduction, fp32 scale by (weight + offset), one rounding
+// (kinomlx/kernels/fused_ops.py:141-193, 412-457); without a weight, the plain fp32 form.
+__global__ void __launch_bounds__(ADALN_THREADS)
+    rms_norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                    __nv_bfloat16* __restrict__ out, int dim, float eps, float offset) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * dim;
+  __nv_bfloat16* orow = out + row * dim;
+  const int nvec = dim >> 3;
+  float v[ADALN_MAXV][8];
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < ADALN_MAXV; ++i) {
+    const int c = threadIdx.x + i * ADALN_THREADS;
+    if (c < nvec) {
+      load8(xr + c * 8, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q = fmaf(v[i][j], v[i][j], q);
+    }
+  }
+  const float inv = rsqrtf(block_sum(q, red) / static_cast<float>(dim) + eps);
+#pragma unroll
+  for (int i = 0; i < ADALN_MAXV; ++i) {
+    const int c = threadIdx.x + i * ADALN_THREADS;
+    if (c < nvec) {
+      float o[8];
+      float fw[8];
+      if (w != nullptr) {
+        load8(w + c * 8, fw);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float r = v[i][j] * inv;
+        if (w != nullptr) r *= fw[j] + offset;
+        o[j] = r;
+      }
+      store8(orow + c * 8, o);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- QK norm + RoPE
+// In place on token-major projections (batch, tokens, heads * 128) with row stride ld:
+//   norm_kind 0: none; 1: RMSNorm per head (weight[128], kinomlx/models/flux2/transformer.py:68-75);
+//             2: RMSNorm over the whole heads*128 row (weight[heads*128],
+//                kinomlx/models/ltx2/transformer/attention.py:278-279, 330-339).
+//   rope_kind 0: none; 1: adjacent pairs, fp32 tables (tokens, 128) with repeated entries
+//                (kinomlx/models/flux2/transformer.py:17-29);
+//             2: split halves, fp32 tables (table_batch, heads, tokens, 64)
+//                (kinomlx/kernels/split_rope.py:35-56).
+// The normalised value is rounded to bf16 before the rotation, as the reference's separate
+// norm and rotate operations are. One CTA per token, 8 threads per head, 16 values per thread.
+__global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int64_t bs,
+                                    int heads, const __nv_bfloat16* __restrict__ w, int norm_kind,
+                                    int rope_kind, const float* __restrict__ cos_t,
+                                    const float* __restrict__ sin_t, int table_batched,
+                                    int table_tokens, int table_offset, float eps) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int b = blockIdx.y;
+  const int h = threadIdx.x >> 3;
+  const int u = threadIdx.x & 7;
+  __nv_bfloat16* row = x + b * bs + static_cast<int64_t>(t) * ld;
+  // element indices held by this thread (two runs of 8)
+  int e0, e1;
+  if (rope_kind == 2) {
+    e0 = h * 128 + u * 8;
+    e1 = e0 + 64;
+  } else {
+    e0 = h * 128 + u * 16;
+    e1 = e0 + 8;
+  }
+  float a[8], c[8];
+  load8(row + e0, a);
+  load8(row + e1, c);
+  if (norm_kind != 0) {
+    float q = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q = fmaf(a[j], a[j], fmaf(c[j], c[j], q));
+    float tot;
+    int width;
+    if (norm_kind == 1) {
+      tot = q;
+#pragma unroll
+      for (int o = 4; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+      width = 128;
+    } else {
+      tot = block_sum(q, red);
+      width = heads * 128;
+    }
+    const float inv = rsqrtf(tot / static_cast<float>(width) + eps);
+    float wa[8], wc[8];
+    const int wo0 = norm_kind == 1 ? (e0 - h * 128) : e0;
+    const int wo1 = norm_kind == 1 ? (e1 - h * 128) : e1;
+    load8(w + wo0, wa);
+    load8(w + wo1, wc);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      a[j] = bf16_round(a[j] * inv * wa[j]);
+      c[j] = bf16_round(c[j] * inv * wc[j]);
+    }
+  }
+  if (rope_kind == 1) {
+    // adjacent pairs (2i, 2i+1): out = x * cos + perp(x) * sin, perp = (-x[2i+1], x[2i])
+    const int tt = table_offset + t;
+    const float* cr = cos_t + (table_batched ? static_cast<int64_t>(b) * table_tokens : 0) * 128 +
+                      static_cast<int64_t>(tt) * 128;
+    const float* sr = sin_t + (table_batched ? static_cast<int64_t>(b) * table_tokens : 0) * 128 +
+                      static_cast<int64_t>(tt) * 128;
+    const int d0 = e0 - h * 128;
+    float ra[8], rc[8];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      const float c0 = cr[d0 + j], c1 = cr[d0 + j + 1], s0 = sr[d0 + j], s1 = sr[d0 + j + 1];
+      ra[j] = __fadd_rn(__fmul_rn(a[j], c0), __fmul_rn(-a[j + 1], s0));
+      ra[j + 1] = __fadd_rn(__fmul_rn(a[j + 1], c1), __fmul_rn(a[j], s1));
+      const float c2 = cr[d0 + 8 + j], c3 = cr[d0 + 9 + j], s2 = sr[d0 + 8 + j],
+                  s3 = sr[d0 + 9 + j];
+      rc[j] = __fadd_rn(__fmul_rn(c[j], c2), __fmul_rn(-c[j + 1], s2));
+      rc[j + 1] = __fadd_rn(__fmul_rn(c[j + 1], c3), __fmul_rn(c[j], s3));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      a[j] = ra[j];
+      c[j] = rc[j];
+    }
+  } else if (rope_kind == 2) {
+    // split halves: first = a (i), second = c (i + 64), table entry (b|0, h, t, i)
+    const int tt = table_offset + t;
+    const int64_t base =
+        ((static_cast<int64_t>(table_batched ? b : 0) * heads + h) * table_tokens + tt) * 64 +
+        u * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float cs = cos_t[base + j];
+      const float sn = sin_t[base + j];
+      const float first_c = __fmul_rn(a[j], cs);
+      const float second_s = __fmul_rn(c[j], sn);
+      const float first_s = __fmul_rn(a[j], sn);
+      const float second_c = __fmul_rn(c[j], cs);
+      a[j] = __fsub_rn(first_c, second_s);
+      c[j] = __fadd_rn(first_s, second_c);
+    }
+  }
+  store8(row + e0, a);
+  store8(row + e1, c);
+}
+
+// Standalone split-half RoPE with the reference kernel's contract: value (B, T, H*2*half) in
+// bf16, tables (table_batch, H, T, half) fp32, one fp32 rounding per product, then the
+// difference or sum, then the cast (kinomlx/kernels/split_rope.py:35-56, 159-163).
+__global__ void split_rope_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ cs,
+                                  const float* __restrict__ sn, __nv_bfloat16* __restrict__ out,
+                                  int batch, int tokens, int heads, int half, int table_batched) {
+  const int64_t n = static_cast<int64_t>(batch) * tokens * heads * half;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < n;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx % half);
+    int64_t r = idx / half;
+    const int h = static_cast<int>(r % heads);
+    r /= heads;
+    const int t = static_cast<int>(r % tokens);
+    const int b = static_cast<int>(r / tokens);
+    const int64_t row = (static_cast<int64_t>(b) * tokens + t) * (heads * 2 * half) +
+                        static_cast<int64_t>(h) * 2 * half + i;
+    const int64_t entry =
+        ((static_cast<int64_t>(table_batched ? b : 0) * heads + h) * tokens + t) * half + i;
+    const float c = cs[entry];
+    const float s = sn[entry];
+    const float first = __bfloat162float(x[row]);
+    const float second = __bfloat162float(x[row + half]);
+    const float first_c = __fmul_rn(first, c);
+    const float second_s = __fmul_rn(second, s);
+    const float first_s = __fmul_rn(first, s);
+    const float second_c = __fmul_rn(second, c);
+    out[row] = __float2bfloat16_rn(__fsub_rn(first_c, second_s));
+    out[row + half] = __float2bfloat16_rn(__fadd_rn(first_s, second_c));
+  }
+}
+
+// ----------------------------------------------------------------------------- elementwise
+enum ElemKind : int {
+  ELEM_GELU = 0,       // fused_ops.py:27-35
+  ELEM_SILU = 1,       // fused_ops.py:40-45
+  ELEM_CFG = 2,        // flux2/sampling.py:272: u + g * (p - u), bf16 ops
+  ELEM_EULER_V = 3,    // flux2/sampling.py:109-113: x + bf16(bf16(dt) * v) in fp32
+  ELEM_EULER_X0 = 4,   // ltx2 wrappers.py:49-65 + samplers/steps.py:36-70
+};
+
+__global__ void elementwise_kernel(int kind, const __nv_bfloat16* __restrict__ a,
+                                   const __nv_bfloat16* __restrict__ bsrc,
+                                   __nv_bfloat16* __restrict__ out, int64_t n, float s0, float s1) {
+  const int64_t nv = n >> 3;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float x[8], y[8], o[8];
+    load8(a + i * 8, x);
+    if (bsrc != nullptr) load8(bsrc + i * 8, y);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      switch (kind) {
+        case ELEM_GELU:
+          o[j] = gelu_tanh_f32(x[j]);
+          break;
+        case ELEM_SILU:
+          o[j] = silu_f32(x[j]);
+          break;
+        case ELEM_CFG: {  // a = cond (positive), b = uncond
+          const float d = bf16_round(x[j] - y[j]);
+          o[j] = y[j] + bf16_round(s0 * d);
+          break;
+        }
+        case ELEM_EULER_V:  // a = sample, b = velocity, s0 = dt
+          o[j] = x[j] + bf16_round(bf16_round(s0) * y[j]);
+          break;
+        case ELEM_EULER_X0: {  // a = sample, b = velocity, s0 = sigma, s1 = sigma_next / sigma
+          const float d = bf16_round(__fsub_rn(x[j], __fmul_rn(s0, y[j])));
+          o[j] = __fadd_rn(d, __fmul_rn(s1, __fsub_rn(x[j], d)));
+          break;
+        }
+        default:
+          o[j] = x[j];
+      }
+    }
+    store8(out + i * 8, o);
+  }
+}
+
+// ----------------------------------------------------------------------------- GEMV (M = batch)
+// y[b, n] = sum_k act(x[b, k]) * w[n, k] + bias[n]; act = identity or SiLU rounded to bf16
+// (kinomlx/models/flux2/transformer.py:223-258 Modulation / TimestepEmbedding,
+//  kinomlx/models/ltx2/transformer/timestep.py:31-85). One warp per output column n streams its
+// weight row with 16-byte loads; the activations sit in shared memory as fp32.
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_MAXB = 4;
+
+__global__ void __launch_bounds__(GEMV_THREADS)
+    gemv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x,
+                const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ bias,
+                __nv_bfloat16* __restrict__ y, int64_t ld_y, int batch, int n, int k, int act) {
+  extern __shared__ float xs[];  // [batch][k]
+  for (int i = threadIdx.x; i < batch * k; i += blockDim.x) {
+    const int b = i / k;
+    const int kk = i - b * k;
+    float v = __bfloat162float(x[b * ld_x + kk]);
+    if (act == 1) v = bf16_round(silu_f32(v));
+    xs[i] = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int col = blockIdx.x * (GEMV_THREADS / 32) + warp;
+  if (col >= n) return;
+  const __nv_bfloat16* wr = w + static_cast<int64_t>(col) * k;
+  float acc[GEMV_MAXB] = {0.f, 0.f, 0.f, 0.f};
+  for (int kk = lane * 8; kk < k; kk += 32 * 8) {
+    float wf[8];
+    load8(wr + kk, wf);
+#pragma unroll
+    for (int b = 0; b < GEMV_MAXB; ++b) {
+      if (b < batch) {
+        const float* xb = xs + b * k + kk;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[b] = fmaf(wf[j], xb[j], acc[b]);
+      }
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < GEMV_MAXB; ++b) {
+    if (b < batch) {
+      float v = warp_sum(acc[b]);
+      if (lane == 0) {
+        if (bias != nullptr) v = bf16_round(v) + __bfloat162float(bias[col]);
+        y[b * ld_y + col] = __float2bfloat16_rn(v);
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- timestep features
+// [cos(t * f_i), sin(t * f_i)], f_i = exp(-ln(10000) * i / half), fp32, stored as bf16
+// (kinomlx/models/flux2/transformer.py:238-241, kinomlx/models/ltx2/transformer/timestep.py:13-28).
+__global__ void timestep_embedding_kernel(const float* __restrict__ t, __nv_bfloat16* __restrict__ out,
+                                          int batch, int dim) {
+  const int half = dim / 2;
+  const int b = blockIdx.x;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float f = expf(-9.210340371976184f * static_cast<float>(i) / static_cast<float>(half));
+    const float ang = t[b] * f;
+    out[b * dim + i] = __float2bfloat16_rn(cosf(ang));
+    out[b * dim + half + i] = __float2bfloat16_rn(sinf(ang));
+  }
+}
+
+}  // namespace kino

@@ -1,0 +1,452 @@
+"""Torch-tensor front end of the C ABI: device memory and streams come from PyTorch, every
+computation is one kino_* launch on the current CUDA stream. No CPU fallback exists; a tensor on
+the wrong device or of the wrong dtype is a ValueError, a refusal by the library a RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from ._lib import (
+    EPI_EULER,
+    EPI_GATED_RESIDUAL,
+    EPI_GELU,
+    EPI_NONE,
+    EPI_SIGMOID2,
+    NORM_LAYER,
+    NORM_RMS,
+    QKNORM_FULL_ROW,
+    QKNORM_NONE,
+    QKNORM_PER_HEAD,
+    ROPE_NONE,
+    ROPE_PAIRS,
+    ROPE_SPLIT,
+)
+
+__all__ = [
+    "EPI_EULER",
+    "EPI_GATED_RESIDUAL",
+    "EPI_GELU",
+    "EPI_NONE",
+    "EPI_SIGMOID2",
+    "NORM_LAYER",
+    "NORM_RMS",
+    "QKNORM_FULL_ROW",
+    "QKNORM_NONE",
+    "QKNORM_PER_HEAD",
+    "ROPE_NONE",
+    "ROPE_PAIRS",
+    "ROPE_SPLIT",
+    "adaln",
+    "attention",
+    "cfg_combine",
+    "device_status",
+    "euler_velocity",
+    "euler_x0",
+    "gelu_tanh",
+    "gemv",
+    "linear",
+    "qk_norm_rope",
+    "rms_norm",
+    "silu",
+    "split_rope",
+    "timestep_embedding",
+]
+
+
+def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t: torch.Tensor, name: str, dtype: torch.dtype = torch.bfloat16) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the kinomlx_b200 kernels have no CPU path)")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.numel() and t.stride(-1) != 1:
+        raise ValueError(f"{name} needs a unit stride in its last dimension")
+
+
+def _as3d(t: torch.Tensor) -> torch.Tensor:
+    return t if t.dim() == 3 else t.unsqueeze(0)
+
+
+def device_status() -> None:
+    """Synchronise the current stream and raise if any kernel wait timed out."""
+    _lib.call("kino_device_status", _stream())
+
+
+def linear(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    out: torch.Tensor | None = None,
+    *,
+    bias: torch.Tensor | None = None,
+    kind: int = EPI_NONE,
+    residual: torch.Tensor | None = None,
+    gate: torch.Tensor | None = None,
+    act_col_begin: int = 0,
+    dt: float = 0.0,
+    sample: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight."""
+    _need(x, "x")
+    _need(w, "w")
+    x3 = _as3d(x)
+    batch, m, k = x3.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"weight {tuple(w.shape)} does not match input width {k}")
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=torch.bfloat16)
+    _need(out, "out")
+    o3 = _as3d(out)
+    if tuple(o3.shape) != (batch, m, n):
+        raise ValueError(f"out {tuple(out.shape)} does not match ({batch}, {m}, {n})")
+    epi = _lib.Epilogue()
+    epi.kind = kind
+    if bias is not None:
+        _need(bias, "bias")
+        epi.bias = bias.data_ptr()
+    if kind == EPI_GATED_RESIDUAL:
+        if residual is None or gate is None:
+            raise ValueError("a gated residual needs residual and gate")
+        _need(residual, "residual")
+        _need(gate, "gate")
+        r3 = _as3d(residual)
+        epi.residual = r3.data_ptr()
+        epi.ld_residual = r3.stride(1)
+        epi.bs_residual = r3.stride(0)
+        g = gate.reshape(-1, gate.shape[-1]) if gate.dim() != 2 else gate
+        epi.gate = g.data_ptr()
+        epi.bs_gate = g.stride(0) if g.shape[0] > 1 else 0
+    if kind == EPI_GELU:
+        epi.act_col_begin = act_col_begin
+    if kind == EPI_EULER:
+        if sample is None:
+            raise ValueError("the Euler epilogue needs the current sample")
+        _need(sample, "sample")
+        s3 = _as3d(sample)
+        epi.aux = s3.data_ptr()
+        epi.ld_aux = s3.stride(1)
+        epi.bs_aux = s3.stride(0)
+        epi.scalar = dt
+    _lib.call(
+        "kino_linear",
+        _ptr(x3),
+        _ptr(w),
+        _ptr(o3),
+        batch,
+        m,
+        n,
+        k,
+        x3.stride(1),
+        x3.stride(0),
+        w.stride(0),
+        o3.stride(1),
+        o3.stride(0),
+        ctypes.byref(epi),
+        _stream(),
+    )
+    return out
+
+
+def gemv(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    silu_input: bool = False,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """y = act(x) @ w.T + bias for a handful of rows (x: (batch, k), batch <= 4)."""
+    _need(x, "x")
+    _need(w, "w")
+    x2 = x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x
+    batch, k = x2.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty((batch, n), device=x.device, dtype=torch.bfloat16)
+    _lib.call(
+        "kino_gemv",
+        _ptr(x2),
+        x2.stride(0),
+        _ptr(w),
+        _ptr(bias),
+        _ptr(out),
+        out.stride(0),
+        batch,
+        n,
+        k,
+        1 if silu_input else 0,
+        _stream(),
+    )
+    return out
+
+
+def attention(
+    q: list[torch.Tensor],
+    k: list[torch.Tensor],
+    v: list[torch.Tensor],
+    out: list[torch.Tensor],
+    *,
+    heads: int,
+    scale: float | None = None,
+) -> list[torch.Tensor]:
+    """Attention over logically concatenated segments; each tensor (batch, tokens, heads*128)."""
+    if not 1 <= len(q) <= 2 or len(out) != len(q) or not 1 <= len(k) <= 2 or len(v) != len(k):
+        raise ValueError("attention takes 1 or 2 query and key/value segments")
+    args = _lib.AttentionArgs()
+    q0 = _as3d(q[0])
+    args.batch = q0.shape[0]
+    args.heads = heads
+    args.head_dim = q0.shape[-1] // heads
+    if args.head_dim * heads != q0.shape[-1]:
+        raise ValueError("query width is not heads * head_dim")
+    args.scale = scale if scale is not None else args.head_dim**-0.5
+    args.n_q = len(q)
+    for s, (qs, os_) in enumerate(zip(q, out)):
+        _need(qs, "q")
+        _need(os_, "out")
+        q3, o3 = _as3d(qs), _as3d(os_)
+        args.q[s] = q3.data_ptr()
+        args.out[s] = o3.data_ptr()
+        args.q_tokens[s] = q3.shape[1]
+        args.ld_q[s] = q3.stride(1)
+        args.bs_q[s] = q3.stride(0)
+        args.ld_out[s] = o3.stride(1)
+        args.bs_out[s] = o3.stride(0)
+    args.n_kv = len(k)
+    for s, (ks, vs) in enumerate(zip(k, v)):
+        _need(ks, "k")
+        _need(vs, "v")
+        k3, v3 = _as3d(ks), _as3d(vs)
+        args.k[s] = k3.data_ptr()
+        args.v[s] = v3.data_ptr()
+        args.kv_tokens[s] = k3.shape[1]
+        args.ld_k[s] = k3.stride(1)
+        args.bs_k[s] = k3.stride(0)
+        args.ld_v[s] = v3.stride(1)
+        args.bs_v[s] = v3.stride(0)
+    _lib.call("kino_attention", ctypes.byref(args), _stream())
+    return out
+
+
+def adaln(
+    x: torch.Tensor,
+    shift: torch.Tensor,
+    scale: torch.Tensor,
+    out: torch.Tensor | None = None,
+    *,
+    norm: int = NORM_LAYER,
+    eps: float = 1e-6,
+) -> torch.Tensor:
+    """norm(x) * (1 + scale) + shift; x (batch, rows, dim), shift/scale (batch, dim)."""
+    _need(x, "x")
+    _need(shift, "shift")
+    _need(scale, "scale")
+    x3 = _as3d(x)
+    batch, rows, dim = x3.shape
+    if out is None:
+        out = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
+    o3 = _as3d(out)
+    sh = shift.reshape(-1, dim)
+    sc = scale.reshape(-1, dim)
+    if sh.stride(0) != sc.stride(0):
+        raise ValueError("shift and scale need the same batch stride")
+    _lib.call(
+        "kino_adaln",
+        _ptr(x3),
+        x3.stride(1),
+        x3.stride(0),
+        _ptr(sh),
+        _ptr(sc),
+        sh.stride(0) if sh.shape[0] > 1 else 0,
+        _ptr(o3),
+        o3.stride(1),
+        o3.stride(0),
+        batch,
+        rows,
+        dim,
+        norm,
+        eps,
+        _stream(),
+    )
+    return out
+
+
+def rms_norm(
+    x: torch.Tensor,
+    weight: torch.Tensor | None = None,
+    eps: float = 1e-6,
+    *,
+    weight_offset: float = 0.0,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    _need(x, "x")
+    if not x.is_contiguous():
+        raise ValueError("rms_norm needs a contiguous input")
+    if out is None:
+        out = torch.empty_like(x)
+    dim = x.shape[-1]
+    _lib.call(
+        "kino_rms_norm",
+        _ptr(x),
+        _ptr(weight),
+        _ptr(out),
+        x.numel() // dim,
+        dim,
+        eps,
+        weight_offset,
+        _stream(),
+    )
+    return out
+
+
+def qk_norm_rope(
+    x: torch.Tensor,
+    *,
+    heads: int,
+    weight: torch.Tensor | None,
+    norm: int,
+    rope: int,
+    cos: torch.Tensor | None = None,
+    sin: torch.Tensor | None = None,
+    table_offset: int = 0,
+    eps: float = 1e-6,
+) -> torch.Tensor:
+    """In place: RMSNorm (per head or full row) then RoPE on x (batch, tokens, heads*128)."""
+    _need(x, "x")
+    x3 = _as3d(x)
+    batch, tokens, width = x3.shape
+    if width != heads * 128:
+        raise ValueError("qk_norm_rope works on 128-wide heads")
+    table_tokens = 0
+    table_batched = 0
+    if rope != ROPE_NONE:
+        if cos is None or sin is None:
+            raise ValueError("RoPE needs cos and sin tables")
+        _need(cos, "cos", torch.float32)
+        _need(sin, "sin", torch.float32)
+        if not (cos.is_contiguous() and sin.is_contiguous()):
+            raise ValueError("RoPE tables must be contiguous")
+        table_tokens = cos.shape[-2]
+        table_batched = int(cos.shape[0] > 1 and cos.dim() >= 3)
+    _lib.call(
+        "kino_qk_norm_rope",
+        _ptr(x3),
+        x3.stride(1),
+        x3.stride(0),
+        batch,
+        tokens,
+        heads,
+        _ptr(weight),
+        norm,
+        rope,
+        _ptr(cos),
+        _ptr(sin),
+        table_batched,
+        table_tokens,
+        table_offset,
+        eps,
+        _stream(),
+    )
+    return x
+
+
+def split_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """value (batch, tokens, heads*2*half), tables (1|batch, heads, tokens, half) fp32."""
+    _need(x, "x")
+    _need(cos, "cos", torch.float32)
+    _need(sin, "sin", torch.float32)
+    table_batch, heads, tokens, half = cos.shape
+    batch = x.shape[0]
+    # keep the contiguous copies alive until the launch is queued
+    x, cos, sin = x.contiguous(), cos.contiguous(), sin.contiguous()
+    out = torch.empty_like(x)
+    _lib.call(
+        "kino_split_rope",
+        _ptr(x),
+        _ptr(cos),
+        _ptr(sin),
+        _ptr(out),
+        batch,
+        tokens,
+        heads,
+        half,
+        int(table_batch == batch and batch > 1),
+        _stream(),
+    )
+    return out
+
+
+def _elementwise(name: str, *args: object) -> None:
+    _lib.call(name, *args, _stream())
+
+
+def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
+    _need(x, "x")
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    _elementwise("kino_gelu_tanh", _ptr(x), _ptr(out), x.numel())
+    return out
+
+
+def silu(x: torch.Tensor) -> torch.Tensor:
+    _need(x, "x")
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    _elementwise("kino_silu", _ptr(x), _ptr(out), x.numel())
+    return out
+
+
+def cfg_combine(cond: torch.Tensor, uncond: torch.Tensor, guidance: float) -> torch.Tensor:
+    _need(cond, "cond")
+    _need(uncond, "uncond")
+    cond, uncond = cond.contiguous(), uncond.contiguous()
+    out = torch.empty_like(cond)
+    _elementwise("kino_cfg_combine", _ptr(cond), _ptr(uncond), guidance, _ptr(out), cond.numel())
+    return out
+
+
+def euler_velocity(
+    x: torch.Tensor, v: torch.Tensor, dt: float, out: torch.Tensor | None = None
+) -> torch.Tensor:
+    _need(x, "x")
+    _need(v, "v")
+    if out is None:
+        out = torch.empty_like(x)
+    _elementwise("kino_euler_velocity", _ptr(x), _ptr(v), dt, _ptr(out), x.numel())
+    return out
+
+
+def euler_x0(
+    x: torch.Tensor, v: torch.Tensor, sigma: float, sigma_next: float
+) -> torch.Tensor:
+    _need(x, "x")
+    _need(v, "v")
+    out = torch.empty_like(x)
+    ratio = float(torch.tensor(sigma_next / sigma, dtype=torch.float32))
+    _elementwise("kino_euler_x0", _ptr(x), _ptr(v), sigma, ratio, _ptr(out), x.numel())
+    return out
+
+
+def timestep_embedding(t: torch.Tensor, dim: int = 256) -> torch.Tensor:
+    """t: fp32 (batch,) on the device -> bf16 (batch, dim) [cos, sin] features."""
+    _need(t, "t", torch.float32)
+    t = t.contiguous()
+    out = torch.empty((t.shape[0], dim), device=t.device, dtype=torch.bfloat16)
+    _elementwise("kino_timestep_embedding", _ptr(t), _ptr(out), t.shape[0], dim)
+    return out
+
+
+def softmax_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,338 @@
+"""Each CUDA kernel against a plain PyTorch fp32 restatement of the same op on identical inputs.
+
+Tolerances: the bf16 parity gate is a max relative error <= 2e-2 per op; attention follows the
+reference's own test bar (relative L2 < 6e-3 against fp32 SDPA for bf16 inputs,
+tests/models/ltx2/test_dense_attention.py:15 in the reference).
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+BF = torch.bfloat16
+
+
+def _gen(seed: int) -> torch.Generator:
+    return torch.Generator().manual_seed(seed)
+
+
+def _randn(shape, seed, scale=1.0):
+    return (torch.randn(shape, generator=_gen(seed)) * scale).to(BF)
+
+
+def _max_rel(out: torch.Tensor, ref: torch.Tensor) -> float:
+    out = out.float().cpu()
+    ref = ref.float().cpu()
+    return float((out - ref).abs().max() / ref.abs().max().clamp_min(1e-30))
+
+
+def _rel_l2(out: torch.Tensor, ref: torch.Tensor) -> float:
+    out = out.float().cpu()
+    ref = ref.float().cpu()
+    return float((out - ref).norm() / ref.norm().clamp_min(1e-30))
+
+
+# ------------------------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize(
+    ("batch", "m", "n", "k"),
+    [
+        (1, 128, 256, 64),
+        (1, 300, 264, 200),
+        (1, 1024, 64, 3072),
+        (2, 517, 384, 128),
+        (1, 4608, 3072, 3072),
+        (1, 1536, 12288, 3072),
+    ],
+)
+def test_linear_matches_fp32(cuda_device, batch, m, n, k):
+    from kinomlx_b200 import ops
+
+    x = _randn((batch, m, k), 1)
+    w = _randn((n, k), 2, 0.02)
+    bias = _randn((n,), 3, 0.1)
+    ref = (x.float() @ w.float().T + bias.float()).to(BF)
+    out = ops.linear(x.to(cuda_device), w.to(cuda_device), bias=bias.to(cuda_device))
+    torch.cuda.synchronize()
+    assert _max_rel(out, ref) <= 2e-2
+    # same fp32 sum, one rounding: almost every element is bit-identical
+    same = (out.cpu() == ref).float().mean().item()
+    assert same > 0.95
+
+
+def test_linear_strided_views_and_epilogues(cuda_device):
+    from kinomlx_b200 import ops
+
+    dev = cuda_device
+    batch, m, k, n = 2, 200, 256, 512
+    big = _randn((batch, m, 3 * k), 4).to(dev)
+    x = big[:, :, k : 2 * k]  # strided view, row stride 3k
+    w = _randn((n, k), 5, 0.05).to(dev)
+    bias = _randn((n,), 6, 0.1).to(dev)
+    xf, wf, bf = x.float().cpu(), w.float().cpu(), bias.float().cpu()
+    proj = (xf @ wf.T + bf).to(BF).float()
+
+    # GELU from column 256 on
+    out = ops.linear(x, w, bias=bias, kind=ops.EPI_GELU, act_col_begin=256)
+    g = proj.clone()
+    t = g[..., 256:]
+    g[..., 256:] = 0.5 * t * (1 + torch.tanh((0.7978845608028654 * (t + 0.044715 * t**3)).clamp(-10, 10)))
+    assert _max_rel(out, g.to(BF)) <= 2e-2
+
+    # gated residual, in place
+    resid = _randn((batch, m, n), 7).to(dev)
+    gate = _randn((batch, n), 8).to(dev)
+    expect = (resid.float().cpu() + (gate.float().cpu()[:, None, :] * proj).to(BF).float()).to(BF)
+    ops.linear(x, w, resid, bias=bias, kind=ops.EPI_GATED_RESIDUAL, residual=resid, gate=gate)
+    torch.cuda.synchronize()
+    assert _max_rel(resid, expect) <= 2e-2
+
+    # Euler epilogue
+    sample = _randn((batch, m, n), 9).to(dev)
+    dt = -0.25
+    v = proj.to(BF)
+    inc = (torch.tensor(dt).to(BF) * v).float()
+    expect = (sample.float().cpu() + inc).to(BF)
+    out = ops.linear(x, w, bias=bias, kind=ops.EPI_EULER, dt=dt, sample=sample)
+    assert _max_rel(out, expect) <= 2e-2
+
+    # 2 * sigmoid gate logits
+    out = ops.linear(x, w, bias=bias, kind=ops.EPI_SIGMOID2)
+    assert _max_rel(out, (2 * torch.sigmoid(proj)).to(BF)) <= 2e-2
+
+
+def test_linear_refuses_unaligned_widths(cuda_device):
+    from kinomlx_b200 import ops
+
+    x = torch.zeros((4, 12), dtype=BF, device=cuda_device)
+    w = torch.zeros((16, 12), dtype=BF, device=cuda_device)
+    with pytest.raises(RuntimeError, match="KINO_ENOTSUPPORTED"):
+        ops.linear(x, w)
+
+
+# ------------------------------------------------------------------------------------ attention
+def _sdpa_ref(q, k, v, heads):
+    tq, tk = q.shape[-2], k.shape[-2]
+    d = q.shape[-1] // heads
+    b = q.shape[0]
+    qh = q.float().cpu().reshape(b, tq, heads, d).transpose(1, 2)
+    kh = k.float().cpu().reshape(b, tk, heads, d).transpose(1, 2)
+    vh = v.float().cpu().reshape(b, tk, heads, d).transpose(1, 2)
+    s = (qh @ kh.transpose(-1, -2)) * d**-0.5
+    o = torch.softmax(s, dim=-1) @ vh
+    return o.transpose(1, 2).reshape(b, tq, heads * d)
+
+
+@pytest.mark.parametrize(
+    ("tq", "tk"),
+    [(7, 7), (16, 16), (33, 33), (517, 517), (300, 1024), (1, 300), (517, 33), (40, 5)],
+)
+def test_attention_ragged_matches_fp32_sdpa(cuda_device, tq, tk):
+    from kinomlx_b200 import ops
+
+    heads = 2
+    q = _randn((1, tq, heads * 128), 11)
+    k = _randn((1, tk, heads * 128), 12)
+    v = _randn((1, tk, heads * 128), 13)
+    out = torch.empty_like(q).to(cuda_device)
+    ops.attention([q.to(cuda_device)], [k.to(cuda_device)], [v.to(cuda_device)], [out], heads=heads)
+    torch.cuda.synchronize()
+    assert _rel_l2(out, _sdpa_ref(q, k, v, heads)) < 6e-3
+
+
+def test_attention_two_segments_equal_concatenation(cuda_device):
+    from kinomlx_b200 import ops
+
+    dev = cuda_device
+    heads, nt, ni, batch = 3, 130, 257, 2
+    qkv_t = _randn((batch, nt, 3 * heads * 128), 21, 2.0).to(dev)
+    qkv_i = _randn((batch, ni, 3 * heads * 128), 22, 2.0).to(dev)
+    w = heads * 128
+    seg = lambda t, j: t[:, :, j * w : (j + 1) * w]
+    out_t = torch.empty((batch, nt, w), dtype=BF, device=dev)
+    out_i = torch.empty((batch, ni, w), dtype=BF, device=dev)
+    ops.attention(
+        [seg(qkv_t, 0), seg(qkv_i, 0)],
+        [seg(qkv_t, 1), seg(qkv_i, 1)],
+        [seg(qkv_t, 2), seg(qkv_i, 2)],
+        [out_t, out_i],
+        heads=heads,
+    )
+    q = torch.cat([seg(qkv_t, 0), seg(qkv_i, 0)], dim=1)
+    k = torch.cat([seg(qkv_t, 1), seg(qkv_i, 1)], dim=1)
+    v = torch.cat([seg(qkv_t, 2), seg(qkv_i, 2)], dim=1)
+    ref = _sdpa_ref(q, k, v, heads)
+    assert _rel_l2(torch.cat([out_t, out_i], dim=1), ref) < 6e-3
+
+
+def test_attention_full_size_flux(cuda_device):
+    from kinomlx_b200 import ops
+
+    heads, n = 24, 4608
+    q = _randn((1, n, heads * 128), 31).to(cuda_device)
+    k = _randn((1, n, heads * 128), 32).to(cuda_device)
+    v = _randn((1, n, heads * 128), 33).to(cuda_device)
+    out = torch.empty_like(q)
+    ops.attention([q], [k], [v], [out], heads=heads)
+    # compare 2 heads on the CPU
+    ref = _sdpa_ref(q[..., :256], k[..., :256], v[..., :256], 2)
+    assert _rel_l2(out[..., :256], ref) < 6e-3
+
+
+# ------------------------------------------------------------------------------------ norms
+def test_adaln_layer_and_rms(cuda_device):
+    from kinomlx_b200 import ops
+
+    dev = cuda_device
+    batch, rows, dim = 2, 37, 3072
+    x = _randn((batch, rows, dim), 41, 3.0)
+    shift = _randn((batch, dim), 42)
+    scale = _randn((batch, dim), 43)
+    xf = x.float()
+    ln = ((xf - xf.mean(-1, keepdim=True)) / torch.sqrt(xf.var(-1, unbiased=False, keepdim=True) + 1e-6)).to(BF)
+    expect = ((ln * (1 + scale[:, None, :])) + shift[:, None, :])  # bf16 ops
+    out = ops.adaln(x.to(dev), shift.to(dev), scale.to(dev), norm=ops.NORM_LAYER)
+    assert _max_rel(out, expect) <= 2e-2
+    rms = (xf / torch.sqrt((xf * xf).mean(-1, keepdim=True) + 1e-6)).to(BF)
+    expect = (rms * (1 + scale[:, None, :])) + shift[:, None, :]
+    out = ops.adaln(x.to(dev), shift.to(dev), scale.to(dev), norm=ops.NORM_RMS)
+    assert _max_rel(out, expect) <= 2e-2
+
+
+def test_rms_norm_weighted(cuda_device):
+    from kinomlx_b200 import ops
+
+    x = _randn((2, 5, 256), 20260816, 2.0)
+    w = _randn((256,), 51)
+    xf = x.float()
+    ref = (xf * torch.rsqrt((xf * xf).mean(-1, keepdim=True) + 1e-6) * (w.float() + 1.0)).to(BF)
+    out = ops.rms_norm(x.to(cuda_device), w.to(cuda_device), 1e-6, weight_offset=1.0)
+    assert _max_rel(out, ref) <= 2e-2
+
+
+def test_qk_norm_rope_per_head_pairs(cuda_device):
+    from kinomlx_b200 import ops
+
+    heads, tokens = 3, 50
+    x = _randn((1, tokens, heads * 128), 61, 2.0)
+    w = _randn((128,), 62)
+    ang = torch.randn((tokens, 64), generator=_gen(63))
+    ang = ang.repeat_interleave(2, dim=-1)
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    xf = x.float().reshape(1, tokens, heads, 128)
+    n = (xf * torch.rsqrt((xf * xf).mean(-1, keepdim=True) + 1e-6) * w.float()).to(BF).float()
+    pairs = n.reshape(1, tokens, heads, 64, 2)
+    perp = torch.stack([-pairs[..., 1], pairs[..., 0]], -1).reshape(n.shape)
+    ref = (n * cos[None, :, None] + perp * sin[None, :, None]).to(BF).reshape(1, tokens, -1)
+    xd = x.to(cuda_device)
+    ops.qk_norm_rope(
+        xd, heads=heads, weight=w.to(cuda_device), norm=ops.QKNORM_PER_HEAD, rope=ops.ROPE_PAIRS,
+        cos=cos.to(cuda_device), sin=sin.to(cuda_device),
+    )
+    assert _max_rel(xd, ref) <= 2e-2
+
+
+def test_qk_norm_rope_full_row_split(cuda_device):
+    from kinomlx_b200 import ops
+
+    heads, tokens = 4, 33
+    x = _randn((2, tokens, heads * 128), 71, 2.0)
+    w = _randn((heads * 128,), 72)
+    ang = torch.randn((1, heads, tokens, 64), generator=_gen(73))
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    xf = x.float()
+    n = (xf * torch.rsqrt((xf * xf).mean(-1, keepdim=True) + 1e-6) * w.float()).to(BF).float()
+    nh = n.reshape(2, tokens, heads, 128).transpose(1, 2)
+    a, c = nh[..., :64], nh[..., 64:]
+    out = torch.cat([a * cos - c * sin, a * sin + c * cos], -1)
+    ref = out.transpose(1, 2).reshape(2, tokens, heads * 128).to(BF)
+    xd = x.to(cuda_device)
+    ops.qk_norm_rope(
+        xd, heads=heads, weight=w.to(cuda_device), norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_SPLIT,
+        cos=cos.to(cuda_device), sin=sin.to(cuda_device),
+    )
+    assert _max_rel(xd, ref) <= 2e-2
+
+
+def test_split_rope_bit_exact_self_test_recipe(cuda_device):
+    """The reference kernel's own self-test inputs (kinomlx/kernels/split_rope.py:120-136)."""
+    from kinomlx_b200 import ops
+
+    batch, heads, tokens, half = 2, 3, 7, 5
+    count = batch * tokens * heads * 2 * half
+    value = (torch.sin(torch.arange(count, dtype=torch.float32) * 0.7310585) * 3.0).to(BF)
+    value = value.reshape(batch, tokens, heads * 2 * half)
+    angles = torch.arange(tokens * heads * half, dtype=torch.float32) * 0.4142135
+    angles = angles.reshape(1, tokens, heads, half).transpose(1, 2)
+    cos, sin = torch.cos(angles), torch.sin(angles)
+    hf = value.reshape(batch, tokens, heads, 2 * half).transpose(1, 2).float()
+    first, second = hf[..., :half], hf[..., half:]
+    graph = torch.cat([first * cos - second * sin, first * sin + second * cos], -1)
+    graph = graph.transpose(1, 2).reshape(value.shape).to(BF)
+    out = ops.split_rope(value.to(cuda_device), cos.to(cuda_device), sin.to(cuda_device))
+    assert torch.equal(out.cpu(), graph)
+
+
+# ------------------------------------------------------------------------------------ elementwise
+def test_gelu_silu_bounds(cuda_device):
+    """Reference bounds: bf16 max-abs 4e-6 / 0.0 vs fp32 formulas on linspace(-8, 8, 65536)
+    (tests/kernels/test_fused_ops.py in the reference); device tanh may differ by one bf16 ulp."""
+    from kinomlx_b200 import ops
+
+    x = torch.linspace(-8, 8, 65536).to(BF)
+    xf = x.float()
+    gelu = (0.5 * xf * (1 + torch.tanh((0.7978845608028654 * (xf + 0.044715 * xf**3)).clamp(-10, 10)))).to(BF)
+    silu = (xf / (1 + torch.exp(-xf))).to(BF)
+    g = ops.gelu_tanh(x.to(cuda_device)).cpu()
+    s = ops.silu(x.to(cuda_device)).cpu()
+    assert (g.float() - gelu.float()).abs().max() <= 2 ** -7 * gelu.float().abs().max()
+    assert (s.float() - silu.float()).abs().max() <= 2 ** -7 * silu.float().abs().max()
+    assert (g == gelu).float().mean() > 0.99
+    assert (s == silu).float().mean() > 0.99
+
+
+def test_cfg_and_euler_rounding_order(cuda_device):
+    from kinomlx_b200 import ops
+
+    cond = _randn((4096, 64), 81)
+    uncond = _randn((4096, 64), 82)
+    ref = uncond + 4.0 * (cond - uncond)  # bf16 ops
+    out = ops.cfg_combine(cond.to(cuda_device), uncond.to(cuda_device), 4.0)
+    assert torch.equal(out.cpu(), ref)
+    # Klein Euler (kinomlx/models/flux2/sampling.py:109-113)
+    x = _randn((4096, 64), 83)
+    v = _randn((4096, 64), 84)
+    dt = float(torch.tensor(0.75, dtype=torch.float32) - torch.tensor(1.0, dtype=torch.float32))
+    inc = torch.tensor(dt, dtype=torch.float32).to(BF) * v
+    ref = (x.float() + inc.float()).to(BF)
+    out = ops.euler_velocity(x.to(cuda_device), v.to(cuda_device), dt)
+    assert torch.equal(out.cpu(), ref)
+    # LTX X0 + Euler
+    sigma, nxt = 0.909375, 0.725
+    x0 = (x.float() - sigma * v.float()).to(BF)
+    ratio = torch.tensor(nxt / sigma, dtype=torch.float32)
+    ref = (x0.float() + ratio * (x.float() - x0.float())).to(BF)
+    out = ops.euler_x0(x.to(cuda_device), v.to(cuda_device), sigma, nxt)
+    assert torch.equal(out.cpu(), ref)
+
+
+def test_gemv_and_timestep_embedding(cuda_device):
+    from kinomlx_b200 import ops
+
+    t = torch.tensor([500.0, 999.0], dtype=torch.float32)
+    freq = torch.exp(-math.log(10000) * torch.arange(128, dtype=torch.float32) / 128)
+    ang = t[:, None] * freq
+    ref = torch.cat([torch.cos(ang), torch.sin(ang)], -1).to(BF)
+    emb = ops.timestep_embedding(t.to(cuda_device), 256)
+    assert _max_rel(emb, ref) <= 2e-2
+    x = _randn((2, 3072), 91)
+    w = _randn((18432, 3072), 92, 0.02)
+    b = _randn((18432,), 93, 0.1)
+    xs = (x.float() / (1 + torch.exp(-x.float()))).to(BF)
+    ref = ((xs.float() @ w.float().T).to(BF).float() + b.float()).to(BF)
+    out = ops.gemv(x.to(cuda_device), w.to(cuda_device), b.to(cuda_device), silu_input=True)
+    assert _max_rel(out, ref) <= 2e-2
