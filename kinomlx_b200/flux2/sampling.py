@@ -1,0 +1,99 @@
+"""Klein Euler trajectory on the device (kinomlx/models/flux2/sampling.py:95-281).
+
+Host work per step is scalar: the timestep's model-dtype round trip and dt, exactly as the
+reference computes them. Without CFG the Euler update runs in the epilogue of the final
+projection; with batched CFG the two velocities are combined by one elementwise kernel and the
+update follows.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+from .. import ops
+from .transformer import Flux2Transformer, PreparedText
+
+
+def schedule(image_tokens: int, steps: int) -> torch.Tensor:
+    """Empirical Klein shift (kinomlx/models/flux2/sampling.py:95-106), fp32."""
+    if image_tokens < 1 or steps < 1:
+        raise ValueError("Schedule requires positive target token and step counts")
+    long = 0.00016927 * image_tokens + 0.45666666
+    short = 8.73809524e-05 * image_tokens + 1.89833333
+    mu = long if image_tokens > 4300 else long + (short - long) * (200 - steps) / 190
+    factor = math.exp(mu)
+    sigma = torch.tensor([1 - i / steps for i in range(steps)], dtype=torch.float32)
+    shifted = factor / (factor + (1 / sigma - 1))
+    return torch.cat([shifted, torch.zeros(1, dtype=torch.float32)])
+
+
+def linear_sigmas(steps: int) -> torch.Tensor:
+    """Explicit schedule linearly spaced from 1.0 to 0.0, fp32."""
+    return torch.from_numpy(np.linspace(1.0, 0.0, steps + 1).astype(np.float32))
+
+
+def timestep_x1000(sigmas: torch.Tensor, index: int, batch: int = 1) -> torch.Tensor:
+    """The value entering the timestep embedding: ((s*1000 -> bf16) / 1000 -> bf16) * 1000 -> bf16
+    (kinomlx/models/flux2/sampling.py:209-212 and transformer.py:315)."""
+    t = ((sigmas[index : index + 1] * 1000).to(torch.bfloat16) / 1000).to(torch.bfloat16)
+    return (t * 1000).to(torch.float32).repeat(batch)
+
+
+def step_delta(sigmas: torch.Tensor, index: int) -> float:
+    """sigmas[i+1] - sigmas[i] in fp32 (kinomlx/models/flux2/sampling.py:240)."""
+    return float(sigmas[index + 1] - sigmas[index])
+
+
+def denoise_step(
+    model: Flux2Transformer,
+    prepared: PreparedText,
+    current: torch.Tensor,
+    sigmas: torch.Tensor,
+    index: int,
+    *,
+    guidance: float = 1.0,
+    cfg: bool = False,
+) -> torch.Tensor:
+    """One Euler step in place on `current` (1, Ni, C); returns `current`."""
+    dt = step_delta(sigmas, index)
+    if not cfg:
+        t = timestep_x1000(sigmas, index, current.shape[0]).to(current.device, non_blocking=True)
+        return model.run(prepared, current, t, euler_dt=dt, sample=current, out=current)
+    t = timestep_x1000(sigmas, index, 2).to(current.device, non_blocking=True)
+    both = model.run(prepared, current.repeat(2, 1, 1), t)
+    velocity = ops.cfg_combine(both[0:1], both[1:2], guidance)
+    return ops.euler_velocity(current, velocity, dt, out=current)
+
+
+def denoise(
+    model: Flux2Transformer,
+    noise: torch.Tensor,
+    text: torch.Tensor,
+    ids: torch.Tensor,
+    *,
+    sigmas: torch.Tensor,
+    negative: torch.Tensor | None = None,
+    guidance: float = 1.0,
+    check_finite: bool = True,
+) -> torch.Tensor:
+    """Denoise `noise` (1, Ni, C) under `text` (1, Nt, C_txt); `ids` are the joint [text, image]
+    positions (1, Nt+Ni, axes). Batched CFG when `negative` is given
+    (kinomlx/models/flux2/sampling.py:116-281)."""
+    if noise.dim() != 3 or noise.shape[0] != 1:
+        raise ValueError("noise must be (1, tokens, channels)")
+    if negative is not None and negative.shape != text.shape:
+        raise ValueError("negative embeddings must match the positive text's shape")
+    cfg = negative is not None and guidance != 1.0
+    conditioned = text if not cfg else torch.cat([text, negative])
+    prepared = model.prepare(conditioned, ids)
+    current = noise.to(model.device, torch.bfloat16).clone()
+    for index in range(len(sigmas) - 1):
+        denoise_step(model, prepared, current, sigmas, index, guidance=guidance, cfg=cfg)
+    if check_finite:
+        ops.device_status()
+        if not bool(torch.isfinite(current).all()):
+            raise FloatingPointError("Klein produced nonfinite latents")
+    return current

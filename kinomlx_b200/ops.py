@@ -439,11 +439,14 @@ def euler_x0(
     return out
 
 
-def timestep_embedding(t: torch.Tensor, dim: int = 256) -> torch.Tensor:
+def timestep_embedding(
+    t: torch.Tensor, dim: int = 256, *, out: torch.Tensor | None = None
+) -> torch.Tensor:
     """t: fp32 (batch,) on the device -> bf16 (batch, dim) [cos, sin] features."""
     _need(t, "t", torch.float32)
     t = t.contiguous()
-    out = torch.empty((t.shape[0], dim), device=t.device, dtype=torch.bfloat16)
+    if out is None:
+        out = torch.empty((t.shape[0], dim), device=t.device, dtype=torch.bfloat16)
     _elementwise("kino_timestep_embedding", _ptr(t), _ptr(out), t.shape[0], dim)
     return out
 
