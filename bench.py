@@ -1,0 +1,467 @@
+#!/usr/bin/env python
+"""Benchmark of the denoise-step hot path on B200.
+
+Workload: image DiT at 1024x1024, 4096 image + 512 text tokens, hidden 3072,
+24 x 128 heads, 8 double-stream + 24 single-stream blocks, GELU-tanh MLP x4, flow-matching
+Euler with sigmas linearly spaced 1 -> 0 over 4 steps, bf16, random-init weights (seed 42),
+N(0, 1) latents (seed 43) and text (seed 44). A "step" is one transformer evaluation plus the
+Euler update (fused into the last projection). Weights (9.4 GB) stream through HBM every step,
+far more than the 126 MB L2, so no explicit L2 flush is needed between timed steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kino|reference]
+
+--impl reference times the reference's CPU path for the same workload: the reference (MLX,
+Python >= 3.15) cannot run on this box, so that arm times the CPU restatement of its formulas
+(oracle/) on all host cores, one double + one single block per step, extrapolated x8 / x24.
+With N > 1 (torchrun) each GPU runs an independent replica (no data-path collective); the step
+time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "DiT denoise-step latency (ms)"
+UNIT = "ms/step"
+WORKLOAD = (
+    "image DiT 1024x1024 (BASELINE config 2): 4096 image + 512 text tokens, hidden 3072, "
+    "24x128 heads, 8 double + 24 single blocks, GELU-tanh MLP x4, 2D axial RoPE theta 10000, "
+    "4-step linear-sigma flow-matching Euler, batch 1, no CFG"
+)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(msg: str) -> None:
+    print(msg, file=sys.stderr, flush=True)
+
+
+def peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def step_flops(dim=3072, heads=24, nt=512, ni=4096, mlp=12288, double=8, single=24, cin=64):
+    """Algorithmic FLOPs of one transformer evaluation (projections + attention)."""
+    n = nt + ni
+    d = dim
+    dbl = 2 * n * (3 * d * d + d * d + 2 * d * mlp) + 4 * n * n * d
+    sgl = 2 * n * (3 * d * d + d * mlp) + 2 * n * (d + mlp) * d + 4 * n * n * d
+    io = 2 * ni * cin * d + 2 * ni * d * cin
+    return double * dbl + single * sgl + io
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = (
+        "index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self) -> None:
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu_index), "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL,
+            )
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.3)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        loaded = [r for r in rows if (num(r[3]) or 0) >= 50] or rows
+        sm = [num(r[1]) for r in loaded if num(r[1]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for r in loaded for j in range(4) if r[5 + j] == "Active"})
+        power = [num(r[4]) for r in loaded if num(r[4]) is not None]
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": num(rows[0][2]),
+            "reasons": reasons,
+            "samples": len(rows),
+            "samples_under_load": len(loaded),
+            "power_w_max": max(power) if power else None,
+        }
+
+
+# ----------------------------------------------------------------------------- distributed
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def physical_gpu(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [x for x in vis.split(",") if x.strip()]
+        if local < len(ids) and ids[local].strip().isdigit():
+            return int(ids[local])
+    return local
+
+
+# ----------------------------------------------------------------------------- CPU oracle sample
+def cpu_sample_ms(threads: int) -> tuple[float, str]:
+    """One double + one single block of the workload on the CPU oracle, extrapolated to a step."""
+    from oracle import flux2 as ref
+    from kinomlx_b200.flux2 import config as fcfg
+    from kinomlx_b200.synthetic import flux_weights, normal
+
+    torch.set_num_threads(threads)
+    v = fcfg.BASELINE.with_blocks(1, 1)
+    w = flux_weights(v, seed=42)
+    nt, ni = 512, 4096
+    image = normal((1, ni, v.dim), seed=1)
+    text = normal((1, nt, v.dim), seed=2)
+    ids = torch.cat([torch.zeros((1, nt, 2), dtype=torch.int64), ref.image_ids(64, 64, 2)], 1)
+    cos, sin = ref.rotary_positions(ids, v)
+    t = torch.tensor([0.5], dtype=torch.bfloat16)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        emb = ref.timestep_embedding(w, t * 1000)
+        im = ref.modulation(w, "double_stream_modulation_img", emb)
+        tm = ref.modulation(w, "double_stream_modulation_txt", emb)
+        sm = ref.modulation(w, "single_stream_modulation", emb)
+        t1 = time.perf_counter()
+        img, txt = ref.double_block(w, 0, image, text, im, tm, cos, sin, v)
+        t2 = time.perf_counter()
+        value = ref.single_block(w, 0, torch.cat([txt, img], 1), sm, cos, sin, v)
+        t3 = time.perf_counter()
+    ms = 1e3 * ((t1 - t0) + 8 * (t2 - t1) + 24 * (t3 - t2))
+    del value
+    sample = (
+        "CPU oracle (torch, bf16 values, fp32 matmul): timestep MLP + modulations + 1 double "
+        "block + 1 single block at 4096+512 tokens, extrapolated x8 double / x24 single"
+    )
+    return ms, sample
+
+
+def run_reference(args, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_sample_ms(threads)
+    times = [cpu_sample_ms(threads)[0] for _ in range(args.steps)]
+    ms = statistics.mean(times)
+    sample = (
+        "CPU restatement of the reference formulas (oracle/, torch CPU): per step 1 double + 1 "
+        "single block at 4096+512 tokens, extrapolated x8 / x24 (the reference's MLX path needs "
+        "macOS and Python >= 3.15 and cannot run on this box)"
+    )
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(ms, 3),
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "l2": "weights 9.4 GB per step exceed L2"},
+        "cpu_baseline": {"value": round(ms, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(ms, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_kino(args, world: int, rank: int, local: int) -> None:
+    from kinomlx_b200 import ops
+    from kinomlx_b200.flux2 import config as fcfg
+    from kinomlx_b200.flux2 import sampling
+    from kinomlx_b200.flux2.transformer import Flux2Transformer
+    from kinomlx_b200.synthetic import flux_weights, normal
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    v = fcfg.BASELINE
+    nt, side = 512, 64
+    ni = side * side
+    weights = flux_weights(v, seed=42, device=device)
+    model = Flux2Transformer(weights, v, device)
+    del weights
+    torch.cuda.empty_cache()
+    noise = normal((1, ni, v.in_channels), seed=43, device=device)
+    text = normal((1, nt, v.context_dim), seed=44, device=device)
+    ids = torch.zeros((1, nt + ni, 2), dtype=torch.int64)
+    ids[0, nt:, 0] = torch.arange(side).repeat_interleave(side)
+    ids[0, nt:, 1] = torch.arange(side).repeat(side)
+    sigmas = sampling.linear_sigmas(4)
+    prepared = model.prepare(text, ids)
+    current = noise.clone()
+    nsched = len(sigmas) - 1
+
+    for i in range(args.warmup):
+        sampling.denoise_step(model, prepared, current, sigmas, i % nsched)
+    torch.cuda.synchronize()
+    ops.device_status()
+
+    # ---- timed region: K device-resident steps, nothing else on the stream
+    sampler = ClockSampler(physical_gpu(local)) if rank == 0 else None
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+    launches0 = ops.launches
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        sampling.denoise_step(model, prepared, current, sigmas, i % nsched)
+    end.record()
+    torch.cuda.synchronize()
+    launches = ops.launches - launches0
+    barrier(world)
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
+    ops.device_status()
+    if not bool(torch.isfinite(current).all()):
+        raise FloatingPointError("non-finite latent in the benchmark")
+
+    # ---- the same K steps again with CUDA events around every launch (per-kernel durations on
+    # the launching stream); kept out of the timed region because the events add ~3% gaps
+    launch_log = ops.LaunchLog()
+    ops.set_launch_log(launch_log)
+    for i in range(args.steps):
+        sampling.denoise_step(model, prepared, current, sigmas, i % nsched)
+    torch.cuda.synchronize()
+    ops.set_launch_log(None)
+
+    # ---- e2e: the public step API with pinned host input/output copies inside the region
+    host_in = noise.cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    dev_cur = torch.empty_like(noise)
+    barrier(world)
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for i in range(args.steps):
+        dev_cur.copy_(host_in, non_blocking=True)
+        sampling.denoise_step(model, prepared, dev_cur, sigmas, i % nsched)
+        host_out.copy_(dev_cur, non_blocking=True)
+    e_end.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end) / args.steps, world)
+    io_bytes = host_in.numel() * host_in.element_size()
+
+    # ---- roofline of the dominant kernel class inside the timed region
+    summary = launch_log.summary()
+    total_ms = sum(s["ms"] for s in summary.values()) or 1.0
+    kernels = {
+        k: {"launches": int(s["launches"]), "ms": round(s["ms"], 3),
+            "share": round(s["ms"] / total_ms, 4),
+            "tflops": round(s["flops"] / (s["ms"] * 1e9), 1) if s["flops"] else None,
+            "gbs": round(s["bytes"] / (s["ms"] * 1e6), 1) if s["bytes"] else None}
+        for k, s in sorted(summary.items(), key=lambda kv: -kv[1]["ms"])
+    }
+    dom = max(summary, key=lambda k: summary[k]["ms"])
+    pk, source = peaks()
+    d = summary[dom]
+    if d["flops"]:
+        achieved = d["flops"] / (d["ms"] * 1e9)  # TFLOP/s
+        peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+        bound, unit = "tensor", "TFLOP/s"
+        per_launch_flops = d["flops"] / d["launches"]
+    else:
+        achieved = d["bytes"] / (d["ms"] * 1e6)
+        peak = float(pk["hbm_gbs"])
+        bound, unit = "hbm", "GB/s"
+        per_launch_flops = None
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.txt"
+    if tf.exists():
+        for line in tf.read_text().splitlines():
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == dom:
+                try:
+                    traffic = float(parts[1])
+                except ValueError:
+                    traffic = None
+    roofline = {
+        "kernel": dom,
+        "bound": bound,
+        "achieved": round(achieved, 1),
+        "peak": peak,
+        "unit": unit,
+        "frac": round(achieved / peak, 4),
+        "peak_source": f"{source} ({'sustained' if bound == 'tensor' else 'copy'})",
+        "traffic": traffic,
+        "algorithmic_per_launch": per_launch_flops,
+        "step_tflops": round(step_flops() / (ms * 1e9), 1),
+        "timing": "per-launch CUDA events over a second pass of the same K steps",
+    }
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        cms, sample = cpu_sample_ms(threads)
+        cpu = {"value": round(cms, 1), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": round(ms, 3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 3),
+            "higher_is_better": False,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) latents and text, random-init N(0,0.02) weights)",
+            "config": {
+                "workload": WORKLOAD,
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "l2": "no flush: 9.4 GB of weights stream per step, inputs exceed the 126 MB L2",
+                "step_gflop": round(step_flops() / 1e9, 1),
+            },
+            "e2e": {"value": round(e2e_ms, 3), "unit": UNIT, "h2d_bytes_per_step": io_bytes,
+                    "d2h_bytes_per_step": io_bytes},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "gpu_launches": launches,
+            "kernels": kernels,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_kernel_case(case: str) -> None:
+    """One launch of one kernel at the workload's largest shape (for ncu captures): `gemm` is the
+    single block's fused projection (4608 x 21504 x 3072, GELU epilogue), `attention` the joint
+    attention over 4608 tokens x 24 heads. Inputs exceed the L2 (weights 132 MB)."""
+    from kinomlx_b200 import ops
+    from kinomlx_b200.synthetic import normal
+
+    dev = torch.device("cuda", 0)
+    n, d = 4608, 3072
+    if case == "gemm":
+        x = normal((1, n, d), seed=1, device=dev)
+        w = normal((3 * d + 4 * d, d), seed=2, device=dev, std=0.02)
+        out = torch.empty((1, n, 7 * d), device=dev, dtype=torch.bfloat16)
+        for _ in range(3):
+            ops.linear(x, w, out, kind=ops.EPI_GELU, act_col_begin=3 * d)
+    else:
+        qkv = normal((1, n, 3 * d), seed=3, device=dev)
+        q, k, v = qkv[..., :d], qkv[..., d : 2 * d], qkv[..., 2 * d :]
+        out = torch.empty((1, n, d), device=dev, dtype=torch.bfloat16)
+        for _ in range(3):
+            ops.attention([q], [k], [v], [out], heads=24)
+    torch.cuda.synchronize()
+    ops.device_status()
+    print(json.dumps({"kernel_case": case, "ok": True}))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["kino", "reference"], default="kino")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--kernel-case", choices=["gemm", "attention"],
+                    help="run 3 launches of one kernel and exit (for ncu captures)")
+    args = ap.parse_args()
+    if args.kernel_case:
+        run_kernel_case(args.kernel_case)
+        return
+    if args.warmup < 3:
+        log("warm-up raised to 3 steps (timing rule)")
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return
+    world, rank, local = dist_setup()
+    try:
+        run_kino(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

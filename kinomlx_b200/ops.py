@@ -58,6 +58,55 @@ __all__ = [
 ]
 
 
+class LaunchLog:
+    """Optional record of every kino_* launch: CUDA events on the launching stream around each
+    call, with the launch's algorithmic FLOPs and bytes. Used by the benchmark to time the
+    dominant kernel inside its timed region; off (None) by default."""
+
+    def __init__(self) -> None:
+        self.records: list[tuple[str, torch.cuda.Event, torch.cuda.Event, float, float]] = []
+
+    def summary(self) -> dict[str, dict[str, float]]:
+        """Per kernel class: launches, total ms, FLOPs and bytes (after a synchronize)."""
+        out: dict[str, dict[str, float]] = {}
+        for label, start, end, flops, nbytes in self.records:
+            entry = out.setdefault(label, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
+            entry["launches"] += 1
+            entry["ms"] += start.elapsed_time(end)
+            entry["flops"] += flops
+            entry["bytes"] += nbytes
+        return out
+
+
+_log: LaunchLog | None = None
+launches = 0  # kino_* launches issued by this process
+
+
+def set_launch_log(log: LaunchLog | None) -> None:
+    global _log
+    _log = log
+
+
+class _timed:
+    def __init__(self, label: str, flops: float = 0.0, nbytes: float = 0.0):
+        self.label, self.flops, self.nbytes = label, flops, nbytes
+
+    def __enter__(self):
+        global launches
+        launches += 1
+        if _log is not None:
+            self.start = torch.cuda.Event(enable_timing=True)
+            self.end = torch.cuda.Event(enable_timing=True)
+            self.start.record()
+        return self
+
+    def __exit__(self, *exc):
+        if _log is not None and exc[0] is None:
+            self.end.record()
+            _log.records.append((self.label, self.start, self.end, self.flops, self.nbytes))
+        return False
+
+
 def _ptr(t: torch.Tensor | None) -> ctypes.c_void_p | None:
     return None if t is None else ctypes.c_void_p(t.data_ptr())
 
@@ -139,23 +188,24 @@ def linear(
         epi.ld_aux = s3.stride(1)
         epi.bs_aux = s3.stride(0)
         epi.scalar = dt
-    _lib.call(
-        "kino_linear",
-        _ptr(x3),
-        _ptr(w),
-        _ptr(o3),
-        batch,
-        m,
-        n,
-        k,
-        x3.stride(1),
-        x3.stride(0),
-        w.stride(0),
-        o3.stride(1),
-        o3.stride(0),
-        ctypes.byref(epi),
-        _stream(),
-    )
+    with _timed("gemm", 2.0 * batch * m * n * k, 2.0 * (batch * m * k + n * k + batch * m * n)):
+        _lib.call(
+            "kino_linear",
+            _ptr(x3),
+            _ptr(w),
+            _ptr(o3),
+            batch,
+            m,
+            n,
+            k,
+            x3.stride(1),
+            x3.stride(0),
+            w.stride(0),
+            o3.stride(1),
+            o3.stride(0),
+            ctypes.byref(epi),
+            _stream(),
+        )
     return out
 
 
@@ -175,20 +225,21 @@ def gemv(
     n = w.shape[0]
     if out is None:
         out = torch.empty((batch, n), device=x.device, dtype=torch.bfloat16)
-    _lib.call(
-        "kino_gemv",
-        _ptr(x2),
-        x2.stride(0),
-        _ptr(w),
-        _ptr(bias),
-        _ptr(out),
-        out.stride(0),
-        batch,
-        n,
-        k,
-        1 if silu_input else 0,
-        _stream(),
-    )
+    with _timed("gemv", 2.0 * batch * n * k, 2.0 * n * k):
+        _lib.call(
+            "kino_gemv",
+            _ptr(x2),
+            x2.stride(0),
+            _ptr(w),
+            _ptr(bias),
+            _ptr(out),
+            out.stride(0),
+            batch,
+            n,
+            k,
+            1 if silu_input else 0,
+            _stream(),
+        )
     return out
 
 
@@ -236,7 +287,11 @@ def attention(
         args.bs_k[s] = k3.stride(0)
         args.ld_v[s] = v3.stride(1)
         args.bs_v[s] = v3.stride(0)
-    _lib.call("kino_attention", ctypes.byref(args), _stream())
+    nq = sum(int(args.q_tokens[i]) for i in range(args.n_q))
+    nk = sum(int(args.kv_tokens[i]) for i in range(args.n_kv))
+    flops = 4.0 * args.batch * heads * nq * nk * args.head_dim
+    with _timed("attention", flops, 2.0 * args.batch * heads * args.head_dim * (2 * nq + 2 * nk)):
+        _lib.call("kino_attention", ctypes.byref(args), _stream())
     return out
 
 
@@ -262,24 +317,25 @@ def adaln(
     sc = scale.reshape(-1, dim)
     if sh.stride(0) != sc.stride(0):
         raise ValueError("shift and scale need the same batch stride")
-    _lib.call(
-        "kino_adaln",
-        _ptr(x3),
-        x3.stride(1),
-        x3.stride(0),
-        _ptr(sh),
-        _ptr(sc),
-        sh.stride(0) if sh.shape[0] > 1 else 0,
-        _ptr(o3),
-        o3.stride(1),
-        o3.stride(0),
-        batch,
-        rows,
-        dim,
-        norm,
-        eps,
-        _stream(),
-    )
+    with _timed("adaln", 0.0, 2.0 * 2 * batch * rows * dim):
+        _lib.call(
+            "kino_adaln",
+            _ptr(x3),
+            x3.stride(1),
+            x3.stride(0),
+            _ptr(sh),
+            _ptr(sc),
+            sh.stride(0) if sh.shape[0] > 1 else 0,
+            _ptr(o3),
+            o3.stride(1),
+            o3.stride(0),
+            batch,
+            rows,
+            dim,
+            norm,
+            eps,
+            _stream(),
+        )
     return out
 
 
@@ -297,17 +353,18 @@ def rms_norm(
     if out is None:
         out = torch.empty_like(x)
     dim = x.shape[-1]
-    _lib.call(
-        "kino_rms_norm",
-        _ptr(x),
-        _ptr(weight),
-        _ptr(out),
-        x.numel() // dim,
-        dim,
-        eps,
-        weight_offset,
-        _stream(),
-    )
+    with _timed("rms_norm", 0.0, 4.0 * x.numel()):
+        _lib.call(
+            "kino_rms_norm",
+            _ptr(x),
+            _ptr(weight),
+            _ptr(out),
+            x.numel() // dim,
+            dim,
+            eps,
+            weight_offset,
+            _stream(),
+        )
     return out
 
 
@@ -340,25 +397,26 @@ def qk_norm_rope(
             raise ValueError("RoPE tables must be contiguous")
         table_tokens = cos.shape[-2]
         table_batched = int(cos.shape[0] > 1 and cos.dim() >= 3)
-    _lib.call(
-        "kino_qk_norm_rope",
-        _ptr(x3),
-        x3.stride(1),
-        x3.stride(0),
-        batch,
-        tokens,
-        heads,
-        _ptr(weight),
-        norm,
-        rope,
-        _ptr(cos),
-        _ptr(sin),
-        table_batched,
-        table_tokens,
-        table_offset,
-        eps,
-        _stream(),
-    )
+    with _timed("qk_norm_rope", 0.0, 4.0 * batch * tokens * width + 2 * 4.0 * tokens * 128):
+        _lib.call(
+            "kino_qk_norm_rope",
+            _ptr(x3),
+            x3.stride(1),
+            x3.stride(0),
+            batch,
+            tokens,
+            heads,
+            _ptr(weight),
+            norm,
+            rope,
+            _ptr(cos),
+            _ptr(sin),
+            table_batched,
+            table_tokens,
+            table_offset,
+            eps,
+            _stream(),
+        )
     return x
 
 
@@ -372,24 +430,26 @@ def split_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     # keep the contiguous copies alive until the launch is queued
     x, cos, sin = x.contiguous(), cos.contiguous(), sin.contiguous()
     out = torch.empty_like(x)
-    _lib.call(
-        "kino_split_rope",
-        _ptr(x),
-        _ptr(cos),
-        _ptr(sin),
-        _ptr(out),
-        batch,
-        tokens,
-        heads,
-        half,
-        int(table_batch == batch and batch > 1),
-        _stream(),
-    )
+    with _timed("split_rope", 0.0, 4.0 * x.numel() + 8.0 * cos.numel()):
+        _lib.call(
+            "kino_split_rope",
+            _ptr(x),
+            _ptr(cos),
+            _ptr(sin),
+            _ptr(out),
+            batch,
+            tokens,
+            heads,
+            half,
+            int(table_batch == batch and batch > 1),
+            _stream(),
+        )
     return out
 
 
 def _elementwise(name: str, *args: object) -> None:
-    _lib.call(name, *args, _stream())
+    with _timed("elementwise"):
+        _lib.call(name, *args, _stream())
 
 
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:

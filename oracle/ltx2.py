@@ -1,0 +1,238 @@
+"""LTX-2 video DiT (video stream only) restated on the CPU (test oracle).
+
+Follows kinomlx/models/ltx2/transformer/{rope,attention,feed_forward,timestep,transformer,model,
+wrappers}.py, kinomlx/models/ltx2/patchifier.py and kinomlx/samplers/steps.py. Every bf16
+operation rounds where the reference's MLX operation does; fp32-opmath kernels round once.
+"""
+
+from __future__ import annotations
+
+import math
+import struct
+from dataclasses import dataclass
+
+import torch
+
+from .fused_ops import gelu_approx, layer_norm, linear, rms_norm, sdpa, silu
+
+
+@dataclass(frozen=True)
+class LTXVariant:
+    dim: int = 4096
+    heads: int = 32
+    head_dim: int = 128
+    context_dim: int = 4096
+    ff_mult: int = 4
+    gated_attention: bool = True
+    eps: float = 1e-6
+    theta: float = 10000.0
+    max_pos: tuple[int, int, int] = (20, 2048, 2048)
+    in_channels: int = 128
+    out_channels: int = 128
+    blocks: int = 48
+    timestep_scale: float = 1000.0
+
+
+def _f32(x: float) -> float:
+    return struct.unpack("<f", struct.pack("<f", x))[0]
+
+
+# kinomlx/models/ltx2/sigmas.py:24-52
+DISTILLED_STAGE_1_SIGMAS = tuple(
+    _f32(x) for x in (1.0, 0.99375, 0.9875, 0.98125, 0.975, 0.909375, 0.725, 0.421875, 0.0)
+)
+DISTILLED_STAGE_2_SIGMAS = tuple(_f32(x) for x in (0.909375, 0.725, 0.421875, 0.0))
+
+
+# ----------------------------------------------------------------------------- positions / RoPE
+def patch_grid_bounds(frames: int, height: int, width: int) -> torch.Tensor:
+    """(1, 3, N, 2) latent-grid start/end bounds for patch size 1, row-major (f, h, w)
+    (kinomlx/models/ltx2/patchifier.py:102-118)."""
+    f, h, w = torch.meshgrid(torch.arange(frames), torch.arange(height), torch.arange(width),
+                             indexing="ij")
+    starts = torch.stack([f, h, w]).reshape(3, -1)
+    return torch.stack([starts, starts + 1], dim=-1)[None].to(torch.float32)
+
+
+def pixel_coords(latent: torch.Tensor, scale=(8, 32, 32), causal_fix: bool = True,
+                 fps: float = 24.0) -> torch.Tensor:
+    """Latent bounds to pixel bounds, causal fix on time, time divided by fps
+    (kinomlx/models/ltx2/patchifier.py:121-146, kinomlx/models/ltx2/conditioning/tools.py:63-74)."""
+    s = torch.tensor(scale, dtype=torch.float32).reshape(1, 3, 1, 1)
+    pix = latent * s
+    if causal_fix:
+        t = torch.clamp(pix[:, 0] + 1 - scale[0], min=0)
+        pix = torch.cat([t[:, None], pix[:, 1:]], dim=1)
+    pix = pix.to(torch.float32)
+    return torch.cat([pix[:, 0:1] / fps, pix[:, 1:]], dim=1)
+
+
+def frequency_grid(theta: float, axes: int, inner_dim: int) -> tuple[float, ...]:
+    """theta^(i/(n-1)) * pi/2 in host double precision (kinomlx/models/ltx2/transformer/rope.py:75-92)."""
+    count = inner_dim // (2 * axes)
+    exps = (0.0,) if count == 1 else tuple(i / (count - 1) for i in range(count))
+    return tuple(math.pow(theta, e) * math.pi / 2 for e in exps)
+
+
+def precompute_freqs_cis(
+    positions: torch.Tensor,
+    *,
+    dim: int,
+    theta: float = 10000.0,
+    max_pos: tuple[int, ...] = (20, 2048, 2048),
+    heads: int = 32,
+    middle: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split-RoPE cos/sin tables (B, heads, T, dim/(2*heads)) in fp32
+    (kinomlx/models/ltx2/transformer/rope.py:95-176)."""
+    if middle:
+        pos = (positions[..., 0] + positions[..., 1]) / 2.0
+    else:
+        pos = positions[..., 0]
+    scale = torch.tensor(max_pos, dtype=torch.float32)[None, :, None]
+    frac = (pos.to(torch.float32) / scale).transpose(1, 2)  # (B, T, axes)
+    grid = torch.tensor(frequency_grid(theta, positions.shape[1], dim), dtype=torch.float32)
+    scaled = frac * 2.0 - 1.0
+    freqs = scaled[..., None] * grid[None, None, None, :]  # (B, T, axes, count)
+    freqs = freqs.transpose(2, 3).reshape(freqs.shape[0], freqs.shape[1], -1)
+    pad = dim // 2 - freqs.shape[-1]
+    cos, sin = torch.cos(freqs), torch.sin(freqs)
+    if pad:
+        cos = torch.cat([torch.ones((*cos.shape[:-1], pad)), cos], dim=-1)
+        sin = torch.cat([torch.zeros((*sin.shape[:-1], pad)), sin], dim=-1)
+    b, t, _ = cos.shape
+    cos = cos.reshape(b, t, heads, -1).transpose(1, 2)
+    sin = sin.reshape(b, t, heads, -1).transpose(1, 2)
+    return cos.contiguous(), sin.contiguous()
+
+
+def apply_split_rotary_emb(value: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Split-half rotation on flattened heads with fp32 tables (B|1, H, T, D/2): one fp32 rounding
+    per product, then the difference or sum, then the cast
+    (kinomlx/models/ltx2/transformer/rope.py:18-61, kinomlx/kernels/split_rope.py:35-56, 87-98)."""
+    b, t, _ = value.shape
+    heads, half = cos.shape[1], cos.shape[-1]
+    hf = value.reshape(b, t, heads, 2 * half).transpose(1, 2).float()
+    first, second = hf[..., :half], hf[..., half:]
+    out = torch.cat([first * cos - second * sin, first * sin + second * cos], dim=-1)
+    return out.transpose(1, 2).reshape(value.shape).to(value.dtype)
+
+
+# ----------------------------------------------------------------------------- timestep / AdaLN
+def timestep_features(t: torch.Tensor, dim: int = 256) -> torch.Tensor:
+    """Canonical cos-then-sin features in fp32 (kinomlx/models/ltx2/transformer/timestep.py:13-28)."""
+    half = dim // 2
+    exponent = -math.log(10000) * torch.arange(half, dtype=torch.float32) / half
+    angles = t[:, None].to(torch.float32) * torch.exp(exponent)[None, :]
+    return torch.cat([torch.cos(angles), torch.sin(angles)], dim=-1)
+
+
+def adaln_single(p: dict, prefix: str, t: torch.Tensor, dtype: torch.dtype):
+    """AdaLayerNormSingle: timestep MLP then linear(silu(emb)) (timestep.py:31-85)."""
+    x = timestep_features(t).to(dtype)
+    x = silu(linear(x, p[f"{prefix}.emb.timestep_embedder.linear_1.weight"],
+                    p[f"{prefix}.emb.timestep_embedder.linear_1.bias"]))
+    emb = linear(x, p[f"{prefix}.emb.timestep_embedder.linear_2.weight"],
+                 p[f"{prefix}.emb.timestep_embedder.linear_2.bias"])
+    mod = linear(silu(emb), p[f"{prefix}.linear.weight"], p[f"{prefix}.linear.bias"])
+    return mod, emb
+
+
+def adaln(value, scale, shift, eps):
+    """rms_norm(x) * (1 + scale) + shift in bf16 ops (ltx2/transformer/transformer.py:16-23)."""
+    return (rms_norm(value, None, eps) * (1.0 + scale) + shift).to(value.dtype)
+
+
+# ----------------------------------------------------------------------------- attention / FF
+def attention(p: dict, prefix: str, x: torch.Tensor, v: LTXVariant, *, context=None, pe=None):
+    """Gated attention with Q/K RMSNorm over all heads and split RoPE
+    (kinomlx/models/ltx2/transformer/attention.py:249-371)."""
+    g = lambda name: p[f"{prefix}.{name}"]
+    gate = None
+    if v.gated_attention:
+        gate = 2.0 * torch.sigmoid(linear(x, g("to_gate_logits.weight"), g("to_gate_logits.bias")).float()).to(x.dtype)
+    src = x if context is None else context
+    value = linear(src, g("to_v.weight"), g("to_v.bias"))
+    q = rms_norm(linear(x, g("to_q.weight"), g("to_q.bias")), g("q_norm.weight"), v.eps)
+    k = rms_norm(linear(src, g("to_k.weight"), g("to_k.bias")), g("k_norm.weight"), v.eps)
+    if pe is not None:
+        q = apply_split_rotary_emb(q, *pe)
+        k = apply_split_rotary_emb(k, *pe)
+    b, tq, _ = q.shape
+    tk = k.shape[1]
+    heads, d = v.heads, v.head_dim
+    out = sdpa(q.reshape(b, tq, heads, d).transpose(1, 2), k.reshape(b, tk, heads, d).transpose(1, 2),
+               value.reshape(b, tk, heads, d).transpose(1, 2), d ** -0.5)
+    out = out.transpose(1, 2)
+    if gate is not None:
+        out = out * gate[..., None]
+    out = out.reshape(b, tq, heads * d)
+    return linear(out, g("to_out.weight"), g("to_out.bias"))
+
+
+def feed_forward(p: dict, prefix: str, x: torch.Tensor) -> torch.Tensor:
+    """proj -> GELU-tanh (fp32 opmath) -> proj (ltx2/transformer/feed_forward.py:37-97)."""
+    h = gelu_approx(linear(x, p[f"{prefix}.project_in.proj.weight"], p[f"{prefix}.project_in.proj.bias"]))
+    return linear(h, p[f"{prefix}.project_out.weight"], p[f"{prefix}.project_out.bias"])
+
+
+def video_block(p: dict, i: int, x, context, timesteps, prompt_timestep, pe, v: LTXVariant):
+    """BasicAVTransformerBlock, video stream without audio (ltx2/transformer/transformer.py:178-392).
+    timesteps: (B, 1, 9, D) modulation; prompt_timestep: (B, 1, 2, D)."""
+    a = f"transformer_blocks.{i}"
+    table = p[f"{a}.scale_shift_table"]
+    vals = (table[None, None] + timesteps)  # bf16 op
+    shift, scale, gate = vals[:, :, 0], vals[:, :, 1], vals[:, :, 2]
+    normalized = adaln(x, scale, shift, v.eps)
+    attended = attention(p, f"{a}.attn1", normalized, v, pe=pe)
+    x = (x + attended * gate).to(x.dtype)
+    shift_q, scale_q, gate_c = vals[:, :, 6], vals[:, :, 7], vals[:, :, 8]
+    prompt = p[f"{a}.prompt_scale_shift_table"][None, None] + prompt_timestep
+    shift_ctx, scale_ctx = prompt[:, :, 0], prompt[:, :, 1]
+    query = adaln(x, scale_q, shift_q, v.eps)
+    ctx = (context * (1.0 + scale_ctx) + shift_ctx).to(context.dtype)
+    cross = attention(p, f"{a}.attn2", query, v, context=ctx)
+    x = (x + (cross * gate_c).to(x.dtype)).to(x.dtype)
+    shift, scale, gate = vals[:, :, 3], vals[:, :, 4], vals[:, :, 5]
+    normalized = adaln(x, scale, shift, v.eps)
+    return (x + feed_forward(p, f"{a}.ff", normalized) * gate).to(x.dtype)
+
+
+def forward(p: dict, latent, context, sigma: float, positions, v: LTXVariant, dtype=torch.bfloat16):
+    """LTXAVModel.__call__ for the video modality with a uniform timestep
+    (ltx2/transformer/model.py:577-635, preprocessing.py:134-213)."""
+    b = latent.shape[0]
+    hidden = linear(latent, p["patchify_proj.weight"], p["patchify_proj.bias"])
+    t = torch.full((b,), sigma, dtype=torch.float32)
+    mod, emb = adaln_single(p, "adaln_single", t * v.timestep_scale, dtype)
+    timesteps = mod.reshape(b, -1, 9, v.dim)
+    emb = emb.reshape(b, -1, v.dim)
+    pmod, _ = adaln_single(p, "prompt_adaln_single", t * v.timestep_scale, dtype)
+    prompt = pmod.reshape(b, -1, 2, v.dim)
+    pe = precompute_freqs_cis(positions, dim=v.dim, theta=v.theta, max_pos=v.max_pos, heads=v.heads)
+    for i in range(v.blocks):
+        hidden = video_block(p, i, hidden, context, timesteps, prompt, pe, v)
+    modulation = (p["scale_shift_table"][None, None] + emb[:, :, None, :]).to(hidden.dtype)
+    shift, scale = modulation[:, :, 0], modulation[:, :, 1]
+    hidden = (layer_norm(hidden, v.eps) * (1.0 + scale) + shift).to(hidden.dtype)
+    return linear(hidden, p["proj_out.weight"], p["proj_out.bias"])
+
+
+def to_denoised(latent, sigma: float, velocity):
+    """x0 = x - t * v in fp32 (ltx2/transformer/wrappers.py:49-65)."""
+    return (latent.float() - torch.tensor(sigma, dtype=torch.float32) * velocity.float()).to(latent.dtype)
+
+
+def euler_step(sample, denoised, sigma: float, sigma_next: float):
+    """denoised + (s'/s)(sample - denoised) in fp32 (kinomlx/samplers/steps.py:36-70)."""
+    ratio = torch.tensor(sigma_next / sigma, dtype=torch.float32)
+    return (denoised.float() + ratio * (sample.float() - denoised.float())).to(sample.dtype)
+
+
+def denoise(p, latent, context, positions, sigmas, v: LTXVariant):
+    """Deterministic-Euler loop (kinomlx/models/ltx2/denoise.py:159-365)."""
+    x = latent
+    for s, n in zip(sigmas[:-1], sigmas[1:]):
+        velocity = forward(p, x, context, s, positions, v)
+        x = euler_step(x, to_denoised(x, s, velocity), s, n)
+    return x

@@ -1,0 +1,104 @@
+"""CPU-side checks of the boundary and the host logic: the C-ABI library loads and exports every
+symbol include/kino.h declares (no compute calls), the torch front end refuses what the kernels
+cannot take, and the host-side scalar math matches the oracle."""
+
+from __future__ import annotations
+
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _declared() -> list[str]:
+    text = (ROOT / "include" / "kino.h").read_text()
+    return sorted(set(re.findall(r"^\s*(?:kino_status|int|const char\*)\s+(kino_\w+)\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    from kinomlx_b200 import _lib
+
+    lib = _lib.load()
+    names = _declared()
+    assert len(names) >= 15
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert lib.kino_abi_version() == 1
+    assert _lib.last_error() == ""
+
+
+def test_ops_refuse_cpu_tensors():
+    from kinomlx_b200 import ops
+
+    x = torch.zeros((4, 16), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.linear(x, x)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gelu_tanh(x)
+
+
+def test_reference_surface_refusals():
+    from kinomlx_b200.kernels import dense_attention, mpp_linear, split_rope
+
+    q = torch.zeros((5, 2 * 64), dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        dense_attention.dense_attention(q, q, q, heads=2)  # 64-wide heads are not built
+    assert not dense_attention.applies(q[None], q[None], heads=2)
+    v = torch.zeros((2, 5, 32), dtype=torch.bfloat16)
+    cos = torch.zeros((1, 2, 5, 8))
+    assert not split_rope.applies(v, cos.half(), cos.half())
+    with pytest.raises(ValueError, match="does not apply"):
+        split_rope.rotate(v, cos.half(), cos.half())
+    assert not mpp_linear.supports(10, 12, 16, transposed=True, dtype=torch.bfloat16)
+    assert mpp_linear.supports(10, 16, 16, transposed=True, dtype=torch.bfloat16)
+
+
+def test_host_schedule_and_timestep_match_oracle():
+    from oracle import flux2 as ref
+    from kinomlx_b200.flux2 import sampling
+
+    for tokens, steps in [(1024, 4), (4096, 28), (4301, 10)]:
+        assert torch.equal(sampling.schedule(tokens, steps), ref.schedule(tokens, steps))
+    sig = sampling.linear_sigmas(4)
+    assert torch.equal(sig, ref.linear_sigmas(4))
+    for i in range(4):
+        t = ref.step_timestep(sig, i, torch.bfloat16)
+        assert float(sampling.timestep_x1000(sig, i)) == float((t * 1000).float())
+        assert sampling.step_delta(sig, i) == float(sig[i + 1] - sig[i])
+
+
+def test_rotary_tables_match_oracle():
+    from oracle import flux2 as ref
+    from kinomlx_b200.flux2 import config
+    from kinomlx_b200.flux2.transformer import rotary_positions
+
+    ids = torch.cat([torch.zeros((1, 7, 2), dtype=torch.int64), ref.image_ids(5, 6, 2)], 1)
+    cos, sin = rotary_positions(ids, config.BASELINE)
+    rc, rs = ref.rotary_positions(ids, config.BASELINE)
+    assert torch.equal(cos, rc[:, :, 0]) and torch.equal(sin, rs[:, :, 0])
+    ids4 = torch.randint(0, 50, (1, 9, 4))
+    cos, _ = rotary_positions(ids4, config.KLEIN)
+    assert torch.equal(cos, ref.rotary_positions(ids4, config.KLEIN)[0][:, :, 0])
+
+
+def test_synthetic_weights_are_seeded_and_shaped():
+    from kinomlx_b200.flux2 import config
+    from kinomlx_b200.synthetic import flux_weight_specs, flux_weights
+
+    v = config.BASELINE.with_blocks(1, 1)
+    specs = flux_weight_specs(v)
+    names = [s[0] for s in specs]
+    assert len(names) == len(set(names))
+    assert ("single_transformer_blocks.0.attn.to_qkv_mlp_proj.weight", (7 * 3072, 3072), "normal") in specs
+    small = config.FluxVariant(dim=256, heads=2, mlp="gelu_tanh", mlp_hidden=1024, rope_axes=(64, 64),
+                               rope_theta=1e4, in_channels=64, context_dim=128, double_blocks=1,
+                               single_blocks=1)
+    a = flux_weights(small, seed=3)
+    b = flux_weights(small, seed=3)
+    assert all(torch.equal(a[k], b[k]) for k in a)
+    assert float(a["x_embedder.weight"].float().std()) == pytest.approx(0.02, rel=0.1)
+    assert torch.equal(a["transformer_blocks.0.attn.norm_q.weight"], torch.ones(128, dtype=torch.bfloat16))
