@@ -30,7 +30,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header; bumped on any signature change. */
+/* ABI version of this header (2); bumped on any signature change. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -50,6 +50,8 @@ int kino_num_sms(void);
 #define KINO_EPI_GATED_RESIDUAL 2 /* out = residual + bf16(gate[b] * bf16(acc + bias)) */
 #define KINO_EPI_EULER 3          /* out = aux + bf16(bf16(scalar) * bf16(acc + bias)), fp32 add */
 #define KINO_EPI_SIGMOID2 4       /* out = 2 * sigmoid(bf16(acc + bias)) */
+#define KINO_EPI_EULER_X0 5       /* v = bf16(acc + bias); x0 = bf16(aux - scalar * v);
+                                     out = x0 + scalar2 * (aux - x0), fp32 (LTX X0 + Euler) */
 
 typedef struct kino_epilogue {
   int kind;                /* KINO_EPI_* */
@@ -61,9 +63,10 @@ typedef struct kino_epilogue {
   int64_t bs_gate;
   int64_t act_col_begin;   /* GELU: first column the activation applies to */
   float scalar;            /* EULER: dt = sigma_next - sigma (fp32) */
-  const void* aux;         /* EULER: current sample, bf16, geometry of out */
+  const void* aux;         /* EULER, EULER_X0: current sample, bf16, geometry of out */
   int64_t ld_aux;
   int64_t bs_aux;
+  float scalar2;           /* EULER_X0: fp32(sigma_next / sigma); `scalar` holds sigma */
 } kino_epilogue;
 
 /* out[b, i, j] = epilogue(sum_k x[b, i, k] * w[j, k]) on tcgen05 tensor cores.
@@ -93,6 +96,9 @@ typedef struct kino_attention_args {
   void* out[2];            /* output of segment s, token-major, may alias q[s] */
   int64_t q_tokens[2];
   int64_t ld_q[2], bs_q[2], ld_out[2], bs_out[2];
+  const void* gate[2];     /* optional (batch, tokens, heads) bf16 output gate per query segment:
+                              out = bf16(bf16(attention) * gate) (LTX gated heads) */
+  int64_t ld_gate[2], bs_gate[2];
   int n_kv;                /* 1 or 2 key/value segments */
   const void* k[2];
   const void* v[2];
@@ -115,6 +121,7 @@ kino_status kino_dense_attention(const void* q, const void* k, const void* v, vo
 /* ------------------------------------------------------------------ norms and rotary */
 #define KINO_NORM_RMS 0
 #define KINO_NORM_LAYER 1
+#define KINO_NORM_NONE 2   /* modulation only: x * (1 + scale) + shift */
 
 /* out = norm(x) * (1 + scale[b]) + shift[b], norm without affine, fp32 statistics.
  * x: batch x rows x dim (ldx, bsx); shift/scale: [batch][dim] at batch stride bs_mod.
@@ -172,6 +179,11 @@ kino_status kino_euler_velocity(const void* x, const void* v, float dt, void* ou
  * kinomlx/samplers/steps.py:36-70). */
 kino_status kino_euler_x0(const void* x, const void* v, float sigma, float ratio, void* out,
                           int64_t n, void* stream);
+
+/* out[r, c] = bf16(a[r, c] + b[c]); a: rows x n, b: n. The per-block modulation tables plus the
+ * step's timestep projection (kinomlx/models/ltx2/transformer/transformer.py:178-186). n % 8 == 0. */
+kino_status kino_add_rows(const void* a, const void* b, void* out, int64_t rows, int64_t n,
+                          void* stream);
 
 /* [cos(t f_i), sin(t f_i)] features, f_i = exp(-ln(10000) i / (dim/2)); t: fp32 device [batch].
  * Replaces kinomlx/models/flux2/transformer.py:238-241 and

@@ -31,9 +31,11 @@ EPI_GELU = 1
 EPI_GATED_RESIDUAL = 2
 EPI_EULER = 3
 EPI_SIGMOID2 = 4
+EPI_EULER_X0 = 5
 
 NORM_RMS = 0
 NORM_LAYER = 1
+NORM_NONE = 2
 
 QKNORM_NONE = 0
 QKNORM_PER_HEAD = 1
@@ -57,6 +59,7 @@ class Epilogue(ctypes.Structure):
         ("aux", c_void_p),
         ("ld_aux", c_int64),
         ("bs_aux", c_int64),
+        ("scalar2", c_float),
     ]
 
 
@@ -74,6 +77,9 @@ class AttentionArgs(ctypes.Structure):
         ("bs_q", c_int64 * 2),
         ("ld_out", c_int64 * 2),
         ("bs_out", c_int64 * 2),
+        ("gate", c_void_p * 2),
+        ("ld_gate", c_int64 * 2),
+        ("bs_gate", c_int64 * 2),
         ("n_kv", c_int),
         ("k", c_void_p * 2),
         ("v", c_void_p * 2),
@@ -114,6 +120,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_cfg_combine": (c_int, [P, P, F, P, I64, P]),
     "kino_euler_velocity": (c_int, [P, P, F, P, I64, P]),
     "kino_euler_x0": (c_int, [P, P, F, F, P, I64, P]),
+    "kino_add_rows": (c_int, [P, P, P, I64, I64, P]),
     "kino_timestep_embedding": (c_int, [P, P, I64, I64, P]),
 }
 

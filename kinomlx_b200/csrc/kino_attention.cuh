@@ -37,6 +37,8 @@ struct AttnParams {
   int kv_tokens[2], kv_blocks[2];
   __nv_bfloat16* out[2];
   int64_t ld_out[2], bs_out[2];
+  const __nv_bfloat16* gate[2];  // optional (batch, tokens, heads) output gate per query segment
+  int64_t ld_gate[2], bs_gate[2];
   float scale_log2;
 };
 
@@ -299,6 +301,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const int t = qtile * ATT_BM + row;
       const bool store = t < p.q_tokens[qseg];
       const float inv_l = 1.0f / l_run;
+      // Optional head gate: bf16(bf16(O / l) * gate[t, head])
+      // (kinomlx/models/ltx2/transformer/attention.py:364-368).
+      const __nv_bfloat16* gp = p.gate[qseg];
+      const float gv = (gp != nullptr && store)
+                           ? __bfloat162float(gp[static_cast<int64_t>(batch) * p.bs_gate[qseg] +
+                                                 static_cast<int64_t>(t) * p.ld_gate[qseg] + head])
+                           : 1.0f;
+      auto fin = [&](uint32_t raw) -> float {
+        const float o = __uint_as_float(raw) * inv_l;
+        return gp != nullptr ? bf16_round(bf16_round(o) * gv) : o;
+      };
       __nv_bfloat16* dst = p.out[qseg] + static_cast<int64_t>(batch) * p.bs_out[qseg] +
                            static_cast<int64_t>(t) * p.ld_out[qseg] + head * ATT_D;
 #pragma unroll 1
@@ -310,14 +323,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(o[g * 8 + 0]) * inv_l,
-                              __uint_as_float(o[g * 8 + 1]) * inv_l);
-            w.y = pack_bf16x2(__uint_as_float(o[g * 8 + 2]) * inv_l,
-                              __uint_as_float(o[g * 8 + 3]) * inv_l);
-            w.z = pack_bf16x2(__uint_as_float(o[g * 8 + 4]) * inv_l,
-                              __uint_as_float(o[g * 8 + 5]) * inv_l);
-            w.w = pack_bf16x2(__uint_as_float(o[g * 8 + 6]) * inv_l,
-                              __uint_as_float(o[g * 8 + 7]) * inv_l);
+            w.x = pack_bf16x2(fin(o[g * 8 + 0]), fin(o[g * 8 + 1]));
+            w.y = pack_bf16x2(fin(o[g * 8 + 2]), fin(o[g * 8 + 3]));
+            w.z = pack_bf16x2(fin(o[g * 8 + 4]), fin(o[g * 8 + 5]));
+            w.w = pack_bf16x2(fin(o[g * 8 + 6]), fin(o[g * 8 + 7]));
             *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = w;
           }
         }

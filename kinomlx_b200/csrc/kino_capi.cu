@@ -142,7 +142,7 @@ kino_status launch_gemm(const void* x, const void* w, void* out, const kino::Gem
 
 extern "C" {
 
-int kino_abi_version(void) { return 1; }
+int kino_abi_version(void) { return 2; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -193,14 +193,15 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
     e.aux = static_cast<const __nv_bfloat16*>(epi->aux);
     e.ld_aux = epi->ld_aux;
     e.bs_aux = epi->bs_aux;
-    if (e.kind < 0 || e.kind > 4) return fail(KINO_EINVAL, "kino_linear: unknown epilogue");
+    e.scalar2 = epi->scalar2;
+    if (e.kind < 0 || e.kind > 5) return fail(KINO_EINVAL, "kino_linear: unknown epilogue");
     if (e.bias != nullptr && !aligned16(e.bias))
       return fail(KINO_EINVAL, "kino_linear: bias not 16-byte aligned");
     if (e.kind == kino::EPI_GATED_RESIDUAL &&
         (e.residual == nullptr || e.gate == nullptr || !aligned16(e.residual) ||
          !aligned16(e.gate) || e.ld_res % 8 || e.bs_res % 8 || e.bs_gate % 8))
       return fail(KINO_EINVAL, "kino_linear: gated residual needs aligned residual and gate");
-    if (e.kind == kino::EPI_EULER &&
+    if ((e.kind == kino::EPI_EULER || e.kind == kino::EPI_EULER_X0) &&
         (e.aux == nullptr || !aligned16(e.aux) || e.ld_aux % 8 || e.bs_aux % 8))
       return fail(KINO_EINVAL, "kino_linear: Euler epilogue needs an aligned sample");
   }
@@ -275,6 +276,9 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
       p.out[s] = static_cast<__nv_bfloat16*>(a->out[s]);
       p.ld_out[s] = a->ld_out[s];
       p.bs_out[s] = a->bs_out[s];
+      p.gate[s] = static_cast<const __nv_bfloat16*>(a->gate[s]);
+      p.ld_gate[s] = a->ld_gate[s];
+      p.bs_gate[s] = a->bs_gate[s];
       tiles += p.q_tiles[s];
     }
     const int ks = s < a->n_kv ? s : 0;
@@ -341,11 +345,12 @@ kino_status kino_adaln(const void* x, int64_t ldx, int64_t bsx, const void* shif
     return fail(KINO_ENOTSUPPORTED, "kino_adaln: dim %% 8, dim <= 8192, aligned operands");
   if (rows < 1 || batch < 1 || rows > 0x7fffffff || batch > 65535)
     return fail(KINO_EINVAL, "kino_adaln: rows/batch");
+  if (norm_kind < 0 || norm_kind > 2) return fail(KINO_EINVAL, "kino_adaln: norm kind");
   dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(batch));
   kino::adaln_kernel<<<grid, kino::ADALN_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, bsx, static_cast<const __nv_bfloat16*>(shift),
       static_cast<const __nv_bfloat16*>(scale), bs_mod, static_cast<__nv_bfloat16*>(out), ldo,
-      bso, static_cast<int>(rows), static_cast<int>(dim), norm_kind == KINO_NORM_LAYER, eps);
+      bso, static_cast<int>(rows), static_cast<int>(dim), norm_kind, eps);
   return check_launch("kino_adaln");
 }
 
@@ -447,6 +452,20 @@ kino_status kino_euler_x0(const void* x, const void* v, float sigma, float ratio
                           int64_t n, void* stream) {
   if (v == nullptr) return fail(KINO_EINVAL, "kino_euler_x0: null");
   return launch_elem(kino::ELEM_EULER_X0, x, v, out, n, sigma, ratio, stream, "kino_euler_x0");
+}
+
+kino_status kino_add_rows(const void* a, const void* b, void* out, int64_t rows, int64_t n,
+                          void* stream) {
+  if (a == nullptr || b == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_add_rows: null");
+  if (n % 8 || !aligned16(a) || !aligned16(b) || !aligned16(out) || rows < 1 || n < 8)
+    return fail(KINO_ENOTSUPPORTED, "kino_add_rows: n %% 8 == 0 and aligned operands");
+  int64_t blocks = (rows * n / 8 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  kino::add_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                          static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
+      static_cast<__nv_bfloat16*>(out), rows, n);
+  return check_launch("kino_add_rows");
 }
 
 kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, int64_t dim,

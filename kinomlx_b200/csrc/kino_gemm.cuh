@@ -26,6 +26,7 @@ enum EpiKind : int {
   EPI_GATED_RESIDUAL = 2,
   EPI_EULER = 3,
   EPI_SIGMOID2 = 4,
+  EPI_EULER_X0 = 5,
 };
 
 struct GemmEpi {
@@ -39,6 +40,7 @@ struct GemmEpi {
   float scalar;                   // Euler dt (fp32, rounded to bf16 as the reference does)
   const __nv_bfloat16* aux;       // Euler current sample
   int64_t ld_aux, bs_aux;
+  float scalar2;                  // EULER_X0: fp32(sigma_next / sigma)
 };
 
 struct GemmShape {
@@ -125,6 +127,29 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
           float& a1 = v[g * 8 + q * 2 + 1];
           a0 = rf.x + bf16_round(gf.x * a0);
           a1 = rf.y + bf16_round(gf.y * a1);
+        }
+      }
+    }
+  } else if (e.kind == EPI_EULER_X0) {
+    // x0 = bf16(x - sigma * v) in fp32, out = x0 + ratio * (x - x0) in fp32
+    // (kinomlx/models/ltx2/transformer/wrappers.py:49-65, kinomlx/samplers/steps.py:36-70)
+    const __nv_bfloat16* xs = e.aux + static_cast<int64_t>(b) * e.bs_aux +
+                              static_cast<int64_t>(row) * e.ld_aux + col0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (col0 + g * 8 < s.n) {
+        const uint4 xx = *reinterpret_cast<const uint4*>(xs + g * 8);
+        const uint32_t x4[4] = {xx.x, xx.y, xx.z, xx.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 xf = unpack_bf16x2(x4[q]);
+          const float xv[2] = {xf.x, xf.y};
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float& a = v[g * 8 + q * 2 + h];
+            const float x0 = bf16_round(__fsub_rn(xv[h], __fmul_rn(e.scalar, a)));
+            a = __fadd_rn(x0, __fmul_rn(e.scalar2, __fsub_rn(xv[h], x0)));
+          }
         }
       }
     }

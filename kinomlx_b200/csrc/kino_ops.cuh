@@ -59,7 +59,9 @@ __global__ void __launch_bounds__(ADALN_THREADS)
     adaln_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x, int64_t bs_x,
                  const __nv_bfloat16* __restrict__ shift, const __nv_bfloat16* __restrict__ scale,
                  int64_t bs_mod, __nv_bfloat16* __restrict__ out, int64_t ld_out, int64_t bs_out,
-                 int rows, int dim, int layer_norm, float eps) {
+                 int rows, int dim, int norm_kind, float eps) {
+  // norm_kind: 0 RMSNorm, 1 LayerNorm, 2 none (modulation only,
+  // kinomlx/models/ltx2/transformer/transformer.py:34-35)
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int b = blockIdx.y;
@@ -78,7 +80,7 @@ __global__ void __launch_bounds__(ADALN_THREADS)
     }
   }
   float mean = 0.0f;
-  if (layer_norm) mean = block_sum(s, red) / static_cast<float>(dim);
+  if (norm_kind == 1) mean = block_sum(s, red) / static_cast<float>(dim);
   float q = 0.0f;
 #pragma unroll
   for (int i = 0; i < ADALN_MAXV; ++i) {
@@ -91,8 +93,11 @@ __global__ void __launch_bounds__(ADALN_THREADS)
       }
     }
   }
-  const float var = block_sum(q, red) / static_cast<float>(dim);
-  const float rstd = rsqrtf(var + eps);
+  float rstd = 1.0f;
+  if (norm_kind != 2) {
+    const float var = block_sum(q, red) / static_cast<float>(dim);
+    rstd = rsqrtf(var + eps);
+  }
   const __nv_bfloat16* sh = shift + b * bs_mod;
   const __nv_bfloat16* sc = scale + b * bs_mod;
 #pragma unroll
@@ -104,7 +109,7 @@ __global__ void __launch_bounds__(ADALN_THREADS)
       load8(sc + c * 8, fc);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float n = bf16_round((v[i][j] - mean) * rstd);
+        const float n = norm_kind == 2 ? v[i][j] : bf16_round((v[i][j] - mean) * rstd);
         const float one_plus = bf16_round(1.0f + fc[j]);
         o[j] = bf16_round(n * one_plus) + fs[j];
       }
@@ -343,6 +348,25 @@ __global__ void elementwise_kernel(int kind, const __nv_bfloat16* __restrict__ a
   }
 }
 
+// out[r, c] = bf16(a[r, c] + b[c]) for a (rows, n) and a broadcast row b (n): the per-block
+// modulation tables plus the step's timestep projection
+// (kinomlx/models/ltx2/transformer/transformer.py:178-186, model.py:585-587).
+__global__ void add_rows_kernel(const __nv_bfloat16* __restrict__ a,
+                                const __nv_bfloat16* __restrict__ b,
+                                __nv_bfloat16* __restrict__ out, int64_t rows, int64_t n) {
+  const int64_t nv = (rows * n) >> 3;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = (i * 8) % n;
+    float x[8], y[8], o[8];
+    load8(a + i * 8, x);
+    load8(b + c, y);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = x[j] + y[j];
+    store8(out + i * 8, o);
+  }
+}
+
 // ----------------------------------------------------------------------------- GEMV (M = batch)
 // y[b, n] = sum_k act(x[b, k]) * w[n, k] + bias[n]; act = identity or SiLU rounded to bf16
 // (kinomlx/models/flux2/transformer.py:223-258 Modulation / TimestepEmbedding,
@@ -387,7 +411,7 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     if (b < batch) {
       float v = warp_sum(acc[b]);
       if (lane == 0) {
-        if (bias != nullptr) v = bf16_round(v) + __bfloat162float(bias[col]);
+        if (bias != nullptr) v += __bfloat162float(bias[col]);  // addmm: bias in the fp32 sum
         y[b * ld_y + col] = __float2bfloat16_rn(v);
       }
     }

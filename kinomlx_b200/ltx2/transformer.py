@@ -1,0 +1,229 @@
+"""LTX-2 video DiT on the sm_100a kernels: the device twin of LTXAVModel's video path
+(kinomlx/models/ltx2/transformer/model.py:577-635, transformer.py:178-392, attention.py:249-371).
+
+Per block: AdaLN (RMSNorm) -> gate logits (GEMM, 2*sigmoid epilogue) and fused q|k|v projection
+with bias -> full-row QK RMSNorm + split RoPE in place -> attention with the per-head gate in its
+epilogue -> out projection with the gated residual in its epilogue; the text cross-attention
+(prompt-modulated context, no RoPE) and the GELU feed-forward follow the same pattern. The step's
+timestep projections are added to every block's modulation table by one kernel. The final
+projection's epilogue applies X0 + Euler.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from .config import LTXVariant
+
+
+def frequency_grid(theta: float, axes: int, inner_dim: int) -> tuple[float, ...]:
+    """theta^(i/(n-1)) * pi/2 on the host in double (kinomlx/models/ltx2/transformer/rope.py:75-92)."""
+    count = inner_dim // (2 * axes)
+    exps = (0.0,) if count == 1 else tuple(i / (count - 1) for i in range(count))
+    return tuple(math.pow(theta, e) * math.pi / 2 for e in exps)
+
+
+def precompute_freqs_cis(positions: torch.Tensor, v: LTXVariant) -> tuple[torch.Tensor, torch.Tensor]:
+    """Split-RoPE tables (B, heads, T, dim/(2 heads)) fp32 from (B, 3, T, 2) pixel bounds using the
+    middle of each patch (kinomlx/models/ltx2/transformer/rope.py:95-176)."""
+    pos = (positions[..., 0] + positions[..., 1]) / 2.0
+    scale = torch.tensor(v.max_pos, dtype=torch.float32)[None, :, None]
+    frac = (pos.to(torch.float32) / scale).transpose(1, 2)
+    grid = torch.tensor(frequency_grid(v.theta, positions.shape[1], v.dim), dtype=torch.float32)
+    freqs = (frac * 2.0 - 1.0)[..., None] * grid[None, None, None, :]
+    freqs = freqs.transpose(2, 3).reshape(freqs.shape[0], freqs.shape[1], -1)
+    pad = v.dim // 2 - freqs.shape[-1]
+    cos, sin = torch.cos(freqs), torch.sin(freqs)
+    if pad:
+        cos = torch.cat([torch.ones((*cos.shape[:-1], pad)), cos], dim=-1)
+        sin = torch.cat([torch.zeros((*sin.shape[:-1], pad)), sin], dim=-1)
+    b, t, _ = cos.shape
+    cos = cos.reshape(b, t, v.heads, -1).transpose(1, 2).contiguous()
+    sin = sin.reshape(b, t, v.heads, -1).transpose(1, 2).contiguous()
+    return cos, sin
+
+
+@dataclass
+class PreparedContext:
+    context: torch.Tensor  # (B, Tc, D) text after the connector
+    cos: torch.Tensor  # (1|B, heads, T, 64) fp32
+    sin: torch.Tensor
+
+
+class _Workspace:
+    def __init__(self, v: LTXVariant, batch: int, tokens: int, ctx_tokens: int, device):
+        d = v.dim
+        e = lambda *s: torch.empty(s, device=device, dtype=torch.bfloat16)
+        self.x = e(batch, tokens, d)
+        self.nrm = e(batch, tokens, d)
+        self.qkv = e(batch, tokens, 3 * d)
+        self.hid = e(batch, tokens, v.ff_mult * d)
+        self.gates = e(batch, tokens, v.heads)
+        self.ctxm = e(batch, ctx_tokens, d)
+        self.ctxkv = e(batch, ctx_tokens, 2 * d)
+        self.t = torch.empty((batch,), device=device, dtype=torch.float32)
+        self.temb = e(batch, 256)
+        self.h1 = e(batch, d)
+        self.emb = e(batch, d)
+        self.mod9 = e(batch, 9 * d)
+        self.ph1 = e(batch, d)
+        self.pemb = e(batch, d)
+        self.pmod = e(batch, 2 * d)
+        self.vals = e(batch, v.blocks, 9 * d)
+        self.prompt = e(batch, v.blocks, 2 * d)
+        self.outmod = e(batch, 2 * d)
+        self.velocity = e(batch, tokens, v.out_channels)
+
+
+class LTXVideoTransformer:
+    """Device LTX-2 video DiT. `weights` uses the reference checkpoint names."""
+
+    def __init__(self, weights: dict[str, torch.Tensor], variant: LTXVariant,
+                 device: torch.device | str = "cuda"):
+        self.v = variant
+        self.device = torch.device(device)
+        dev = lambda t: t.to(self.device, torch.bfloat16).contiguous()
+        w = weights
+        self.patch_w, self.patch_b = dev(w["patchify_proj.weight"]), dev(w["patchify_proj.bias"])
+
+        def adaln(prefix):
+            g = lambda n: dev(w[f"{prefix}.{n}"])
+            return {
+                "l1w": g("emb.timestep_embedder.linear_1.weight"),
+                "l1b": g("emb.timestep_embedder.linear_1.bias"),
+                "l2w": g("emb.timestep_embedder.linear_2.weight"),
+                "l2b": g("emb.timestep_embedder.linear_2.bias"),
+                "w": g("linear.weight"),
+                "b": g("linear.bias"),
+            }
+
+        self.adaln = adaln("adaln_single")
+        self.prompt_adaln = adaln("prompt_adaln_single")
+        tables, prompts = [], []
+        self.blocks = []
+        for i in range(variant.blocks):
+            a = f"transformer_blocks.{i}"
+            g = lambda n: w[f"{a}.{n}"]
+            tables.append(g("scale_shift_table").reshape(-1))
+            prompts.append(g("prompt_scale_shift_table").reshape(-1))
+            self.blocks.append({
+                "qkv_w": dev(torch.cat([g("attn1.to_q.weight"), g("attn1.to_k.weight"), g("attn1.to_v.weight")])),
+                "qkv_b": dev(torch.cat([g("attn1.to_q.bias"), g("attn1.to_k.bias"), g("attn1.to_v.bias")])),
+                "g1_w": dev(g("attn1.to_gate_logits.weight")),
+                "g1_b": dev(g("attn1.to_gate_logits.bias")),
+                "o1_w": dev(g("attn1.to_out.weight")),
+                "o1_b": dev(g("attn1.to_out.bias")),
+                "qn1": dev(g("attn1.q_norm.weight")),
+                "kn1": dev(g("attn1.k_norm.weight")),
+                "q2_w": dev(g("attn2.to_q.weight")),
+                "q2_b": dev(g("attn2.to_q.bias")),
+                "kv2_w": dev(torch.cat([g("attn2.to_k.weight"), g("attn2.to_v.weight")])),
+                "kv2_b": dev(torch.cat([g("attn2.to_k.bias"), g("attn2.to_v.bias")])),
+                "g2_w": dev(g("attn2.to_gate_logits.weight")),
+                "g2_b": dev(g("attn2.to_gate_logits.bias")),
+                "o2_w": dev(g("attn2.to_out.weight")),
+                "o2_b": dev(g("attn2.to_out.bias")),
+                "qn2": dev(g("attn2.q_norm.weight")),
+                "kn2": dev(g("attn2.k_norm.weight")),
+                "ff_in_w": dev(g("ff.project_in.proj.weight")),
+                "ff_in_b": dev(g("ff.project_in.proj.bias")),
+                "ff_out_w": dev(g("ff.project_out.weight")),
+                "ff_out_b": dev(g("ff.project_out.bias")),
+            })
+        self.tables = dev(torch.stack(tables))  # (L, 9D)
+        self.prompt_tables = dev(torch.stack(prompts))  # (L, 2D)
+        self.out_table = dev(w["scale_shift_table"])  # (2, D)
+        self.proj_w, self.proj_b = dev(w["proj_out.weight"]), dev(w["proj_out.bias"])
+        self._ws: dict[tuple[int, int, int], _Workspace] = {}
+
+    def prepare(self, context: torch.Tensor, positions: torch.Tensor) -> PreparedContext:
+        cos, sin = precompute_freqs_cis(positions.cpu(), self.v)
+        return PreparedContext(context.to(self.device, torch.bfloat16).contiguous(),
+                               cos.to(self.device), sin.to(self.device))
+
+    def workspace(self, batch: int, tokens: int, ctx_tokens: int) -> _Workspace:
+        key = (batch, tokens, ctx_tokens)
+        if key not in self._ws:
+            self._ws[key] = _Workspace(self.v, batch, tokens, ctx_tokens, self.device)
+        return self._ws[key]
+
+    # ------------------------------------------------------------------ per step embeddings
+    def _embed(self, ws: _Workspace, sigma: float) -> None:
+        """AdaLayerNormSingle for the block modulations and the prompt AdaLN
+        (kinomlx/models/ltx2/transformer/preprocessing.py:66-83, timestep.py:31-85)."""
+        ws.t.fill_(float(torch.tensor(sigma, dtype=torch.float32) * self.v.timestep_scale))
+        ops.timestep_embedding(ws.t, 256, out=ws.temb)
+        for p, h1, emb, mod in ((self.adaln, ws.h1, ws.emb, ws.mod9),
+                                (self.prompt_adaln, ws.ph1, ws.pemb, ws.pmod)):
+            ops.gemv(ws.temb, p["l1w"], p["l1b"], out=h1)
+            ops.gemv(h1, p["l2w"], p["l2b"], silu_input=True, out=emb)
+            ops.gemv(emb, p["w"], p["b"], silu_input=True, out=mod)
+        for b in range(ws.x.shape[0]):
+            ops.add_rows(self.tables, ws.mod9[b], out=ws.vals[b])
+            ops.add_rows(self.prompt_tables, ws.pmod[b], out=ws.prompt[b])
+            ops.add_rows(self.out_table, ws.emb[b], out=ws.outmod[b].view(2, -1))
+
+    # ------------------------------------------------------------------ block
+    def _block(self, ws: _Workspace, i: int, p: dict, prepared: PreparedContext) -> None:
+        v, d, h = self.v, self.v.dim, self.v.heads
+        val = lambda j: ws.vals[:, i, j * d : (j + 1) * d]
+        x, nrm = ws.x, ws.nrm
+        q, k, vv = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
+        # self-attention
+        ops.adaln(x, val(0), val(1), nrm, norm=ops.NORM_RMS, eps=v.eps)
+        ops.linear(nrm, p["g1_w"], ws.gates, bias=p["g1_b"], kind=ops.EPI_SIGMOID2)
+        ops.linear(nrm, p["qkv_w"], ws.qkv, bias=p["qkv_b"])
+        ops.qk_norm_rope(q, heads=h, weight=p["qn1"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_SPLIT,
+                         cos=prepared.cos, sin=prepared.sin, eps=v.eps)
+        ops.qk_norm_rope(k, heads=h, weight=p["kn1"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_SPLIT,
+                         cos=prepared.cos, sin=prepared.sin, eps=v.eps)
+        ops.attention([q], [k], [vv], [q], heads=h, gate=[ws.gates])
+        ops.linear(q, p["o1_w"], x, bias=p["o1_b"], kind=ops.EPI_GATED_RESIDUAL, residual=x,
+                   gate=val(2))
+        # text cross-attention with the prompt-modulated context
+        pr = lambda j: ws.prompt[:, i, j * d : (j + 1) * d]
+        ops.adaln(x, val(6), val(7), nrm, norm=ops.NORM_RMS, eps=v.eps)
+        ops.adaln(prepared.context, pr(0), pr(1), ws.ctxm, norm=ops.NORM_NONE)
+        ops.linear(nrm, p["g2_w"], ws.gates, bias=p["g2_b"], kind=ops.EPI_SIGMOID2)
+        ops.linear(nrm, p["q2_w"], q, bias=p["q2_b"])
+        ops.linear(ws.ctxm, p["kv2_w"], ws.ctxkv, bias=p["kv2_b"])
+        k2, v2 = ws.ctxkv[..., :d], ws.ctxkv[..., d:]
+        ops.qk_norm_rope(q, heads=h, weight=p["qn2"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_NONE,
+                         eps=v.eps)
+        ops.qk_norm_rope(k2, heads=h, weight=p["kn2"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_NONE,
+                         eps=v.eps)
+        ops.attention([q], [k2], [v2], [q], heads=h, gate=[ws.gates])
+        ops.linear(q, p["o2_w"], x, bias=p["o2_b"], kind=ops.EPI_GATED_RESIDUAL, residual=x,
+                   gate=val(8))
+        # feed-forward
+        ops.adaln(x, val(3), val(4), nrm, norm=ops.NORM_RMS, eps=v.eps)
+        ops.linear(nrm, p["ff_in_w"], ws.hid, bias=p["ff_in_b"], kind=ops.EPI_GELU)
+        ops.linear(ws.hid, p["ff_out_w"], x, bias=p["ff_out_b"], kind=ops.EPI_GATED_RESIDUAL,
+                   residual=x, gate=val(5))
+
+    # ------------------------------------------------------------------ forward
+    def run(self, prepared: PreparedContext, latent: torch.Tensor, sigma: float, *,
+            sigma_next: float | None = None, out: torch.Tensor | None = None,
+            blocks: range | None = None) -> torch.Tensor:
+        """Velocity for `latent` (B, T, C) at `sigma`; with `sigma_next`, the next latent of the
+        deterministic Euler step (X0 + Euler fused into the final projection)."""
+        batch, tokens, _ = latent.shape
+        ws = self.workspace(batch, tokens, prepared.context.shape[1])
+        self._embed(ws, sigma)
+        ops.linear(latent, self.patch_w, ws.x, bias=self.patch_b)
+        for i in blocks if blocks is not None else range(self.v.blocks):
+            self._block(ws, i, self.blocks[i], prepared)
+        d = self.v.dim
+        ops.adaln(ws.x, ws.outmod[:, :d], ws.outmod[:, d:], ws.nrm, norm=ops.NORM_LAYER,
+                  eps=self.v.eps)
+        if sigma_next is None:
+            return ops.linear(ws.nrm, self.proj_w, ws.velocity if out is None else out,
+                              bias=self.proj_b)
+        ratio = float(torch.tensor(sigma_next / sigma, dtype=torch.float32))
+        return ops.linear(ws.nrm, self.proj_w, out, bias=self.proj_b, kind=ops.EPI_EULER_X0,
+                          sigma=float(torch.tensor(sigma, dtype=torch.float32)), ratio=ratio,
+                          sample=latent)

@@ -16,8 +16,10 @@ from ._lib import (
     EPI_GATED_RESIDUAL,
     EPI_GELU,
     EPI_NONE,
+    EPI_EULER_X0,
     EPI_SIGMOID2,
     NORM_LAYER,
+    NORM_NONE,
     NORM_RMS,
     QKNORM_FULL_ROW,
     QKNORM_NONE,
@@ -32,8 +34,10 @@ __all__ = [
     "EPI_GATED_RESIDUAL",
     "EPI_GELU",
     "EPI_NONE",
+    "EPI_EULER_X0",
     "EPI_SIGMOID2",
     "NORM_LAYER",
+    "NORM_NONE",
     "NORM_RMS",
     "QKNORM_FULL_ROW",
     "QKNORM_NONE",
@@ -42,6 +46,7 @@ __all__ = [
     "ROPE_PAIRS",
     "ROPE_SPLIT",
     "adaln",
+    "add_rows",
     "attention",
     "cfg_combine",
     "device_status",
@@ -145,8 +150,13 @@ def linear(
     act_col_begin: int = 0,
     dt: float = 0.0,
     sample: torch.Tensor | None = None,
+    sigma: float = 0.0,
+    ratio: float = 0.0,
 ) -> torch.Tensor:
-    """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight."""
+    """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight.
+
+    EPI_EULER uses `dt` and `sample`; EPI_EULER_X0 uses `sigma`, `ratio` (fp32 sigma_next /
+    sigma) and `sample`."""
     _need(x, "x")
     _need(w, "w")
     x3 = _as3d(x)
@@ -179,7 +189,7 @@ def linear(
         epi.bs_gate = g.stride(0) if g.shape[0] > 1 else 0
     if kind == EPI_GELU:
         epi.act_col_begin = act_col_begin
-    if kind == EPI_EULER:
+    if kind in (EPI_EULER, EPI_EULER_X0):
         if sample is None:
             raise ValueError("the Euler epilogue needs the current sample")
         _need(sample, "sample")
@@ -187,7 +197,8 @@ def linear(
         epi.aux = s3.data_ptr()
         epi.ld_aux = s3.stride(1)
         epi.bs_aux = s3.stride(0)
-        epi.scalar = dt
+        epi.scalar = dt if kind == EPI_EULER else sigma
+        epi.scalar2 = ratio
     with _timed("gemm", 2.0 * batch * m * n * k, 2.0 * (batch * m * k + n * k + batch * m * n)):
         _lib.call(
             "kino_linear",
@@ -251,8 +262,10 @@ def attention(
     *,
     heads: int,
     scale: float | None = None,
+    gate: list[torch.Tensor | None] | None = None,
 ) -> list[torch.Tensor]:
-    """Attention over logically concatenated segments; each tensor (batch, tokens, heads*128)."""
+    """Attention over logically concatenated segments; each tensor (batch, tokens, heads*128).
+    `gate[s]` (batch, tokens, heads), if given, multiplies segment s's output per head."""
     if not 1 <= len(q) <= 2 or len(out) != len(q) or not 1 <= len(k) <= 2 or len(v) != len(k):
         raise ValueError("attention takes 1 or 2 query and key/value segments")
     args = _lib.AttentionArgs()
@@ -275,6 +288,15 @@ def attention(
         args.bs_q[s] = q3.stride(0)
         args.ld_out[s] = o3.stride(1)
         args.bs_out[s] = o3.stride(0)
+        g = gate[s] if gate is not None else None
+        if g is not None:
+            _need(g, "gate")
+            g3 = _as3d(g)
+            if tuple(g3.shape) != (q3.shape[0], q3.shape[1], heads):
+                raise ValueError("attention gate must be (batch, tokens, heads)")
+            args.gate[s] = g3.data_ptr()
+            args.ld_gate[s] = g3.stride(1)
+            args.bs_gate[s] = g3.stride(0)
     args.n_kv = len(k)
     for s, (ks, vs) in enumerate(zip(k, v)):
         _need(ks, "k")
@@ -336,6 +358,21 @@ def adaln(
             eps,
             _stream(),
         )
+    return out
+
+
+def add_rows(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = a + b with b (n,) broadcast over the rows of a (..., n), bf16."""
+    _need(a, "a")
+    _need(b, "b")
+    if not a.is_contiguous() or b.numel() != a.shape[-1]:
+        raise ValueError("add_rows needs a contiguous (..., n) tensor and an (n,) row")
+    b = b.contiguous()
+    if out is None:
+        out = torch.empty_like(a)
+    n = a.shape[-1]
+    with _timed("elementwise", 0.0, 6.0 * a.numel()):
+        _lib.call("kino_add_rows", _ptr(a), _ptr(b), _ptr(out), a.numel() // n, n, _stream())
     return out
 
 

@@ -52,6 +52,49 @@ def flux_weight_specs(v: FluxVariant, double: int | None = None, single: int | N
     return specs
 
 
+def ltx_weight_specs(v, blocks: int | None = None):
+    """(name, shape, kind) in draw order for the LTX-2 video stream; names follow the reference
+    checkpoint (kinomlx/models/ltx2/transformer/model.py:205-233, transformer.py:85-176)."""
+    d, h = v.dim, v.heads
+    nb = v.blocks if blocks is None else blocks
+    specs = [("patchify_proj.weight", (d, v.in_channels), "normal"),
+             ("patchify_proj.bias", (d,), "normal")]
+    for pre, n in (("adaln_single", 9), ("prompt_adaln_single", 2)):
+        specs += [
+            (f"{pre}.emb.timestep_embedder.linear_1.weight", (d, 256), "normal"),
+            (f"{pre}.emb.timestep_embedder.linear_1.bias", (d,), "normal"),
+            (f"{pre}.emb.timestep_embedder.linear_2.weight", (d, d), "normal"),
+            (f"{pre}.emb.timestep_embedder.linear_2.bias", (d,), "normal"),
+            (f"{pre}.linear.weight", (n * d, d), "normal"),
+            (f"{pre}.linear.bias", (n * d,), "normal"),
+        ]
+    for i in range(nb):
+        a = f"transformer_blocks.{i}"
+        specs += [(f"{a}.scale_shift_table", (9, d), "normal"),
+                  (f"{a}.prompt_scale_shift_table", (2, d), "normal")]
+        for attn, src in (("attn1", d), ("attn2", v.context_dim)):
+            specs += [(f"{a}.{attn}.to_q.weight", (d, d), "normal"), (f"{a}.{attn}.to_q.bias", (d,), "normal"),
+                      (f"{a}.{attn}.to_k.weight", (d, src), "normal"), (f"{a}.{attn}.to_k.bias", (d,), "normal"),
+                      (f"{a}.{attn}.to_v.weight", (d, src), "normal"), (f"{a}.{attn}.to_v.bias", (d,), "normal"),
+                      (f"{a}.{attn}.to_out.weight", (d, d), "normal"), (f"{a}.{attn}.to_out.bias", (d,), "normal"),
+                      (f"{a}.{attn}.to_gate_logits.weight", (h, d), "normal"),
+                      (f"{a}.{attn}.to_gate_logits.bias", (h,), "normal"),
+                      (f"{a}.{attn}.q_norm.weight", (d,), "ones"),
+                      (f"{a}.{attn}.k_norm.weight", (d,), "ones")]
+        specs += [(f"{a}.ff.project_in.proj.weight", (v.ff_mult * d, d), "normal"),
+                  (f"{a}.ff.project_in.proj.bias", (v.ff_mult * d,), "normal"),
+                  (f"{a}.ff.project_out.weight", (d, v.ff_mult * d), "normal"),
+                  (f"{a}.ff.project_out.bias", (d,), "normal")]
+    specs += [("scale_shift_table", (2, d), "normal"),
+              ("proj_out.weight", (v.out_channels, d), "normal"),
+              ("proj_out.bias", (v.out_channels,), "normal")]
+    return specs
+
+
+def ltx_weights(v, *, seed: int = 0, device="cpu", dtype=torch.bfloat16, blocks: int | None = None):
+    return make_weights(ltx_weight_specs(v, blocks), seed=seed, device=device, dtype=dtype)
+
+
 def make_weights(specs, *, seed: int = 0, device="cpu", dtype=torch.bfloat16, std: float = 0.02):
     gen = torch.Generator(device=device).manual_seed(seed)
     out: dict[str, torch.Tensor] = {}
