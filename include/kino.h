@@ -191,6 +191,63 @@ kino_status kino_add_rows(const void* a, const void* b, void* out, int64_t rows,
 kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, int64_t dim,
                                     void* stream);
 
+/* ------------------------------------------------------------------ video VAE decode */
+typedef struct kino_conv3d_args {
+  const void* x;            /* (frames, height, width, in_channels) bf16, channels-last */
+  int64_t frames, height, width, in_channels;   /* in_channels % 64 == 0 */
+  const void* weight;       /* (out_channels, 3, 3, 3, in_channels) bf16 (OTHWI) */
+  int64_t out_channels;
+  const void* bias;         /* (out_channels) bf16 or NULL: added in bf16 after the rounding */
+  const void* residual;     /* geometry of out, or NULL (no depth-to-space only) */
+  void* out;                /* plain: (F, H, W, N); depth-to-space: (F*st - (st>1), H*sh, W*sw, N/(st*sh*sw)) */
+  int causal;               /* 1: two copies of the first frame in front; 0: one at each end */
+  int stride_t, stride_h, stride_w;  /* depth-to-space of the output; weight rows sub-position-major */
+} kino_conv3d_args;
+
+/* 3x3x3 convolution with temporal replicate and spatial zero padding as an implicit GEMM on
+ * tcgen05 (TMA loads the shifted input boxes; no im2col buffer). Replaces Conv3dBlock and
+ * WinogradConv3d (kinomlx/models/ltx2/video_vae/blocks.py:97-139,
+ * kinomlx/kernels/winograd_conv3d.py:688) and the depth-to-space of
+ * DepthToSpaceUpsample3d (kinomlx/models/ltx2/video_vae/decoder.py:80-121). */
+kino_status kino_conv3d(const kino_conv3d_args* args, void* stream);
+
+/* Stepwise PixelNorm over channels (+ SiLU if apply_silu), channels <= 1024.
+ * Replaces kinomlx.kernels.pixel_norm / pixel_norm_fp16 (kinomlx/kernels/fused_ops.py:460-493)
+ * and the silu(pixel_norm(x)) pairs of kinomlx/models/ltx2/video_vae/blocks.py:165-168. */
+kino_status kino_pixel_norm(const void* x, void* out, int64_t voxels, int64_t channels, float eps,
+                            int apply_silu, void* stream);
+
+/* Bytes of device workspace kino_group_norm needs for this shape. */
+int64_t kino_group_norm_workspace_size(int64_t voxels, int64_t channels);
+
+/* Affine GroupNorm(32) on channels-last x with fp32 two-pass statistics (+ SiLU). The grid-wide
+ * reduction writes partial sums into the caller's `workspace` (at least
+ * kino_group_norm_workspace_size bytes). Replaces kinomlx.kernels.group_norm
+ * (kinomlx/kernels/fused_ops.py:375-409). 32 <= channels <= 2048. */
+kino_status kino_group_norm(const void* x, const void* weight, const void* bias, void* out,
+                            int64_t voxels, int64_t channels, float eps, int apply_silu,
+                            void* workspace, int64_t workspace_bytes, void* stream);
+
+/* latent (channels, voxels) bf16 (BCFHW, batch 1) -> bf16(x * std + mean) channels-last.
+ * Replaces PerChannelStatistics.denormalize + the BCFHW->BFHWC transpose
+ * (kinomlx/models/ltx2/video_vae/decoder.py:227-233). */
+kino_status kino_latent_to_bfhwc(const void* latent, const float* std_of_means,
+                                 const float* mean_of_means, void* out, int64_t channels,
+                                 int64_t voxels, void* stream);
+
+/* Accumulate one decoded tile (frames, height, width, channels*patch^2) bf16 into an fp32 BCFHW
+ * canvas at pixel offset (y0, x0), unpatchified and weighted by mask_h x mask_w; the masks are
+ * added to the (out_height, out_width) weight canvas. Replaces the trapezoid blend of
+ * kinomlx/models/ltx2/video_vae/tiling.py:1310-1330 with unpatchify (blocks.py:200-230). */
+kino_status kino_tile_blend(const void* decoded, int64_t frames, int64_t height, int64_t width,
+                            int64_t channels, int64_t patch, float* canvas, float* weights,
+                            int64_t out_height, int64_t out_width, int64_t y0, int64_t x0,
+                            const float* mask_h, const float* mask_w, void* stream);
+
+/* canvas[p, y, x] /= max(weights[y, x], 1e-8) (kinomlx/models/ltx2/video_vae/tiling.py:1369). */
+kino_status kino_blend_normalize(float* canvas, const float* weights, int64_t planes, int64_t hw,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

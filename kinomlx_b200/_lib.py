@@ -91,6 +91,25 @@ class AttentionArgs(ctypes.Structure):
     ]
 
 
+class Conv3dArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p),
+        ("frames", c_int64),
+        ("height", c_int64),
+        ("width", c_int64),
+        ("in_channels", c_int64),
+        ("weight", c_void_p),
+        ("out_channels", c_int64),
+        ("bias", c_void_p),
+        ("residual", c_void_p),
+        ("out", c_void_p),
+        ("causal", c_int),
+        ("stride_t", c_int),
+        ("stride_h", c_int),
+        ("stride_w", c_int),
+    ]
+
+
 I64 = c_int64
 P = c_void_p
 F = c_float
@@ -122,6 +141,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_euler_x0": (c_int, [P, P, F, F, P, I64, P]),
     "kino_add_rows": (c_int, [P, P, P, I64, I64, P]),
     "kino_timestep_embedding": (c_int, [P, P, I64, I64, P]),
+    "kino_conv3d": (c_int, [POINTER(Conv3dArgs), P]),
+    "kino_pixel_norm": (c_int, [P, P, I64, I64, F, c_int, P]),
+    "kino_group_norm_workspace_size": (c_int64, [I64, I64]),
+    "kino_group_norm": (c_int, [P, P, P, P, I64, I64, F, c_int, P, I64, P]),
+    "kino_latent_to_bfhwc": (c_int, [P, P, P, P, I64, I64, P]),
+    "kino_tile_blend": (c_int, [P, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, P, P, P]),
+    "kino_blend_normalize": (c_int, [P, P, I64, I64, P]),
 }
 
 _LIB: ctypes.CDLL | None = None

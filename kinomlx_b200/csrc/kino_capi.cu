@@ -10,7 +10,9 @@
 #include "kino_attention.cuh"
 #include "kino_common.cuh"
 #include "kino_gemm.cuh"
+#include "kino_conv3d.cuh"
 #include "kino_ops.cuh"
+#include "kino_vae.cuh"
 
 namespace {
 
@@ -136,6 +138,44 @@ kino_status launch_gemm(const void* x, const void* w, void* out, const kino::Gem
   kernel<<<grid, kino::GEMM_THREADS, L::TOTAL, stream>>>(
       ma, mb, reinterpret_cast<__nv_bfloat16*>(out), s, e);
   return check_launch("kino_linear");
+}
+
+template <int BN, int STAGES>
+kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cudaStream_t stream,
+                        int slot) {
+  using L = kino::GemmSmem<BN, STAGES>;
+  CUtensorMap mx, mw;
+  const uint64_t dx[4] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W),
+                          static_cast<uint64_t>(s0.H), static_cast<uint64_t>(s0.F)};
+  const uint64_t sx[3] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W) * s0.Cin,
+                          static_cast<uint64_t>(s0.H) * s0.W * s0.Cin};
+  const uint32_t bx[4] = {64, static_cast<uint32_t>(s0.tw), static_cast<uint32_t>(s0.th), 1};
+  kino_status st = make_map(&mx, a->x, 4, dx, sx, bx);
+  if (st != KINO_OK) return st;
+  const uint64_t k = 27ull * s0.Cin;
+  const uint64_t dw[2] = {k, static_cast<uint64_t>(s0.N)};
+  const uint64_t sw[1] = {k};
+  const uint32_t bw[2] = {64, static_cast<uint32_t>(BN)};
+  st = make_map(&mw, a->weight, 2, dw, sw, bw);
+  if (st != KINO_OK) return st;
+  kino::ConvShape s = s0;
+  s.tiles_n = (s.N + BN - 1) / BN;
+  s.num_tiles = s.tiles_m * s.tiles_n;
+  auto kernel = kino::conv3d_tc_kernel<BN, STAGES>;
+  st = ensure_smem(kernel, L::TOTAL, slot);
+  if (st != KINO_OK) return st;
+  const int grid = s.num_tiles < device_sms() ? s.num_tiles : device_sms();
+  kino::ConvEpi e;
+  e.bias = static_cast<const __nv_bfloat16*>(a->bias);
+  e.residual = static_cast<const __nv_bfloat16*>(a->residual);
+  kernel<<<grid, kino::GEMM_THREADS, L::TOTAL, stream>>>(
+      mx, mw, static_cast<__nv_bfloat16*>(a->out), s, e);
+  return check_launch("kino_conv3d");
+}
+
+int gn_parts(int64_t voxels) {
+  int64_t p = (voxels + 31) / 32;
+  return static_cast<int>(p < 592 ? (p < 1 ? 1 : p) : 592);
 }
 
 }  // namespace
@@ -477,6 +517,156 @@ kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, in
                                     static_cast<cudaStream_t>(stream)>>>(
       t, static_cast<__nv_bfloat16*>(out), static_cast<int>(batch), static_cast<int>(dim));
   return check_launch("kino_timestep_embedding");
+}
+
+kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
+  if (a == nullptr || a->x == nullptr || a->weight == nullptr || a->out == nullptr)
+    return fail(KINO_EINVAL, "kino_conv3d: null operand");
+  if (a->frames < 1 || a->height < 1 || a->width < 1 || a->out_channels < 8)
+    return fail(KINO_EINVAL, "kino_conv3d: empty shape");
+  if (a->in_channels % 64 != 0 || a->in_channels > 8192)
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d: in_channels must be a multiple of 64");
+  const int st = a->stride_t, sh = a->stride_h, sw = a->stride_w;
+  if (st < 1 || st > 2 || sh < 1 || sh > 2 || sw < 1 || sw > 2)
+    return fail(KINO_EINVAL, "kino_conv3d: depth-to-space strides must be 1 or 2");
+  const int64_t sub = static_cast<int64_t>(st) * sh * sw;
+  if (a->out_channels % sub) return fail(KINO_EINVAL, "kino_conv3d: channels vs strides");
+  const int64_t co = a->out_channels / sub;
+  if (a->out_channels % 8 || (sub > 1 && co % 32))
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d: output channels per voxel must be 8k (32k with depth-to-space)");
+  if (a->residual != nullptr && sub > 1)
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d: residual add only without depth-to-space");
+  if (a->bias != nullptr && !aligned16(a->bias)) return fail(KINO_EINVAL, "kino_conv3d: bias alignment");
+  if ((a->residual != nullptr && !aligned16(a->residual)) || !aligned16(a->out))
+    return fail(KINO_EINVAL, "kino_conv3d: output/residual alignment");
+  if (a->frames * a->height * a->width > (1ll << 31))
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d: too many voxels");
+  kino::ConvShape s;
+  std::memset(&s, 0, sizeof(s));
+  s.F = static_cast<int>(a->frames);
+  s.H = static_cast<int>(a->height);
+  s.W = static_cast<int>(a->width);
+  s.Cin = static_cast<int>(a->in_channels);
+  s.N = static_cast<int>(a->out_channels);
+  s.tw = s.W >= 32 ? 32 : (s.W >= 16 ? 16 : 8);
+  int th = 128 / s.tw;
+  while (th > 1 && th / 2 >= s.H) th /= 2;  // do not waste rows on short frames
+  s.th = th;
+  s.tf = 128 / (s.th * s.tw);
+  s.fb = (s.F + s.tf - 1) / s.tf;
+  s.hb = (s.H + s.th - 1) / s.th;
+  s.wb = (s.W + s.tw - 1) / s.tw;
+  s.tiles_m = s.fb * s.hb * s.wb;
+  s.cblocks = s.Cin / 64;
+  s.kblocks = 27 * s.cblocks;
+  s.pad_front = a->causal ? 2 : 1;
+  s.st = st;
+  s.sh = sh;
+  s.sw = sw;
+  s.drop = st > 1 ? 1 : 0;
+  s.Co = static_cast<int>(co);
+  s.Fo = s.F * st - s.drop;
+  s.Ho = s.H * sh;
+  s.Wo = s.W * sw;
+  cudaStream_t strm = static_cast<cudaStream_t>(stream);
+  if (a->out_channels <= 128) return launch_conv<128, 6>(a, s, strm, 4);
+  return launch_conv<256, 4>(a, s, strm, 5);
+}
+
+kino_status kino_pixel_norm(const void* x, void* out, int64_t voxels, int64_t channels, float eps,
+                            int apply_silu, void* stream) {
+  if (x == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_pixel_norm: null");
+  if (channels % 8 || channels > 1024 || !aligned16(x) || !aligned16(out) || voxels < 1)
+    return fail(KINO_ENOTSUPPORTED, "kino_pixel_norm: channels %% 8, <= 1024, aligned");
+  const int64_t threads = voxels * 32;
+  const int64_t blocks = (threads + 255) / 256;
+  kino::pixel_norm_silu_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), voxels,
+      static_cast<int>(channels), eps, apply_silu);
+  return check_launch("kino_pixel_norm");
+}
+
+int64_t kino_group_norm_workspace_size(int64_t voxels, int64_t channels) {
+  (void)channels;
+  return (static_cast<int64_t>(gn_parts(voxels)) + 2) * kino::GN_GROUPS * sizeof(float);
+}
+
+kino_status kino_group_norm(const void* x, const void* weight, const void* bias, void* out,
+                            int64_t voxels, int64_t channels, float eps, int apply_silu,
+                            void* workspace, int64_t workspace_bytes, void* stream) {
+  if (x == nullptr || weight == nullptr || bias == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_group_norm: null operand");
+  if (workspace == nullptr || workspace_bytes < kino_group_norm_workspace_size(voxels, channels))
+    return fail(KINO_EINVAL, "kino_group_norm: workspace smaller than kino_group_norm_workspace_size");
+  if (channels % (8 * kino::GN_GROUPS) && (channels % kino::GN_GROUPS || channels % 8))
+    return fail(KINO_ENOTSUPPORTED, "kino_group_norm: channels must split into 32 groups");
+  if (channels > 2048 || channels < 32 || !aligned16(x) || !aligned16(out) ||
+      !aligned16(weight) || !aligned16(bias) || voxels < 1)
+    return fail(KINO_ENOTSUPPORTED, "kino_group_norm: 32 <= channels <= 2048, aligned operands");
+  const int parts = gn_parts(voxels);
+  float* ws = static_cast<float*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* xb = static_cast<const __nv_bfloat16*>(x);
+  const int c = static_cast<int>(channels);
+  const int64_t count = voxels * (channels / kino::GN_GROUPS);
+  for (int pass = 0; pass < 2; ++pass) {
+    kino::group_norm_partial_kernel<<<parts, kino::GN_THREADS, 0, s>>>(xb, voxels, c, ws, parts,
+                                                                       pass);
+    kino::group_norm_finalize_kernel<<<1, 32, 0, s>>>(ws, parts, count, eps, pass);
+  }
+  int64_t blocks = (voxels * channels / 8 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  kino::group_norm_apply_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+      xb, static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(bias),
+      static_cast<__nv_bfloat16*>(out), voxels, c, ws, parts, apply_silu);
+  return check_launch("kino_group_norm");
+}
+
+kino_status kino_latent_to_bfhwc(const void* latent, const float* std_of_means,
+                                 const float* mean_of_means, void* out, int64_t channels,
+                                 int64_t voxels, void* stream) {
+  if (latent == nullptr || std_of_means == nullptr || mean_of_means == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_latent_to_bfhwc: null");
+  if (channels < 1 || voxels < 1) return fail(KINO_EINVAL, "kino_latent_to_bfhwc: empty");
+  int64_t blocks = (channels * voxels + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  kino::latent_to_bfhwc_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(latent), std_of_means, mean_of_means,
+      static_cast<__nv_bfloat16*>(out), static_cast<int>(channels), voxels);
+  return check_launch("kino_latent_to_bfhwc");
+}
+
+kino_status kino_tile_blend(const void* decoded, int64_t frames, int64_t height, int64_t width,
+                            int64_t channels, int64_t patch, float* canvas, float* weights,
+                            int64_t out_height, int64_t out_width, int64_t y0, int64_t x0,
+                            const float* mask_h, const float* mask_w, void* stream) {
+  if (decoded == nullptr || canvas == nullptr || weights == nullptr || mask_h == nullptr ||
+      mask_w == nullptr)
+    return fail(KINO_EINVAL, "kino_tile_blend: null");
+  if (y0 < 0 || x0 < 0 || y0 + height * patch > out_height || x0 + width * patch > out_width)
+    return fail(KINO_EINVAL, "kino_tile_blend: tile outside the canvas");
+  const int64_t n = channels * frames * height * patch * width * patch;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  kino::tile_blend_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                            static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(decoded), static_cast<int>(frames),
+      static_cast<int>(height), static_cast<int>(width), static_cast<int>(channels),
+      static_cast<int>(patch), canvas, weights, static_cast<int>(out_height),
+      static_cast<int>(out_width), static_cast<int>(y0), static_cast<int>(x0), mask_h, mask_w);
+  return check_launch("kino_tile_blend");
+}
+
+kino_status kino_blend_normalize(float* canvas, const float* weights, int64_t planes, int64_t hw,
+                                 void* stream) {
+  if (canvas == nullptr || weights == nullptr) return fail(KINO_EINVAL, "kino_blend_normalize: null");
+  int64_t blocks = (planes * hw + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  kino::blend_normalize_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(canvas, weights, planes, hw);
+  return check_launch("kino_blend_normalize");
 }
 
 }  // extern "C"

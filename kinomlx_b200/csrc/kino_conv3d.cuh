@@ -1,0 +1,260 @@
+// 3x3x3 video-VAE convolution as an implicit GEMM on tcgen05, channels-last (F, H, W, C).
+//
+//   out[f, h, w, n] = sum_{kt, kh, kw, c} xpad[f + kt, h + kh, w + kw, c] * weight[n, kt, kh, kw, c]
+//
+// Restates Conv3dBlock (kinomlx/models/ltx2/video_vae/blocks.py:97-139): temporal replicate
+// padding (causal: two copies of the first frame; otherwise one at each end), spatial zero
+// padding of one, fp32 accumulation rounded to bf16, then the bias added in bf16, and optionally
+// the residual added in bf16 (blocks.py:165-169). The weight is the reference's OTHWI layout,
+// i.e. an (N, 27 * Cin) K-major matrix.
+//
+// GEMM view: M = output voxels, N = output channels, K = 27 * Cin. An M tile is a box of
+// tf x th x tw voxels (128 in all). For each K block (one tap (kt, kh, kw), 64 channels) the TMA
+// producer loads the shifted input box of every frame of the tile straight from the unpadded
+// tensor: spatial padding is the TMA's zero fill at out-of-range coordinates (the channel
+// coordinate stays 64-aligned), temporal replicate padding is a clamp of the frame coordinate.
+// No im2col buffer, no padded copy. The MMA and epilogue roles are the GEMM's.
+//
+// Epilogue store modes: plain (same geometry), or depth-to-space (decoder.py:80-121): the
+// weight rows are reordered on the host to sub-position-major order (n = sub * C' + c), so a
+// 32-column chunk is 32 channels of one destination voxel; the first output frame is dropped
+// when the temporal stride is 2.
+#pragma once
+#include "kino_common.cuh"
+#include "kino_gemm.cuh"
+
+namespace kino {
+
+struct ConvShape {
+  int F, H, W, Cin, N;
+  int tf, th, tw;
+  int fb, hb, wb;
+  int tiles_m, tiles_n, num_tiles, kblocks, cblocks;
+  int pad_front;
+  int st, sh, sw, drop;  // depth-to-space strides (1,1,1,0 = plain store)
+  int Fo, Ho, Wo, Co;    // output geometry
+};
+
+struct ConvEpi {
+  const __nv_bfloat16* bias;      // [N] (in the same row order as the weight) or null
+  const __nv_bfloat16* residual;  // plain mode only: same geometry as the output, or null
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    conv3d_tc_kernel(const __grid_constant__ CUtensorMap map_x,
+                     const __grid_constant__ CUtensorMap map_w, __nv_bfloat16* __restrict__ out,
+                     const ConvShape s, const ConvEpi e) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = warp_id();
+  const uint32_t lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&map_x);
+    tma_prefetch(&map_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+  const int box_rows = s.th * s.tw;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x) {
+        const int mt = t % s.tiles_m;
+        const int nt = t / s.tiles_m;
+        const int wbi = mt % s.wb;
+        const int hbi = (mt / s.wb) % s.hb;
+        const int fbi = mt / (s.wb * s.hb);
+        const int f0 = fbi * s.tf, h0 = hbi * s.th, w0 = wbi * s.tw;
+        for (int kb = 0; kb < s.kblocks; ++kb) {
+          const int tap = kb / s.cblocks;
+          const int cb = kb - tap * s.cblocks;
+          const int kt = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+          uint8_t* sa = smem + stage * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          mbar_expect_tx(&full[stage], L::STAGE_BYTES);
+          for (int fi = 0; fi < s.tf; ++fi) {
+            int fs = f0 + fi + kt - s.pad_front;
+            fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
+            tma_load_4d(sa + fi * box_rows * 128, &map_x, &full[stage], cb * 64, w0 + kw - 1,
+                        h0 + kh - 1, fs);
+          }
+          tma_load_2d(sb, &map_w, &full[stage], kb * GEMM_BK, nt * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      if (*abort_flag) {
+        for (int i = 0; i < STAGES && i < issued; ++i) {
+          if (--stage < 0) {
+            stage = STAGES - 1;
+            phase ^= 1u;
+          }
+          const uint64_t t0 = global_ns();
+          while (!mbar_try_wait(&full[stage], phase) && global_ns() - t0 < 200000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(GEMM_BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < s.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            umma_bf16(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32), idesc,
+                      (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      umma_commit(drain);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 200000000ull) {
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int m = quarter * 32 + static_cast<int>(lane);
+    const int cpo = s.Co;  // channels per output voxel
+    int local = 0;
+    for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
+      const int mt = t % s.tiles_m;
+      const int nt = t / s.tiles_m;
+      const int wbi = mt % s.wb;
+      const int hbi = (mt / s.wb) % s.hb;
+      const int fbi = mt / (s.wb * s.hb);
+      const int wi = m % s.tw, hi = (m / s.tw) % s.th, fi = m / box_rows;
+      const int f = fbi * s.tf + fi, h = hbi * s.th + hi, w = wbi * s.tw + wi;
+      const bool valid = f < s.F && h < s.H && w < s.W;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((quarter * 32) << 16) + acc * BN + c * 32, r);
+        tmem_wait_ld();
+        const int n0 = nt * BN + c * 32;
+        if (!valid || n0 >= s.N) continue;
+        // destination voxel and channel offset of this 32-column chunk
+        const int sub = n0 / cpo;
+        const int ch0 = n0 - sub * cpo;
+        const int a = sub / (s.sh * s.sw), bb = (sub / s.sw) % s.sh, ee = sub % s.sw;
+        const int fo = f * s.st + a - s.drop, ho = h * s.sh + bb, wo = w * s.sw + ee;
+        if (fo < 0 || fo >= s.Fo) continue;
+        const int64_t off = ((static_cast<int64_t>(fo) * s.Ho + ho) * s.Wo + wo) * cpo + ch0;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = bf16_round(__uint_as_float(r[j]));
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (n0 + g * 8 < s.N) {
+            float add[8];
+            if (e.bias != nullptr) {
+              const uint4 raw = *reinterpret_cast<const uint4*>(e.bias + n0 + g * 8);
+              const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float2 fb = unpack_bf16x2(w4[q]);
+                add[2 * q] = fb.x;
+                add[2 * q + 1] = fb.y;
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[g * 8 + j] = bf16_round(v[g * 8 + j] + add[j]);
+            }
+            if (e.residual != nullptr) {
+              const uint4 raw = *reinterpret_cast<const uint4*>(e.residual + off + g * 8);
+              const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float2 fr = unpack_bf16x2(w4[q]);
+                v[g * 8 + 2 * q] += fr.x;
+                v[g * 8 + 2 * q + 1] += fr.y;
+              }
+            }
+            uint4 o;
+            o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
+            o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
+            o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
+            o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
+            *reinterpret_cast<uint4*>(out + off + g * 8) = o;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+}  // namespace kino

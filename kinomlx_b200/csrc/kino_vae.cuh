@@ -1,0 +1,199 @@
+// Bandwidth-bound kernels of the video-VAE decode (channels-last activations, bf16).
+#pragma once
+#include "kino_common.cuh"
+#include "kino_ops.cuh"
+
+namespace kino {
+
+// ----------------------------------------------------------------------------- PixelNorm + SiLU
+// Stepwise PixelNorm over channels in the activation dtype (kinomlx/kernels/fused_ops.py:460-476:
+// square, mean, + eps, sqrt, divide, each rounded to bf16; the mean accumulates in fp32), then
+// SiLU with fp32 opmath (fused_ops.py:40-45, blocks.py:165-168). One warp per voxel.
+__global__ void pixel_norm_silu_kernel(const __nv_bfloat16* __restrict__ x,
+                                       __nv_bfloat16* __restrict__ out, int64_t voxels, int C,
+                                       float eps, int apply_silu) {
+  const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_global >= voxels) return;
+  const __nv_bfloat16* row = x + warp_global * C;
+  __nv_bfloat16* orow = out + warp_global * C;
+  const int nvec = C >> 3;
+  float v[4][8];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+      load8(row + c * 8, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += bf16_round(v[i][j] * v[i][j]);
+    }
+  }
+  s = warp_sum(s);
+  const float mean = bf16_round(s / static_cast<float>(C));
+  const float shifted = bf16_round(mean + eps);
+  const float rms = bf16_round(sqrtf(shifted));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float y = bf16_round(__fdiv_rn(v[i][j], rms));
+        o[j] = apply_silu ? silu_f32(y) : y;
+      }
+      store8(orow + c * 8, o);
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------- GroupNorm
+// Affine GroupNorm with fp32 two-pass statistics over each group's channels and all voxels
+// (kinomlx/kernels/fused_ops.py:47-139, 375-409), then optionally SiLU. The statistics need a
+// grid-wide reduction: every CTA writes its partial sums for the 32 groups into a caller-owned
+// workspace, a one-CTA pass turns them into the mean (then the reciprocal std), and the apply
+// pass normalises. Workspace layout (floats): partial[parts][32], mean[32], rstd[32].
+constexpr int GN_GROUPS = 32;
+constexpr int GN_THREADS = 256;
+
+// pass 0: sum(x); pass 1: sum((x - mean)^2)
+__global__ void __launch_bounds__(GN_THREADS)
+    group_norm_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t voxels, int C,
+                              float* __restrict__ ws, int parts, int pass) {
+  __shared__ float gsum[GN_GROUPS];
+  if (threadIdx.x < GN_GROUPS) gsum[threadIdx.x] = 0.0f;
+  __syncthreads();
+  const int vec_per_row = C >> 3;
+  const int rows_per_iter = GN_THREADS / vec_per_row;  // C <= 2048
+  const int cv = threadIdx.x % vec_per_row;
+  const int r0 = threadIdx.x / vec_per_row;
+  const int gs = C / GN_GROUPS;
+  const float* mean = ws + static_cast<int64_t>(parts) * GN_GROUPS;
+  float m[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) m[j] = pass ? mean[(cv * 8 + j) / gs] : 0.0f;
+  float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (r0 < rows_per_iter) {
+    const int64_t per = (voxels + parts - 1) / parts;
+    const int64_t begin = blockIdx.x * per;
+    const int64_t end = begin + per < voxels ? begin + per : voxels;
+    for (int64_t v = begin + r0; v < end; v += rows_per_iter) {
+      float f[8];
+      load8(x + v * C + cv * 8, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = f[j] - m[j];
+        acc[j] += pass ? d * d : f[j];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) atomicAdd(&gsum[(cv * 8 + j) / gs], acc[j]);
+  }
+  __syncthreads();
+  if (threadIdx.x < GN_GROUPS) ws[static_cast<int64_t>(blockIdx.x) * GN_GROUPS + threadIdx.x] =
+      gsum[threadIdx.x];
+}
+
+// One CTA of 32 threads: reduce the partials of group g; pass 0 writes mean, pass 1 rstd.
+__global__ void group_norm_finalize_kernel(float* __restrict__ ws, int parts, int64_t count,
+                                           float eps, int pass) {
+  const int g = threadIdx.x;
+  if (g >= GN_GROUPS) return;
+  float s = 0.0f;
+  for (int p = 0; p < parts; ++p) s += ws[static_cast<int64_t>(p) * GN_GROUPS + g];
+  float* mean = ws + static_cast<int64_t>(parts) * GN_GROUPS;
+  float* rstd = mean + GN_GROUPS;
+  if (pass == 0) {
+    mean[g] = s / static_cast<float>(count);
+  } else {
+    rstd[g] = rsqrtf(s / static_cast<float>(count) + eps);
+  }
+}
+
+__global__ void group_norm_apply_kernel(const __nv_bfloat16* __restrict__ x,
+                                        const __nv_bfloat16* __restrict__ weight,
+                                        const __nv_bfloat16* __restrict__ bias,
+                                        __nv_bfloat16* __restrict__ out, int64_t voxels, int C,
+                                        const float* __restrict__ ws, int parts, int apply_silu) {
+  const int gs = C / GN_GROUPS;
+  const float* mean = ws + static_cast<int64_t>(parts) * GN_GROUPS;
+  const float* rstd = mean + GN_GROUPS;
+  const int64_t nv = (voxels * C) >> 3;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c0 = static_cast<int>((i * 8) % C);
+    float f[8], w[8], b[8], o[8];
+    load8(x + i * 8, f);
+    load8(weight + c0, w);
+    load8(bias + c0, b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int g = (c0 + j) / gs;
+      const float y = (f[j] - mean[g]) * rstd[g] * w[j] + b[j];
+      o[j] = apply_silu ? silu_f32(bf16_round(y)) : y;
+    }
+    store8(out + i * 8, o);
+  }
+}
+
+// ----------------------------------------------------------------------------- latent -> BFHWC
+// x * std[c] + mean[c] in fp32 from a bf16 BCFHW latent, rounded to bf16 channels-last
+// (kinomlx/models/ltx2/video_vae/decoder.py:227-233, ops.py:185-188).
+__global__ void latent_to_bfhwc_kernel(const __nv_bfloat16* __restrict__ latent,
+                                       const float* __restrict__ stdv,
+                                       const float* __restrict__ meanv,
+                                       __nv_bfloat16* __restrict__ out, int C, int64_t voxels) {
+  const int64_t n = voxels * C;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % C);
+    const int64_t v = i / C;
+    const float val = __bfloat162float(latent[static_cast<int64_t>(c) * voxels + v]);
+    out[i] = __float2bfloat16_rn(val * stdv[c] + meanv[c]);
+  }
+}
+
+// ----------------------------------------------------------------------------- tile blend
+// One decoded tile (Ft, h, w, 3 * p * p) bf16 from conv_out: unpatchify (packed channel index
+// c * p^2 + pw * p + ph, blocks.py:200-230), widen to fp32 and accumulate decoded * mask into the
+// fp32 BCFHW canvas at the tile's pixel offset; the first call for a tile position also adds the
+// mask to the weight canvas (tiling.py:1310-1330).
+__global__ void tile_blend_kernel(const __nv_bfloat16* __restrict__ dec, int Ft, int ht, int wt,
+                                  int channels, int patch, float* __restrict__ canvas,
+                                  float* __restrict__ wcanvas, int Hout, int Wout, int y0, int x0,
+                                  const float* __restrict__ mask_h, const float* __restrict__ mask_w) {
+  const int Hp = ht * patch, Wp = wt * patch;
+  const int64_t n = static_cast<int64_t>(channels) * Ft * Hp * Wp;
+  const int packed = channels * patch * patch;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int xx = static_cast<int>(i % Wp);
+    int64_t r = i / Wp;
+    const int yy = static_cast<int>(r % Hp);
+    r /= Hp;
+    const int f = static_cast<int>(r % Ft);
+    const int c = static_cast<int>(r / Ft);
+    const int h = yy / patch, ph = yy % patch, w = xx / patch, pw = xx % patch;
+    const int64_t src = ((static_cast<int64_t>(f) * ht + h) * wt + w) * packed +
+                        (c * patch + pw) * patch + ph;
+    const float m = mask_h[yy] * mask_w[xx];
+    const float val = __bfloat162float(dec[src]) * m;
+    const int64_t dst = ((static_cast<int64_t>(c) * Ft + f) * Hout + (y0 + yy)) * Wout + (x0 + xx);
+    canvas[dst] += val;
+    if (c == 0 && f == 0) wcanvas[static_cast<int64_t>(y0 + yy) * Wout + (x0 + xx)] += m;
+  }
+}
+
+// canvas[c, f, y, x] /= max(weights[y, x], 1e-8) (tiling.py:1369)
+__global__ void blend_normalize_kernel(float* __restrict__ canvas,
+                                       const float* __restrict__ wcanvas, int64_t planes,
+                                       int64_t hw) {
+  const int64_t n = planes * hw;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    canvas[i] = canvas[i] / fmaxf(wcanvas[i % hw], 1e-8f);
+  }
+}
+
+}  // namespace kino

@@ -48,17 +48,23 @@ __all__ = [
     "adaln",
     "add_rows",
     "attention",
+    "blend_normalize",
     "cfg_combine",
+    "conv3d",
     "device_status",
     "euler_velocity",
     "euler_x0",
     "gelu_tanh",
     "gemv",
+    "group_norm",
+    "latent_to_bfhwc",
     "linear",
+    "pixel_norm",
     "qk_norm_rope",
     "rms_norm",
     "silu",
     "split_rope",
+    "tile_blend",
     "timestep_embedding",
 ]
 
@@ -550,3 +556,118 @@ def timestep_embedding(
 
 def softmax_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+# ----------------------------------------------------------------------------- video VAE
+def conv3d(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    *,
+    causal: bool,
+    stride: tuple[int, int, int] = (1, 1, 1),
+    residual: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """3x3x3 conv of channels-last x (F, H, W, Cin) with an (N, 3, 3, 3, Cin) weight; with a
+    depth-to-space `stride` the weight rows must be sub-position-major (n = sub * C' + c)."""
+    _need(x, "x")
+    _need(weight, "weight")
+    if not x.is_contiguous() or not weight.is_contiguous():
+        raise ValueError("conv3d needs contiguous channels-last input and OTHWI weight")
+    x4 = x[0] if x.dim() == 5 else x
+    f, h, w, cin = x4.shape
+    n = weight.shape[0]
+    if tuple(weight.shape[1:]) != (3, 3, 3, cin):
+        raise ValueError(f"weight {tuple(weight.shape)} does not match {cin} input channels")
+    st, sh, sw = stride
+    sub = st * sh * sw
+    oshape = (f * st - (1 if st > 1 else 0), h * sh, w * sw, n // sub)
+    if out is None:
+        out = torch.empty(oshape, device=x.device, dtype=torch.bfloat16)
+    if residual is not None:
+        _need(residual, "residual")
+    args = _lib.Conv3dArgs()
+    args.x = x4.data_ptr()
+    args.frames, args.height, args.width, args.in_channels = f, h, w, cin
+    args.weight = weight.data_ptr()
+    args.out_channels = n
+    args.bias = bias.data_ptr() if bias is not None else None
+    args.residual = residual.data_ptr() if residual is not None else None
+    args.out = out.data_ptr()
+    args.causal = 1 if causal else 0
+    args.stride_t, args.stride_h, args.stride_w = st, sh, sw
+    with _timed("conv3d", 2.0 * f * h * w * n * 27 * cin, 2.0 * (x4.numel() + weight.numel() + out.numel())):
+        _lib.call("kino_conv3d", ctypes.byref(args), _stream())
+    return out
+
+
+def pixel_norm(x: torch.Tensor, eps: float = 1e-8, *, silu: bool = False,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Stepwise PixelNorm over the last (channel) axis, optionally followed by SiLU."""
+    _need(x, "x")
+    if not x.is_contiguous():
+        raise ValueError("pixel_norm needs a contiguous channels-last input")
+    if out is None:
+        out = torch.empty_like(x)
+    c = x.shape[-1]
+    with _timed("norm", 0.0, 4.0 * x.numel()):
+        _lib.call("kino_pixel_norm", _ptr(x), _ptr(out), x.numel() // c, c, eps, int(silu), _stream())
+    return out
+
+
+def group_norm(x: torch.Tensor, groups: int, weight: torch.Tensor, bias: torch.Tensor,
+               eps: float, *, silu: bool = False, out: torch.Tensor | None = None,
+               workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Affine GroupNorm(32) over channels-last x with fp32 two-pass statistics (+ SiLU). The
+    reduction's partial sums go to `workspace` (caller memory; allocated here if not given)."""
+    if groups != 32:
+        raise ValueError("the GroupNorm kernel takes 32 groups")
+    _need(x, "x")
+    if not x.is_contiguous():
+        raise ValueError("group_norm needs a contiguous channels-last input")
+    c = x.shape[-1]
+    voxels = x.numel() // c
+    need = int(_lib.load().kino_group_norm_workspace_size(voxels, c))
+    if workspace is None:
+        workspace = torch.empty(need, device=x.device, dtype=torch.uint8)
+    if out is None:
+        out = torch.empty_like(x)
+    with _timed("norm", 0.0, 8.0 * x.numel()):
+        _lib.call("kino_group_norm", _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), voxels, c, eps,
+                  int(silu), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream())
+    return out
+
+
+def latent_to_bfhwc(latent: torch.Tensor, std: torch.Tensor, mean: torch.Tensor) -> torch.Tensor:
+    """(1, C, F, H, W) bf16 latent -> (F, H, W, C) bf16 of latent * std + mean (fp32 math)."""
+    _need(latent, "latent")
+    if latent.dim() != 5 or latent.shape[0] != 1 or not latent.is_contiguous():
+        raise ValueError("latent must be a contiguous (1, C, F, H, W) tensor")
+    _, c, f, h, w = latent.shape
+    std, mean = std.float().contiguous(), mean.float().contiguous()
+    out = torch.empty((f, h, w, c), device=latent.device, dtype=torch.bfloat16)
+    with _timed("elementwise", 0.0, 4.0 * latent.numel()):
+        _lib.call("kino_latent_to_bfhwc", _ptr(latent), _ptr(std), _ptr(mean), _ptr(out), c,
+                  f * h * w, _stream())
+    return out
+
+
+def tile_blend(decoded: torch.Tensor, canvas: torch.Tensor, weights: torch.Tensor, y0: int, x0: int,
+               mask_h: torch.Tensor, mask_w: torch.Tensor, patch: int = 4) -> None:
+    """Accumulate a decoded tile (F, h, w, C * patch^2) into the fp32 (1, C, F, H, W) canvas."""
+    _need(decoded, "decoded")
+    f, h, w, packed = decoded.shape
+    c = packed // (patch * patch)
+    mask_h, mask_w = mask_h.float().contiguous(), mask_w.float().contiguous()
+    with _timed("elementwise", 0.0, 2.0 * decoded.numel() + 8.0 * decoded.numel()):
+        _lib.call("kino_tile_blend", _ptr(decoded), f, h, w, c, patch, _ptr(canvas), _ptr(weights),
+                  canvas.shape[-2], canvas.shape[-1], y0, x0, _ptr(mask_h), _ptr(mask_w), _stream())
+
+
+def blend_normalize(canvas: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+    hw = canvas.shape[-2] * canvas.shape[-1]
+    with _timed("elementwise", 0.0, 8.0 * canvas.numel()):
+        _lib.call("kino_blend_normalize", _ptr(canvas), _ptr(weights), canvas.numel() // hw, hw,
+                  _stream())
+    return canvas

@@ -220,35 +220,3 @@ def decode_tiled(p: dict, latent: torch.Tensor, v: VaeVariant, tile: int = 8, ov
             out[:, :, :, hs, ws] += dec * mask
             weights[:, :, :, hs, ws] += mask
     return out / torch.clamp(weights, min=1e-8)
-
-
-def weight_specs(v: VaeVariant):
-    """(name, shape, kind) of the decoder's parameters in draw order."""
-    specs = [
-        ("per_channel_statistics.std_of_means", (v.latent_channels,), "ones_f32"),
-        ("per_channel_statistics.mean_of_means", (v.latent_channels,), "zeros_f32"),
-    ]
-    c = v.top_width
-    specs += [("conv_in.weight", (c, 3, 3, 3, v.latent_channels), "normal"),
-              ("conv_in.bias", (c,), "zeros")]
-    for i, blk in enumerate(v.blocks):
-        if blk[0] == "res":
-            for j in range(blk[1]):
-                a = f"up_blocks.{i}.res_blocks.{j}"
-                for k in (1, 2):
-                    if v.norm == "group32":
-                        specs += [(f"{a}.norm{k}.weight", (c,), "ones"),
-                                  (f"{a}.norm{k}.bias", (c,), "zeros")]
-                    specs += [(f"{a}.conv{k}.weight", (c, 3, 3, 3, c), "normal"),
-                              (f"{a}.conv{k}.bias", (c,), "zeros")]
-        else:
-            stride, mult = blk[1], blk[2]
-            cout = c // mult
-            specs += [(f"up_blocks.{i}.conv.weight", (math.prod(stride) * cout, 3, 3, 3, c), "normal"),
-                      (f"up_blocks.{i}.conv.bias", (math.prod(stride) * cout,), "zeros")]
-            c = cout
-    if v.norm == "group32":
-        specs += [("norm_out.weight", (c,), "ones"), ("norm_out.bias", (c,), "zeros")]
-    specs += [("conv_out.weight", (v.out_channels * v.patch ** 2, 3, 3, 3, c), "normal"),
-              ("conv_out.bias", (v.out_channels * v.patch ** 2,), "zeros")]
-    return specs

@@ -15,7 +15,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def _declared() -> list[str]:
     text = (ROOT / "include" / "kino.h").read_text()
-    return sorted(set(re.findall(r"^\s*(?:kino_status|int|const char\*)\s+(kino_\w+)\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:kino_status|int|int64_t|const char\*)\s+(kino_\w+)\(", text, re.M)))
 
 
 def test_library_exports_every_declared_symbol():
