@@ -228,6 +228,28 @@ kino_status kino_group_norm(const void* x, const void* weight, const void* bias,
                             int64_t voxels, int64_t channels, float eps, int apply_silu,
                             void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Largest scratch kino_group_norm_noalloc can use: 80 KiB, enough for every shape
+ * kino_group_norm accepts (its statistics use at most 592 partial sums per group). */
+#define KINO_GROUP_NORM_NOALLOC_SCRATCH_BYTES 81920
+
+/* kino_group_norm without a caller workspace, for callers that cannot allocate device memory:
+ * hosts that own every device allocation themselves (a plugin inside a media or inference server
+ * with a fixed memory budget, an allocator that hands out only tensors) or pipelines that must
+ * not call cudaMalloc/cudaFree mid-run, since those calls can synchronise the device. This entry
+ * point has no counterpart in the reference (MLX allocates its own temporaries).
+ *
+ * Its statistics scratch is one fixed array inside the library (the size above), which every GPU
+ * that loads the library keeps until the process exits; nothing is allocated per call. The first
+ * call on each device looks up that array's device address (cudaGetSymbolAddress) with the device
+ * current; make that first call before any stream capture. Every call shares the one array and
+ * leaves its contents behind: each call writes every scratch word before reading it, so no
+ * clearing is needed, but calls that overlap on the GPU (for example on two streams) race on the
+ * array and must be serialised by the caller. Shapes needing more scratch than the maximum are
+ * refused with KINO_ENOTSUPPORTED. Same arguments and results as kino_group_norm otherwise. */
+kino_status kino_group_norm_noalloc(const void* x, const void* weight, const void* bias,
+                                    void* out, int64_t voxels, int64_t channels, float eps,
+                                    int apply_silu, void* stream);
+
 /* latent (channels, voxels) bf16 (BCFHW, batch 1) -> bf16(x * std + mean) channels-last.
  * Replaces PerChannelStatistics.denormalize + the BCFHW->BFHWC transpose
  * (kinomlx/models/ltx2/video_vae/decoder.py:227-233). */

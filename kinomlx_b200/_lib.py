@@ -145,6 +145,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_pixel_norm": (c_int, [P, P, I64, I64, F, c_int, P]),
     "kino_group_norm_workspace_size": (c_int64, [I64, I64]),
     "kino_group_norm": (c_int, [P, P, P, P, I64, I64, F, c_int, P, I64, P]),
+    "kino_group_norm_noalloc": (c_int, [P, P, P, P, I64, I64, F, c_int, P]),
     "kino_latent_to_bfhwc": (c_int, [P, P, P, P, I64, I64, P]),
     "kino_tile_blend": (c_int, [P, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, P, P, P]),
     "kino_blend_normalize": (c_int, [P, P, I64, I64, P]),

@@ -14,6 +14,12 @@
 #include "kino_ops.cuh"
 #include "kino_vae.cuh"
 
+// Scratch of kino_group_norm_noalloc: a fixed device array that every GPU loading this library
+// holds until the process exits. Host code only sees a stand-in symbol for it, so its device
+// address is looked up once per device (cudaGetSymbolAddress, with that device current) and
+// passed to the kernels like any workspace pointer.
+static __device__ __align__(256) unsigned char g_group_norm_scratch[KINO_GROUP_NORM_NOALLOC_SCRATCH_BYTES];
+
 namespace {
 
 thread_local char g_err[512] = {0};
@@ -176,6 +182,31 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
 int gn_parts(int64_t voxels) {
   int64_t p = (voxels + 31) / 32;
   return static_cast<int>(p < 592 ? (p < 1 ? 1 : p) : 592);
+}
+
+void* group_norm_scratch_address(kino_status* status) {
+  static std::mutex lock;
+  static void* addresses[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *status = fail(KINO_ECUDA, "kino_group_norm_noalloc: no current device (%s)",
+                   cudaGetErrorString(e));
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> guard(lock);
+  if (addresses[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_group_norm_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *status = fail(KINO_ECUDA, "kino_group_norm_noalloc: cudaGetSymbolAddress failed (%s)",
+                     cudaGetErrorString(e));
+      return nullptr;
+    }
+    addresses[dev] = p;
+  }
+  *status = KINO_OK;
+  return addresses[dev];
 }
 
 }  // namespace
@@ -621,6 +652,22 @@ kino_status kino_group_norm(const void* x, const void* weight, const void* bias,
       xb, static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(bias),
       static_cast<__nv_bfloat16*>(out), voxels, c, ws, parts, apply_silu);
   return check_launch("kino_group_norm");
+}
+
+kino_status kino_group_norm_noalloc(const void* x, const void* weight, const void* bias,
+                                    void* out, int64_t voxels, int64_t channels, float eps,
+                                    int apply_silu, void* stream) {
+  const int64_t need = kino_group_norm_workspace_size(voxels, channels);
+  if (need > KINO_GROUP_NORM_NOALLOC_SCRATCH_BYTES)
+    return fail(KINO_ENOTSUPPORTED,
+                "kino_group_norm_noalloc: this shape needs %lld bytes of scratch, above the "
+                "static maximum of %d bytes; use kino_group_norm with a caller workspace",
+                (long long)need, KINO_GROUP_NORM_NOALLOC_SCRATCH_BYTES);
+  kino_status st = KINO_OK;
+  void* scratch = group_norm_scratch_address(&st);
+  if (scratch == nullptr) return st;
+  return kino_group_norm(x, weight, bias, out, voxels, channels, eps, apply_silu, scratch,
+                         KINO_GROUP_NORM_NOALLOC_SCRATCH_BYTES, stream);
 }
 
 kino_status kino_latent_to_bfhwc(const void* latent, const float* std_of_means,
