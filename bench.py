@@ -13,8 +13,9 @@ far more than the 126 MB L2, so no explicit L2 flush is needed between timed ste
 --impl reference times the reference's CPU path for the same workload: the reference (MLX,
 Python >= 3.15) cannot run on this box, so that arm times the CPU restatement of its formulas
 (oracle/) on all host cores, one double + one single block per step, extrapolated x8 / x24.
-With N > 1 (torchrun) each GPU runs an independent replica (no data-path collective); the step
-time is the max over ranks.
+With N > 1 (torchrun) the same step runs with Ulysses sequence parallelism: each rank holds
+1/N of the text and image tokens, q/k/v and the attention output cross an NCCL all-to-all around
+every attention (strong scaling); the step time is the max over ranks.
 """
 
 from __future__ import annotations
@@ -249,6 +250,7 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
     from kinomlx_b200.flux2 import config as fcfg
     from kinomlx_b200.flux2 import sampling
     from kinomlx_b200.flux2.transformer import Flux2Transformer
+    from kinomlx_b200.sequence_parallel import SequenceParallel
     from kinomlx_b200.synthetic import flux_weights, normal
 
     device = torch.device("cuda", local)
@@ -257,10 +259,13 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
     nt, side = 512, 64
     ni = side * side
     weights = flux_weights(v, seed=42, device=device)
-    model = Flux2Transformer(weights, v, device)
+    # N > 1: Ulysses sequence parallelism over all ranks (strong scaling: the same step, its
+    # tokens sharded, one all-to-all each way around every attention)
+    model = Flux2Transformer(weights, v, device, sp=SequenceParallel() if world > 1 else None)
     del weights
     torch.cuda.empty_cache()
-    noise = normal((1, ni, v.in_channels), seed=43, device=device)
+    i0, i1 = model.sp.shard(ni)
+    noise = normal((1, ni, v.in_channels), seed=43, device=device)[:, i0:i1].contiguous()
     text = normal((1, nt, v.context_dim), seed=44, device=device)
     ids = torch.zeros((1, nt + ni, 2), dtype=torch.int64)
     ids[0, nt:, 0] = torch.arange(side).repeat_interleave(side)
@@ -386,13 +391,13 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
             "warmup": args.warmup,
             "ms_per_step": round(ms, 3),
             "higher_is_better": False,
-            "scaling": "weak",
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) latents and text, random-init N(0,0.02) weights)",
             "config": {
                 "workload": WORKLOAD,
-                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "parallelism": f"ulysses sequence parallel x{world} (NCCL all-to-all)" if world > 1 else "single GPU",
                 "l2": "no flush: 9.4 GB of weights stream per step, inputs exceed the 126 MB L2",
                 "step_gflop": round(step_flops() / 1e9, 1),
             },

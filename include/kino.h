@@ -185,6 +185,20 @@ kino_status kino_euler_x0(const void* x, const void* v, float sigma, float ratio
 kino_status kino_add_rows(const void* a, const void* b, void* out, int64_t rows, int64_t n,
                           void* stream);
 
+/* ------------------------------------------------------------------ sequence parallelism
+ * No reference counterpart (KinoMLX runs on one device): the layout steps around the all-to-all
+ * of Ulysses sequence parallelism. width = heads * 128 must split into `parts` head groups. */
+
+/* dst[j, t, :] = src[t, j*width/parts : (j+1)*width/parts]; src rows at stride ld. */
+kino_status kino_heads_pack(const void* src, int64_t ld, void* dst, int64_t tokens,
+                           int64_t width, int64_t parts, void* stream);
+
+/* dst[t, j*width/parts + c] = src[j, t, c], times gate[t, head] (bf16 product) when gate is not
+ * NULL (the LTX per-head gate, kinomlx/models/ltx2/transformer/attention.py:364-368). */
+kino_status kino_heads_unpack(const void* src, void* dst, int64_t ld, int64_t tokens,
+                             int64_t width, int64_t parts, const void* gate, int64_t ld_gate,
+                             void* stream);
+
 /* [cos(t f_i), sin(t f_i)] features, f_i = exp(-ln(10000) i / (dim/2)); t: fp32 device [batch].
  * Replaces kinomlx/models/flux2/transformer.py:238-241 and
  * kinomlx/models/ltx2/transformer/timestep.py:13-28. */

@@ -140,6 +140,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_euler_velocity": (c_int, [P, P, F, P, I64, P]),
     "kino_euler_x0": (c_int, [P, P, F, F, P, I64, P]),
     "kino_add_rows": (c_int, [P, P, P, I64, I64, P]),
+    "kino_heads_pack": (c_int, [P, I64, P, I64, I64, I64, P]),
+    "kino_heads_unpack": (c_int, [P, P, I64, I64, I64, I64, P, I64, P]),
     "kino_timestep_embedding": (c_int, [P, P, I64, I64, P]),
     "kino_conv3d": (c_int, [POINTER(Conv3dArgs), P]),
     "kino_pixel_norm": (c_int, [P, P, I64, I64, F, c_int, P]),

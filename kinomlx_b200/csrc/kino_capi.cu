@@ -539,6 +539,38 @@ kino_status kino_add_rows(const void* a, const void* b, void* out, int64_t rows,
   return check_launch("kino_add_rows");
 }
 
+kino_status kino_heads_pack(const void* src, int64_t ld, void* dst, int64_t tokens,
+                           int64_t width, int64_t parts, void* stream) {
+  if (src == nullptr || dst == nullptr) return fail(KINO_EINVAL, "kino_heads_pack: null");
+  if (parts < 1 || width % (parts * 128) || ld % 8 || !aligned16(src) || !aligned16(dst))
+    return fail(KINO_ENOTSUPPORTED, "kino_heads_pack: width must split into 128-wide heads per part");
+  int64_t blocks = (tokens * width / 8 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) return KINO_OK;
+  kino::heads_pack_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                            static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), ld, static_cast<__nv_bfloat16*>(dst),
+      static_cast<int>(tokens), static_cast<int>(width), static_cast<int>(parts));
+  return check_launch("kino_heads_pack");
+}
+
+kino_status kino_heads_unpack(const void* src, void* dst, int64_t ld, int64_t tokens,
+                             int64_t width, int64_t parts, const void* gate, int64_t ld_gate,
+                             void* stream) {
+  if (src == nullptr || dst == nullptr) return fail(KINO_EINVAL, "kino_heads_unpack: null");
+  if (parts < 1 || width % (parts * 128) || ld % 8 || !aligned16(src) || !aligned16(dst))
+    return fail(KINO_ENOTSUPPORTED, "kino_heads_unpack: width must split into 128-wide heads per part");
+  int64_t blocks = (tokens * width / 8 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) return KINO_OK;
+  kino::heads_unpack_kernel<<<static_cast<unsigned>(blocks), 256, 0,
+                              static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst), ld,
+      static_cast<int>(tokens), static_cast<int>(width), static_cast<int>(parts),
+      static_cast<const __nv_bfloat16*>(gate), ld_gate);
+  return check_launch("kino_heads_unpack");
+}
+
 kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, int64_t dim,
                                     void* stream) {
   if (t == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_timestep_embedding: null");

@@ -367,6 +367,55 @@ __global__ void add_rows_kernel(const __nv_bfloat16* __restrict__ a,
   }
 }
 
+// ----------------------------------------------------------------------------- Ulysses packing
+// Sequence parallelism (no reference counterpart: the reference runs on one device). Before an
+// attention, each rank's token rows (tokens, heads * 128) are cut into `parts` head groups and
+// laid out (parts, tokens, heads/parts * 128), so chunk j goes to rank j in one all-to-all and
+// arrives as a contiguous token-major block; after the attention the reverse unpack rebuilds the
+// rows, optionally multiplying each head by its gate: bf16(bf16(o) * gate[t, head]).
+__global__ void heads_pack_kernel(const __nv_bfloat16* __restrict__ src, int64_t ld,
+                                  __nv_bfloat16* __restrict__ dst, int tokens, int width,
+                                  int parts) {
+  const int chunk = width / parts;  // elements per rank per token
+  const int64_t nv = (static_cast<int64_t>(tokens) * width) >> 3;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i * 8;
+    const int t = static_cast<int>(e / width);
+    const int c = static_cast<int>(e % width);
+    const int j = c / chunk, cc = c % chunk;
+    *reinterpret_cast<uint4*>(dst + (static_cast<int64_t>(j) * tokens + t) * chunk + cc) =
+        *reinterpret_cast<const uint4*>(src + static_cast<int64_t>(t) * ld + c);
+  }
+}
+
+__global__ void heads_unpack_kernel(const __nv_bfloat16* __restrict__ src,
+                                    __nv_bfloat16* __restrict__ dst, int64_t ld, int tokens,
+                                    int width, int parts, const __nv_bfloat16* __restrict__ gate,
+                                    int64_t ld_gate) {
+  const int chunk = width / parts;
+  const int64_t nv = (static_cast<int64_t>(tokens) * width) >> 3;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i * 8;
+    const int t = static_cast<int>(e / width);
+    const int c = static_cast<int>(e % width);
+    const int j = c / chunk, cc = c % chunk;
+    const uint4 raw =
+        *reinterpret_cast<const uint4*>(src + (static_cast<int64_t>(j) * tokens + t) * chunk + cc);
+    if (gate == nullptr) {
+      *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(t) * ld + c) = raw;
+    } else {
+      const float g = __bfloat162float(gate[static_cast<int64_t>(t) * ld_gate + c / 128]);
+      float f[8];
+      load8(src + (static_cast<int64_t>(j) * tokens + t) * chunk + cc, f);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) f[q] = f[q] * g;
+      store8(dst + static_cast<int64_t>(t) * ld + c, f);
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------- GEMV (M = batch)
 // y[b, n] = sum_k act(x[b, k]) * w[n, k] + bias[n]; act = identity or SiLU rounded to bf16
 // (kinomlx/models/flux2/transformer.py:223-258 Modulation / TimestepEmbedding,

@@ -89,9 +89,11 @@ def denoise(
     cfg = negative is not None and guidance != 1.0
     conditioned = text if not cfg else torch.cat([text, negative])
     prepared = model.prepare(conditioned, ids)
-    current = noise.to(model.device, torch.bfloat16).clone()
+    i0, i1 = model.sp.shard(noise.shape[1])
+    current = noise[:, i0:i1].to(model.device, torch.bfloat16).clone()
     for index in range(len(sigmas) - 1):
         denoise_step(model, prepared, current, sigmas, index, guidance=guidance, cfg=cfg)
+    current = model.sp.all_gather_tokens(current)
     if check_finite:
         ops.device_status()
         if not bool(torch.isfinite(current).all()):

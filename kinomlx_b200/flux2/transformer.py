@@ -21,6 +21,7 @@ from dataclasses import dataclass
 import torch
 
 from .. import ops
+from ..sequence_parallel import SequenceParallel
 from .config import FluxVariant
 
 
@@ -69,7 +70,10 @@ class Flux2Transformer:
     """Device Flux2 MMDiT. `weights` uses the reference checkpoint names."""
 
     def __init__(self, weights: dict[str, torch.Tensor], variant: FluxVariant,
-                 device: torch.device | str = "cuda"):
+                 device: torch.device | str = "cuda", *, sp: SequenceParallel | None = None):
+        """`sp` shards the tokens over a process group (Ulysses); each rank then holds
+        Nt/P text and Ni/P image tokens and passes its own latent shard to `run`."""
+        self.sp = sp if sp is not None else SequenceParallel.single()
         if variant.mlp != "gelu_tanh":
             raise ValueError(
                 "this build runs the GELU-tanh MLP variant; SwiGLU (Klein) is not implemented"
@@ -129,6 +133,13 @@ class Flux2Transformer:
         text = text.to(self.device, torch.bfloat16)
         projected = ops.linear(text, self.context_embedder)
         cos, sin = rotary_positions(ids, self.v)
+        if self.sp.size > 1:
+            nt = text.shape[1]
+            t0, t1 = self.sp.shard(nt)
+            i0, i1 = self.sp.shard(ids.shape[1] - nt)
+            rows = torch.cat([torch.arange(t0, t1), nt + torch.arange(i0, i1)])
+            projected = projected[:, t0:t1].contiguous()
+            cos, sin = cos[:, rows].contiguous(), sin[:, rows].contiguous()
         return PreparedText(projected, cos.to(self.device), sin.to(self.device))
 
     def workspace(self, batch: int, nt: int, ni: int) -> _Workspace:
@@ -153,7 +164,7 @@ class Flux2Transformer:
                              rope=ops.ROPE_PAIRS, cos=cos, sin=sin, table_offset=0)
             ops.qk_norm_rope(part[:, nt:], heads=h, weight=p[wi], norm=ops.QKNORM_PER_HEAD,
                              rope=ops.ROPE_PAIRS, cos=cos, sin=sin, table_offset=nt)
-        ops.attention([q], [k], [v], [q], heads=h)
+        self.sp.attention(q, k, v, q, heads=h)
         ops.linear(q[:, nt:], p["to_out"], img, kind=ops.EPI_GATED_RESIDUAL, residual=img,
                    gate=m(0, 2))
         ops.linear(q[:, :nt], p["to_add_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
@@ -177,7 +188,7 @@ class Flux2Transformer:
                          rope=ops.ROPE_PAIRS, cos=cos, sin=sin)
         ops.qk_norm_rope(k, heads=h, weight=p["norm_k"], norm=ops.QKNORM_PER_HEAD,
                          rope=ops.ROPE_PAIRS, cos=cos, sin=sin)
-        ops.attention([q], [k], [v], [q], heads=h)
+        self.sp.attention(q, k, v, q, heads=h)
         ops.linear(ws.big[..., 2 * d :], p["to_out"], ws.stream, kind=ops.EPI_GATED_RESIDUAL,
                    residual=ws.stream, gate=sm(2))
 

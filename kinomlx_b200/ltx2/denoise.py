@@ -28,10 +28,12 @@ def denoise_loop(model: LTXVideoTransformer, latent: torch.Tensor, context: torc
                  positions: torch.Tensor, sigmas=DISTILLED_STAGE_1_SIGMAS,
                  check_finite: bool = True) -> torch.Tensor:
     prepared = model.prepare(context, positions)
-    x = latent.to(model.device, torch.bfloat16).clone()
+    t0, t1 = model.sp.shard(latent.shape[1])
+    x = latent[:, t0:t1].to(model.device, torch.bfloat16).clone()
     values = fp32(sigmas)
     for s, n in zip(values[:-1], values[1:]):
         denoise_step(model, prepared, x, s, n)
+    x = model.sp.all_gather_tokens(x)
     if check_finite:
         ops.device_status()
         if not bool(torch.isfinite(x).all()):

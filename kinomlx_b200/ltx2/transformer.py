@@ -17,6 +17,7 @@ from dataclasses import dataclass
 import torch
 
 from .. import ops
+from ..sequence_parallel import SequenceParallel
 from .config import LTXVariant
 
 
@@ -83,7 +84,10 @@ class LTXVideoTransformer:
     """Device LTX-2 video DiT. `weights` uses the reference checkpoint names."""
 
     def __init__(self, weights: dict[str, torch.Tensor], variant: LTXVariant,
-                 device: torch.device | str = "cuda"):
+                 device: torch.device | str = "cuda", *, sp: SequenceParallel | None = None):
+        """`sp` shards the video tokens over a process group (Ulysses sequence parallelism for
+        the self-attention; the text cross-attention stays local with the full context)."""
+        self.sp = sp if sp is not None else SequenceParallel.single()
         self.v = variant
         self.device = torch.device(device)
         dev = lambda t: t.to(self.device, torch.bfloat16).contiguous()
@@ -142,6 +146,9 @@ class LTXVideoTransformer:
 
     def prepare(self, context: torch.Tensor, positions: torch.Tensor) -> PreparedContext:
         cos, sin = precompute_freqs_cis(positions.cpu(), self.v)
+        if self.sp.size > 1:
+            t0, t1 = self.sp.shard(cos.shape[2])
+            cos, sin = cos[:, :, t0:t1].contiguous(), sin[:, :, t0:t1].contiguous()
         return PreparedContext(context.to(self.device, torch.bfloat16).contiguous(),
                                cos.to(self.device), sin.to(self.device))
 
@@ -181,7 +188,7 @@ class LTXVideoTransformer:
                          cos=prepared.cos, sin=prepared.sin, eps=v.eps)
         ops.qk_norm_rope(k, heads=h, weight=p["kn1"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_SPLIT,
                          cos=prepared.cos, sin=prepared.sin, eps=v.eps)
-        ops.attention([q], [k], [vv], [q], heads=h, gate=[ws.gates])
+        self.sp.attention(q, k, vv, q, heads=h, gate=ws.gates)
         ops.linear(q, p["o1_w"], x, bias=p["o1_b"], kind=ops.EPI_GATED_RESIDUAL, residual=x,
                    gate=val(2))
         # text cross-attention with the prompt-modulated context

@@ -671,3 +671,29 @@ def blend_normalize(canvas: torch.Tensor, weights: torch.Tensor) -> torch.Tensor
         _lib.call("kino_blend_normalize", _ptr(canvas), _ptr(weights), canvas.numel() // hw, hw,
                   _stream())
     return canvas
+
+
+# ----------------------------------------------------------------------------- sequence parallel
+def heads_pack(src: torch.Tensor, parts: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """(tokens, width) rows (any row stride) -> (parts, tokens, width / parts) head groups."""
+    _need(src, "src")
+    tokens, width = src.shape[-2], src.shape[-1]
+    if out is None:
+        out = torch.empty((parts, tokens, width // parts), device=src.device, dtype=torch.bfloat16)
+    with _timed("pack", 0.0, 4.0 * tokens * width):
+        _lib.call("kino_heads_pack", _ptr(src), src.stride(-2), _ptr(out), tokens, width, parts,
+                  _stream())
+    return out
+
+
+def heads_unpack(src: torch.Tensor, out: torch.Tensor, gate: torch.Tensor | None = None) -> torch.Tensor:
+    """(parts, tokens, width / parts) -> (tokens, width) rows of `out` (any row stride), times the
+    per-(token, head) gate if given."""
+    _need(src, "src")
+    _need(out, "out")
+    parts, tokens, chunk = src.shape
+    width = parts * chunk
+    with _timed("pack", 0.0, 4.0 * tokens * width):
+        _lib.call("kino_heads_unpack", _ptr(src), _ptr(out), out.stride(-2), tokens, width, parts,
+                  _ptr(gate), gate.stride(-2) if gate is not None else 0, _stream())
+    return out

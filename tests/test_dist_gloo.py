@@ -60,3 +60,85 @@ def test_shard_helpers():
     with pytest.raises(ValueError):
         dist.head_shards(24, 5)
     assert dist.cfg_groups(4) == [[0, 1], [2, 3]]
+
+
+class _CpuOps:
+    """CPU stand-ins for the three device ops SequenceParallel launches, so its all-to-all
+    ordering and layout logic can run on gloo ranks."""
+
+    @staticmethod
+    def heads_pack(src, parts, out):
+        tokens, width = src.shape
+        out.copy_(src.reshape(tokens, parts, width // parts).transpose(0, 1))
+        return out
+
+    @staticmethod
+    def heads_unpack(src, out, gate=None):
+        parts, tokens, chunk = src.shape
+        rows = src.transpose(0, 1).reshape(tokens, parts * chunk)
+        if gate is not None:
+            rows = (rows.reshape(tokens, -1, 128) * gate[..., None]).reshape(tokens, -1)
+        out.copy_(rows)
+        return out
+
+    @staticmethod
+    def attention(q, k, v, out, heads, gate=None):
+        from oracle.fused_ops import sdpa
+
+        b, t, w = q[0].shape
+        d = w // heads
+        split = lambda x: x.reshape(b, x.shape[1], heads, d).transpose(1, 2)
+        o = sdpa(split(q[0]), split(k[0]), split(v[0]), d ** -0.5).transpose(1, 2).reshape(b, t, w)
+        out[0].copy_(o)
+
+
+def _sp_worker(rank: int, size: int, port: int, queue) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(size),
+                      RANK=str(rank), LOCAL_RANK=str(rank))
+    import torch
+
+    from kinomlx_b200 import dist, sequence_parallel
+
+    sequence_parallel.ops = _CpuOps
+    dist.init("gloo", timeout_s=60)
+    heads, tokens = 4, 12
+    gen = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn((1, tokens, heads * 128), generator=gen).to(torch.bfloat16) for _ in range(3))
+    gate = torch.rand((1, tokens, heads), generator=gen).to(torch.bfloat16)
+    sp = sequence_parallel.SequenceParallel()
+    t0, t1 = sp.shard(tokens)
+    out = torch.zeros((1, t1 - t0, heads * 128), dtype=torch.bfloat16)
+    sp.attention(q[:, t0:t1], k[:, t0:t1], v[:, t0:t1], out, heads=heads, gate=gate[:, t0:t1])
+    full = sp.all_gather_tokens(out)
+    import torch.distributed as tdist
+
+    tdist.destroy_process_group()
+    queue.put((rank, full.float().numpy().tolist()))
+
+
+def test_two_gloo_ranks_ulysses_attention_equals_full_attention():
+    """The sequence-parallel all-to-all attention on 2 gloo ranks equals one-device attention
+    with the per-head gate (the layout and ordering logic that runs on NCCL on the GPUs)."""
+    import torch
+
+    from oracle.fused_ops import sdpa
+
+    size, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_sp_worker, args=(r, size, port, queue)) for r in range(size)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=180) for _ in range(size))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    heads, tokens = 4, 12
+    gen = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn((1, tokens, heads * 128), generator=gen).to(torch.bfloat16) for _ in range(3))
+    gate = torch.rand((1, tokens, heads), generator=gen).to(torch.bfloat16)
+    split = lambda x: x.reshape(1, tokens, heads, 128).transpose(1, 2)
+    o = sdpa(split(q), split(k), split(v), 128 ** -0.5).transpose(1, 2)
+    expect = (o * gate[..., None]).reshape(1, tokens, heads * 128)
+    for r in range(size):
+        assert torch.equal(torch.tensor(results[r]).to(torch.bfloat16), expect)

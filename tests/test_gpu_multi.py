@@ -1,0 +1,107 @@
+"""Multi-GPU paths on NCCL (skipped with fewer than 2 GPUs): Ulysses sequence parallelism of the
+Flux2 and LTX-2 denoise loops against the same loop on one GPU, same weights and inputs.
+
+Only the key order inside each attention changes (rank-major), so the results agree to fp32
+summation-order noise: cosine >= 0.9999 and max relative error <= 1e-2.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs"),
+]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _flux_case():
+    from oracle import flux2 as ref
+    from kinomlx_b200.flux2.config import FluxVariant
+    from kinomlx_b200.synthetic import flux_weights, normal
+
+    v = FluxVariant(dim=1024, heads=8, mlp="gelu_tanh", mlp_hidden=4096, rope_axes=(64, 64),
+                    rope_theta=10000.0, in_channels=64, context_dim=256, double_blocks=2,
+                    single_blocks=2)
+    w = flux_weights(v, seed=42)
+    nt, side = 64, 16
+    noise = normal((1, side * side, v.in_channels), seed=43)
+    text = normal((1, nt, v.context_dim), seed=44)
+    ids = torch.cat([torch.zeros((1, nt, 2), dtype=torch.int64), ref.image_ids(side, side, 2)], 1)
+    return v, w, noise, text, ids
+
+
+def _ltx_case():
+    from oracle import ltx2 as ref
+    from kinomlx_b200.ltx2.config import LTXVariant
+    from kinomlx_b200.synthetic import ltx_weights, normal
+
+    v = LTXVariant(dim=1024, heads=8, context_dim=1024, blocks=2)
+    w = ltx_weights(v, seed=7)
+    grid = (2, 8, 8)
+    latent = normal((1, 128, 128), seed=8)
+    context = normal((1, 32, 1024), seed=9)
+    pos = ref.pixel_coords(ref.patch_grid_bounds(*grid))
+    return v, w, latent, context, pos
+
+
+def _run(case: str, device, sp=None):
+    if case == "flux":
+        from kinomlx_b200.flux2 import sampling
+        from kinomlx_b200.flux2.transformer import Flux2Transformer
+
+        v, w, noise, text, ids = _flux_case()
+        model = Flux2Transformer(w, v, device, sp=sp)
+        return sampling.denoise(model, noise, text, ids, sigmas=sampling.linear_sigmas(3))
+    from kinomlx_b200.ltx2 import denoise as ldn
+    from kinomlx_b200.ltx2.transformer import LTXVideoTransformer
+
+    v, w, latent, context, pos = _ltx_case()
+    model = LTXVideoTransformer(w, v, device, sp=sp)
+    return ldn.denoise_loop(model, latent, context, pos, sigmas=ldn.DISTILLED_STAGE_1_SIGMAS[5:])
+
+
+def _worker(rank: int, size: int, port: int, case: str, queue) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(size),
+                      RANK=str(rank), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    from kinomlx_b200 import dist
+    from kinomlx_b200.sequence_parallel import SequenceParallel
+
+    dist.init("nccl", timeout_s=120)
+    out = _run(case, torch.device("cuda", rank), SequenceParallel())
+    torch.cuda.synchronize()
+    import torch.distributed as tdist
+
+    tdist.destroy_process_group()
+    queue.put((rank, out.float().cpu().numpy().tolist()))
+
+
+@pytest.mark.parametrize("case", ["flux", "ltx"])
+def test_ulysses_two_gpus_matches_one_gpu(cuda_device, case):
+    size, port = 2, _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_worker, args=(r, size, port, case, queue)) for r in range(size)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=600) for _ in range(size))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    expect = _run(case, cuda_device).float().cpu()
+    for r in range(size):
+        got = torch.tensor(results[r])
+        cos = float(torch.nn.functional.cosine_similarity(got.flatten(), expect.flatten(), dim=0))
+        max_rel = float((got - expect).abs().max() / expect.abs().max())
+        assert cos >= 0.9999 and max_rel <= 1e-2, (case, r, cos, max_rel)
