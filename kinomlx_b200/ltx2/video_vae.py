@@ -171,15 +171,14 @@ class VideoDecoder:
         return ops.conv3d(x, *self.conv_out, causal=causal)
 
     def decode_tiled(self, latent: torch.Tensor, *, tile: int = 8, overlap: int = 2,
-                     tiles: list[int] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+                     tiles: list[int] | None = None, canvas: torch.Tensor | None = None,
+                     weights: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
         """Tiled decode (tiling.py:1053-1386, time untiled): returns the fp32 (1, C, F, H, W)
         canvas of weighted tile sums and the (H, W) weight canvas, before normalisation. `tiles`
         restricts the work to some tile indices (a rank's share on several GPUs)."""
         _, _, f, h, w = latent.shape
         scale = self.spatial_scale
         plan = tile_plan(h, w, tile, overlap, scale)
-        frames = None
-        canvas = weights = None
         for idx, (h0, h1, w0, w1, y0, x0, mh, mw) in enumerate(plan):
             if tiles is not None and idx not in tiles:
                 continue

@@ -1,5 +1,6 @@
-"""Multi-GPU paths on NCCL (skipped with fewer than 2 GPUs): Ulysses sequence parallelism of the
-Flux2 and LTX-2 denoise loops against the same loop on one GPU, same weights and inputs.
+"""Multi-GPU paths on NCCL (skipped with fewer than 2 GPUs) against the same computation on one
+GPU, same weights and inputs: Ulysses sequence parallelism of the Flux2 and LTX-2 denoise loops,
+the CFG branch split, and the VAE tile scatter.
 
 Only the key order inside each attention changes (rank-major), so the results agree to fp32
 summation-order noise: cosine >= 0.9999 and max relative error <= 1e-2.
@@ -56,7 +57,32 @@ def _ltx_case():
     return v, w, latent, context, pos
 
 
+MINI_VAE = (("res", 1), ("d2s", (2, 2, 2), 2), ("res", 1), ("d2s", (1, 2, 2), 1), ("res", 1))
+
+
+def _vae_case(device):
+    from kinomlx_b200.ltx2 import video_vae as vae
+    from kinomlx_b200.synthetic import make_weights, normal
+
+    v = vae.VaeVariant(norm="group32", causal=True, top_width=256, blocks=MINI_VAE)
+    w = make_weights(vae.vae_weight_specs(v), seed=13)
+    return vae.VideoDecoder(w, v, device), normal((1, 128, 2, 7, 10), seed=14).to(device)
+
+
 def _run(case: str, device, sp=None):
+    if case == "vae":
+        dec, latent = _vae_case(device)
+        return dec.decode(latent, tile=4, overlap=1)
+    if case == "cfg":
+        from kinomlx_b200.flux2 import sampling
+        from kinomlx_b200.flux2.transformer import Flux2Transformer
+        from kinomlx_b200.synthetic import normal
+
+        v, w, noise, text, ids = _flux_case()
+        negative = normal(tuple(text.shape), seed=45)
+        model = Flux2Transformer(w, v, device)
+        return sampling.denoise(model, noise, text, ids, sigmas=sampling.linear_sigmas(3),
+                                negative=negative, guidance=4.0)
     if case == "flux":
         from kinomlx_b200.flux2 import sampling
         from kinomlx_b200.flux2.transformer import Flux2Transformer
@@ -79,7 +105,31 @@ def _worker(rank: int, size: int, port: int, case: str, queue) -> None:
     from kinomlx_b200.sequence_parallel import SequenceParallel
 
     dist.init("nccl", timeout_s=120)
-    out = _run(case, torch.device("cuda", rank), SequenceParallel())
+    device = torch.device("cuda", rank)
+    if case == "cfg":
+        from kinomlx_b200.flux2 import sampling
+        from kinomlx_b200.flux2.transformer import Flux2Transformer
+        from kinomlx_b200.multi_gpu import CfgSplit, cfg_split_step
+        from kinomlx_b200.synthetic import normal
+
+        cfg = CfgSplit()
+        v, w, noise, text, ids = _flux_case()
+        negative = normal(tuple(text.shape), seed=45)
+        model = Flux2Transformer(w, v, device, sp=cfg.sp)
+        prepared = model.prepare(text if cfg.branch == 0 else negative, ids)
+        i0, i1 = cfg.sp.shard(noise.shape[1])
+        current = noise[:, i0:i1].to(device).clone()
+        sig = sampling.linear_sigmas(3)
+        for i in range(3):
+            cfg_split_step(model, prepared, current, sig, i, 4.0, cfg)
+        out = cfg.sp.all_gather_tokens(current)
+    elif case == "vae":
+        from kinomlx_b200.multi_gpu import decode_tiles_distributed
+
+        dec, latent = _vae_case(device)
+        out = decode_tiles_distributed(dec, latent, tile=4, overlap=1)
+    else:
+        out = _run(case, device, SequenceParallel())
     torch.cuda.synchronize()
     import torch.distributed as tdist
 
@@ -87,8 +137,10 @@ def _worker(rank: int, size: int, port: int, case: str, queue) -> None:
     queue.put((rank, out.float().cpu().numpy().tolist()))
 
 
-@pytest.mark.parametrize("case", ["flux", "ltx"])
-def test_ulysses_two_gpus_matches_one_gpu(cuda_device, case):
+@pytest.mark.parametrize("case", ["flux", "ltx", "cfg", "vae"])
+def test_two_gpus_match_one_gpu(cuda_device, case):
+    """flux/ltx: Ulysses over 2 ranks; cfg: conditional and unconditional branch on different
+    GPUs with the velocity exchange; vae: tiles split over 2 ranks, canvases all-reduced."""
     size, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
