@@ -374,6 +374,12 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
         "timing": "per-launch CUDA events over a second pass of the same K steps",
     }
 
+    secondary = None
+    if not args.no_secondary:
+        model = prepared = current = None
+        torch.cuda.empty_cache()
+        secondary = run_secondary(world, rank, local)
+
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
         threads = os.cpu_count() or 1
@@ -408,8 +414,145 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
             "gpu_launches": launches,
             "kernels": kernels,
             "clocks": clocks,
+            "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
+
+
+def ltx_step_flops(tokens=9216, ctx=256, dim=4096, heads=32, blocks=48, ff=4, cin=128):
+    """Algorithmic FLOPs of one LTX-2 video-stream transformer evaluation."""
+    d = dim
+    per = 2 * tokens * (4 * d * d + 2 * d * d + 2 * ff * d * d + 2 * heads * d) + 2 * ctx * 2 * d * d
+    per += 4 * tokens * tokens * d + 4 * tokens * ctx * d
+    return blocks * per + 2 * tokens * cin * d * 2
+
+
+def vae_decode_flops(decoder, latent_shape, tile=8, overlap=2):
+    """Conv FLOPs of the tiled decode (every tile, overlap included)."""
+    from kinomlx_b200.ltx2.video_vae import tile_plan
+
+    _, _, f, h, w = latent_shape
+    total = 0
+    for h0, h1, w0, w1, *_ in tile_plan(h, w, tile, overlap, decoder.spatial_scale):
+        ff, hh, ww, c = f, h1 - h0, w1 - w0, decoder.v.top_width
+        total += 2 * ff * hh * ww * c * 27 * decoder.v.latent_channels
+        for blk in decoder.v.blocks:
+            if blk[0] == "res":
+                total += blk[1] * 2 * (2 * ff * hh * ww * c * 27 * c)
+            else:
+                (st, sh, sw), mult = blk[1], blk[2]
+                n = st * sh * sw * (c // mult)
+                total += 2 * ff * hh * ww * n * 27 * c
+                ff, hh, ww, c = ff * st - (1 if st > 1 else 0), hh * sh, ww * sw, c // mult
+        total += 2 * ff * hh * ww * decoder.v.out_channels * decoder.v.patch ** 2 * 27 * c
+    return total
+
+
+def _time(fn, warmup: int, steps: int, world: int) -> float:
+    for _ in range(warmup):
+        fn()
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return max_over_ranks(a.elapsed_time(b) / steps, world)
+
+
+def run_secondary(world: int, rank: int, local: int) -> dict:
+    """BASELINE configs 3-5 on the same GPUs (2 warm-up + 3 timed repetitions each): the
+    metric's second half (VAE decode frames/s) and the other step latencies, each with its
+    whole-step throughput against the measured sustained bf16 peak."""
+    from kinomlx_b200.flux2 import config as fcfg
+    from kinomlx_b200.flux2 import sampling
+    from kinomlx_b200.flux2.transformer import Flux2Transformer
+    from kinomlx_b200.ltx2 import config as lcfg
+    from kinomlx_b200.ltx2 import video_vae as vae
+    from kinomlx_b200.ltx2.transformer import LTXVideoTransformer
+    from kinomlx_b200.multi_gpu import CfgSplit, cfg_split_step, decode_tiles_distributed
+    from kinomlx_b200.sequence_parallel import SequenceParallel
+    from kinomlx_b200.synthetic import flux_weights, ltx_weights, make_weights, normal
+
+    device = torch.device("cuda", local)
+    pk, _ = peaks()
+    peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    out = {}
+
+    # config 3: CFG over a batch of 2 (1 GPU) or the branch split (+ Ulysses inside each half)
+    v = fcfg.BASELINE
+    nt, side = 512, 64
+    ids = torch.zeros((1, nt + side * side, 2), dtype=torch.int64)
+    ids[0, nt:, 0] = torch.arange(side).repeat_interleave(side)
+    ids[0, nt:, 1] = torch.arange(side).repeat(side)
+    text = normal((1, nt, v.context_dim), seed=44, device=device)
+    negative = normal((1, nt, v.context_dim), seed=45, device=device)
+    sig = sampling.linear_sigmas(28)
+    weights = flux_weights(v, seed=42, device=device)
+    if world == 1:
+        model = Flux2Transformer(weights, v, device)
+        prepared = model.prepare(torch.cat([text, negative]), ids)
+        cur = normal((1, side * side, v.in_channels), seed=43, device=device)
+        step = lambda: sampling.denoise_step(model, prepared, cur, sig, 0, guidance=4.0, cfg=True)
+        mode = "batch 2 on one GPU"
+    elif world % 2 == 0:
+        cfg = CfgSplit()
+        model = Flux2Transformer(weights, v, device, sp=cfg.sp)
+        prepared = model.prepare(text if cfg.branch == 0 else negative, ids)
+        i0, i1 = cfg.sp.shard(side * side)
+        cur = normal((1, side * side, v.in_channels), seed=43, device=device)[:, i0:i1].contiguous()
+        step = lambda: cfg_split_step(model, prepared, cur, sig, 0, 4.0, cfg)
+        mode = f"branches split over 2 x {world // 2} GPUs (Ulysses inside each half)"
+    else:
+        step = None
+    del weights
+    if step is not None:
+        ms = _time(step, 2, 3, world)
+        out["config3_cfg"] = {"ms_per_step": round(ms, 3), "mode": mode,
+                              "step_tflops": round(2 * step_flops() / (ms * 1e9), 1),
+                              "frac_of_peak": round(2 * step_flops() / (ms * 1e9) / peak, 4)}
+    model = prepared = None
+    torch.cuda.empty_cache()
+
+    # config 4: LTX-2 video DiT step, 9216 video tokens + 256 text tokens, 48 blocks
+    lv = lcfg.BASELINE_VIDEO
+    sp = SequenceParallel() if world > 1 else None
+    lmodel = LTXVideoTransformer(ltx_weights(lv, seed=0, device=device), lv, device, sp=sp)
+    torch.cuda.empty_cache()
+    f, h, w = 16, 18, 32
+    fr, hr, wr = torch.meshgrid(torch.arange(f), torch.arange(h), torch.arange(w), indexing="ij")
+    starts = torch.stack([fr, hr, wr]).reshape(3, -1).float()
+    bounds = torch.stack([starts, starts + 1], -1)[None]
+    scale = torch.tensor([8.0, 32.0, 32.0]).reshape(1, 3, 1, 1)
+    pix = bounds * scale
+    pix[:, 0] = torch.clamp(pix[:, 0] + 1 - 8, min=0) / 24.0
+    context = normal((1, 256, lv.context_dim), seed=2, device=device)
+    lprep = lmodel.prepare(context, pix)
+    t0, t1 = lmodel.sp.shard(f * h * w)
+    lat = normal((1, f * h * w, lv.in_channels), seed=1, device=device)[:, t0:t1].contiguous()
+    ms = _time(lambda: lmodel.run(lprep, lat, 0.725, sigma_next=0.421875, out=lat), 2, 3, world)
+    out["config4_video_dit"] = {"ms_per_step": round(ms, 3),
+                                "mode": f"Ulysses x{world}" if world > 1 else "single GPU",
+                                "step_tflops": round(ltx_step_flops() / (ms * 1e9), 1),
+                                "frac_of_peak": round(ltx_step_flops() / (ms * 1e9) / peak, 4)}
+    lmodel = lprep = lat = None
+    torch.cuda.empty_cache()
+
+    # config 5: tiled causal GroupNorm(32) VAE decode, 128x16x18x32 -> 3x121x576x1024, 15 tiles
+    vv = vae.BASELINE_VAE
+    dec = vae.VideoDecoder(make_weights(vae.vae_weight_specs(vv), seed=0, device=device), vv, device)
+    latent = normal((1, 128, 16, 18, 32), seed=0, device=device)
+    fn = (lambda: dec.decode(latent)) if world == 1 else (lambda: decode_tiles_distributed(dec, latent))
+    ms = _time(fn, 1, 2, world)
+    flops = vae_decode_flops(dec, latent.shape)
+    out["config5_vae_decode"] = {"frames_per_s": round(121 / (ms / 1e3), 2), "ms_per_decode": round(ms, 2),
+                                 "mode": f"tiles over {world} GPUs" if world > 1 else "single GPU",
+                                 "tiled_tflop": round(flops / 1e12, 1),
+                                 "tflops": round(flops / (ms * 1e9), 1),
+                                 "frac_of_peak": round(flops / (ms * 1e9) / peak, 4)}
+    return out
 
 
 def run_kernel_case(case: str) -> None:
@@ -445,6 +588,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["kino", "reference"], default="kino")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
     ap.add_argument("--kernel-case", choices=["gemm", "attention"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     args = ap.parse_args()
