@@ -3,32 +3,37 @@
 // Restates the math of the reference's attention calls: softmax(q k^T * d^-1/2) v per head
 // (kinomlx/models/flux2/kv.py:48-54 joint attention through MLX SDPA,
 //  kinomlx/models/ltx2/kernels/dense_attention.py:107-151 token-major dense attention,
-//  kinomlx/models/ltx2/transformer/attention.py:144-161 unmasked SDPA).
+//  kinomlx/models/ltx2/transformer/attention.py:144-161 unmasked SDPA, 364-368 head gates).
 //
 // Layout: q, k and v are token-major, (batch, tokens, heads * 128) with any row stride, which is
-// what the projections write; the reference's dense kernel takes the same layout. Queries and
-// keys may each come in two segments (text tokens, then image tokens) that are concatenated
-// logically but never in memory: each 128-row tile belongs to one segment.
+// what the projections write. Queries and keys may each come in two segments (text tokens, then
+// image tokens) that are concatenated logically but never in memory: each 128-row tile belongs
+// to one segment.
 //
-// One CTA computes 128 queries of one head:
-//   warp 0      TMA: Q once, then K and V tiles of 128 keys through a 2-stage ring
-//   warp 1      tensor memory owner and MMA issuer: S = Q K^T into one of two S buffers,
-//               O += P V into the O buffer
-//   warps 2..5  softmax, one query row per thread: tcgen05.ld the S row, online max/sum in the
-//               exp2 domain, rescale O in tensor memory only when the running max grows by more
-//               than 2^8 (exact: the stale max cancels in the final division), write P as bf16
-//               into 128-byte-swizzled shared memory for the next MMA, finally O / l.
-// V is consumed in place as an MN-major operand (no transpose pass).
+// One CTA computes two 128-query tiles (A and B) of one head, in ping-pong so that one tile's
+// tensor-core work runs under the other tile's softmax:
+//   warp 0      TMA: Q_A and Q_B once, then K and V tiles of 128 keys through a 2-stage ring
+//   warp 1      tensor-memory owner and MMA issuer, in the order
+//                 S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
+//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B, one query row per thread:
+//               tcgen05.ld the S row, online max/sum in the exp2 domain, rescale O in tensor
+//               memory only when the running max grows by more than 2^8 (the stale max cancels
+//               in the final division), write P as bf16 pairs back over S in tensor memory.
+// Tensor memory (512 columns): S_A [0,128) with P_A in [0,64), S_B [128,256) with P_B in
+// [128,192), O_A [256,384), O_B [384,512). The PV product takes P straight from tensor memory
+// (the TMEM-A form of tcgen05.mma) and V in place from shared memory as an MN-major operand.
+// MMAs of one issuing thread run in order, so S(j+1) overwriting P(j) after PV(j) is safe, and
+// the commit that signals S(j+1) also covers PV(j), so O is settled whenever the softmax sees S.
 #pragma once
 #include "kino_common.cuh"
 
 namespace kino {
 
-constexpr int ATT_BM = 128;       // queries per CTA
-constexpr int ATT_BN = 128;       // keys per block
-constexpr int ATT_D = 128;        // head dim
+constexpr int ATT_BM = 128;  // queries per tile
+constexpr int ATT_BN = 128;  // keys per block
+constexpr int ATT_D = 128;   // head dim
 constexpr int ATT_STAGES = 2;
-constexpr int ATT_THREADS = 192;
+constexpr int ATT_THREADS = 320;
 
 struct AttnParams {
   int batch, heads;
@@ -43,14 +48,13 @@ struct AttnParams {
 };
 
 struct AttnSmem {
-  static constexpr int HALF = ATT_BM * 64 * 2;             // 16 KB: 128 rows x 128 bytes
-  static constexpr int Q_OFF = 0;                          // 2 halves (d 0..63, 64..127)
-  static constexpr int P_OFF = Q_OFF + 2 * HALF;           // 2 halves (keys 0..63, 64..127)
-  static constexpr int KV_OFF = P_OFF + 2 * HALF;          // per stage: K 2 halves, V 2 halves
+  static constexpr int HALF = ATT_BM * 64 * 2;      // 16 KB: 128 rows x 128 bytes
+  static constexpr int Q_OFF = 0;                   // tile t at Q_OFF + t * 2 * HALF
+  static constexpr int KV_OFF = 4 * HALF;           // per stage: K 2 halves, V 2 halves
   static constexpr int STAGE = 4 * HALF;
   static constexpr int BAR_OFF = KV_OFF + ATT_STAGES * STAGE;
-  // q_full, kv_full[S], kv_empty[S], s_full[2], p_full, o_done, drain
-  static constexpr int NBAR = 1 + 2 * ATT_STAGES + 2 + 3;
+  // q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_done, drain
+  static constexpr int NBAR = 1 + 2 * ATT_STAGES + 2 + 2 + 2;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
 };
 
@@ -64,6 +68,32 @@ __device__ __forceinline__ uint64_t sdesc_mn128(uint32_t saddr, uint32_t lbo) {
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(2u) << 61;
   return d;
+}
+
+// D (tensor memory) += A (tensor memory, 128 lanes x 16 bf16 packed in 8 columns) * B (smem).
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+struct QTile {
+  int seg, tile;
+  bool valid;
+};
+
+__device__ __forceinline__ QTile q_tile_of(const AttnParams& p, int global) {
+  QTile t;
+  const int total = p.q_tiles[0] + (p.nq_seg > 1 ? p.q_tiles[1] : 0);
+  t.valid = global < total;
+  t.seg = (global < p.q_tiles[0]) ? 0 : 1;
+  t.tile = global - (t.seg ? p.q_tiles[0] : 0);
+  return t;
 }
 
 __global__ void __launch_bounds__(ATT_THREADS, 1)
@@ -81,9 +111,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + ATT_STAGES;
-  uint64_t* s_full = kv_empty + ATT_STAGES;
-  uint64_t* p_full = s_full + 2;
-  uint64_t* o_done = p_full + 1;
+  uint64_t* s_full = kv_empty + ATT_STAGES;  // [tile]
+  uint64_t* p_full = s_full + 2;             // [tile]
+  uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -92,8 +122,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t lane = lane_id();
   const int head = blockIdx.y;
   const int batch = blockIdx.z;
-  const int qseg = (static_cast<int>(blockIdx.x) < p.q_tiles[0]) ? 0 : 1;
-  const int qtile = static_cast<int>(blockIdx.x) - (qseg ? p.q_tiles[0] : 0);
+  const QTile tiles[2] = {q_tile_of(p, 2 * blockIdx.x), q_tile_of(p, 2 * blockIdx.x + 1)};
+  const bool has_b = tiles[1].valid;
   const int nblk = p.kv_blocks[0] + (p.nkv_seg > 1 ? p.kv_blocks[1] : 0);
 
   if (threadIdx.x == 0) {
@@ -102,9 +132,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(&s_full[0], 1);
-    mbar_init(&s_full[1], 1);
-    mbar_init(p_full, 128);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 128);
+    }
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -118,16 +149,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // tensor memory columns: S0 [0,128), S1 [128,256), O [256,384)
-  const uint32_t O_COL = 256;
 
   if (warp == 0) {
     if (lane == 0) {
-      const CUtensorMap* mq = qseg ? &mq1 : &mq0;
-      uint8_t* sq = smem + L::Q_OFF;
-      mbar_expect_tx(q_full, 2 * L::HALF);
-      tma_load_4d(sq, mq, q_full, 0, qtile * ATT_BM, head, batch);
-      tma_load_4d(sq + L::HALF, mq, q_full, 64, qtile * ATT_BM, head, batch);
+      mbar_expect_tx(q_full, (has_b ? 4 : 2) * L::HALF);
+      for (int t = 0; t < (has_b ? 2 : 1); ++t) {
+        const CUtensorMap* mq = tiles[t].seg ? &mq1 : &mq0;
+        uint8_t* sq = smem + L::Q_OFF + t * 2 * L::HALF;
+        tma_load_4d(sq, mq, q_full, 0, tiles[t].tile * ATT_BM, head, batch);
+        tma_load_4d(sq + L::HALF, mq, q_full, 64, tiles[t].tile * ATT_BM, head, batch);
+      }
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
         const int stage = j % ATT_STAGES;
@@ -165,169 +196,178 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16(ATT_BM, ATT_BN);
       constexpr uint32_t idesc_o = idesc_bf16(ATT_BM, ATT_D) | (1u << 16);  // B (V) MN-major
-      const uint32_t sq = smem_u32(smem + L::Q_OFF);
-      const uint32_t sp = smem_u32(smem + L::P_OFF);
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      auto issue_s = [&](int j) -> bool {
-        const int stage = j % ATT_STAGES;
-        if (!mbar_wait(&kv_full[stage], (j / ATT_STAGES) & 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t sk = smem_u32(smem + L::KV_OFF + stage * L::STAGE);
-        const uint32_t d_tmem = tmem + (j & 1) * ATT_BN;
+      const int ntile = has_b ? 2 : 1;
+      auto s_mma = [&](int t, int j) {
+        const uint32_t sq = smem_u32(smem + L::Q_OFF + t * 2 * L::HALF);
+        const uint32_t sk = smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE);
 #pragma unroll
         for (int kk = 0; kk < ATT_D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::HALF + (kk & 3) * 32;
-          umma_bf16(d_tmem, sdesc_k128(sq + off), sdesc_k128(sk + off), idesc_s,
+          umma_bf16(tmem + t * 128, sdesc_k128(sq + off), sdesc_k128(sk + off), idesc_s,
                     kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
-        return true;
+        umma_commit(&s_full[t]);
       };
-      if (ok && nblk > 0) ok = issue_s(0);
-      for (int j = 0; ok && j < nblk; ++j) {
-        if (j + 1 < nblk && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, j & 1, abort_flag)) break;
-        tc_fence_after();
-        const int stage = j % ATT_STAGES;
-        const uint32_t sv = smem_u32(smem + L::KV_OFF + stage * L::STAGE + 2 * L::HALF);
+      auto pv_mma = [&](int t, int j) {
+        const uint32_t sv =
+            smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE + 2 * L::HALF);
 #pragma unroll
         for (int kk = 0; kk < ATT_BN / 16; ++kk) {
-          const uint32_t poff = (kk >> 2) * L::HALF + (kk & 3) * 32;
-          umma_bf16(tmem + O_COL, sdesc_k128(sp + poff), sdesc_mn128(sv + kk * 2048, L::HALF),
-                    idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                       sdesc_mn128(sv + kk * 2048, L::HALF), idesc_o,
+                       (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&kv_empty[stage]);
-        umma_commit(o_done);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag) && nblk > 0;
+      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < ntile; ++t) s_mma(t, 0);
       }
+      for (int j = 0; ok && j < nblk; ++j) {
+        const bool more = j + 1 < nblk;
+        for (int t = 0; t < ntile && ok; ++t) {
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          pv_mma(t, j);
+          if (t == ntile - 1) umma_commit(&kv_empty[j % ATT_STAGES]);
+          if (more) {
+            if (t == 0) {
+              if (!mbar_wait(&kv_full[(j + 1) % ATT_STAGES], ((j + 1) / ATT_STAGES) & 1,
+                             abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            s_mma(t, j + 1);
+          }
+        }
+      }
+      umma_commit(o_done);
       umma_commit(drain);
       const uint64_t t0 = global_ns();
       while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 200000000ull) {
       }
     }
   } else {
-    // softmax warps 2..5: one query row per thread
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + static_cast<int>(lane);
-    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const float sl2 = p.scale_log2;
-    float m_run = -INFINITY;  // running max of s * scale * log2(e)
-    float l_run = 0.0f;
-    uint8_t* sp = smem + L::P_OFF;
-    bool ok = true;
-    for (int j = 0; j < nblk; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int kseg = (j < p.kv_blocks[0]) ? 0 : 1;
-      const int kb = j - (kseg ? p.kv_blocks[0] : 0);
-      const int valid = min(ATT_BN, p.kv_tokens[kseg] - kb * ATT_BN);
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + (j & 1) * ATT_BN + c * 32, sr[c]);
-      tmem_wait_ld();
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(sr[c][i]);
-          if (c * 32 + i >= valid) v = -INFINITY;
-          sr[c][i] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
-        }
-      }
-      const float m_blk = mx * sl2;
-      if (j > 0) {
-        if (!mbar_wait(o_done, (j - 1) & 1, abort_flag)) {
+    // softmax warps: 2..5 tile A, 6..9 tile B; one query row per thread
+    const int t = (warp - 2) >> 2;
+    const QTile qt = tiles[t];
+    if (qt.valid) {
+      const int quarter = warp & 3;
+      const int row = quarter * 32 + static_cast<int>(lane);
+      const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+      const uint32_t s_col = tmem + lane_base + t * 128;
+      const uint32_t o_col = tmem + lane_base + 256 + t * 128;
+      const float sl2 = p.scale_log2;
+      float m_run = -INFINITY;  // running max of s * scale * log2(e)
+      float l_run = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < nblk; ++j) {
+        if (!mbar_wait(&s_full[t], j & 1, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const bool need = m_blk > m_run + 8.0f;
-        if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? ex2_approx(m_run - m_blk) : 1.0f;
-          if (need) {
-            m_run = m_blk;
-            l_run *= alpha;
-          }
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tmem + lane_base + O_COL + c * 32, o);
-            tmem_wait_ld();
+        const int kseg = (j < p.kv_blocks[0]) ? 0 : 1;
+        const int kb = j - (kseg ? p.kv_blocks[0] : 0);
+        const int valid = min(ATT_BN, p.kv_tokens[kseg] - kb * ATT_BN);
+        uint32_t sr[4][32];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tmem + lane_base + O_COL + c * 32, o);
-          }
-          tmem_wait_st();
-        }
-      } else {
-        m_run = m_blk;
-      }
-      // P = exp2(s * scale * log2 e - m_run), rounded to bf16 for the MMA; l sums the same
-      // rounded values.
-      float lsum = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float s0 = __uint_as_float(sr[c][2 * i]);
-          const float s1 = __uint_as_float(sr[c][2 * i + 1]);
-          const float p0 = ex2_approx(fmaf(s0, sl2, -m_run));
-          const float p1 = ex2_approx(fmaf(s1, sl2, -m_run));
-          packed[i] = pack_bf16x2(p0, p1);
-          const float2 r = unpack_bf16x2(packed[i]);
-          lsum += r.x + r.y;
-        }
-        // keys c*32 .. c*32+31 live in half (c >> 1), 16-byte chunks (c & 1) * 4 .. + 3
-        uint8_t* rowp = sp + (c >> 1) * L::HALF + row * 128;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int chunk = ((c & 1) * 4 + q) ^ (row & 7);
-          *reinterpret_cast<uint4*>(rowp + chunk * 16) =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-        }
-      }
-      l_run += lsum;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    if (ok && nblk > 0 && mbar_wait(o_done, (nblk - 1) & 1, abort_flag)) {
-      tc_fence_after();
-      const int t = qtile * ATT_BM + row;
-      const bool store = t < p.q_tokens[qseg];
-      const float inv_l = 1.0f / l_run;
-      // Optional head gate: bf16(bf16(O / l) * gate[t, head])
-      // (kinomlx/models/ltx2/transformer/attention.py:364-368).
-      const __nv_bfloat16* gp = p.gate[qseg];
-      const float gv = (gp != nullptr && store)
-                           ? __bfloat162float(gp[static_cast<int64_t>(batch) * p.bs_gate[qseg] +
-                                                 static_cast<int64_t>(t) * p.ld_gate[qseg] + head])
-                           : 1.0f;
-      auto fin = [&](uint32_t raw) -> float {
-        const float o = __uint_as_float(raw) * inv_l;
-        return gp != nullptr ? bf16_round(bf16_round(o) * gv) : o;
-      };
-      __nv_bfloat16* dst = p.out[qseg] + static_cast<int64_t>(batch) * p.bs_out[qseg] +
-                           static_cast<int64_t>(t) * p.ld_out[qseg] + head * ATT_D;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_base + O_COL + c * 32, o);
+        for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, sr[c]);
         tmem_wait_ld();
-        if (store) {
+        float mx = -INFINITY;
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 w;
-            w.x = pack_bf16x2(fin(o[g * 8 + 0]), fin(o[g * 8 + 1]));
-            w.y = pack_bf16x2(fin(o[g * 8 + 2]), fin(o[g * 8 + 3]));
-            w.z = pack_bf16x2(fin(o[g * 8 + 4]), fin(o[g * 8 + 5]));
-            w.w = pack_bf16x2(fin(o[g * 8 + 6]), fin(o[g * 8 + 7]));
-            *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = w;
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float v = __uint_as_float(sr[c][i]);
+            if (c * 32 + i >= valid) v = -INFINITY;
+            sr[c][i] = __float_as_uint(v);
+            mx = fmaxf(mx, v);
+          }
+        }
+        const float m_blk = mx * sl2;
+        if (j > 0) {
+          const bool need = m_blk > m_run + 8.0f;
+          if (__any_sync(0xffffffffu, need)) {
+            const float alpha = need ? ex2_approx(m_run - m_blk) : 1.0f;
+            if (need) {
+              m_run = m_blk;
+              l_run *= alpha;
+            }
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t o[32];
+              tmem_ld32(o_col + c * 32, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st32(o_col + c * 32, o);
+            }
+          }
+        } else {
+          m_run = m_blk;
+        }
+        // P = exp2(s * scale * log2 e - m_run) as bf16 pairs over S's first 64 columns; l sums
+        // the same rounded values the MMA sees.
+        float lsum = 0.0f;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t packed[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float s0 = __uint_as_float(sr[2 * h2 + (i >> 4)][(2 * i) & 31]);
+            const float s1 = __uint_as_float(sr[2 * h2 + (i >> 4)][(2 * i + 1) & 31]);
+            packed[i] = pack_bf16x2(ex2_approx(fmaf(s0, sl2, -m_run)),
+                                    ex2_approx(fmaf(s1, sl2, -m_run)));
+            const float2 r = unpack_bf16x2(packed[i]);
+            lsum += r.x + r.y;
+          }
+          tmem_st32(s_col + h2 * 32, packed);
+        }
+        l_run += lsum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[t]);
+      }
+      if (ok && nblk > 0 && mbar_wait(o_done, 0, abort_flag)) {
+        tc_fence_after();
+        const int tok = qt.tile * ATT_BM + row;
+        const bool store = tok < p.q_tokens[qt.seg];
+        const float inv_l = 1.0f / l_run;
+        // Optional head gate: bf16(bf16(O / l) * gate[t, head])
+        const __nv_bfloat16* gp = p.gate[qt.seg];
+        const float gv =
+            (gp != nullptr && store)
+                ? __bfloat162float(gp[static_cast<int64_t>(batch) * p.bs_gate[qt.seg] +
+                                      static_cast<int64_t>(tok) * p.ld_gate[qt.seg] + head])
+                : 1.0f;
+        auto fin = [&](uint32_t raw) -> float {
+          const float o = __uint_as_float(raw) * inv_l;
+          return gp != nullptr ? bf16_round(bf16_round(o) * gv) : o;
+        };
+        __nv_bfloat16* dst = p.out[qt.seg] + static_cast<int64_t>(batch) * p.bs_out[qt.seg] +
+                             static_cast<int64_t>(tok) * p.ld_out[qt.seg] + head * ATT_D;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_col + c * 32, o);
+          tmem_wait_ld();
+          if (store) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 w;
+              w.x = pack_bf16x2(fin(o[g * 8 + 0]), fin(o[g * 8 + 1]));
+              w.y = pack_bf16x2(fin(o[g * 8 + 2]), fin(o[g * 8 + 3]));
+              w.z = pack_bf16x2(fin(o[g * 8 + 4]), fin(o[g * 8 + 5]));
+              w.w = pack_bf16x2(fin(o[g * 8 + 6]), fin(o[g * 8 + 7]));
+              *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = w;
+            }
           }
         }
       }

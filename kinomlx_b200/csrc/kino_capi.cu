@@ -375,7 +375,7 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
   }
   kino_status st = ensure_smem(kino::attention_tc_kernel, kino::AttnSmem::TOTAL, 3);
   if (st != KINO_OK) return st;
-  dim3 grid(tiles, p.heads, p.batch);
+  dim3 grid((tiles + 1) / 2, p.heads, p.batch);  // two 128-query tiles per CTA
   kino::attention_tc_kernel<<<grid, kino::ATT_THREADS, kino::AttnSmem::TOTAL,
                               static_cast<cudaStream_t>(stream)>>>(mq[0], mq[1], mk[0], mk[1],
                                                                    mv[0], mv[1], p);
