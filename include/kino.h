@@ -52,6 +52,10 @@ int kino_num_sms(void);
 #define KINO_EPI_SIGMOID2 4       /* out = 2 * sigmoid(bf16(acc + bias)) */
 #define KINO_EPI_EULER_X0 5       /* v = bf16(acc + bias); x0 = bf16(aux - scalar * v);
                                      out = x0 + scalar2 * (aux - x0), fp32 (LTX X0 + Euler) */
+#define KINO_EPI_SWIGLU 6         /* columns >= act_col_begin: weight rows in blocks of 16 gate +
+                                     16 content; out col act_col_begin + (col - act_col_begin)/2
+                                     = bf16(bf16(silu(gate)) * content); earlier columns plain.
+                                     Output width act_col_begin + (n - act_col_begin) / 2 */
 
 typedef struct kino_epilogue {
   int kind;                /* KINO_EPI_* */

@@ -32,6 +32,7 @@ EPI_GATED_RESIDUAL = 2
 EPI_EULER = 3
 EPI_SIGMOID2 = 4
 EPI_EULER_X0 = 5
+EPI_SWIGLU = 6
 
 NORM_RMS = 0
 NORM_LAYER = 1

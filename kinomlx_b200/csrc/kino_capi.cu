@@ -243,7 +243,12 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
     return fail(KINO_ENOTSUPPORTED,
                 "kino_linear: k, n and strides must be multiples of 8 (k=%lld n=%lld)",
                 (long long)k, (long long)n);
-  if (ldx < k || ldw < k || ldo < n) return fail(KINO_EINVAL, "kino_linear: stride below width");
+  const bool swiglu = epi != nullptr && epi->kind == kino::EPI_SWIGLU;
+  const int64_t n_out = swiglu ? epi->act_col_begin + (n - epi->act_col_begin) / 2 : n;
+  if (ldx < k || ldw < k || ldo < n_out)
+    return fail(KINO_EINVAL, "kino_linear: stride below width");
+  if (swiglu && (epi->act_col_begin % 32 || (n - epi->act_col_begin) % 32 || epi->act_col_begin < 0))
+    return fail(KINO_ENOTSUPPORTED, "kino_linear: SwiGLU columns must come in blocks of 32");
   if (m > (1 << 30) || n > (1 << 30) || k > (1 << 30) || batch > 65535)
     return fail(KINO_ENOTSUPPORTED, "kino_linear: shape too large");
   if (!aligned16(out)) return fail(KINO_EINVAL, "kino_linear: out not 16-byte aligned");
@@ -265,7 +270,7 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
     e.ld_aux = epi->ld_aux;
     e.bs_aux = epi->bs_aux;
     e.scalar2 = epi->scalar2;
-    if (e.kind < 0 || e.kind > 5) return fail(KINO_EINVAL, "kino_linear: unknown epilogue");
+    if (e.kind < 0 || e.kind > 6) return fail(KINO_EINVAL, "kino_linear: unknown epilogue");
     if (e.bias != nullptr && !aligned16(e.bias))
       return fail(KINO_EINVAL, "kino_linear: bias not 16-byte aligned");
     if (e.kind == kino::EPI_GATED_RESIDUAL &&

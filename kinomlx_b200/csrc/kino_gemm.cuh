@@ -27,6 +27,7 @@ enum EpiKind : int {
   EPI_EULER = 3,
   EPI_SIGMOID2 = 4,
   EPI_EULER_X0 = 5,
+  EPI_SWIGLU = 6,
 };
 
 struct GemmEpi {
@@ -101,6 +102,25 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
   for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
 
   const int64_t out_off = static_cast<int64_t>(b) * s.bs_out + static_cast<int64_t>(row) * s.ldo;
+  if (e.kind == EPI_SWIGLU && col0 >= e.act_col_begin) {
+    // Weight rows were interleaved on the host in blocks of 16 gate + 16 content rows, so this
+    // chunk holds gate[0..16) then content[0..16) of 16 output columns:
+    // bf16(bf16(silu(gate)) * content) (kinomlx/models/flux2/transformer.py:63-65).
+    float o[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j] = bf16_round(silu_f32(v[j])) * v[16 + j];
+    __nv_bfloat16* dst = out + out_off + e.act_col_begin + (col0 - e.act_col_begin) / 2;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      uint4 w;
+      w.x = pack_bf16x2(o[g * 8 + 0], o[g * 8 + 1]);
+      w.y = pack_bf16x2(o[g * 8 + 2], o[g * 8 + 3]);
+      w.z = pack_bf16x2(o[g * 8 + 4], o[g * 8 + 5]);
+      w.w = pack_bf16x2(o[g * 8 + 6], o[g * 8 + 7]);
+      *reinterpret_cast<uint4*>(dst + g * 8) = w;
+    }
+    return;
+  }
   if (e.kind == EPI_GELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j)

@@ -6,8 +6,8 @@ Memory layout (one workspace per batch/token shape, allocated once):
                            of it, so the single blocks' concatenation costs nothing
   nrm    (B, N, D)         AdaLN output, the A operand of the next projection
   qkv    (B, N, 3D)        fused [q | k | v] of both streams; attention writes its output over q
-  hid    (B, N, mlp_in)    MLP activations of the double blocks
-  big    (B, N, 3D+mlp_in) single-block fused projection laid out [k | v | q | mlp] so that the
+  hid    (B, N, H)         MLP activations of the double blocks (H = activated MLP width)
+  big    (B, N, 3D+H)      single-block fused projection laid out [k | v | q | act(mlp)] so the
                            attention output (written over q) and the activated MLP are one
                            contiguous (D + mlp_hidden)-wide operand of to_out
 Projections run on the tcgen05 GEMM with their epilogue fused (GELU, gated residual, Euler);
@@ -56,8 +56,8 @@ class _Workspace:
         self.stream = e(batch, n, d)
         self.nrm = e(batch, n, d)
         self.qkv = e(batch, n, 3 * d)
-        self.hid = e(batch, n, v.mlp_in)
-        self.big = e(batch, n, 3 * d + v.mlp_in)
+        self.hid = e(batch, n, v.mlp_hidden)
+        self.big = e(batch, n, 3 * d + v.mlp_hidden)
         self.t = torch.empty((batch,), device=device, dtype=torch.float32)
         self.temb = e(batch, 256)
         self.emb1 = e(batch, d)
@@ -74,12 +74,14 @@ class Flux2Transformer:
         """`sp` shards the tokens over a process group (Ulysses); each rank then holds
         Nt/P text and Ni/P image tokens and passes its own latent shard to `run`."""
         self.sp = sp if sp is not None else SequenceParallel.single()
-        if variant.mlp != "gelu_tanh":
-            raise ValueError(
-                "this build runs the GELU-tanh MLP variant; SwiGLU (Klein) is not implemented"
-            )
+        if variant.mlp not in ("gelu_tanh", "swiglu"):
+            raise ValueError(f"unknown MLP kind {variant.mlp!r}")
         self.v = variant
         self.device = torch.device(device)
+        swiglu = variant.mlp == "swiglu"
+        # SwiGLU up projections: gate/content rows interleaved for the fused epilogue
+        self.act_kind = ops.EPI_SWIGLU if swiglu else ops.EPI_GELU
+        mlp_rows = ops.swiglu_interleave if swiglu else (lambda t: t)
         dev = lambda t: t.to(self.device, torch.bfloat16).contiguous()
         w = weights
         d = variant.dim
@@ -108,9 +110,9 @@ class Flux2Transformer:
                 "norm_k": dev(g("norm_k")),
                 "norm_added_q": dev(g("norm_added_q")),
                 "norm_added_k": dev(g("norm_added_k")),
-                "ff_in": dev(w[f"{a}.ff.linear_in.weight"]),
+                "ff_in": dev(mlp_rows(w[f"{a}.ff.linear_in.weight"])),
                 "ff_out": dev(w[f"{a}.ff.linear_out.weight"]),
-                "ffc_in": dev(w[f"{a}.ff_context.linear_in.weight"]),
+                "ffc_in": dev(mlp_rows(w[f"{a}.ff_context.linear_in.weight"])),
                 "ffc_out": dev(w[f"{a}.ff_context.linear_out.weight"]),
             })
         self.single = []
@@ -119,7 +121,7 @@ class Flux2Transformer:
             fused = w[f"{a}.to_qkv_mlp_proj.weight"]
             q, k, vv, mlp = fused[:d], fused[d : 2 * d], fused[2 * d : 3 * d], fused[3 * d :]
             self.single.append({
-                "fused": dev(torch.cat([k, vv, q, mlp])),  # [k | v | q | mlp]
+                "fused": dev(torch.cat([k, vv, q, mlp_rows(mlp)])),  # [k | v | q | mlp]
                 "to_out": dev(w[f"{a}.to_out.weight"]),
                 "norm_q": dev(w[f"{a}.norm_q.weight"]),
                 "norm_k": dev(w[f"{a}.norm_k.weight"]),
@@ -170,11 +172,11 @@ class Flux2Transformer:
         ops.linear(q[:, :nt], p["to_add_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
                    gate=m(6, 2))
         ops.adaln(img, m(0, 3), m(0, 4), img_n, norm=ops.NORM_LAYER)
-        ops.linear(img_n, p["ff_in"], ws.hid[:, nt:], kind=ops.EPI_GELU)
+        ops.linear(img_n, p["ff_in"], ws.hid[:, nt:], kind=self.act_kind)
         ops.linear(ws.hid[:, nt:], p["ff_out"], img, kind=ops.EPI_GATED_RESIDUAL, residual=img,
                    gate=m(0, 5))
         ops.adaln(txt, m(6, 3), m(6, 4), txt_n, norm=ops.NORM_LAYER)
-        ops.linear(txt_n, p["ffc_in"], ws.hid[:, :nt], kind=ops.EPI_GELU)
+        ops.linear(txt_n, p["ffc_in"], ws.hid[:, :nt], kind=self.act_kind)
         ops.linear(ws.hid[:, :nt], p["ffc_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
                    gate=m(6, 5))
 
@@ -182,7 +184,7 @@ class Flux2Transformer:
         d, h = self.v.dim, self.v.heads
         sm = lambda j: ws.mods[:, (12 + j) * d : (13 + j) * d]
         ops.adaln(ws.stream, sm(0), sm(1), ws.nrm, norm=ops.NORM_LAYER)
-        ops.linear(ws.nrm, p["fused"], ws.big, kind=ops.EPI_GELU, act_col_begin=3 * d)
+        ops.linear(ws.nrm, p["fused"], ws.big, kind=self.act_kind, act_col_begin=3 * d)
         k, v, q = ws.big[..., :d], ws.big[..., d : 2 * d], ws.big[..., 2 * d : 3 * d]
         ops.qk_norm_rope(q, heads=h, weight=p["norm_q"], norm=ops.QKNORM_PER_HEAD,
                          rope=ops.ROPE_PAIRS, cos=cos, sin=sin)

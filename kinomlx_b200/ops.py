@@ -18,6 +18,7 @@ from ._lib import (
     EPI_NONE,
     EPI_EULER_X0,
     EPI_SIGMOID2,
+    EPI_SWIGLU,
     NORM_LAYER,
     NORM_NONE,
     NORM_RMS,
@@ -36,6 +37,7 @@ __all__ = [
     "EPI_NONE",
     "EPI_EULER_X0",
     "EPI_SIGMOID2",
+    "EPI_SWIGLU",
     "NORM_LAYER",
     "NORM_NONE",
     "NORM_RMS",
@@ -161,6 +163,9 @@ def linear(
 ) -> torch.Tensor:
     """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight.
 
+    EPI_SWIGLU: columns from `act_col_begin` on come in blocks of 16 gate + 16 content rows
+    (see `swiglu_interleave`) and produce half as many output columns.
+
     EPI_EULER uses `dt` and `sample`; EPI_EULER_X0 uses `sigma`, `ratio` (fp32 sigma_next /
     sigma) and `sample`."""
     _need(x, "x")
@@ -170,12 +175,13 @@ def linear(
     n = w.shape[0]
     if w.shape[1] != k:
         raise ValueError(f"weight {tuple(w.shape)} does not match input width {k}")
+    n_out = act_col_begin + (n - act_col_begin) // 2 if kind == EPI_SWIGLU else n
     if out is None:
-        out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=torch.bfloat16)
+        out = torch.empty((*x.shape[:-1], n_out), device=x.device, dtype=torch.bfloat16)
     _need(out, "out")
     o3 = _as3d(out)
-    if tuple(o3.shape) != (batch, m, n):
-        raise ValueError(f"out {tuple(out.shape)} does not match ({batch}, {m}, {n})")
+    if tuple(o3.shape) != (batch, m, n_out):
+        raise ValueError(f"out {tuple(out.shape)} does not match ({batch}, {m}, {n_out})")
     epi = _lib.Epilogue()
     epi.kind = kind
     if bias is not None:
@@ -193,7 +199,7 @@ def linear(
         g = gate.reshape(-1, gate.shape[-1]) if gate.dim() != 2 else gate
         epi.gate = g.data_ptr()
         epi.bs_gate = g.stride(0) if g.shape[0] > 1 else 0
-    if kind == EPI_GELU:
+    if kind in (EPI_GELU, EPI_SWIGLU):
         epi.act_col_begin = act_col_begin
     if kind in (EPI_EULER, EPI_EULER_X0):
         if sample is None:
@@ -224,6 +230,17 @@ def linear(
             _stream(),
         )
     return out
+
+
+def swiglu_interleave(w: torch.Tensor) -> torch.Tensor:
+    """Rows [gate (H); content (H)] of a SwiGLU up projection -> blocks of 16 gate rows followed
+    by the 16 matching content rows, the order the EPI_SWIGLU epilogue reads."""
+    h = w.shape[0] // 2
+    if h % 16:
+        raise ValueError("SwiGLU width must be a multiple of 16")
+    gate = w[:h].reshape(h // 16, 16, *w.shape[1:])
+    content = w[h:].reshape(h // 16, 16, *w.shape[1:])
+    return torch.cat([gate, content], dim=1).reshape(w.shape)
 
 
 def gemv(

@@ -124,3 +124,28 @@ def test_full_size_step_is_finite(cuda_device):
     assert bool(torch.isfinite(a).all())
     assert torch.equal(a, b)
     assert float((a.float() - noise.float()).abs().max()) > 0
+
+
+def test_klein_swiglu_variant_matches_oracle(cuda_device):
+    """The reference's own Klein graph shape (SwiGLU MLP with gate first, 4 interleaved-pair RoPE
+    axes of 32 dims, theta 2000, 128-channel latents), narrowed to hidden 1024 / 8 heads so the
+    oracle stays quick: a 2-step trajectory, final-latent cosine >= 0.999."""
+    v = fcfg.FluxVariant(dim=1024, heads=8, mlp="swiglu", mlp_hidden=3072,
+                         rope_axes=(32, 32, 32, 32), rope_theta=2000.0, in_channels=128,
+                         context_dim=512, double_blocks=1, single_blocks=1)
+    w = flux_weights(v, seed=21)
+    h, wd, nt = 8, 12, 40
+    noise = normal((1, h * wd, v.in_channels), seed=22)
+    text = normal((1, nt, v.context_dim), seed=23)
+    img = torch.zeros((1, h * wd, 4), dtype=torch.int64)
+    img[0, :, 1] = torch.arange(h).repeat_interleave(wd)
+    img[0, :, 2] = torch.arange(wd).repeat(h)
+    txt = torch.zeros((1, nt, 4), dtype=torch.int64)
+    txt[0, :, 3] = torch.arange(nt)
+    ids = torch.cat([txt, img], 1)
+    sigmas = ref.schedule(h * wd, 2)
+    expect = ref.denoise(w, noise, text, ids, sigmas, v)
+    model = Flux2Transformer(w, v, cuda_device)
+    out = sampling.denoise(model, noise, text, ids, sigmas=sampling.schedule(h * wd, 2))
+    rel_l2, max_rel, cosine = _metrics(out, expect)
+    assert cosine >= 0.999 and rel_l2 <= 3e-2, (rel_l2, max_rel, cosine)
