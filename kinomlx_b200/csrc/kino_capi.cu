@@ -2,6 +2,7 @@
 // extern "C" entry points declared in include/kino.h. One translation unit holds every kernel so
 // the device error word is a single symbol without relocatable device code.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -179,6 +180,63 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   return check_launch("kino_conv3d");
 }
 
+template <int STAGES>
+kino_status launch_gemm_2sm(const void* x, const void* w, void* out, const kino::GemmShape& s0,
+                            int64_t ldx, int64_t bsx, int64_t ldw, const kino::GemmEpi& e,
+                            cudaStream_t stream, int slot) {
+  using L = kino::Gemm2SmSmem<STAGES>;
+  CUtensorMap ma, mb;
+  const uint64_t da[3] = {static_cast<uint64_t>(s0.k), static_cast<uint64_t>(s0.m),
+                          static_cast<uint64_t>(s0.batch)};
+  const uint64_t sa[2] = {static_cast<uint64_t>(ldx),
+                          static_cast<uint64_t>(s0.batch > 1 ? bsx : ldx * s0.m)};
+  const uint32_t ba[3] = {64, 128, 1};
+  kino_status st = make_map(&ma, x, 3, da, sa, ba);
+  if (st != KINO_OK) return st;
+  const uint64_t db[2] = {static_cast<uint64_t>(s0.k), static_cast<uint64_t>(s0.n)};
+  const uint64_t sb[1] = {static_cast<uint64_t>(ldw)};
+  const uint32_t bb[2] = {64, 128};
+  st = make_map(&mb, w, 2, db, sb, bb);
+  if (st != KINO_OK) return st;
+  kino::GemmShape s = s0;
+  s.tiles_m = (s.m + 255) / 256;
+  s.tiles_n = (s.n + 255) / 256;
+  s.num_tiles = s.tiles_m * s.tiles_n * s.batch;
+  s.kblocks = (s.k + kino::GEMM_BK - 1) / kino::GEMM_BK;
+  auto kernel = kino::gemm_bf16_2sm_kernel<STAGES>;
+  st = ensure_smem(kernel, L::TOTAL, slot);
+  if (st != KINO_OK) return st;
+  const int max_pairs = device_sms() / 2;
+  const int pairs = s.num_tiles < max_pairs ? s.num_tiles : max_pairs;
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kino::GEMM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = L::TOTAL;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, ma, mb,
+                                             reinterpret_cast<__nv_bfloat16*>(out), s, e);
+  if (err != cudaSuccess) return fail(KINO_ECUDA, "kino_linear (2-SM): %s", cudaGetErrorString(err));
+  return check_launch("kino_linear (2-SM)");
+}
+
+// CTA-pair GEMM tiles unless KINO_GEMM_PAIRS=0 in the environment (kept for A/B measurements).
+bool gemm_pairs_enabled() {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* v = getenv("KINO_GEMM_PAIRS");
+    enabled = (v != nullptr && v[0] == '0') ? 0 : 1;
+  }
+  return enabled == 1;
+}
+
 int gn_parts(int64_t voxels) {
   int64_t p = (voxels + 31) / 32;
   return static_cast<int>(p < 592 ? (p < 1 ? 1 : p) : 592);
@@ -291,6 +349,10 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
   s.bs_out = batch > 1 ? bso : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (n <= 128) return launch_gemm<128, 6>(x, w, out, s, ldx, bsx, ldw, e, st, 0);
+  // CTA pairs pay off once the 1-SM tiles would fill more than one wave of the GPU
+  // (measured: 512 x 9216 x 3072 runs faster on single CTAs, 4096 rows and up on pairs).
+  if (m >= 1024 && gemm_pairs_enabled())
+    return launch_gemm_2sm<6>(x, w, out, s, ldx, bsx, ldw, e, st, 6);
   return launch_gemm<256, 4>(x, w, out, s, ldx, bsx, ldw, e, st, 1);
 }
 

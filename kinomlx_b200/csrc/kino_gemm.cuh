@@ -366,3 +366,183 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 }
 
 }  // namespace kino
+
+namespace kino {
+
+// ----------------------------------------------------------------------------- 2-SM variant
+// The same product on CTA pairs (cluster of 2): one 256 x 256 output tile per pair per step,
+// issued by the even CTA as tcgen05.mma.cta_group::2 (M = 256). Each CTA loads its 128 rows of A
+// and its 128 rows of the weight (N half) into its own shared memory, 32 KB per stage instead of
+// the 48 KB a 1-SM 128 x 256 tile needs, so six stages fit and each SM's operand traffic per
+// tensor cycle drops by a third. TMA loads complete on the even CTA's barriers (no multicast
+// loads); MMA completion is committed to both CTAs' barriers; each CTA's epilogue drains its own
+// tensor memory (its 128 rows of the tile) and tells the even CTA when the accumulator is free.
+template <int STAGES>
+struct Gemm2SmSmem {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;   // 16 KB: this CTA's 128 rows of A
+  static constexpr int B_BYTES = 128 * GEMM_BK * 2;       // 16 KB: this CTA's 128 weight rows
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int TOTAL = TILE_BYTES + BAR_BYTES + 1024;
+};
+
+template <int STAGES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_bf16_2sm_kernel(const __grid_constant__ CUtensorMap map_a,
+                         const __grid_constant__ CUtensorMap map_b,
+                         __nv_bfloat16* __restrict__ out, const GemmShape s, const GemmEpi e) {
+  using L = Gemm2SmSmem<STAGES>;
+  constexpr int BN = 256;  // pair tile width; this CTA loads BN / 2 weight rows
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_rank();  // 0: leader (issues the MMAs), 1: peer
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&map_a);
+    tma_prefetch(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive or complete_tx
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = pair; t < s.num_tiles; t += pairs) {
+        int b, mt, nt;
+        gemm_tile_coords(s, t, b, mt, nt);
+        for (int kb = 0; kb < s.kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+          uint8_t* sa = smem + stage * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          const uint32_t leader_full = smem_u32(&full[stage]) & kPairLeaderMask;
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
+          tma_load_3d_pair(sa, &map_a, leader_full, kb * GEMM_BK, mt * 256 + rank * 128, b);
+          tma_load_2d_pair(sb, &map_b, leader_full, kb * GEMM_BK, nt * BN + rank * 128);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      // In a normal run every load was consumed by the leader's MMAs before the final cluster
+      // barrier. After a timeout, give loads still in flight a bounded moment to land.
+      if (*abort_flag && issued > 0) {
+        const uint64_t t0 = global_ns();
+        while (global_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16(256, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = pair; t < s.num_tiles; t += pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < s.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            umma_bf16_pair(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32), idesc,
+                           (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+      }
+      umma_commit_pair(drain, 0x1);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 200000000ull) {
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + static_cast<int>(lane);
+    const uint32_t leader_tempty0 = cluster_addr(smem_u32(&tempty[0]), 0);
+    int local = 0;
+    for (int t = pair; t < s.num_tiles; t += pairs, ++local) {
+      int b, mt, nt;
+      gemm_tile_coords(s, t, b, mt, nt);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int row = mt * 256 + row_in_tile;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((quarter * 32) << 16) + acc * BN + c * 32, r);
+        tmem_wait_ld();
+        gemm_epilogue_store(s, e, out, b, row, nt * BN + c * 32, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs have drained; neither CTA's memory is in use any more
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
+  }
+}
+
+}  // namespace kino
