@@ -30,7 +30,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (2); bumped on any signature change. */
+/* ABI version of this header (3); bumped on any signature change. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -71,6 +71,23 @@ typedef struct kino_epilogue {
   int64_t ld_aux;
   int64_t bs_aux;
   float scalar2;           /* EULER_X0: fp32(sigma_next / sigma); `scalar` holds sigma */
+  /* Optional fused QK norm + RoPE, independent of `kind`: for r in {0, 1} with
+   * norm_weight[r] != NULL, the columns [norm_col[r], norm_col[r] + norm_width) (128-aligned,
+   * 128-wide heads) are RMS-normalised per head with the 128-entry weight (fp32 statistics,
+   * eps norm_eps, rounded to bf16) and rotated by adjacent pairs with the fp32 tables rope_cos /
+   * rope_sin. The tables are head-dim-major, (128, T) with T = (rope_batched ? batch : 1) *
+   * rope_rows: output row i of batch b reads column (rope_batched ? b : 0) * rope_rows +
+   * rope_offset + i of each of the 128 table rows (kinomlx/models/flux2/transformer.py:25-29,
+   * 68-75). */
+  const void* norm_weight[2];
+  int64_t norm_col[2];
+  int64_t norm_width;
+  const float* rope_cos;
+  const float* rope_sin;
+  int64_t rope_rows;
+  int64_t rope_offset;
+  int rope_batched;
+  float norm_eps;
 } kino_epilogue;
 
 /* out[b, i, j] = epilogue(sum_k x[b, i, k] * w[j, k]) on tcgen05 tensor cores.

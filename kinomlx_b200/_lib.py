@@ -61,6 +61,15 @@ class Epilogue(ctypes.Structure):
         ("ld_aux", c_int64),
         ("bs_aux", c_int64),
         ("scalar2", c_float),
+        ("norm_weight", c_void_p * 2),
+        ("norm_col", c_int64 * 2),
+        ("norm_width", c_int64),
+        ("rope_cos", c_void_p),
+        ("rope_sin", c_void_p),
+        ("rope_rows", c_int64),
+        ("rope_offset", c_int64),
+        ("rope_batched", c_int),
+        ("norm_eps", c_float),
     ]
 
 

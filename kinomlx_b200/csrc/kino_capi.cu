@@ -271,7 +271,7 @@ void* group_norm_scratch_address(kino_status* status) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 2; }
+int kino_abi_version(void) { return 3; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -338,6 +338,33 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
     if ((e.kind == kino::EPI_EULER || e.kind == kino::EPI_EULER_X0) &&
         (e.aux == nullptr || !aligned16(e.aux) || e.ld_aux % 8 || e.bs_aux % 8))
       return fail(KINO_EINVAL, "kino_linear: Euler epilogue needs an aligned sample");
+    for (int r = 0; r < 2; ++r) {
+      e.norm_w[r] = static_cast<const __nv_bfloat16*>(epi->norm_weight[r]);
+      e.norm_col[r] = epi->norm_col[r];
+    }
+    e.norm_width = epi->norm_width;
+    e.rope_cos = epi->rope_cos;
+    e.rope_sin = epi->rope_sin;
+    e.rope_rows = epi->rope_rows;
+    e.rope_offset = epi->rope_offset;
+    e.rope_batched = epi->rope_batched;
+    e.norm_eps = epi->norm_eps;
+    if (e.norm_w[0] != nullptr || e.norm_w[1] != nullptr) {
+      if (e.rope_cos == nullptr || e.rope_sin == nullptr || !aligned16(e.rope_cos) ||
+          !aligned16(e.rope_sin) || e.norm_width <= 0 || e.norm_width % 128)
+        return fail(KINO_EINVAL, "kino_linear: QK norm needs 128-wide heads and aligned tables");
+      for (int r = 0; r < 2; ++r)
+        if (e.norm_w[r] != nullptr &&
+            (!aligned16(e.norm_w[r]) || e.norm_col[r] % 128 || e.norm_col[r] < 0 ||
+             e.norm_col[r] + e.norm_width > n))
+          return fail(KINO_EINVAL, "kino_linear: QK norm range outside the product");
+      if (e.rope_offset < 0 || e.rope_offset + m > e.rope_rows)
+        return fail(KINO_EINVAL, "kino_linear: RoPE table shorter than the rows");
+      if (e.kind == kino::EPI_SWIGLU &&
+          ((e.norm_w[0] && e.norm_col[0] + e.norm_width > e.act_col_begin) ||
+           (e.norm_w[1] && e.norm_col[1] + e.norm_width > e.act_col_begin)))
+        return fail(KINO_EINVAL, "kino_linear: QK norm ranges must precede the SwiGLU columns");
+    }
   }
   kino::GemmShape s;
   std::memset(&s, 0, sizeof(s));

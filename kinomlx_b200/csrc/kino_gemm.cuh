@@ -42,6 +42,17 @@ struct GemmEpi {
   const __nv_bfloat16* aux;       // Euler current sample
   int64_t ld_aux, bs_aux;
   float scalar2;                  // EULER_X0: fp32(sigma_next / sigma)
+  // Per-head RMSNorm + adjacent-pair RoPE on up to two head-aligned column ranges (q and k of a
+  // fused projection): range r covers [norm_col[r], norm_col[r] + norm_width) and uses the
+  // 128-entry weight norm_w[r]; rows read RoPE table row rope_offset + row.
+  const __nv_bfloat16* norm_w[2];
+  int64_t norm_col[2];
+  int64_t norm_width;
+  const float* rope_cos;
+  const float* rope_sin;
+  int64_t rope_rows, rope_offset;
+  int rope_batched;
+  float norm_eps;
 };
 
 struct GemmShape {
@@ -207,6 +218,115 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
   }
 }
 
+// Which norm range (0/1) holds the 128-column group starting at col, or -1.
+__device__ __forceinline__ int gemm_norm_range(const GemmEpi& e, int col) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+    if (e.norm_w[r] != nullptr && col >= e.norm_col[r] && col < e.norm_col[r] + e.norm_width)
+      return r;
+  return -1;
+}
+
+// One 128-wide head of one row: bias, rounding to bf16 (the projection's output), RMSNorm over
+// the head with fp32 statistics and fp32 scale, rounding to bf16 (kinomlx/kernels/fused_ops.py
+// rms_norm; kinomlx/models/flux2/transformer.py:68-75), then x * cos + perp(x) * sin on adjacent
+// pairs with fp32 tables, one rounding (kinomlx/models/flux2/transformer.py:25-29).
+__device__ __forceinline__ void gemm_head_chunk(const GemmEpi& e, int col, uint32_t taddr,
+                                                float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32(taddr, r);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (e.bias != nullptr) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(e.bias + col + g * 8);
+      const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 t = unpack_bf16x2(w4[q]);
+        v[g * 8 + 2 * q] += t.x;
+        v[g * 8 + 2 * q + 1] += t.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
+}
+
+// Two passes over the head's accumulator columns in tensor memory (statistics, then the
+// normalised, rotated store) keep 32 values live instead of 128.
+__device__ __forceinline__ void gemm_epilogue_head(const GemmShape& s, const GemmEpi& e,
+                                                   __nv_bfloat16* out, int b, int row, int col0,
+                                                   int range, uint32_t taddr) {
+  float ss = 0.0f;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    gemm_head_chunk(e, col0 + c * 32, taddr + c * 32, v);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+  }
+  // tcgen05.ld is warp-collective: every lane loads, only rows inside the product store
+  const bool live = row < s.m && col0 < s.n;
+  const float inv = rsqrtf(ss / 128.0f + e.norm_eps);
+  const __nv_bfloat16* w = e.norm_w[range];
+  // Tables are head-dim-major, (128, table columns): the 32 threads of a warp hold 32
+  // consecutive rows, so each head-dim entry below is one contiguous 128-byte read.
+  const int64_t trow = (e.rope_batched ? static_cast<int64_t>(b) * e.rope_rows : 0) +
+                       e.rope_offset + row;
+  const int64_t tstride = e.rope_rows * (e.rope_batched ? s.batch : 1);
+  __nv_bfloat16* dst = out + static_cast<int64_t>(b) * s.bs_out + static_cast<int64_t>(row) * s.ldo +
+                       col0;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    gemm_head_chunk(e, col0 + c * 32, taddr + c * 32, v);
+    if (!live) continue;
+    const float* cs = e.rope_cos + trow + static_cast<int64_t>(c * 32) * tstride;
+    const float* sn = e.rope_sin + trow + static_cast<int64_t>(c * 32) * tstride;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(w + c * 32 + g * 8);
+      const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+      uint32_t o4[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = g * 8 + 2 * q;
+        const float2 t = unpack_bf16x2(w4[q]);
+        const float x0 = bf16_round(v[j] * inv * t.x);
+        const float x1 = bf16_round(v[j + 1] * inv * t.y);
+        const float c0 = __ldg(cs + j * tstride), c1 = __ldg(cs + (j + 1) * tstride);
+        const float s0 = __ldg(sn + j * tstride), s1 = __ldg(sn + (j + 1) * tstride);
+        o4[q] = pack_bf16x2(__fadd_rn(__fmul_rn(x0, c0), __fmul_rn(-x1, s0)),
+                            __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1)));
+      }
+      *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+    }
+  }
+}
+
+__device__ __forceinline__ void gemm_epilogue_row(const GemmShape& s, const GemmEpi& e,
+                                                  __nv_bfloat16* out, int b, int row, int col_base,
+                                                  uint32_t taddr, int width) {
+#pragma unroll 1
+  for (int g = 0; g < width; g += 128) {
+    const int range = gemm_norm_range(e, col_base + g);
+    if (range >= 0) {
+      gemm_epilogue_head(s, e, out, b, row, col_base + g, range, taddr + g);
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < 4 && g + c * 32 < width; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + g + c * 32, r);
+        tmem_wait_ld();
+        gemm_epilogue_store(s, e, out, b, row, col_base + g + c * 32, r);
+      }
+    }
+  }
+}
+
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a,
@@ -344,13 +464,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int row = mt * GEMM_BM + row_in_tile;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((quarter * 32) << 16) + acc * BN + c * 32, r);
-        tmem_wait_ld();
-        gemm_epilogue_store(s, e, out, b, row, nt * BN + c * 32, r);
-      }
+      gemm_epilogue_row(s, e, out, b, row, nt * BN,
+                        tmem_base + ((quarter * 32) << 16) + acc * BN, BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -523,13 +638,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int row = mt * 256 + row_in_tile;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((quarter * 32) << 16) + acc * BN + c * 32, r);
-        tmem_wait_ld();
-        gemm_epilogue_store(s, e, out, b, row, nt * BN + c * 32, r);
-      }
+      gemm_epilogue_row(s, e, out, b, row, nt * BN,
+                        tmem_base + ((quarter * 32) << 16) + acc * BN, BN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);

@@ -44,8 +44,7 @@ class PreparedText:
     """Once-per-generation state (kinomlx/models/flux2/transformer.py:283-292)."""
 
     text: torch.Tensor  # projected text (B, Nt, D)
-    cos: torch.Tensor  # (1|B, N, 128) fp32
-    sin: torch.Tensor
+    rope: ops.RopeTables  # joint [text, image] tables, head-dim-major on the device
 
 
 class _Workspace:
@@ -142,7 +141,7 @@ class Flux2Transformer:
             rows = torch.cat([torch.arange(t0, t1), nt + torch.arange(i0, i1)])
             projected = projected[:, t0:t1].contiguous()
             cos, sin = cos[:, rows].contiguous(), sin[:, rows].contiguous()
-        return PreparedText(projected, cos.to(self.device), sin.to(self.device))
+        return PreparedText(projected, ops.RopeTables(cos.to(self.device), sin.to(self.device)))
 
     def workspace(self, batch: int, nt: int, ni: int) -> _Workspace:
         key = (batch, nt, ni)
@@ -151,21 +150,20 @@ class Flux2Transformer:
         return self._ws[key]
 
     # ------------------------------------------------------------------ blocks
-    def _double_block(self, ws: _Workspace, p: dict, cos, sin) -> None:
+    def _double_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
         d, nt, h = self.v.dim, ws.nt, self.v.heads
         txt, img = ws.stream[:, :nt], ws.stream[:, nt:]
         txt_n, img_n = ws.nrm[:, :nt], ws.nrm[:, nt:]
         m = lambda base, j: ws.mods[:, (base + j) * d : (base + j + 1) * d]  # img base 0, txt 6
         ops.adaln(img, m(0, 0), m(0, 1), img_n, norm=ops.NORM_LAYER)
         ops.adaln(txt, m(6, 0), m(6, 1), txt_n, norm=ops.NORM_LAYER)
-        ops.linear(img_n, p["img_qkv"], ws.qkv[:, nt:])
-        ops.linear(txt_n, p["txt_qkv"], ws.qkv[:, :nt])
+        # q/k RMSNorm + RoPE run in the projection's epilogue (image rows read table rows from nt)
+        ops.linear(img_n, p["img_qkv"], ws.qkv[:, nt:], qk_norm=[(0, p["norm_q"]), (d, p["norm_k"])],
+                   norm_width=d, rope=(rope, nt))
+        ops.linear(txt_n, p["txt_qkv"], ws.qkv[:, :nt],
+                   qk_norm=[(0, p["norm_added_q"]), (d, p["norm_added_k"])], norm_width=d,
+                   rope=(rope, 0))
         q, k, v = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
-        for part, wt, wi in ((q, "norm_added_q", "norm_q"), (k, "norm_added_k", "norm_k")):
-            ops.qk_norm_rope(part[:, :nt], heads=h, weight=p[wt], norm=ops.QKNORM_PER_HEAD,
-                             rope=ops.ROPE_PAIRS, cos=cos, sin=sin, table_offset=0)
-            ops.qk_norm_rope(part[:, nt:], heads=h, weight=p[wi], norm=ops.QKNORM_PER_HEAD,
-                             rope=ops.ROPE_PAIRS, cos=cos, sin=sin, table_offset=nt)
         self.sp.attention(q, k, v, q, heads=h)
         ops.linear(q[:, nt:], p["to_out"], img, kind=ops.EPI_GATED_RESIDUAL, residual=img,
                    gate=m(0, 2))
@@ -180,16 +178,15 @@ class Flux2Transformer:
         ops.linear(ws.hid[:, :nt], p["ffc_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
                    gate=m(6, 5))
 
-    def _single_block(self, ws: _Workspace, p: dict, cos, sin) -> None:
+    def _single_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
         d, h = self.v.dim, self.v.heads
         sm = lambda j: ws.mods[:, (12 + j) * d : (13 + j) * d]
         ops.adaln(ws.stream, sm(0), sm(1), ws.nrm, norm=ops.NORM_LAYER)
-        ops.linear(ws.nrm, p["fused"], ws.big, kind=self.act_kind, act_col_begin=3 * d)
+        # [k | v | q | mlp]: k and q normalised and rotated, the MLP activated, in one epilogue
+        ops.linear(ws.nrm, p["fused"], ws.big, kind=self.act_kind, act_col_begin=3 * d,
+                   qk_norm=[(0, p["norm_k"]), (2 * d, p["norm_q"])], norm_width=d,
+                   rope=(rope, 0))
         k, v, q = ws.big[..., :d], ws.big[..., d : 2 * d], ws.big[..., 2 * d : 3 * d]
-        ops.qk_norm_rope(q, heads=h, weight=p["norm_q"], norm=ops.QKNORM_PER_HEAD,
-                         rope=ops.ROPE_PAIRS, cos=cos, sin=sin)
-        ops.qk_norm_rope(k, heads=h, weight=p["norm_k"], norm=ops.QKNORM_PER_HEAD,
-                         rope=ops.ROPE_PAIRS, cos=cos, sin=sin)
         self.sp.attention(q, k, v, q, heads=h)
         ops.linear(ws.big[..., 2 * d :], p["to_out"], ws.stream, kind=ops.EPI_GATED_RESIDUAL,
                    residual=ws.stream, gate=sm(2))
@@ -204,7 +201,7 @@ class Flux2Transformer:
         self._embed(ws, timestep_x1000)
         ws.stream[:, :nt].copy_(text)
         ws.stream[:, nt:].copy_(image)
-        self._double_block(ws, self.double[index], cos, sin)
+        self._double_block(ws, self.double[index], ops.RopeTables(cos, sin))
         return ws.stream[:, nt:].clone(), ws.stream[:, :nt].clone()
 
     def single_block(self, index: int, value: torch.Tensor, text_tokens: int,
@@ -214,7 +211,7 @@ class Flux2Transformer:
         ws = self.workspace(batch, text_tokens, n - text_tokens)
         self._embed(ws, timestep_x1000)
         ws.stream.copy_(value)
-        self._single_block(ws, self.single[index], cos, sin)
+        self._single_block(ws, self.single[index], ops.RopeTables(cos, sin))
         return ws.stream.clone()
 
     # ------------------------------------------------------------------ forward
@@ -239,9 +236,9 @@ class Flux2Transformer:
         ws.stream[:, :nt].copy_(prepared.text)
         ops.linear(image, self.x_embedder, ws.stream[:, nt:])
         for p in self.double:
-            self._double_block(ws, p, prepared.cos, prepared.sin)
+            self._double_block(ws, p, prepared.rope)
         for p in self.single:
-            self._single_block(ws, p, prepared.cos, prepared.sin)
+            self._single_block(ws, p, prepared.rope)
         d = self.v.dim
         om = lambda j: ws.mods[:, (15 + j) * d : (16 + j) * d]  # [scale | shift]
         ops.adaln(ws.stream[:, nt:], om(1), om(0), ws.nrm[:, nt:], norm=ops.NORM_LAYER)

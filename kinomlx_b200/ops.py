@@ -62,6 +62,7 @@ __all__ = [
     "latent_to_bfhwc",
     "linear",
     "pixel_norm",
+    "RopeTables",
     "qk_norm_rope",
     "rms_norm",
     "silu",
@@ -146,6 +147,23 @@ def device_status() -> None:
     _lib.call("kino_device_status", _stream())
 
 
+class RopeTables:
+    """Pair-RoPE tables for the fused QK-norm epilogue of `linear`, stored head-dim-major.
+
+    Built once per generation from (1|B, N, 128) fp32 cos/sin tables: the device copy is
+    (128, T) with T = (B if batched else 1) * N, so batch b row i sits in column b * N + i and
+    the 32 rows a warp's epilogue holds read one contiguous span per head-dim column."""
+
+    def __init__(self, cos: torch.Tensor, sin: torch.Tensor):
+        if cos.shape != sin.shape or cos.shape[-1] != 128:
+            raise ValueError("RoPE tables are (..., tokens, 128) cos/sin pairs")
+        c3, s3 = cos.reshape(-1, cos.shape[-2], 128), sin.reshape(-1, sin.shape[-2], 128)
+        self.rows = c3.shape[1]
+        self.batched = c3.shape[0] > 1
+        self.cos_t = c3.to(torch.float32).permute(2, 0, 1).reshape(128, -1).contiguous()
+        self.sin_t = s3.to(torch.float32).permute(2, 0, 1).reshape(128, -1).contiguous()
+
+
 def linear(
     x: torch.Tensor,
     w: torch.Tensor,
@@ -160,6 +178,10 @@ def linear(
     sample: torch.Tensor | None = None,
     sigma: float = 0.0,
     ratio: float = 0.0,
+    qk_norm: list[tuple[int, torch.Tensor]] | None = None,
+    norm_width: int = 0,
+    rope: tuple[RopeTables, int] | None = None,
+    eps: float = 1e-6,
 ) -> torch.Tensor:
     """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight.
 
@@ -211,6 +233,25 @@ def linear(
         epi.bs_aux = s3.stride(0)
         epi.scalar = dt if kind == EPI_EULER else sigma
         epi.scalar2 = ratio
+    if qk_norm:
+        # fused per-head RMSNorm + adjacent-pair RoPE on (column, weight) ranges of norm_width
+        if rope is None or len(qk_norm) > 2:
+            raise ValueError("qk_norm takes up to two (column, weight) ranges and rope tables")
+        tables, offset = rope
+        if tables.batched and tables.cos_t.shape[1] != batch * tables.rows:
+            raise ValueError("batched RoPE tables must hold one table per batch entry")
+        _need(tables.cos_t, "cos", torch.float32)
+        _need(tables.sin_t, "sin", torch.float32)
+        for r, (col, weight) in enumerate(qk_norm):
+            _need(weight, "norm weight")
+            epi.norm_weight[r] = weight.data_ptr()
+            epi.norm_col[r] = col
+        epi.norm_width = norm_width
+        epi.rope_cos, epi.rope_sin = tables.cos_t.data_ptr(), tables.sin_t.data_ptr()
+        epi.rope_rows = tables.rows
+        epi.rope_offset = offset
+        epi.rope_batched = int(tables.batched)
+        epi.norm_eps = eps
     with _timed("gemm", 2.0 * batch * m * n * k, 2.0 * (batch * m * k + n * k + batch * m * n)):
         _lib.call(
             "kino_linear",

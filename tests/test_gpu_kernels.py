@@ -336,3 +336,39 @@ def test_gemv_and_timestep_embedding(cuda_device):
     ref = ((xs.float() @ w.float().T).to(BF).float() + b.float()).to(BF)
     out = ops.gemv(x.to(cuda_device), w.to(cuda_device), b.to(cuda_device), silu_input=True)
     assert _max_rel(out, ref) <= 2e-2
+
+
+def test_linear_fused_qk_norm_rope_and_gelu(cuda_device):
+    """[k | v | q | mlp] projection with per-head RMSNorm + pair RoPE on k and q and GELU on the
+    MLP columns in one epilogue, against the separate fp32 formulas."""
+    from kinomlx_b200 import ops
+
+    dev = cuda_device
+    m, k, heads = 300, 256, 2
+    d = heads * 128
+    n = 3 * d + 512
+    x = _randn((1, m, k), 101)
+    w = _randn((n, k), 102, 0.05)
+    nq = _randn((128,), 103) + 1
+    nk = _randn((128,), 104) + 1
+    ang = torch.randn((m + 40, 64), generator=_gen(105)).repeat_interleave(2, dim=-1)
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    proj = (x.float() @ w.float().T).to(BF).float()[0]
+
+    def norm_rope(part, weight, off):
+        h = part.reshape(m, heads, 128)
+        y = (h * torch.rsqrt((h * h).mean(-1, keepdim=True) + 1e-6) * weight.float()).to(BF).float()
+        c, s = cos[off : off + m, None], sin[off : off + m, None]
+        pairs = y.reshape(m, heads, 64, 2)
+        perp = torch.stack([-pairs[..., 1], pairs[..., 0]], -1).reshape(y.shape)
+        return (y * c + perp * s).reshape(m, d)
+
+    t = proj[:, 3 * d :]
+    gelu = 0.5 * t * (1 + torch.tanh((0.7978845608028654 * (t + 0.044715 * t**3)).clamp(-10, 10)))
+    expect = torch.cat([norm_rope(proj[:, :d], nk, 40), proj[:, d : 2 * d],
+                        norm_rope(proj[:, 2 * d : 3 * d], nq, 40), gelu], dim=1).to(BF)
+    out = ops.linear(x.to(dev), w.to(dev), kind=ops.EPI_GELU, act_col_begin=3 * d,
+                     qk_norm=[(0, nk.to(dev)), (2 * d, nq.to(dev))], norm_width=d,
+                     rope=(ops.RopeTables(cos.to(dev), sin.to(dev)), 40))
+    assert _max_rel(out[0], expect) <= 2e-2
+    assert (out[0].cpu() == expect).float().mean() > 0.95
