@@ -556,9 +556,11 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
 
 
 def run_kernel_case(case: str) -> None:
-    """One launch of one kernel at the workload's largest shape (for ncu captures): `gemm` is the
-    single block's fused projection (4608 x 21504 x 3072, GELU epilogue), `attention` the joint
-    attention over 4608 tokens x 24 heads. Inputs exceed the L2 (weights 132 MB)."""
+    """Three launches of one kernel at a workload shape (for ncu captures). `gemm`: the single
+    block's fused projection, 4608 x 21504 x 3072, with its in-step epilogue (per-head RMSNorm +
+    RoPE on k and q, GELU on the MLP columns); `attention`: the joint attention over 4608 tokens
+    x 24 heads; `conv3d`: a 256-channel causal 3x3x3 VAE conv over 25 x 96 x 128 voxels. Inputs
+    exceed the L2 (weights 132 MB; conv activations 157 MB)."""
     from kinomlx_b200 import ops
     from kinomlx_b200.synthetic import normal
 
@@ -567,15 +569,27 @@ def run_kernel_case(case: str) -> None:
     if case == "gemm":
         x = normal((1, n, d), seed=1, device=dev)
         w = normal((3 * d + 4 * d, d), seed=2, device=dev, std=0.02)
+        nk = normal((128,), seed=4, device=dev)
+        nq = normal((128,), seed=5, device=dev)
+        ang = torch.randn((1, n, 64), generator=torch.Generator().manual_seed(6))
+        rope = ops.RopeTables(torch.cos(ang).repeat_interleave(2, -1).to(dev),
+                              torch.sin(ang).repeat_interleave(2, -1).to(dev))
         out = torch.empty((1, n, 7 * d), device=dev, dtype=torch.bfloat16)
         for _ in range(3):
-            ops.linear(x, w, out, kind=ops.EPI_GELU, act_col_begin=3 * d)
-    else:
+            ops.linear(x, w, out, kind=ops.EPI_GELU, act_col_begin=3 * d,
+                       qk_norm=[(0, nk), (2 * d, nq)], norm_width=d, rope=(rope, 0))
+    elif case == "attention":
         qkv = normal((1, n, 3 * d), seed=3, device=dev)
         q, k, v = qkv[..., :d], qkv[..., d : 2 * d], qkv[..., 2 * d :]
         out = torch.empty((1, n, d), device=dev, dtype=torch.bfloat16)
         for _ in range(3):
             ops.attention([q], [k], [v], [out], heads=24)
+    else:
+        x = normal((25, 96, 128, 256), seed=7, device=dev)
+        w = normal((256, 3, 3, 3, 256), seed=8, device=dev, std=0.02)
+        bias = normal((256,), seed=9, device=dev)
+        for _ in range(3):
+            ops.conv3d(x, w, bias, causal=True)
     torch.cuda.synchronize()
     ops.device_status()
     print(json.dumps({"kernel_case": case, "ok": True}))
@@ -590,7 +604,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
-    ap.add_argument("--kernel-case", choices=["gemm", "attention"],
+    ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     args = ap.parse_args()
     if args.kernel_case:

@@ -34,6 +34,12 @@ constexpr int ATT_BN = 128;  // keys per block
 constexpr int ATT_D = 128;   // head dim
 constexpr int ATT_STAGES = 2;
 constexpr int ATT_THREADS = 320;
+// Pairs i of each 64-column half whose bit (i % 8) is set take the FMA-pipe exponential
+// (exp2_poly_x2) instead of the special-function unit: bits 1, 4, 6 = 24 of 64 pairs per row.
+#ifndef KINO_ATT_EMU_MASK
+#define KINO_ATT_EMU_MASK 0x52
+#endif
+constexpr unsigned ATT_EMU_MASK = KINO_ATT_EMU_MASK;
 
 struct AttnParams {
   int batch, heads;
@@ -280,57 +286,92 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, sr[c]);
         tmem_wait_ld();
-        float mx = -INFINITY;
+        const bool ragged = valid < ATT_BN;  // only a segment's last key block; warp-uniform
+        if (ragged) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i >= valid) sr[c][i] = __float_as_uint(-INFINITY);
+          }
+        }
+        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float v = __uint_as_float(sr[c][i]);
-            if (c * 32 + i >= valid) v = -INFINITY;
-            sr[c][i] = __float_as_uint(v);
-            mx = fmaxf(mx, v);
+          for (int i = 0; i < 32; i += 8) {
+            mq[(i >> 3) & 3] = max3f(mq[(i >> 3) & 3], __uint_as_float(sr[c][i]),
+                                     __uint_as_float(sr[c][i + 1]));
+            mq[(i >> 3) & 3] = max3f(mq[(i >> 3) & 3], __uint_as_float(sr[c][i + 2]),
+                                     __uint_as_float(sr[c][i + 3]));
+            mq[(i >> 3) & 3] = max3f(mq[(i >> 3) & 3], __uint_as_float(sr[c][i + 4]),
+                                     __uint_as_float(sr[c][i + 5]));
+            mq[(i >> 3) & 3] = max3f(mq[(i >> 3) & 3], __uint_as_float(sr[c][i + 6]),
+                                     __uint_as_float(sr[c][i + 7]));
           }
         }
+        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
         const float m_blk = mx * sl2;
+        // Lazy rescale: the running max moves only when a block's max exceeds it by > 2^8; O is
+        // rescaled below, once S is consumed (PV of the previous block has completed: it was
+        // issued before this block's S).
+        float alpha = 1.0f;
+        bool rescale = false;
         if (j > 0) {
           const bool need = m_blk > m_run + 8.0f;
-          if (__any_sync(0xffffffffu, need)) {
-            const float alpha = need ? ex2_approx(m_run - m_blk) : 1.0f;
-            if (need) {
-              m_run = m_blk;
-              l_run *= alpha;
-            }
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              uint32_t o[32];
-              tmem_ld32(o_col + c * 32, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-              tmem_st32(o_col + c * 32, o);
-            }
+          rescale = __any_sync(0xffffffffu, need);
+          if (need) {
+            alpha = ex2_approx(m_run - m_blk);
+            m_run = m_blk;
+            l_run *= alpha;
           }
         } else {
           m_run = m_blk;
         }
-        // P = exp2(s * scale * log2 e - m_run) as bf16 pairs over S's first 64 columns; l sums
-        // the same rounded values the MMA sees.
-        float lsum = 0.0f;
+        // P = exp2(s * scale * log2 e - m_run) as bf16 pairs over S's first 64 columns, l the
+        // fp32 sum. Part of the pairs take the FMA-pipe exponential; it gives 2^-126 rather than
+        // 0 for a masked key, whose V row is TMA zero fill, so only l sees it (by 2^-126 each).
+        const uint64_t sl2x2 = f2_pack(sl2, sl2);
+        const uint64_t negm = f2_pack(-m_run, -m_run);
+        uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+        {
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          uint32_t packed[32];
+          for (int q8 = 0; q8 < 8; ++q8) {
+            uint32_t packed[8];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float s0 = __uint_as_float(sr[2 * h2 + (i >> 4)][(2 * i) & 31]);
-            const float s1 = __uint_as_float(sr[2 * h2 + (i >> 4)][(2 * i + 1) & 31]);
-            packed[i] = pack_bf16x2(ex2_approx(fmaf(s0, sl2, -m_run)),
-                                    ex2_approx(fmaf(s1, sl2, -m_run)));
-            const float2 r = unpack_bf16x2(packed[i]);
-            lsum += r.x + r.y;
+            for (int u = 0; u < 8; ++u) {
+              const int i = q8 * 8 + u;  // pair index over the row's 128 columns
+              const uint32_t* src = sr[i >> 4];
+              const int e = (2 * i) & 31;
+              const uint64_t xs = f2_fma(f2_pack(__uint_as_float(src[e]), __uint_as_float(src[e + 1])),
+                                         sl2x2, negm);
+              uint64_t ev;
+              if ((ATT_EMU_MASK >> (i & 7)) & 1) {
+                ev = exp2_poly_x2(xs);
+              } else {
+                const float2 xv = f2_unpack(xs);
+                ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
+              }
+              lsum2[i & 1] = f2_add(lsum2[i & 1], ev);
+              const float2 e2 = f2_unpack(ev);
+              packed[u] = pack_bf16x2(e2.x, e2.y);
+            }
+            tmem_st8(s_col + q8 * 8, packed);
           }
-          tmem_st32(s_col + h2 * 32, packed);
         }
-        l_run += lsum;
+        const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
+        l_run += ls.x + ls.y;
+        if (rescale) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_col + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(o_col + c * 32, o);
+          }
+        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&p_full[t]);

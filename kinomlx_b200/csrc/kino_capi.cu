@@ -175,7 +175,7 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   kino::ConvEpi e;
   e.bias = static_cast<const __nv_bfloat16*>(a->bias);
   e.residual = static_cast<const __nv_bfloat16*>(a->residual);
-  kernel<<<grid, kino::GEMM_THREADS, L::TOTAL, stream>>>(
+  kernel<<<grid, kino::CONV_THREADS, L::TOTAL, stream>>>(
       mx, mw, static_cast<__nv_bfloat16*>(a->out), s, e);
   return check_launch("kino_conv3d");
 }
@@ -226,6 +226,11 @@ kino_status launch_gemm_2sm(const void* x, const void* w, void* out, const kino:
   if (err != cudaSuccess) return fail(KINO_ECUDA, "kino_linear (2-SM): %s", cudaGetErrorString(err));
   return check_launch("kino_linear (2-SM)");
 }
+
+// Pipeline depth of the CTA-pair GEMM (32 KiB per stage per CTA; 7 is the most that fits).
+#ifndef KINO_GEMM_PAIR_STAGES
+#define KINO_GEMM_PAIR_STAGES 7
+#endif
 
 // CTA-pair GEMM tiles unless KINO_GEMM_PAIRS=0 in the environment (kept for A/B measurements).
 bool gemm_pairs_enabled() {
@@ -379,7 +384,7 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
   // CTA pairs pay off once the 1-SM tiles would fill more than one wave of the GPU
   // (measured: 512 x 9216 x 3072 runs faster on single CTAs, 4096 rows and up on pairs).
   if (m >= 1024 && gemm_pairs_enabled())
-    return launch_gemm_2sm<6>(x, w, out, s, ldx, bsx, ldw, e, st, 6);
+    return launch_gemm_2sm<KINO_GEMM_PAIR_STAGES>(x, w, out, s, ldx, bsx, ldw, e, st, 6);
   return launch_gemm<256, 4>(x, w, out, s, ldx, bsx, ldw, e, st, 1);
 }
 

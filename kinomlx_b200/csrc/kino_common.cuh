@@ -201,6 +201,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+               "r"(r[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -238,6 +245,68 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes of math)
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair on the FMA pipes instead of the special-function unit, used for part of the
+// softmax so that exponentials and tensor-core work take similar time. Method: Cody-Waite style
+// range reduction x = j + f, j = round-to-nearest(x) taken from the low mantissa bits of
+// x + 1.5 * 2^23, f in [-1/2, 1/2]; 2^f by a degree-3 polynomial whose coefficients minimise the
+// maximum relative error on [-1/2, 1/2] (Lawson's iteratively reweighted least squares;
+// 7.5e-5 relative, against bf16's 2^-9 half ulp); 2^j added into the exponent field. x is
+// clamped to >= -126 (results below 2^-126 read as 2^-126, far below a bf16 ulp of the row
+// maximum's 1); x <= 127.
+__device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  float2 xv = f2_unpack(x);
+  xv.x = fmaxf(xv.x, -126.0f);
+  xv.y = fmaxf(xv.y, -126.0f);
+  const uint64_t xc = f2_pack(xv.x, xv.y);
+  const uint64_t t = f2_add(xc, f2_pack(kShift, kShift));
+  const uint64_t f = f2_sub(xc, f2_sub(t, f2_pack(kShift, kShift)));
+  uint64_t p = f2_fma(f2_pack(0.0551713427f, 0.0551713427f), f, f2_pack(0.2426103414f, 0.2426103414f));
+  p = f2_fma(p, f, f2_pack(0.6932609672f, 0.6932609672f));
+  p = f2_fma(p, f, f2_pack(0.9999281213f, 0.9999281213f));
+  const float2 tv = f2_unpack(t), pv = f2_unpack(p);
+  // bits(t) = bits(1.5 * 2^23) + j, and bits(1.5 * 2^23) << 23 vanishes mod 2^32
+  return f2_pack(__int_as_float(__float_as_int(pv.x) + (__float_as_int(tv.x) << 23)),
+                 __int_as_float(__float_as_int(pv.y) + (__float_as_int(tv.y) << 23)));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -250,13 +319,29 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
 
 // tanh-approximate GELU with fp32 opmath; the inner argument is clamped to +-10 where tanh has
 // saturated in every low-precision type.
-__device__ __forceinline__ float gelu_tanh_f32(float x) {
-  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  const float t = tanhf(fminf(fmaxf(inner, -10.0f), 10.0f));
-  return 0.5f * x * (1.0f + t);
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
+// GELU, tanh form: 0.5 x (1 + tanh u), u = sqrt(2/pi) (x + 0.044715 x^3). Evaluated through the
+// identity 0.5 (1 + tanh u) = 1 / (1 + e^(-2u)) with the special-function unit's exp2 and
+// reciprocal: no cancellation in the negative tail, +-inf limits exact (x / inf = -0, x / 1 = x).
+__device__ __forceinline__ float gelu_tanh_f32(float x) {
+  // -2 sqrt(2/pi) log2(e)
+  const float t = -2.302208198144325f * x * fmaf(0.044715f * x, x, 1.0f);
+  return x * rcp_approx(1.0f + ex2_approx(t));
+}
+
+// SiLU x / (1 + e^-x) with the library exp and an IEEE divide: bf16 results equal the fp32
+// formula's (the standalone op and the VAE norms, which are bandwidth-bound anyway).
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + expf(-x)); }
+
+// SiLU for GEMM epilogues: x * rcp(1 + 2^(-x log2 e)) on the special-function unit.
+__device__ __forceinline__ float silu_fast_f32(float x) {
+  return x * rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * x));
+}
 
 }  // namespace kino
 

@@ -41,7 +41,7 @@ struct ConvEpi {
 };
 
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(CONV_THREADS, 1)
     conv3d_tc_kernel(const __grid_constant__ CUtensorMap map_x,
                      const __grid_constant__ CUtensorMap map_w, __nv_bfloat16* __restrict__ out,
                      const ConvShape s, const ConvEpi e) {

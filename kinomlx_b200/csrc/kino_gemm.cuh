@@ -63,7 +63,13 @@ struct GemmShape {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 192;
+// Warp 0 TMA, warp 1 MMA, warps 2..9 epilogue: two warps per tensor-memory lane quarter, each
+// draining half of the tile's columns, so the fused epilogues (QK norm + RoPE, GELU) finish
+// within the next tile's MMAs.
+constexpr int GEMM_EPI_WARPS = 8;
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
+// The implicit-GEMM conv keeps one epilogue warp per quarter.
+constexpr int CONV_THREADS = 192;
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -119,7 +125,7 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
     // bf16(bf16(silu(gate)) * content) (kinomlx/models/flux2/transformer.py:63-65).
     float o[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) o[j] = bf16_round(silu_f32(v[j])) * v[16 + j];
+    for (int j = 0; j < 16; ++j) o[j] = bf16_round(silu_fast_f32(v[j])) * v[16 + j];
     __nv_bfloat16* dst = out + out_off + e.act_col_begin + (col0 - e.act_col_begin) / 2;
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
@@ -354,7 +360,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], GEMM_EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -452,8 +458,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else {
-    // Epilogue warps 2..5. Tensor-memory lane quarter is fixed by warp id % 4.
+    // Epilogue warps 2..9. Tensor-memory lane quarter is fixed by warp id % 4; the two warps
+    // of a quarter take the two column halves of a 256-wide tile (whole 128-column heads).
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int SPLIT = BN >= 256 ? 2 : 1;
+    constexpr int WIDTH = BN / SPLIT;
     const int row_in_tile = quarter * 32 + static_cast<int>(lane);
     int local = 0;
     for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
@@ -464,8 +474,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int row = mt * GEMM_BM + row_in_tile;
-      gemm_epilogue_row(s, e, out, b, row, nt * BN,
-                        tmem_base + ((quarter * 32) << 16) + acc * BN, BN);
+      if (half < SPLIT)
+        gemm_epilogue_row(s, e, out, b, row, nt * BN + half * WIDTH,
+                          tmem_base + ((quarter * 32) << 16) + acc * BN + half * WIDTH, WIDTH);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -533,7 +544,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 8);  // 4 epilogue warps in each CTA of the pair
+      mbar_init(&tempty[i], 2 * GEMM_EPI_WARPS);  // the epilogue warps of both CTAs
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -627,6 +638,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;  // column half of the 256-wide tile (two heads each)
     const int row_in_tile = static_cast<int>(rank) * 128 + quarter * 32 + static_cast<int>(lane);
     const uint32_t leader_tempty0 = cluster_addr(smem_u32(&tempty[0]), 0);
     int local = 0;
@@ -638,8 +650,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int row = mt * 256 + row_in_tile;
-      gemm_epilogue_row(s, e, out, b, row, nt * BN,
-                        tmem_base + ((quarter * 32) << 16) + acc * BN, BN);
+      gemm_epilogue_row(s, e, out, b, row, nt * BN + half * (BN / 2),
+                        tmem_base + ((quarter * 32) << 16) + acc * BN + half * (BN / 2), BN / 2);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);

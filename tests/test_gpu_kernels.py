@@ -279,20 +279,26 @@ def test_split_rope_bit_exact_self_test_recipe(cuda_device):
 
 # ------------------------------------------------------------------------------------ elementwise
 def test_gelu_silu_bounds(cuda_device):
-    """Reference bounds: bf16 max-abs 4e-6 / 0.0 vs fp32 formulas on linspace(-8, 8, 65536)
-    (tests/kernels/test_fused_ops.py in the reference); device tanh may differ by one bf16 ulp."""
+    """On the reference's grid (tests/kernels/test_fused_ops.py: linspace(-8, 8, 65536) in bf16).
+    GELU: the device evaluates 0.5 (1 + tanh u) as the logistic 1 / (1 + e^(-2u)), which is
+    exact where the fp32 tanh formula cancels (the negative tail), so it is held to the float64
+    GELU (bf16 equal almost everywhere) and to the per-op bound against the fp32 formula (max
+    relative error <= 2e-2; one bf16 ulp elementwise). SiLU: equal to the fp32 formula, the
+    reference's bound (max abs 0 in bf16)."""
     from kinomlx_b200 import ops
 
     x = torch.linspace(-8, 8, 65536).to(BF)
-    xf = x.float()
-    gelu = (0.5 * xf * (1 + torch.tanh((0.7978845608028654 * (xf + 0.044715 * xf**3)).clamp(-10, 10)))).to(BF)
+    xf, x64 = x.float(), x.double()
+    gelu32 = (0.5 * xf * (1 + torch.tanh((0.7978845608028654 * (xf + 0.044715 * xf**3)).clamp(-10, 10)))).to(BF)
+    gelu64 = (x64 * torch.special.expit(2 * 0.7978845608028654 * (x64 + 0.044715 * x64**3))).to(BF)
     silu = (xf / (1 + torch.exp(-xf))).to(BF)
     g = ops.gelu_tanh(x.to(cuda_device)).cpu()
     s = ops.silu(x.to(cuda_device)).cpu()
-    assert (g.float() - gelu.float()).abs().max() <= 2 ** -7 * gelu.float().abs().max()
-    assert (s.float() - silu.float()).abs().max() <= 2 ** -7 * silu.float().abs().max()
-    assert (g == gelu).float().mean() > 0.99
-    assert (s == silu).float().mean() > 0.99
+    assert (g == gelu64).float().mean() > 0.99
+    assert (g.float() - gelu32.float()).abs().max() <= 2e-2 * gelu32.float().abs().max()
+    # where the fp32 formula underflows to -0 the exact value is below 1e-6 in magnitude
+    assert ((g.float() - gelu32.float()).abs() <= gelu32.float().abs() * 2.0**-7 + 1e-6).all()
+    assert torch.equal(s, silu)
 
 
 def test_cfg_and_euler_rounding_order(cuda_device):
