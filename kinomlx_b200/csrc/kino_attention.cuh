@@ -7,37 +7,42 @@
 //
 // Layout: q, k and v are token-major, (batch, tokens, heads * 128) with any row stride, which is
 // what the projections write. Queries and keys may each come in two segments (text tokens, then
-// image tokens) that are concatenated logically but never in memory: each 128-row tile belongs
-// to one segment.
+// image tokens) that are concatenated logically but never in memory: each 128-row query tile and
+// each 64-key block belongs to one segment.
 //
-// One CTA computes two 128-query tiles (A and B) of one head, in ping-pong so that one tile's
-// tensor-core work runs under the other tile's softmax:
-//   warp 0      TMA: Q_A and Q_B once, then K and V tiles of 128 keys through a 2-stage ring
+// One CTA computes two 128-query tiles (A and B) of one head over key blocks of 64:
+//   warp 0      TMA: Q_A and Q_B once, then K and V blocks through a 4-stage ring
 //   warp 1      tensor-memory owner and MMA issuer, in the order
-//                 S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
+//                 S_A(0) S_B(0) S_A(1) S_B(1) | PV_A(j) S_A(j+2) PV_B(j) S_B(j+2) | ...
 //   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B, one query row per thread:
-//               tcgen05.ld the S row, online max/sum in the exp2 domain, rescale O in tensor
-//               memory only when the running max grows by more than 2^8 (the stale max cancels
-//               in the final division), write P as bf16 pairs back over S in tensor memory.
-// Tensor memory (512 columns): S_A [0,128) with P_A in [0,64), S_B [128,256) with P_B in
-// [128,192), O_A [256,384), O_B [384,512). The PV product takes P straight from tensor memory
-// (the TMEM-A form of tcgen05.mma) and V in place from shared memory as an MN-major operand.
-// MMAs of one issuing thread run in order, so S(j+1) overwriting P(j) after PV(j) is safe, and
-// the commit that signals S(j+1) also covers PV(j), so O is settled whenever the softmax sees S.
+//               tcgen05.ld the row's 64 scores, online max/sum in the exp2 domain (part of the
+//               exponentials on the FMA pipes), P as bf16 pairs back over the scores, O rescaled
+//               in tensor memory only when the running max grows by more than 2^8 (the stale
+//               max cancels in the final division).
+// Tensor memory (512 columns): S of tile t, block j at [128t + 64(j % 2), +64) with P in its
+// first 32 columns, O_A [256,384), O_B [384,512). Each tile's S is double-buffered, so S(j + 1)
+// is computed while the softmax of block j runs and the softmax never waits for a PV product;
+// the two tiles keep both softmax warp sets busy. The PV product takes P straight from tensor
+// memory (the TMEM-A form of tcgen05.mma) and V in place from shared memory as an MN-major
+// operand. MMAs of one issuing thread run in order, so S(j + 2) overwriting P(j) after PV(j) is
+// safe, and the commit that signals S(j) also covers PV(j - 2).
 #pragma once
 #include "kino_common.cuh"
 
 namespace kino {
 
 constexpr int ATT_BM = 128;  // queries per tile
-constexpr int ATT_BN = 128;  // keys per block
+constexpr int ATT_BN = 64;   // keys per block
 constexpr int ATT_D = 128;   // head dim
-constexpr int ATT_STAGES = 2;
+#ifndef KINO_ATT_STAGES
+#define KINO_ATT_STAGES 4
+#endif
+constexpr int ATT_STAGES = KINO_ATT_STAGES;  // K + V blocks in flight
 constexpr int ATT_THREADS = 320;
-// Pairs i of each 64-column half whose bit (i % 8) is set take the FMA-pipe exponential
-// (exp2_poly_x2) instead of the special-function unit: bits 1, 4, 6 = 24 of 64 pairs per row.
+// Key pairs i of a block whose bit (i % 8) is set take the FMA-pipe exponential
+// (exp2_poly_x2) instead of the special-function unit: bits 1 and 4 = 2 of every 8 pairs.
 #ifndef KINO_ATT_EMU_MASK
-#define KINO_ATT_EMU_MASK 0x52
+#define KINO_ATT_EMU_MASK 0x12
 #endif
 constexpr unsigned ATT_EMU_MASK = KINO_ATT_EMU_MASK;
 
@@ -54,13 +59,14 @@ struct AttnParams {
 };
 
 struct AttnSmem {
-  static constexpr int HALF = ATT_BM * 64 * 2;      // 16 KB: 128 rows x 128 bytes
-  static constexpr int Q_OFF = 0;                   // tile t at Q_OFF + t * 2 * HALF
-  static constexpr int KV_OFF = 4 * HALF;           // per stage: K 2 halves, V 2 halves
-  static constexpr int STAGE = 4 * HALF;
+  static constexpr int QHALF = ATT_BM * 64 * 2;   // 16 KB: 128 query rows x 64 dims
+  static constexpr int KHALF = ATT_BN * 64 * 2;   // 8 KB: 64 key rows x 64 dims
+  static constexpr int Q_OFF = 0;                 // tile t at Q_OFF + t * 2 * QHALF
+  static constexpr int KV_OFF = 4 * QHALF;        // per stage: K 2 halves, V 2 halves
+  static constexpr int STAGE = 4 * KHALF;
   static constexpr int BAR_OFF = KV_OFF + ATT_STAGES * STAGE;
-  // q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_done, drain
-  static constexpr int NBAR = 1 + 2 * ATT_STAGES + 2 + 2 + 2;
+  // q_full, kv_full[S], kv_empty[S], s_full[2][2], p_full[2][2], o_ready[2], o_done, drain
+  static constexpr int NBAR = 1 + 2 * ATT_STAGES + 4 + 4 + 2 + 2;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
 };
 
@@ -117,9 +123,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + ATT_STAGES;
-  uint64_t* s_full = kv_empty + ATT_STAGES;  // [tile]
-  uint64_t* p_full = s_full + 2;             // [tile]
-  uint64_t* o_done = p_full + 2;
+  uint64_t* s_full = kv_empty + ATT_STAGES;  // [tile][S buffer]
+  uint64_t* p_full = s_full + 4;             // [tile][S buffer]
+  uint64_t* o_ready = p_full + 4;            // [tile], one phase per PV
+  uint64_t* o_done = o_ready + 2;
   uint64_t* drain = o_done + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -138,10 +145,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 128);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);  // one arrive per softmax warp of the tile
     }
+    for (int t = 0; t < 2; ++t) mbar_init(&o_ready[t], 1);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -158,12 +166,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, (has_b ? 4 : 2) * L::HALF);
+      mbar_expect_tx(q_full, (has_b ? 4 : 2) * L::QHALF);
       for (int t = 0; t < (has_b ? 2 : 1); ++t) {
         const CUtensorMap* mq = tiles[t].seg ? &mq1 : &mq0;
-        uint8_t* sq = smem + L::Q_OFF + t * 2 * L::HALF;
+        uint8_t* sq = smem + L::Q_OFF + t * 2 * L::QHALF;
         tma_load_4d(sq, mq, q_full, 0, tiles[t].tile * ATT_BM, head, batch);
-        tma_load_4d(sq + L::HALF, mq, q_full, 64, tiles[t].tile * ATT_BM, head, batch);
+        tma_load_4d(sq + L::QHALF, mq, q_full, 64, tiles[t].tile * ATT_BM, head, batch);
       }
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
@@ -175,13 +183,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const CUtensorMap* mk = kseg ? &mk1 : &mk0;
         const CUtensorMap* mv = kseg ? &mv1 : &mv0;
         uint8_t* sk = smem + L::KV_OFF + stage * L::STAGE;
-        uint8_t* sv = sk + 2 * L::HALF;
-        mbar_expect_tx(&kv_full[stage], 4 * L::HALF);
+        uint8_t* sv = sk + 2 * L::KHALF;
+        mbar_expect_tx(&kv_full[stage], 4 * L::KHALF);
         const int t0 = kb * ATT_BN;
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          tma_load_4d(sk + h2 * L::HALF, mk, &kv_full[stage], h2 * 64, t0, head, batch);
-          tma_load_4d(sv + h2 * L::HALF, mv, &kv_full[stage], h2 * 64, t0, head, batch);
+          tma_load_4d(sk + h2 * L::KHALF, mk, &kv_full[stage], h2 * 64, t0, head, batch);
+          tma_load_4d(sv + h2 * L::KHALF, mv, &kv_full[stage], h2 * 64, t0, head, batch);
         }
         ++issued;
       }
@@ -203,54 +211,49 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       constexpr uint32_t idesc_s = idesc_bf16(ATT_BM, ATT_BN);
       constexpr uint32_t idesc_o = idesc_bf16(ATT_BM, ATT_D) | (1u << 16);  // B (V) MN-major
       const int ntile = has_b ? 2 : 1;
-      auto s_mma = [&](int t, int j) {
-        const uint32_t sq = smem_u32(smem + L::Q_OFF + t * 2 * L::HALF);
-        const uint32_t sk = smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE);
+      // S_t(j) into buffer j % 2 of tile t, once K(j) has landed
+      auto s_mma = [&](int t, int j) -> bool {
+        const int stage = j % ATT_STAGES;
+        if (t == 0 && !mbar_wait(&kv_full[stage], (j / ATT_STAGES) & 1, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t sq = smem_u32(smem + L::Q_OFF + t * 2 * L::QHALF);
+        const uint32_t sk = smem_u32(smem + L::KV_OFF + stage * L::STAGE);
 #pragma unroll
         for (int kk = 0; kk < ATT_D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::HALF + (kk & 3) * 32;
-          umma_bf16(tmem + t * 128, sdesc_k128(sq + off), sdesc_k128(sk + off), idesc_s,
+          umma_bf16(tmem + t * 128 + (j & 1) * 64,
+                    sdesc_k128(sq + (kk >> 2) * L::QHALF + (kk & 3) * 32),
+                    sdesc_k128(sk + (kk >> 2) * L::KHALF + (kk & 3) * 32), idesc_s,
                     kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[t]);
+        umma_commit(&s_full[t * 2 + (j & 1)]);
+        return true;
       };
       auto pv_mma = [&](int t, int j) {
         const uint32_t sv =
-            smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE + 2 * L::HALF);
+            smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE + 2 * L::KHALF);
+        const uint32_t pbase = tmem + t * 128 + (j & 1) * 64;
 #pragma unroll
         for (int kk = 0; kk < ATT_BN / 16; ++kk) {
-          umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                       sdesc_mn128(sv + kk * 2048, L::HALF), idesc_o,
+          umma_bf16_ts(tmem + 256 + t * 128, pbase + kk * 8,
+                       sdesc_mn128(sv + kk * 2048, L::KHALF), idesc_o,
                        (j > 0 || kk > 0) ? 1u : 0u);
         }
+        umma_commit(&o_ready[t]);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag) && nblk > 0;
-      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < ntile; ++t) s_mma(t, 0);
-      }
+      if (ok) tc_fence_after();
+      for (int j = 0; ok && j < 2 && j < nblk; ++j)
+        for (int t = 0; ok && t < ntile; ++t) ok = s_mma(t, j);
       for (int j = 0; ok && j < nblk; ++j) {
-        const bool more = j + 1 < nblk;
         for (int t = 0; t < ntile && ok; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag)) {
+          if (!mbar_wait(&p_full[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           pv_mma(t, j);
           if (t == ntile - 1) umma_commit(&kv_empty[j % ATT_STAGES]);
-          if (more) {
-            if (t == 0) {
-              if (!mbar_wait(&kv_full[(j + 1) % ATT_STAGES], ((j + 1) / ATT_STAGES) & 1,
-                             abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-            }
-            s_mma(t, j + 1);
-          }
+          if (j + 2 < nblk) ok = s_mma(t, j + 2);
         }
       }
       umma_commit(o_done);
@@ -267,54 +270,49 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const int quarter = warp & 3;
       const int row = quarter * 32 + static_cast<int>(lane);
       const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-      const uint32_t s_col = tmem + lane_base + t * 128;
       const uint32_t o_col = tmem + lane_base + 256 + t * 128;
       const float sl2 = p.scale_log2;
       float m_run = -INFINITY;  // running max of s * scale * log2(e)
       float l_run = 0.0f;
       bool ok = true;
       for (int j = 0; j < nblk; ++j) {
-        if (!mbar_wait(&s_full[t], j & 1, abort_flag)) {
+        const int buf = j & 1;
+        if (!mbar_wait(&s_full[t * 2 + buf], (j >> 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const uint32_t s_col = tmem + lane_base + t * 128 + buf * 64;
         const int kseg = (j < p.kv_blocks[0]) ? 0 : 1;
         const int kb = j - (kseg ? p.kv_blocks[0] : 0);
         const int valid = min(ATT_BN, p.kv_tokens[kseg] - kb * ATT_BN);
-        uint32_t sr[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(s_col + c * 32, sr[c]);
+        uint32_t sr[2][32];
+        tmem_ld32(s_col, sr[0]);
+        tmem_ld32(s_col + 32, sr[1]);
         tmem_wait_ld();
-        const bool ragged = valid < ATT_BN;  // only a segment's last key block; warp-uniform
-        if (ragged) {
+        if (valid < ATT_BN) {  // only a segment's last key block; warp-uniform
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               if (c * 32 + i >= valid) sr[c][i] = __float_as_uint(-INFINITY);
           }
         }
-        float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        float mq[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            mq[(i >> 3) & 3] = max3f(mq[(i >> 3) & 3], __uint_as_float(sr[c][i]),
-                                     __uint_as_float(sr[c][i + 1]));
-            mq[(i >> 3) & 3] = max3f(mq[(i >> 3) & 3], __uint_as_float(sr[c][i + 2]),
-                                     __uint_as_float(sr[c][i + 3]));
-            mq[(i >> 3) & 3] = max3f(mq[(i >> 3) & 3], __uint_as_float(sr[c][i + 4]),
-                                     __uint_as_float(sr[c][i + 5]));
-            mq[(i >> 3) & 3] = max3f(mq[(i >> 3) & 3], __uint_as_float(sr[c][i + 6]),
-                                     __uint_as_float(sr[c][i + 7]));
-          }
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
+          float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+          a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
+          a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
+          a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
+          a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
+          a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
+          a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
+          mq[q] = fmaxf(a, __uint_as_float(v[15]));
         }
-        const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-        const float m_blk = mx * sl2;
-        // Lazy rescale: the running max moves only when a block's max exceeds it by > 2^8; O is
-        // rescaled below, once S is consumed (PV of the previous block has completed: it was
-        // issued before this block's S).
+        const float m_blk = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
+        // Lazy rescale: the running max moves only when a block's max exceeds it by > 2^8.
         float alpha = 1.0f;
         bool rescale = false;
         if (j > 0) {
@@ -328,40 +326,42 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         } else {
           m_run = m_blk;
         }
-        // P = exp2(s * scale * log2 e - m_run) as bf16 pairs over S's first 64 columns, l the
-        // fp32 sum. Part of the pairs take the FMA-pipe exponential; it gives 2^-126 rather than
-        // 0 for a masked key, whose V row is TMA zero fill, so only l sees it (by 2^-126 each).
         const uint64_t sl2x2 = f2_pack(sl2, sl2);
         const uint64_t negm = f2_pack(-m_run, -m_run);
         uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
-        {
 #pragma unroll
-          for (int q8 = 0; q8 < 8; ++q8) {
-            uint32_t packed[8];
+        for (int q8 = 0; q8 < 4; ++q8) {
+          uint32_t packed[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int i = q8 * 8 + u;  // pair index over the row's 128 columns
-              const uint32_t* src = sr[i >> 4];
-              const int e = (2 * i) & 31;
-              const uint64_t xs = f2_fma(f2_pack(__uint_as_float(src[e]), __uint_as_float(src[e + 1])),
-                                         sl2x2, negm);
-              uint64_t ev;
-              if ((ATT_EMU_MASK >> (i & 7)) & 1) {
-                ev = exp2_poly_x2(xs);
-              } else {
-                const float2 xv = f2_unpack(xs);
-                ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
-              }
-              lsum2[i & 1] = f2_add(lsum2[i & 1], ev);
-              const float2 e2 = f2_unpack(ev);
-              packed[u] = pack_bf16x2(e2.x, e2.y);
+          for (int u = 0; u < 8; ++u) {
+            const int i = q8 * 8 + u;  // key pair index within the block
+            const uint32_t* v = sr[i >> 4];
+            const int e = (2 * i) & 31;
+            const uint64_t xs =
+                f2_fma(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sl2x2, negm);
+            uint64_t ev;
+            if ((ATT_EMU_MASK >> (i & 7)) & 1) {
+              ev = exp2_poly_x2(xs);
+            } else {
+              const float2 xv = f2_unpack(xs);
+              ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
             }
-            tmem_st8(s_col + q8 * 8, packed);
+            lsum2[u & 1] = f2_add(lsum2[u & 1], ev);
+            const float2 e2 = f2_unpack(ev);
+            packed[u] = pack_bf16x2(e2.x, e2.y);
           }
+          tmem_st8(s_col + q8 * 8, packed);
         }
         const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
         l_run += ls.x + ls.y;
         if (rescale) {
+          // O must hold PV(j - 1) before it is scaled (PV(j - 2) completed before S(j) did,
+          // so the parity names the right phase)
+          if (!mbar_wait(&o_ready[t], (j - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -374,7 +374,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[t]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t * 2 + buf]);
       }
       if (ok && nblk > 0 && mbar_wait(o_done, 0, abort_flag)) {
         tc_fence_after();

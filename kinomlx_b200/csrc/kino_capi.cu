@@ -425,7 +425,8 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
   p.nkv_seg = a->n_kv;
   p.scale_log2 = a->scale * 1.4426950408889634f;
   CUtensorMap mq[2], mk[2], mv[2];
-  const uint32_t box[4] = {64, 128, 1, 1};
+  const uint32_t box[4] = {64, kino::ATT_BM, 1, 1};
+  const uint32_t kvbox[4] = {64, kino::ATT_BN, 1, 1};
   int tiles = 0;
   for (int s = 0; s < 2; ++s) {
     const int qs = s < a->n_q ? s : 0;
@@ -463,13 +464,13 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
                             static_cast<uint64_t>(a->batch > 1 ? a->bs_k[ks] : 8)};
     const uint64_t sv[3] = {static_cast<uint64_t>(a->ld_v[ks]), 128,
                             static_cast<uint64_t>(a->batch > 1 ? a->bs_v[ks] : 8)};
-    st = make_map(&mk[s], a->k[ks], 4, dk, sk, box);
+    st = make_map(&mk[s], a->k[ks], 4, dk, sk, kvbox);
     if (st != KINO_OK) return st;
-    st = make_map(&mv[s], a->v[ks], 4, dk, sv, box);
+    st = make_map(&mv[s], a->v[ks], 4, dk, sv, kvbox);
     if (st != KINO_OK) return st;
     if (s < a->n_kv) {
       p.kv_tokens[s] = static_cast<int>(a->kv_tokens[s]);
-      p.kv_blocks[s] = (p.kv_tokens[s] + 127) / 128;
+      p.kv_blocks[s] = (p.kv_tokens[s] + kino::ATT_BN - 1) / kino::ATT_BN;
     }
   }
   kino_status st = ensure_smem(kino::attention_tc_kernel, kino::AttnSmem::TOTAL, 3);
