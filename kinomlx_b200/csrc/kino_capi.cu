@@ -517,8 +517,28 @@ kino_status kino_adaln(const void* x, int64_t ldx, int64_t bsx, const void* shif
   if (rows < 1 || batch < 1 || rows > 0x7fffffff || batch > 65535)
     return fail(KINO_EINVAL, "kino_adaln: rows/batch");
   if (norm_kind < 0 || norm_kind > 2) return fail(KINO_EINVAL, "kino_adaln: norm kind");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // warp per row where the width is a multiple of 256 the kernel is instantiated for
+  auto warp_form = [&](auto kernel) {
+    dim3 wgrid(static_cast<unsigned>((rows + kino::ADALN_WARPS - 1) / kino::ADALN_WARPS),
+               static_cast<unsigned>(batch));
+    kernel<<<wgrid, kino::ADALN_WARPS * 32, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, bsx, static_cast<const __nv_bfloat16*>(shift),
+        static_cast<const __nv_bfloat16*>(scale), bs_mod, static_cast<__nv_bfloat16*>(out), ldo,
+        bso, static_cast<int>(rows), norm_kind, eps);
+    return check_launch("kino_adaln");
+  };
+  switch (dim) {
+    case 256: return warp_form(kino::adaln_warp_kernel<1>);
+    case 512: return warp_form(kino::adaln_warp_kernel<2>);
+    case 1024: return warp_form(kino::adaln_warp_kernel<4>);
+    case 2048: return warp_form(kino::adaln_warp_kernel<8>);
+    case 3072: return warp_form(kino::adaln_warp_kernel<12>);
+    case 4096: return warp_form(kino::adaln_warp_kernel<16>);
+    default: break;
+  }
   dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(batch));
-  kino::adaln_kernel<<<grid, kino::ADALN_THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+  kino::adaln_kernel<<<grid, kino::ADALN_THREADS, 0, st>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, bsx, static_cast<const __nv_bfloat16*>(shift),
       static_cast<const __nv_bfloat16*>(scale), bs_mod, static_cast<__nv_bfloat16*>(out), ldo,
       bso, static_cast<int>(rows), static_cast<int>(dim), norm_kind, eps);

@@ -118,6 +118,98 @@ __global__ void __launch_bounds__(ADALN_THREADS)
   }
 }
 
+// Warp-per-row form of the same modulated norm for dim = 256 * VPL: a warp holds its row in
+// registers as packed bf16 (VPL 16-byte vectors per lane), reduces with shuffles only, and reads
+// shift and bf16(1 + scale) from shared memory, filled once per CTA. Same rounding points as
+// adaln_kernel.
+constexpr int ADALN_WARPS = 8;
+
+template <int VPL>
+__global__ void __launch_bounds__(ADALN_WARPS * 32)
+    adaln_warp_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x, int64_t bs_x,
+                      const __nv_bfloat16* __restrict__ shift,
+                      const __nv_bfloat16* __restrict__ scale, int64_t bs_mod,
+                      __nv_bfloat16* __restrict__ out, int64_t ld_out, int64_t bs_out, int rows,
+                      int norm_kind, float eps) {
+  constexpr int DIM = VPL * 256;
+  __shared__ uint4 s_shift[DIM / 8];
+  __shared__ uint4 s_onep[DIM / 8];  // bf16(1 + scale)
+  const int b = blockIdx.y;
+  const __nv_bfloat16* sh = shift + b * bs_mod;
+  const __nv_bfloat16* sc = scale + b * bs_mod;
+  for (int c = threadIdx.x; c < DIM / 8; c += ADALN_WARPS * 32) {
+    s_shift[c] = *reinterpret_cast<const uint4*>(sh + c * 8);
+    float f[8], o[8];
+    load8(sc + c * 8, f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = 1.0f + f[j];
+    uint4 w;
+    w.x = pack_bf16x2(o[0], o[1]);
+    w.y = pack_bf16x2(o[2], o[3]);
+    w.z = pack_bf16x2(o[4], o[5]);
+    w.w = pack_bf16x2(o[6], o[7]);
+    s_onep[c] = w;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * ADALN_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const __nv_bfloat16* xr = x + b * bs_x + static_cast<int64_t>(row) * ld_x;
+  __nv_bfloat16* orow = out + b * bs_out + static_cast<int64_t>(row) * ld_out;
+  uint4 raw[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) raw[i] = *reinterpret_cast<const uint4*>(xr + (i * 32 + lane) * 8);
+  auto unpack = [](const uint4& r, float (&f)[8]) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 t = unpack_bf16x2(w[k]);
+      f[2 * k] = t.x;
+      f[2 * k + 1] = t.y;
+    }
+  };
+  float mean = 0.0f, rstd = 1.0f;
+  if (norm_kind != 2) {
+    if (norm_kind == 1) {
+      float s = 0.0f;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        float f[8];
+        unpack(raw[i], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += f[j];
+      }
+      mean = warp_sum(s) / static_cast<float>(DIM);
+    }
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      float f[8];
+      unpack(raw[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = f[j] - mean;
+        q += d * d;
+      }
+    }
+    rstd = rsqrtf(warp_sum(q) / static_cast<float>(DIM) + eps);
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = i * 32 + lane;
+    float f[8], fs[8], op[8], o[8];
+    unpack(raw[i], f);
+    unpack(s_shift[c], fs);
+    unpack(s_onep[c], op);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float n = norm_kind == 2 ? f[j] : bf16_round((f[j] - mean) * rstd);
+      o[j] = bf16_round(n * op[j]) + fs[j];
+    }
+    store8(orow + c * 8, o);
+  }
+}
+
 // ----------------------------------------------------------------------------- RMSNorm
 // Weighted RMSNorm with fp32 reduction, fp32 scale by (weight + offset), one rounding
 // (kinomlx/kernels/fused_ops.py:141-193, 412-457); without a weight, the plain fp32 form.
