@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
+  griddep_wait();  // the previous kernel has finished with its memory and tensor memory
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {

@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "../../include/kino.h"
 #include "kino_attention.cuh"
@@ -33,10 +34,62 @@ kino_status fail(kino_status code, const char* fmt, ...) {
   return code;
 }
 
+thread_local cudaError_t t_launch_error = cudaSuccess;
+
 kino_status check_launch(const char* what) {
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = t_launch_error;
+  t_launch_error = cudaSuccess;
+  const cudaError_t last = cudaGetLastError();
+  if (e == cudaSuccess) e = last;
   if (e != cudaSuccess) return fail(KINO_ECUDA, "%s: %s", what, cudaGetErrorString(e));
   return KINO_OK;
+}
+
+// Programmatic dependent launch (the kernel's prologue may overlap the previous kernel's tail;
+// every kernel waits with griddepcontrol.wait before touching global memory) unless
+// KINO_PDL=0 in the environment.
+bool pdl_enabled() {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* v = getenv("KINO_PDL");
+    enabled = (v != nullptr && v[0] == '0') ? 0 : 1;
+  }
+  return enabled == 1;
+}
+
+// Launch with the PDL attribute (and a cluster of `cluster_x` CTAs when > 1); a failure is
+// reported by the next check_launch().
+template <typename... KArgs, typename... Args>
+void launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+               int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[n].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  ++n;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess && t_launch_error == cudaSuccess) t_launch_error = e;
+}
+
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                Args&&... args) {
+  launch_ex(kernel, grid, block, smem, stream, 1, std::forward<Args>(args)...);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -142,7 +195,7 @@ kino_status launch_gemm(const void* x, const void* w, void* out, const kino::Gem
   st = ensure_smem(kernel, L::TOTAL, slot);
   if (st != KINO_OK) return st;
   const int grid = s.num_tiles < device_sms() ? s.num_tiles : device_sms();
-  kernel<<<grid, kino::GEMM_THREADS, L::TOTAL, stream>>>(
+  launch_pdl(kernel, dim3(grid), dim3(kino::GEMM_THREADS), L::TOTAL, stream,
       ma, mb, reinterpret_cast<__nv_bfloat16*>(out), s, e);
   return check_launch("kino_linear");
 }
@@ -175,7 +228,7 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   kino::ConvEpi e;
   e.bias = static_cast<const __nv_bfloat16*>(a->bias);
   e.residual = static_cast<const __nv_bfloat16*>(a->residual);
-  kernel<<<grid, kino::CONV_THREADS, L::TOTAL, stream>>>(
+  launch_pdl(kernel, dim3(grid), dim3(kino::CONV_THREADS), L::TOTAL, stream,
       mx, mw, static_cast<__nv_bfloat16*>(a->out), s, e);
   return check_launch("kino_conv3d");
 }
@@ -208,22 +261,8 @@ kino_status launch_gemm_2sm(const void* x, const void* w, void* out, const kino:
   if (st != KINO_OK) return st;
   const int max_pairs = device_sms() / 2;
   const int pairs = s.num_tiles < max_pairs ? s.num_tiles : max_pairs;
-  cudaLaunchConfig_t cfg;
-  std::memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kino::GEMM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = L::TOTAL;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, ma, mb,
-                                             reinterpret_cast<__nv_bfloat16*>(out), s, e);
-  if (err != cudaSuccess) return fail(KINO_ECUDA, "kino_linear (2-SM): %s", cudaGetErrorString(err));
+  launch_ex(kernel, dim3(2 * pairs, 1, 1), dim3(kino::GEMM_THREADS, 1, 1), L::TOTAL, stream, 2, ma,
+            mb, reinterpret_cast<__nv_bfloat16*>(out), s, e);
   return check_launch("kino_linear (2-SM)");
 }
 
@@ -401,7 +440,7 @@ kino_status kino_gemv(const void* x, int64_t ldx, const void* w, const void* bia
   if (s != KINO_OK) return s;
   const int per = kino::GEMV_THREADS / 32;
   const int grid = static_cast<int>((n + per - 1) / per);
-  kino::gemv_kernel<<<grid, kino::GEMV_THREADS, smem, static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::gemv_kernel, dim3(grid), dim3(kino::GEMV_THREADS), smem, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w),
       static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(y), ldy,
       static_cast<int>(batch), static_cast<int>(n), static_cast<int>(k), act);
@@ -476,8 +515,7 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
   kino_status st = ensure_smem(kino::attention_tc_kernel, kino::AttnSmem::TOTAL, 3);
   if (st != KINO_OK) return st;
   dim3 grid((tiles + 1) / 2, p.heads, p.batch);  // two 128-query tiles per CTA
-  kino::attention_tc_kernel<<<grid, kino::ATT_THREADS, kino::AttnSmem::TOTAL,
-                              static_cast<cudaStream_t>(stream)>>>(mq[0], mq[1], mk[0], mk[1],
+  launch_pdl(kino::attention_tc_kernel, dim3(grid), dim3(kino::ATT_THREADS), kino::AttnSmem::TOTAL, static_cast<cudaStream_t>(stream), mq[0], mq[1], mk[0], mk[1],
                                                                    mv[0], mv[1], p);
   return check_launch("kino_attention");
 }
@@ -522,7 +560,7 @@ kino_status kino_adaln(const void* x, int64_t ldx, int64_t bsx, const void* shif
   auto warp_form = [&](auto kernel) {
     dim3 wgrid(static_cast<unsigned>((rows + kino::ADALN_WARPS - 1) / kino::ADALN_WARPS),
                static_cast<unsigned>(batch));
-    kernel<<<wgrid, kino::ADALN_WARPS * 32, 0, st>>>(
+    launch_pdl(kernel, dim3(wgrid), dim3(kino::ADALN_WARPS * 32), 0, st,
         static_cast<const __nv_bfloat16*>(x), ldx, bsx, static_cast<const __nv_bfloat16*>(shift),
         static_cast<const __nv_bfloat16*>(scale), bs_mod, static_cast<__nv_bfloat16*>(out), ldo,
         bso, static_cast<int>(rows), norm_kind, eps);
@@ -538,7 +576,7 @@ kino_status kino_adaln(const void* x, int64_t ldx, int64_t bsx, const void* shif
     default: break;
   }
   dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(batch));
-  kino::adaln_kernel<<<grid, kino::ADALN_THREADS, 0, st>>>(
+  launch_pdl(kino::adaln_kernel, dim3(grid), dim3(kino::ADALN_THREADS), 0, st,
       static_cast<const __nv_bfloat16*>(x), ldx, bsx, static_cast<const __nv_bfloat16*>(shift),
       static_cast<const __nv_bfloat16*>(scale), bs_mod, static_cast<__nv_bfloat16*>(out), ldo,
       bso, static_cast<int>(rows), static_cast<int>(dim), norm_kind, eps);
@@ -552,8 +590,7 @@ kino_status kino_rms_norm(const void* x, const void* weight, void* out, int64_t 
       (weight != nullptr && !aligned16(weight)))
     return fail(KINO_ENOTSUPPORTED, "kino_rms_norm: dim %% 8, dim <= 8192, aligned operands");
   if (rows < 1 || rows > 0x7fffffff) return fail(KINO_EINVAL, "kino_rms_norm: rows");
-  kino::rms_norm_kernel<<<static_cast<unsigned>(rows), kino::ADALN_THREADS, 0,
-                          static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::rms_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kino::ADALN_THREADS), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
       static_cast<__nv_bfloat16*>(out), static_cast<int>(dim), eps, weight_offset);
   return check_launch("kino_rms_norm");
@@ -577,8 +614,7 @@ kino_status kino_qk_norm_rope(void* x, int64_t ld, int64_t bs, int64_t batch, in
   if (rope_kind != 0 && table_offset + tokens > table_tokens)
     return fail(KINO_EINVAL, "kino_qk_norm_rope: table too short");
   dim3 grid(static_cast<unsigned>(tokens), static_cast<unsigned>(batch));
-  kino::qk_norm_rope_kernel<<<grid, static_cast<unsigned>(heads * 8), 0,
-                              static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::qk_norm_rope_kernel, dim3(grid), dim3(static_cast<unsigned>(heads * 8)), 0, static_cast<cudaStream_t>(stream),
       static_cast<__nv_bfloat16*>(x), ld, bs, static_cast<int>(heads),
       static_cast<const __nv_bfloat16*>(weight), norm_kind, rope_kind, cos_table, sin_table,
       table_batched, static_cast<int>(table_tokens), static_cast<int>(table_offset), eps);
@@ -595,8 +631,7 @@ kino_status kino_split_rope(const void* x, const float* cos_table, const float* 
   const int64_t n = batch * tokens * heads * half;
   int64_t blocks = (n + 255) / 256;
   if (blocks > 65535 * 8) blocks = 65535 * 8;
-  kino::split_rope_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                            static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::split_rope_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(x), cos_table, sin_table,
       static_cast<__nv_bfloat16*>(out), static_cast<int>(batch), static_cast<int>(tokens),
       static_cast<int>(heads), static_cast<int>(half), table_batched);
@@ -611,8 +646,7 @@ static kino_status launch_elem(int kind, const void* a, const void* b, void* out
   if (n == 0) return KINO_OK;
   int64_t blocks = (n / 8 + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  kino::elementwise_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                             static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::elementwise_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       kind, static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
       static_cast<__nv_bfloat16*>(out), n, s0, s1);
   return check_launch(name);
@@ -652,8 +686,7 @@ kino_status kino_add_rows(const void* a, const void* b, void* out, int64_t rows,
     return fail(KINO_ENOTSUPPORTED, "kino_add_rows: n %% 8 == 0 and aligned operands");
   int64_t blocks = (rows * n / 8 + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  kino::add_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                          static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::add_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(a), static_cast<const __nv_bfloat16*>(b),
       static_cast<__nv_bfloat16*>(out), rows, n);
   return check_launch("kino_add_rows");
@@ -667,8 +700,7 @@ kino_status kino_heads_pack(const void* src, int64_t ld, void* dst, int64_t toke
   int64_t blocks = (tokens * width / 8 + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) return KINO_OK;
-  kino::heads_pack_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                            static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::heads_pack_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(src), ld, static_cast<__nv_bfloat16*>(dst),
       static_cast<int>(tokens), static_cast<int>(width), static_cast<int>(parts));
   return check_launch("kino_heads_pack");
@@ -683,8 +715,7 @@ kino_status kino_heads_unpack(const void* src, void* dst, int64_t ld, int64_t to
   int64_t blocks = (tokens * width / 8 + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) return KINO_OK;
-  kino::heads_unpack_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                              static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::heads_unpack_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst), ld,
       static_cast<int>(tokens), static_cast<int>(width), static_cast<int>(parts),
       static_cast<const __nv_bfloat16*>(gate), ld_gate);
@@ -696,8 +727,7 @@ kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, in
   if (t == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_timestep_embedding: null");
   if (batch < 1 || dim < 2 || dim % 2 || batch > 65535)
     return fail(KINO_EINVAL, "kino_timestep_embedding: shape");
-  kino::timestep_embedding_kernel<<<static_cast<unsigned>(batch), 128, 0,
-                                    static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::timestep_embedding_kernel, dim3(static_cast<unsigned>(batch)), dim3(128), 0, static_cast<cudaStream_t>(stream),
       t, static_cast<__nv_bfloat16*>(out), static_cast<int>(batch), static_cast<int>(dim));
   return check_launch("kino_timestep_embedding");
 }
@@ -763,8 +793,7 @@ kino_status kino_pixel_norm(const void* x, void* out, int64_t voxels, int64_t ch
     return fail(KINO_ENOTSUPPORTED, "kino_pixel_norm: channels %% 8, <= 1024, aligned");
   const int64_t threads = voxels * 32;
   const int64_t blocks = (threads + 255) / 256;
-  kino::pixel_norm_silu_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::pixel_norm_silu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), voxels,
       static_cast<int>(channels), eps, apply_silu);
   return check_launch("kino_pixel_norm");
@@ -794,13 +823,13 @@ kino_status kino_group_norm(const void* x, const void* weight, const void* bias,
   const int c = static_cast<int>(channels);
   const int64_t count = voxels * (channels / kino::GN_GROUPS);
   for (int pass = 0; pass < 2; ++pass) {
-    kino::group_norm_partial_kernel<<<parts, kino::GN_THREADS, 0, s>>>(xb, voxels, c, ws, parts,
+    launch_pdl(kino::group_norm_partial_kernel, dim3(parts), dim3(kino::GN_THREADS), 0, s, xb, voxels, c, ws, parts,
                                                                        pass);
-    kino::group_norm_finalize_kernel<<<1, 32, 0, s>>>(ws, parts, count, eps, pass);
+    launch_pdl(kino::group_norm_finalize_kernel, dim3(1), dim3(32), 0, s, ws, parts, count, eps, pass);
   }
   int64_t blocks = (voxels * channels / 8 + 255) / 256;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  kino::group_norm_apply_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+  launch_pdl(kino::group_norm_apply_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
       xb, static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(bias),
       static_cast<__nv_bfloat16*>(out), voxels, c, ws, parts, apply_silu);
   return check_launch("kino_group_norm");
@@ -830,8 +859,7 @@ kino_status kino_latent_to_bfhwc(const void* latent, const float* std_of_means,
   if (channels < 1 || voxels < 1) return fail(KINO_EINVAL, "kino_latent_to_bfhwc: empty");
   int64_t blocks = (channels * voxels + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
-  kino::latent_to_bfhwc_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::latent_to_bfhwc_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(latent), std_of_means, mean_of_means,
       static_cast<__nv_bfloat16*>(out), static_cast<int>(channels), voxels);
   return check_launch("kino_latent_to_bfhwc");
@@ -849,8 +877,7 @@ kino_status kino_tile_blend(const void* decoded, int64_t frames, int64_t height,
   const int64_t n = channels * frames * height * patch * width * patch;
   int64_t blocks = (n + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
-  kino::tile_blend_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                            static_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(kino::tile_blend_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(decoded), static_cast<int>(frames),
       static_cast<int>(height), static_cast<int>(width), static_cast<int>(channels),
       static_cast<int>(patch), canvas, weights, static_cast<int>(out_height),
@@ -863,8 +890,7 @@ kino_status kino_blend_normalize(float* canvas, const float* weights, int64_t pl
   if (canvas == nullptr || weights == nullptr) return fail(KINO_EINVAL, "kino_blend_normalize: null");
   int64_t blocks = (planes * hw + 255) / 256;
   if (blocks > 148 * 32) blocks = 148 * 32;
-  kino::blend_normalize_kernel<<<static_cast<unsigned>(blocks), 256, 0,
-                                 static_cast<cudaStream_t>(stream)>>>(canvas, weights, planes, hw);
+  launch_pdl(kino::blend_normalize_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream), canvas, weights, planes, hw);
   return check_launch("kino_blend_normalize");
 }
 

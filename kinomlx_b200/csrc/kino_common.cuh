@@ -40,6 +40,17 @@ __device__ __forceinline__ uint32_t lane_id() {
 
 __device__ __forceinline__ int warp_id() { return threadIdx.x >> 5; }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while the previous kernel
+// on the stream is still finishing; griddep_wait() blocks until that kernel has completed and
+// its memory is visible (a no-op without the launch attribute). Every kernel calls it before
+// its first access to global memory (and before allocating tensor memory, which the previous
+// kernel may still hold); griddep_launch() lets the next kernel start its own prologue early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- mbarriers
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

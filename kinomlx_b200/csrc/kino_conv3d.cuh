@@ -76,6 +76,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     tma_prefetch(&map_x);
     tma_prefetch(&map_w);
   }
+  griddep_wait();  // the previous kernel has finished with its memory and tensor memory
   if (warp == 1) {
     tmem_alloc(tmem_base_slot, 2 * BN);
     tmem_relinquish();
@@ -84,6 +85,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  griddep_launch();
   const int box_rows = s.th * s.tw;
 
   if (warp == 0) {

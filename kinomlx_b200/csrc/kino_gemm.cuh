@@ -370,6 +370,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tma_prefetch(&map_a);
     tma_prefetch(&map_b);
   }
+  griddep_wait();  // the previous kernel has finished with its memory and tensor memory
   if (warp == 1) {
     tmem_alloc(tmem_base_slot, 2 * BN);
     tmem_relinquish();
@@ -378,6 +379,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -554,6 +556,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tma_prefetch(&map_a);
     tma_prefetch(&map_b);
   }
+  griddep_wait();  // the previous kernel has finished with its memory and tensor memory
   if (warp == 1) {
     tmem_alloc_pair(tmem_base_slot, 2 * BN);
     tmem_relinquish_pair();
@@ -563,6 +566,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   cluster_sync();  // barriers of both CTAs initialised before any remote arrive or complete_tx
   tc_fence_after();
   const uint32_t tmem_base = *tmem_base_slot;
+  griddep_launch();
 
   if (warp == 0) {
     if (lane == 0) {

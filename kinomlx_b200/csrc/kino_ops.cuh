@@ -60,6 +60,8 @@ __global__ void __launch_bounds__(ADALN_THREADS)
                  const __nv_bfloat16* __restrict__ shift, const __nv_bfloat16* __restrict__ scale,
                  int64_t bs_mod, __nv_bfloat16* __restrict__ out, int64_t ld_out, int64_t bs_out,
                  int rows, int dim, int norm_kind, float eps) {
+  griddep_wait();
+  griddep_launch();
   // norm_kind: 0 RMSNorm, 1 LayerNorm, 2 none (modulation only,
   // kinomlx/models/ltx2/transformer/transformer.py:34-35)
   __shared__ float red[32];
@@ -131,6 +133,8 @@ __global__ void __launch_bounds__(ADALN_WARPS * 32)
                       const __nv_bfloat16* __restrict__ scale, int64_t bs_mod,
                       __nv_bfloat16* __restrict__ out, int64_t ld_out, int64_t bs_out, int rows,
                       int norm_kind, float eps) {
+  griddep_wait();
+  griddep_launch();
   constexpr int DIM = VPL * 256;
   __shared__ uint4 s_shift[DIM / 8];
   __shared__ uint4 s_onep[DIM / 8];  // bf16(1 + scale)
@@ -216,6 +220,8 @@ __global__ void __launch_bounds__(ADALN_WARPS * 32)
 __global__ void __launch_bounds__(ADALN_THREADS)
     rms_norm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                     __nv_bfloat16* __restrict__ out, int dim, float eps, float offset) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * dim;
@@ -269,6 +275,8 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, i
                                     int rope_kind, const float* __restrict__ cos_t,
                                     const float* __restrict__ sin_t, int table_batched,
                                     int table_tokens, int table_offset, float eps) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float red[32];
   const int t = blockIdx.x;
   const int b = blockIdx.y;
@@ -366,6 +374,8 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, i
 __global__ void split_rope_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ cs,
                                   const float* __restrict__ sn, __nv_bfloat16* __restrict__ out,
                                   int batch, int tokens, int heads, int half, int table_batched) {
+  griddep_wait();
+  griddep_launch();
   const int64_t n = static_cast<int64_t>(batch) * tokens * heads * half;
   for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < n;
        idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -404,6 +414,8 @@ enum ElemKind : int {
 __global__ void elementwise_kernel(int kind, const __nv_bfloat16* __restrict__ a,
                                    const __nv_bfloat16* __restrict__ bsrc,
                                    __nv_bfloat16* __restrict__ out, int64_t n, float s0, float s1) {
+  griddep_wait();
+  griddep_launch();
   const int64_t nv = n >> 3;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -446,6 +458,8 @@ __global__ void elementwise_kernel(int kind, const __nv_bfloat16* __restrict__ a
 __global__ void add_rows_kernel(const __nv_bfloat16* __restrict__ a,
                                 const __nv_bfloat16* __restrict__ b,
                                 __nv_bfloat16* __restrict__ out, int64_t rows, int64_t n) {
+  griddep_wait();
+  griddep_launch();
   const int64_t nv = (rows * n) >> 3;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -468,6 +482,8 @@ __global__ void add_rows_kernel(const __nv_bfloat16* __restrict__ a,
 __global__ void heads_pack_kernel(const __nv_bfloat16* __restrict__ src, int64_t ld,
                                   __nv_bfloat16* __restrict__ dst, int tokens, int width,
                                   int parts) {
+  griddep_wait();
+  griddep_launch();
   const int chunk = width / parts;  // elements per rank per token
   const int64_t nv = (static_cast<int64_t>(tokens) * width) >> 3;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
@@ -485,6 +501,8 @@ __global__ void heads_unpack_kernel(const __nv_bfloat16* __restrict__ src,
                                     __nv_bfloat16* __restrict__ dst, int64_t ld, int tokens,
                                     int width, int parts, const __nv_bfloat16* __restrict__ gate,
                                     int64_t ld_gate) {
+  griddep_wait();
+  griddep_launch();
   const int chunk = width / parts;
   const int64_t nv = (static_cast<int64_t>(tokens) * width) >> 3;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
@@ -520,6 +538,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld_x,
                 const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ bias,
                 __nv_bfloat16* __restrict__ y, int64_t ld_y, int batch, int n, int k, int act) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ float xs[];  // [batch][k]
   for (int i = threadIdx.x; i < batch * k; i += blockDim.x) {
     const int b = i / k;
@@ -564,6 +584,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 // (kinomlx/models/flux2/transformer.py:238-241, kinomlx/models/ltx2/transformer/timestep.py:13-28).
 __global__ void timestep_embedding_kernel(const float* __restrict__ t, __nv_bfloat16* __restrict__ out,
                                           int batch, int dim) {
+  griddep_wait();
+  griddep_launch();
   const int half = dim / 2;
   const int b = blockIdx.x;
   for (int i = threadIdx.x; i < half; i += blockDim.x) {

@@ -12,6 +12,8 @@ namespace kino {
 __global__ void pixel_norm_silu_kernel(const __nv_bfloat16* __restrict__ x,
                                        __nv_bfloat16* __restrict__ out, int64_t voxels, int C,
                                        float eps, int apply_silu) {
+  griddep_wait();
+  griddep_launch();
   const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp_global >= voxels) return;
@@ -61,6 +63,8 @@ constexpr int GN_THREADS = 256;
 __global__ void __launch_bounds__(GN_THREADS)
     group_norm_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t voxels, int C,
                               float* __restrict__ ws, int parts, int pass) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float gsum[GN_GROUPS];
   if (threadIdx.x < GN_GROUPS) gsum[threadIdx.x] = 0.0f;
   __syncthreads();
@@ -98,6 +102,8 @@ __global__ void __launch_bounds__(GN_THREADS)
 // One CTA of 32 threads: reduce the partials of group g; pass 0 writes mean, pass 1 rstd.
 __global__ void group_norm_finalize_kernel(float* __restrict__ ws, int parts, int64_t count,
                                            float eps, int pass) {
+  griddep_wait();
+  griddep_launch();
   const int g = threadIdx.x;
   if (g >= GN_GROUPS) return;
   float s = 0.0f;
@@ -116,6 +122,8 @@ __global__ void group_norm_apply_kernel(const __nv_bfloat16* __restrict__ x,
                                         const __nv_bfloat16* __restrict__ bias,
                                         __nv_bfloat16* __restrict__ out, int64_t voxels, int C,
                                         const float* __restrict__ ws, int parts, int apply_silu) {
+  griddep_wait();
+  griddep_launch();
   const int gs = C / GN_GROUPS;
   const float* mean = ws + static_cast<int64_t>(parts) * GN_GROUPS;
   const float* rstd = mean + GN_GROUPS;
@@ -144,6 +152,8 @@ __global__ void latent_to_bfhwc_kernel(const __nv_bfloat16* __restrict__ latent,
                                        const float* __restrict__ stdv,
                                        const float* __restrict__ meanv,
                                        __nv_bfloat16* __restrict__ out, int C, int64_t voxels) {
+  griddep_wait();
+  griddep_launch();
   const int64_t n = voxels * C;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -163,6 +173,8 @@ __global__ void tile_blend_kernel(const __nv_bfloat16* __restrict__ dec, int Ft,
                                   int channels, int patch, float* __restrict__ canvas,
                                   float* __restrict__ wcanvas, int Hout, int Wout, int y0, int x0,
                                   const float* __restrict__ mask_h, const float* __restrict__ mask_w) {
+  griddep_wait();
+  griddep_launch();
   const int Hp = ht * patch, Wp = wt * patch;
   const int64_t n = static_cast<int64_t>(channels) * Ft * Hp * Wp;
   const int packed = channels * patch * patch;
@@ -189,6 +201,8 @@ __global__ void tile_blend_kernel(const __nv_bfloat16* __restrict__ dec, int Ft,
 __global__ void blend_normalize_kernel(float* __restrict__ canvas,
                                        const float* __restrict__ wcanvas, int64_t planes,
                                        int64_t hw) {
+  griddep_wait();
+  griddep_launch();
   const int64_t n = planes * hw;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
