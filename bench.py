@@ -350,16 +350,20 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
         peak = float(pk["hbm_gbs"])
         bound, unit = "hbm", "GB/s"
         per_launch_flops = None
-    traffic = None
+    # DRAM bytes of one launch of the kernel class from an ncu capture: "<class> <read+write
+    # bytes> <algorithmic bytes of that launch> <which launch>"
+    traffic = traffic_alg = traffic_launch = None
     tf = ROOT / "profiles" / "traffic.txt"
     if tf.exists():
         for line in tf.read_text().splitlines():
-            parts = line.split()
+            parts = line.split(maxsplit=3)
             if len(parts) >= 2 and parts[0] == dom:
                 try:
                     traffic = float(parts[1])
+                    traffic_alg = float(parts[2]) if len(parts) > 2 else None
                 except ValueError:
-                    traffic = None
+                    traffic = traffic_alg = None
+                traffic_launch = parts[3] if len(parts) > 3 else None
     roofline = {
         "kernel": dom,
         "bound": bound,
@@ -369,6 +373,8 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
         "frac": round(achieved / peak, 4),
         "peak_source": f"{source} ({'sustained' if bound == 'tensor' else 'copy'})",
         "traffic": traffic,
+        "traffic_launch": traffic_launch,
+        "traffic_algorithmic_bytes": traffic_alg,
         "algorithmic_per_launch": per_launch_flops,
         "step_tflops": round(step_flops() / (ms * 1e9), 1),
         "timing": "per-launch CUDA events over a second pass of the same K steps",
