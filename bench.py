@@ -623,6 +623,8 @@ def main() -> None:
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
         return
+    # NCCL's own messages (its version banner included) go to stderr: stdout carries one JSON line
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     world, rank, local = dist_setup()
     try:
         run_kino(args, world, rank, local)
