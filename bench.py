@@ -51,6 +51,27 @@ def log(msg: str) -> None:
     print(msg, file=sys.stderr, flush=True)
 
 
+_RESULT_OUT = sys.stdout
+
+
+def reserve_stdout() -> None:
+    """Keep the process's stdout for the result line alone: file descriptor 1 and sys.stdout are
+    pointed at stderr (libraries that print at the C level, NCCL's banner among them, land
+    there), and the original stdout is kept for emit()."""
+    global _RESULT_OUT
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    _RESULT_OUT = os.fdopen(saved, "w")
+    sys.stdout = sys.stderr
+
+
+def emit(obj: dict) -> None:
+    """The one JSON result line."""
+    _RESULT_OUT.write(json.dumps(obj) + "\n")
+    _RESULT_OUT.flush()
+
+
 def peaks() -> tuple[dict, str]:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -241,7 +262,7 @@ def run_reference(args, world: int, rank: int) -> None:
         "e2e": {"value": round(ms, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -422,7 +443,7 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
             "clocks": clocks,
             "secondary": secondary,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def ltx_step_flops(tokens=9216, ctx=256, dim=4096, heads=32, blocks=48, ff=4, cin=128):
@@ -620,11 +641,11 @@ def main() -> None:
         log("warm-up raised to 3 steps (timing rule)")
         args.warmup = 3
     if args.impl == "reference":
+        reserve_stdout()
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
         return
-    # NCCL's own messages (its version banner included) go to stderr: stdout carries one JSON line
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    reserve_stdout()
     world, rank, local = dist_setup()
     try:
         run_kino(args, world, rank, local)
