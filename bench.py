@@ -14,8 +14,9 @@ far more than the 126 MB L2, so no explicit L2 flush is needed between timed ste
 Python >= 3.15) cannot run on this box, so that arm times the CPU restatement of its formulas
 (oracle/) on all host cores, one double + one single block per step, extrapolated x8 / x24.
 With N > 1 (torchrun) the same step runs with Ulysses sequence parallelism: each rank holds
-1/N of the text and image tokens, q/k/v and the attention output cross an NCCL all-to-all around
-every attention (strong scaling); the step time is the max over ranks.
+1/N of the text and image tokens; the q/k/v projection epilogues store each head group straight
+into its owner GPU's buffer over NVLink and the attention stores its rows straight back (device
+barriers between; strong scaling); the step time is the max over ranks.
 """
 
 from __future__ import annotations
@@ -282,7 +283,10 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
     weights = flux_weights(v, seed=42, device=device)
     # N > 1: Ulysses sequence parallelism over all ranks (strong scaling: the same step, its
     # tokens sharded, one all-to-all each way around every attention)
-    model = Flux2Transformer(weights, v, device, sp=SequenceParallel() if world > 1 else None)
+    # N > 1: Ulysses over the peer transport (q/k/v and attention rows cross NVLink inside the
+    # projection and attention kernels)
+    model = Flux2Transformer(weights, v, device,
+                             sp=SequenceParallel(peer=True) if world > 1 else None)
     del weights
     torch.cuda.empty_cache()
     i0, i1 = model.sp.shard(ni)
@@ -402,6 +406,7 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
     }
 
     secondary = None
+    model.sp.close()
     if not args.no_secondary:
         model = prepared = current = None
         torch.cuda.empty_cache()
@@ -525,7 +530,7 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
         step = lambda: sampling.denoise_step(model, prepared, cur, sig, 0, guidance=4.0, cfg=True)
         mode = "batch 2 on one GPU"
     elif world % 2 == 0:
-        cfg = CfgSplit()
+        cfg = CfgSplit(peer=True)
         model = Flux2Transformer(weights, v, device, sp=cfg.sp)
         prepared = model.prepare(text if cfg.branch == 0 else negative, ids)
         i0, i1 = cfg.sp.shard(side * side)
@@ -540,12 +545,14 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
         out["config3_cfg"] = {"ms_per_step": round(ms, 3), "mode": mode,
                               "step_tflops": round(2 * step_flops() / (ms * 1e9), 1),
                               "frac_of_peak": round(2 * step_flops() / (ms * 1e9) / peak, 4)}
+    if step is not None:
+        model.sp.close()
     model = prepared = None
     torch.cuda.empty_cache()
 
     # config 4: LTX-2 video DiT step, 9216 video tokens + 256 text tokens, 48 blocks
     lv = lcfg.BASELINE_VIDEO
-    sp = SequenceParallel() if world > 1 else None
+    sp = SequenceParallel(peer=True) if world > 1 else None
     lmodel = LTXVideoTransformer(ltx_weights(lv, seed=0, device=device), lv, device, sp=sp)
     torch.cuda.empty_cache()
     f, h, w = 16, 18, 32
@@ -564,6 +571,7 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
                                 "mode": f"Ulysses x{world}" if world > 1 else "single GPU",
                                 "step_tflops": round(ltx_step_flops() / (ms * 1e9), 1),
                                 "frac_of_peak": round(ltx_step_flops() / (ms * 1e9) / peak, 4)}
+    lmodel.sp.close()
     lmodel = lprep = lat = None
     torch.cuda.empty_cache()
 

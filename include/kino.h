@@ -30,7 +30,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (3); bumped on any signature change. */
+/* ABI version of this header (4); bumped on any signature change. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -88,6 +88,22 @@ typedef struct kino_epilogue {
   int64_t rope_offset;
   int rope_batched;
   float norm_eps;
+  /* Optional sequence-parallel scatter (batch 1; no counterpart in the reference, which runs
+   * on one device): output columns [0, scatter_cols) are stored into other GPUs' receive
+   * buffers instead of `out`. Column c of segment s = c / seg_width goes to rank
+   * r = (c % seg_width) / part_width, row scatter_row0 + i, column
+   * seg_slot[s] * part_width + c % part_width of scatter_ptrs[r] (a device array of `world`
+   * pointers to bf16 buffers of scatter_rows rows, row stride scatter_ld). part_width is a
+   * multiple of 128; columns past scatter_cols go to `out` as usual. */
+  void* const* scatter_ptrs;
+  int64_t world;
+  int64_t scatter_cols;
+  int64_t seg_width;
+  int64_t part_width;
+  int64_t scatter_ld;
+  int64_t scatter_row0;
+  int64_t scatter_rows;
+  int seg_slot[4];
 } kino_epilogue;
 
 /* out[b, i, j] = epilogue(sum_k x[b, i, k] * w[j, k]) on tcgen05 tensor cores.
@@ -125,6 +141,19 @@ typedef struct kino_attention_args {
   const void* v[2];
   int64_t kv_tokens[2];
   int64_t ld_k[2], bs_k[2], ld_v[2], bs_v[2];
+  /* Optional sequence-parallel return (batch 1, one query segment; no counterpart in the
+   * reference): query row t belongs to rank t / rows_per_rank of `world`; its output row goes to
+   * out_peers[rank] + (t % rows_per_rank) * ld_out[0] + out_col_offset + head * 128 (buffers of
+   * rows_per_rank rows and out_cols columns), and with gate_peers its gate is read from
+   * gate_peers[rank] at row t % rows_per_rank (stride ld_gate[0]), column
+   * gate_head_offset + head. out_peers and gate_peers are device arrays of `world` pointers. */
+  void* const* out_peers;
+  const void* const* gate_peers;
+  int64_t world;
+  int64_t rows_per_rank;
+  int64_t out_col_offset;
+  int64_t out_cols;
+  int64_t gate_head_offset;
 } kino_attention_args;
 
 /* softmax(q k^T * scale) v over all key segments, per head, token-major operands.
@@ -174,6 +203,19 @@ kino_status kino_qk_norm_rope(void* x, int64_t ld, int64_t bs, int64_t batch, in
                               int64_t heads, const void* weight, int norm_kind, int rope_kind,
                               const float* cos_table, const float* sin_table, int table_batched,
                               int64_t table_tokens, int64_t table_offset, float eps, void* stream);
+
+/* kino_qk_norm_rope for batch 1 with the result stored into the sequence-parallel receive
+ * buffers instead of in place (no counterpart in the reference, which runs on one device): head
+ * h of token t goes to rank r = h / (heads / world), row dst_row0 + t, columns
+ * [dst_slot * (heads / world) * 128 + (h % (heads / world)) * 128, +128) of dst_ptrs[r] (a
+ * device array of `world` bf16 buffers of dst_rows rows, row stride dst_ld). */
+kino_status kino_qk_norm_rope_to_peers(const void* x, int64_t ld, int64_t tokens, int64_t heads,
+                                       const void* weight, int norm_kind, int rope_kind,
+                                       const float* cos_table, const float* sin_table,
+                                       int table_batched, int64_t table_tokens,
+                                       int64_t table_offset, float eps, void* const* dst_ptrs,
+                                       int64_t world, int64_t dst_ld, int64_t dst_row0,
+                                       int64_t dst_rows, int64_t dst_slot, void* stream);
 
 /* value (batch, tokens, heads*2*half) bf16, tables (table_batch, heads, tokens, half) fp32.
  * Replaces kinomlx.kernels.split_rope.rotate (kinomlx/kernels/split_rope.py:159-163) with the
@@ -304,6 +346,28 @@ kino_status kino_tile_blend(const void* decoded, int64_t frames, int64_t height,
 /* canvas[p, y, x] /= max(weights[y, x], 1e-8) (kinomlx/models/ltx2/video_vae/tiling.py:1369). */
 kino_status kino_blend_normalize(float* canvas, const float* weights, int64_t planes, int64_t hw,
                                  void* stream);
+
+/* ------------------------------------------------------------------ peer memory (NVLink)
+ * Buffers that the other GPUs of a sequence-parallel group map (CUDA IPC) and write into: the
+ * q/k/v receive buffers, the projection outputs the attention returns its rows to, and the
+ * barrier flags. No counterpart in the reference (one device). */
+typedef struct kino_ipc_handle {
+  unsigned char bytes[64];
+} kino_ipc_handle;
+
+/* cudaMalloc `bytes` (zero-filled) and export an IPC handle for it. */
+kino_status kino_peer_alloc(int64_t bytes, void** ptr, kino_ipc_handle* handle);
+kino_status kino_peer_free(void* ptr);
+/* Map another process's buffer (same node) into this process; close with kino_peer_close. */
+kino_status kino_peer_open(const kino_ipc_handle* handle, void** ptr);
+kino_status kino_peer_close(void* ptr);
+
+/* Arrival barrier number `epoch` (1, 2, ...) across `world` GPUs (world <= 32): flags is a
+ * device array of `world` pointers to each rank's `world` uint32 flags (zero-initialised). Rank
+ * `rank` publishes its earlier stores, marks its arrival in every rank's flags and waits (at most
+ * 2 s, then KINO_ETIMEOUT in kino_device_status) until every rank has arrived. */
+kino_status kino_peer_barrier(void* const* flags, int64_t rank, int64_t world, int64_t epoch,
+                              void* stream);
 
 #ifdef __cplusplus
 }

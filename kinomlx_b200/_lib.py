@@ -70,6 +70,15 @@ class Epilogue(ctypes.Structure):
         ("rope_offset", c_int64),
         ("rope_batched", c_int),
         ("norm_eps", c_float),
+        ("scatter_ptrs", c_void_p),
+        ("world", c_int64),
+        ("scatter_cols", c_int64),
+        ("seg_width", c_int64),
+        ("part_width", c_int64),
+        ("scatter_ld", c_int64),
+        ("scatter_row0", c_int64),
+        ("scatter_rows", c_int64),
+        ("seg_slot", c_int * 4),
     ]
 
 
@@ -98,6 +107,13 @@ class AttentionArgs(ctypes.Structure):
         ("bs_k", c_int64 * 2),
         ("ld_v", c_int64 * 2),
         ("bs_v", c_int64 * 2),
+        ("out_peers", c_void_p),
+        ("gate_peers", c_void_p),
+        ("world", c_int64),
+        ("rows_per_rank", c_int64),
+        ("out_col_offset", c_int64),
+        ("out_cols", c_int64),
+        ("gate_head_offset", c_int64),
     ]
 
 
@@ -118,6 +134,10 @@ class Conv3dArgs(ctypes.Structure):
         ("stride_h", c_int),
         ("stride_w", c_int),
     ]
+
+
+class IpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
 
 I64 = c_int64
@@ -143,6 +163,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         c_int,
         [P, I64, I64, I64, I64, I64, P, c_int, c_int, P, P, c_int, I64, I64, F, P],
     ),
+    "kino_qk_norm_rope_to_peers": (
+        c_int,
+        [P, I64, I64, I64, P, c_int, c_int, P, P, c_int, I64, I64, F, P, I64, I64, I64, I64, I64, P],
+    ),
     "kino_split_rope": (c_int, [P, P, P, P, I64, I64, I64, I64, c_int, P]),
     "kino_gelu_tanh": (c_int, [P, P, I64, P]),
     "kino_silu": (c_int, [P, P, I64, P]),
@@ -161,6 +185,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_latent_to_bfhwc": (c_int, [P, P, P, P, I64, I64, P]),
     "kino_tile_blend": (c_int, [P, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, P, P, P]),
     "kino_blend_normalize": (c_int, [P, P, I64, I64, P]),
+    "kino_peer_alloc": (c_int, [I64, POINTER(c_void_p), POINTER(IpcHandle)]),
+    "kino_peer_free": (c_int, [P]),
+    "kino_peer_open": (c_int, [POINTER(IpcHandle), POINTER(c_void_p)]),
+    "kino_peer_close": (c_int, [P]),
+    "kino_peer_barrier": (c_int, [P, I64, I64, I64, P]),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -56,6 +56,15 @@ struct AttnParams {
   const __nv_bfloat16* gate[2];  // optional (batch, tokens, heads) output gate per query segment
   int64_t ld_gate[2], bs_gate[2];
   float scale_log2;
+  // Sequence-parallel return (batch 1, one query segment): query row t belongs to rank
+  // t / rows_per_rank; its output goes to out_peers[rank] + (t % rows_per_rank) * ld_out[0] +
+  // out_col_offset + head * 128 and its gate is read from gate_peers[rank] (row stride
+  // ld_gate[0], column gate_head_offset + head). Null out_peers: plain `out`.
+  __nv_bfloat16* const* out_peers;
+  const __nv_bfloat16* const* gate_peers;
+  int rows_per_rank;
+  int64_t out_col_offset;
+  int gate_head_offset;
 };
 
 struct AttnSmem {
@@ -386,17 +395,31 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const float inv_l = 1.0f / l_run;
         // Optional head gate: bf16(bf16(O / l) * gate[t, head])
         const __nv_bfloat16* gp = p.gate[qt.seg];
-        const float gv =
-            (gp != nullptr && store)
-                ? __bfloat162float(gp[static_cast<int64_t>(batch) * p.bs_gate[qt.seg] +
-                                      static_cast<int64_t>(tok) * p.ld_gate[qt.seg] + head])
-                : 1.0f;
+        __nv_bfloat16* dst;
+        float gv = 1.0f;
+        if (p.out_peers != nullptr) {
+          // the row's owner GPU: its output buffer and its gate, over NVLink
+          const int owner = tok / p.rows_per_rank;
+          const int64_t lt = tok - static_cast<int64_t>(owner) * p.rows_per_rank;
+          dst = (store ? p.out_peers[owner] : p.out_peers[0]) + lt * p.ld_out[0] +
+                p.out_col_offset + head * ATT_D;
+          if (p.gate_peers != nullptr) {
+            gp = p.gate_peers[0];
+            if (store)
+              gv = __bfloat162float(
+                  p.gate_peers[owner][lt * p.ld_gate[0] + p.gate_head_offset + head]);
+          }
+        } else {
+          dst = p.out[qt.seg] + static_cast<int64_t>(batch) * p.bs_out[qt.seg] +
+                static_cast<int64_t>(tok) * p.ld_out[qt.seg] + head * ATT_D;
+          if (gp != nullptr && store)
+            gv = __bfloat162float(gp[static_cast<int64_t>(batch) * p.bs_gate[qt.seg] +
+                                     static_cast<int64_t>(tok) * p.ld_gate[qt.seg] + head]);
+        }
         auto fin = [&](uint32_t raw) -> float {
           const float o = __uint_as_float(raw) * inv_l;
           return gp != nullptr ? bf16_round(bf16_round(o) * gv) : o;
         };
-        __nv_bfloat16* dst = p.out[qt.seg] + static_cast<int64_t>(batch) * p.bs_out[qt.seg] +
-                             static_cast<int64_t>(tok) * p.ld_out[qt.seg] + head * ATT_D;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -414,6 +437,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             }
           }
         }
+        // rows returned to other GPUs: visible before the next kernel signals
+        if (p.out_peers != nullptr) __threadfence_system();
       }
     }
   }

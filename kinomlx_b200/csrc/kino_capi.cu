@@ -14,6 +14,7 @@
 #include "kino_gemm.cuh"
 #include "kino_conv3d.cuh"
 #include "kino_ops.cuh"
+#include "kino_peer.cuh"
 #include "kino_vae.cuh"
 
 // Scratch of kino_group_norm_noalloc: a fixed device array that every GPU loading this library
@@ -281,6 +282,35 @@ bool gemm_pairs_enabled() {
   return enabled == 1;
 }
 
+// Tile shape of a product: 1 = CTA pairs with 256 x 256 tiles, 2 = one SM with 128 x 256 tiles,
+// 3 = one SM with 128 x 128 tiles. The persistent kernels run ceil(tiles / slots) waves of
+// equal-length tiles, so the estimate is waves x tile time, the tile time relative to the
+// CTA-pair kernel's per-SM share (128 x 256) with the single-SM kernels' measured throughput
+// ratios (per mille).
+#ifndef KINO_GEMM_E1
+#define KINO_GEMM_E1 930
+#endif
+#ifndef KINO_GEMM_E1B
+#define KINO_GEMM_E1B 860
+#endif
+#ifndef KINO_GEMM_FORCE
+#define KINO_GEMM_FORCE 0
+#endif
+int gemm_tiling(int64_t batch, int64_t m, int64_t n) {
+  if (KINO_GEMM_FORCE != 0) return KINO_GEMM_FORCE;
+  if (n <= 128) return 3;
+  const int64_t sms = device_sms();
+  auto waves = [&](int64_t tiles, int64_t slots) { return (tiles + slots - 1) / slots; };
+  const int64_t t2 = batch * ((m + 255) / 256) * ((n + 255) / 256);
+  const int64_t t1 = batch * ((m + 127) / 128) * ((n + 255) / 256);
+  const int64_t t3 = batch * ((m + 127) / 128) * ((n + 127) / 128);
+  const double e2 = gemm_pairs_enabled() ? waves(t2, sms / 2) * 1000.0 : 1e30;
+  const double e1 = waves(t1, sms) * 1000.0 * 1000.0 / KINO_GEMM_E1;
+  const double e3 = waves(t3, sms) * 500.0 * 1000.0 / KINO_GEMM_E1B;
+  if (e2 <= e1 && e2 <= e3) return 1;
+  return e1 <= e3 ? 2 : 3;
+}
+
 int gn_parts(int64_t voxels) {
   int64_t p = (voxels + 31) / 32;
   return static_cast<int>(p < 592 ? (p < 1 ? 1 : p) : 592);
@@ -315,7 +345,7 @@ void* group_norm_scratch_address(kino_status* status) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 3; }
+int kino_abi_version(void) { return 4; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -410,6 +440,28 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
         return fail(KINO_EINVAL, "kino_linear: QK norm ranges must precede the SwiGLU columns");
     }
   }
+  if (epi != nullptr && epi->scatter_ptrs != nullptr) {
+    const int64_t pw = epi->part_width, sw = epi->seg_width, sc = epi->scatter_cols;
+    if (batch != 1) return fail(KINO_EINVAL, "kino_linear: scatter needs batch 1");
+    if (epi->world < 1 || epi->world > kino::PEER_MAX_WORLD)
+      return fail(KINO_EINVAL, "kino_linear: scatter world 1..%d", kino::PEER_MAX_WORLD);
+    if (pw <= 0 || pw % 128 || sw <= 0 || sw % pw || sw / pw != epi->world || sc <= 0 ||
+        sc % sw || sc / sw > 4 || sc > n || (swiglu && sc > epi->act_col_begin))
+      return fail(KINO_EINVAL, "kino_linear: scatter segments must split into world parts of "
+                               "128-column heads and precede the other columns");
+    if (epi->scatter_ld % 8 || epi->scatter_row0 < 0 || epi->scatter_row0 + m > epi->scatter_rows)
+      return fail(KINO_EINVAL, "kino_linear: scatter rows outside the receive buffers");
+    for (int64_t g = 0; g < sc / sw; ++g)
+      if (epi->seg_slot[g] < 0 || (epi->seg_slot[g] + 1) * pw > epi->scatter_ld)
+        return fail(KINO_EINVAL, "kino_linear: scatter slot outside the receive row");
+    e.scatter_ptrs = reinterpret_cast<__nv_bfloat16* const*>(epi->scatter_ptrs);
+    e.scatter_cols = static_cast<int>(sc);
+    e.seg_width = static_cast<int>(sw);
+    e.part_width = static_cast<int>(pw);
+    e.scatter_ld = epi->scatter_ld;
+    e.scatter_row0 = epi->scatter_row0;
+    for (int g = 0; g < 4; ++g) e.seg_slot[g] = epi->seg_slot[g];
+  }
   kino::GemmShape s;
   std::memset(&s, 0, sizeof(s));
   s.batch = static_cast<int>(batch);
@@ -419,12 +471,14 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
   s.ldo = ldo;
   s.bs_out = batch > 1 ? bso : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (n <= 128) return launch_gemm<128, 6>(x, w, out, s, ldx, bsx, ldw, e, st, 0);
-  // CTA pairs pay off once the 1-SM tiles would fill more than one wave of the GPU
-  // (measured: 512 x 9216 x 3072 runs faster on single CTAs, 4096 rows and up on pairs).
-  if (m >= 1024 && gemm_pairs_enabled())
-    return launch_gemm_2sm<KINO_GEMM_PAIR_STAGES>(x, w, out, s, ldx, bsx, ldw, e, st, 6);
-  return launch_gemm<256, 4>(x, w, out, s, ldx, bsx, ldw, e, st, 1);
+  switch (gemm_tiling(batch, m, n)) {
+    case 1:
+      return launch_gemm_2sm<KINO_GEMM_PAIR_STAGES>(x, w, out, s, ldx, bsx, ldw, e, st, 6);
+    case 2:
+      return launch_gemm<256, 4>(x, w, out, s, ldx, bsx, ldw, e, st, 1);
+    default:
+      return launch_gemm<128, 6>(x, w, out, s, ldx, bsx, ldw, e, st, 0);
+  }
 }
 
 kino_status kino_gemv(const void* x, int64_t ldx, const void* w, const void* bias, void* y,
@@ -511,6 +565,25 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
       p.kv_tokens[s] = static_cast<int>(a->kv_tokens[s]);
       p.kv_blocks[s] = (p.kv_tokens[s] + kino::ATT_BN - 1) / kino::ATT_BN;
     }
+  }
+  if (a->out_peers != nullptr) {
+    if (a->batch != 1 || a->n_q != 1)
+      return fail(KINO_EINVAL, "kino_attention: peer return needs batch 1, one query segment");
+    if (a->world < 1 || a->world > kino::PEER_MAX_WORLD || a->rows_per_rank < 1 ||
+        a->rows_per_rank * a->world < a->q_tokens[0] || a->out_col_offset < 0 ||
+        a->out_col_offset % 8 || a->out_col_offset + a->heads * 128 > a->out_cols ||
+        a->out_cols > a->ld_out[0])
+      return fail(KINO_EINVAL, "kino_attention: peer return rows/columns outside the buffers");
+    if (a->gate_peers != nullptr &&
+        (a->gate_head_offset < 0 || a->gate_head_offset + a->heads > a->ld_gate[0]))
+      return fail(KINO_EINVAL, "kino_attention: peer gate columns outside the gate rows");
+    p.out_peers = reinterpret_cast<__nv_bfloat16* const*>(a->out_peers);
+    p.gate_peers = reinterpret_cast<const __nv_bfloat16* const*>(a->gate_peers);
+    p.rows_per_rank = static_cast<int>(a->rows_per_rank);
+    p.out_col_offset = a->out_col_offset;
+    p.gate_head_offset = static_cast<int>(a->gate_head_offset);
+    p.ld_out[0] = a->ld_out[0];
+    p.ld_gate[0] = a->ld_gate[0];
   }
   kino_status st = ensure_smem(kino::attention_tc_kernel, kino::AttnSmem::TOTAL, 3);
   if (st != KINO_OK) return st;
@@ -617,8 +690,41 @@ kino_status kino_qk_norm_rope(void* x, int64_t ld, int64_t bs, int64_t batch, in
   launch_pdl(kino::qk_norm_rope_kernel, dim3(grid), dim3(static_cast<unsigned>(heads * 8)), 0, static_cast<cudaStream_t>(stream),
       static_cast<__nv_bfloat16*>(x), ld, bs, static_cast<int>(heads),
       static_cast<const __nv_bfloat16*>(weight), norm_kind, rope_kind, cos_table, sin_table,
-      table_batched, static_cast<int>(table_tokens), static_cast<int>(table_offset), eps);
+      table_batched, static_cast<int>(table_tokens), static_cast<int>(table_offset), eps,
+      static_cast<__nv_bfloat16* const*>(nullptr), 0, int64_t{0}, int64_t{0}, 0);
   return check_launch("kino_qk_norm_rope");
+}
+
+kino_status kino_qk_norm_rope_to_peers(const void* x, int64_t ld, int64_t tokens, int64_t heads,
+                                       const void* weight, int norm_kind, int rope_kind,
+                                       const float* cos_table, const float* sin_table,
+                                       int table_batched, int64_t table_tokens,
+                                       int64_t table_offset, float eps, void* const* dst_ptrs,
+                                       int64_t world, int64_t dst_ld, int64_t dst_row0,
+                                       int64_t dst_rows, int64_t dst_slot, void* stream) {
+  if (x == nullptr || dst_ptrs == nullptr) return fail(KINO_EINVAL, "kino_qk_norm_rope_to_peers: null");
+  if (norm_kind < 0 || norm_kind > 2 || rope_kind < 0 || rope_kind > 2)
+    return fail(KINO_EINVAL, "kino_qk_norm_rope_to_peers: bad kind");
+  if (norm_kind != 0 && (weight == nullptr || !aligned16(weight)))
+    return fail(KINO_EINVAL, "kino_qk_norm_rope_to_peers: norm needs an aligned weight");
+  if (rope_kind != 0 && (cos_table == nullptr || sin_table == nullptr))
+    return fail(KINO_EINVAL, "kino_qk_norm_rope_to_peers: rope needs tables");
+  if (heads < 1 || heads > 128 || ld % 8 || !aligned16(x))
+    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_to_peers: heads <= 128, aligned rows");
+  if (tokens < 1) return fail(KINO_EINVAL, "kino_qk_norm_rope_to_peers: empty");
+  if (rope_kind != 0 && table_offset + tokens > table_tokens)
+    return fail(KINO_EINVAL, "kino_qk_norm_rope_to_peers: table too short");
+  if (world < 1 || world > kino::PEER_MAX_WORLD || heads % world || dst_ld % 8 || dst_row0 < 0 ||
+      dst_row0 + tokens > dst_rows || dst_slot < 0 || (dst_slot + 1) * (heads / world) * 128 > dst_ld)
+    return fail(KINO_EINVAL, "kino_qk_norm_rope_to_peers: destination outside the receive buffers");
+  launch_pdl(kino::qk_norm_rope_kernel, dim3(static_cast<unsigned>(tokens), 1),
+             dim3(static_cast<unsigned>(heads * 8)), 0, static_cast<cudaStream_t>(stream),
+             const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(x)), ld, int64_t{0},
+             static_cast<int>(heads), static_cast<const __nv_bfloat16*>(weight), norm_kind,
+             rope_kind, cos_table, sin_table, table_batched, static_cast<int>(table_tokens),
+             static_cast<int>(table_offset), eps, reinterpret_cast<__nv_bfloat16* const*>(dst_ptrs),
+             static_cast<int>(heads / world), dst_ld, dst_row0, static_cast<int>(dst_slot));
+  return check_launch("kino_qk_norm_rope_to_peers");
 }
 
 kino_status kino_split_rope(const void* x, const float* cos_table, const float* sin_table,
@@ -892,6 +998,60 @@ kino_status kino_blend_normalize(float* canvas, const float* weights, int64_t pl
   if (blocks > 148 * 32) blocks = 148 * 32;
   launch_pdl(kino::blend_normalize_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream), canvas, weights, planes, hw);
   return check_launch("kino_blend_normalize");
+}
+
+// ---------------------------------------------------------------- peer memory
+kino_status kino_peer_alloc(int64_t bytes, void** ptr, kino_ipc_handle* handle) {
+  if (ptr == nullptr || handle == nullptr || bytes < 1)
+    return fail(KINO_EINVAL, "kino_peer_alloc: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return fail(KINO_ECUDA, "kino_peer_alloc: %s", cudaGetErrorString(e));
+  e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(KINO_ECUDA, "kino_peer_alloc: %s", cudaGetErrorString(e));
+  }
+  static_assert(sizeof(h) == sizeof(handle->bytes), "IPC handle size");
+  std::memcpy(handle->bytes, &h, sizeof(h));
+  *ptr = p;
+  return KINO_OK;
+}
+
+kino_status kino_peer_free(void* ptr) {
+  if (ptr == nullptr) return fail(KINO_EINVAL, "kino_peer_free: null");
+  const cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return fail(KINO_ECUDA, "kino_peer_free: %s", cudaGetErrorString(e));
+  return KINO_OK;
+}
+
+kino_status kino_peer_open(const kino_ipc_handle* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return fail(KINO_EINVAL, "kino_peer_open: null");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(KINO_ECUDA, "kino_peer_open: %s", cudaGetErrorString(e));
+  return KINO_OK;
+}
+
+kino_status kino_peer_close(void* ptr) {
+  if (ptr == nullptr) return fail(KINO_EINVAL, "kino_peer_close: null");
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return fail(KINO_ECUDA, "kino_peer_close: %s", cudaGetErrorString(e));
+  return KINO_OK;
+}
+
+kino_status kino_peer_barrier(void* const* flags, int64_t rank, int64_t world, int64_t epoch,
+                              void* stream) {
+  if (flags == nullptr) return fail(KINO_EINVAL, "kino_peer_barrier: null flags");
+  if (world < 1 || world > kino::PEER_MAX_WORLD || rank < 0 || rank >= world || epoch < 1)
+    return fail(KINO_EINVAL, "kino_peer_barrier: rank/world/epoch");
+  launch_pdl(kino::peer_barrier_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+             reinterpret_cast<uint32_t* const*>(flags), static_cast<int>(rank),
+             static_cast<int>(world), static_cast<uint32_t>(epoch));
+  return check_launch("kino_peer_barrier");
 }
 
 }  // extern "C"

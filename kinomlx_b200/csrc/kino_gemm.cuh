@@ -53,7 +53,32 @@ struct GemmEpi {
   int64_t rope_rows, rope_offset;
   int rope_batched;
   float norm_eps;
+  // Sequence-parallel scatter (batch 1): output columns [0, scatter_cols) are stored straight
+  // into the receive buffers of the GPUs that own their heads. Column c of segment
+  // s = c / seg_width (q, k or v) goes to rank r = (c % seg_width) / part_width, row
+  // scatter_row0 + row, column seg_slot[s] * part_width + c % part_width of scatter_ptrs[r]
+  // (row stride scatter_ld). Null scatter_ptrs: every column to `out`.
+  __nv_bfloat16* const* scatter_ptrs;
+  int scatter_cols, seg_width, part_width;
+  int64_t scatter_ld, scatter_row0;
+  int seg_slot[4];
 };
+
+// Where the 32- or 128-column chunk of output row `row` starting at col0 is stored: this GPU's
+// output, or another GPU's receive buffer for scattered columns (a chunk never straddles a part:
+// part widths are multiples of 128).
+__device__ __forceinline__ __nv_bfloat16* gemm_dst(const GemmEpi& e, __nv_bfloat16* out,
+                                                   int64_t out_off, int row, int col0) {
+  if (e.scatter_ptrs != nullptr && col0 < e.scatter_cols) {
+    const int seg = col0 / e.seg_width;
+    const int within = col0 - seg * e.seg_width;
+    const int r = within / e.part_width;
+    const int c = within - r * e.part_width;
+    return e.scatter_ptrs[r] + (e.scatter_row0 + row) * e.scatter_ld +
+           static_cast<int64_t>(e.seg_slot[seg]) * e.part_width + c;
+  }
+  return out + out_off + col0;
+}
 
 struct GemmShape {
   int batch, m, n, k;
@@ -210,7 +235,7 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
       }
     }
   }
-  __nv_bfloat16* dst = out + out_off + col0;
+  __nv_bfloat16* dst = gemm_dst(e, out, out_off, row, col0);
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     if (col0 + g * 8 < s.n) {
@@ -283,8 +308,8 @@ __device__ __forceinline__ void gemm_epilogue_head(const GemmShape& s, const Gem
   const int64_t trow = (e.rope_batched ? static_cast<int64_t>(b) * e.rope_rows : 0) +
                        e.rope_offset + row;
   const int64_t tstride = e.rope_rows * (e.rope_batched ? s.batch : 1);
-  __nv_bfloat16* dst = out + static_cast<int64_t>(b) * s.bs_out + static_cast<int64_t>(row) * s.ldo +
-                       col0;
+  __nv_bfloat16* dst = gemm_dst(e, out, static_cast<int64_t>(b) * s.bs_out +
+                                          static_cast<int64_t>(row) * s.ldo, row, col0);
 #pragma unroll 1
   for (int c = 0; c < 4; ++c) {
     float v[32];
@@ -483,6 +508,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    // scattered rows went to other GPUs: make them visible before the next kernel signals
+    if (e.scatter_ptrs != nullptr) __threadfence_system();
   }
 
   tc_fence_before();
@@ -660,6 +687,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
     }
+    // scattered rows went to other GPUs: make them visible before the next kernel signals
+    if (e.scatter_ptrs != nullptr) __threadfence_system();
   }
 
   tc_fence_before();

@@ -274,7 +274,10 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, i
                                     int heads, const __nv_bfloat16* __restrict__ w, int norm_kind,
                                     int rope_kind, const float* __restrict__ cos_t,
                                     const float* __restrict__ sin_t, int table_batched,
-                                    int table_tokens, int table_offset, float eps) {
+                                    int table_tokens, int table_offset, float eps,
+                                    __nv_bfloat16* const* __restrict__ dst_ptrs = nullptr,
+                                    int heads_per_rank = 0, int64_t dst_ld = 0,
+                                    int64_t dst_row0 = 0, int dst_slot = 0) {
   griddep_wait();
   griddep_launch();
   __shared__ float red[32];
@@ -364,8 +367,19 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, i
       c[j] = __fadd_rn(first_s, second_c);
     }
   }
-  store8(row + e0, a);
-  store8(row + e1, c);
+  if (dst_ptrs == nullptr) {
+    store8(row + e0, a);
+    store8(row + e1, c);
+  } else {
+    // sequence parallel: head h goes to the receive buffer of the rank that owns it
+    const int owner = h / heads_per_rank;
+    __nv_bfloat16* dst = dst_ptrs[owner] + (dst_row0 + t) * dst_ld +
+                         static_cast<int64_t>(dst_slot) * heads_per_rank * 128 +
+                         (h - owner * heads_per_rank) * 128 - h * 128;
+    store8(dst + e0, a);
+    store8(dst + e1, c);
+    __threadfence_system();
+  }
 }
 
 // Standalone split-half RoPE with the reference kernel's contract: value (B, T, H*2*half) in

@@ -48,15 +48,23 @@ class PreparedText:
 
 
 class _Workspace:
-    def __init__(self, v: FluxVariant, batch: int, nt: int, ni: int, device: torch.device):
+    def __init__(self, v: FluxVariant, batch: int, nt: int, ni: int, device: torch.device,
+                 sp: SequenceParallel):
         n, d = nt + ni, v.dim
         e = lambda *shape: torch.empty(shape, device=device, dtype=torch.bfloat16)
         self.batch, self.nt, self.ni = batch, nt, ni
         self.stream = e(batch, n, d)
         self.nrm = e(batch, n, d)
-        self.qkv = e(batch, n, 3 * d)
         self.hid = e(batch, n, v.mlp_hidden)
-        self.big = e(batch, n, 3 * d + v.mlp_hidden)
+        # the projections the attention returns its rows to are shared with the other GPUs
+        # under the peer transport (their addresses in qkv_ptrs / big_ptrs)
+        self.peer = sp.peer is not None and batch == 1
+        if self.peer:
+            self.qkv, self.qkv_ptrs = sp.shared((batch, n, 3 * d))
+            self.big, self.big_ptrs = sp.shared((batch, n, 3 * d + v.mlp_hidden))
+        else:
+            self.qkv = e(batch, n, 3 * d)
+            self.big = e(batch, n, 3 * d + v.mlp_hidden)
         self.t = torch.empty((batch,), device=device, dtype=torch.float32)
         self.temb = e(batch, 256)
         self.emb1 = e(batch, d)
@@ -146,7 +154,7 @@ class Flux2Transformer:
     def workspace(self, batch: int, nt: int, ni: int) -> _Workspace:
         key = (batch, nt, ni)
         if key not in self._ws:
-            self._ws[key] = _Workspace(self.v, batch, nt, ni, self.device)
+            self._ws[key] = _Workspace(self.v, batch, nt, ni, self.device, self.sp)
         return self._ws[key]
 
     # ------------------------------------------------------------------ blocks
@@ -157,14 +165,21 @@ class Flux2Transformer:
         m = lambda base, j: ws.mods[:, (base + j) * d : (base + j + 1) * d]  # img base 0, txt 6
         ops.adaln(img, m(0, 0), m(0, 1), img_n, norm=ops.NORM_LAYER)
         ops.adaln(txt, m(6, 0), m(6, 1), txt_n, norm=ops.NORM_LAYER)
-        # q/k RMSNorm + RoPE run in the projection's epilogue (image rows read table rows from nt)
+        # q/k RMSNorm + RoPE run in the projection's epilogue (image rows read table rows from nt);
+        # under the peer transport the same epilogue stores q/k/v into the head owners' buffers
+        recv = self.sp.receive(nt + ws.ni, d) if ws.peer else None
         ops.linear(img_n, p["img_qkv"], ws.qkv[:, nt:], qk_norm=[(0, p["norm_q"]), (d, p["norm_k"])],
-                   norm_width=d, rope=(rope, nt))
+                   norm_width=d, rope=(rope, nt),
+                   scatter=self.sp.scatter(recv, d, (0, 1, 2), nt) if recv else None)
         ops.linear(txt_n, p["txt_qkv"], ws.qkv[:, :nt],
                    qk_norm=[(0, p["norm_added_q"]), (d, p["norm_added_k"])], norm_width=d,
-                   rope=(rope, 0))
+                   rope=(rope, 0), scatter=self.sp.scatter(recv, d, (0, 1, 2), 0) if recv else None)
         q, k, v = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
-        self.sp.attention(q, k, v, q, heads=h)
+        if recv:
+            self.sp.attention_from_peers(recv, heads=h, out_ptrs=ws.qkv_ptrs, out_ld=3 * d,
+                                         out_cols=3 * d, out_col=0)
+        else:
+            self.sp.attention(q, k, v, q, heads=h)
         ops.linear(q[:, nt:], p["to_out"], img, kind=ops.EPI_GATED_RESIDUAL, residual=img,
                    gate=m(0, 2))
         ops.linear(q[:, :nt], p["to_add_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
@@ -183,11 +198,17 @@ class Flux2Transformer:
         sm = lambda j: ws.mods[:, (12 + j) * d : (13 + j) * d]
         ops.adaln(ws.stream, sm(0), sm(1), ws.nrm, norm=ops.NORM_LAYER)
         # [k | v | q | mlp]: k and q normalised and rotated, the MLP activated, in one epilogue
+        recv = self.sp.receive(ws.nt + ws.ni, d) if ws.peer else None
         ops.linear(ws.nrm, p["fused"], ws.big, kind=self.act_kind, act_col_begin=3 * d,
                    qk_norm=[(0, p["norm_k"]), (2 * d, p["norm_q"])], norm_width=d,
-                   rope=(rope, 0))
+                   rope=(rope, 0), scatter=self.sp.scatter(recv, d, (1, 2, 0), 0) if recv else None)
         k, v, q = ws.big[..., :d], ws.big[..., d : 2 * d], ws.big[..., 2 * d : 3 * d]
-        self.sp.attention(q, k, v, q, heads=h)
+        if recv:
+            self.sp.attention_from_peers(recv, heads=h, out_ptrs=ws.big_ptrs,
+                                         out_ld=ws.big.shape[-1], out_cols=ws.big.shape[-1],
+                                         out_col=2 * d)
+        else:
+            self.sp.attention(q, k, v, q, heads=h)
         ops.linear(ws.big[..., 2 * d :], p["to_out"], ws.stream, kind=ops.EPI_GATED_RESIDUAL,
                    residual=ws.stream, gate=sm(2))
 

@@ -56,14 +56,22 @@ class PreparedContext:
 
 
 class _Workspace:
-    def __init__(self, v: LTXVariant, batch: int, tokens: int, ctx_tokens: int, device):
+    def __init__(self, v: LTXVariant, batch: int, tokens: int, ctx_tokens: int, device,
+                 sp: SequenceParallel):
         d = v.dim
         e = lambda *s: torch.empty(s, device=device, dtype=torch.bfloat16)
         self.x = e(batch, tokens, d)
         self.nrm = e(batch, tokens, d)
-        self.qkv = e(batch, tokens, 3 * d)
         self.hid = e(batch, tokens, v.ff_mult * d)
-        self.gates = e(batch, tokens, v.heads)
+        # [v | q | k] projection and the head gates: the self-attention returns its rows into the
+        # owners' q columns and reads their gates, so under the peer transport both are shared
+        self.peer = sp.peer is not None and batch == 1
+        if self.peer:
+            self.qkv, self.qkv_ptrs = sp.shared((batch, tokens, 3 * d))
+            self.gates, self.gate_ptrs = sp.shared((batch, tokens, v.heads))
+        else:
+            self.qkv = e(batch, tokens, 3 * d)
+            self.gates = e(batch, tokens, v.heads)
         self.ctxm = e(batch, ctx_tokens, d)
         self.ctxkv = e(batch, ctx_tokens, 2 * d)
         self.t = torch.empty((batch,), device=device, dtype=torch.float32)
@@ -115,8 +123,9 @@ class LTXVideoTransformer:
             tables.append(g("scale_shift_table").reshape(-1))
             prompts.append(g("prompt_scale_shift_table").reshape(-1))
             self.blocks.append({
-                "qkv_w": dev(torch.cat([g("attn1.to_q.weight"), g("attn1.to_k.weight"), g("attn1.to_v.weight")])),
-                "qkv_b": dev(torch.cat([g("attn1.to_q.bias"), g("attn1.to_k.bias"), g("attn1.to_v.bias")])),
+                # [v | q | k]: v first, so the sequence-parallel projection scatters it directly
+                "qkv_w": dev(torch.cat([g("attn1.to_v.weight"), g("attn1.to_q.weight"), g("attn1.to_k.weight")])),
+                "qkv_b": dev(torch.cat([g("attn1.to_v.bias"), g("attn1.to_q.bias"), g("attn1.to_k.bias")])),
                 "g1_w": dev(g("attn1.to_gate_logits.weight")),
                 "g1_b": dev(g("attn1.to_gate_logits.bias")),
                 "o1_w": dev(g("attn1.to_out.weight")),
@@ -155,7 +164,7 @@ class LTXVideoTransformer:
     def workspace(self, batch: int, tokens: int, ctx_tokens: int) -> _Workspace:
         key = (batch, tokens, ctx_tokens)
         if key not in self._ws:
-            self._ws[key] = _Workspace(self.v, batch, tokens, ctx_tokens, self.device)
+            self._ws[key] = _Workspace(self.v, batch, tokens, ctx_tokens, self.device, self.sp)
         return self._ws[key]
 
     # ------------------------------------------------------------------ per step embeddings
@@ -179,16 +188,30 @@ class LTXVideoTransformer:
         v, d, h = self.v, self.v.dim, self.v.heads
         val = lambda j: ws.vals[:, i, j * d : (j + 1) * d]
         x, nrm = ws.x, ws.nrm
-        q, k, vv = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
+        vv, q, k = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
         # self-attention
         ops.adaln(x, val(0), val(1), nrm, norm=ops.NORM_RMS, eps=v.eps)
         ops.linear(nrm, p["g1_w"], ws.gates, bias=p["g1_b"], kind=ops.EPI_SIGMOID2)
-        ops.linear(nrm, p["qkv_w"], ws.qkv, bias=p["qkv_b"])
-        ops.qk_norm_rope(q, heads=h, weight=p["qn1"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_SPLIT,
-                         cos=prepared.cos, sin=prepared.sin, eps=v.eps)
-        ops.qk_norm_rope(k, heads=h, weight=p["kn1"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_SPLIT,
-                         cos=prepared.cos, sin=prepared.sin, eps=v.eps)
-        self.sp.attention(q, k, vv, q, heads=h, gate=ws.gates)
+        if ws.peer:
+            # v straight from the projection epilogue, q and k after their full-row norm and
+            # RoPE, into the head owners' receive buffers; rows come back into q
+            recv = self.sp.receive(x.shape[1], d)
+            ops.linear(nrm, p["qkv_w"], ws.qkv, bias=p["qkv_b"],
+                       scatter=self.sp.scatter(recv, d, (2,), 0))
+            for t, wn, slot in ((q, p["qn1"], 0), (k, p["kn1"], 1)):
+                ops.qk_norm_rope(t, heads=h, weight=wn, norm=ops.QKNORM_FULL_ROW,
+                                 rope=ops.ROPE_SPLIT, cos=prepared.cos, sin=prepared.sin, eps=v.eps,
+                                 scatter=self.sp.scatter(recv, d, (slot,), 0))
+            self.sp.attention_from_peers(recv, heads=h, out_ptrs=ws.qkv_ptrs, out_ld=3 * d,
+                                         out_cols=3 * d, out_col=d,
+                                         gate=(ws.gate_ptrs, ws.gates.shape[-1]))
+        else:
+            ops.linear(nrm, p["qkv_w"], ws.qkv, bias=p["qkv_b"])
+            ops.qk_norm_rope(q, heads=h, weight=p["qn1"], norm=ops.QKNORM_FULL_ROW,
+                             rope=ops.ROPE_SPLIT, cos=prepared.cos, sin=prepared.sin, eps=v.eps)
+            ops.qk_norm_rope(k, heads=h, weight=p["kn1"], norm=ops.QKNORM_FULL_ROW,
+                             rope=ops.ROPE_SPLIT, cos=prepared.cos, sin=prepared.sin, eps=v.eps)
+            self.sp.attention(q, k, vv, q, heads=h, gate=ws.gates)
         ops.linear(q, p["o1_w"], x, bias=p["o1_b"], kind=ops.EPI_GATED_RESIDUAL, residual=x,
                    gate=val(2))
         # text cross-attention with the prompt-modulated context

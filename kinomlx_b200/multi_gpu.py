@@ -23,7 +23,8 @@ from .sequence_parallel import SequenceParallel
 class CfgSplit:
     """Process groups of the CFG split; every rank must construct it (same order of new_group)."""
 
-    def __init__(self):
+    def __init__(self, *, peer: bool = False):
+        """peer: Ulysses inside each branch over the peer transport instead of NCCL."""
         if not dist.is_initialized():
             raise RuntimeError("the CFG split needs an initialised process group")
         world, rank = dist.get_world_size(), dist.get_rank()
@@ -33,7 +34,7 @@ class CfgSplit:
         branch_groups = [dist.new_group(list(range(half))), dist.new_group(list(range(half, world)))]
         pair_groups = [dist.new_group([i, i + half]) for i in range(half)]
         self.branch = 0 if rank < half else 1  # 0: conditional, 1: unconditional
-        self.sp = SequenceParallel(branch_groups[self.branch])
+        self.sp = SequenceParallel(branch_groups[self.branch], peer=peer)
         self.pair = pair_groups[rank % half]
 
     def combine(self, velocity: torch.Tensor, guidance: float) -> torch.Tensor:

@@ -164,6 +164,34 @@ class RopeTables:
         self.sin_t = s3.to(torch.float32).permute(2, 0, 1).reshape(128, -1).contiguous()
 
 
+class Scatter:
+    """Sequence-parallel scatter of a projection's first `segments * seg_width` output columns
+    into the receive buffers of the GPUs that own their heads (see kino_epilogue in kino.h).
+
+    ptrs: int64 device tensor of `world` receive-buffer addresses (bf16, `rows` rows of `ld`);
+    segment s (q, k or v, in the projection's column order) lands in slot `slots[s]` of a
+    receive row; output row i goes to receive row `row0 + i`."""
+
+    def __init__(self, ptrs: torch.Tensor, world: int, seg_width: int, segments: int, ld: int,
+                 rows: int, row0: int, slots: tuple[int, ...]):
+        self.ptrs, self.world, self.seg_width, self.segments = ptrs, world, seg_width, segments
+        self.ld, self.rows, self.row0, self.slots = ld, rows, row0, tuple(slots)
+
+
+class PeerReturn:
+    """Where a sequence-parallel attention sends its rows back (see kino_attention_args): query
+    row t goes to rank t // rows_per_rank, row t % rows_per_rank of out_ptrs[rank] (row stride
+    ld, `cols` columns), at column col_offset + head * 128; with gate_ptrs, its gate is read from
+    the owner's gate rows (stride ld_gate) at column gate_head_offset + head."""
+
+    def __init__(self, out_ptrs: torch.Tensor, world: int, rows_per_rank: int, ld: int,
+                 cols: int, col_offset: int, gate_ptrs: torch.Tensor | None = None,
+                 ld_gate: int = 0, gate_head_offset: int = 0):
+        self.out_ptrs, self.world, self.rows_per_rank = out_ptrs, world, rows_per_rank
+        self.ld, self.cols, self.col_offset = ld, cols, col_offset
+        self.gate_ptrs, self.ld_gate, self.gate_head_offset = gate_ptrs, ld_gate, gate_head_offset
+
+
 def linear(
     x: torch.Tensor,
     w: torch.Tensor,
@@ -182,6 +210,7 @@ def linear(
     norm_width: int = 0,
     rope: tuple[RopeTables, int] | None = None,
     eps: float = 1e-6,
+    scatter: Scatter | None = None,
 ) -> torch.Tensor:
     """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight.
 
@@ -252,6 +281,17 @@ def linear(
         epi.rope_offset = offset
         epi.rope_batched = int(tables.batched)
         epi.norm_eps = eps
+    if scatter is not None:
+        epi.scatter_ptrs = scatter.ptrs.data_ptr()
+        epi.world = scatter.world
+        epi.scatter_cols = scatter.segments * scatter.seg_width
+        epi.seg_width = scatter.seg_width
+        epi.part_width = scatter.seg_width // scatter.world
+        epi.scatter_ld = scatter.ld
+        epi.scatter_row0 = scatter.row0
+        epi.scatter_rows = scatter.rows
+        for i, slot in enumerate(scatter.slots):
+            epi.seg_slot[i] = slot
     with _timed("gemm", 2.0 * batch * m * n * k, 2.0 * (batch * m * k + n * k + batch * m * n)):
         _lib.call(
             "kino_linear",
@@ -327,9 +367,11 @@ def attention(
     heads: int,
     scale: float | None = None,
     gate: list[torch.Tensor | None] | None = None,
+    peer_return: PeerReturn | None = None,
 ) -> list[torch.Tensor]:
     """Attention over logically concatenated segments; each tensor (batch, tokens, heads*128).
-    `gate[s]` (batch, tokens, heads), if given, multiplies segment s's output per head."""
+    `gate[s]` (batch, tokens, heads), if given, multiplies segment s's output per head. With
+    `peer_return`, output rows go to their owner GPUs instead of `out`."""
     if not 1 <= len(q) <= 2 or len(out) != len(q) or not 1 <= len(k) <= 2 or len(v) != len(k):
         raise ValueError("attention takes 1 or 2 query and key/value segments")
     args = _lib.AttentionArgs()
@@ -373,6 +415,18 @@ def attention(
         args.bs_k[s] = k3.stride(0)
         args.ld_v[s] = v3.stride(1)
         args.bs_v[s] = v3.stride(0)
+    if peer_return is not None:
+        r = peer_return
+        args.out_peers = r.out_ptrs.data_ptr()
+        args.world = r.world
+        args.rows_per_rank = r.rows_per_rank
+        args.out_col_offset = r.col_offset
+        args.out_cols = r.cols
+        args.ld_out[0] = r.ld
+        if r.gate_ptrs is not None:
+            args.gate_peers = r.gate_ptrs.data_ptr()
+            args.ld_gate[0] = r.ld_gate
+            args.gate_head_offset = r.gate_head_offset
     nq = sum(int(args.q_tokens[i]) for i in range(args.n_q))
     nk = sum(int(args.kv_tokens[i]) for i in range(args.n_kv))
     flops = 4.0 * args.batch * heads * nq * nk * args.head_dim
@@ -480,8 +534,11 @@ def qk_norm_rope(
     sin: torch.Tensor | None = None,
     table_offset: int = 0,
     eps: float = 1e-6,
+    scatter: Scatter | None = None,
 ) -> torch.Tensor:
-    """In place: RMSNorm (per head or full row) then RoPE on x (batch, tokens, heads*128)."""
+    """In place: RMSNorm (per head or full row) then RoPE on x (batch, tokens, heads*128).
+    With `scatter` (batch 1, one segment), the result goes to the head owners' receive buffers
+    (slot scatter.slots[0]) instead."""
     _need(x, "x")
     x3 = _as3d(x)
     batch, tokens, width = x3.shape
@@ -498,6 +555,15 @@ def qk_norm_rope(
             raise ValueError("RoPE tables must be contiguous")
         table_tokens = cos.shape[-2]
         table_batched = int(cos.shape[0] > 1 and cos.dim() >= 3)
+    if scatter is not None:
+        if batch != 1:
+            raise ValueError("the scattered form takes batch 1")
+        with _timed("qk_norm_rope", 0.0, 4.0 * tokens * width + 2 * 4.0 * tokens * 128):
+            _lib.call("kino_qk_norm_rope_to_peers", _ptr(x3), x3.stride(1), tokens, heads,
+                      _ptr(weight), norm, rope, _ptr(cos), _ptr(sin), table_batched, table_tokens,
+                      table_offset, eps, _ptr(scatter.ptrs), scatter.world, scatter.ld,
+                      scatter.row0, scatter.rows, scatter.slots[0], _stream())
+        return x
     with _timed("qk_norm_rope", 0.0, 4.0 * batch * tokens * width + 2 * 4.0 * tokens * 128):
         _lib.call(
             "kino_qk_norm_rope",
@@ -755,3 +821,35 @@ def heads_unpack(src: torch.Tensor, out: torch.Tensor, gate: torch.Tensor | None
         _lib.call("kino_heads_unpack", _ptr(src), _ptr(out), out.stride(-2), tokens, width, parts,
                   _ptr(gate), gate.stride(-2) if gate is not None else 0, _stream())
     return out
+
+
+# ----------------------------------------------------------------------------- peer memory
+def peer_alloc(nbytes: int) -> tuple[int, bytes]:
+    """cudaMalloc'd, zero-filled bytes on the current device and their IPC handle."""
+    ptr = ctypes.c_void_p()
+    handle = _lib.IpcHandle()
+    _lib.call("kino_peer_alloc", nbytes, ctypes.byref(ptr), ctypes.byref(handle))
+    return int(ptr.value), bytes(handle.bytes)
+
+
+def peer_free(ptr: int) -> None:
+    _lib.call("kino_peer_free", ctypes.c_void_p(ptr))
+
+
+def peer_open(handle: bytes) -> int:
+    """Map another process's peer_alloc buffer (same node) into this process."""
+    h = _lib.IpcHandle()
+    ctypes.memmove(h.bytes, handle, 64)
+    ptr = ctypes.c_void_p()
+    _lib.call("kino_peer_open", ctypes.byref(h), ctypes.byref(ptr))
+    return int(ptr.value)
+
+
+def peer_close(ptr: int) -> None:
+    _lib.call("kino_peer_close", ctypes.c_void_p(ptr))
+
+
+def peer_barrier(flag_ptrs: torch.Tensor, rank: int, world: int, epoch: int) -> None:
+    """Cross-GPU arrival barrier number `epoch` on the current stream (kino_peer_barrier)."""
+    with _timed("barrier", 0.0, 0.0):
+        _lib.call("kino_peer_barrier", _ptr(flag_ptrs), rank, world, epoch, _stream())

@@ -1,6 +1,6 @@
-"""Multi-GPU paths on NCCL (skipped with fewer than 2 GPUs) against the same computation on one
-GPU, same weights and inputs: Ulysses sequence parallelism of the Flux2 and LTX-2 denoise loops,
-the CFG branch split, and the VAE tile scatter.
+"""Multi-GPU paths (skipped with fewer than 2 GPUs) against the same computation on one GPU,
+same weights and inputs: Ulysses sequence parallelism of the Flux2 and LTX-2 denoise loops over
+NCCL and over the peer transport, the CFG branch split, and the VAE tile scatter.
 
 Only the key order inside each attention changes (rank-major), so the results agree to fp32
 summation-order noise: cosine >= 0.9999 and max relative error <= 1e-2.
@@ -129,7 +129,10 @@ def _worker(rank: int, size: int, port: int, case: str, queue) -> None:
         dec, latent = _vae_case(device)
         out = decode_tiles_distributed(dec, latent, tile=4, overlap=1)
     else:
-        out = _run(case, device, SequenceParallel())
+        sp = SequenceParallel(peer=case.endswith("_peer"))
+        out = _run(case.removesuffix("_peer"), device, sp)
+        torch.cuda.synchronize()
+        sp.close()
     torch.cuda.synchronize()
     import torch.distributed as tdist
 
@@ -137,10 +140,12 @@ def _worker(rank: int, size: int, port: int, case: str, queue) -> None:
     queue.put((rank, out.float().cpu().numpy().tolist()))
 
 
-@pytest.mark.parametrize("case", ["flux", "ltx", "cfg", "vae"])
+@pytest.mark.parametrize("case", ["flux", "ltx", "flux_peer", "ltx_peer", "cfg", "vae"])
 def test_two_gpus_match_one_gpu(cuda_device, case):
-    """flux/ltx: Ulysses over 2 ranks; cfg: conditional and unconditional branch on different
-    GPUs with the velocity exchange; vae: tiles split over 2 ranks, canvases all-reduced."""
+    """flux/ltx: Ulysses over 2 ranks through NCCL all-to-alls; *_peer: the same through the
+    peer transport (projection epilogues and attention store into the other GPU's buffers over
+    NVLink, device barriers); cfg: conditional and unconditional branch on different GPUs with
+    the velocity exchange; vae: tiles split over 2 ranks, canvases all-reduced."""
     size, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
@@ -151,7 +156,7 @@ def test_two_gpus_match_one_gpu(cuda_device, case):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    expect = _run(case, cuda_device).float().cpu()
+    expect = _run(case.removesuffix("_peer"), cuda_device).float().cpu()
     for r in range(size):
         got = torch.tensor(results[r])
         cos = float(torch.nn.functional.cosine_similarity(got.flatten(), expect.flatten(), dim=0))
