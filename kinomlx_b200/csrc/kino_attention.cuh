@@ -8,41 +8,40 @@
 // Layout: q, k and v are token-major, (batch, tokens, heads * 128) with any row stride, which is
 // what the projections write. Queries and keys may each come in two segments (text tokens, then
 // image tokens) that are concatenated logically but never in memory: each 128-row query tile and
-// each 64-key block belongs to one segment.
+// each 128-key block belongs to one segment.
 //
-// One CTA computes two 128-query tiles (A and B) of one head over key blocks of 64:
-//   warp 0      TMA: Q_A and Q_B once, then K and V blocks through a 4-stage ring
+// One CTA computes two 128-query tiles (A and B) of one head in ping-pong:
+//   warp 0      TMA: Q_A and Q_B once, then K and V blocks of 128 keys through a 2-stage ring
 //   warp 1      tensor-memory owner and MMA issuer, in the order
-//                 S_A(0) S_B(0) S_A(1) S_B(1) | PV_A(j) S_A(j+2) PV_B(j) S_B(j+2) | ...
-//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B, one query row per thread:
-//               tcgen05.ld the row's 64 scores, online max/sum in the exp2 domain (part of the
-//               exponentials on the FMA pipes), P as bf16 pairs back over the scores, O rescaled
-//               in tensor memory only when the running max grows by more than 2^8 (the stale
-//               max cancels in the final division).
-// Tensor memory (512 columns): S of tile t, block j at [128t + 64(j % 2), +64) with P in its
-// first 32 columns, O_A [256,384), O_B [384,512). Each tile's S is double-buffered, so S(j + 1)
-// is computed while the softmax of block j runs and the softmax never waits for a PV product;
-// the two tiles keep both softmax warp sets busy. The PV product takes P straight from tensor
-// memory (the TMEM-A form of tcgen05.mma) and V in place from shared memory as an MN-major
-// operand. MMAs of one issuing thread run in order, so S(j + 2) overwriting P(j) after PV(j) is
-// safe, and the commit that signals S(j) also covers PV(j - 2).
+//                 S_A(0) S_B(0) | PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) | ...
+//               so one tile's products run while the other tile's softmax does
+//   warps 2..9  the softmax of whichever tile is next, A(j), B(j), A(j+1), ...: two warps per
+//               tensor-memory lane quarter (32 query rows), each on 64 of the block's 128 keys;
+//               tcgen05.ld the half row, exchange the half-row maxima through shared memory (an
+//               mbarrier per quarter), exponentials in the exp2 domain (part on the FMA pipes),
+//               P as bf16 pairs back over the half's own scores. O is rescaled in tensor memory
+//               only when the running max grows by more than 2^8 (the stale max cancels in the
+//               final division).
+// Tensor memory (512 columns): S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512). P of
+// keys 0..63 sits in columns [0,32) and of keys 64..127 in [64,96) of its S. The PV product takes
+// P straight from tensor memory (the TMEM-A form of tcgen05.mma) and V in place from shared
+// memory as an MN-major operand. MMAs of one issuing thread run in order, so S(j+1) overwriting
+// P(j) after PV(j) is safe, and the commit that signals S(j+1) also covers PV(j), so O is
+// settled whenever the softmax sees S.
 #pragma once
 #include "kino_common.cuh"
 
 namespace kino {
 
 constexpr int ATT_BM = 128;  // queries per tile
-constexpr int ATT_BN = 64;   // keys per block
+constexpr int ATT_BN = 128;  // keys per block
 constexpr int ATT_D = 128;   // head dim
-#ifndef KINO_ATT_STAGES
-#define KINO_ATT_STAGES 4
-#endif
-constexpr int ATT_STAGES = KINO_ATT_STAGES;  // K + V blocks in flight
+constexpr int ATT_STAGES = 2;  // K + V blocks in flight
 constexpr int ATT_THREADS = 320;
 // Key pairs i of a block whose bit (i % 8) is set take the FMA-pipe exponential
-// (exp2_poly_x2) instead of the special-function unit: bits 1 and 4 = 2 of every 8 pairs.
+// (exp2_poly_x2) instead of the special-function unit: bits 1, 4, 6 = 3 of every 8 pairs.
 #ifndef KINO_ATT_EMU_MASK
-#define KINO_ATT_EMU_MASK 0x12
+#define KINO_ATT_EMU_MASK 0x52
 #endif
 constexpr unsigned ATT_EMU_MASK = KINO_ATT_EMU_MASK;
 
@@ -68,14 +67,15 @@ struct AttnParams {
 };
 
 struct AttnSmem {
-  static constexpr int QHALF = ATT_BM * 64 * 2;   // 16 KB: 128 query rows x 64 dims
-  static constexpr int KHALF = ATT_BN * 64 * 2;   // 8 KB: 64 key rows x 64 dims
-  static constexpr int Q_OFF = 0;                 // tile t at Q_OFF + t * 2 * QHALF
-  static constexpr int KV_OFF = 4 * QHALF;        // per stage: K 2 halves, V 2 halves
-  static constexpr int STAGE = 4 * KHALF;
-  static constexpr int BAR_OFF = KV_OFF + ATT_STAGES * STAGE;
-  // q_full, kv_full[S], kv_empty[S], s_full[2][2], p_full[2][2], o_ready[2], o_done, drain
-  static constexpr int NBAR = 1 + 2 * ATT_STAGES + 4 + 4 + 2 + 2;
+  static constexpr int HALF = 128 * 64 * 2;    // 16 KB: 128 rows x 64 dims
+  static constexpr int Q_OFF = 0;              // tile t at Q_OFF + t * 2 * HALF
+  static constexpr int KV_OFF = 4 * HALF;      // per stage: K 2 halves, V 2 halves
+  static constexpr int STAGE = 4 * HALF;
+  static constexpr int X_OFF = KV_OFF + ATT_STAGES * STAGE;  // maxima [tile][parity][half][128]
+  static constexpr int L_OFF = X_OFF + 2 * 2 * 2 * 128 * 4;  // sums [tile][half][128]
+  static constexpr int BAR_OFF = L_OFF + 2 * 2 * 128 * 4;
+  // q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_done, drain, xbar[4][2][2], lbar[4]
+  static constexpr int NBAR = 1 + 2 * ATT_STAGES + 2 + 2 + 2 + 16 + 4;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
 };
 
@@ -132,11 +132,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + ATT_STAGES;
-  uint64_t* s_full = kv_empty + ATT_STAGES;  // [tile][S buffer]
-  uint64_t* p_full = s_full + 4;             // [tile][S buffer]
-  uint64_t* o_ready = p_full + 4;            // [tile], one phase per PV
-  uint64_t* o_done = o_ready + 2;
+  uint64_t* s_full = kv_empty + ATT_STAGES;  // [tile]
+  uint64_t* p_full = s_full + 2;             // [tile]
+  uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 1;
+  uint64_t* xbar = drain + 1;                // [quarter][tile][block parity]
+  uint64_t* lbar = xbar + 16;                // [quarter]
+  float* xmax = reinterpret_cast<float*>(smem + L::X_OFF);
+  float* xsum = reinterpret_cast<float*>(smem + L::L_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -146,6 +149,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const int batch = blockIdx.z;
   const QTile tiles[2] = {q_tile_of(p, 2 * blockIdx.x), q_tile_of(p, 2 * blockIdx.x + 1)};
   const bool has_b = tiles[1].valid;
+  const int ntile = has_b ? 2 : 1;
   const int nblk = p.kv_blocks[0] + (p.nkv_seg > 1 ? p.kv_blocks[1] : 0);
 
   if (threadIdx.x == 0) {
@@ -154,13 +158,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);  // one arrive per softmax warp of the tile
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 8);  // one arrive per softmax warp
     }
-    for (int t = 0; t < 2; ++t) mbar_init(&o_ready[t], 1);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
+    for (int i = 0; i < 16; ++i) mbar_init(&xbar[i], 64);  // the two warps of a quarter
+    for (int i = 0; i < 4; ++i) mbar_init(&lbar[i], 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -177,12 +182,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, (has_b ? 4 : 2) * L::QHALF);
-      for (int t = 0; t < (has_b ? 2 : 1); ++t) {
+      mbar_expect_tx(q_full, (has_b ? 4 : 2) * L::HALF);
+      for (int t = 0; t < ntile; ++t) {
         const CUtensorMap* mq = tiles[t].seg ? &mq1 : &mq0;
-        uint8_t* sq = smem + L::Q_OFF + t * 2 * L::QHALF;
+        uint8_t* sq = smem + L::Q_OFF + t * 2 * L::HALF;
         tma_load_4d(sq, mq, q_full, 0, tiles[t].tile * ATT_BM, head, batch);
-        tma_load_4d(sq + L::QHALF, mq, q_full, 64, tiles[t].tile * ATT_BM, head, batch);
+        tma_load_4d(sq + L::HALF, mq, q_full, 64, tiles[t].tile * ATT_BM, head, batch);
       }
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
@@ -194,13 +199,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const CUtensorMap* mk = kseg ? &mk1 : &mk0;
         const CUtensorMap* mv = kseg ? &mv1 : &mv0;
         uint8_t* sk = smem + L::KV_OFF + stage * L::STAGE;
-        uint8_t* sv = sk + 2 * L::KHALF;
-        mbar_expect_tx(&kv_full[stage], 4 * L::KHALF);
+        uint8_t* sv = sk + 2 * L::HALF;
+        mbar_expect_tx(&kv_full[stage], 4 * L::HALF);
         const int t0 = kb * ATT_BN;
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          tma_load_4d(sk + h2 * L::KHALF, mk, &kv_full[stage], h2 * 64, t0, head, batch);
-          tma_load_4d(sv + h2 * L::KHALF, mv, &kv_full[stage], h2 * 64, t0, head, batch);
+          tma_load_4d(sk + h2 * L::HALF, mk, &kv_full[stage], h2 * 64, t0, head, batch);
+          tma_load_4d(sv + h2 * L::HALF, mv, &kv_full[stage], h2 * 64, t0, head, batch);
         }
         ++issued;
       }
@@ -221,50 +226,55 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16(ATT_BM, ATT_BN);
       constexpr uint32_t idesc_o = idesc_bf16(ATT_BM, ATT_D) | (1u << 16);  // B (V) MN-major
-      const int ntile = has_b ? 2 : 1;
-      // S_t(j) into buffer j % 2 of tile t, once K(j) has landed
-      auto s_mma = [&](int t, int j) -> bool {
-        const int stage = j % ATT_STAGES;
-        if (t == 0 && !mbar_wait(&kv_full[stage], (j / ATT_STAGES) & 1, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t sq = smem_u32(smem + L::Q_OFF + t * 2 * L::QHALF);
-        const uint32_t sk = smem_u32(smem + L::KV_OFF + stage * L::STAGE);
+      auto s_mma = [&](int t, int j) {
+        const uint32_t sq = smem_u32(smem + L::Q_OFF + t * 2 * L::HALF);
+        const uint32_t sk = smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE);
 #pragma unroll
         for (int kk = 0; kk < ATT_D / 16; ++kk) {
-          umma_bf16(tmem + t * 128 + (j & 1) * 64,
-                    sdesc_k128(sq + (kk >> 2) * L::QHALF + (kk & 3) * 32),
-                    sdesc_k128(sk + (kk >> 2) * L::KHALF + (kk & 3) * 32), idesc_s,
+          const uint32_t off = (kk >> 2) * L::HALF + (kk & 3) * 32;
+          umma_bf16(tmem + t * 128, sdesc_k128(sq + off), sdesc_k128(sk + off), idesc_s,
                     kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[t * 2 + (j & 1)]);
-        return true;
+        umma_commit(&s_full[t]);
       };
       auto pv_mma = [&](int t, int j) {
         const uint32_t sv =
-            smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE + 2 * L::KHALF);
-        const uint32_t pbase = tmem + t * 128 + (j & 1) * 64;
+            smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE + 2 * L::HALF);
 #pragma unroll
         for (int kk = 0; kk < ATT_BN / 16; ++kk) {
-          umma_bf16_ts(tmem + 256 + t * 128, pbase + kk * 8,
-                       sdesc_mn128(sv + kk * 2048, L::KHALF), idesc_o,
+          // keys 16kk .. 16kk+15: P columns 8kk (first 64 keys) or 8kk + 32 (last 64)
+          umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8 + (kk >= 4 ? 32 : 0),
+                       sdesc_mn128(sv + kk * 2048, L::HALF), idesc_o,
                        (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&o_ready[t]);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag) && nblk > 0;
-      if (ok) tc_fence_after();
-      for (int j = 0; ok && j < 2 && j < nblk; ++j)
-        for (int t = 0; ok && t < ntile; ++t) ok = s_mma(t, j);
+      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < ntile; ++t) s_mma(t, 0);
+      }
       for (int j = 0; ok && j < nblk; ++j) {
+        const bool more = j + 1 < nblk;
         for (int t = 0; t < ntile && ok; ++t) {
-          if (!mbar_wait(&p_full[t * 2 + (j & 1)], (j >> 1) & 1, abort_flag)) {
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           pv_mma(t, j);
           if (t == ntile - 1) umma_commit(&kv_empty[j % ATT_STAGES]);
-          if (j + 2 < nblk) ok = s_mma(t, j + 2);
+          if (more) {
+            if (t == 0) {
+              if (!mbar_wait(&kv_full[(j + 1) % ATT_STAGES], ((j + 1) / ATT_STAGES) & 1,
+                             abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            s_mma(t, j + 1);
+          }
         }
       }
       umma_commit(o_done);
@@ -274,34 +284,31 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
     }
   } else {
-    // softmax warps: 2..5 tile A, 6..9 tile B; one query row per thread
-    const int t = (warp - 2) >> 2;
-    const QTile qt = tiles[t];
-    if (qt.valid) {
-      const int quarter = warp & 3;
-      const int row = quarter * 32 + static_cast<int>(lane);
-      const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-      const uint32_t o_col = tmem + lane_base + 256 + t * 128;
-      const float sl2 = p.scale_log2;
-      float m_run = -INFINITY;  // running max of s * scale * log2(e)
-      float l_run = 0.0f;
-      bool ok = true;
-      for (int j = 0; j < nblk; ++j) {
-        const int buf = j & 1;
-        if (!mbar_wait(&s_full[t * 2 + buf], (j >> 1) & 1, abort_flag)) {
+    // softmax warps 2..9: lane quarter warp % 4 (32 rows), key half (warp - 2) / 4
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + static_cast<int>(lane);
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const float sl2 = p.scale_log2;
+    float m_run[2] = {-INFINITY, -INFINITY};  // per tile: running max of s * scale * log2(e)
+    float l_run[2] = {0.0f, 0.0f};            // per tile: this half's share of the row sum
+    bool ok = true;
+    for (int j = 0; j < nblk && ok; ++j) {
+      const int kseg = (j < p.kv_blocks[0]) ? 0 : 1;
+      const int kb = j - (kseg ? p.kv_blocks[0] : 0);
+      const int valid = min(ATT_BN, p.kv_tokens[kseg] - kb * ATT_BN) - half * 64;
+      for (int t = 0; t < ntile; ++t) {
+        if (!mbar_wait(&s_full[t], j & 1, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t s_col = tmem + lane_base + t * 128 + buf * 64;
-        const int kseg = (j < p.kv_blocks[0]) ? 0 : 1;
-        const int kb = j - (kseg ? p.kv_blocks[0] : 0);
-        const int valid = min(ATT_BN, p.kv_tokens[kseg] - kb * ATT_BN);
+        const uint32_t s_col = tmem + lane_base + t * 128 + half * 64;
         uint32_t sr[2][32];
         tmem_ld32(s_col, sr[0]);
         tmem_ld32(s_col + 32, sr[1]);
         tmem_wait_ld();
-        if (valid < ATT_BN) {  // only a segment's last key block; warp-uniform
+        if (valid < 64) {  // only a segment's last key block; warp-uniform
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
 #pragma unroll
@@ -322,30 +329,41 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
           mq[q] = fmaxf(a, __uint_as_float(v[15]));
         }
-        const float m_blk = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
-        // Lazy rescale: the running max moves only when a block's max exceeds it by > 2^8.
+        const float mine = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+        // exchange the half-row maxima with the quarter's other warp
+        float* xm = xmax + (t * 2 + (j & 1)) * 256;
+        xm[half * 128 + row] = mine;
+        uint64_t* xb = &xbar[(quarter * 2 + t) * 2 + (j & 1)];
+        mbar_arrive(xb);
+        if (!mbar_wait(xb, (j >> 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const float m_blk = fmaxf(mine, xm[(1 - half) * 128 + row]) * sl2;
+        // Lazy rescale, decided identically by both halves of a row. O of this tile holds PV(j-1)
+        // (completed before S(j) was signalled).
         float alpha = 1.0f;
         bool rescale = false;
         if (j > 0) {
-          const bool need = m_blk > m_run + 8.0f;
+          const bool need = m_blk > m_run[t] + 8.0f;
           rescale = __any_sync(0xffffffffu, need);
           if (need) {
-            alpha = ex2_approx(m_run - m_blk);
-            m_run = m_blk;
-            l_run *= alpha;
+            alpha = ex2_approx(m_run[t] - m_blk);
+            m_run[t] = m_blk;
+            l_run[t] *= alpha;
           }
         } else {
-          m_run = m_blk;
+          m_run[t] = m_blk;
         }
         const uint64_t sl2x2 = f2_pack(sl2, sl2);
-        const uint64_t negm = f2_pack(-m_run, -m_run);
+        const uint64_t negm = f2_pack(-m_run[t], -m_run[t]);
         uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
           uint32_t packed[8];
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
-            const int i = q8 * 8 + u;  // key pair index within the block
+            const int i = q8 * 8 + u;  // key pair index within the half block
             const uint32_t* v = sr[i >> 4];
             const int e = (2 * i) & 31;
             const uint64_t xs =
@@ -364,17 +382,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           tmem_st8(s_col + q8 * 8, packed);
         }
         const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
-        l_run += ls.x + ls.y;
+        l_run[t] += ls.x + ls.y;
         if (rescale) {
-          // O must hold PV(j - 1) before it is scaled (PV(j - 2) completed before S(j) did,
-          // so the parity names the right phase)
-          if (!mbar_wait(&o_ready[t], (j - 1) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+          const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * 64;
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             uint32_t o[32];
             tmem_ld32(o_col + c * 32, o);
             tmem_wait_ld();
@@ -386,13 +398,22 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t * 2 + buf]);
+        if (lane == 0) mbar_arrive(&p_full[t]);
       }
-      if (ok && nblk > 0 && mbar_wait(o_done, 0, abort_flag)) {
-        tc_fence_after();
+    }
+    if (ok && nblk > 0) {
+      // row sums: this half's shares to shared memory for the other warp of the quarter
+      for (int t = 0; t < ntile; ++t) xsum[(t * 2 + half) * 128 + row] = l_run[t];
+      mbar_arrive(&lbar[quarter]);
+      ok = mbar_wait(&lbar[quarter], 0, abort_flag);
+    }
+    if (ok && nblk > 0 && mbar_wait(o_done, 0, abort_flag)) {
+      tc_fence_after();
+      for (int t = 0; t < ntile; ++t) {
+        const QTile qt = tiles[t];
         const int tok = qt.tile * ATT_BM + row;
         const bool store = tok < p.q_tokens[qt.seg];
-        const float inv_l = 1.0f / l_run;
+        const float inv_l = 1.0f / (l_run[t] + xsum[(t * 2 + 1 - half) * 128 + row]);
         // Optional head gate: bf16(bf16(O / l) * gate[t, head])
         const __nv_bfloat16* gp = p.gate[qt.seg];
         __nv_bfloat16* dst;
@@ -420,8 +441,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           const float o = __uint_as_float(raw) * inv_l;
           return gp != nullptr ? bf16_round(bf16_round(o) * gv) : o;
         };
+        const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * 64;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t o[32];
           tmem_ld32(o_col + c * 32, o);
           tmem_wait_ld();
@@ -433,13 +455,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
               w.y = pack_bf16x2(fin(o[g * 8 + 2]), fin(o[g * 8 + 3]));
               w.z = pack_bf16x2(fin(o[g * 8 + 4]), fin(o[g * 8 + 5]));
               w.w = pack_bf16x2(fin(o[g * 8 + 6]), fin(o[g * 8 + 7]));
-              *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = w;
+              *reinterpret_cast<uint4*>(dst + half * 64 + c * 32 + g * 8) = w;
             }
           }
         }
-        // rows returned to other GPUs: visible before the next kernel signals
-        if (p.out_peers != nullptr) __threadfence_system();
       }
+      // rows returned to other GPUs: visible before the next kernel signals
+      if (p.out_peers != nullptr) __threadfence_system();
     }
   }
 
