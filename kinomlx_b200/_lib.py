@@ -79,6 +79,11 @@ class Epilogue(ctypes.Structure):
         ("scatter_row0", c_int64),
         ("scatter_rows", c_int64),
         ("seg_slot", c_int * 4),
+        ("w_lead", c_void_p),
+        ("ldw_lead", c_int64),
+        ("lead_rows", c_int64),
+        ("norm_weight_lead", c_void_p * 2),
+        ("gate_lead", c_void_p),
     ]
 
 

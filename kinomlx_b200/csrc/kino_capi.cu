@@ -172,9 +172,9 @@ kino_status ensure_smem(K kernel, int bytes, int slot) {
 template <int BN, int STAGES>
 kino_status launch_gemm(const void* x, const void* w, void* out, const kino::GemmShape& s0,
                         int64_t ldx, int64_t bsx, int64_t ldw, const kino::GemmEpi& e,
-                        cudaStream_t stream, int slot) {
+                        cudaStream_t stream, int slot, const void* w_lead, int64_t ldw_lead) {
   using L = kino::GemmSmem<BN, STAGES>;
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mbl;
   const uint64_t da[3] = {static_cast<uint64_t>(s0.k), static_cast<uint64_t>(s0.m),
                           static_cast<uint64_t>(s0.batch)};
   const uint64_t sa[2] = {static_cast<uint64_t>(ldx),
@@ -187,6 +187,12 @@ kino_status launch_gemm(const void* x, const void* w, void* out, const kino::Gem
   const uint32_t bb[2] = {64, static_cast<uint32_t>(BN)};
   st = make_map(&mb, w, 2, db, sb, bb);
   if (st != KINO_OK) return st;
+  mbl = mb;
+  if (w_lead != nullptr) {
+    const uint64_t sbl[1] = {static_cast<uint64_t>(ldw_lead)};
+    st = make_map(&mbl, w_lead, 2, db, sbl, bb);
+    if (st != KINO_OK) return st;
+  }
   kino::GemmShape s = s0;
   s.tiles_m = (s.m + kino::GEMM_BM - 1) / kino::GEMM_BM;
   s.tiles_n = (s.n + BN - 1) / BN;
@@ -197,7 +203,7 @@ kino_status launch_gemm(const void* x, const void* w, void* out, const kino::Gem
   if (st != KINO_OK) return st;
   const int grid = s.num_tiles < device_sms() ? s.num_tiles : device_sms();
   launch_pdl(kernel, dim3(grid), dim3(kino::GEMM_THREADS), L::TOTAL, stream,
-      ma, mb, reinterpret_cast<__nv_bfloat16*>(out), s, e);
+      ma, mb, mbl, reinterpret_cast<__nv_bfloat16*>(out), s, e);
   return check_launch("kino_linear");
 }
 
@@ -237,9 +243,9 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
 template <int STAGES>
 kino_status launch_gemm_2sm(const void* x, const void* w, void* out, const kino::GemmShape& s0,
                             int64_t ldx, int64_t bsx, int64_t ldw, const kino::GemmEpi& e,
-                            cudaStream_t stream, int slot) {
+                            cudaStream_t stream, int slot, const void* w_lead, int64_t ldw_lead) {
   using L = kino::Gemm2SmSmem<STAGES>;
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mbl;
   const uint64_t da[3] = {static_cast<uint64_t>(s0.k), static_cast<uint64_t>(s0.m),
                           static_cast<uint64_t>(s0.batch)};
   const uint64_t sa[2] = {static_cast<uint64_t>(ldx),
@@ -252,6 +258,12 @@ kino_status launch_gemm_2sm(const void* x, const void* w, void* out, const kino:
   const uint32_t bb[2] = {64, 128};
   st = make_map(&mb, w, 2, db, sb, bb);
   if (st != KINO_OK) return st;
+  mbl = mb;
+  if (w_lead != nullptr) {
+    const uint64_t sbl[1] = {static_cast<uint64_t>(ldw_lead)};
+    st = make_map(&mbl, w_lead, 2, db, sbl, bb);
+    if (st != KINO_OK) return st;
+  }
   kino::GemmShape s = s0;
   s.tiles_m = (s.m + 255) / 256;
   s.tiles_n = (s.n + 255) / 256;
@@ -263,7 +275,7 @@ kino_status launch_gemm_2sm(const void* x, const void* w, void* out, const kino:
   const int max_pairs = device_sms() / 2;
   const int pairs = s.num_tiles < max_pairs ? s.num_tiles : max_pairs;
   launch_ex(kernel, dim3(2 * pairs, 1, 1), dim3(kino::GEMM_THREADS, 1, 1), L::TOTAL, stream, 2, ma,
-            mb, reinterpret_cast<__nv_bfloat16*>(out), s, e);
+            mb, mbl, reinterpret_cast<__nv_bfloat16*>(out), s, e);
   return check_launch("kino_linear (2-SM)");
 }
 
@@ -462,6 +474,28 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
     e.scatter_row0 = epi->scatter_row0;
     for (int g = 0; g < 4; ++g) e.seg_slot[g] = epi->seg_slot[g];
   }
+  const void* w_lead = nullptr;
+  int64_t ldw_lead = 0;
+  e.lead_rows = 0;
+  if (epi != nullptr && epi->lead_rows > 0) {
+    if (batch != 1 || epi->lead_rows % 256 || epi->lead_rows >= m || epi->w_lead == nullptr ||
+        !aligned16(epi->w_lead) || epi->ldw_lead % 8 || epi->ldw_lead < k)
+      return fail(KINO_EINVAL, "kino_linear: lead rows need batch 1, a multiple of 256 below m "
+                               "and an aligned lead weight");
+    for (int r = 0; r < 2; ++r)
+      if ((e.norm_w[r] != nullptr) != (epi->norm_weight_lead[r] != nullptr) ||
+          (epi->norm_weight_lead[r] != nullptr && !aligned16(epi->norm_weight_lead[r])))
+        return fail(KINO_EINVAL, "kino_linear: lead rows need QK norm weights like the others");
+    if (e.kind == kino::EPI_GATED_RESIDUAL &&
+        (epi->gate_lead == nullptr || !aligned16(epi->gate_lead)))
+      return fail(KINO_EINVAL, "kino_linear: lead rows need their own aligned gate");
+    w_lead = epi->w_lead;
+    ldw_lead = epi->ldw_lead;
+    e.lead_rows = static_cast<int>(epi->lead_rows);
+    for (int r = 0; r < 2; ++r)
+      e.norm_w_lead[r] = static_cast<const __nv_bfloat16*>(epi->norm_weight_lead[r]);
+    e.gate_lead = static_cast<const __nv_bfloat16*>(epi->gate_lead);
+  }
   kino::GemmShape s;
   std::memset(&s, 0, sizeof(s));
   s.batch = static_cast<int>(batch);
@@ -473,11 +507,12 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (gemm_tiling(batch, m, n)) {
     case 1:
-      return launch_gemm_2sm<KINO_GEMM_PAIR_STAGES>(x, w, out, s, ldx, bsx, ldw, e, st, 6);
+      return launch_gemm_2sm<KINO_GEMM_PAIR_STAGES>(x, w, out, s, ldx, bsx, ldw, e, st, 6, w_lead,
+                                                    ldw_lead);
     case 2:
-      return launch_gemm<256, 4>(x, w, out, s, ldx, bsx, ldw, e, st, 1);
+      return launch_gemm<256, 4>(x, w, out, s, ldx, bsx, ldw, e, st, 1, w_lead, ldw_lead);
     default:
-      return launch_gemm<128, 6>(x, w, out, s, ldx, bsx, ldw, e, st, 0);
+      return launch_gemm<128, 6>(x, w, out, s, ldx, bsx, ldw, e, st, 0, w_lead, ldw_lead);
   }
 }
 

@@ -62,6 +62,11 @@ struct GemmEpi {
   int scatter_cols, seg_width, part_width;
   int64_t scatter_ld, scatter_row0;
   int seg_slot[4];
+  // Rows [0, lead_rows) (batch 1, whole tiles) take the second weight (its own tensor map) and
+  // these norm weights and gate: the text rows of a joint [text | image] sequence.
+  int lead_rows;
+  const __nv_bfloat16* norm_w_lead[2];
+  const __nv_bfloat16* gate_lead;
 };
 
 // Where the 32- or 128-column chunk of output row `row` starting at col0 is stored: this GPU's
@@ -173,7 +178,8 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
   } else if (e.kind == EPI_GATED_RESIDUAL) {
     const __nv_bfloat16* res = e.residual + static_cast<int64_t>(b) * e.bs_res +
                                static_cast<int64_t>(row) * e.ld_res + col0;
-    const __nv_bfloat16* gte = e.gate + static_cast<int64_t>(b) * e.bs_gate + col0;
+    const __nv_bfloat16* gte =
+        (row < e.lead_rows ? e.gate_lead : e.gate) + static_cast<int64_t>(b) * e.bs_gate + col0;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       if (col0 + g * 8 < s.n) {
@@ -302,7 +308,7 @@ __device__ __forceinline__ void gemm_epilogue_head(const GemmShape& s, const Gem
   // tcgen05.ld is warp-collective: every lane loads, only rows inside the product store
   const bool live = row < s.m && col0 < s.n;
   const float inv = rsqrtf(ss / 128.0f + e.norm_eps);
-  const __nv_bfloat16* w = e.norm_w[range];
+  const __nv_bfloat16* w = row < e.lead_rows ? e.norm_w_lead[range] : e.norm_w[range];
   // Tables are head-dim-major, (128, table columns): the 32 threads of a warp hold 32
   // consecutive rows, so each head-dim entry below is one contiguous 128-byte read.
   const int64_t trow = (e.rope_batched ? static_cast<int64_t>(b) * e.rope_rows : 0) +
@@ -361,7 +367,9 @@ __device__ __forceinline__ void gemm_epilogue_row(const GemmShape& s, const Gemm
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a,
-                        const __grid_constant__ CUtensorMap map_b, __nv_bfloat16* __restrict__ out,
+                        const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_b_lead,
+                        __nv_bfloat16* __restrict__ out,
                         const GemmShape s, const GemmEpi e) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -394,6 +402,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch(&map_a);
     tma_prefetch(&map_b);
+    tma_prefetch(&map_b_lead);
   }
   griddep_wait();  // the previous kernel has finished with its memory and tensor memory
   if (warp == 1) {
@@ -420,7 +429,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint8_t* sb = sa + L::A_BYTES;
           mbar_expect_tx(&full[stage], L::STAGE_BYTES);
           tma_load_3d(sa, &map_a, &full[stage], kb * GEMM_BK, mt * GEMM_BM, b);
-          tma_load_2d(sb, &map_b, &full[stage], kb * GEMM_BK, nt * BN);
+          tma_load_2d(sb, mt * GEMM_BM < e.lead_rows ? &map_b_lead : &map_b, &full[stage],
+                      kb * GEMM_BK, nt * BN);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -546,6 +556,7 @@ template <int STAGES>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_2sm_kernel(const __grid_constant__ CUtensorMap map_a,
                          const __grid_constant__ CUtensorMap map_b,
+                         const __grid_constant__ CUtensorMap map_b_lead,
                          __nv_bfloat16* __restrict__ out, const GemmShape s, const GemmEpi e) {
   using L = Gemm2SmSmem<STAGES>;
   constexpr int BN = 256;  // pair tile width; this CTA loads BN / 2 weight rows
@@ -582,6 +593,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch(&map_a);
     tma_prefetch(&map_b);
+    tma_prefetch(&map_b_lead);
   }
   griddep_wait();  // the previous kernel has finished with its memory and tensor memory
   if (warp == 1) {
@@ -610,7 +622,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const uint32_t leader_full = smem_u32(&full[stage]) & kPairLeaderMask;
           if (rank == 0) mbar_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
           tma_load_3d_pair(sa, &map_a, leader_full, kb * GEMM_BK, mt * 256 + rank * 128, b);
-          tma_load_2d_pair(sb, &map_b, leader_full, kb * GEMM_BK, nt * BN + rank * 128);
+          tma_load_2d_pair(sb, mt * 256 < e.lead_rows ? &map_b_lead : &map_b, leader_full,
+                           kb * GEMM_BK, nt * BN + rank * 128);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;

@@ -159,6 +159,9 @@ class Flux2Transformer:
 
     # ------------------------------------------------------------------ blocks
     def _double_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
+        if ws.batch == 1 and ws.nt % 256 == 0 and ws.ni > 0:
+            self._double_block_joint(ws, p, rope)
+            return
         d, nt, h = self.v.dim, ws.nt, self.v.heads
         txt, img = ws.stream[:, :nt], ws.stream[:, nt:]
         txt_n, img_n = ws.nrm[:, :nt], ws.nrm[:, nt:]
@@ -192,6 +195,38 @@ class Flux2Transformer:
         ops.linear(txt_n, p["ffc_in"], ws.hid[:, :nt], kind=self.act_kind)
         ops.linear(ws.hid[:, :nt], p["ffc_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
                    gate=m(6, 5))
+
+    def _double_block_joint(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
+        """The double block with each projection of the two streams in one launch over the joint
+        [text | image] rows: text rows use the text stream's weights, norms and gates (lead
+        rows), image rows the image stream's. The streams stay independent; only the launch
+        order interleaves them."""
+        d, nt, h = self.v.dim, ws.nt, self.v.heads
+        txt, img = ws.stream[:, :nt], ws.stream[:, nt:]
+        txt_n, img_n = ws.nrm[:, :nt], ws.nrm[:, nt:]
+        m = lambda base, j: ws.mods[:, (base + j) * d : (base + j + 1) * d]  # img base 0, txt 6
+        ops.adaln(img, m(0, 0), m(0, 1), img_n, norm=ops.NORM_LAYER)
+        ops.adaln(txt, m(6, 0), m(6, 1), txt_n, norm=ops.NORM_LAYER)
+        recv = self.sp.receive(nt + ws.ni, d) if ws.peer else None
+        ops.linear(ws.nrm, p["img_qkv"], ws.qkv, qk_norm=[(0, p["norm_q"]), (d, p["norm_k"])],
+                   norm_width=d, rope=(rope, 0), lead_w=p["txt_qkv"], lead_rows=nt,
+                   lead_qk_norm=[p["norm_added_q"], p["norm_added_k"]],
+                   scatter=self.sp.scatter(recv, d, (0, 1, 2), 0) if recv else None)
+        q, k, v = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
+        if recv:
+            self.sp.attention_from_peers(recv, heads=h, out_ptrs=ws.qkv_ptrs, out_ld=3 * d,
+                                         out_cols=3 * d, out_col=0)
+        else:
+            self.sp.attention(q, k, v, q, heads=h)
+        ops.linear(q, p["to_out"], ws.stream, kind=ops.EPI_GATED_RESIDUAL, residual=ws.stream,
+                   gate=m(0, 2), lead_w=p["to_add_out"], lead_rows=nt, lead_gate=m(6, 2))
+        ops.adaln(img, m(0, 3), m(0, 4), img_n, norm=ops.NORM_LAYER)
+        ops.adaln(txt, m(6, 3), m(6, 4), txt_n, norm=ops.NORM_LAYER)
+        ops.linear(ws.nrm, p["ff_in"], ws.hid, kind=self.act_kind, lead_w=p["ffc_in"],
+                   lead_rows=nt)
+        ops.linear(ws.hid, p["ff_out"], ws.stream, kind=ops.EPI_GATED_RESIDUAL,
+                   residual=ws.stream, gate=m(0, 5), lead_w=p["ffc_out"], lead_rows=nt,
+                   lead_gate=m(6, 5))
 
     def _single_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
         d, h = self.v.dim, self.v.heads

@@ -211,8 +211,16 @@ def linear(
     rope: tuple[RopeTables, int] | None = None,
     eps: float = 1e-6,
     scatter: Scatter | None = None,
+    lead_w: torch.Tensor | None = None,
+    lead_rows: int = 0,
+    lead_qk_norm: list[torch.Tensor] | None = None,
+    lead_gate: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight.
+
+    With `lead_w` (batch 1, lead_rows a multiple of 256 below m), rows [0, lead_rows) use that
+    weight and `lead_qk_norm` / `lead_gate` in place of the qk_norm weights and the gate: the
+    text and image streams of a joint sequence in one launch.
 
     EPI_SWIGLU: columns from `act_col_begin` on come in blocks of 16 gate + 16 content rows
     (see `swiglu_interleave`) and produce half as many output columns.
@@ -281,6 +289,19 @@ def linear(
         epi.rope_offset = offset
         epi.rope_batched = int(tables.batched)
         epi.norm_eps = eps
+    if lead_w is not None:
+        _need(lead_w, "lead_w")
+        if tuple(lead_w.shape) != tuple(w.shape) or lead_w.stride(1) != 1:
+            raise ValueError("the lead weight must match the weight's shape")
+        epi.w_lead = lead_w.data_ptr()
+        epi.ldw_lead = lead_w.stride(0)
+        epi.lead_rows = lead_rows
+        for r, wt in enumerate(lead_qk_norm or []):
+            _need(wt, "lead norm weight")
+            epi.norm_weight_lead[r] = wt.data_ptr()
+        if lead_gate is not None:
+            _need(lead_gate, "lead gate")
+            epi.gate_lead = lead_gate.data_ptr()
     if scatter is not None:
         epi.scatter_ptrs = scatter.ptrs.data_ptr()
         epi.world = scatter.world
