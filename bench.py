@@ -494,6 +494,25 @@ def _time(fn, warmup: int, steps: int, world: int) -> float:
     return max_over_ranks(a.elapsed_time(b) / steps, world)
 
 
+def _kernel_shares(fn) -> dict:
+    """One extra run of fn with per-launch CUDA events: time share of each kernel class."""
+    from kinomlx_b200 import ops
+
+    log_ = ops.LaunchLog()
+    ops.set_launch_log(log_)
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        ops.set_launch_log(None)
+    summary = log_.summary()
+    total = sum(v["ms"] for v in summary.values()) or 1.0
+    return {k: {"launches": int(v["launches"]), "ms": round(v["ms"], 3),
+                "share": round(v["ms"] / total, 4),
+                "tflops": round(v["flops"] / (v["ms"] * 1e9), 1) if v["flops"] else None}
+            for k, v in sorted(summary.items(), key=lambda kv: -kv[1]["ms"])}
+
+
 def run_secondary(world: int, rank: int, local: int) -> dict:
     """BASELINE configs 3-5 on the same GPUs (2 warm-up + 3 timed repetitions each): the
     metric's second half (VAE decode frames/s) and the other step latencies, each with its
@@ -544,7 +563,8 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
         ms = _time(step, 2, 3, world)
         out["config3_cfg"] = {"ms_per_step": round(ms, 3), "mode": mode,
                               "step_tflops": round(2 * step_flops() / (ms * 1e9), 1),
-                              "frac_of_peak": round(2 * step_flops() / (ms * 1e9) / peak, 4)}
+                              "frac_of_peak": round(2 * step_flops() / (ms * 1e9) / peak, 4),
+                              "kernels": _kernel_shares(step)}
     if step is not None:
         model.sp.close()
     model = prepared = None
@@ -566,11 +586,13 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
     lprep = lmodel.prepare(context, pix)
     t0, t1 = lmodel.sp.shard(f * h * w)
     lat = normal((1, f * h * w, lv.in_channels), seed=1, device=device)[:, t0:t1].contiguous()
-    ms = _time(lambda: lmodel.run(lprep, lat, 0.725, sigma_next=0.421875, out=lat), 2, 3, world)
+    lstep = lambda: lmodel.run(lprep, lat, 0.725, sigma_next=0.421875, out=lat)
+    ms = _time(lstep, 2, 3, world)
     out["config4_video_dit"] = {"ms_per_step": round(ms, 3),
                                 "mode": f"Ulysses x{world}" if world > 1 else "single GPU",
                                 "step_tflops": round(ltx_step_flops() / (ms * 1e9), 1),
-                                "frac_of_peak": round(ltx_step_flops() / (ms * 1e9) / peak, 4)}
+                                "frac_of_peak": round(ltx_step_flops() / (ms * 1e9) / peak, 4),
+                                "kernels": _kernel_shares(lstep)}
     lmodel.sp.close()
     lmodel = lprep = lat = None
     torch.cuda.empty_cache()
@@ -586,7 +608,8 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
                                  "mode": f"tiles over {world} GPUs" if world > 1 else "single GPU",
                                  "tiled_tflop": round(flops / 1e12, 1),
                                  "tflops": round(flops / (ms * 1e9), 1),
-                                 "frac_of_peak": round(flops / (ms * 1e9) / peak, 4)}
+                                 "frac_of_peak": round(flops / (ms * 1e9) / peak, 4),
+                                 "kernels": _kernel_shares(fn)}
     return out
 
 

@@ -104,9 +104,10 @@ typedef struct kino_epilogue {
   int64_t scatter_row0;
   int64_t scatter_rows;
   int seg_slot[4];
-  /* Optional lead rows (batch 1; lead_rows a multiple of 256 below m): output rows
-   * [0, lead_rows) are computed with the weight w_lead (row stride ldw_lead, same n x k) and,
-   * where used, norm_weight_lead and gate_lead instead of w, norm_weight and gate. One launch
+  /* Optional lead rows (lead_rows a multiple of 256 below m): output rows [0, lead_rows) of
+   * every batch entry are computed with the weight w_lead (row stride ldw_lead, same n x k)
+   * and, where used, norm_weight_lead and gate_lead (batch stride bs_gate) instead of w,
+   * norm_weight and gate. One launch
    * then covers the text and image rows of a joint sequence whose two streams have their own
    * projections (kinomlx/models/flux2/transformer.py:77-117, DoubleBlock). */
   const void* w_lead;

@@ -478,10 +478,10 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
   int64_t ldw_lead = 0;
   e.lead_rows = 0;
   if (epi != nullptr && epi->lead_rows > 0) {
-    if (batch != 1 || epi->lead_rows % 256 || epi->lead_rows >= m || epi->w_lead == nullptr ||
+    if (epi->lead_rows % 256 || epi->lead_rows >= m || epi->w_lead == nullptr ||
         !aligned16(epi->w_lead) || epi->ldw_lead % 8 || epi->ldw_lead < k)
-      return fail(KINO_EINVAL, "kino_linear: lead rows need batch 1, a multiple of 256 below m "
-                               "and an aligned lead weight");
+      return fail(KINO_EINVAL, "kino_linear: lead rows need a multiple of 256 below m and an "
+                               "aligned lead weight");
     for (int r = 0; r < 2; ++r)
       if ((e.norm_w[r] != nullptr) != (epi->norm_weight_lead[r] != nullptr) ||
           (epi->norm_weight_lead[r] != nullptr && !aligned16(epi->norm_weight_lead[r])))

@@ -159,7 +159,7 @@ class Flux2Transformer:
 
     # ------------------------------------------------------------------ blocks
     def _double_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
-        if ws.batch == 1 and ws.nt % 256 == 0 and ws.ni > 0:
+        if ws.nt % 256 == 0 and ws.ni > 0:
             self._double_block_joint(ws, p, rope)
             return
         d, nt, h = self.v.dim, ws.nt, self.v.heads

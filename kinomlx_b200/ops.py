@@ -218,9 +218,9 @@ def linear(
 ) -> torch.Tensor:
     """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight.
 
-    With `lead_w` (batch 1, lead_rows a multiple of 256 below m), rows [0, lead_rows) use that
-    weight and `lead_qk_norm` / `lead_gate` in place of the qk_norm weights and the gate: the
-    text and image streams of a joint sequence in one launch.
+    With `lead_w` (lead_rows a multiple of 256 below m), rows [0, lead_rows) of every batch
+    entry use that weight and `lead_qk_norm` / `lead_gate` in place of the qk_norm weights and
+    the gate: the text and image streams of a joint sequence in one launch.
 
     EPI_SWIGLU: columns from `act_col_begin` on come in blocks of 16 gate + 16 content rows
     (see `swiglu_interleave`) and produce half as many output columns.

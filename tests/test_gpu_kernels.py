@@ -380,24 +380,25 @@ def test_linear_fused_qk_norm_rope_and_gelu(cuda_device):
     assert (out[0].cpu() == expect).float().mean() > 0.95
 
 
-@pytest.mark.parametrize("m,n,k", [(768, 512, 256), (2560, 2048, 512)])
-def test_linear_lead_rows_use_their_own_weight_norm_and_gate(cuda_device, m, n, k):
-    """One launch over a joint [text | image] sequence: the first 256 rows take the lead weight,
-    QK norm weights and gate, the rest the main ones; equal to two separate products."""
+@pytest.mark.parametrize("batch,m,n,k", [(1, 768, 512, 256), (1, 2560, 2048, 512), (2, 768, 768, 256)])
+def test_linear_lead_rows_use_their_own_weight_norm_and_gate(cuda_device, batch, m, n, k):
+    """One launch over a joint [text | image] sequence: the first 256 rows of every batch entry
+    take the lead weight and gate, the rest the main ones; equal to two separate products."""
     from kinomlx_b200 import ops
 
     dev = cuda_device
     lead = 256
-    x = _randn((1, m, k), 201)
+    x = _randn((batch, m, k), 201)
     w, wl = _randn((n, k), 202, 0.05), _randn((n, k), 203, 0.05)
-    gate, gate_l = _randn((1, n), 204), _randn((1, n), 205)
-    res = _randn((1, m, n), 206)
-    expect = torch.empty((1, m, n), dtype=torch.float32)
-    for rows, wt, g in ((slice(0, lead), wl, gate_l), (slice(lead, m), w, gate)):
-        y = (x[0, rows].float() @ wt.float().T).to(BF).float()
-        expect[0, rows] = res[0, rows].float() + (g.float() * y).to(BF).float()
+    gate, gate_l = _randn((batch, n), 204), _randn((batch, n), 205)
+    res = _randn((batch, m, n), 206)
+    expect = torch.empty((batch, m, n), dtype=torch.float32)
+    for b in range(batch):
+        for rows, wt, g in ((slice(0, lead), wl, gate_l), (slice(lead, m), w, gate)):
+            y = (x[b, rows].float() @ wt.float().T).to(BF).float()
+            expect[b, rows] = res[b, rows].float() + (g[b].float() * y).to(BF).float()
     out = res.clone().to(dev)
     ops.linear(x.to(dev), w.to(dev), out, kind=ops.EPI_GATED_RESIDUAL, residual=out,
                gate=gate.to(dev), lead_w=wl.to(dev), lead_rows=lead, lead_gate=gate_l.to(dev))
-    assert _max_rel(out[0], expect[0].to(BF)) <= 2e-2
-    assert (out[0].cpu() == expect[0].to(BF)).float().mean() > 0.95
+    assert _max_rel(out, expect.to(BF)) <= 2e-2
+    assert (out.cpu() == expect.to(BF)).float().mean() > 0.95
