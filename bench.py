@@ -509,7 +509,8 @@ def _kernel_shares(fn) -> dict:
     total = sum(v["ms"] for v in summary.values()) or 1.0
     return {k: {"launches": int(v["launches"]), "ms": round(v["ms"], 3),
                 "share": round(v["ms"] / total, 4),
-                "tflops": round(v["flops"] / (v["ms"] * 1e9), 1) if v["flops"] else None}
+                "tflops": round(v["flops"] / (v["ms"] * 1e9), 1) if v["flops"] else None,
+                "gbs": round(v["bytes"] / (v["ms"] * 1e6), 1) if v["bytes"] else None}
             for k, v in sorted(summary.items(), key=lambda kv: -kv[1]["ms"])}
 
 

@@ -290,6 +290,11 @@ typedef struct kino_conv3d_args {
   void* out;                /* plain: (F, H, W, N); depth-to-space: (F*st - (st>1), H*sh, W*sw, N/(st*sh*sw)) */
   int causal;               /* 1: two copies of the first frame in front; 0: one at each end */
   int stride_t, stride_h, stride_w;  /* depth-to-space of the output; weight rows sub-position-major */
+  /* Optional GroupNorm(32) statistics of the stored output for the next layer's norm
+   * (kino_group_norm_from_stats): a device buffer of kino_conv3d_stats_size() bytes, its
+   * capacity in records (4 per SM). Output channels per voxel 32..1024, group size dividing 32. */
+  void* stats;
+  int64_t stats_records;
 } kino_conv3d_args;
 
 /* 3x3x3 convolution with temporal replicate and spatial zero padding as an implicit GEMM on
@@ -315,6 +320,19 @@ int64_t kino_group_norm_workspace_size(int64_t voxels, int64_t channels);
 kino_status kino_group_norm(const void* x, const void* weight, const void* bias, void* out,
                             int64_t voxels, int64_t channels, float eps, int apply_silu,
                             void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Bytes of the statistics buffer kino_conv3d fills for kino_group_norm_from_stats on the current
+ * device: a header, mean and rstd, and 4 records per SM of 32 x (count, mean, m2) floats. */
+int64_t kino_conv3d_stats_size(void);
+
+/* Affine GroupNorm(32) (+ SiLU) of the output of the kino_conv3d call that filled `stats`: the
+ * statistics the conv's epilogue gathered (count, mean and sum of squared deviations per group,
+ * merged with Chan's pairwise formula) replace the two statistics passes over x of
+ * kino_group_norm, leaving one read and one write of the activation. No counterpart in the
+ * reference (its GroupNorm reads x for its statistics). */
+kino_status kino_group_norm_from_stats(const void* x, const void* weight, const void* bias,
+                                       void* out, int64_t voxels, int64_t channels, float eps,
+                                       int apply_silu, void* stats, void* stream);
 
 /* Largest scratch kino_group_norm_noalloc can use: 80 KiB, enough for every shape
  * kino_group_norm accepts (its statistics use at most 592 partial sums per group). */

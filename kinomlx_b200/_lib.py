@@ -138,6 +138,8 @@ class Conv3dArgs(ctypes.Structure):
         ("stride_t", c_int),
         ("stride_h", c_int),
         ("stride_w", c_int),
+        ("stats", c_void_p),
+        ("stats_records", c_int64),
     ]
 
 
@@ -186,6 +188,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_pixel_norm": (c_int, [P, P, I64, I64, F, c_int, P]),
     "kino_group_norm_workspace_size": (c_int64, [I64, I64]),
     "kino_group_norm": (c_int, [P, P, P, P, I64, I64, F, c_int, P, I64, P]),
+    "kino_conv3d_stats_size": (c_int64, []),
+    "kino_group_norm_from_stats": (c_int, [P, P, P, P, I64, I64, F, c_int, P, P]),
     "kino_group_norm_noalloc": (c_int, [P, P, P, P, I64, I64, F, c_int, P]),
     "kino_latent_to_bfhwc": (c_int, [P, P, P, P, I64, I64, P]),
     "kino_tile_blend": (c_int, [P, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, P, P, P]),

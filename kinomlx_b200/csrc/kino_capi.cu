@@ -235,6 +235,11 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   kino::ConvEpi e;
   e.bias = static_cast<const __nv_bfloat16*>(a->bias);
   e.residual = static_cast<const __nv_bfloat16*>(a->residual);
+  e.stats = static_cast<float*>(a->stats);
+  e.group_size = s.Co / kino::GN_GROUPS;
+  if (e.stats != nullptr && grid * 4 > a->stats_records)
+    return fail(KINO_EINVAL, "kino_conv3d: statistics buffer holds %lld records, %d needed",
+                (long long)a->stats_records, grid * 4);
   launch_pdl(kernel, dim3(grid), dim3(kino::CONV_THREADS), L::TOTAL, stream,
       mx, mw, static_cast<__nv_bfloat16*>(a->out), s, e);
   return check_launch("kino_conv3d");
@@ -895,6 +900,11 @@ kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
     return fail(KINO_EINVAL, "kino_conv3d: output/residual alignment");
   if (a->frames * a->height * a->width > (1ll << 31))
     return fail(KINO_ENOTSUPPORTED, "kino_conv3d: too many voxels");
+  if (a->stats != nullptr &&
+      (co % kino::GN_GROUPS || 32 % (co / kino::GN_GROUPS) || a->out_channels % 32 ||
+       !aligned16(a->stats)))
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d: GroupNorm(32) statistics need 32..1024 output "
+                                    "channels per voxel with a group size dividing 32");
   kino::ConvShape s;
   std::memset(&s, 0, sizeof(s));
   s.F = static_cast<int>(a->frames);
@@ -968,12 +978,42 @@ kino_status kino_group_norm(const void* x, const void* weight, const void* bias,
                                                                        pass);
     launch_pdl(kino::group_norm_finalize_kernel, dim3(1), dim3(32), 0, s, ws, parts, count, eps, pass);
   }
-  int64_t blocks = (voxels * channels / 8 + 255) / 256;
-  if (blocks > 148 * 16) blocks = 148 * 16;
+  const int64_t rows_per_cta = 256 / (channels / 8);
+  int64_t blocks = (voxels + rows_per_cta - 1) / rows_per_cta;
+  if (blocks > static_cast<int64_t>(device_sms()) * 8) blocks = static_cast<int64_t>(device_sms()) * 8;
   launch_pdl(kino::group_norm_apply_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
       xb, static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(bias),
-      static_cast<__nv_bfloat16*>(out), voxels, c, ws, parts, apply_silu);
+      static_cast<__nv_bfloat16*>(out), voxels, c, ws + static_cast<int64_t>(parts) * kino::GN_GROUPS,
+      ws + static_cast<int64_t>(parts) * kino::GN_GROUPS + kino::GN_GROUPS, apply_silu);
   return check_launch("kino_group_norm");
+}
+
+int64_t kino_conv3d_stats_size(void) {
+  return (kino::GN_STATS_RECORDS + 4 * static_cast<int64_t>(device_sms()) * 96) * 4;
+}
+
+kino_status kino_group_norm_from_stats(const void* x, const void* weight, const void* bias,
+                                       void* out, int64_t voxels, int64_t channels, float eps,
+                                       int apply_silu, void* stats, void* stream) {
+  if (x == nullptr || weight == nullptr || bias == nullptr || out == nullptr || stats == nullptr)
+    return fail(KINO_EINVAL, "kino_group_norm_from_stats: null operand");
+  if (channels % kino::GN_GROUPS || channels % 8 || channels > 2048 || channels < 32 ||
+      !aligned16(x) || !aligned16(out) || !aligned16(weight) || !aligned16(bias) ||
+      !aligned16(stats) || voxels < 1)
+    return fail(KINO_ENOTSUPPORTED,
+                "kino_group_norm_from_stats: 32 <= channels <= 2048 in 32 groups, aligned operands");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* st = static_cast<float*>(stats);
+  launch_pdl(kino::group_norm_merge_kernel, dim3(1), dim3(1024), 0, s, st, eps);
+  const int64_t rows_per_cta = 256 / (channels / 8);
+  int64_t blocks = (voxels + rows_per_cta - 1) / rows_per_cta;
+  if (blocks > static_cast<int64_t>(device_sms()) * 8) blocks = static_cast<int64_t>(device_sms()) * 8;
+  launch_pdl(kino::group_norm_apply_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
+             static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
+             static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), voxels,
+             static_cast<int>(channels), static_cast<const float*>(st + 4),
+             static_cast<const float*>(st + 36), apply_silu);
+  return check_launch("kino_group_norm_from_stats");
 }
 
 kino_status kino_group_norm_noalloc(const void* x, const void* weight, const void* bias,

@@ -330,6 +330,12 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
 
 // tanh-approximate GELU with fp32 opmath; the inner argument is clamped to +-10 where tanh has
 // saturated in every low-precision type.
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -38,7 +38,53 @@ struct ConvShape {
 struct ConvEpi {
   const __nv_bfloat16* bias;      // [N] (in the same row order as the weight) or null
   const __nv_bfloat16* residual;  // plain mode only: same geometry as the output, or null
+  // GroupNorm(32) statistics of the stored output (the next layer's norm), or null: every
+  // epilogue warp keeps, in lane g, the count, mean and sum of squared deviations of group g
+  // over the values it stored (merged chunk by chunk with Chan's pairwise formula) and writes
+  // them as record (CTA * 4 + lane quarter); CTA 0 writes the record count into the header.
+  float* stats;
+  int group_size;  // output channels per group (output channels / 32)
 };
+
+// GroupNorm statistics layout (floats): [0] record count (int), [4, 36) mean, [36, 68) rstd,
+// record r at GN_STATS_RECORDS + r * 96: (count, mean, m2) for each of the 32 groups.
+constexpr int GN_STATS_RECORDS = 128;
+
+// (n_a, mean_a, m2_a) <- merge with (n_b, mean_b, m2_b) (Chan, Golub & LeVeque).
+__device__ __forceinline__ void chan_merge(float& na, float& ma, float& m2a, float nb, float mb,
+                                           float m2b) {
+  if (nb <= 0.0f) return;
+  const float n = na + nb;
+  const float delta = mb - ma;
+  ma += delta * (nb / n);
+  m2a += m2b + delta * delta * (na * nb / n);
+  na = n;
+}
+
+// GroupNorm statistics of one 32-channel chunk (groups of GS channels) over a warp's 32 voxels
+// (the live ones): count, mean and m2 per group, merged into the lane that owns the group.
+template <int GS>
+__device__ __forceinline__ void conv_chunk_stats(const float (&v)[32], bool live, int first,
+                                                 uint32_t lane, float& n, float& mean,
+                                                 float& m2) {
+  const float cnt = __popc(__ballot_sync(0xffffffffu, live)) * static_cast<float>(GS);
+  if (cnt <= 0.0f) return;
+#pragma unroll
+  for (int k0 = 0; k0 < 32; k0 += GS) {
+    float s1 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < GS; ++j) s1 += v[k0 + j];
+    const float mean_c = warp_sum_f(live ? s1 : 0.0f) / cnt;
+    float d2 = 0.0f;
+#pragma unroll
+    for (int j = 0; j < GS; ++j) {
+      const float dv = v[k0 + j] - mean_c;
+      d2 = fmaf(dv, dv, d2);
+    }
+    const float m2_c = warp_sum_f(live ? d2 : 0.0f);
+    if (static_cast<int>(lane) == first + k0 / GS) chan_merge(n, mean, m2, cnt, mean_c, m2_c);
+  }
+}
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(CONV_THREADS, 1)
@@ -179,6 +225,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     const int quarter = warp & 3;
     const int m = quarter * 32 + static_cast<int>(lane);
     const int cpo = s.Co;  // channels per output voxel
+    float gn_n = 0.0f, gn_mean = 0.0f, gn_m2 = 0.0f;  // statistics of group `lane`
     int local = 0;
     for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
       const int mt = t % s.tiles_m;
@@ -199,14 +246,15 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         tmem_ld32(tmem_base + ((quarter * 32) << 16) + acc * BN + c * 32, r);
         tmem_wait_ld();
         const int n0 = nt * BN + c * 32;
-        if (!valid || n0 >= s.N) continue;
+        if (n0 >= s.N) continue;  // warp-uniform
         // destination voxel and channel offset of this 32-column chunk
         const int sub = n0 / cpo;
         const int ch0 = n0 - sub * cpo;
         const int a = sub / (s.sh * s.sw), bb = (sub / s.sw) % s.sh, ee = sub % s.sw;
         const int fo = f * s.st + a - s.drop, ho = h * s.sh + bb, wo = w * s.sw + ee;
-        if (fo < 0 || fo >= s.Fo) continue;
-        const int64_t off = ((static_cast<int64_t>(fo) * s.Ho + ho) * s.Wo + wo) * cpo + ch0;
+        const bool live = valid && fo >= 0 && fo < s.Fo;
+        const int64_t off =
+            live ? ((static_cast<int64_t>(fo) * s.Ho + ho) * s.Wo + wo) * cpo + ch0 : 0;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = bf16_round(__uint_as_float(r[j]));
@@ -226,7 +274,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 8; ++j) v[g * 8 + j] = bf16_round(v[g * 8 + j] + add[j]);
             }
-            if (e.residual != nullptr) {
+            if (e.residual != nullptr && live) {
               const uint4 raw = *reinterpret_cast<const uint4*>(e.residual + off + g * 8);
               const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
@@ -241,13 +289,36 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
             o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
             o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
             o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-            *reinterpret_cast<uint4*>(out + off + g * 8) = o;
+            if (live) *reinterpret_cast<uint4*>(out + off + g * 8) = o;
+          }
+        }
+        if (e.stats != nullptr) {
+          // the stored (bf16) values of this chunk, group by group: the warp's 32 voxels give
+          // one (count, mean, m2) per group, merged into the lane that owns the group
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
+          const int first = ch0 / e.group_size;
+          switch (e.group_size) {
+            case 1: conv_chunk_stats<1>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+            case 2: conv_chunk_stats<2>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+            case 4: conv_chunk_stats<4>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+            case 8: conv_chunk_stats<8>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+            case 16: conv_chunk_stats<16>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+            default: conv_chunk_stats<32>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
           }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if (e.stats != nullptr) {
+      float* rec = e.stats + GN_STATS_RECORDS + (blockIdx.x * 4 + quarter) * 96 + lane * 3;
+      rec[0] = gn_n;
+      rec[1] = gn_mean;
+      rec[2] = gn_m2;
+      if (blockIdx.x == 0 && warp == 2 && lane == 0)
+        *reinterpret_cast<int*>(e.stats) = static_cast<int>(gridDim.x) * 4;
     }
   }
 

@@ -117,31 +117,88 @@ __global__ void group_norm_finalize_kernel(float* __restrict__ ws, int parts, in
   }
 }
 
-__global__ void group_norm_apply_kernel(const __nv_bfloat16* __restrict__ x,
-                                        const __nv_bfloat16* __restrict__ weight,
-                                        const __nv_bfloat16* __restrict__ bias,
-                                        __nv_bfloat16* __restrict__ out, int64_t voxels, int C,
-                                        const float* __restrict__ ws, int parts, int apply_silu) {
+// Statistics from the producing conv's epilogue (see ConvEpi::stats): merge the records of
+// each group (Chan, Golub & LeVeque, in double precision) into mean and rstd. One warp per
+// group (1024 threads): lanes merge strided records, then a shuffle tree merges the lanes.
+__device__ __forceinline__ void chan_merge_d(double& n, double& mean, double& m2, double nb,
+                                             double mb, double m2b) {
+  if (nb <= 0.0) return;
+  if (n <= 0.0) {
+    n = nb;
+    mean = mb;
+    m2 = m2b;
+    return;
+  }
+  const double tot = n + nb;
+  const double delta = mb - mean;
+  mean += delta * (nb / tot);
+  m2 += m2b + delta * delta * (n * nb / tot);
+  n = tot;
+}
+
+__global__ void __launch_bounds__(1024) group_norm_merge_kernel(float* __restrict__ stats,
+                                                               float eps) {
+  griddep_wait();
+  griddep_launch();
+  const int g = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int records = *reinterpret_cast<const int*>(stats);
+  double n = 0.0, mean = 0.0, m2 = 0.0;
+  for (int r = lane; r < records; r += 32) {
+    const float* rec = stats + 128 + r * 96 + g * 3;
+    chan_merge_d(n, mean, m2, rec[0], rec[1], rec[2]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double nb = __shfl_xor_sync(0xffffffffu, n, o);
+    const double mb = __shfl_xor_sync(0xffffffffu, mean, o);
+    const double m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+    chan_merge_d(n, mean, m2, nb, mb, m2b);
+  }
+  if (lane == 0) {
+    stats[4 + g] = static_cast<float>(mean);
+    stats[36 + g] = rsqrtf(static_cast<float>(m2 / (n > 0.0 ? n : 1.0)) + eps);
+  }
+}
+
+// y = (x - mean[g]) * rstd[g] * w + b in fp32, rounded to bf16, then SiLU (special-function
+// exp2 and reciprocal; the activation's own rounding dominates). Each thread owns one 8-channel
+// vector of every voxel it visits, so its weights, biases and group statistics stay in
+// registers; threads of a CTA cover C / 8 vectors x (256 / (C / 8)) voxels per step.
+__global__ void __launch_bounds__(256)
+    group_norm_apply_kernel(const __nv_bfloat16* __restrict__ x,
+                            const __nv_bfloat16* __restrict__ weight,
+                            const __nv_bfloat16* __restrict__ bias,
+                            __nv_bfloat16* __restrict__ out, int64_t voxels, int C,
+                            const float* __restrict__ mean, const float* __restrict__ rstd,
+                            int apply_silu) {
   griddep_wait();
   griddep_launch();
   const int gs = C / GN_GROUPS;
-  const float* mean = ws + static_cast<int64_t>(parts) * GN_GROUPS;
-  const float* rstd = mean + GN_GROUPS;
-  const int64_t nv = (voxels * C) >> 3;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int c0 = static_cast<int>((i * 8) % C);
-    float f[8], w[8], b[8], o[8];
-    load8(x + i * 8, f);
-    load8(weight + c0, w);
-    load8(bias + c0, b);
+  const int vecs = C >> 3;
+  const int rows = 256 / vecs;
+  const int cv = threadIdx.x % vecs;
+  const int r0 = threadIdx.x / vecs;
+  if (r0 >= rows) return;
+  const int c0 = cv * 8;
+  float w[8], b[8], m[8], rs[8];
+  load8(weight + c0, w);
+  load8(bias + c0, b);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    m[j] = mean[(c0 + j) / gs];
+    rs[j] = rstd[(c0 + j) / gs];
+  }
+  const int64_t step = static_cast<int64_t>(gridDim.x) * rows;
+  for (int64_t v = static_cast<int64_t>(blockIdx.x) * rows + r0; v < voxels; v += step) {
+    float f[8], o[8];
+    load8(x + v * C + c0, f);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int g = (c0 + j) / gs;
-      const float y = (f[j] - mean[g]) * rstd[g] * w[j] + b[j];
-      o[j] = apply_silu ? silu_f32(bf16_round(y)) : y;
+      const float y = (f[j] - m[j]) * rs[j] * w[j] + b[j];
+      o[j] = apply_silu ? silu_fast_f32(bf16_round(y)) : y;
     }
-    store8(out + i * 8, o);
+    store8(out + v * C + c0, o);
   }
 }
 

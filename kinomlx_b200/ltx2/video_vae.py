@@ -145,28 +145,35 @@ class VideoDecoder:
         if variant.norm == "group32":
             self.norm_out = (dev(w["norm_out.weight"]), dev(w["norm_out.bias"]))
         self.conv_out = (dev(w["conv_out.weight"]), dev(w["conv_out.bias"]))
+        self._stats: torch.Tensor | None = None  # GroupNorm statistics from the producing conv
 
     def _norm_silu(self, x: torch.Tensor, params) -> torch.Tensor:
         if self.v.norm == "pixel":
             return ops.pixel_norm(x, self.v.norm_eps, silu=True)
-        return ops.group_norm(x, 32, params[0], params[1], self.v.group_eps, silu=True)
+        # GroupNorm statistics come from the epilogue of the conv that produced x
+        return ops.group_norm_from_stats(x, params[0], params[1], self.v.group_eps, self._stats,
+                                         silu=True)
 
     def decode_features(self, latent: torch.Tensor) -> torch.Tensor:
         """Normalised latent (1, C, F, H, W) -> conv_out output (F', H', W', C_out * p^2) bf16
         (decoder.py:213-255 without the unpatchify)."""
         causal = self.v.causal
+        group = self.v.norm != "pixel"
+        if group and self._stats is None:
+            self._stats = ops.conv_stats_buffer(self.device)
+        st = self._stats if group else None  # every GroupNorm input is the previous conv's output
         x = ops.latent_to_bfhwc(latent.to(self.device, torch.bfloat16).contiguous(), self.std, self.mean)
-        x = ops.conv3d(x, *self.conv_in, causal=causal)
+        x = ops.conv3d(x, *self.conv_in, causal=causal, stats=st)
         for kind, payload in self.stages:
             if kind == "res":
                 for entry in payload:
                     h = self._norm_silu(x, entry.get("norm1"))
-                    h = ops.conv3d(h, *entry["conv1"], causal=causal)
+                    h = ops.conv3d(h, *entry["conv1"], causal=causal, stats=st)
                     h = self._norm_silu(h, entry.get("norm2"))
-                    x = ops.conv3d(h, *entry["conv2"], causal=causal, residual=x, out=x)
+                    x = ops.conv3d(h, *entry["conv2"], causal=causal, residual=x, out=x, stats=st)
             else:
                 wt, bs, stride = payload
-                x = ops.conv3d(x, wt, bs, causal=causal, stride=stride)
+                x = ops.conv3d(x, wt, bs, causal=causal, stride=stride, stats=st)
         x = self._norm_silu(x, self.norm_out)
         return ops.conv3d(x, *self.conv_out, causal=causal)
 

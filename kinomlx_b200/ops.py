@@ -713,9 +713,12 @@ def conv3d(
     stride: tuple[int, int, int] = (1, 1, 1),
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
+    stats: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """3x3x3 conv of channels-last x (F, H, W, Cin) with an (N, 3, 3, 3, Cin) weight; with a
-    depth-to-space `stride` the weight rows must be sub-position-major (n = sub * C' + c)."""
+    depth-to-space `stride` the weight rows must be sub-position-major (n = sub * C' + c).
+    `stats` (a conv_stats_buffer()) receives the GroupNorm(32) statistics of the output for
+    group_norm_from_stats."""
     _need(x, "x")
     _need(weight, "weight")
     if not x.is_contiguous() or not weight.is_contiguous():
@@ -742,6 +745,10 @@ def conv3d(
     args.out = out.data_ptr()
     args.causal = 1 if causal else 0
     args.stride_t, args.stride_h, args.stride_w = st, sh, sw
+    if stats is not None:
+        _need(stats, "stats", torch.float32)
+        args.stats = stats.data_ptr()
+        args.stats_records = (stats.numel() - 128) // 96
     with _timed("conv3d", 2.0 * f * h * w * n * 27 * cin, 2.0 * (x4.numel() + weight.numel() + out.numel())):
         _lib.call("kino_conv3d", ctypes.byref(args), _stream())
     return out
@@ -781,6 +788,26 @@ def group_norm(x: torch.Tensor, groups: int, weight: torch.Tensor, bias: torch.T
     with _timed("norm", 0.0, 8.0 * x.numel()):
         _lib.call("kino_group_norm", _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), voxels, c, eps,
                   int(silu), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream())
+    return out
+
+
+def conv_stats_buffer(device: torch.device | None = None) -> torch.Tensor:
+    """A GroupNorm statistics buffer for conv3d(stats=...) on the current device."""
+    nbytes = int(_lib.load().kino_conv3d_stats_size())
+    return torch.zeros((nbytes // 4,), device=device or torch.device("cuda"), dtype=torch.float32)
+
+
+def group_norm_from_stats(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
+                          stats: torch.Tensor, *, silu: bool = False,
+                          out: torch.Tensor | None = None) -> torch.Tensor:
+    """Affine GroupNorm(32) (+ SiLU) of x, the output of the conv3d that filled `stats`."""
+    _need(x, "x")
+    c = x.shape[-1]
+    if out is None:
+        out = torch.empty_like(x)
+    with _timed("norm", 0.0, 4.0 * x.numel()):
+        _lib.call("kino_group_norm_from_stats", _ptr(x), _ptr(weight), _ptr(bias), _ptr(out),
+                  x.numel() // c, c, eps, int(silu), _ptr(stats), _stream())
     return out
 
 

@@ -127,3 +127,35 @@ def test_config5_shapes_first_stages_run(cuda_device):
     torch.cuda.synchronize()
     assert tuple(out.shape) == (1, 3, 121, 256, 256)
     assert bool(torch.isfinite(out).all())
+
+
+@pytest.mark.parametrize(
+    ("f", "h", "w", "cin", "n", "causal", "stride", "residual"),
+    [
+        (5, 9, 11, 64, 128, True, (1, 1, 1), True),
+        (4, 6, 10, 128, 256, True, (2, 2, 2), False),
+        (3, 20, 36, 64, 1024, False, (1, 1, 1), False),
+        (2, 16, 40, 128, 64, True, (1, 1, 1), False),
+    ],
+)
+def test_group_norm_from_conv_statistics(cuda_device, f, h, w, cin, n, causal, stride, residual):
+    """GroupNorm(32) + SiLU from the statistics the conv's epilogue gathered (Chan-merged count,
+    mean and m2 per group) against the two-pass fp32 GroupNorm of the same conv output (oracle
+    formula): the same bf16 values almost everywhere, per-op bound max relative error 2e-2."""
+    dev = cuda_device
+    x = normal((f, h, w, cin), seed=31, device=dev)
+    wt = normal((n, 3, 3, 3, cin), seed=32, device=dev, std=0.05)
+    bias = normal((n,), seed=33, device=dev)
+    sub = math.prod(stride)
+    co = n // sub
+    res = normal((f, h, w, co), seed=34, device=dev) if residual else None
+    stats = ops.conv_stats_buffer(dev)
+    y = ops.conv3d(x, wt, bias, causal=causal, stride=stride, residual=res, stats=stats)
+    gw = normal((co,), seed=35, device=dev) + 1
+    gb = normal((co,), seed=36, device=dev)
+    got = ops.group_norm_from_stats(y, gw, gb, 1e-6, stats, silu=True)
+    expect = fo.group_norm(y.reshape(1, -1, co).cpu(), 32, gw.cpu(), gb.cpu(), 1e-6)
+    expect = fo.silu(expect).reshape(y.shape)
+    _, max_rel, cosine = _metrics(got, expect)
+    assert max_rel <= 2e-2 and cosine >= 0.9999, (max_rel, cosine)
+    assert (got.cpu() == expect).float().mean() > 0.97
