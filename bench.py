@@ -618,8 +618,9 @@ def run_kernel_case(case: str) -> None:
     """Three launches of one kernel at a workload shape (for ncu captures). `gemm`: the single
     block's fused projection, 4608 x 21504 x 3072, with its in-step epilogue (per-head RMSNorm +
     RoPE on k and q, GELU on the MLP columns); `attention`: the joint attention over 4608 tokens
-    x 24 heads; `conv3d`: a 256-channel causal 3x3x3 VAE conv over 25 x 96 x 128 voxels. Inputs
-    exceed the L2 (weights 132 MB; conv activations 157 MB)."""
+    x 24 heads; `conv3d`: a 256-channel causal 3x3x3 VAE conv over 25 x 96 x 128 voxels;
+    `conv3d_narrow`: a 128-channel one over 49 x 96 x 128 voxels with residual and GroupNorm
+    statistics. Inputs exceed the L2 (weights 132 MB; conv activations 154-157 MB)."""
     from kinomlx_b200 import ops
     from kinomlx_b200.synthetic import normal
 
@@ -643,12 +644,22 @@ def run_kernel_case(case: str) -> None:
         out = torch.empty((1, n, d), device=dev, dtype=torch.bfloat16)
         for _ in range(3):
             ops.attention([q], [k], [v], [out], heads=24)
-    else:
+    elif case == "conv3d":
         x = normal((25, 96, 128, 256), seed=7, device=dev)
         w = normal((256, 3, 3, 3, 256), seed=8, device=dev, std=0.02)
         bias = normal((256,), seed=9, device=dev)
         for _ in range(3):
             ops.conv3d(x, w, bias, causal=True)
+    else:
+        # the decoder's last stage: 128 -> 128 channels at full resolution, with the residual
+        # and the GroupNorm statistics of the next norm
+        x = normal((49, 96, 128, 128), seed=7, device=dev)
+        w = normal((128, 3, 3, 3, 128), seed=8, device=dev, std=0.02)
+        bias = normal((128,), seed=9, device=dev)
+        res = normal((49, 96, 128, 128), seed=10, device=dev)
+        stats = ops.conv_stats_buffer(dev)
+        for _ in range(3):
+            ops.conv3d(x, w, bias, causal=True, residual=res, stats=stats)
     torch.cuda.synchronize()
     ops.device_status()
     print(json.dumps({"kernel_case": case, "ok": True}))
@@ -663,7 +674,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
-    ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d"],
+    ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     args = ap.parse_args()
     if args.kernel_case:

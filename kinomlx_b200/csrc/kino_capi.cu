@@ -207,10 +207,10 @@ kino_status launch_gemm(const void* x, const void* w, void* out, const kino::Gem
   return check_launch("kino_linear");
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int MT>
 kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cudaStream_t stream,
                         int slot) {
-  using L = kino::GemmSmem<BN, STAGES>;
+  using L = kino::ConvSmem<BN, STAGES, MT>;
   CUtensorMap mx, mw;
   const uint64_t dx[4] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W),
                           static_cast<uint64_t>(s0.H), static_cast<uint64_t>(s0.F)};
@@ -226,9 +226,10 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   st = make_map(&mw, a->weight, 2, dw, sw, bw);
   if (st != KINO_OK) return st;
   kino::ConvShape s = s0;
+  s.tiles_m = (s.boxes + MT - 1) / MT;
   s.tiles_n = (s.N + BN - 1) / BN;
   s.num_tiles = s.tiles_m * s.tiles_n;
-  auto kernel = kino::conv3d_tc_kernel<BN, STAGES>;
+  auto kernel = kino::conv3d_tc_kernel<BN, STAGES, MT>;
   st = ensure_smem(kernel, L::TOTAL, slot);
   if (st != KINO_OK) return st;
   const int grid = s.num_tiles < device_sms() ? s.num_tiles : device_sms();
@@ -243,6 +244,46 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   launch_pdl(kernel, dim3(grid), dim3(kino::CONV_THREADS), L::TOTAL, stream,
       mx, mw, static_cast<__nv_bfloat16*>(a->out), s, e);
   return check_launch("kino_conv3d");
+}
+
+template <int BN, int STAGES>
+kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0,
+                            cudaStream_t stream, int slot) {
+  using L = kino::ConvPairSmem<BN, STAGES>;
+  CUtensorMap mx, mw;
+  const uint64_t dx[4] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W),
+                          static_cast<uint64_t>(s0.H), static_cast<uint64_t>(s0.F)};
+  const uint64_t sx[3] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W) * s0.Cin,
+                          static_cast<uint64_t>(s0.H) * s0.W * s0.Cin};
+  const uint32_t bx[4] = {64, static_cast<uint32_t>(s0.tw), static_cast<uint32_t>(s0.th), 1};
+  kino_status st = make_map(&mx, a->x, 4, dx, sx, bx);
+  if (st != KINO_OK) return st;
+  const uint64_t k = 27ull * s0.Cin;
+  const uint64_t dw[2] = {k, static_cast<uint64_t>(s0.N)};
+  const uint64_t sw[1] = {k};
+  const uint32_t bw[2] = {64, static_cast<uint32_t>(BN / 2)};
+  st = make_map(&mw, a->weight, 2, dw, sw, bw);
+  if (st != KINO_OK) return st;
+  kino::ConvShape s = s0;
+  s.tiles_m = (s.boxes + 1) / 2;
+  s.tiles_n = (s.N + BN - 1) / BN;
+  s.num_tiles = s.tiles_m * s.tiles_n;
+  auto kernel = kino::conv3d_2sm_kernel<BN, STAGES>;
+  st = ensure_smem(kernel, L::TOTAL, slot);
+  if (st != KINO_OK) return st;
+  const int max_pairs = device_sms() / 2;
+  const int pairs = s.num_tiles < max_pairs ? s.num_tiles : max_pairs;
+  kino::ConvEpi e;
+  e.bias = static_cast<const __nv_bfloat16*>(a->bias);
+  e.residual = static_cast<const __nv_bfloat16*>(a->residual);
+  e.stats = static_cast<float*>(a->stats);
+  e.group_size = s.Co / kino::GN_GROUPS;
+  if (e.stats != nullptr && 2 * pairs * 4 > a->stats_records)
+    return fail(KINO_EINVAL, "kino_conv3d: statistics buffer holds %lld records, %d needed",
+                (long long)a->stats_records, 2 * pairs * 4);
+  launch_ex(kernel, dim3(2 * pairs), dim3(kino::CONV_THREADS), L::TOTAL, stream, 2, mx, mw,
+            static_cast<__nv_bfloat16*>(a->out), s, e);
+  return check_launch("kino_conv3d (2-SM)");
 }
 
 template <int STAGES>
@@ -878,6 +919,14 @@ kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, in
   return check_launch("kino_timestep_embedding");
 }
 
+#ifndef KINO_CONV_PAIR_BOXES
+#define KINO_CONV_PAIR_BOXES 1
+#endif
+// CTA-pair convolution tiles (M = 256 over two SMs) when enough pair tiles fill the GPU.
+#ifndef KINO_CONV_CTA_PAIRS
+#define KINO_CONV_CTA_PAIRS 1
+#endif
+
 kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
   if (a == nullptr || a->x == nullptr || a->weight == nullptr || a->out == nullptr)
     return fail(KINO_EINVAL, "kino_conv3d: null operand");
@@ -920,7 +969,7 @@ kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
   s.fb = (s.F + s.tf - 1) / s.tf;
   s.hb = (s.H + s.th - 1) / s.th;
   s.wb = (s.W + s.tw - 1) / s.tw;
-  s.tiles_m = s.fb * s.hb * s.wb;
+  s.boxes = s.fb * s.hb * s.wb;
   s.cblocks = s.Cin / 64;
   s.kblocks = 27 * s.cblocks;
   s.pad_front = a->causal ? 2 : 1;
@@ -933,8 +982,20 @@ kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
   s.Ho = s.H * sh;
   s.Wo = s.W * sw;
   cudaStream_t strm = static_cast<cudaStream_t>(stream);
-  if (a->out_channels <= 128) return launch_conv<128, 6>(a, s, strm, 4);
-  return launch_conv<256, 4>(a, s, strm, 5);
+  // CTA pairs (two boxes per tile, M = 256) once they fill a wave of the GPU's SM pairs
+  const int64_t pair_tiles = ((s.boxes + 1) / 2) * ((s.N + 255) / 256);
+  const int64_t narrow_pair_tiles = ((s.boxes + 1) / 2) * ((s.N + 127) / 128);
+  if (a->out_channels <= 128) {
+    if (KINO_CONV_CTA_PAIRS && gemm_pairs_enabled() && narrow_pair_tiles >= device_sms() / 2)
+      return launch_conv_2sm<128, 8>(a, s, strm, 8);
+    // narrow outputs: two boxes per tile share the weight block when that still fills the GPU
+    if (KINO_CONV_PAIR_BOXES && s.boxes >= 2 * device_sms())
+      return launch_conv<128, 4, 2>(a, s, strm, 7);
+    return launch_conv<128, 6, 1>(a, s, strm, 4);
+  }
+  if (KINO_CONV_CTA_PAIRS && gemm_pairs_enabled() && pair_tiles >= device_sms() / 2)
+    return launch_conv_2sm<256, 6>(a, s, strm, 9);
+  return launch_conv<256, 4, 1>(a, s, strm, 5);
 }
 
 kino_status kino_pixel_norm(const void* x, void* out, int64_t voxels, int64_t channels, float eps,

@@ -29,7 +29,8 @@ struct ConvShape {
   int F, H, W, Cin, N;
   int tf, th, tw;
   int fb, hb, wb;
-  int tiles_m, tiles_n, num_tiles, kblocks, cblocks;
+  int boxes;  // fb * hb * wb voxel boxes of 128
+  int tiles_m, tiles_n, num_tiles, kblocks, cblocks;  // an M tile is MT consecutive boxes
   int pad_front;
   int st, sh, sw, drop;  // depth-to-space strides (1,1,1,0 = plain store)
   int Fo, Ho, Wo, Co;    // output geometry
@@ -86,12 +87,113 @@ __device__ __forceinline__ void conv_chunk_stats(const float (&v)[32], bool live
   }
 }
 
-template <int BN, int STAGES>
+// Epilogue of one 128-voxel box of an M tile: thread `m` (its voxel) reads BN accumulator
+// columns at taddr, adds bias and residual, stores (plain or depth-to-space) and gathers the
+// GroupNorm statistics of what it stored.
+template <int BN>
+__device__ __forceinline__ void conv_store_box(const ConvShape& s, const ConvEpi& e,
+                                               __nv_bfloat16* __restrict__ out, int box, int nt,
+                                               uint32_t taddr, int m, uint32_t lane,
+                                               float& gn_n, float& gn_mean, float& gn_m2) {
+  const int box_rows = s.th * s.tw;
+  const int cpo = s.Co;  // channels per output voxel
+  const int wbi = box % s.wb;
+  const int hbi = (box / s.wb) % s.hb;
+  const int fbi = box / (s.wb * s.hb);
+  const int wi = m % s.tw, hi = (m / s.tw) % s.th, fi = m / box_rows;
+  const int f = fbi * s.tf + fi, h = hbi * s.th + hi, w = wbi * s.tw + wi;
+  const bool valid = f < s.F && h < s.H && w < s.W;
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld32(taddr + c * 32, r);
+    tmem_wait_ld();
+    const int n0 = nt * BN + c * 32;
+    if (n0 >= s.N) continue;  // warp-uniform
+    // destination voxel and channel offset of this 32-column chunk
+    const int sub = n0 / cpo;
+    const int ch0 = n0 - sub * cpo;
+    const int a = sub / (s.sh * s.sw), bb = (sub / s.sw) % s.sh, ee = sub % s.sw;
+    const int fo = f * s.st + a - s.drop, ho = h * s.sh + bb, wo = w * s.sw + ee;
+    const bool live = valid && fo >= 0 && fo < s.Fo;
+    const int64_t off =
+        live ? ((static_cast<int64_t>(fo) * s.Ho + ho) * s.Wo + wo) * cpo + ch0 : 0;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = bf16_round(__uint_as_float(r[j]));
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      if (n0 + g * 8 < s.N) {
+        float add[8];
+        if (e.bias != nullptr) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(e.bias + n0 + g * 8);
+          const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 fb = unpack_bf16x2(w4[q]);
+            add[2 * q] = fb.x;
+            add[2 * q + 1] = fb.y;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[g * 8 + j] = bf16_round(v[g * 8 + j] + add[j]);
+        }
+        if (e.residual != nullptr && live) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(e.residual + off + g * 8);
+          const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 fr = unpack_bf16x2(w4[q]);
+            v[g * 8 + 2 * q] += fr.x;
+            v[g * 8 + 2 * q + 1] += fr.y;
+          }
+        }
+        uint4 o;
+        o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
+        o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
+        o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
+        o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
+        if (live) *reinterpret_cast<uint4*>(out + off + g * 8) = o;
+      }
+    }
+    if (e.stats != nullptr) {
+      // the stored (bf16) values of this chunk, group by group: the warp's 32 voxels give
+      // one (count, mean, m2) per group, merged into the lane that owns the group
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
+      const int first = ch0 / e.group_size;
+      switch (e.group_size) {
+        case 1: conv_chunk_stats<1>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+        case 2: conv_chunk_stats<2>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+        case 4: conv_chunk_stats<4>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+        case 8: conv_chunk_stats<8>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+        case 16: conv_chunk_stats<16>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+        default: conv_chunk_stats<32>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
+      }
+    }
+  }
+}
+
+// Shared memory of a conv tile of MT voxel boxes: per stage MT A boxes (128 x 64 each) and one
+// weight block (BN x 64) that all of them use.
+template <int BN, int STAGES, int MT>
+struct ConvSmem {
+  static constexpr int A1_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int A_BYTES = MT * A1_BYTES;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int TOTAL = TILE_BYTES + BAR_BYTES + 1024;
+};
+
+// MT > 1 (narrow outputs, BN = 128): MT boxes share each weight block, so the tile's operand
+// traffic per tensor-core cycle falls from 2 to (MT + 1) / MT blocks of 16 KB per 128 x 128 x 64.
+template <int BN, int STAGES, int MT>
 __global__ void __launch_bounds__(CONV_THREADS, 1)
     conv3d_tc_kernel(const __grid_constant__ CUtensorMap map_x,
                      const __grid_constant__ CUtensorMap map_w, __nv_bfloat16* __restrict__ out,
                      const ConvShape s, const ConvEpi e) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = ConvSmem<BN, STAGES, MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -124,7 +226,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   }
   griddep_wait();  // the previous kernel has finished with its memory and tensor memory
   if (warp == 1) {
-    tmem_alloc(tmem_base_slot, 2 * BN);
+    tmem_alloc(tmem_base_slot, 2 * MT * BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -142,10 +244,6 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x) {
         const int mt = t % s.tiles_m;
         const int nt = t / s.tiles_m;
-        const int wbi = mt % s.wb;
-        const int hbi = (mt / s.wb) % s.hb;
-        const int fbi = mt / (s.wb * s.hb);
-        const int f0 = fbi * s.tf, h0 = hbi * s.th, w0 = wbi * s.tw;
         for (int kb = 0; kb < s.kblocks; ++kb) {
           const int tap = kb / s.cblocks;
           const int cb = kb - tap * s.cblocks;
@@ -154,11 +252,21 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           uint8_t* sa = smem + stage * L::STAGE_BYTES;
           uint8_t* sb = sa + L::A_BYTES;
           mbar_expect_tx(&full[stage], L::STAGE_BYTES);
-          for (int fi = 0; fi < s.tf; ++fi) {
-            int fs = f0 + fi + kt - s.pad_front;
-            fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
-            tma_load_4d(sa + fi * box_rows * 128, &map_x, &full[stage], cb * 64, w0 + kw - 1,
-                        h0 + kh - 1, fs);
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            const int box = mt * MT + i;
+            const int wbi = box % s.wb;
+            const int hbi = (box / s.wb) % s.hb;
+            const int fbi = box / (s.wb * s.hb);
+            // a box past the last one loads zero fill (width coordinate out of range)
+            const int f0 = fbi * s.tf, h0 = hbi * s.th;
+            const int w0 = box < s.boxes ? wbi * s.tw : s.W + 64;
+            for (int fi = 0; fi < s.tf; ++fi) {
+              int fs = f0 + fi + kt - s.pad_front;
+              fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
+              tma_load_4d(sa + i * L::A1_BYTES + fi * box_rows * 128, &map_x, &full[stage],
+                          cb * 64, w0 + kw - 1, h0 + kh - 1, fs);
+            }
           }
           tma_load_2d(sb, &map_w, &full[stage], kb * GEMM_BK, nt * BN);
           ++issued;
@@ -192,7 +300,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * MT * BN;
         bool ok = true;
         for (int kb = 0; kb < s.kblocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
@@ -203,9 +311,12 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
           const uint32_t sb = sa + L::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
-            umma_bf16(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32), idesc,
-                      (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int i = 0; i < MT; ++i) {
+#pragma unroll
+            for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+              umma_bf16(d_tmem + i * BN, sdesc_k128(sa + i * L::A1_BYTES + kk * 32),
+                        sdesc_k128(sb + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -224,89 +335,22 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   } else {
     const int quarter = warp & 3;
     const int m = quarter * 32 + static_cast<int>(lane);
-    const int cpo = s.Co;  // channels per output voxel
     float gn_n = 0.0f, gn_mean = 0.0f, gn_m2 = 0.0f;  // statistics of group `lane`
     int local = 0;
     for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
       const int mt = t % s.tiles_m;
       const int nt = t / s.tiles_m;
-      const int wbi = mt % s.wb;
-      const int hbi = (mt / s.wb) % s.hb;
-      const int fbi = mt / (s.wb * s.hb);
-      const int wi = m % s.tw, hi = (m / s.tw) % s.th, fi = m / box_rows;
-      const int f = fbi * s.tf + fi, h = hbi * s.th + hi, w = wbi * s.tw + wi;
-      const bool valid = f < s.F && h < s.H && w < s.W;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((quarter * 32) << 16) + acc * BN + c * 32, r);
-        tmem_wait_ld();
-        const int n0 = nt * BN + c * 32;
-        if (n0 >= s.N) continue;  // warp-uniform
-        // destination voxel and channel offset of this 32-column chunk
-        const int sub = n0 / cpo;
-        const int ch0 = n0 - sub * cpo;
-        const int a = sub / (s.sh * s.sw), bb = (sub / s.sw) % s.sh, ee = sub % s.sw;
-        const int fo = f * s.st + a - s.drop, ho = h * s.sh + bb, wo = w * s.sw + ee;
-        const bool live = valid && fo >= 0 && fo < s.Fo;
-        const int64_t off =
-            live ? ((static_cast<int64_t>(fo) * s.Ho + ho) * s.Wo + wo) * cpo + ch0 : 0;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = bf16_round(__uint_as_float(r[j]));
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          if (n0 + g * 8 < s.N) {
-            float add[8];
-            if (e.bias != nullptr) {
-              const uint4 raw = *reinterpret_cast<const uint4*>(e.bias + n0 + g * 8);
-              const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float2 fb = unpack_bf16x2(w4[q]);
-                add[2 * q] = fb.x;
-                add[2 * q + 1] = fb.y;
-              }
-#pragma unroll
-              for (int j = 0; j < 8; ++j) v[g * 8 + j] = bf16_round(v[g * 8 + j] + add[j]);
-            }
-            if (e.residual != nullptr && live) {
-              const uint4 raw = *reinterpret_cast<const uint4*>(e.residual + off + g * 8);
-              const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float2 fr = unpack_bf16x2(w4[q]);
-                v[g * 8 + 2 * q] += fr.x;
-                v[g * 8 + 2 * q + 1] += fr.y;
-              }
-            }
-            uint4 o;
-            o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-            o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-            o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-            o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-            if (live) *reinterpret_cast<uint4*>(out + off + g * 8) = o;
-          }
-        }
-        if (e.stats != nullptr) {
-          // the stored (bf16) values of this chunk, group by group: the warp's 32 voxels give
-          // one (count, mean, m2) per group, merged into the lane that owns the group
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
-          const int first = ch0 / e.group_size;
-          switch (e.group_size) {
-            case 1: conv_chunk_stats<1>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
-            case 2: conv_chunk_stats<2>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
-            case 4: conv_chunk_stats<4>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
-            case 8: conv_chunk_stats<8>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
-            case 16: conv_chunk_stats<16>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
-            default: conv_chunk_stats<32>(v, live, first, lane, gn_n, gn_mean, gn_m2); break;
-          }
-        }
+      for (int bi = 0; bi < MT; ++bi) {
+        const int box = mt * MT + bi;
+        if (box >= s.boxes) break;  // warp-uniform
+        conv_store_box<BN>(s, e, out, box, nt,
+                           tmem_base + ((quarter * 32) << 16) + acc * MT * BN + bi * BN, m, lane,
+                           gn_n, gn_mean, gn_m2);
       }
       tc_fence_before();
       __syncwarp();
@@ -326,7 +370,203 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    tmem_dealloc(tmem_base, 2 * MT * BN);
+  }
+}
+
+// ----------------------------------------------------------------------------- CTA pairs
+// The same convolution on CTA pairs (cluster of 2): a pair tile is two consecutive voxel boxes
+// (one per CTA, M = 256) by BN output channels, issued by the even CTA as
+// tcgen05.mma.cta_group::2. Each CTA loads its own box and BN / 2 of the weight rows, so the
+// per-SM operand traffic per tensor-core cycle is three quarters (BN = 256) or a little over
+// half (BN = 128) of the single-CTA tile's. TMA loads complete on the even CTA's barriers (no
+// multicast loads); MMA completion is committed to both CTAs; each CTA stores its own box.
+template <int BN, int STAGES>
+struct ConvPairSmem {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;      // 16 KB: this CTA's box
+  static constexpr int B_BYTES = (BN / 2) * GEMM_BK * 2;     // this CTA's half of the weights
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
+  static constexpr int TOTAL = TILE_BYTES + BAR_BYTES + 1024;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(CONV_THREADS, 1)
+    conv3d_2sm_kernel(const __grid_constant__ CUtensorMap map_x,
+                      const __grid_constant__ CUtensorMap map_w, __nv_bfloat16* __restrict__ out,
+                      const ConvShape s, const ConvEpi e) {
+  using L = ConvPairSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+
+  const int warp = warp_id();
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_rank();  // 0: leader (issues the MMAs), 1: peer
+  const int pair = blockIdx.x >> 1;
+  const int pairs = gridDim.x >> 1;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 8);  // the 4 epilogue warps of both CTAs
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&map_x);
+    tma_prefetch(&map_w);
+  }
+  griddep_wait();  // the previous kernel has finished with its memory and tensor memory
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_base_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive or complete_tx
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+  griddep_launch();
+  const int box_rows = s.th * s.tw;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = pair; t < s.num_tiles; t += pairs) {
+        const int mt = t % s.tiles_m;
+        const int nt = t / s.tiles_m;
+        const int box = mt * 2 + static_cast<int>(rank);
+        const int wbi = box % s.wb;
+        const int hbi = (box / s.wb) % s.hb;
+        const int fbi = box / (s.wb * s.hb);
+        // a box past the last one loads zero fill (width coordinate out of range)
+        const int f0 = fbi * s.tf, h0 = hbi * s.th;
+        const int w0 = box < s.boxes ? wbi * s.tw : s.W + 64;
+        for (int kb = 0; kb < s.kblocks; ++kb) {
+          const int tap = kb / s.cblocks;
+          const int cb = kb - tap * s.cblocks;
+          const int kt = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
+          uint8_t* sa = smem + stage * L::STAGE_BYTES;
+          uint8_t* sb = sa + L::A_BYTES;
+          const uint32_t leader_full = smem_u32(&full[stage]) & kPairLeaderMask;
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
+          for (int fi = 0; fi < s.tf; ++fi) {
+            int fs = f0 + fi + kt - s.pad_front;
+            fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
+            tma_load_4d_pair(sa + fi * box_rows * 128, &map_x, leader_full, cb * 64, w0 + kw - 1,
+                             h0 + kh - 1, fs);
+          }
+          tma_load_2d_pair(sb, &map_w, leader_full, kb * GEMM_BK,
+                           nt * BN + static_cast<int>(rank) * (BN / 2));
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      // After a timeout, give loads still in flight a bounded moment to land.
+      if (*abort_flag && issued > 0) {
+        const uint64_t t0 = global_ns();
+        while (global_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = idesc_bf16(256, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int t = pair; t < s.num_tiles; t += pairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < s.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
+          const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+            umma_bf16_pair(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32), idesc,
+                           (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&tfull[acc], 0x3);
+      }
+      umma_commit_pair(drain, 0x1);
+      const uint64_t t0 = global_ns();
+      while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 200000000ull) {
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int m = quarter * 32 + static_cast<int>(lane);
+    const uint32_t leader_tempty0 = cluster_addr(smem_u32(&tempty[0]), 0);
+    float gn_n = 0.0f, gn_mean = 0.0f, gn_m2 = 0.0f;  // statistics of group `lane`
+    int local = 0;
+    for (int t = pair; t < s.num_tiles; t += pairs, ++local) {
+      const int mt = t % s.tiles_m;
+      const int nt = t / s.tiles_m;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int box = mt * 2 + static_cast<int>(rank);
+      if (box < s.boxes)  // warp-uniform
+        conv_store_box<BN>(s, e, out, box, nt, tmem_base + ((quarter * 32) << 16) + acc * BN, m,
+                           lane, gn_n, gn_mean, gn_m2);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
+    }
+    if (e.stats != nullptr) {
+      float* rec = e.stats + GN_STATS_RECORDS + (blockIdx.x * 4 + quarter) * 96 + lane * 3;
+      rec[0] = gn_n;
+      rec[1] = gn_mean;
+      rec[2] = gn_m2;
+      if (blockIdx.x == 0 && warp == 2 && lane == 0)
+        *reinterpret_cast<int*>(e.stats) = static_cast<int>(gridDim.x) * 4;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the leader's MMAs have drained; neither CTA's memory is in use any more
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
   }
 }
 

@@ -38,6 +38,14 @@ def _metrics(out, expect):
         (4, 6, 10, 128, 256, True, (2, 2, 2), False),
         (3, 20, 36, 64, 128, False, (1, 2, 2), False),
         (3, 12, 8, 64, 64, False, (2, 1, 1), False),
+        # enough voxel boxes for a wave of CTA pairs: M = 256 tiles over two SMs, each SM loading
+        # its own box and half of the weight rows (an odd box count leaves the odd CTA of the
+        # last pair on zero fill; 96 and 320 outputs leave part of a half-block past the end)
+        (8, 64, 128, 64, 128, True, (1, 1, 1), True),
+        (11, 36, 80, 128, 64, False, (1, 1, 1), False),
+        (9, 40, 72, 64, 256, True, (1, 1, 1), True),
+        (7, 44, 76, 128, 96, False, (1, 1, 1), False),
+        (6, 40, 64, 64, 320, True, (1, 1, 1), False),
     ],
 )
 def test_conv3d_matches_oracle(cuda_device, f, h, w, cin, n, causal, stride, residual):
@@ -136,6 +144,7 @@ def test_config5_shapes_first_stages_run(cuda_device):
         (4, 6, 10, 128, 256, True, (2, 2, 2), False),
         (3, 20, 36, 64, 1024, False, (1, 1, 1), False),
         (2, 16, 40, 128, 64, True, (1, 1, 1), False),
+        (11, 36, 80, 64, 128, True, (1, 1, 1), True),
     ],
 )
 def test_group_norm_from_conv_statistics(cuda_device, f, h, w, cin, n, causal, stride, residual):
