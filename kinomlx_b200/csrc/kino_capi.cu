@@ -369,6 +369,23 @@ int gemm_tiling(int64_t batch, int64_t m, int64_t n) {
   return e1 <= e3 ? 2 : 3;
 }
 
+// Grid of the GroupNorm apply pass: one resident wave at most, so that the grid-stride loop
+// gives every CTA the same share.
+int64_t gn_apply_blocks(int64_t voxels, int64_t channels) {
+  static int resident = 0;
+  if (resident == 0) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kino::group_norm_apply_kernel, 256,
+                                                      0) != cudaSuccess || per_sm < 1)
+      per_sm = 2;
+    resident = per_sm;
+  }
+  const int64_t rows_per_cta = 256 / (channels / 8);
+  const int64_t blocks = (voxels + rows_per_cta - 1) / rows_per_cta;
+  const int64_t cap = static_cast<int64_t>(device_sms()) * resident;
+  return blocks < cap ? blocks : cap;
+}
+
 int gn_parts(int64_t voxels) {
   int64_t p = (voxels + 31) / 32;
   return static_cast<int>(p < 592 ? (p < 1 ? 1 : p) : 592);
@@ -1039,9 +1056,7 @@ kino_status kino_group_norm(const void* x, const void* weight, const void* bias,
                                                                        pass);
     launch_pdl(kino::group_norm_finalize_kernel, dim3(1), dim3(32), 0, s, ws, parts, count, eps, pass);
   }
-  const int64_t rows_per_cta = 256 / (channels / 8);
-  int64_t blocks = (voxels + rows_per_cta - 1) / rows_per_cta;
-  if (blocks > static_cast<int64_t>(device_sms()) * 8) blocks = static_cast<int64_t>(device_sms()) * 8;
+  const int64_t blocks = gn_apply_blocks(voxels, channels);
   launch_pdl(kino::group_norm_apply_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
       xb, static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(bias),
       static_cast<__nv_bfloat16*>(out), voxels, c, ws + static_cast<int64_t>(parts) * kino::GN_GROUPS,
@@ -1065,10 +1080,8 @@ kino_status kino_group_norm_from_stats(const void* x, const void* weight, const 
                 "kino_group_norm_from_stats: 32 <= channels <= 2048 in 32 groups, aligned operands");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* st = static_cast<float*>(stats);
-  launch_pdl(kino::group_norm_merge_kernel, dim3(1), dim3(1024), 0, s, st, eps);
-  const int64_t rows_per_cta = 256 / (channels / 8);
-  int64_t blocks = (voxels + rows_per_cta - 1) / rows_per_cta;
-  if (blocks > static_cast<int64_t>(device_sms()) * 8) blocks = static_cast<int64_t>(device_sms()) * 8;
+  launch_pdl(kino::group_norm_merge_kernel, dim3(kino::GN_GROUPS), dim3(kino::GN_MERGE_THREADS), 0, s, st, eps);
+  const int64_t blocks = gn_apply_blocks(voxels, channels);
   launch_pdl(kino::group_norm_apply_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, s,
              static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
              static_cast<const __nv_bfloat16*>(bias), static_cast<__nv_bfloat16*>(out), voxels,

@@ -117,54 +117,98 @@ __global__ void group_norm_finalize_kernel(float* __restrict__ ws, int parts, in
   }
 }
 
-// Statistics from the producing conv's epilogue (see ConvEpi::stats): merge the records of
-// each group (Chan, Golub & LeVeque, in double precision) into mean and rstd. One warp per
-// group (1024 threads): lanes merge strided records, then a shuffle tree merges the lanes.
-__device__ __forceinline__ void chan_merge_d(double& n, double& mean, double& m2, double nb,
-                                             double mb, double m2b) {
-  if (nb <= 0.0) return;
-  if (n <= 0.0) {
-    n = nb;
-    mean = mb;
-    m2 = m2b;
-    return;
-  }
-  const double tot = n + nb;
-  const double delta = mb - mean;
-  mean += delta * (nb / tot);
-  m2 += m2b + delta * delta * (n * nb / tot);
-  n = tot;
+// Statistics from the producing conv's epilogue (see ConvEpi::stats): combine the records of
+// each group into mean and rstd. One CTA of GN_MERGE_THREADS per group; each thread loads its
+// few records at once (their latencies overlap), then two block reductions with no division
+// inside the loops: the group's count and mean from sum(n_i) and sum(n_i * mean_i), then
+// m2 = sum(m2_i + n_i * (mean_i - mean)^2), the exact pooled sum of squared deviations about
+// the group mean (every term non-negative, so fp32 sums stay accurate).
+constexpr int GN_MERGE_THREADS = 256;
+
+__device__ __forceinline__ float gn_block_sum(float v, float* red) {
+  v = warp_sum_f(v);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float t = (threadIdx.x & 31) < (GN_MERGE_THREADS / 32) ? red[threadIdx.x & 31] : 0.0f;
+  t = warp_sum_f(t);
+  __syncthreads();  // red is reused by the next reduction
+  return t;
 }
 
-__global__ void __launch_bounds__(1024) group_norm_merge_kernel(float* __restrict__ stats,
-                                                               float eps) {
+__global__ void __launch_bounds__(GN_MERGE_THREADS) group_norm_merge_kernel(
+    float* __restrict__ stats, float eps) {
+  __shared__ float red[GN_MERGE_THREADS / 32];
   griddep_wait();
   griddep_launch();
-  const int g = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+  const int g = blockIdx.x;
   const int records = *reinterpret_cast<const int*>(stats);
-  double n = 0.0, mean = 0.0, m2 = 0.0;
-  for (int r = lane; r < records; r += 32) {
-    const float* rec = stats + 128 + r * 96 + g * 3;
-    chan_merge_d(n, mean, m2, rec[0], rec[1], rec[2]);
-  }
+  const float* base = stats + 128 + g * 3;
+  constexpr int PER = 4;  // records per thread held in registers (more are read in a loop)
+  float rn[PER], rm[PER];
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const double nb = __shfl_xor_sync(0xffffffffu, n, o);
-    const double mb = __shfl_xor_sync(0xffffffffu, mean, o);
-    const double m2b = __shfl_xor_sync(0xffffffffu, m2, o);
-    chan_merge_d(n, mean, m2, nb, mb, m2b);
+  for (int i = 0; i < PER; ++i) {
+    const int r = threadIdx.x + GN_MERGE_THREADS * i;
+    const bool ok = r < records;
+    rn[i] = ok ? base[r * 96] : 0.0f;
+    rm[i] = ok ? base[r * 96 + 1] : 0.0f;
   }
-  if (lane == 0) {
-    stats[4 + g] = static_cast<float>(mean);
-    stats[36 + g] = rsqrtf(static_cast<float>(m2 / (n > 0.0 ? n : 1.0)) + eps);
+  float n = 0.0f, s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    n += rn[i];
+    s = fmaf(rn[i], rm[i], s);
+  }
+  for (int r = threadIdx.x + GN_MERGE_THREADS * PER; r < records; r += GN_MERGE_THREADS) {
+    n += base[r * 96];
+    s = fmaf(base[r * 96], base[r * 96 + 1], s);
+  }
+  n = gn_block_sum(n, red);
+  s = gn_block_sum(s, red);
+  const float count = n > 0.0f ? n : 1.0f;
+  const float mean = s / count;
+  float m2 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int r = threadIdx.x + GN_MERGE_THREADS * i;
+    const float d = rm[i] - mean;
+    m2 += fmaf(rn[i] * d, d, r < records ? base[r * 96 + 2] : 0.0f);
+  }
+  for (int r = threadIdx.x + GN_MERGE_THREADS * PER; r < records; r += GN_MERGE_THREADS) {
+    const float* rec = base + r * 96;
+    const float d = rec[1] - mean;
+    m2 += fmaf(rec[0] * d, d, rec[2]);
+  }
+  m2 = gn_block_sum(m2, red);
+  if (threadIdx.x == 0) {
+    stats[4 + g] = mean;
+    stats[36 + g] = rsqrtf(m2 / count + eps);
   }
 }
 
 // y = (x - mean[g]) * rstd[g] * w + b in fp32, rounded to bf16, then SiLU (special-function
 // exp2 and reciprocal; the activation's own rounding dominates). Each thread owns one 8-channel
 // vector of every voxel it visits, so its weights, biases and group statistics stay in
-// registers; threads of a CTA cover C / 8 vectors x (256 / (C / 8)) voxels per step.
+// registers; threads of a CTA cover C / 8 vectors x (256 / (C / 8)) voxels per step. The pass
+// is HBM-bound: each thread keeps four 16-byte loads in flight (voxels v, v + step, ...) so that
+// the bytes in flight per SM cover the memory latency at the occupancy the registers allow.
+__device__ __forceinline__ void gn_apply8(const uint4 raw, const float (&m)[8],
+                                          const float (&rs)[8], const float (&w)[8],
+                                          const float (&b)[8], int apply_silu,
+                                          __nv_bfloat16* dst) {
+  const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = unpack_bf16x2(u[i]);
+    const float y0 = (t.x - m[2 * i]) * rs[2 * i] * w[2 * i] + b[2 * i];
+    const float y1 = (t.y - m[2 * i + 1]) * rs[2 * i + 1] * w[2 * i + 1] + b[2 * i + 1];
+    o[2 * i] = apply_silu ? silu_fast_f32(bf16_round(y0)) : y0;
+    o[2 * i + 1] = apply_silu ? silu_fast_f32(bf16_round(y1)) : y1;
+  }
+  store8(dst, o);
+}
+
 __global__ void __launch_bounds__(256)
     group_norm_apply_kernel(const __nv_bfloat16* __restrict__ x,
                             const __nv_bfloat16* __restrict__ weight,
@@ -190,16 +234,18 @@ __global__ void __launch_bounds__(256)
     rs[j] = rstd[(c0 + j) / gs];
   }
   const int64_t step = static_cast<int64_t>(gridDim.x) * rows;
-  for (int64_t v = static_cast<int64_t>(blockIdx.x) * rows + r0; v < voxels; v += step) {
-    float f[8], o[8];
-    load8(x + v * C + c0, f);
+  int64_t v = static_cast<int64_t>(blockIdx.x) * rows + r0;
+  for (; v + 3 * step < voxels; v += 4 * step) {
+    uint4 raw[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float y = (f[j] - m[j]) * rs[j] * w[j] + b[j];
-      o[j] = apply_silu ? silu_fast_f32(bf16_round(y)) : y;
-    }
-    store8(out + v * C + c0, o);
+    for (int u = 0; u < 4; ++u)
+      raw[u] = __ldg(reinterpret_cast<const uint4*>(x + (v + u * step) * C + c0));
+#pragma unroll
+    for (int u = 0; u < 4; ++u) gn_apply8(raw[u], m, rs, w, b, apply_silu, out + (v + u * step) * C + c0);
   }
+  for (; v < voxels; v += step)
+    gn_apply8(__ldg(reinterpret_cast<const uint4*>(x + v * C + c0)), m, rs, w, b, apply_silu,
+              out + v * C + c0);
 }
 
 // ----------------------------------------------------------------------------- latent -> BFHWC
