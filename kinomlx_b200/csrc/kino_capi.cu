@@ -246,10 +246,10 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   return check_launch("kino_conv3d");
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KSUB>
 kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0,
                             cudaStream_t stream, int slot) {
-  using L = kino::ConvPairSmem<BN, STAGES>;
+  using L = kino::ConvPairSmem<BN, STAGES, KSUB>;
   CUtensorMap mx, mw;
   const uint64_t dx[4] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W),
                           static_cast<uint64_t>(s0.H), static_cast<uint64_t>(s0.F)};
@@ -268,7 +268,7 @@ kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0
   s.tiles_m = (s.boxes + 1) / 2;
   s.tiles_n = (s.N + BN - 1) / BN;
   s.num_tiles = s.tiles_m * s.tiles_n;
-  auto kernel = kino::conv3d_2sm_kernel<BN, STAGES>;
+  auto kernel = kino::conv3d_2sm_kernel<BN, STAGES, KSUB>;
   st = ensure_smem(kernel, L::TOTAL, slot);
   if (st != KINO_OK) return st;
   const int max_pairs = device_sms() / 2;
@@ -281,7 +281,7 @@ kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0
   if (e.stats != nullptr && 2 * pairs * 4 > a->stats_records)
     return fail(KINO_EINVAL, "kino_conv3d: statistics buffer holds %lld records, %d needed",
                 (long long)a->stats_records, 2 * pairs * 4);
-  launch_ex(kernel, dim3(2 * pairs), dim3(kino::CONV_THREADS), L::TOTAL, stream, 2, mx, mw,
+  launch_ex(kernel, dim3(2 * pairs), dim3(kino::CONV_PAIR_THREADS), L::TOTAL, stream, 2, mx, mw,
             static_cast<__nv_bfloat16*>(a->out), s, e);
   return check_launch("kino_conv3d (2-SM)");
 }
@@ -939,9 +939,23 @@ kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, in
 #ifndef KINO_CONV_PAIR_BOXES
 #define KINO_CONV_PAIR_BOXES 1
 #endif
-// CTA-pair convolution tiles (M = 256 over two SMs) when enough pair tiles fill the GPU.
+// CTA-pair convolution tiles (M = 256 over two SMs) when enough pair tiles fill the GPU:
+// pipeline stages x K blocks per stage (24 KB per block and CTA for 128 output channels,
+// 32 KB for 256).
 #ifndef KINO_CONV_CTA_PAIRS
 #define KINO_CONV_CTA_PAIRS 1
+#endif
+#ifndef KINO_CONV_NARROW_STAGES
+#define KINO_CONV_NARROW_STAGES 2
+#endif
+#ifndef KINO_CONV_NARROW_KSUB
+#define KINO_CONV_NARROW_KSUB 4
+#endif
+#ifndef KINO_CONV_WIDE_STAGES
+#define KINO_CONV_WIDE_STAGES 6
+#endif
+#ifndef KINO_CONV_WIDE_KSUB
+#define KINO_CONV_WIDE_KSUB 1
 #endif
 
 kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
@@ -1004,14 +1018,14 @@ kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
   const int64_t narrow_pair_tiles = ((s.boxes + 1) / 2) * ((s.N + 127) / 128);
   if (a->out_channels <= 128) {
     if (KINO_CONV_CTA_PAIRS && gemm_pairs_enabled() && narrow_pair_tiles >= device_sms() / 2)
-      return launch_conv_2sm<128, 8>(a, s, strm, 8);
+      return launch_conv_2sm<128, KINO_CONV_NARROW_STAGES, KINO_CONV_NARROW_KSUB>(a, s, strm, 8);
     // narrow outputs: two boxes per tile share the weight block when that still fills the GPU
     if (KINO_CONV_PAIR_BOXES && s.boxes >= 2 * device_sms())
       return launch_conv<128, 4, 2>(a, s, strm, 7);
     return launch_conv<128, 6, 1>(a, s, strm, 4);
   }
   if (KINO_CONV_CTA_PAIRS && gemm_pairs_enabled() && pair_tiles >= device_sms() / 2)
-    return launch_conv_2sm<256, 6>(a, s, strm, 9);
+    return launch_conv_2sm<256, KINO_CONV_WIDE_STAGES, KINO_CONV_WIDE_KSUB>(a, s, strm, 9);
   return launch_conv<256, 4, 1>(a, s, strm, 5);
 }
 
@@ -1065,6 +1079,7 @@ kino_status kino_group_norm(const void* x, const void* weight, const void* bias,
 }
 
 int64_t kino_conv3d_stats_size(void) {
+  // one record per TMEM lane quarter of every CTA
   return (kino::GN_STATS_RECORDS + 4 * static_cast<int64_t>(device_sms()) * 96) * 4;
 }
 

@@ -42,7 +42,8 @@ struct ConvEpi {
   // GroupNorm(32) statistics of the stored output (the next layer's norm), or null: every
   // epilogue warp keeps, in lane g, the count, mean and sum of squared deviations of group g
   // over the values it stored (merged chunk by chunk with Chan's pairwise formula) and writes
-  // them as record (CTA * 4 + lane quarter); CTA 0 writes the record count into the header.
+  // them as one record per lane quarter (CTA * 4 + quarter); CTA 0 writes the record count
+  // into the header.
   float* stats;
   int group_size;  // output channels per group (output channels / 32)
 };
@@ -87,14 +88,15 @@ __device__ __forceinline__ void conv_chunk_stats(const float (&v)[32], bool live
   }
 }
 
-// Epilogue of one 128-voxel box of an M tile: thread `m` (its voxel) reads BN accumulator
-// columns at taddr, adds bias and residual, stores (plain or depth-to-space) and gathers the
-// GroupNorm statistics of what it stored.
+// Epilogue of one 128-voxel box of an M tile: thread `m` (its voxel) reads the accumulator
+// columns of 32-column chunks [c_begin, c_end) at taddr, adds bias and residual, stores (plain or
+// depth-to-space) and gathers the GroupNorm statistics of what it stored.
 template <int BN>
 __device__ __forceinline__ void conv_store_box(const ConvShape& s, const ConvEpi& e,
                                                __nv_bfloat16* __restrict__ out, int box, int nt,
                                                uint32_t taddr, int m, uint32_t lane,
-                                               float& gn_n, float& gn_mean, float& gn_m2) {
+                                               float& gn_n, float& gn_mean, float& gn_m2,
+                                               int c_begin = 0, int c_end = BN / 32) {
   const int box_rows = s.th * s.tw;
   const int cpo = s.Co;  // channels per output voxel
   const int wbi = box % s.wb;
@@ -104,12 +106,9 @@ __device__ __forceinline__ void conv_store_box(const ConvShape& s, const ConvEpi
   const int f = fbi * s.tf + fi, h = hbi * s.th + hi, w = wbi * s.tw + wi;
   const bool valid = f < s.F && h < s.H && w < s.W;
 #pragma unroll 1
-  for (int c = 0; c < BN / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld32(taddr + c * 32, r);
-    tmem_wait_ld();
+  for (int c = c_begin; c < c_end; ++c) {
     const int n0 = nt * BN + c * 32;
-    if (n0 >= s.N) continue;  // warp-uniform
+    if (n0 >= s.N) break;  // warp-uniform
     // destination voxel and channel offset of this 32-column chunk
     const int sub = n0 / cpo;
     const int ch0 = n0 - sub * cpo;
@@ -118,6 +117,17 @@ __device__ __forceinline__ void conv_store_box(const ConvShape& s, const ConvEpi
     const bool live = valid && fo >= 0 && fo < s.Fo;
     const int64_t off =
         live ? ((static_cast<int64_t>(fo) * s.Ho + ho) * s.Wo + wo) * cpo + ch0 : 0;
+    // the chunk's residual loads go out before the accumulator read, so their latencies overlap
+    uint4 res[4];
+    const bool use_res = e.residual != nullptr && live;
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      res[g] = (use_res && n0 + g * 8 < s.N)
+                   ? *reinterpret_cast<const uint4*>(e.residual + off + g * 8)
+                   : make_uint4(0u, 0u, 0u, 0u);
+    uint32_t r[32];
+    tmem_ld32(taddr + c * 32, r);
+    tmem_wait_ld();
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = bf16_round(__uint_as_float(r[j]));
@@ -137,9 +147,8 @@ __device__ __forceinline__ void conv_store_box(const ConvShape& s, const ConvEpi
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[g * 8 + j] = bf16_round(v[g * 8 + j] + add[j]);
         }
-        if (e.residual != nullptr && live) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(e.residual + off + g * 8);
-          const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+        if (use_res) {
+          const uint32_t w4[4] = {res[g].x, res[g].y, res[g].z, res[g].w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float2 fr = unpack_bf16x2(w4[q]);
@@ -381,26 +390,32 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 // per-SM operand traffic per tensor-core cycle is three quarters (BN = 256) or a little over
 // half (BN = 128) of the single-CTA tile's. TMA loads complete on the even CTA's barriers (no
 // multicast loads); MMA completion is committed to both CTAs; each CTA stores its own box.
-template <int BN, int STAGES>
+// A stage holds KSUB consecutive K blocks (each: this CTA's box and its half of the weight
+// rows), so that one barrier round trip covers KSUB x 4 MMAs: with BN = 128 an MMA is only 64
+// tensor cycles and the per-stage wait would otherwise show between the groups.
+template <int BN, int STAGES, int KSUB>
 struct ConvPairSmem {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;      // 16 KB: this CTA's box
   static constexpr int B_BYTES = (BN / 2) * GEMM_BK * 2;     // this CTA's half of the weights
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SUB_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = KSUB * SUB_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int XCH_BYTES = 4 * 32 * 3 * 4;  // GroupNorm statistics handed between halves
   static constexpr int BAR_BYTES = (2 * STAGES + 5) * 8 + 16;
-  static constexpr int TOTAL = TILE_BYTES + BAR_BYTES + 1024;
+  static constexpr int TOTAL = TILE_BYTES + XCH_BYTES + BAR_BYTES + 1024;
 };
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(CONV_THREADS, 1)
+template <int BN, int STAGES, int KSUB>
+__global__ void __launch_bounds__(CONV_PAIR_THREADS, 1)
     conv3d_2sm_kernel(const __grid_constant__ CUtensorMap map_x,
                       const __grid_constant__ CUtensorMap map_w, __nv_bfloat16* __restrict__ out,
                       const ConvShape s, const ConvEpi e) {
-  using L = ConvPairSmem<BN, STAGES>;
+  using L = ConvPairSmem<BN, STAGES, KSUB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES);
+  float* stats_xch = reinterpret_cast<float*>(smem + L::TILE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES + L::XCH_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -420,7 +435,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 8);  // the 4 epilogue warps of both CTAs
+      mbar_init(&tempty[i], 2 * CONV_PAIR_EPI_WARPS);  // the epilogue warps of both CTAs
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -458,23 +473,27 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         // a box past the last one loads zero fill (width coordinate out of range)
         const int f0 = fbi * s.tf, h0 = hbi * s.th;
         const int w0 = box < s.boxes ? wbi * s.tw : s.W + 64;
-        for (int kb = 0; kb < s.kblocks; ++kb) {
-          const int tap = kb / s.cblocks;
-          const int cb = kb - tap * s.cblocks;
-          const int kt = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+        for (int kb0 = 0; kb0 < s.kblocks; kb0 += KSUB) {
+          const int nsub = s.kblocks - kb0 < KSUB ? s.kblocks - kb0 : KSUB;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
-          uint8_t* sa = smem + stage * L::STAGE_BYTES;
-          uint8_t* sb = sa + L::A_BYTES;
           const uint32_t leader_full = smem_u32(&full[stage]) & kPairLeaderMask;
-          if (rank == 0) mbar_expect_tx(&full[stage], 2 * L::STAGE_BYTES);
-          for (int fi = 0; fi < s.tf; ++fi) {
-            int fs = f0 + fi + kt - s.pad_front;
-            fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
-            tma_load_4d_pair(sa + fi * box_rows * 128, &map_x, leader_full, cb * 64, w0 + kw - 1,
-                             h0 + kh - 1, fs);
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * nsub * L::SUB_BYTES);
+          for (int j = 0; j < nsub; ++j) {
+            const int kb = kb0 + j;
+            const int tap = kb / s.cblocks;
+            const int cb = kb - tap * s.cblocks;
+            const int kt = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+            uint8_t* sa = smem + stage * L::STAGE_BYTES + j * L::SUB_BYTES;
+            uint8_t* sb = sa + L::A_BYTES;
+            for (int fi = 0; fi < s.tf; ++fi) {
+              int fs = f0 + fi + kt - s.pad_front;
+              fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
+              tma_load_4d_pair(sa + fi * box_rows * 128, &map_x, leader_full, cb * 64,
+                               w0 + kw - 1, h0 + kh - 1, fs);
+            }
+            tma_load_2d_pair(sb, &map_w, leader_full, kb * GEMM_BK,
+                             nt * BN + static_cast<int>(rank) * (BN / 2));
           }
-          tma_load_2d_pair(sb, &map_w, leader_full, kb * GEMM_BK,
-                           nt * BN + static_cast<int>(rank) * (BN / 2));
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -503,18 +522,23 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < s.kblocks; ++kb) {
+        for (int kb0 = 0; kb0 < s.kblocks; kb0 += KSUB) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES);
-          const uint32_t sb = sa + L::A_BYTES;
 #pragma unroll
-          for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
-            umma_bf16_pair(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32), idesc,
-                           (kb > 0 || kk > 0) ? 1u : 0u);
+          for (int j = 0; j < KSUB; ++j) {
+            if (kb0 + j < s.kblocks) {
+              const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES + j * L::SUB_BYTES);
+              const uint32_t sb = sa + L::A_BYTES;
+#pragma unroll
+              for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+                umma_bf16_pair(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32), idesc,
+                               (kb0 + j > 0 || kk > 0) ? 1u : 0u);
+              }
+            }
           }
           umma_commit_pair(&empty[stage], 0x3);
           if (++stage == STAGES) {
@@ -531,7 +555,9 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       }
     }
   } else {
+    // two warps per TMEM lane quarter, one per half of the tile's 32-column chunks
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int m = quarter * 32 + static_cast<int>(lane);
     const uint32_t leader_tempty0 = cluster_addr(smem_u32(&tempty[0]), 0);
     float gn_n = 0.0f, gn_mean = 0.0f, gn_m2 = 0.0f;  // statistics of group `lane`
@@ -546,18 +572,30 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       const int box = mt * 2 + static_cast<int>(rank);
       if (box < s.boxes)  // warp-uniform
         conv_store_box<BN>(s, e, out, box, nt, tmem_base + ((quarter * 32) << 16) + acc * BN, m,
-                           lane, gn_n, gn_mean, gn_m2);
+                           lane, gn_n, gn_mean, gn_m2, half * (BN / 64), (half + 1) * (BN / 64));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
     }
     if (e.stats != nullptr) {
-      float* rec = e.stats + GN_STATS_RECORDS + (blockIdx.x * 4 + quarter) * 96 + lane * 3;
-      rec[0] = gn_n;
-      rec[1] = gn_mean;
-      rec[2] = gn_m2;
-      if (blockIdx.x == 0 && warp == 2 && lane == 0)
-        *reinterpret_cast<int*>(e.stats) = static_cast<int>(gridDim.x) * 4;
+      // the two warps of a lane quarter merge their statistics (their groups overlap under
+      // depth-to-space) into one record per quarter: record (CTA * 4 + quarter)
+      float* xch = stats_xch + (quarter * 32 + static_cast<int>(lane)) * 3;
+      if (half == 1) {
+        xch[0] = gn_n;
+        xch[1] = gn_mean;
+        xch[2] = gn_m2;
+      }
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+      if (half == 0) {
+        chan_merge(gn_n, gn_mean, gn_m2, xch[0], xch[1], xch[2]);
+        float* rec = e.stats + GN_STATS_RECORDS + (blockIdx.x * 4 + quarter) * 96 + lane * 3;
+        rec[0] = gn_n;
+        rec[1] = gn_mean;
+        rec[2] = gn_m2;
+        if (blockIdx.x == 0 && warp == 2 && lane == 0)
+          *reinterpret_cast<int*>(e.stats) = static_cast<int>(gridDim.x) * 4;
+      }
     }
   }
 

@@ -100,6 +100,9 @@ constexpr int GEMM_EPI_WARPS = 8;
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 // The implicit-GEMM conv keeps one epilogue warp per quarter.
 constexpr int CONV_THREADS = 192;
+// The CTA-pair conv: warp 0 TMA, warp 1 MMA, eight epilogue warps (two per TMEM lane quarter).
+constexpr int CONV_PAIR_EPI_WARPS = 8;
+constexpr int CONV_PAIR_THREADS = 32 * (2 + CONV_PAIR_EPI_WARPS);
 
 template <int BN, int STAGES>
 struct GemmSmem {
