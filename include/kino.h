@@ -30,7 +30,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (4); bumped on any signature change. */
+/* ABI version of this header (5); bumped on any signature change. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -295,6 +295,12 @@ typedef struct kino_conv3d_args {
    * capacity in records (4 per SM). Output channels per voxel 32..1024, group size dividing 32. */
   void* stats;
   int64_t stats_records;
+  /* Optional split-K workspace (device, kino_conv3d_workspace_size() bytes, zero-filled once
+   * before its first use; every launch leaves it ready for the next), or NULL. With it, a conv
+   * whose output tiles fill less than half of the GPU splits its 27 * Cin reduction over several
+   * CTAs (fp32 partial sums, added in a fixed order by the CTA that completes the tile). */
+  void* workspace;
+  int64_t workspace_bytes;
 } kino_conv3d_args;
 
 /* 3x3x3 convolution with temporal replicate and spatial zero padding as an implicit GEMM on
@@ -320,6 +326,9 @@ int64_t kino_group_norm_workspace_size(int64_t voxels, int64_t channels);
 kino_status kino_group_norm(const void* x, const void* weight, const void* bias, void* out,
                             int64_t voxels, int64_t channels, float eps, int apply_silu,
                             void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Bytes of the split-K workspace kino_conv3d_args.workspace takes on the current device. */
+int64_t kino_conv3d_workspace_size(void);
 
 /* Bytes of the statistics buffer kino_conv3d fills for kino_group_norm_from_stats on the current
  * device: a header, mean and rstd, and 4 records per SM of 32 x (count, mean, m2) floats. */

@@ -140,6 +140,8 @@ class Conv3dArgs(ctypes.Structure):
         ("stride_w", c_int),
         ("stats", c_void_p),
         ("stats_records", c_int64),
+        ("workspace", c_void_p),
+        ("workspace_bytes", c_int64),
     ]
 
 
@@ -189,6 +191,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_group_norm_workspace_size": (c_int64, [I64, I64]),
     "kino_group_norm": (c_int, [P, P, P, P, I64, I64, F, c_int, P, I64, P]),
     "kino_conv3d_stats_size": (c_int64, []),
+    "kino_conv3d_workspace_size": (c_int64, []),
     "kino_group_norm_from_stats": (c_int, [P, P, P, P, I64, I64, F, c_int, P, P]),
     "kino_group_norm_noalloc": (c_int, [P, P, P, P, I64, I64, F, c_int, P]),
     "kino_latent_to_bfhwc": (c_int, [P, P, P, P, I64, I64, P]),

@@ -207,6 +207,14 @@ kino_status launch_gemm(const void* x, const void* w, void* out, const kino::Gem
   return check_launch("kino_linear");
 }
 
+// Split-K workspace of the single-SM conv: tile counters first (one int per tile and lane
+// quarter), then the fp32 partial sums.
+#ifndef KINO_CONV_SPLIT_K
+#define KINO_CONV_SPLIT_K 1
+#endif
+constexpr int64_t KINO_CONV_SPLIT_COUNTERS_BYTES = 16384;
+constexpr int64_t KINO_CONV_SPLIT_WORKSPACE_BYTES = KINO_CONV_SPLIT_COUNTERS_BYTES + (48ll << 20);
+
 template <int BN, int STAGES, int MT>
 kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cudaStream_t stream,
                         int slot) {
@@ -228,12 +236,36 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   kino::ConvShape s = s0;
   s.tiles_m = (s.boxes + MT - 1) / MT;
   s.tiles_n = (s.N + BN - 1) / BN;
-  s.num_tiles = s.tiles_m * s.tiles_n;
+  s.splits = 1;
+  s.kper = s.kblocks;
+  kino::ConvEpi e;
+  e.split_count = nullptr;
+  e.split_partial = nullptr;
+  // Split-K when the output tiles fill less than half of the SMs and the caller gave a
+  // workspace: at least 32 K blocks per split (below that the partial sums' round trip costs
+  // more than the idle SMs), at most 8 splits, partials within the workspace.
+  const int64_t tiles = static_cast<int64_t>(s.tiles_m) * s.tiles_n;
+  if (KINO_CONV_SPLIT_K && MT == 1 && a->workspace != nullptr && 2 * tiles <= device_sms() &&
+      4 * tiles * 4 <= KINO_CONV_SPLIT_COUNTERS_BYTES) {
+    int splits = static_cast<int>(device_sms() / tiles);
+    if (splits > 8) splits = 8;
+    if (splits > s.kblocks / 32) splits = s.kblocks / 32;
+    while (splits > 1 && KINO_CONV_SPLIT_COUNTERS_BYTES + tiles * splits * 128 * BN * 4 >
+                              a->workspace_bytes)
+      --splits;
+    if (splits > 1) {
+      s.kper = (s.kblocks + splits - 1) / splits;
+      s.splits = (s.kblocks + s.kper - 1) / s.kper;
+      e.split_count = static_cast<int*>(a->workspace);
+      e.split_partial = reinterpret_cast<float*>(static_cast<char*>(a->workspace) +
+                                                 KINO_CONV_SPLIT_COUNTERS_BYTES);
+    }
+  }
+  s.num_tiles = s.tiles_m * s.tiles_n * s.splits;
   auto kernel = kino::conv3d_tc_kernel<BN, STAGES, MT>;
   st = ensure_smem(kernel, L::TOTAL, slot);
   if (st != KINO_OK) return st;
   const int grid = s.num_tiles < device_sms() ? s.num_tiles : device_sms();
-  kino::ConvEpi e;
   e.bias = static_cast<const __nv_bfloat16*>(a->bias);
   e.residual = static_cast<const __nv_bfloat16*>(a->residual);
   e.stats = static_cast<float*>(a->stats);
@@ -268,6 +300,8 @@ kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0
   s.tiles_m = (s.boxes + 1) / 2;
   s.tiles_n = (s.N + BN - 1) / BN;
   s.num_tiles = s.tiles_m * s.tiles_n;
+  s.splits = 1;
+  s.kper = s.kblocks;
   auto kernel = kino::conv3d_2sm_kernel<BN, STAGES, KSUB>;
   st = ensure_smem(kernel, L::TOTAL, slot);
   if (st != KINO_OK) return st;
@@ -278,6 +312,8 @@ kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0
   e.residual = static_cast<const __nv_bfloat16*>(a->residual);
   e.stats = static_cast<float*>(a->stats);
   e.group_size = s.Co / kino::GN_GROUPS;
+  e.split_count = nullptr;
+  e.split_partial = nullptr;
   if (e.stats != nullptr && 2 * pairs * 4 > a->stats_records)
     return fail(KINO_EINVAL, "kino_conv3d: statistics buffer holds %lld records, %d needed",
                 (long long)a->stats_records, 2 * pairs * 4);
@@ -420,7 +456,7 @@ void* group_norm_scratch_address(kino_status* status) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 4; }
+int kino_abi_version(void) { return 5; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -975,6 +1011,10 @@ kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
     return fail(KINO_ENOTSUPPORTED, "kino_conv3d: output channels per voxel must be 8k (32k with depth-to-space)");
   if (a->residual != nullptr && sub > 1)
     return fail(KINO_ENOTSUPPORTED, "kino_conv3d: residual add only without depth-to-space");
+  if (a->workspace != nullptr &&
+      (!aligned16(a->workspace) || a->workspace_bytes < KINO_CONV_SPLIT_COUNTERS_BYTES))
+    return fail(KINO_EINVAL, "kino_conv3d: workspace must be 16-byte aligned and at least %lld bytes",
+                (long long)KINO_CONV_SPLIT_COUNTERS_BYTES);
   if (a->bias != nullptr && !aligned16(a->bias)) return fail(KINO_EINVAL, "kino_conv3d: bias alignment");
   if ((a->residual != nullptr && !aligned16(a->residual)) || !aligned16(a->out))
     return fail(KINO_EINVAL, "kino_conv3d: output/residual alignment");
@@ -1077,6 +1117,8 @@ kino_status kino_group_norm(const void* x, const void* weight, const void* bias,
       ws + static_cast<int64_t>(parts) * kino::GN_GROUPS + kino::GN_GROUPS, apply_silu);
   return check_launch("kino_group_norm");
 }
+
+int64_t kino_conv3d_workspace_size(void) { return KINO_CONV_SPLIT_WORKSPACE_BYTES; }
 
 int64_t kino_conv3d_stats_size(void) {
   // one record per TMEM lane quarter of every CTA

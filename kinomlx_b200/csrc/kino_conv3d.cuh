@@ -31,6 +31,7 @@ struct ConvShape {
   int fb, hb, wb;
   int boxes;  // fb * hb * wb voxel boxes of 128
   int tiles_m, tiles_n, num_tiles, kblocks, cblocks;  // an M tile is MT consecutive boxes
+  int splits, kper;  // split-K: num_tiles = tiles_m * tiles_n * splits, kper K blocks per split
   int pad_front;
   int st, sh, sw, drop;  // depth-to-space strides (1,1,1,0 = plain store)
   int Fo, Ho, Wo, Co;    // output geometry
@@ -46,6 +47,10 @@ struct ConvEpi {
   // into the header.
   float* stats;
   int group_size;  // output channels per group (output channels / 32)
+  // Split-K (single-SM kernel, MT = 1): int arrival counters, one per output tile (zero between
+  // launches), and the fp32 partial accumulators [tile][split][128 rows][BN].
+  int* split_count;
+  float* split_partial;
 };
 
 // GroupNorm statistics layout (floats): [0] record count (int), [4, 36) mean, [36, 68) rstd,
@@ -96,7 +101,8 @@ __device__ __forceinline__ void conv_store_box(const ConvShape& s, const ConvEpi
                                                __nv_bfloat16* __restrict__ out, int box, int nt,
                                                uint32_t taddr, int m, uint32_t lane,
                                                float& gn_n, float& gn_mean, float& gn_m2,
-                                               int c_begin = 0, int c_end = BN / 32) {
+                                               int c_begin = 0, int c_end = BN / 32,
+                                               const float* psum = nullptr, int splits = 0) {
   const int box_rows = s.th * s.tw;
   const int cpo = s.Co;  // channels per output voxel
   const int wbi = box % s.wb;
@@ -126,8 +132,30 @@ __device__ __forceinline__ void conv_store_box(const ConvShape& s, const ConvEpi
                    ? *reinterpret_cast<const uint4*>(e.residual + off + g * 8)
                    : make_uint4(0u, 0u, 0u, 0u);
     uint32_t r[32];
-    tmem_ld32(taddr + c * 32, r);
-    tmem_wait_ld();
+    if (psum == nullptr) {
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+    } else {
+      // split-K: the splits' fp32 partial sums of this row, added in split order (the same
+      // order whichever CTA finishes last, so the result does not depend on timing)
+      float acc32[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc32[j] = 0.0f;
+      for (int ks = 0; ks < splits; ++ks) {
+        const float4* src =
+            reinterpret_cast<const float4*>(psum + (static_cast<int64_t>(ks) * 128 + m) * BN + c * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 f4 = __ldcg(src + q);
+          acc32[4 * q] += f4.x;
+          acc32[4 * q + 1] += f4.y;
+          acc32[4 * q + 2] += f4.z;
+          acc32[4 * q + 3] += f4.w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(acc32[j]);
+    }
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = bf16_round(__uint_as_float(r[j]));
@@ -251,9 +279,12 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;
       for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x) {
-        const int mt = t % s.tiles_m;
-        const int nt = t / s.tiles_m;
-        for (int kb = 0; kb < s.kblocks; ++kb) {
+        const int tile = t % (s.tiles_m * s.tiles_n);
+        const int mt = tile % s.tiles_m;
+        const int nt = tile / s.tiles_m;
+        const int kb_begin = (t / (s.tiles_m * s.tiles_n)) * s.kper;
+        const int kb_end = kb_begin + s.kper < s.kblocks ? kb_begin + s.kper : s.kblocks;
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           const int tap = kb / s.cblocks;
           const int cb = kb - tap * s.cblocks;
           const int kt = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
@@ -311,7 +342,9 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * MT * BN;
         bool ok = true;
-        for (int kb = 0; kb < s.kblocks; ++kb) {
+        const int kb_begin = (t / (s.tiles_m * s.tiles_n)) * s.kper;
+        const int kb_end = kb_begin + s.kper < s.kblocks ? kb_begin + s.kper : s.kblocks;
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
             break;
@@ -324,7 +357,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 #pragma unroll
             for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
               umma_bf16(d_tmem + i * BN, sdesc_k128(sa + i * L::A1_BYTES + kk * 32),
-                        sdesc_k128(sb + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                        sdesc_k128(sb + kk * 32), idesc, (kb > kb_begin || kk > 0) ? 1u : 0u);
             }
           }
           umma_commit(&empty[stage]);
@@ -347,12 +380,53 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     float gn_n = 0.0f, gn_mean = 0.0f, gn_m2 = 0.0f;  // statistics of group `lane`
     int local = 0;
     for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
-      const int mt = t % s.tiles_m;
-      const int nt = t / s.tiles_m;
+      const int tile = t % (s.tiles_m * s.tiles_n);
+      const int mt = tile % s.tiles_m;
+      const int nt = tile / s.tiles_m;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
       tc_fence_after();
+      if (MT == 1 && s.splits > 1) {
+        // split-K: store this split's fp32 accumulators, free the TMEM buffer, and let the CTA
+        // that completes the tile's last split run the epilogue over all partial sums
+        const int ks = t / (s.tiles_m * s.tiles_n);
+        float* part = e.split_partial + static_cast<int64_t>(tile) * s.splits * 128 * BN;
+        const uint32_t taddr = tmem_base + ((quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          float4* dst = reinterpret_cast<float4*>(part + (static_cast<int64_t>(ks) * 128 + m) * BN + c * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(dst + q, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                        __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        // Each warp owns its 32 rows: its partial rows are out (fence) before its counter
+        // (tile, lane quarter) moves; the warp that brings the counter to `splits` sums them.
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          int* cnt = e.split_count + tile * 4 + quarter;
+          const int prev = atomicAdd(cnt, 1);
+          last = prev == s.splits - 1;
+          if (last) atomicExch(cnt, 0);  // ready for the next launch
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          __threadfence();
+          if (mt < s.boxes)
+            conv_store_box<BN>(s, e, out, mt, nt, 0u, m, lane, gn_n, gn_mean, gn_m2, 0, BN / 32,
+                               part, s.splits);
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int bi = 0; bi < MT; ++bi) {
         const int box = mt * MT + bi;

@@ -146,6 +146,7 @@ class VideoDecoder:
             self.norm_out = (dev(w["norm_out.weight"]), dev(w["norm_out.bias"]))
         self.conv_out = (dev(w["conv_out.weight"]), dev(w["conv_out.bias"]))
         self._stats: torch.Tensor | None = None  # GroupNorm statistics from the producing conv
+        self._conv_ws: torch.Tensor | None = None  # split-K workspace of the small-grid convs
 
     def _norm_silu(self, x: torch.Tensor, params) -> torch.Tensor:
         if self.v.norm == "pixel":
@@ -161,21 +162,25 @@ class VideoDecoder:
         group = self.v.norm != "pixel"
         if group and self._stats is None:
             self._stats = ops.conv_stats_buffer(self.device)
+        if self._conv_ws is None:
+            self._conv_ws = ops.conv_workspace(self.device)
         st = self._stats if group else None  # every GroupNorm input is the previous conv's output
+        ws = self._conv_ws
         x = ops.latent_to_bfhwc(latent.to(self.device, torch.bfloat16).contiguous(), self.std, self.mean)
-        x = ops.conv3d(x, *self.conv_in, causal=causal, stats=st)
+        x = ops.conv3d(x, *self.conv_in, causal=causal, stats=st, workspace=ws)
         for kind, payload in self.stages:
             if kind == "res":
                 for entry in payload:
                     h = self._norm_silu(x, entry.get("norm1"))
-                    h = ops.conv3d(h, *entry["conv1"], causal=causal, stats=st)
+                    h = ops.conv3d(h, *entry["conv1"], causal=causal, stats=st, workspace=ws)
                     h = self._norm_silu(h, entry.get("norm2"))
-                    x = ops.conv3d(h, *entry["conv2"], causal=causal, residual=x, out=x, stats=st)
+                    x = ops.conv3d(h, *entry["conv2"], causal=causal, residual=x, out=x, stats=st,
+                                   workspace=ws)
             else:
                 wt, bs, stride = payload
-                x = ops.conv3d(x, wt, bs, causal=causal, stride=stride, stats=st)
+                x = ops.conv3d(x, wt, bs, causal=causal, stride=stride, stats=st, workspace=ws)
         x = self._norm_silu(x, self.norm_out)
-        return ops.conv3d(x, *self.conv_out, causal=causal)
+        return ops.conv3d(x, *self.conv_out, causal=causal, workspace=ws)
 
     def decode_tiled(self, latent: torch.Tensor, *, tile: int = 8, overlap: int = 2,
                      tiles: list[int] | None = None, canvas: torch.Tensor | None = None,

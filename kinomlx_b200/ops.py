@@ -714,11 +714,13 @@ def conv3d(
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
     stats: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """3x3x3 conv of channels-last x (F, H, W, Cin) with an (N, 3, 3, 3, Cin) weight; with a
     depth-to-space `stride` the weight rows must be sub-position-major (n = sub * C' + c).
     `stats` (a conv_stats_buffer()) receives the GroupNorm(32) statistics of the output for
-    group_norm_from_stats."""
+    group_norm_from_stats. `workspace` (a conv_workspace()) lets a conv whose output tiles fill
+    less than half of the GPU split its reduction over several CTAs."""
     _need(x, "x")
     _need(weight, "weight")
     if not x.is_contiguous() or not weight.is_contiguous():
@@ -749,6 +751,10 @@ def conv3d(
         _need(stats, "stats", torch.float32)
         args.stats = stats.data_ptr()
         args.stats_records = (stats.numel() - 128) // 96
+    if workspace is not None:
+        _need(workspace, "workspace", torch.uint8)
+        args.workspace = workspace.data_ptr()
+        args.workspace_bytes = workspace.numel()
     with _timed("conv3d", 2.0 * f * h * w * n * 27 * cin, 2.0 * (x4.numel() + weight.numel() + out.numel())):
         _lib.call("kino_conv3d", ctypes.byref(args), _stream())
     return out
@@ -789,6 +795,13 @@ def group_norm(x: torch.Tensor, groups: int, weight: torch.Tensor, bias: torch.T
         _lib.call("kino_group_norm", _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), voxels, c, eps,
                   int(silu), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream())
     return out
+
+
+def conv_workspace(device: torch.device | None = None) -> torch.Tensor:
+    """A zero-filled split-K workspace for conv3d(workspace=...) on the current device (every
+    launch leaves it ready for the next; one per stream of convs)."""
+    nbytes = int(_lib.load().kino_conv3d_workspace_size())
+    return torch.zeros((nbytes,), device=device or torch.device("cuda"), dtype=torch.uint8)
 
 
 def conv_stats_buffer(device: torch.device | None = None) -> torch.Tensor:

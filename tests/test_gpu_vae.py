@@ -76,6 +76,55 @@ def test_conv3d_matches_oracle(cuda_device, f, h, w, cin, n, causal, stride, res
     assert (out.cpu() == exp).float().mean() > 0.95
 
 
+@pytest.mark.parametrize(
+    ("f", "h", "w", "cin", "n", "causal", "stride", "residual"),
+    [
+        # output tiles filling under half of the SMs with a long reduction: split-K over CTAs
+        (4, 8, 8, 256, 512, True, (1, 1, 1), True),
+        (3, 6, 8, 1024, 256, False, (1, 1, 1), False),
+        (3, 8, 8, 512, 1024, True, (1, 2, 2), False),
+        (5, 8, 8, 512, 128, True, (1, 1, 1), True),
+        (3, 6, 8, 256, 96, False, (1, 1, 1), False),
+    ],
+)
+def test_conv3d_split_k_matches_oracle(cuda_device, f, h, w, cin, n, causal, stride, residual):
+    """Split-K convs (fp32 partial sums added in split order by the CTA that completes the tile)
+    against the oracle, against the same conv without a workspace, and a second launch on the
+    same workspace (its tile counters back at zero) giving identical bytes."""
+    dev = cuda_device
+    x = normal((1, f, h, w, cin), seed=41)
+    wt = normal((n, 3, 3, 3, cin), seed=42, std=0.05)
+    b = normal((n,), seed=43, std=0.1)
+    sub = math.prod(stride)
+    ws = ops.conv_workspace(dev)
+    if sub == 1:
+        exp = ref.conv3d(x, wt, b, causal)
+        res = normal(exp.shape, seed=44) if residual else None
+        if res is not None:
+            exp = exp + res
+        args = (x.to(dev).contiguous(), wt.to(dev), b.to(dev))
+        kw = dict(causal=causal, residual=None if res is None else res[0].to(dev))
+    else:
+        cout = n // sub
+        p = {"u.conv.weight": wt, "u.conv.bias": b}
+        exp = ref.upsample(p, "u", x, stride, cin // cout, ref.VaeVariant(causal=causal))
+        wd = wt.reshape(cout, sub, 3, 3, 3, cin).transpose(0, 1).reshape(wt.shape)
+        bd = b.reshape(cout, sub).transpose(0, 1).reshape(-1)
+        args = (x.to(dev).contiguous(), wd.to(dev).contiguous(), bd.to(dev).contiguous())
+        kw = dict(causal=causal, stride=stride)
+    split = ops.conv3d(*args, workspace=ws, **kw)
+    again = ops.conv3d(*args, workspace=ws, **kw)
+    whole = ops.conv3d(*args, **kw)
+    torch.cuda.synchronize()
+    assert int(ws[:16384].view(torch.int32).abs().sum()) == 0  # counters reset
+    assert torch.equal(split, again)
+    exp = exp[0]
+    rel_l2, max_rel, _ = _metrics(split, exp)
+    assert max_rel <= 2e-2, (rel_l2, max_rel)
+    assert (split.cpu() == exp).float().mean() > 0.95
+    assert (split == whole).float().mean() > 0.95
+
+
 def test_pixel_and_group_norm_silu(cuda_device):
     x = normal((3, 7, 9, 256), seed=5, std=2.0)
     exp = fo.silu(fo.pixel_norm(x, dim=-1, eps=1e-8))
@@ -145,6 +194,8 @@ def test_config5_shapes_first_stages_run(cuda_device):
         (3, 20, 36, 64, 1024, False, (1, 1, 1), False),
         (2, 16, 40, 128, 64, True, (1, 1, 1), False),
         (11, 36, 80, 64, 128, True, (1, 1, 1), True),
+        (4, 8, 8, 512, 512, True, (1, 1, 1), True),  # split-K: statistics from the last split
+        (3, 8, 8, 256, 512, True, (1, 2, 2), False),
     ],
 )
 def test_group_norm_from_conv_statistics(cuda_device, f, h, w, cin, n, causal, stride, residual):
@@ -159,7 +210,8 @@ def test_group_norm_from_conv_statistics(cuda_device, f, h, w, cin, n, causal, s
     co = n // sub
     res = normal((f, h, w, co), seed=34, device=dev) if residual else None
     stats = ops.conv_stats_buffer(dev)
-    y = ops.conv3d(x, wt, bias, causal=causal, stride=stride, residual=res, stats=stats)
+    y = ops.conv3d(x, wt, bias, causal=causal, stride=stride, residual=res, stats=stats,
+                   workspace=ops.conv_workspace(dev))
     gw = normal((co,), seed=35, device=dev) + 1
     gb = normal((co,), seed=36, device=dev)
     got = ops.group_norm_from_stats(y, gw, gb, 1e-6, stats, silu=True)
