@@ -190,8 +190,12 @@ __global__ void __launch_bounds__(GN_MERGE_THREADS) group_norm_merge_kernel(
 // exp2 and reciprocal; the activation's own rounding dominates). Each thread owns one 8-channel
 // vector of every voxel it visits, so its weights, biases and group statistics stay in
 // registers; threads of a CTA cover C / 8 vectors x (256 / (C / 8)) voxels per step. The pass
-// is HBM-bound: each thread keeps four 16-byte loads in flight (voxels v, v + step, ...) so that
-// the bytes in flight per SM cover the memory latency at the occupancy the registers allow.
+// is HBM-bound: each thread keeps KINO_GN_APPLY_UNROLL 16-byte loads in flight (voxels v,
+// v + step, ...) so that the bytes in flight per SM cover the memory latency at the occupancy
+// the registers allow.
+#ifndef KINO_GN_APPLY_UNROLL
+#define KINO_GN_APPLY_UNROLL 4
+#endif
 __device__ __forceinline__ void gn_apply8(const uint4 raw, const float (&m)[8],
                                           const float (&rs)[8], const float (&w)[8],
                                           const float (&b)[8], int apply_silu,
@@ -235,13 +239,14 @@ __global__ void __launch_bounds__(256)
   }
   const int64_t step = static_cast<int64_t>(gridDim.x) * rows;
   int64_t v = static_cast<int64_t>(blockIdx.x) * rows + r0;
-  for (; v + 3 * step < voxels; v += 4 * step) {
-    uint4 raw[4];
+  constexpr int U = KINO_GN_APPLY_UNROLL;
+  for (; v + (U - 1) * step < voxels; v += U * step) {
+    uint4 raw[U];
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
+    for (int u = 0; u < U; ++u)
       raw[u] = __ldg(reinterpret_cast<const uint4*>(x + (v + u * step) * C + c0));
 #pragma unroll
-    for (int u = 0; u < 4; ++u) gn_apply8(raw[u], m, rs, w, b, apply_silu, out + (v + u * step) * C + c0);
+    for (int u = 0; u < U; ++u) gn_apply8(raw[u], m, rs, w, b, apply_silu, out + (v + u * step) * C + c0);
   }
   for (; v < voxels; v += step)
     gn_apply8(__ldg(reinterpret_cast<const uint4*>(x + v * C + c0)), m, rs, w, b, apply_silu,

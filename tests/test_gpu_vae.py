@@ -46,6 +46,7 @@ def _metrics(out, expect):
         (9, 40, 72, 64, 256, True, (1, 1, 1), True),
         (7, 44, 76, 128, 96, False, (1, 1, 1), False),
         (6, 40, 64, 64, 320, True, (1, 1, 1), False),
+        (8, 64, 64, 128, 48, True, (1, 1, 1), False),  # the decoder's conv_out width, in pairs
     ],
 )
 def test_conv3d_matches_oracle(cuda_device, f, h, w, cin, n, causal, stride, residual):
