@@ -30,7 +30,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (5); bumped on any signature change. */
+/* ABI version of this header (6); bumped on any signature change. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -115,6 +115,11 @@ typedef struct kino_epilogue {
   int64_t lead_rows;
   const void* norm_weight_lead[2];
   const void* gate_lead;
+  /* 1: the product is rounded to bf16 before the bias is added (then rounded again), as the
+   * reference's packed linears do (quantized_matmul, then + bias:
+   * kinomlx/models/ltx2/weights/quantization.py:32-43); 0: one rounding of acc + bias (addmm).
+   * Not with the fused QK norm. */
+  int bias_after_round;
 } kino_epilogue;
 
 /* out[b, i, j] = epilogue(sum_k x[b, i, k] * w[j, k]) on tcgen05 tensor cores.
@@ -278,6 +283,24 @@ kino_status kino_heads_unpack(const void* src, void* dst, int64_t ld, int64_t to
  * kinomlx/models/ltx2/transformer/timestep.py:13-28. */
 kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, int64_t dim,
                                     void* stream);
+
+/* ------------------------------------------------------------------ quantised weights */
+#define KINO_QUANT_AFFINE 0 /* w = scale * q + bias, bf16 scale and bias per group, 2/4/8 bits */
+#define KINO_QUANT_MXFP8 1  /* E4M3 x E8M0 scale per 32 */
+#define KINO_QUANT_MXFP4 2  /* E2M1 x E8M0 scale per 32 */
+#define KINO_QUANT_NVFP4 3  /* E2M1 x E4M3 scale per 16 */
+
+/* Dequantise a group-quantised (rows, cols) weight into bf16: `words` holds the codes packed
+ * along each row, little-endian in uint32 words ((rows, cols * bits / 32)); `scales` (and, for
+ * affine, `biases`) hold one value per group of `group_size` codes ((rows, cols / group_size):
+ * bf16 for affine, uint8 E8M0 / E4M3 codes otherwise). out is (rows, cols), or (cols, rows) with
+ * transpose_out (the reference's pretransposed weights, packed from weight.T). Float modes are
+ * exact in fp32, affine is one fp32 fma; one rounding to bf16. Requires cols to be a multiple of
+ * 16 and of the group size (and rows % 16 == 0 with transpose_out). Replaces the weight side of MLX's quantized_matmul as called
+ * by kinomlx/models/ltx2/weights/quantization.py:26-43 (modes and groups: tensors.py:185-203). */
+kino_status kino_dequantize(const void* words, const void* scales, const void* biases, void* out,
+                            int64_t rows, int64_t cols, int mode, int group_size, int bits,
+                            int transpose_out, void* stream);
 
 /* ------------------------------------------------------------------ video VAE decode */
 typedef struct kino_conv3d_args {

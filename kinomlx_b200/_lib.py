@@ -84,6 +84,7 @@ class Epilogue(ctypes.Structure):
         ("lead_rows", c_int64),
         ("norm_weight_lead", c_void_p * 2),
         ("gate_lead", c_void_p),
+        ("bias_after_round", c_int),
     ]
 
 
@@ -192,6 +193,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_group_norm": (c_int, [P, P, P, P, I64, I64, F, c_int, P, I64, P]),
     "kino_conv3d_stats_size": (c_int64, []),
     "kino_conv3d_workspace_size": (c_int64, []),
+    "kino_dequantize": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, I64, I64, c_int, c_int,
+                                c_int, c_int, c_void_p]),
     "kino_group_norm_from_stats": (c_int, [P, P, P, P, I64, I64, F, c_int, P, P]),
     "kino_group_norm_noalloc": (c_int, [P, P, P, P, I64, I64, F, c_int, P]),
     "kino_latent_to_bfhwc": (c_int, [P, P, P, P, I64, I64, P]),

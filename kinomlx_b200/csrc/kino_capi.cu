@@ -16,6 +16,7 @@
 #include "kino_ops.cuh"
 #include "kino_peer.cuh"
 #include "kino_vae.cuh"
+#include "kino_quant.cuh"
 
 // Scratch of kino_group_norm_noalloc: a fixed device array that every GPU loading this library
 // holds until the process exits. Host code only sees a stand-in symbol for it, so its device
@@ -456,7 +457,7 @@ void* group_norm_scratch_address(kino_status* status) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 5; }
+int kino_abi_version(void) { return 6; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -572,6 +573,12 @@ kino_status kino_linear(const void* x, const void* w, void* out, int64_t batch, 
     e.scatter_ld = epi->scatter_ld;
     e.scatter_row0 = epi->scatter_row0;
     for (int g = 0; g < 4; ++g) e.seg_slot[g] = epi->seg_slot[g];
+  }
+  if (epi != nullptr && epi->bias_after_round) {
+    if (e.norm_w[0] != nullptr || e.norm_w[1] != nullptr)
+      return fail(KINO_ENOTSUPPORTED, "kino_linear: bias after rounding is not combined with the "
+                                      "fused QK norm");
+    e.bias_after_round = 1;
   }
   const void* w_lead = nullptr;
   int64_t ldw_lead = 0;
@@ -1161,6 +1168,47 @@ kino_status kino_group_norm_noalloc(const void* x, const void* weight, const voi
   if (scratch == nullptr) return st;
   return kino_group_norm(x, weight, bias, out, voxels, channels, eps, apply_silu, scratch,
                          KINO_GROUP_NORM_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+kino_status kino_dequantize(const void* words, const void* scales, const void* biases, void* out,
+                            int64_t rows, int64_t cols, int mode, int group_size, int bits,
+                            int transpose_out, void* stream) {
+  if (words == nullptr || scales == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_dequantize: null operand");
+  if (mode < KINO_QUANT_AFFINE || mode > KINO_QUANT_NVFP4)
+    return fail(KINO_EINVAL, "kino_dequantize: unknown mode %d", mode);
+  if (mode == KINO_QUANT_AFFINE && biases == nullptr)
+    return fail(KINO_EINVAL, "kino_dequantize: affine mode needs biases");
+  const bool ok_bits = mode == KINO_QUANT_AFFINE ? (bits == 2 || bits == 4 || bits == 8)
+                                                 : bits == (mode == KINO_QUANT_MXFP8 ? 8 : 4);
+  const bool ok_group = mode == KINO_QUANT_AFFINE
+                            ? (group_size == 32 || group_size == 64 || group_size == 128)
+                            : group_size == (mode == KINO_QUANT_NVFP4 ? 16 : 32);
+  if (!ok_bits || !ok_group)
+    return fail(KINO_ENOTSUPPORTED, "kino_dequantize: mode %d takes neither %d bits nor groups of %d",
+                mode, bits, group_size);
+  if (rows < 1 || cols < 1 || cols % 16 || cols % group_size || (transpose_out && rows % 16) ||
+      rows > (1ll << 31) / kino::DQ_TILE)
+    return fail(KINO_ENOTSUPPORTED, "kino_dequantize: columns must be a multiple of the group size "
+                                    "and of 16 (and rows of 16 for a transposed output)");
+  if (!aligned16(words) || !aligned16(out))
+    return fail(KINO_EINVAL, "kino_dequantize: words and out must be 16-byte aligned");
+  const dim3 grid(static_cast<unsigned>((cols + kino::DQ_TILE - 1) / kino::DQ_TILE),
+                  static_cast<unsigned>((rows + kino::DQ_TILE - 1) / kino::DQ_TILE));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint32_t* w = static_cast<const uint32_t*>(words);
+  const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(biases);
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+  if (bits == 8)
+    launch_pdl(kino::dequant_kernel<8>, grid, dim3(kino::DQ_THREADS), 0, s, w, scales, b, o, rows,
+               cols, mode, group_size, transpose_out);
+  else if (bits == 4)
+    launch_pdl(kino::dequant_kernel<4>, grid, dim3(kino::DQ_THREADS), 0, s, w, scales, b, o, rows,
+               cols, mode, group_size, transpose_out);
+  else
+    launch_pdl(kino::dequant_kernel<2>, grid, dim3(kino::DQ_THREADS), 0, s, w, scales, b, o, rows,
+               cols, mode, group_size, transpose_out);
+  return check_launch("kino_dequantize");
 }
 
 kino_status kino_latent_to_bfhwc(const void* latent, const float* std_of_means,

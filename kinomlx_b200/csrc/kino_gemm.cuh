@@ -67,6 +67,7 @@ struct GemmEpi {
   int lead_rows;
   const __nv_bfloat16* norm_w_lead[2];
   const __nv_bfloat16* gate_lead;
+  int bias_after_round;  // round the product to bf16 before adding the bias (packed linears)
 };
 
 // Where the 32- or 128-column chunk of output row `row` starting at col0 is stored: this GPU's
@@ -133,6 +134,10 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]);
   if (e.bias != nullptr) {
+    if (e.bias_after_round) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = bf16_round(v[j]);
+    }
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       if (col0 + g * 8 < s.n) {

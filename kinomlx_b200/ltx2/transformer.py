@@ -18,6 +18,7 @@ import torch
 
 from .. import ops
 from ..sequence_parallel import SequenceParallel
+from . import quantization as qz
 from .config import LTXVariant
 
 
@@ -92,9 +93,17 @@ class LTXVideoTransformer:
     """Device LTX-2 video DiT. `weights` uses the reference checkpoint names."""
 
     def __init__(self, weights: dict[str, torch.Tensor], variant: LTXVariant,
-                 device: torch.device | str = "cuda", *, sp: SequenceParallel | None = None):
+                 device: torch.device | str = "cuda", *, sp: SequenceParallel | None = None,
+                 quantize: str = "off"):
         """`sp` shards the video tokens over a process group (Ulysses sequence parallelism for
-        the self-attention; the text cross-attention stays local with the full context)."""
+        the self-attention; the text cross-attention stays local with the full context).
+        `quantize` is the reference's `transformer_quantize` (weights/schema.py:13-18): "off",
+        "mxfp8-blocks" or "mxfp8-blocks-pretranspose" -- the block linears stay packed in HBM
+        (taken as given when the checkpoint has `*.scales`, else converted here) and are
+        dequantised into a bf16 scratch right before their GEMMs."""
+        if quantize not in qz.MODES:
+            raise ValueError(f"unsupported transformer_quantize {quantize!r}")
+        self.quantize = quantize
         self.sp = sp if sp is not None else SequenceParallel.single()
         self.v = variant
         self.device = torch.device(device)
@@ -117,9 +126,50 @@ class LTXVideoTransformer:
         self.prompt_adaln = adaln("prompt_adaln_single")
         tables, prompts = [], []
         self.blocks = []
+        packed = quantize != "off"
+        transposed = quantize == "mxfp8-blocks-pretranspose"
+        scratch_elems = 0
         for i in range(variant.blocks):
             a = f"transformer_blocks.{i}"
             g = lambda n: w[f"{a}.{n}"]
+            if packed:
+                # the block linears, packed; biases and norm weights stay bf16 (below)
+                pk = lambda *bases: qz.PackedGroup([
+                    qz.packed_from_checkpoint(w, f"{a}.{b}", transposed=transposed,
+                                              device=self.device) for b in bases])
+                groups = {
+                    "qkv_w": pk("attn1.to_v", "attn1.to_q", "attn1.to_k"),
+                    "g1_w": pk("attn1.to_gate_logits"),
+                    "o1_w": pk("attn1.to_out"),
+                    "q2_w": pk("attn2.to_q"),
+                    "kv2_w": pk("attn2.to_k", "attn2.to_v"),
+                    "g2_w": pk("attn2.to_gate_logits"),
+                    "o2_w": pk("attn2.to_out"),
+                    "ff_in_w": pk("ff.project_in.proj"),
+                    "ff_out_w": pk("ff.project_out"),
+                }
+                scratch_elems = max([scratch_elems] + [gr.out_features * gr.in_features
+                                                       for gr in groups.values()])
+                blk: dict = dict(groups)
+                blk.update({
+                    "qkv_b": dev(torch.cat([g("attn1.to_v.bias"), g("attn1.to_q.bias"), g("attn1.to_k.bias")])),
+                    "g1_b": dev(g("attn1.to_gate_logits.bias")),
+                    "o1_b": dev(g("attn1.to_out.bias")),
+                    "qn1": dev(g("attn1.q_norm.weight")),
+                    "kn1": dev(g("attn1.k_norm.weight")),
+                    "q2_b": dev(g("attn2.to_q.bias")),
+                    "kv2_b": dev(torch.cat([g("attn2.to_k.bias"), g("attn2.to_v.bias")])),
+                    "g2_b": dev(g("attn2.to_gate_logits.bias")),
+                    "o2_b": dev(g("attn2.to_out.bias")),
+                    "qn2": dev(g("attn2.q_norm.weight")),
+                    "kn2": dev(g("attn2.k_norm.weight")),
+                    "ff_in_b": dev(g("ff.project_in.proj.bias")),
+                    "ff_out_b": dev(g("ff.project_out.bias")),
+                })
+                tables.append(g("scale_shift_table").reshape(-1))
+                prompts.append(g("prompt_scale_shift_table").reshape(-1))
+                self.blocks.append(blk)
+                continue
             tables.append(g("scale_shift_table").reshape(-1))
             prompts.append(g("prompt_scale_shift_table").reshape(-1))
             self.blocks.append({
@@ -152,6 +202,20 @@ class LTXVideoTransformer:
         self.out_table = dev(w["scale_shift_table"])  # (2, D)
         self.proj_w, self.proj_b = dev(w["proj_out.weight"]), dev(w["proj_out.bias"])
         self._ws: dict[tuple[int, int, int], _Workspace] = {}
+        # one bf16 buffer for the packed linears' dequantised weights, reused by every GEMM on
+        # the stream (each dequantisation waits for the previous GEMM to finish reading it)
+        self._dq = (torch.empty(scratch_elems, device=self.device, dtype=torch.bfloat16)
+                    if packed else None)
+
+    def _wt(self, p: dict, name: str) -> torch.Tensor:
+        """The bf16 (out, in) weight of a block linear: resident, or dequantised into the scratch."""
+        w = p[name]
+        return w.dequantize(self._dq) if isinstance(w, qz.PackedGroup) else w
+
+    def _lin(self, x, p: dict, name: str, out, **kw):
+        """A block linear; packed ones round the product to bf16 before adding the bias, as the
+        reference's quantised linears do (weights/quantization.py:32-43)."""
+        return ops.linear(x, self._wt(p, name), out, bias_after_round=self.quantize != "off", **kw)
 
     def prepare(self, context: torch.Tensor, positions: torch.Tensor) -> PreparedContext:
         cos, sin = precompute_freqs_cis(positions.cpu(), self.v)
@@ -191,12 +255,12 @@ class LTXVideoTransformer:
         vv, q, k = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
         # self-attention
         ops.adaln(x, val(0), val(1), nrm, norm=ops.NORM_RMS, eps=v.eps)
-        ops.linear(nrm, p["g1_w"], ws.gates, bias=p["g1_b"], kind=ops.EPI_SIGMOID2)
+        self._lin(nrm, p, "g1_w", ws.gates, bias=p["g1_b"], kind=ops.EPI_SIGMOID2)
         if ws.peer:
             # v straight from the projection epilogue, q and k after their full-row norm and
             # RoPE, into the head owners' receive buffers; rows come back into q
             recv = self.sp.receive(x.shape[1], d)
-            ops.linear(nrm, p["qkv_w"], ws.qkv, bias=p["qkv_b"],
+            self._lin(nrm, p, "qkv_w", ws.qkv, bias=p["qkv_b"],
                        scatter=self.sp.scatter(recv, d, (2,), 0))
             for t, wn, slot in ((q, p["qn1"], 0), (k, p["kn1"], 1)):
                 ops.qk_norm_rope(t, heads=h, weight=wn, norm=ops.QKNORM_FULL_ROW,
@@ -206,34 +270,34 @@ class LTXVideoTransformer:
                                          out_cols=3 * d, out_col=d,
                                          gate=(ws.gate_ptrs, ws.gates.shape[-1]))
         else:
-            ops.linear(nrm, p["qkv_w"], ws.qkv, bias=p["qkv_b"])
+            self._lin(nrm, p, "qkv_w", ws.qkv, bias=p["qkv_b"])
             ops.qk_norm_rope(q, heads=h, weight=p["qn1"], norm=ops.QKNORM_FULL_ROW,
                              rope=ops.ROPE_SPLIT, cos=prepared.cos, sin=prepared.sin, eps=v.eps)
             ops.qk_norm_rope(k, heads=h, weight=p["kn1"], norm=ops.QKNORM_FULL_ROW,
                              rope=ops.ROPE_SPLIT, cos=prepared.cos, sin=prepared.sin, eps=v.eps)
             self.sp.attention(q, k, vv, q, heads=h, gate=ws.gates)
-        ops.linear(q, p["o1_w"], x, bias=p["o1_b"], kind=ops.EPI_GATED_RESIDUAL, residual=x,
-                   gate=val(2))
+        self._lin(q, p, "o1_w", x, bias=p["o1_b"], kind=ops.EPI_GATED_RESIDUAL,
+                   residual=x, gate=val(2))
         # text cross-attention with the prompt-modulated context
         pr = lambda j: ws.prompt[:, i, j * d : (j + 1) * d]
         ops.adaln(x, val(6), val(7), nrm, norm=ops.NORM_RMS, eps=v.eps)
         ops.adaln(prepared.context, pr(0), pr(1), ws.ctxm, norm=ops.NORM_NONE)
-        ops.linear(nrm, p["g2_w"], ws.gates, bias=p["g2_b"], kind=ops.EPI_SIGMOID2)
-        ops.linear(nrm, p["q2_w"], q, bias=p["q2_b"])
-        ops.linear(ws.ctxm, p["kv2_w"], ws.ctxkv, bias=p["kv2_b"])
+        self._lin(nrm, p, "g2_w", ws.gates, bias=p["g2_b"], kind=ops.EPI_SIGMOID2)
+        self._lin(nrm, p, "q2_w", q, bias=p["q2_b"])
+        self._lin(ws.ctxm, p, "kv2_w", ws.ctxkv, bias=p["kv2_b"])
         k2, v2 = ws.ctxkv[..., :d], ws.ctxkv[..., d:]
         ops.qk_norm_rope(q, heads=h, weight=p["qn2"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_NONE,
                          eps=v.eps)
         ops.qk_norm_rope(k2, heads=h, weight=p["kn2"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_NONE,
                          eps=v.eps)
         ops.attention([q], [k2], [v2], [q], heads=h, gate=[ws.gates])
-        ops.linear(q, p["o2_w"], x, bias=p["o2_b"], kind=ops.EPI_GATED_RESIDUAL, residual=x,
-                   gate=val(8))
+        self._lin(q, p, "o2_w", x, bias=p["o2_b"], kind=ops.EPI_GATED_RESIDUAL,
+                   residual=x, gate=val(8))
         # feed-forward
         ops.adaln(x, val(3), val(4), nrm, norm=ops.NORM_RMS, eps=v.eps)
-        ops.linear(nrm, p["ff_in_w"], ws.hid, bias=p["ff_in_b"], kind=ops.EPI_GELU)
-        ops.linear(ws.hid, p["ff_out_w"], x, bias=p["ff_out_b"], kind=ops.EPI_GATED_RESIDUAL,
-                   residual=x, gate=val(5))
+        self._lin(nrm, p, "ff_in_w", ws.hid, bias=p["ff_in_b"], kind=ops.EPI_GELU)
+        self._lin(ws.hid, p, "ff_out_w", x, bias=p["ff_out_b"],
+                   kind=ops.EPI_GATED_RESIDUAL, residual=x, gate=val(5))
 
     # ------------------------------------------------------------------ forward
     def run(self, prepared: PreparedContext, latent: torch.Tensor, sigma: float, *,

@@ -215,6 +215,7 @@ def linear(
     lead_rows: int = 0,
     lead_qk_norm: list[torch.Tensor] | None = None,
     lead_gate: torch.Tensor | None = None,
+    bias_after_round: bool = False,
 ) -> torch.Tensor:
     """out = epilogue(x @ w.T) for x (batch, m, k) or (m, k) and an (n, k) weight.
 
@@ -302,6 +303,7 @@ def linear(
         if lead_gate is not None:
             _need(lead_gate, "lead gate")
             epi.gate_lead = lead_gate.data_ptr()
+    epi.bias_after_round = int(bias_after_round)
     if scatter is not None:
         epi.scatter_ptrs = scatter.ptrs.data_ptr()
         epi.world = scatter.world
@@ -795,6 +797,85 @@ def group_norm(x: torch.Tensor, groups: int, weight: torch.Tensor, bias: torch.T
         _lib.call("kino_group_norm", _ptr(x), _ptr(weight), _ptr(bias), _ptr(out), voxels, c, eps,
                   int(silu), _ptr(workspace), workspace.numel() * workspace.element_size(), _stream())
     return out
+
+
+QUANT_MODES = {"affine": 0, "mxfp8": 1, "mxfp4": 2, "nvfp4": 3}
+
+
+def dequantize(
+    words: torch.Tensor,
+    scales: torch.Tensor,
+    biases: torch.Tensor | None,
+    *,
+    mode: str,
+    group_size: int,
+    bits: int,
+    transpose_out: bool = False,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """bf16 weight from packed codes `words` ((rows, cols * bits / 32) 32-bit words), per-group
+    `scales` (bf16 for affine, uint8 E8M0 / E4M3 codes otherwise) and affine `biases`; (rows, cols),
+    or (cols, rows) with `transpose_out`."""
+    if mode not in QUANT_MODES:
+        raise ValueError(f"unknown quantisation mode {mode!r}")
+    if words.dtype not in (torch.int32, torch.uint32) or not words.is_cuda or not words.is_contiguous():
+        raise ValueError("words must be a contiguous CUDA int32/uint32 tensor")
+    rows = words.shape[0]
+    cols = words.shape[1] * 32 // bits
+    if mode == "affine":
+        _need(scales, "scales")
+        if biases is None:
+            raise ValueError("affine mode needs biases")
+        _need(biases, "biases")
+    else:
+        _need(scales, "scales", torch.uint8)
+    if tuple(scales.shape) != (rows, cols // group_size):
+        raise ValueError(f"scales {tuple(scales.shape)} do not match {rows} x {cols} in groups of {group_size}")
+    shape = (cols, rows) if transpose_out else (rows, cols)
+    if out is None:
+        out = torch.empty(shape, device=words.device, dtype=torch.bfloat16)
+    elif tuple(out.shape) != shape:
+        raise ValueError(f"out must be {shape}")
+    with _timed("dequant", 0.0, words.numel() * 4 + out.numel() * 2):
+        _lib.call("kino_dequantize", _ptr(words), _ptr(scales), _ptr(biases), _ptr(out), rows, cols,
+                  QUANT_MODES[mode], group_size, bits, int(transpose_out), _stream())
+    return out
+
+
+def quantized_linear(
+    x: torch.Tensor,
+    words: torch.Tensor,
+    scales: torch.Tensor,
+    biases: torch.Tensor | None,
+    *,
+    mode: str,
+    group_size: int,
+    bits: int,
+    transpose: bool,
+    bias: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    scratch: torch.Tensor | None = None,
+    **epilogue,
+) -> torch.Tensor:
+    """MLX quantized_matmul semantics on the tcgen05 GEMM: `transpose` -> x @ W^T with W packed as
+    (out, in) along `in`; otherwise x @ W with W packed from weight.T as (in, out) along `out`.
+    The weight is dequantised into `scratch` (a bf16 buffer of at least out x in elements, reused
+    by every call on the stream) and multiplied with fp32 accumulation; the product is rounded to
+    bf16 before the bias is added, as the reference's quantised linear does; `epilogue` keywords
+    go to `linear` (kind, residual, gate, ...)."""
+    rows = words.shape[0]
+    cols = words.shape[1] * 32 // bits
+    n, k = (rows, cols) if transpose else (cols, rows)
+    if scratch is None:
+        w = torch.empty((n, k), device=words.device, dtype=torch.bfloat16)
+    else:
+        if scratch.dtype != torch.bfloat16 or scratch.numel() < n * k:
+            raise ValueError("scratch must be a bf16 buffer of at least out x in elements")
+        w = scratch.view(-1)[: n * k].view(n, k)
+    dequantize(words, scales, biases, mode=mode, group_size=group_size, bits=bits,
+               transpose_out=not transpose, out=w)
+    epilogue.setdefault("bias_after_round", True)
+    return linear(x, w, out, bias=bias, **epilogue)
 
 
 def conv_workspace(device: torch.device | None = None) -> torch.Tensor:

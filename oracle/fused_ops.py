@@ -86,6 +86,16 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> t
     return y.to(x.dtype)
 
 
+def linear_then_bias(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None) -> torch.Tensor:
+    """A packed (quantised) linear: the matmul rounded to the activation dtype, then the bias added
+    as a separate bf16 operation (kinomlx/models/ltx2/weights/quantization.py:32-43:
+    `mx.quantized_matmul(...)` then `result + bias`)."""
+    y = (x.float() @ w.float().T).to(x.dtype)
+    if b is not None:
+        y = (y.float() + b.float()).to(x.dtype)
+    return y
+
+
 def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
     """Scaled dot-product attention on (B, H, T, D) in fp32, one rounding
     (mx.fast.scaled_dot_product_attention at kinomlx/models/flux2/kv.py:48-54)."""

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 
 import torch
 
-from .fused_ops import gelu_approx, layer_norm, linear, rms_norm, sdpa, silu
+from .fused_ops import gelu_approx, layer_norm, linear, linear_then_bias, rms_norm, sdpa, silu
 
 
 @dataclass(frozen=True)
@@ -31,6 +31,13 @@ class LTXVariant:
     out_channels: int = 128
     blocks: int = 48
     timestep_scale: float = 1000.0
+    # the block linears packed (the reference's transformer_quantize modes): each runs as a
+    # quantised matmul rounded to bf16, then + bias (weights/quantization.py:32-43)
+    packed_blocks: bool = False
+
+
+def _blin(v: LTXVariant):
+    return linear_then_bias if getattr(v, "packed_blocks", False) else linear
 
 
 def _f32(x: float) -> float:
@@ -148,13 +155,14 @@ def attention(p: dict, prefix: str, x: torch.Tensor, v: LTXVariant, *, context=N
     """Gated attention with Q/K RMSNorm over all heads and split RoPE
     (kinomlx/models/ltx2/transformer/attention.py:249-371)."""
     g = lambda name: p[f"{prefix}.{name}"]
+    lin = _blin(v)
     gate = None
     if v.gated_attention:
-        gate = 2.0 * torch.sigmoid(linear(x, g("to_gate_logits.weight"), g("to_gate_logits.bias")).float()).to(x.dtype)
+        gate = 2.0 * torch.sigmoid(lin(x, g("to_gate_logits.weight"), g("to_gate_logits.bias")).float()).to(x.dtype)
     src = x if context is None else context
-    value = linear(src, g("to_v.weight"), g("to_v.bias"))
-    q = rms_norm(linear(x, g("to_q.weight"), g("to_q.bias")), g("q_norm.weight"), v.eps)
-    k = rms_norm(linear(src, g("to_k.weight"), g("to_k.bias")), g("k_norm.weight"), v.eps)
+    value = lin(src, g("to_v.weight"), g("to_v.bias"))
+    q = rms_norm(lin(x, g("to_q.weight"), g("to_q.bias")), g("q_norm.weight"), v.eps)
+    k = rms_norm(lin(src, g("to_k.weight"), g("to_k.bias")), g("k_norm.weight"), v.eps)
     if pe is not None:
         q = apply_split_rotary_emb(q, *pe)
         k = apply_split_rotary_emb(k, *pe)
@@ -167,13 +175,13 @@ def attention(p: dict, prefix: str, x: torch.Tensor, v: LTXVariant, *, context=N
     if gate is not None:
         out = out * gate[..., None]
     out = out.reshape(b, tq, heads * d)
-    return linear(out, g("to_out.weight"), g("to_out.bias"))
+    return lin(out, g("to_out.weight"), g("to_out.bias"))
 
 
-def feed_forward(p: dict, prefix: str, x: torch.Tensor) -> torch.Tensor:
+def feed_forward(p: dict, prefix: str, x: torch.Tensor, lin=linear) -> torch.Tensor:
     """proj -> GELU-tanh (fp32 opmath) -> proj (ltx2/transformer/feed_forward.py:37-97)."""
-    h = gelu_approx(linear(x, p[f"{prefix}.project_in.proj.weight"], p[f"{prefix}.project_in.proj.bias"]))
-    return linear(h, p[f"{prefix}.project_out.weight"], p[f"{prefix}.project_out.bias"])
+    h = gelu_approx(lin(x, p[f"{prefix}.project_in.proj.weight"], p[f"{prefix}.project_in.proj.bias"]))
+    return lin(h, p[f"{prefix}.project_out.weight"], p[f"{prefix}.project_out.bias"])
 
 
 def video_block(p: dict, i: int, x, context, timesteps, prompt_timestep, pe, v: LTXVariant):
@@ -195,7 +203,7 @@ def video_block(p: dict, i: int, x, context, timesteps, prompt_timestep, pe, v: 
     x = (x + (cross * gate_c).to(x.dtype)).to(x.dtype)
     shift, scale, gate = vals[:, :, 3], vals[:, :, 4], vals[:, :, 5]
     normalized = adaln(x, scale, shift, v.eps)
-    return (x + feed_forward(p, f"{a}.ff", normalized) * gate).to(x.dtype)
+    return (x + feed_forward(p, f"{a}.ff", normalized, _blin(v)) * gate).to(x.dtype)
 
 
 def forward(p: dict, latent, context, sigma: float, positions, v: LTXVariant, dtype=torch.bfloat16):
