@@ -30,7 +30,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (6); bumped on any signature change. */
+/* ABI version of this header (7); bumped on any signature change. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -407,6 +407,84 @@ kino_status kino_tile_blend(const void* decoded, int64_t frames, int64_t height,
 /* canvas[p, y, x] /= max(weights[y, x], 1e-8) (kinomlx/models/ltx2/video_vae/tiling.py:1369). */
 kino_status kino_blend_normalize(float* canvas, const float* weights, int64_t planes, int64_t hw,
                                  void* stream);
+
+/* ------------------------------------------------------------------ fp32 parity mode
+ * The Flux2 block operators in single precision on the CUDA cores, for the reference's fp32
+ * graph (MLX arrays in float32; BASELINE's fp32 gate is a per-op max relative error <= 1e-4).
+ * Every product and sum is fp32; where the reference's graph has separate operations the
+ * results are rounded separately (no fused multiply-add in the epilogues). Tensors are float*,
+ * strides in elements, row strides multiples of 4 with 16-byte aligned operands. */
+
+typedef struct kino_epilogue_f32 {
+  int kind;                /* KINO_EPI_NONE, KINO_EPI_GELU, KINO_EPI_GATED_RESIDUAL, KINO_EPI_EULER */
+  const float* bias;       /* [n] or NULL: acc + bias */
+  const float* residual;   /* GATED_RESIDUAL: out = residual + gate[b] * (acc + bias); may alias out */
+  int64_t ld_residual;
+  int64_t bs_residual;
+  const float* gate;       /* GATED_RESIDUAL: [batch][n] at batch stride bs_gate */
+  int64_t bs_gate;
+  int64_t act_col_begin;   /* GELU: tanh-GELU (inner clamped to +-10) on columns >= act_col_begin */
+  float scalar;            /* EULER: out = aux + scalar * (acc + bias) */
+  const float* aux;        /* EULER: current sample, geometry of out; may alias out */
+  int64_t ld_aux;
+  int64_t bs_aux;
+} kino_epilogue_f32;
+
+/* kino_linear in fp32: out[b, i, j] = epilogue(sum_k x[b, i, k] * w[j, k]); w (n, k) row-major.
+ * k % 4 == 0. x and w must not overlap out. Replaces the fp32 case of kinomlx.kernels.mpp_linear
+ * .linear / mx.addmm (kinomlx/kernels/mpp_linear.py:469-506, kinomlx/modeling/layers.py:8-31),
+ * with the gated residual of kinomlx/models/flux2/transformer.py:159-167 and the Euler update of
+ * kinomlx/models/flux2/sampling.py:109-113 in the epilogue. */
+kino_status kino_linear_f32(const float* x, const float* w, float* out, int64_t batch, int64_t m,
+                            int64_t n, int64_t k, int64_t ldx, int64_t bsx, int64_t ldw,
+                            int64_t ldo, int64_t bso, const kino_epilogue_f32* epi, void* stream);
+
+/* softmax(q k^T * scale) v per (batch, head), head_dim 128, token-major q (q_tokens rows),
+ * k and v (kv_tokens rows); out like q and may alias it. Replaces MLX SDPA in fp32
+ * (kinomlx/models/flux2/kv.py:48-54, kinomlx/models/flux2/transformer.py:35-53). */
+kino_status kino_attention_f32(const float* q, const float* k, const float* v, float* out,
+                               int64_t batch, int64_t heads, int64_t q_tokens, int64_t kv_tokens,
+                               int64_t ld_q, int64_t bs_q, int64_t ld_k, int64_t bs_k,
+                               int64_t ld_v, int64_t bs_v, int64_t ld_out, int64_t bs_out,
+                               float scale, void* stream);
+
+/* kino_adaln in fp32: out = norm(x) * (1 + scale[b]) + shift[b], dim <= 8192
+ * (kinomlx/models/flux2/transformer.py:56-60). */
+kino_status kino_adaln_f32(const float* x, int64_t ldx, int64_t bsx, const float* shift,
+                           const float* scale, int64_t bs_mod, float* out, int64_t ldo,
+                           int64_t bso, int64_t batch, int64_t rows, int64_t dim, int norm_kind,
+                           float eps, void* stream);
+
+/* kino_qk_norm_rope in fp32, in place: KINO_QKNORM_PER_HEAD (or NONE) then KINO_ROPE_PAIRS (or
+ * NONE); tables token-major, (table_batch, table_tokens, 128) fp32. Replaces QKNorm + rotate
+ * (kinomlx/models/flux2/transformer.py:17-32, 68-75). */
+kino_status kino_qk_norm_rope_f32(float* x, int64_t ld, int64_t bs, int64_t batch,
+                                  int64_t tokens, int64_t heads, const float* weight,
+                                  int norm_kind, int rope_kind, const float* cos_table,
+                                  const float* sin_table, int table_batched, int64_t table_tokens,
+                                  int64_t table_offset, float eps, void* stream);
+
+/* fp32 tanh-GELU and SiLU (kinomlx/kernels/fused_ops.py:27-45, 327-372). */
+kino_status kino_gelu_tanh_f32(const float* x, float* out, int64_t n, void* stream);
+kino_status kino_silu_f32(const float* x, float* out, int64_t n, void* stream);
+
+/* out = uncond + guidance * (cond - uncond) (kinomlx/models/flux2/sampling.py:264-280). */
+kino_status kino_cfg_combine_f32(const float* cond, const float* uncond, float guidance,
+                                 float* out, int64_t n, void* stream);
+
+/* out = x + dt * v (kinomlx/models/flux2/sampling.py:109-113 with the model dtype fp32). */
+kino_status kino_euler_velocity_f32(const float* x, const float* v, float dt, float* out,
+                                    int64_t n, void* stream);
+
+/* out[b, r, c] = silu(x[b, r, c]) * x[b, r, width + c], gate half first
+ * (kinomlx/models/flux2/transformer.py:63-65); out may alias x. */
+kino_status kino_swiglu_f32(const float* x, int64_t ldx, int64_t bsx, float* out, int64_t ldo,
+                            int64_t bso, int64_t batch, int64_t rows, int64_t width,
+                            void* stream);
+
+/* kino_timestep_embedding with fp32 features (kinomlx/models/flux2/transformer.py:238-241). */
+kino_status kino_timestep_embedding_f32(const float* t, float* out, int64_t batch, int64_t dim,
+                                        void* stream);
 
 /* ------------------------------------------------------------------ peer memory (NVLink)
  * Buffers that the other GPUs of a sequence-parallel group map (CUDA IPC) and write into: the

@@ -146,6 +146,23 @@ class Conv3dArgs(ctypes.Structure):
     ]
 
 
+class EpilogueF32(ctypes.Structure):
+    _fields_ = [
+        ("kind", c_int),
+        ("bias", c_void_p),
+        ("residual", c_void_p),
+        ("ld_residual", c_int64),
+        ("bs_residual", c_int64),
+        ("gate", c_void_p),
+        ("bs_gate", c_int64),
+        ("act_col_begin", c_int64),
+        ("scalar", c_float),
+        ("aux", c_void_p),
+        ("ld_aux", c_int64),
+        ("bs_aux", c_int64),
+    ]
+
+
 class IpcHandle(ctypes.Structure):
     _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
@@ -200,6 +217,25 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_latent_to_bfhwc": (c_int, [P, P, P, P, I64, I64, P]),
     "kino_tile_blend": (c_int, [P, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, P, P, P]),
     "kino_blend_normalize": (c_int, [P, P, I64, I64, P]),
+    "kino_linear_f32": (
+        c_int,
+        [P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, POINTER(EpilogueF32), P],
+    ),
+    "kino_attention_f32": (
+        c_int,
+        [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, F, P],
+    ),
+    "kino_adaln_f32": (c_int, [P, I64, I64, P, P, I64, P, I64, I64, I64, I64, I64, c_int, F, P]),
+    "kino_qk_norm_rope_f32": (
+        c_int,
+        [P, I64, I64, I64, I64, I64, P, c_int, c_int, P, P, c_int, I64, I64, F, P],
+    ),
+    "kino_gelu_tanh_f32": (c_int, [P, P, I64, P]),
+    "kino_silu_f32": (c_int, [P, P, I64, P]),
+    "kino_cfg_combine_f32": (c_int, [P, P, F, P, I64, P]),
+    "kino_euler_velocity_f32": (c_int, [P, P, F, P, I64, P]),
+    "kino_swiglu_f32": (c_int, [P, I64, I64, P, I64, I64, I64, I64, I64, P]),
+    "kino_timestep_embedding_f32": (c_int, [P, P, I64, I64, P]),
     "kino_peer_alloc": (c_int, [I64, POINTER(c_void_p), POINTER(IpcHandle)]),
     "kino_peer_free": (c_int, [P]),
     "kino_peer_open": (c_int, [POINTER(IpcHandle), POINTER(c_void_p)]),

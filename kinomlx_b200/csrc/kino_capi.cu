@@ -17,6 +17,7 @@
 #include "kino_peer.cuh"
 #include "kino_vae.cuh"
 #include "kino_quant.cuh"
+#include "kino_f32.cuh"
 
 // Scratch of kino_group_norm_noalloc: a fixed device array that every GPU loading this library
 // holds until the process exits. Host code only sees a stand-in symbol for it, so its device
@@ -457,7 +458,7 @@ void* group_norm_scratch_address(kino_status* status) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 6; }
+int kino_abi_version(void) { return 7; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -1306,6 +1307,193 @@ kino_status kino_peer_barrier(void* const* flags, int64_t rank, int64_t world, i
              reinterpret_cast<uint32_t* const*>(flags), static_cast<int>(rank),
              static_cast<int>(world), static_cast<uint32_t>(epoch));
   return check_launch("kino_peer_barrier");
+}
+
+
+// ---------------------------------------------------------------- fp32 parity mode
+kino_status kino_linear_f32(const float* x, const float* w, float* out, int64_t batch, int64_t m,
+                            int64_t n, int64_t k, int64_t ldx, int64_t bsx, int64_t ldw,
+                            int64_t ldo, int64_t bso, const kino_epilogue_f32* epi,
+                            void* stream) {
+  if (x == nullptr || w == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_linear_f32: null operand");
+  if (batch < 1 || m < 1 || n < 1 || k < 1) return fail(KINO_EINVAL, "kino_linear_f32: empty shape");
+  if (k % 4 || ldx % 4 || ldw % 4 || bsx % 4 || !aligned16(x) || !aligned16(w))
+    return fail(KINO_ENOTSUPPORTED, "kino_linear_f32: k and the operand strides must be multiples "
+                "of 4 with 16-byte aligned operands");
+  if (ldx < k || ldw < k || ldo < n) return fail(KINO_EINVAL, "kino_linear_f32: stride below width");
+  if (m > 0x7fffffffLL || n > 0x7fffffffLL || k > 0x7fffffffLL || batch > 65535 ||
+      (m + kino::F32_BM - 1) / kino::F32_BM > 65535)
+    return fail(KINO_ENOTSUPPORTED, "kino_linear_f32: shape too large");
+  kino::F32Epi e;
+  std::memset(&e, 0, sizeof(e));
+  if (epi != nullptr) {
+    if (epi->kind < KINO_EPI_NONE || epi->kind > KINO_EPI_EULER)
+      return fail(KINO_ENOTSUPPORTED, "kino_linear_f32: epilogue %d (NONE, GELU, GATED_RESIDUAL "
+                  "or EULER)", epi->kind);
+    if (epi->kind == KINO_EPI_GATED_RESIDUAL && (epi->residual == nullptr || epi->gate == nullptr))
+      return fail(KINO_EINVAL, "kino_linear_f32: gated residual needs residual and gate");
+    if (epi->kind == KINO_EPI_EULER && epi->aux == nullptr)
+      return fail(KINO_EINVAL, "kino_linear_f32: Euler epilogue needs the sample");
+    e.kind = epi->kind;
+    e.bias = epi->bias;
+    e.residual = epi->residual;
+    e.ld_res = epi->ld_residual;
+    e.bs_res = epi->bs_residual;
+    e.gate = epi->gate;
+    e.bs_gate = epi->bs_gate;
+    e.act_col_begin = epi->act_col_begin;
+    e.scalar = epi->scalar;
+    e.aux = epi->aux;
+    e.ld_aux = epi->ld_aux;
+    e.bs_aux = epi->bs_aux;
+  }
+  const dim3 grid(static_cast<unsigned>((n + kino::F32_BN - 1) / kino::F32_BN),
+                  static_cast<unsigned>((m + kino::F32_BM - 1) / kino::F32_BM),
+                  static_cast<unsigned>(batch));
+  launch_pdl(kino::gemm_f32_kernel, grid, dim3(kino::F32_THREADS), 0,
+             static_cast<cudaStream_t>(stream), x, w, out, static_cast<int>(m),
+             static_cast<int>(n), static_cast<int>(k), ldx, bsx, ldw, ldo, bso, e);
+  return check_launch("kino_linear_f32");
+}
+
+kino_status kino_attention_f32(const float* q, const float* k, const float* v, float* out,
+                               int64_t batch, int64_t heads, int64_t q_tokens, int64_t kv_tokens,
+                               int64_t ld_q, int64_t bs_q, int64_t ld_k, int64_t bs_k,
+                               int64_t ld_v, int64_t bs_v, int64_t ld_out, int64_t bs_out,
+                               float scale, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_attention_f32: null operand");
+  if (batch < 1 || heads < 1 || q_tokens < 1 || kv_tokens < 1)
+    return fail(KINO_EINVAL, "kino_attention_f32: empty shape");
+  if (batch > 65535 || heads > 65535 || q_tokens > 0x7fffffffLL || kv_tokens > 0x7fffffffLL)
+    return fail(KINO_ENOTSUPPORTED, "kino_attention_f32: shape too large");
+  if (ld_q % 4 || ld_k % 4 || ld_v % 4 || ld_out % 4 || bs_q % 4 || bs_k % 4 || bs_v % 4 ||
+      bs_out % 4 || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(KINO_ENOTSUPPORTED, "kino_attention_f32: strides must be multiples of 4 with "
+                "16-byte aligned operands");
+  if (ld_q < heads * 128 || ld_k < heads * 128 || ld_v < heads * 128 || ld_out < heads * 128)
+    return fail(KINO_EINVAL, "kino_attention_f32: row stride below heads * 128");
+  const int smem = static_cast<int>(sizeof(kino::Fa32Smem));
+  kino_status st = ensure_smem(kino::attention_f32_kernel, smem, 10);
+  if (st != KINO_OK) return st;
+  const dim3 grid(static_cast<unsigned>((q_tokens + kino::FA32_BQ - 1) / kino::FA32_BQ),
+                  static_cast<unsigned>(heads), static_cast<unsigned>(batch));
+  launch_pdl(kino::attention_f32_kernel, grid, dim3(kino::FA32_THREADS), smem,
+             static_cast<cudaStream_t>(stream), q, k, v, out, static_cast<int>(q_tokens),
+             static_cast<int>(kv_tokens), ld_q, bs_q, ld_k, bs_k, ld_v, bs_v, ld_out, bs_out,
+             scale);
+  return check_launch("kino_attention_f32");
+}
+
+kino_status kino_adaln_f32(const float* x, int64_t ldx, int64_t bsx, const float* shift,
+                           const float* scale, int64_t bs_mod, float* out, int64_t ldo,
+                           int64_t bso, int64_t batch, int64_t rows, int64_t dim, int norm_kind,
+                           float eps, void* stream) {
+  if (x == nullptr || shift == nullptr || scale == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_adaln_f32: null");
+  if (dim < 1 || dim > 32 * kino::ADALN32_THREADS)
+    return fail(KINO_ENOTSUPPORTED, "kino_adaln_f32: dim must be 1..8192");
+  if (rows < 1 || batch < 1 || batch * rows > 0x7fffffffLL)
+    return fail(KINO_EINVAL, "kino_adaln_f32: rows/batch");
+  if (norm_kind < KINO_NORM_RMS || norm_kind > KINO_NORM_NONE)
+    return fail(KINO_EINVAL, "kino_adaln_f32: norm kind");
+  launch_pdl(kino::adaln_f32_kernel, dim3(static_cast<unsigned>(batch * rows)),
+             dim3(kino::ADALN32_THREADS), 0, static_cast<cudaStream_t>(stream), x, ldx, bsx,
+             shift, scale, bs_mod, out, ldo, bso, static_cast<int>(rows), static_cast<int>(dim),
+             norm_kind, eps);
+  return check_launch("kino_adaln_f32");
+}
+
+kino_status kino_qk_norm_rope_f32(float* x, int64_t ld, int64_t bs, int64_t batch,
+                                  int64_t tokens, int64_t heads, const float* weight,
+                                  int norm_kind, int rope_kind, const float* cos_table,
+                                  const float* sin_table, int table_batched, int64_t table_tokens,
+                                  int64_t table_offset, float eps, void* stream) {
+  if (x == nullptr) return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: null");
+  if ((norm_kind != KINO_QKNORM_NONE && norm_kind != KINO_QKNORM_PER_HEAD) ||
+      (rope_kind != KINO_ROPE_NONE && rope_kind != KINO_ROPE_PAIRS))
+    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: per-head norm and pair RoPE only");
+  if (norm_kind == KINO_QKNORM_PER_HEAD && (weight == nullptr || !aligned16(weight)))
+    return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: norm needs an aligned weight");
+  if (rope_kind == KINO_ROPE_PAIRS &&
+      (cos_table == nullptr || sin_table == nullptr || !aligned16(cos_table) ||
+       !aligned16(sin_table)))
+    return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: rope needs aligned tables");
+  if (ld % 4 || bs % 4 || !aligned16(x) || ld < heads * 128)
+    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: aligned rows of heads * 128");
+  if (tokens < 1 || batch < 1 || heads < 1) return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: empty");
+  if (rope_kind == KINO_ROPE_PAIRS && (table_offset < 0 || table_offset + tokens > table_tokens))
+    return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: table too short");
+  const int64_t items = batch * tokens * heads;
+  const int64_t blocks = (items + 7) / 8;
+  if (blocks > 0x7fffffffLL || tokens > 0x7fffffffLL)
+    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: shape too large");
+  launch_pdl(kino::qk_norm_rope_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), x, ld, bs, static_cast<int>(tokens),
+             static_cast<int>(heads), weight, norm_kind == KINO_QKNORM_PER_HEAD ? 1 : 0,
+             rope_kind == KINO_ROPE_PAIRS ? 1 : 0, cos_table, sin_table, table_batched,
+             table_tokens, table_offset, eps, items);
+  return check_launch("kino_qk_norm_rope_f32");
+}
+
+static kino_status launch_elem_f32(int kind, const float* a, const float* b, float* out,
+                                   int64_t n, float s0, void* stream, const char* name) {
+  if (a == nullptr || out == nullptr) return fail(KINO_EINVAL, "%s: null", name);
+  if (n < 0) return fail(KINO_EINVAL, "%s: negative size", name);
+  if (n == 0) return KINO_OK;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  launch_pdl(kino::elementwise_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), kind, a, b, out, n, s0);
+  return check_launch(name);
+}
+
+kino_status kino_gelu_tanh_f32(const float* x, float* out, int64_t n, void* stream) {
+  return launch_elem_f32(kino::ELEM32_GELU, x, nullptr, out, n, 0.f, stream, "kino_gelu_tanh_f32");
+}
+
+kino_status kino_silu_f32(const float* x, float* out, int64_t n, void* stream) {
+  return launch_elem_f32(kino::ELEM32_SILU, x, nullptr, out, n, 0.f, stream, "kino_silu_f32");
+}
+
+kino_status kino_cfg_combine_f32(const float* cond, const float* uncond, float guidance,
+                                 float* out, int64_t n, void* stream) {
+  if (uncond == nullptr) return fail(KINO_EINVAL, "kino_cfg_combine_f32: null");
+  return launch_elem_f32(kino::ELEM32_CFG, cond, uncond, out, n, guidance, stream,
+                         "kino_cfg_combine_f32");
+}
+
+kino_status kino_euler_velocity_f32(const float* x, const float* v, float dt, float* out,
+                                    int64_t n, void* stream) {
+  if (v == nullptr) return fail(KINO_EINVAL, "kino_euler_velocity_f32: null");
+  return launch_elem_f32(kino::ELEM32_EULER_V, x, v, out, n, dt, stream, "kino_euler_velocity_f32");
+}
+
+kino_status kino_swiglu_f32(const float* x, int64_t ldx, int64_t bsx, float* out, int64_t ldo,
+                            int64_t bso, int64_t batch, int64_t rows, int64_t width,
+                            void* stream) {
+  if (x == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_swiglu_f32: null");
+  if (batch < 1 || rows < 1 || width < 1 || width > 0x7fffffffLL || ldx < 2 * width ||
+      ldo < width)
+    return fail(KINO_EINVAL, "kino_swiglu_f32: shape/strides");
+  const int64_t total = batch * rows * width;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  launch_pdl(kino::swiglu_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), x, ldx, bsx, out, ldo, bso, rows,
+             static_cast<int>(width), total);
+  return check_launch("kino_swiglu_f32");
+}
+
+kino_status kino_timestep_embedding_f32(const float* t, float* out, int64_t batch, int64_t dim,
+                                        void* stream) {
+  if (t == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_timestep_embedding_f32: null");
+  if (batch < 1 || batch > 65535 || dim < 2 || dim % 2)
+    return fail(KINO_EINVAL, "kino_timestep_embedding_f32: batch 1..65535, even dim");
+  launch_pdl(kino::timestep_embedding_f32_kernel, dim3(static_cast<unsigned>(batch)), dim3(128),
+             0, static_cast<cudaStream_t>(stream), t, out, static_cast<int>(dim));
+  return check_launch("kino_timestep_embedding_f32");
 }
 
 }  // extern "C"

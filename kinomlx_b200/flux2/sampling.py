@@ -13,7 +13,7 @@ import math
 import numpy as np
 import torch
 
-from .. import ops
+from .. import ops, ops_f32
 from .transformer import Flux2Transformer, PreparedText
 
 
@@ -35,10 +35,12 @@ def linear_sigmas(steps: int) -> torch.Tensor:
     return torch.from_numpy(np.linspace(1.0, 0.0, steps + 1).astype(np.float32))
 
 
-def timestep_x1000(sigmas: torch.Tensor, index: int, batch: int = 1) -> torch.Tensor:
-    """The value entering the timestep embedding: ((s*1000 -> bf16) / 1000 -> bf16) * 1000 -> bf16
-    (kinomlx/models/flux2/sampling.py:209-212 and transformer.py:315)."""
-    t = ((sigmas[index : index + 1] * 1000).to(torch.bfloat16) / 1000).to(torch.bfloat16)
+def timestep_x1000(sigmas: torch.Tensor, index: int, batch: int = 1,
+                   dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """The value entering the timestep embedding: ((s*1000 -> dtype) / 1000 -> dtype) * 1000 ->
+    dtype, with dtype the model's (kinomlx/models/flux2/sampling.py:209-212 and
+    transformer.py:315); returned as fp32."""
+    t = ((sigmas[index : index + 1] * 1000).to(dtype) / 1000).to(dtype)
     return (t * 1000).to(torch.float32).repeat(batch)
 
 
@@ -57,15 +59,20 @@ def denoise_step(
     guidance: float = 1.0,
     cfg: bool = False,
 ) -> torch.Tensor:
-    """One Euler step in place on `current` (1, Ni, C); returns `current`."""
+    """One Euler step in place on `current` (1, Ni, C); returns `current`. The model's `dtype`
+    (bf16, or fp32 for the parity-mode transformer) sets the timestep rounding and the
+    elementwise kernels."""
     dt = step_delta(sigmas, index)
+    dtype = getattr(model, "dtype", torch.bfloat16)
+    elementwise = ops_f32 if dtype == torch.float32 else ops
     if not cfg:
-        t = timestep_x1000(sigmas, index, current.shape[0]).to(current.device, non_blocking=True)
+        t = timestep_x1000(sigmas, index, current.shape[0], dtype).to(current.device,
+                                                                      non_blocking=True)
         return model.run(prepared, current, t, euler_dt=dt, sample=current, out=current)
-    t = timestep_x1000(sigmas, index, 2).to(current.device, non_blocking=True)
+    t = timestep_x1000(sigmas, index, 2, dtype).to(current.device, non_blocking=True)
     both = model.run(prepared, current.repeat(2, 1, 1), t)
-    velocity = ops.cfg_combine(both[0:1], both[1:2], guidance)
-    return ops.euler_velocity(current, velocity, dt, out=current)
+    velocity = elementwise.cfg_combine(both[0:1], both[1:2], guidance)
+    return elementwise.euler_velocity(current, velocity, dt, out=current)
 
 
 def denoise(
@@ -90,7 +97,7 @@ def denoise(
     conditioned = text if not cfg else torch.cat([text, negative])
     prepared = model.prepare(conditioned, ids)
     i0, i1 = model.sp.shard(noise.shape[1])
-    current = noise[:, i0:i1].to(model.device, torch.bfloat16).clone()
+    current = noise[:, i0:i1].to(model.device, getattr(model, "dtype", torch.bfloat16)).clone()
     for index in range(len(sigmas) - 1):
         denoise_step(model, prepared, current, sigmas, index, guidance=guidance, cfg=cfg)
     current = model.sp.all_gather_tokens(current)

@@ -1,0 +1,250 @@
+"""fp32 parity mode: torch front end of the kino_*_f32 entry points.
+
+The reference's graphs run in whatever dtype their arrays carry; in float32 every MLX op keeps
+fp32 (kinomlx/kernels/fused_ops.py's fp32 opmath, mx.addmm, mx.fast.scaled_dot_product_attention).
+These wrappers take fp32 CUDA tensors and launch the fp32 kernels; like `ops`, they have no CPU
+path and raise on a tensor of another device or dtype.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import EPI_EULER, EPI_GATED_RESIDUAL, EPI_GELU, EPI_NONE, NORM_LAYER
+from .ops import _as3d, _need, _ptr, _stream, _timed
+
+F32 = torch.float32
+
+__all__ = [
+    "adaln",
+    "attention",
+    "cfg_combine",
+    "euler_velocity",
+    "gelu_tanh",
+    "linear",
+    "qk_norm_rope",
+    "silu",
+    "swiglu",
+    "timestep_embedding",
+]
+
+
+def linear(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    out: torch.Tensor | None = None,
+    *,
+    bias: torch.Tensor | None = None,
+    kind: int = EPI_NONE,
+    residual: torch.Tensor | None = None,
+    gate: torch.Tensor | None = None,
+    act_col_begin: int = 0,
+    dt: float = 0.0,
+    sample: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """out = epilogue(x @ w.T) in fp32 for x (batch, m, k) or (m, k) and an (n, k) weight.
+    EPI_GELU applies to columns >= act_col_begin; EPI_GATED_RESIDUAL computes
+    residual + gate * y (gate (batch, n)); EPI_EULER computes sample + dt * y."""
+    _need(x, "x", F32)
+    _need(w, "w", F32)
+    x3 = _as3d(x)
+    batch, m, k = x3.shape
+    n = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"weight {tuple(w.shape)} does not match input width {k}")
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n), device=x.device, dtype=F32)
+    _need(out, "out", F32)
+    o3 = _as3d(out)
+    if tuple(o3.shape) != (batch, m, n):
+        raise ValueError(f"out {tuple(out.shape)} does not match ({batch}, {m}, {n})")
+    epi = _lib.EpilogueF32()
+    epi.kind = kind
+    if bias is not None:
+        _need(bias, "bias", F32)
+        epi.bias = bias.data_ptr()
+    if kind == EPI_GATED_RESIDUAL:
+        if residual is None or gate is None:
+            raise ValueError("a gated residual needs residual and gate")
+        _need(residual, "residual", F32)
+        _need(gate, "gate", F32)
+        r3 = _as3d(residual)
+        epi.residual = r3.data_ptr()
+        epi.ld_residual = r3.stride(1)
+        epi.bs_residual = r3.stride(0)
+        g = gate.reshape(-1, gate.shape[-1]) if gate.dim() != 2 else gate
+        epi.gate = g.data_ptr()
+        epi.bs_gate = g.stride(0) if g.shape[0] > 1 else 0
+    elif kind == EPI_GELU:
+        epi.act_col_begin = act_col_begin
+    elif kind == EPI_EULER:
+        if sample is None:
+            raise ValueError("the Euler epilogue needs the current sample")
+        _need(sample, "sample", F32)
+        s3 = _as3d(sample)
+        epi.aux = s3.data_ptr()
+        epi.ld_aux = s3.stride(1)
+        epi.bs_aux = s3.stride(0)
+        epi.scalar = dt
+    elif kind != EPI_NONE:
+        raise ValueError(f"epilogue {kind} has no fp32 form")
+    with _timed("gemm_f32", 2.0 * batch * m * n * k, 4.0 * (batch * m * k + n * k + batch * m * n)):
+        _lib.call("kino_linear_f32", _ptr(x3), _ptr(w), _ptr(o3), batch, m, n, k, x3.stride(1),
+                  x3.stride(0), w.stride(0), o3.stride(1), o3.stride(0), ctypes.byref(epi),
+                  _stream())
+    return out
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None,
+              *, heads: int, scale: float | None = None) -> torch.Tensor:
+    """softmax(q k^T * scale) v with q, k, v (batch, tokens, heads * 128) token-major fp32;
+    `out` may be `q` itself."""
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t, name, F32)
+    q3, k3, v3 = _as3d(q), _as3d(k), _as3d(v)
+    batch, tq, width = q3.shape
+    if width != heads * 128 or k3.shape[-1] != width or v3.shape[-1] != width:
+        raise ValueError("fp32 attention takes 128-wide heads")
+    if k3.shape[:2] != v3.shape[:2] or k3.shape[0] != batch:
+        raise ValueError("k and v must share (batch, tokens) with q's batch")
+    if out is None:
+        out = torch.empty(q.shape, device=q.device, dtype=F32)
+    _need(out, "out", F32)
+    o3 = _as3d(out)
+    tk = k3.shape[1]
+    sc = scale if scale is not None else 128**-0.5
+    flops = 4.0 * batch * heads * tq * tk * 128
+    with _timed("attention_f32", flops, 4.0 * batch * width * (2 * tq + 2 * tk)):
+        _lib.call("kino_attention_f32", _ptr(q3), _ptr(k3), _ptr(v3), _ptr(o3), batch, heads, tq,
+                  tk, q3.stride(1), q3.stride(0), k3.stride(1), k3.stride(0), v3.stride(1),
+                  v3.stride(0), o3.stride(1), o3.stride(0), sc, _stream())
+    return out
+
+
+def adaln(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+          out: torch.Tensor | None = None, *, norm: int = NORM_LAYER,
+          eps: float = 1e-6) -> torch.Tensor:
+    """norm(x) * (1 + scale) + shift in fp32; x (batch, rows, dim), shift/scale (batch, dim)."""
+    _need(x, "x", F32)
+    _need(shift, "shift", F32)
+    _need(scale, "scale", F32)
+    x3 = _as3d(x)
+    batch, rows, dim = x3.shape
+    if out is None:
+        out = torch.empty(x.shape, device=x.device, dtype=F32)
+    _need(out, "out", F32)
+    o3 = _as3d(out)
+    sh = shift.reshape(-1, dim)
+    sc = scale.reshape(-1, dim)
+    if sh.stride(0) != sc.stride(0):
+        raise ValueError("shift and scale need the same batch stride")
+    with _timed("adaln_f32", 0.0, 2.0 * 4 * batch * rows * dim):
+        _lib.call("kino_adaln_f32", _ptr(x3), x3.stride(1), x3.stride(0), _ptr(sh), _ptr(sc),
+                  sh.stride(0) if sh.shape[0] > 1 else 0, _ptr(o3), o3.stride(1), o3.stride(0),
+                  batch, rows, dim, norm, eps, _stream())
+    return out
+
+
+def qk_norm_rope(x: torch.Tensor, *, heads: int, weight: torch.Tensor | None, norm: int,
+                 rope: int, cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                 table_offset: int = 0, eps: float = 1e-6) -> torch.Tensor:
+    """In place on x (batch, tokens, heads*128) fp32: per-head RMSNorm with `weight`, then the
+    adjacent-pair RoPE from token-major (1|batch, table_tokens, 128) fp32 tables."""
+    _need(x, "x", F32)
+    x3 = _as3d(x)
+    batch, tokens, width = x3.shape
+    if width != heads * 128:
+        raise ValueError("qk_norm_rope works on 128-wide heads")
+    if weight is not None:
+        _need(weight, "weight", F32)
+    table_tokens, table_batched = 0, 0
+    if cos is not None:
+        _need(cos, "cos", F32)
+        _need(sin, "sin", F32)
+        if not (cos.is_contiguous() and sin.is_contiguous()) or cos.shape[-1] != 128:
+            raise ValueError("RoPE tables must be contiguous (..., tokens, 128)")
+        table_tokens = cos.shape[-2]
+        table_batched = int(cos.dim() >= 3 and cos.shape[0] > 1)
+    with _timed("qk_norm_rope_f32", 0.0, 8.0 * batch * tokens * width):
+        _lib.call("kino_qk_norm_rope_f32", _ptr(x3), x3.stride(1), x3.stride(0), batch, tokens,
+                  heads, _ptr(weight), norm, rope, _ptr(cos), _ptr(sin), table_batched,
+                  table_tokens, table_offset, eps, _stream())
+    return x
+
+
+def _unary(name: str, x: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+    _need(x, "x", F32)
+    x = x.contiguous()
+    if out is None:
+        out = torch.empty_like(x)
+    with _timed("elementwise_f32"):
+        _lib.call(name, _ptr(x), _ptr(out), x.numel(), _stream())
+    return out
+
+
+def gelu_tanh(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    return _unary("kino_gelu_tanh_f32", x, out)
+
+
+def silu(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    return _unary("kino_silu_f32", x, out)
+
+
+def cfg_combine(cond: torch.Tensor, uncond: torch.Tensor, guidance: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    _need(cond, "cond", F32)
+    _need(uncond, "uncond", F32)
+    cond, uncond = cond.contiguous(), uncond.contiguous()
+    if out is None:
+        out = torch.empty_like(cond)
+    with _timed("elementwise_f32"):
+        _lib.call("kino_cfg_combine_f32", _ptr(cond), _ptr(uncond), guidance, _ptr(out),
+                  cond.numel(), _stream())
+    return out
+
+
+def euler_velocity(x: torch.Tensor, v: torch.Tensor, dt: float,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    _need(x, "x", F32)
+    _need(v, "v", F32)
+    if not (x.is_contiguous() and v.is_contiguous()):
+        raise ValueError("euler_velocity takes contiguous tensors")
+    if out is None:
+        out = torch.empty_like(x)
+    with _timed("elementwise_f32"):
+        _lib.call("kino_euler_velocity_f32", _ptr(x), _ptr(v), dt, _ptr(out), x.numel(),
+                  _stream())
+    return out
+
+
+def swiglu(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(gate) * content over the last dimension [gate | content] of x (batch, rows, 2H) or
+    (rows, 2H); `out` (..., H) may be the gate half of x itself (x[..., :H])."""
+    _need(x, "x", F32)
+    width = x.shape[-1] // 2
+    x3 = _as3d(x)
+    if out is None:
+        out = torch.empty((*x.shape[:-1], width), device=x.device, dtype=F32)
+    _need(out, "out", F32)
+    o3 = _as3d(out)
+    if tuple(o3.shape) != (x3.shape[0], x3.shape[1], width):
+        raise ValueError("swiglu output must be (..., H) for an input of (..., 2H)")
+    with _timed("elementwise_f32"):
+        _lib.call("kino_swiglu_f32", _ptr(x3), x3.stride(1), x3.stride(0), _ptr(o3), o3.stride(1),
+                  o3.stride(0), x3.shape[0], x3.shape[1], width, _stream())
+    return out
+
+
+def timestep_embedding(t: torch.Tensor, dim: int = 256, *,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """t: fp32 (batch,) on the device -> fp32 (batch, dim) [cos, sin] features."""
+    _need(t, "t", F32)
+    t = t.contiguous()
+    if out is None:
+        out = torch.empty((t.shape[0], dim), device=t.device, dtype=F32)
+    with _timed("elementwise_f32"):
+        _lib.call("kino_timestep_embedding_f32", _ptr(t), _ptr(out), t.shape[0], dim, _stream())
+    return out

@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     for name in names:
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.kino_abi_version() == 6
+    assert lib.kino_abi_version() == 7
     assert _lib.last_error() == ""
 
 
@@ -102,3 +102,33 @@ def test_synthetic_weights_are_seeded_and_shaped():
     assert all(torch.equal(a[k], b[k]) for k in a)
     assert float(a["x_embedder.weight"].float().std()) == pytest.approx(0.02, rel=0.1)
     assert torch.equal(a["transformer_blocks.0.attn.norm_q.weight"], torch.ones(128, dtype=torch.bfloat16))
+
+
+def test_f32_front_end_refuses_cpu_and_bf16():
+    from kinomlx_b200 import ops_f32
+
+    x = torch.zeros((4, 16), dtype=torch.float32)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops_f32.linear(x, x)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops_f32.attention(x, x, x, heads=1)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops_f32.silu(x)
+
+
+def test_fp32_timestep_matches_oracle():
+    """The fp32 model's timestep goes through fp32, not bf16 (sampling.py:209-212 with the model
+    dtype fp32), so it differs from the bf16 value where bf16 would round it."""
+    from oracle import flux2 as ref
+    from kinomlx_b200.flux2 import sampling
+
+    sig = sampling.schedule(1024, 7)
+    for i in range(7):
+        t = ref.step_timestep(sig, i, torch.float32)
+        assert float(sampling.timestep_x1000(sig, i, dtype=torch.float32)) == float(
+            (t.to(torch.float32) * 1000).float())
+    assert any(
+        float(sampling.timestep_x1000(sig, i, dtype=torch.float32))
+        != float(sampling.timestep_x1000(sig, i))
+        for i in range(7)
+    )

@@ -1,0 +1,250 @@
+"""fp32 parity mode against the CPU oracle in fp32 (BASELINE: per-op max relative error <= 1e-4
+in fp32 mode; config 1 asks for the double block in fp32 as well as bf16).
+
+Max relative error here is max |device - oracle| / max |oracle| over the whole output, the same
+measure the bf16 tests use. Every case compares the fp32 CUDA kernels (through the C ABI) with the
+oracle's fp32 restatement on identical seeded inputs drawn on the CPU.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from oracle import flux2 as ref
+from oracle import fused_ops as rops
+from kinomlx_b200 import _lib
+from kinomlx_b200 import ops_f32 as f
+from kinomlx_b200.flux2 import config as fcfg
+from kinomlx_b200.flux2 import sampling
+from kinomlx_b200.flux2.transformer import rotary_positions
+from kinomlx_b200.flux2.transformer_f32 import Flux2TransformerF32
+from kinomlx_b200.synthetic import flux_weights, normal
+
+pytestmark = pytest.mark.gpu
+F32 = torch.float32
+TOL = 1e-4  # BASELINE's fp32-mode gate
+
+
+def _max_rel(out: torch.Tensor, expect: torch.Tensor) -> float:
+    o, e = out.float().cpu().flatten(), expect.float().cpu().flatten()
+    return float((o - e).abs().max() / e.abs().max())
+
+
+def _cos(out: torch.Tensor, expect: torch.Tensor) -> float:
+    o, e = out.float().cpu().flatten(), expect.float().cpu().flatten()
+    return float(torch.nn.functional.cosine_similarity(o.double(), e.double(), dim=0))
+
+
+def _r(shape, seed, std=1.0):
+    return normal(shape, seed=seed, dtype=F32, std=std)
+
+
+@pytest.mark.parametrize("m,n,k,batch", [(77, 200, 36, 1), (300, 384, 1024, 2), (1, 18432, 3072, 1)])
+def test_linear_f32_plain_and_bias(cuda_device, m, n, k, batch):
+    x, w, b = _r((batch, m, k), 1), _r((n, k), 2, 0.02), _r((n,), 3)
+    out = f.linear(x.to(cuda_device), w.to(cuda_device), bias=b.to(cuda_device))
+    assert _max_rel(out, rops.linear(x, w, b)) <= TOL
+
+
+def test_linear_f32_epilogues(cuda_device):
+    """GELU on a column range, gated residual with a per-batch gate (in place), Euler update."""
+    dev = cuda_device
+    batch, m, n, k = 2, 133, 264, 520
+    x, w = _r((batch, m, k), 4), _r((n, k), 5, 0.02)
+    y = rops.linear(x, w)
+    out = f.linear(x.to(dev), w.to(dev), kind=_lib.EPI_GELU, act_col_begin=128)
+    expect = torch.cat([y[..., :128], rops.gelu_approx(y[..., 128:])], -1)
+    assert _max_rel(out, expect) <= TOL
+    res, gate = _r((batch, m, n), 6), _r((batch, n), 7)
+    res_d = res.to(dev)
+    f.linear(x.to(dev), w.to(dev), res_d, kind=_lib.EPI_GATED_RESIDUAL, residual=res_d,
+             gate=gate.to(dev))
+    assert _max_rel(res_d, res + gate[:, None] * y) <= TOL
+    cur = _r((batch, m, n), 8)
+    cur_d = cur.to(dev)
+    f.linear(x.to(dev), w.to(dev), cur_d, kind=_lib.EPI_EULER, dt=-0.25, sample=cur_d)
+    assert _max_rel(cur_d, ref.euler_step(cur, y, torch.tensor(-0.25))) <= TOL
+
+
+@pytest.mark.parametrize("batch,tq,tk,heads", [(2, 77, 130, 2), (1, 1536, 1536, 24)])
+def test_attention_f32_matches_sdpa(cuda_device, batch, tq, tk, heads):
+    q, k, v = _r((batch, tq, heads * 128), 9), _r((batch, tk, heads * 128), 10), _r((batch, tk, heads * 128), 11)
+    sh = lambda t: t.reshape(*t.shape[:2], heads, 128).transpose(1, 2)
+    expect = rops.sdpa(sh(q), sh(k), sh(v), scale=128**-0.5).transpose(1, 2).reshape(q.shape)
+    qd = q.to(cuda_device)
+    out = f.attention(qd, k.to(cuda_device), v.to(cuda_device), qd, heads=heads)  # over q
+    assert _max_rel(out, expect) <= TOL
+
+
+@pytest.mark.parametrize("dim", [200, 3072])
+@pytest.mark.parametrize("norm", [_lib.NORM_LAYER, _lib.NORM_RMS, _lib.NORM_NONE])
+def test_adaln_f32(cuda_device, dim, norm):
+    batch, rows = 2, 37
+    x, shift, scale = _r((batch, rows, dim), 12), _r((batch, 1, dim), 13), _r((batch, 1, dim), 14)
+    if norm == _lib.NORM_LAYER:
+        base = rops.layer_norm(x, 1e-6)
+    elif norm == _lib.NORM_RMS:
+        base = rops.rms_norm(x, None, 1e-6)
+    else:
+        base = x
+    expect = base * (1 + scale) + shift
+    out = f.adaln(x.to(cuda_device), shift[:, 0].to(cuda_device), scale[:, 0].to(cuda_device),
+                  norm=norm)
+    assert _max_rel(out, expect) <= TOL
+
+
+def test_qk_norm_rope_f32(cuda_device):
+    """Per-head RMSNorm with weight, then the adjacent-pair rotation, on a column slice of a wider
+    row and at a table offset (the image rows of a joint sequence)."""
+    heads, tokens, offset = 3, 50, 7
+    v = fcfg.BASELINE
+    ids = torch.cat([torch.zeros((1, offset, 2), dtype=torch.int64), ref.image_ids(5, 10, 2)], 1)
+    cos4, sin4 = ref.rotary_positions(ids, v)
+    cos, sin = rotary_positions(ids, v)
+    x = _r((2, tokens, 3 * heads * 128), 15)
+    weight = 1 + _r((128,), 16, 0.1)
+    sl = x[..., heads * 128 : 2 * heads * 128].reshape(2, tokens, heads, 128)
+    expect = ref.rotate(rops.rms_norm(sl, weight, 1e-6), cos4[:, offset:], sin4[:, offset:])
+    xd = x.to(cuda_device)
+    f.qk_norm_rope(xd[..., heads * 128 : 2 * heads * 128], heads=heads, weight=weight.to(cuda_device),
+                   norm=_lib.QKNORM_PER_HEAD, rope=_lib.ROPE_PAIRS, cos=cos.to(cuda_device),
+                   sin=sin.to(cuda_device), table_offset=offset)
+    got = xd.cpu()
+    assert _max_rel(got[..., heads * 128 : 2 * heads * 128], expect.reshape(2, tokens, -1)) <= TOL
+    assert torch.equal(got[..., : heads * 128], x[..., : heads * 128])  # untouched neighbours
+    assert torch.equal(got[..., 2 * heads * 128 :], x[..., 2 * heads * 128 :])
+
+
+def test_elementwise_f32(cuda_device):
+    dev = cuda_device
+    x, y = _r((4099,), 17, 3.0), _r((4099,), 18)
+    assert _max_rel(f.gelu_tanh(x.to(dev)), rops.gelu_approx(x)) <= TOL
+    assert _max_rel(f.silu(x.to(dev)), rops.silu(x)) <= TOL
+    assert _max_rel(f.cfg_combine(x.to(dev), y.to(dev), 4.0), y + 4.0 * (x - y)) <= TOL
+    assert _max_rel(f.euler_velocity(x.to(dev), y.to(dev), -0.125),
+                    ref.euler_step(x, y, torch.tensor(-0.125))) <= TOL
+    h = _r((2, 9, 2 * 96), 19)
+    hd = h.to(dev)
+    out = f.swiglu(hd, out=hd[..., :96])  # in place over the gate half
+    assert _max_rel(out, ref.swiglu(h)) <= TOL
+    t = torch.tensor([500.0, 875.0])
+    got = f.timestep_embedding(t.to(dev), 256)
+    freq = torch.exp(-torch.log(torch.tensor(10000.0)) * torch.arange(128, dtype=F32) / 128)
+    ang = t[:, None] * freq
+    assert _max_rel(got, torch.cat([torch.cos(ang), torch.sin(ang)], -1)) <= TOL
+
+
+def _block_inputs(v, seed, nt, h, wd):
+    w = flux_weights(v, seed=seed, dtype=F32)
+    ids = torch.cat([torch.zeros((1, nt, 2), dtype=torch.int64), ref.image_ids(h, wd, 2)], 1)
+    return w, ids
+
+
+def test_config1_double_block_f32(cuda_device):
+    """BASELINE config 1 in fp32: one MMDiT double block, 512 text + 1024 image tokens, hidden
+    3072, 24 heads, t = 0.5, seed 0, weights N(0, 0.02) drawn in fp32."""
+    v = fcfg.BASELINE.with_blocks(1, 0)
+    w, ids = _block_inputs(v, 0, 512, 32, 32)
+    image = _r((1, 1024, v.dim), 1)
+    text = _r((1, 512, v.dim), 2)
+    t = torch.tensor([0.5], dtype=F32)
+    cos4, sin4 = ref.rotary_positions(ids, v)
+    emb = ref.timestep_embedding(w, t * 1000)
+    im = ref.modulation(w, "double_stream_modulation_img", emb)
+    tm = ref.modulation(w, "double_stream_modulation_txt", emb)
+    exp_img, exp_txt = ref.double_block(w, 0, image, text, im, tm, cos4, sin4, v)
+
+    dev = cuda_device
+    model = Flux2TransformerF32(w, v, dev)
+    cos, sin = rotary_positions(ids, v)
+    img, txt = model.double_block(0, image.to(dev), text.to(dev), (t * 1000).to(dev),
+                                  cos.to(dev), sin.to(dev))
+    for out, exp in ((img, exp_img), (txt, exp_txt)):
+        assert out.dtype == F32
+        assert _max_rel(out, exp) <= TOL, _max_rel(out, exp)
+        assert _cos(out, exp) >= 0.99999
+
+
+@pytest.mark.parametrize("mlp", ["gelu_tanh", "swiglu"])
+def test_single_block_f32(cuda_device, mlp):
+    if mlp == "gelu_tanh":
+        v = fcfg.BASELINE.with_blocks(0, 1)
+    else:
+        v = fcfg.FluxVariant(dim=1024, heads=8, mlp="swiglu", mlp_hidden=3072, rope_axes=(64, 64),
+                             rope_theta=10000.0, in_channels=64, context_dim=512,
+                             double_blocks=0, single_blocks=1)
+    nt, h, wd = 100, 12, 20
+    w, ids = _block_inputs(v, 5, nt, h, wd)
+    value = _r((1, nt + h * wd, v.dim), 6)
+    t = torch.tensor([0.75], dtype=F32)
+    cos4, sin4 = ref.rotary_positions(ids, v)
+    emb = ref.timestep_embedding(w, t * 1000)
+    sm = ref.modulation(w, "single_stream_modulation", emb)
+    expect = ref.single_block(w, 0, value, sm, cos4, sin4, v)
+    dev = cuda_device
+    model = Flux2TransformerF32(w, v, dev)
+    cos, sin = rotary_positions(ids, v)
+    out = model.single_block(0, value.to(dev), nt, (t * 1000).to(dev), cos.to(dev), sin.to(dev))
+    assert _max_rel(out, expect) <= TOL, _max_rel(out, expect)
+
+
+def test_klein_double_block_f32(cuda_device):
+    """SwiGLU (gate first) double block at hidden 1024 / 8 heads, batch 2 (per-entry modulation)."""
+    v = fcfg.FluxVariant(dim=1024, heads=8, mlp="swiglu", mlp_hidden=3072, rope_axes=(64, 64),
+                         rope_theta=10000.0, in_channels=64, context_dim=512, double_blocks=1,
+                         single_blocks=0)
+    nt, h, wd = 48, 8, 10
+    w, ids = _block_inputs(v, 30, nt, h, wd)
+    image, text = _r((2, h * wd, v.dim), 31), _r((2, nt, v.dim), 32)
+    t = torch.tensor([0.25, 0.875], dtype=F32)
+    cos4, sin4 = ref.rotary_positions(ids, v)
+    emb = ref.timestep_embedding(w, t * 1000)
+    im = ref.modulation(w, "double_stream_modulation_img", emb)
+    tm = ref.modulation(w, "double_stream_modulation_txt", emb)
+    exp_img, exp_txt = ref.double_block(w, 0, image, text, im, tm, cos4, sin4, v)
+    dev = cuda_device
+    model = Flux2TransformerF32(w, v, dev)
+    cos, sin = rotary_positions(ids, v)
+    img, txt = model.double_block(0, image.to(dev), text.to(dev), (t * 1000).to(dev),
+                                  cos.to(dev), sin.to(dev))
+    assert _max_rel(img, exp_img) <= TOL and _max_rel(txt, exp_txt) <= TOL
+
+
+@pytest.mark.parametrize("cfg", [False, True])
+def test_denoise_f32_matches_oracle(cuda_device, cfg):
+    """The whole fp32 trajectory (1 double + 1 single block at hidden 512, 3 Euler steps, with and
+    without batched CFG): final latent within the per-op bound and cosine >= 0.999 (BASELINE)."""
+    v = fcfg.FluxVariant(dim=512, heads=4, mlp="gelu_tanh", mlp_hidden=2048, rope_axes=(64, 64),
+                         rope_theta=10000.0, in_channels=64, context_dim=256, double_blocks=1,
+                         single_blocks=1)
+    nt, h, wd = 32, 8, 8
+    w, ids = _block_inputs(v, 40, nt, h, wd)
+    noise = _r((1, h * wd, v.in_channels), 41)
+    text = _r((1, nt, v.context_dim), 42)
+    negative = _r((1, nt, v.context_dim), 43) if cfg else None
+    sigmas = ref.linear_sigmas(3)
+    guidance = 4.0 if cfg else 1.0
+    expect = ref.denoise(w, noise, text, ids, sigmas, v, negative=negative, guidance=guidance)
+    model = Flux2TransformerF32(w, v, cuda_device)
+    out = sampling.denoise(model, noise, text, ids, sigmas=sampling.linear_sigmas(3),
+                           negative=negative, guidance=guidance)
+    assert out.dtype == F32
+    assert _max_rel(out, expect) <= TOL, _max_rel(out, expect)
+    assert _cos(out, expect) >= 0.999
+
+
+def test_f32_refusals(cuda_device):
+    """Contract violations come back as errors, not silent work: a k that is not a multiple of 4,
+    a misaligned row stride, an epilogue with no fp32 form, a table too short for the rows."""
+    dev = cuda_device
+    with pytest.raises(RuntimeError, match="ENOTSUPPORTED"):
+        f.linear(torch.zeros((4, 6), device=dev), torch.zeros((8, 6), device=dev))
+    with pytest.raises(ValueError, match="no fp32 form"):
+        f.linear(torch.zeros((4, 8), device=dev), torch.zeros((8, 8), device=dev),
+                 kind=_lib.EPI_SWIGLU)
+    x = torch.zeros((1, 5, 128), device=dev)
+    tab = torch.zeros((1, 4, 128), device=dev)
+    with pytest.raises(RuntimeError, match="EINVAL"):
+        f.qk_norm_rope(x, heads=1, weight=None, norm=_lib.QKNORM_NONE, rope=_lib.ROPE_PAIRS,
+                       cos=tab, sin=tab)
