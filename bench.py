@@ -514,8 +514,41 @@ def _kernel_shares(fn) -> dict:
             for k, v in sorted(summary.items(), key=lambda kv: -kv[1]["ms"])}
 
 
+CONFIG1_FLOP = 376.9e9  # one double block at config 1: 347.9 GFLOP linear + 29.0 attention
+
+
+def config1_block(device: torch.device) -> dict:
+    """one MMDiT double block (512 text + 1024 image tokens, hidden 3072,
+    24 heads, t = 0.5) in bf16 on the tensor cores and in fp32 (parity mode) on the CUDA cores;
+    each timed call also runs the timestep MLP and the modulation products."""
+    from kinomlx_b200.flux2 import config as fcfg
+    from kinomlx_b200.flux2.transformer import Flux2Transformer, rotary_positions
+    from kinomlx_b200.flux2.transformer_f32 import Flux2TransformerF32
+    from kinomlx_b200.synthetic import flux_weights, normal
+
+    v = fcfg.BASELINE.with_blocks(1, 0)
+    nt, side = 512, 32
+    ids = torch.zeros((1, nt + side * side, 2), dtype=torch.int64)
+    ids[0, nt:, 0] = torch.arange(side).repeat_interleave(side)
+    ids[0, nt:, 1] = torch.arange(side).repeat(side)
+    cos, sin = rotary_positions(ids, v)
+    cos, sin = cos.to(device), sin.to(device)
+    t = torch.tensor([500.0], device=device)
+    out = {}
+    for name, cls, dtype in (("bf16", Flux2Transformer, torch.bfloat16),
+                             ("fp32", Flux2TransformerF32, torch.float32)):
+        model = cls(flux_weights(v, seed=0, device=device, dtype=dtype), v, device)
+        img = normal((1, side * side, v.dim), seed=1, device=device, dtype=dtype)
+        txt = normal((1, nt, v.dim), seed=2, device=device, dtype=dtype)
+        ms = _time(lambda: model.double_block(0, img, txt, t, cos, sin), 3, 5, 1)
+        out[name] = {"ms": round(ms, 3), "tflops": round(CONFIG1_FLOP / (ms * 1e9), 1)}
+        model = None
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_secondary(world: int, rank: int, local: int) -> dict:
-    """BASELINE configs 3-5 on the same GPUs (2 warm-up + 3 timed repetitions each): the
+    """BASELINE configs 1 (one GPU) and 3-5 on the same GPUs (2 warm-up + 3 timed repetitions each): the
     metric's second half (VAE decode frames/s) and the other step latencies, each with its
     whole-step throughput against the measured sustained bf16 peak."""
     from kinomlx_b200.flux2 import config as fcfg
@@ -532,6 +565,10 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
     pk, _ = peaks()
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
     out = {}
+
+    # config 1: the double block alone, bf16 and fp32
+    if world == 1:
+        out["config1_double_block"] = config1_block(device)
 
     # config 3: CFG over a batch of 2 (1 GPU) or the branch split (+ Ulysses inside each half)
     v = fcfg.BASELINE

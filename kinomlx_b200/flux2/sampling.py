@@ -65,11 +65,11 @@ def denoise_step(
     dt = step_delta(sigmas, index)
     dtype = getattr(model, "dtype", torch.bfloat16)
     elementwise = ops_f32 if dtype == torch.float32 else ops
+    # the timestep reaches the device as a fill value: a copy from pageable host memory would
+    # wait for the stream to drain before every step
+    t = float(timestep_x1000(sigmas, index, 1, dtype))
     if not cfg:
-        t = timestep_x1000(sigmas, index, current.shape[0], dtype).to(current.device,
-                                                                      non_blocking=True)
         return model.run(prepared, current, t, euler_dt=dt, sample=current, out=current)
-    t = timestep_x1000(sigmas, index, 2, dtype).to(current.device, non_blocking=True)
     both = model.run(prepared, current.repeat(2, 1, 1), t)
     velocity = elementwise.cfg_combine(both[0:1], both[1:2], guidance)
     return elementwise.euler_velocity(current, velocity, dt, out=current)

@@ -271,15 +271,18 @@ class Flux2Transformer:
         return ws.stream.clone()
 
     # ------------------------------------------------------------------ forward
-    def _embed(self, ws: _Workspace, timestep_x1000: torch.Tensor) -> None:
+    def _embed(self, ws: _Workspace, timestep_x1000: torch.Tensor | float) -> None:
         """Timestep MLP and every modulation vector (kinomlx/models/flux2/transformer.py:315-318)."""
-        ws.t.copy_(timestep_x1000, non_blocking=True)
+        if isinstance(timestep_x1000, torch.Tensor):
+            ws.t.copy_(timestep_x1000, non_blocking=True)
+        else:  # one value for every batch entry: a fill, no host-to-device copy
+            ws.t.fill_(float(timestep_x1000))
         ops.timestep_embedding(ws.t, 256, out=ws.temb)
         ops.gemv(ws.temb, self.t_lin1, out=ws.emb1)
         ops.gemv(ws.emb1, self.t_lin2, silu_input=True, out=ws.emb)
         ops.gemv(ws.emb, self.mod_all, silu_input=True, out=ws.mods)
 
-    def run(self, prepared: PreparedText, image: torch.Tensor, timestep_x1000: torch.Tensor,
+    def run(self, prepared: PreparedText, image: torch.Tensor, timestep_x1000: torch.Tensor | float,
             *, euler_dt: float | None = None, sample: torch.Tensor | None = None,
             out: torch.Tensor | None = None) -> torch.Tensor:
         """One transformer evaluation. With `euler_dt`, the final projection's epilogue applies

@@ -215,10 +215,13 @@ class Flux2TransformerF32:
         return ws.stream.clone()
 
     # ------------------------------------------------------------------ forward
-    def _embed(self, ws: _Workspace, timestep_x1000: torch.Tensor) -> None:
+    def _embed(self, ws: _Workspace, timestep_x1000: torch.Tensor | float) -> None:
         """Timestep MLP and every modulation vector (kinomlx/models/flux2/transformer.py:223-258,
         315-318): linear_2(silu(linear_1(sinusoid(t)))), then linear(silu(emb)) for all four."""
-        ws.t.copy_(timestep_x1000, non_blocking=True)
+        if isinstance(timestep_x1000, torch.Tensor):
+            ws.t.copy_(timestep_x1000, non_blocking=True)
+        else:  # one value for every batch entry: a fill, no host-to-device copy
+            ws.t.fill_(float(timestep_x1000))
         f.timestep_embedding(ws.t, 256, out=ws.temb)
         f.linear(ws.temb, self.t_lin1, ws.emb1)
         f.silu(ws.emb1, out=ws.act)
@@ -226,7 +229,7 @@ class Flux2TransformerF32:
         f.silu(ws.emb, out=ws.act)
         f.linear(ws.act, self.mod_all, ws.mods)
 
-    def run(self, prepared: PreparedTextF32, image: torch.Tensor, timestep_x1000: torch.Tensor,
+    def run(self, prepared: PreparedTextF32, image: torch.Tensor, timestep_x1000: torch.Tensor | float,
             *, euler_dt: float | None = None, sample: torch.Tensor | None = None,
             out: torch.Tensor | None = None) -> torch.Tensor:
         """One transformer evaluation (kinomlx/models/flux2/transformer.py:307-358). With

@@ -50,7 +50,7 @@ def cfg_split_step(model, prepared, current: torch.Tensor, sigmas: torch.Tensor,
     holds this rank's branch text (positive or negative) and `model.sp` is `cfg.sp`."""
     from .flux2.sampling import step_delta, timestep_x1000
 
-    t = timestep_x1000(sigmas, index, 1).to(current.device, non_blocking=True)
+    t = float(timestep_x1000(sigmas, index, 1))
     velocity = model.run(prepared, current, t)
     combined = cfg.combine(velocity, guidance)
     return ops.euler_velocity(current, combined, step_delta(sigmas, index), out=current)
