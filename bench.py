@@ -687,6 +687,9 @@ def run_kernel_case(case: str) -> None:
         bias = normal((256,), seed=9, device=dev)
         for _ in range(3):
             ops.conv3d(x, w, bias, causal=True)
+    elif case == "bandwidth":
+        run_bandwidth_case(dev)
+        return
     else:
         # the decoder's last stage: 128 -> 128 channels at full resolution, with the residual
         # and the GroupNorm statistics of the next norm
@@ -702,6 +705,103 @@ def run_kernel_case(case: str) -> None:
     print(json.dumps({"kernel_case": case, "ok": True}))
 
 
+def run_bandwidth_case(dev: torch.device) -> None:
+    """The HBM-bound kernels at workload shapes, three launches each with the L2 flushed before
+    every launch (a 256 MB write) and the GPU held busy while the launch is queued: achieved GB/s = algorithmic bytes / CUDA-event time of
+    launches 2 and 3, against the measured copy bandwidth. Shapes: the LTX video block's rows
+    (9216 x 4096) for AdaLN and the full-row QK norm + split RoPE, the Flux step's rows
+    (4608 x 3072) for its LayerNorm AdaLN, the LTX FF width (9216 x 16384) for the standalone
+    GELU, the last VAE stage (49 x 96 x 128 voxels x 128 channels) for PixelNorm + SiLU and the
+    GroupNorm apply pass, one decoded VAE tile for the blend, a 16384 x 4096 mxfp8 weight for the
+    dequantisation."""
+    from kinomlx_b200 import ops
+    from kinomlx_b200.synthetic import normal
+
+    bf = torch.bfloat16
+    flush = torch.empty(256 << 20, device=dev, dtype=torch.uint8)
+    results = {}
+
+    def measure(name: str, nbytes: float, fn) -> None:
+        fn()
+        total = 0.0
+        for _ in range(2):
+            flush.fill_(1)
+            # keep the GPU busy while the host queues the events and the launch, so the timed
+            # span holds the kernel and not the host's enqueue latency
+            torch.cuda._sleep(400_000)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            total += a.elapsed_time(b)
+        ms = total / 2
+        results[name] = {"bytes": nbytes, "ms": round(ms, 4), "gbs": round(nbytes / (ms * 1e6), 1)}
+
+    n, d = 9216, 4096
+    x = normal((1, n, d), seed=1, device=dev)
+    shift = normal((1, d), seed=2, device=dev)
+    scale = normal((1, d), seed=3, device=dev)
+    y = torch.empty_like(x)
+    measure("adaln_rms_9216x4096", 4.0 * n * d,
+            lambda: ops.adaln(x, shift, scale, y, norm=ops.NORM_RMS))
+    xf = normal((1, 4608, 3072), seed=4, device=dev)
+    yf = torch.empty_like(xf)
+    sf, cf = normal((1, 3072), seed=5, device=dev), normal((1, 3072), seed=6, device=dev)
+    measure("adaln_layer_4608x3072", 4.0 * 4608 * 3072,
+            lambda: ops.adaln(xf, sf, cf, yf, norm=ops.NORM_LAYER))
+    xf = yf = None
+    wq = normal((d,), seed=7, device=dev)
+    ang = torch.rand((1, 32, n, 64), device=dev) * 6.0
+    cos, sin = torch.cos(ang).contiguous(), torch.sin(ang).contiguous()
+    ang = None
+    measure("qk_norm_rope_fullrow_split_9216x4096", 4.0 * n * d + 8.0 * n * d / 2,
+            lambda: ops.qk_norm_rope(x, heads=32, weight=wq, norm=ops.QKNORM_FULL_ROW,
+                                     rope=ops.ROPE_SPLIT, cos=cos, sin=sin))
+    measure("split_rope_9216x4096", 4.0 * n * d + 8.0 * n * d / 2,
+            lambda: ops.split_rope(x, cos, sin))
+    x = y = cos = sin = None
+    h = normal((n, 16384), seed=8, device=dev)
+    measure("gelu_tanh_9216x16384", 4.0 * h.numel(), lambda: ops.gelu_tanh(h))
+    h = None
+    torch.cuda.empty_cache()
+    vox = normal((49, 96, 128, 128), seed=9, device=dev)
+    measure("pixel_norm_silu_49x96x128x128", 4.0 * vox.numel(),
+            lambda: ops.pixel_norm(vox, silu=True))
+    w = normal((128, 3, 3, 3, 128), seed=10, device=dev, std=0.02)
+    bias = normal((128,), seed=11, device=dev)
+    stats = ops.conv_stats_buffer(dev)
+    conv = ops.conv3d(vox, w, bias, causal=True, stats=stats)
+    gw, gb = normal((128,), seed=12, device=dev), normal((128,), seed=13, device=dev)
+    gout = torch.empty_like(conv)
+    measure("group_norm_from_stats_silu_49x96x128x128", 4.0 * conv.numel(),
+            lambda: ops.group_norm_from_stats(conv, gw, gb, 1e-6, stats, silu=True, out=gout))
+    vox = conv = gout = None
+    torch.cuda.empty_cache()
+    tile = normal((121, 64, 64, 48), seed=14, device=dev)
+    canvas = torch.zeros((1, 3, 121, 576, 1024), device=dev, dtype=torch.float32)
+    weights = torch.zeros((576, 1024), device=dev, dtype=torch.float32)
+    ramp = torch.ones(256, device=dev)
+    measure("tile_blend_121x256x256x3", 2.0 * tile.numel() + 8.0 * tile.numel(),
+            lambda: ops.tile_blend(tile, canvas, weights, 0, 0, ramp, ramp))
+    tile = canvas = weights = None
+    torch.cuda.empty_cache()
+    rows, cols = 16384, 4096
+    words = torch.randint(-2**31, 2**31 - 1, (rows, cols // 4), device=dev, dtype=torch.int32)
+    scales = torch.randint(118, 130, (rows, cols // 32), device=dev, dtype=torch.uint8)
+    wout = torch.empty((rows, cols), device=dev, dtype=bf)
+    measure("dequant_mxfp8_16384x4096", 4.0 * words.numel() + scales.numel() + 2.0 * rows * cols,
+            lambda: ops.dequantize(words, scales, None, mode="mxfp8", group_size=32, bits=8,
+                                   out=wout))
+    torch.cuda.synchronize()
+    ops.device_status()
+    pk, source = peaks()
+    for r in results.values():
+        r["frac_of_copy_peak"] = round(r["gbs"] / float(pk["hbm_gbs"]), 4)
+    print(json.dumps({"kernel_case": "bandwidth", "ok": True, "peak_gbs": pk["hbm_gbs"],
+                      "peak_source": source, "kernels": results}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -711,7 +811,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
-    ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow"],
+    ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow",
+                                              "bandwidth"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     args = ap.parse_args()
     if args.kernel_case:

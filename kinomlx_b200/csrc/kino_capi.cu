@@ -876,6 +876,20 @@ kino_status kino_split_rope(const void* x, const float* cos_table, const float* 
     return fail(KINO_EINVAL, "kino_split_rope: null");
   if (batch < 1 || tokens < 1 || heads < 1 || half < 1)
     return fail(KINO_EINVAL, "kino_split_rope: empty");
+  const auto aligned = [](const void* p, uintptr_t a) {
+    return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+  };
+  if (half % 4 == 0 && aligned(x, 8) && aligned(out, 8) && aligned(cos_table, 16) &&
+      aligned(sin_table, 16) && batch * tokens <= 0x7fffffffLL && heads * half <= 0x3fffffffLL) {
+    const int64_t rows = batch * tokens;
+    const unsigned blocks = static_cast<unsigned>(rows < 148 * 16 ? rows : 148 * 16);
+    launch_pdl(kino::split_rope_vec4_kernel, dim3(blocks), dim3(256), 0,
+               static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x), cos_table,
+               sin_table, static_cast<__nv_bfloat16*>(out), static_cast<int>(batch),
+               static_cast<int>(tokens), static_cast<int>(heads), static_cast<int>(half),
+               table_batched);
+    return check_launch("kino_split_rope");
+  }
   const int64_t n = batch * tokens * heads * half;
   int64_t blocks = (n + 255) / 256;
   if (blocks > 65535 * 8) blocks = 65535 * 8;
@@ -1082,6 +1096,22 @@ kino_status kino_pixel_norm(const void* x, void* out, int64_t voxels, int64_t ch
   if (x == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_pixel_norm: null");
   if (channels % 8 || channels > 1024 || !aligned16(x) || !aligned16(out) || voxels < 1)
     return fail(KINO_ENOTSUPPORTED, "kino_pixel_norm: channels %% 8, <= 1024, aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto vec_form = [&](auto kernel, int64_t voxels_per_warp) {
+    const int64_t warps = (voxels + voxels_per_warp - 1) / voxels_per_warp;
+    launch_pdl(kernel, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256), 0, st,
+               static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(out), voxels,
+               eps, apply_silu);
+    return check_launch("kino_pixel_norm");
+  };
+  switch (channels) {
+    case 64: return vec_form(kino::pixel_norm_silu_vec_kernel<64>, 4);
+    case 128: return vec_form(kino::pixel_norm_silu_vec_kernel<128>, 2);
+    case 256: return vec_form(kino::pixel_norm_silu_vec_kernel<256>, 1);
+    case 512: return vec_form(kino::pixel_norm_silu_vec_kernel<512>, 1);
+    case 1024: return vec_form(kino::pixel_norm_silu_vec_kernel<1024>, 1);
+    default: break;
+  }
   const int64_t threads = voxels * 32;
   const int64_t blocks = (threads + 255) / 256;
   launch_pdl(kino::pixel_norm_silu_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
@@ -1235,9 +1265,12 @@ kino_status kino_tile_blend(const void* decoded, int64_t frames, int64_t height,
     return fail(KINO_EINVAL, "kino_tile_blend: null");
   if (y0 < 0 || x0 < 0 || y0 + height * patch > out_height || x0 + width * patch > out_width)
     return fail(KINO_EINVAL, "kino_tile_blend: tile outside the canvas");
-  const int64_t n = channels * frames * height * patch * width * patch;
-  int64_t blocks = (n + 255) / 256;
-  if (blocks > 148 * 32) blocks = 148 * 32;
+  const int64_t nrows = channels * frames * height * patch;
+  if (nrows > 0x7fffffffLL || width * patch > 0x7fffffffLL || channels * patch * patch > 0x7fffffffLL)
+    return fail(KINO_ENOTSUPPORTED, "kino_tile_blend: tile too large");
+  int64_t blocks = nrows;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) return KINO_OK;
   launch_pdl(kino::tile_blend_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(decoded), static_cast<int>(frames),
       static_cast<int>(height), static_cast<int>(width), static_cast<int>(channels),

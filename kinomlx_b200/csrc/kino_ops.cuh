@@ -416,6 +416,54 @@ __global__ void split_rope_kernel(const __nv_bfloat16* __restrict__ x, const flo
   }
 }
 
+// split_rope_kernel for half % 4 == 0: four pairs per thread with 8-byte value and 16-byte table
+// loads, one (batch, token) row per CTA iteration with 32-bit index math; identical arithmetic.
+__global__ void split_rope_vec4_kernel(const __nv_bfloat16* __restrict__ x,
+                                       const float* __restrict__ cs, const float* __restrict__ sn,
+                                       __nv_bfloat16* __restrict__ out, int batch, int tokens,
+                                       int heads, int half, int table_batched) {
+  griddep_wait();
+  griddep_launch();
+  const int groups = half >> 2;  // four-pair groups per head
+  const int per_row = heads * groups;
+  const int rows = batch * tokens;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int b = r / tokens;
+    const int t = r - b * tokens;
+    const int64_t xrow = static_cast<int64_t>(r) * heads * 2 * half;
+    for (int j = threadIdx.x; j < per_row; j += blockDim.x) {
+      const int h = j / groups;
+      const int i = (j - h * groups) * 4;
+      const int64_t xo = xrow + static_cast<int64_t>(h) * 2 * half + i;
+      const int64_t eo =
+          ((static_cast<int64_t>(table_batched ? b : 0) * heads + h) * tokens + t) * half + i;
+      const float4 c = *reinterpret_cast<const float4*>(cs + eo);
+      const float4 sv = *reinterpret_cast<const float4*>(sn + eo);
+      const uint2 fa = *reinterpret_cast<const uint2*>(x + xo);
+      const uint2 sa = *reinterpret_cast<const uint2*>(x + xo + half);
+      const float2 f01 = unpack_bf16x2(fa.x), f23 = unpack_bf16x2(fa.y);
+      const float2 s01 = unpack_bf16x2(sa.x), s23 = unpack_bf16x2(sa.y);
+      const float first[4] = {f01.x, f01.y, f23.x, f23.y};
+      const float second[4] = {s01.x, s01.y, s23.x, s23.y};
+      const float cv[4] = {c.x, c.y, c.z, c.w};
+      const float svv[4] = {sv.x, sv.y, sv.z, sv.w};
+      float o1[4], o2[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        o1[k] = __fsub_rn(__fmul_rn(first[k], cv[k]), __fmul_rn(second[k], svv[k]));
+        o2[k] = __fadd_rn(__fmul_rn(first[k], svv[k]), __fmul_rn(second[k], cv[k]));
+      }
+      uint2 w1, w2;
+      w1.x = pack_bf16x2(o1[0], o1[1]);
+      w1.y = pack_bf16x2(o1[2], o1[3]);
+      w2.x = pack_bf16x2(o2[0], o2[1]);
+      w2.y = pack_bf16x2(o2[2], o2[3]);
+      *reinterpret_cast<uint2*>(out + xo) = w1;
+      *reinterpret_cast<uint2*>(out + xo + half) = w2;
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------- elementwise
 enum ElemKind : int {
   ELEM_GELU = 0,       // fused_ops.py:27-35

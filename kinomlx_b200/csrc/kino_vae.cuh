@@ -50,6 +50,57 @@ __global__ void pixel_norm_silu_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
+// The same PixelNorm (+ SiLU) for C in {64, 128, ..., 1024}: C/8 threads per voxel (at most 32),
+// each holding C/256 (at least one) 16-byte vectors, so every lane of a warp works (two to four
+// voxels per warp at C <= 128) and the group's sum of squares is a shuffle over its own lanes.
+// Per-element operations as above; only the fp32 summation order of the mean differs.
+template <int C>
+__global__ void __launch_bounds__(256)
+    pixel_norm_silu_vec_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out,
+                               int64_t voxels, float eps, int apply_silu) {
+  griddep_wait();
+  griddep_launch();
+  constexpr int T = C / 8 < 32 ? C / 8 : 32;  // threads per voxel
+  constexpr int K = C / (8 * T);              // 16-byte vectors per thread
+  constexpr int VW = 32 / T;                  // voxels per warp
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int64_t voxel = warp_global * VW + lane / T;
+  const int sub = lane % T;
+  const bool live = voxel < voxels;
+  const __nv_bfloat16* row = x + (live ? voxel : 0) * C;
+  float v[K][8];
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    if (live) {
+      load8(row + (k * T + sub) * 8, v[k]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[k][j] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += bf16_round(v[k][j] * v[k][j]);
+  }
+#pragma unroll
+  for (int o = T / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (!live) return;
+  const float mean = bf16_round(s / static_cast<float>(C));
+  const float shifted = bf16_round(mean + eps);
+  const float rms = bf16_round(sqrtf(shifted));
+  __nv_bfloat16* orow = out + voxel * C;
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float y = bf16_round(__fdiv_rn(v[k][j], rms));
+      o[j] = apply_silu ? silu_f32(y) : y;
+    }
+    store8(orow + (k * T + sub) * 8, o);
+  }
+}
+
 // ----------------------------------------------------------------------------- GroupNorm
 // Affine GroupNorm with fp32 two-pass statistics over each group's channels and all voxels
 // (kinomlx/kernels/fused_ops.py:47-139, 375-409), then optionally SiLU. The statistics need a
@@ -283,25 +334,31 @@ __global__ void tile_blend_kernel(const __nv_bfloat16* __restrict__ dec, int Ft,
                                   const float* __restrict__ mask_h, const float* __restrict__ mask_w) {
   griddep_wait();
   griddep_launch();
+  // one output row (channel, frame, y) per CTA iteration, the row's pixels across the threads:
+  // the index arithmetic is per row, in 32 bits, and the canvas accesses are coalesced
   const int Hp = ht * patch, Wp = wt * patch;
-  const int64_t n = static_cast<int64_t>(channels) * Ft * Hp * Wp;
+  const int nrows = channels * Ft * Hp;
   const int packed = channels * patch * patch;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int xx = static_cast<int>(i % Wp);
-    int64_t r = i / Wp;
-    const int yy = static_cast<int>(r % Hp);
-    r /= Hp;
-    const int f = static_cast<int>(r % Ft);
-    const int c = static_cast<int>(r / Ft);
-    const int h = yy / patch, ph = yy % patch, w = xx / patch, pw = xx % patch;
-    const int64_t src = ((static_cast<int64_t>(f) * ht + h) * wt + w) * packed +
-                        (c * patch + pw) * patch + ph;
-    const float m = mask_h[yy] * mask_w[xx];
-    const float val = __bfloat162float(dec[src]) * m;
-    const int64_t dst = ((static_cast<int64_t>(c) * Ft + f) * Hout + (y0 + yy)) * Wout + (x0 + xx);
-    canvas[dst] += val;
-    if (c == 0 && f == 0) wcanvas[static_cast<int64_t>(y0 + yy) * Wout + (x0 + xx)] += m;
+  for (int rr = blockIdx.x; rr < nrows; rr += gridDim.x) {
+    const int yy = rr % Hp;
+    const int cf = rr / Hp;
+    const int f = cf % Ft;
+    const int c = cf / Ft;
+    const int h = yy / patch, ph = yy - (yy / patch) * patch;
+    const float mh = mask_h[yy];
+    const int64_t src_row = (static_cast<int64_t>(f) * ht + h) * wt * packed +
+                            static_cast<int64_t>(c) * patch * patch + ph;
+    const int64_t dst_row =
+        ((static_cast<int64_t>(c) * Ft + f) * Hout + (y0 + yy)) * static_cast<int64_t>(Wout) + x0;
+    const bool first_plane = c == 0 && f == 0;
+    for (int xx = threadIdx.x; xx < Wp; xx += blockDim.x) {
+      const int w = xx / patch, pw = xx - (xx / patch) * patch;
+      const float m = mh * mask_w[xx];
+      const float val =
+          __bfloat162float(dec[src_row + static_cast<int64_t>(w) * packed + pw * patch]) * m;
+      canvas[dst_row + xx] += val;
+      if (first_plane) wcanvas[static_cast<int64_t>(y0 + yy) * Wout + x0 + xx] += m;
+    }
   }
 }
 

@@ -277,6 +277,43 @@ def test_split_rope_bit_exact_self_test_recipe(cuda_device):
     assert torch.equal(out.cpu(), graph)
 
 
+@pytest.mark.parametrize("batch,heads,tokens,half,table_batch",
+                         [(1, 32, 300, 64, 1), (2, 3, 17, 8, 2), (2, 2, 5, 12, 1)])
+def test_split_rope_vector_path_bit_exact(cuda_device, batch, heads, tokens, half, table_batch):
+    """half % 4 == 0 runs the four-pair kernel: bit-identical to the reference graph
+    (kinomlx/kernels/split_rope.py:87-98), with shared and per-batch tables."""
+    from kinomlx_b200 import ops
+
+    value = _randn((batch, tokens, heads * 2 * half), 51)
+    angles = torch.rand((table_batch, heads, tokens, half),
+                        generator=torch.Generator().manual_seed(52)) * 6.0
+    cos, sin = torch.cos(angles), torch.sin(angles)
+    hf = value.reshape(batch, tokens, heads, 2 * half).transpose(1, 2).float()
+    first, second = hf[..., :half], hf[..., half:]
+    graph = torch.cat([first * cos - second * sin, first * sin + second * cos], -1)
+    graph = graph.transpose(1, 2).reshape(value.shape).to(BF)
+    out = ops.split_rope(value.to(cuda_device), cos.to(cuda_device), sin.to(cuda_device))
+    assert torch.equal(out.cpu(), graph)
+
+
+@pytest.mark.parametrize("channels", [64, 128, 512, 1024, 96])
+def test_pixel_norm_widths(cuda_device, channels):
+    """Every PixelNorm (+ SiLU) form: the vector kernels (64..1024, powers of two) and the
+    warp-per-voxel kernel (other widths), against the stepwise bf16 oracle
+    (kinomlx/kernels/fused_ops.py:460-476, blocks.py:165-168)."""
+    from kinomlx_b200 import ops
+    from oracle import fused_ops as fo
+
+    x = _randn((3, 7, 11, channels), 53)
+    for silu in (False, True):
+        exp = fo.pixel_norm(x, dim=-1, eps=1e-8)
+        if silu:
+            exp = fo.silu(exp)
+        out = ops.pixel_norm(x.to(cuda_device), 1e-8, silu=silu).cpu()
+        assert _max_rel(out, exp) <= 2e-2
+        assert (out == exp).float().mean() > 0.97
+
+
 # ------------------------------------------------------------------------------------ elementwise
 def test_gelu_silu_bounds(cuda_device):
     """On the reference's grid (tests/kernels/test_fused_ops.py: linspace(-8, 8, 65536) in bf16).
