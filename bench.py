@@ -690,6 +690,36 @@ def run_kernel_case(case: str) -> None:
     elif case == "bandwidth":
         run_bandwidth_case(dev)
         return
+    elif case == "f32":
+        # fp32 parity mode at config 1: the image stream's FF up projection (1024 x 12288 x 3072,
+        # GELU epilogue) and the joint attention over 1536 tokens x 24 heads
+        from kinomlx_b200 import ops_f32
+
+        f32 = torch.float32
+        x = normal((1, 1024, d), seed=1, device=dev, dtype=f32)
+        w = normal((4 * d, d), seed=2, device=dev, dtype=f32, std=0.02)
+        out = torch.empty((1, 1024, 4 * d), device=dev, dtype=f32)
+        qkv = normal((1, 1536, 3 * d), seed=3, device=dev, dtype=f32)
+        q, k, v = qkv[..., :d], qkv[..., d : 2 * d], qkv[..., 2 * d :]
+        att = torch.empty((1, 1536, d), device=dev, dtype=f32)
+        times = {}
+        for name, fn, flop in (
+            ("gemm_f32", lambda: ops_f32.linear(x, w, out, kind=ops.EPI_GELU), 2.0 * 1024 * 4 * d * d),
+            ("attention_f32", lambda: ops_f32.attention(q, k, v, att, heads=24),
+             4.0 * 1536 * 1536 * 24 * 128),
+        ):
+            fn()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / 2
+            times[name] = {"ms": round(ms, 4), "tflops": round(flop / (ms * 1e9), 1)}
+        ops.device_status()
+        print(json.dumps({"kernel_case": case, "ok": True, "kernels": times}))
+        return
     else:
         # the decoder's last stage: 128 -> 128 channels at full resolution, with the residual
         # and the GroupNorm statistics of the next norm
@@ -812,7 +842,7 @@ def main() -> None:
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
     ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow",
-                                              "bandwidth"],
+                                              "bandwidth", "f32"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     args = ap.parse_args()
     if args.kernel_case:
