@@ -30,7 +30,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (7); bumped on any signature change. */
+/* ABI version of this header (8); bumped on any signature change. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -416,7 +416,7 @@ kino_status kino_blend_normalize(float* canvas, const float* weights, int64_t pl
  * strides in elements, row strides multiples of 4 with 16-byte aligned operands. */
 
 typedef struct kino_epilogue_f32 {
-  int kind;                /* KINO_EPI_NONE, KINO_EPI_GELU, KINO_EPI_GATED_RESIDUAL, KINO_EPI_EULER */
+  int kind;                /* KINO_EPI_NONE, _GELU, _GATED_RESIDUAL, _EULER, _SIGMOID2 or _EULER_X0 */
   const float* bias;       /* [n] or NULL: acc + bias */
   const float* residual;   /* GATED_RESIDUAL: out = residual + gate[b] * (acc + bias); may alias out */
   int64_t ld_residual;
@@ -424,10 +424,13 @@ typedef struct kino_epilogue_f32 {
   const float* gate;       /* GATED_RESIDUAL: [batch][n] at batch stride bs_gate */
   int64_t bs_gate;
   int64_t act_col_begin;   /* GELU: tanh-GELU (inner clamped to +-10) on columns >= act_col_begin */
-  float scalar;            /* EULER: out = aux + scalar * (acc + bias) */
-  const float* aux;        /* EULER: current sample, geometry of out; may alias out */
+  float scalar;            /* EULER: out = aux + scalar * (acc + bias); EULER_X0: sigma */
+  const float* aux;        /* EULER, EULER_X0: current sample, geometry of out; may alias out */
   int64_t ld_aux;
   int64_t bs_aux;
+  float scalar2;           /* EULER_X0: v = acc + bias; x0 = aux - scalar * v;
+                              out = x0 + scalar2 * (aux - x0) (scalar2 = sigma_next / sigma).
+                              SIGMOID2 needs no operand: out = 2 * sigmoid(acc + bias) */
 } kino_epilogue_f32;
 
 /* kino_linear in fp32: out[b, i, j] = epilogue(sum_k x[b, i, k] * w[j, k]); w (n, k) row-major.
@@ -440,13 +443,16 @@ kino_status kino_linear_f32(const float* x, const float* w, float* out, int64_t 
                             int64_t ldo, int64_t bso, const kino_epilogue_f32* epi, void* stream);
 
 /* softmax(q k^T * scale) v per (batch, head), head_dim 128, token-major q (q_tokens rows),
- * k and v (kv_tokens rows); out like q and may alias it. Replaces MLX SDPA in fp32
- * (kinomlx/models/flux2/kv.py:48-54, kinomlx/models/flux2/transformer.py:35-53). */
+ * k and v (kv_tokens rows); out like q and may alias it. With `gate` (batch, q_tokens, heads)
+ * at row stride ld_gate and batch stride bs_gate, each head's output is multiplied by its gate.
+ * Replaces MLX SDPA in fp32 (kinomlx/models/flux2/kv.py:48-54, kinomlx/models/flux2/
+ * transformer.py:35-53, kinomlx/models/ltx2/transformer/attention.py:144-161, 364-368). */
 kino_status kino_attention_f32(const float* q, const float* k, const float* v, float* out,
                                int64_t batch, int64_t heads, int64_t q_tokens, int64_t kv_tokens,
                                int64_t ld_q, int64_t bs_q, int64_t ld_k, int64_t bs_k,
                                int64_t ld_v, int64_t bs_v, int64_t ld_out, int64_t bs_out,
-                               float scale, void* stream);
+                               float scale, const float* gate, int64_t ld_gate, int64_t bs_gate,
+                               void* stream);
 
 /* kino_adaln in fp32: out = norm(x) * (1 + scale[b]) + shift[b], dim <= 8192
  * (kinomlx/models/flux2/transformer.py:56-60). */
@@ -455,14 +461,21 @@ kino_status kino_adaln_f32(const float* x, int64_t ldx, int64_t bsx, const float
                            int64_t bso, int64_t batch, int64_t rows, int64_t dim, int norm_kind,
                            float eps, void* stream);
 
-/* kino_qk_norm_rope in fp32, in place: KINO_QKNORM_PER_HEAD (or NONE) then KINO_ROPE_PAIRS (or
- * NONE); tables token-major, (table_batch, table_tokens, 128) fp32. Replaces QKNorm + rotate
- * (kinomlx/models/flux2/transformer.py:17-32, 68-75). */
+/* kino_qk_norm_rope in fp32, in place, in one of two forms: KINO_QKNORM_PER_HEAD (or NONE) then
+ * KINO_ROPE_PAIRS (or NONE) with token-major tables (table_batch, table_tokens, 128), replacing
+ * QKNorm + rotate (kinomlx/models/flux2/transformer.py:17-32, 68-75); or KINO_QKNORM_FULL_ROW (or
+ * NONE) then KINO_ROPE_SPLIT (or NONE) with tables (table_batch, heads, table_tokens, 64), rows
+ * up to 8192 wide, replacing q_norm/k_norm + apply_split_rotary_emb
+ * (kinomlx/models/ltx2/transformer/attention.py:330-342). */
 kino_status kino_qk_norm_rope_f32(float* x, int64_t ld, int64_t bs, int64_t batch,
                                   int64_t tokens, int64_t heads, const float* weight,
                                   int norm_kind, int rope_kind, const float* cos_table,
                                   const float* sin_table, int table_batched, int64_t table_tokens,
                                   int64_t table_offset, float eps, void* stream);
+
+/* out[r, c] = a[r, c] + b[c], fp32 (kinomlx/models/ltx2/transformer/transformer.py:178-186). */
+kino_status kino_add_rows_f32(const float* a, const float* b, float* out, int64_t rows, int64_t n,
+                              void* stream);
 
 /* fp32 tanh-GELU and SiLU (kinomlx/kernels/fused_ops.py:27-45, 327-372). */
 kino_status kino_gelu_tanh_f32(const float* x, float* out, int64_t n, void* stream);

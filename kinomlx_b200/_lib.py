@@ -160,6 +160,7 @@ class EpilogueF32(ctypes.Structure):
         ("aux", c_void_p),
         ("ld_aux", c_int64),
         ("bs_aux", c_int64),
+        ("scalar2", c_float),
     ]
 
 
@@ -223,13 +224,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "kino_attention_f32": (
         c_int,
-        [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, F, P],
+        [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, F, P, I64, I64, P],
     ),
     "kino_adaln_f32": (c_int, [P, I64, I64, P, P, I64, P, I64, I64, I64, I64, I64, c_int, F, P]),
     "kino_qk_norm_rope_f32": (
         c_int,
         [P, I64, I64, I64, I64, I64, P, c_int, c_int, P, P, c_int, I64, I64, F, P],
     ),
+    "kino_add_rows_f32": (c_int, [P, P, P, I64, I64, P]),
     "kino_gelu_tanh_f32": (c_int, [P, P, I64, P]),
     "kino_silu_f32": (c_int, [P, P, I64, P]),
     "kino_cfg_combine_f32": (c_int, [P, P, F, P, I64, P]),

@@ -458,7 +458,7 @@ void* group_norm_scratch_address(kino_status* status) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 7; }
+int kino_abi_version(void) { return 8; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -1361,12 +1361,12 @@ kino_status kino_linear_f32(const float* x, const float* w, float* out, int64_t 
   kino::F32Epi e;
   std::memset(&e, 0, sizeof(e));
   if (epi != nullptr) {
-    if (epi->kind < KINO_EPI_NONE || epi->kind > KINO_EPI_EULER)
-      return fail(KINO_ENOTSUPPORTED, "kino_linear_f32: epilogue %d (NONE, GELU, GATED_RESIDUAL "
-                  "or EULER)", epi->kind);
+    if (epi->kind < KINO_EPI_NONE || epi->kind > KINO_EPI_EULER_X0)
+      return fail(KINO_ENOTSUPPORTED, "kino_linear_f32: epilogue %d (NONE, GELU, GATED_RESIDUAL, "
+                  "EULER, SIGMOID2 or EULER_X0)", epi->kind);
     if (epi->kind == KINO_EPI_GATED_RESIDUAL && (epi->residual == nullptr || epi->gate == nullptr))
       return fail(KINO_EINVAL, "kino_linear_f32: gated residual needs residual and gate");
-    if (epi->kind == KINO_EPI_EULER && epi->aux == nullptr)
+    if ((epi->kind == KINO_EPI_EULER || epi->kind == KINO_EPI_EULER_X0) && epi->aux == nullptr)
       return fail(KINO_EINVAL, "kino_linear_f32: Euler epilogue needs the sample");
     e.kind = epi->kind;
     e.bias = epi->bias;
@@ -1380,6 +1380,7 @@ kino_status kino_linear_f32(const float* x, const float* w, float* out, int64_t 
     e.aux = epi->aux;
     e.ld_aux = epi->ld_aux;
     e.bs_aux = epi->bs_aux;
+    e.scalar2 = epi->scalar2;
   }
   const dim3 grid(static_cast<unsigned>((n + kino::F32_BN - 1) / kino::F32_BN),
                   static_cast<unsigned>((m + kino::F32_BM - 1) / kino::F32_BM),
@@ -1394,9 +1395,12 @@ kino_status kino_attention_f32(const float* q, const float* k, const float* v, f
                                int64_t batch, int64_t heads, int64_t q_tokens, int64_t kv_tokens,
                                int64_t ld_q, int64_t bs_q, int64_t ld_k, int64_t bs_k,
                                int64_t ld_v, int64_t bs_v, int64_t ld_out, int64_t bs_out,
-                               float scale, void* stream) {
+                               float scale, const float* gate, int64_t ld_gate, int64_t bs_gate,
+                               void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
     return fail(KINO_EINVAL, "kino_attention_f32: null operand");
+  if (gate != nullptr && ld_gate < heads)
+    return fail(KINO_EINVAL, "kino_attention_f32: gate rows shorter than heads");
   if (batch < 1 || heads < 1 || q_tokens < 1 || kv_tokens < 1)
     return fail(KINO_EINVAL, "kino_attention_f32: empty shape");
   if (batch > 65535 || heads > 65535 || q_tokens > 0x7fffffffLL || kv_tokens > 0x7fffffffLL)
@@ -1415,7 +1419,7 @@ kino_status kino_attention_f32(const float* q, const float* k, const float* v, f
   launch_pdl(kino::attention_f32_kernel, grid, dim3(kino::FA32_THREADS), smem,
              static_cast<cudaStream_t>(stream), q, k, v, out, static_cast<int>(q_tokens),
              static_cast<int>(kv_tokens), ld_q, bs_q, ld_k, bs_k, ld_v, bs_v, ld_out, bs_out,
-             scale);
+             scale, gate, ld_gate, bs_gate);
   return check_launch("kino_attention_f32");
 }
 
@@ -1444,30 +1448,59 @@ kino_status kino_qk_norm_rope_f32(float* x, int64_t ld, int64_t bs, int64_t batc
                                   const float* sin_table, int table_batched, int64_t table_tokens,
                                   int64_t table_offset, float eps, void* stream) {
   if (x == nullptr) return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: null");
-  if ((norm_kind != KINO_QKNORM_NONE && norm_kind != KINO_QKNORM_PER_HEAD) ||
-      (rope_kind != KINO_ROPE_NONE && rope_kind != KINO_ROPE_PAIRS))
-    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: per-head norm and pair RoPE only");
-  if (norm_kind == KINO_QKNORM_PER_HEAD && (weight == nullptr || !aligned16(weight)))
+  // per-head norm with pair RoPE (Flux2), or full-row norm with split RoPE (LTX-2)
+  const bool flux_form = (norm_kind == KINO_QKNORM_NONE || norm_kind == KINO_QKNORM_PER_HEAD) &&
+                         (rope_kind == KINO_ROPE_NONE || rope_kind == KINO_ROPE_PAIRS);
+  const bool ltx_form = (norm_kind == KINO_QKNORM_NONE || norm_kind == KINO_QKNORM_FULL_ROW) &&
+                        (rope_kind == KINO_ROPE_NONE || rope_kind == KINO_ROPE_SPLIT);
+  if (!flux_form && !ltx_form)
+    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: per-head norm with pair RoPE or "
+                "full-row norm with split RoPE");
+  if (norm_kind != KINO_QKNORM_NONE && (weight == nullptr || !aligned16(weight)))
     return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: norm needs an aligned weight");
-  if (rope_kind == KINO_ROPE_PAIRS &&
+  if (rope_kind != KINO_ROPE_NONE &&
       (cos_table == nullptr || sin_table == nullptr || !aligned16(cos_table) ||
        !aligned16(sin_table)))
     return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: rope needs aligned tables");
   if (ld % 4 || bs % 4 || !aligned16(x) || ld < heads * 128)
     return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: aligned rows of heads * 128");
   if (tokens < 1 || batch < 1 || heads < 1) return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: empty");
-  if (rope_kind == KINO_ROPE_PAIRS && (table_offset < 0 || table_offset + tokens > table_tokens))
+  if (rope_kind != KINO_ROPE_NONE && (table_offset < 0 || table_offset + tokens > table_tokens))
     return fail(KINO_EINVAL, "kino_qk_norm_rope_f32: table too short");
+  if (tokens > 0x7fffffffLL || batch * tokens > 0x7fffffffLL)
+    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: shape too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!flux_form) {
+    if (heads * 64 > 256 * kino::QKROW32_MAX_PAIRS)
+      return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: full-row form takes rows up to 8192");
+    launch_pdl(kino::qk_norm_rope_row_f32_kernel, dim3(static_cast<unsigned>(batch * tokens)),
+               dim3(256), 0, st, x, ld, bs, static_cast<int>(tokens), static_cast<int>(heads),
+               weight, norm_kind == KINO_QKNORM_FULL_ROW ? 1 : 0,
+               rope_kind == KINO_ROPE_SPLIT ? 1 : 0, cos_table, sin_table, table_batched,
+               table_tokens, table_offset, eps);
+    return check_launch("kino_qk_norm_rope_f32");
+  }
   const int64_t items = batch * tokens * heads;
   const int64_t blocks = (items + 7) / 8;
-  if (blocks > 0x7fffffffLL || tokens > 0x7fffffffLL)
-    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: shape too large");
-  launch_pdl(kino::qk_norm_rope_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
-             static_cast<cudaStream_t>(stream), x, ld, bs, static_cast<int>(tokens),
-             static_cast<int>(heads), weight, norm_kind == KINO_QKNORM_PER_HEAD ? 1 : 0,
-             rope_kind == KINO_ROPE_PAIRS ? 1 : 0, cos_table, sin_table, table_batched,
-             table_tokens, table_offset, eps, items);
+  if (blocks > 0x7fffffffLL) return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope_f32: shape too large");
+  launch_pdl(kino::qk_norm_rope_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, st,
+             x, ld, bs, static_cast<int>(tokens), static_cast<int>(heads), weight,
+             norm_kind == KINO_QKNORM_PER_HEAD ? 1 : 0, rope_kind == KINO_ROPE_PAIRS ? 1 : 0,
+             cos_table, sin_table, table_batched, table_tokens, table_offset, eps, items);
   return check_launch("kino_qk_norm_rope_f32");
+}
+
+kino_status kino_add_rows_f32(const float* a, const float* b, float* out, int64_t rows, int64_t n,
+                              void* stream) {
+  if (a == nullptr || b == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_add_rows_f32: null");
+  if (rows < 1 || n < 1 || n > 0x7fffffffLL) return fail(KINO_EINVAL, "kino_add_rows_f32: shape");
+  const int64_t total = rows * n;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  launch_pdl(kino::add_rows_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), a, b, out, total, static_cast<int>(n));
+  return check_launch("kino_add_rows_f32");
 }
 
 static kino_status launch_elem_f32(int kind, const float* a, const float* b, float* out,

@@ -24,7 +24,9 @@ constexpr int F32_PAD = 4;  // keeps float4 alignment, halves the transposed-sto
 constexpr int F32_THREADS = 256;
 
 struct F32Epi {
-  int kind;  // EPI_NONE (0), EPI_GELU (1), EPI_GATED_RESIDUAL (2), EPI_EULER (3)
+  // EPI_NONE (0), EPI_GELU (1), EPI_GATED_RESIDUAL (2), EPI_EULER (3), EPI_SIGMOID2 (4),
+  // EPI_EULER_X0 (5)
+  int kind;
   const float* bias;
   const float* residual;
   int64_t ld_res, bs_res;
@@ -34,6 +36,7 @@ struct F32Epi {
   float scalar;
   const float* aux;
   int64_t ld_aux, bs_aux;
+  float scalar2;
 };
 
 // tanh-GELU exactly as the reference formula reads in fp32: the inner argument clamped to +-10
@@ -150,6 +153,15 @@ __global__ void __launch_bounds__(F32_THREADS, 2)
       } else if (e.kind == 3) {
         const float cur = e.aux[static_cast<int64_t>(b) * e.bs_aux + static_cast<int64_t>(r) * e.ld_aux + c];
         v = __fadd_rn(cur, __fmul_rn(e.scalar, v));
+      } else if (e.kind == 4) {
+        // 2 * sigmoid(v) (kinomlx/models/ltx2/transformer/attention.py:298-303)
+        v = __fmul_rn(2.0f, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v))));
+      } else if (e.kind == 5) {
+        // x0 = x - sigma * v, then x0 + ratio * (x - x0) (ltx2/transformer/wrappers.py:49-65,
+        // samplers/steps.py:36-70)
+        const float cur = e.aux[static_cast<int64_t>(b) * e.bs_aux + static_cast<int64_t>(r) * e.ld_aux + c];
+        const float x0 = __fsub_rn(cur, __fmul_rn(e.scalar, v));
+        v = __fadd_rn(x0, __fmul_rn(e.scalar2, __fsub_rn(cur, x0)));
       }
       ob[static_cast<int64_t>(r) * ldo + c] = v;
     }
@@ -180,7 +192,8 @@ __global__ void __launch_bounds__(FA32_THREADS, 1)
     attention_f32_kernel(const float* q, const float* __restrict__ k,
                          const float* __restrict__ vv, float* out, int tq, int tk, int64_t ld_q,
                          int64_t bs_q, int64_t ld_k, int64_t bs_k, int64_t ld_v, int64_t bs_v,
-                         int64_t ld_o, int64_t bs_o, float scale) {
+                         int64_t ld_o, int64_t bs_o, float scale, const float* __restrict__ gate,
+                         int64_t ld_g, int64_t bs_g) {
   extern __shared__ __align__(16) unsigned char fa32_raw[];
   Fa32Smem& s = *reinterpret_cast<Fa32Smem*>(fa32_raw);
   griddep_wait();
@@ -330,15 +343,17 @@ __global__ void __launch_bounds__(FA32_THREADS, 1)
     const int t = q0 + ty * 4 + i;
     if (t >= tq) continue;
     const float l = s.lsum[ty * 4 + i];
-    float4 w0, w1;
-    w0.x = __fdiv_rn(o[i][0], l);
-    w0.y = __fdiv_rn(o[i][1], l);
-    w0.z = __fdiv_rn(o[i][2], l);
-    w0.w = __fdiv_rn(o[i][3], l);
-    w1.x = __fdiv_rn(o[i][4], l);
-    w1.y = __fdiv_rn(o[i][5], l);
-    w1.z = __fdiv_rn(o[i][6], l);
-    w1.w = __fdiv_rn(o[i][7], l);
+    float r[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) r[c] = __fdiv_rn(o[i][c], l);
+    if (gate != nullptr) {
+      // per-(token, head) output gate (kinomlx/models/ltx2/transformer/attention.py:364-368)
+      const float g = gate[static_cast<int64_t>(b) * bs_g + static_cast<int64_t>(t) * ld_g + h];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) r[c] = __fmul_rn(r[c], g);
+    }
+    const float4 w0 = make_float4(r[0], r[1], r[2], r[3]);
+    const float4 w1 = make_float4(r[4], r[5], r[6], r[7]);
     *reinterpret_cast<float4*>(ob + static_cast<int64_t>(t) * ld_o + tx * 4) = w0;
     *reinterpret_cast<float4*>(ob + static_cast<int64_t>(t) * ld_o + 64 + tx * 4) = w1;
   }
@@ -453,6 +468,79 @@ __global__ void __launch_bounds__(256)
     v = r;
   }
   *reinterpret_cast<float4*>(p) = v;
+}
+
+// In place on token-major x (batch x tokens x heads*128): RMSNorm over the whole row with a
+// (heads*128) weight (fp32 statistics, eps), then the split-half rotation of each head
+// (first, second) = (x[i], x[i + 64]) -> (first c - second s, first s + second c) with fp32
+// tables (table_batch, heads, table_tokens, 64), token t reading table row table_offset + t
+// (kinomlx/models/ltx2/transformer/attention.py:330-342, rope.py:18-61). One CTA of 256 threads
+// per (batch, token) row; thread k holds the pairs k + 256 j (pair p = head * 64 + i).
+constexpr int QKROW32_MAX_PAIRS = 16;  // per thread: rows up to 8192 wide
+
+__global__ void __launch_bounds__(256)
+    qk_norm_rope_row_f32_kernel(float* x, int64_t ld, int64_t bs, int tokens, int heads,
+                                const float* __restrict__ weight, int full_row_norm,
+                                int rope_split, const float* __restrict__ cos_t,
+                                const float* __restrict__ sin_t, int table_batched,
+                                int64_t table_tokens, int64_t table_offset, float eps) {
+  __shared__ float red[8];
+  griddep_wait();
+  griddep_launch();
+  const int b = blockIdx.x / tokens;
+  const int t = blockIdx.x % tokens;
+  float* row = x + static_cast<int64_t>(b) * bs + static_cast<int64_t>(t) * ld;
+  const int pairs = heads * 64;
+  float e1[QKROW32_MAX_PAIRS], e2[QKROW32_MAX_PAIRS];
+#pragma unroll
+  for (int j = 0; j < QKROW32_MAX_PAIRS; ++j) {
+    const int p = threadIdx.x + j * 256;
+    const int base = (p >> 6) * 128 + (p & 63);
+    e1[j] = p < pairs ? row[base] : 0.f;
+    e2[j] = p < pairs ? row[base + 64] : 0.f;
+  }
+  if (full_row_norm) {
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < QKROW32_MAX_PAIRS; ++j) q += e1[j] * e1[j] + e2[j] * e2[j];
+    const float inv = rsqrtf(__fdiv_rn(block_sum_256(q, red), static_cast<float>(heads * 128)) + eps);
+#pragma unroll
+    for (int j = 0; j < QKROW32_MAX_PAIRS; ++j) {
+      const int p = threadIdx.x + j * 256;
+      if (p >= pairs) continue;
+      const int base = (p >> 6) * 128 + (p & 63);
+      e1[j] = __fmul_rn(__fmul_rn(e1[j], inv), weight[base]);
+      e2[j] = __fmul_rn(__fmul_rn(e2[j], inv), weight[base + 64]);
+    }
+  }
+  const int64_t trow = (table_batched ? static_cast<int64_t>(b) : 0) * heads;
+#pragma unroll
+  for (int j = 0; j < QKROW32_MAX_PAIRS; ++j) {
+    const int p = threadIdx.x + j * 256;
+    if (p >= pairs) continue;
+    const int h = p >> 6, i = p & 63;
+    const int base = h * 128 + i;
+    float o1 = e1[j], o2 = e2[j];
+    if (rope_split) {
+      const int64_t entry = ((trow + h) * table_tokens + table_offset + t) * 64 + i;
+      const float c = cos_t[entry], sn = sin_t[entry];
+      o1 = __fsub_rn(__fmul_rn(e1[j], c), __fmul_rn(e2[j], sn));
+      o2 = __fadd_rn(__fmul_rn(e1[j], sn), __fmul_rn(e2[j], c));
+    }
+    row[base] = o1;
+    row[base + 64] = o2;
+  }
+}
+
+// out[r, c] = a[r, c] + b[c] (the per-block modulation tables plus the step's timestep
+// projection, kinomlx/models/ltx2/transformer/transformer.py:178-186).
+__global__ void add_rows_f32_kernel(const float* __restrict__ a, const float* __restrict__ bv,
+                                    float* __restrict__ out, int64_t total, int n) {
+  griddep_wait();
+  griddep_launch();
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = __fadd_rn(a[i], bv[i % n]);
 }
 
 // ---------------------------------------------------------------- elementwise

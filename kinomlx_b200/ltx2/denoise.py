@@ -29,7 +29,7 @@ def denoise_loop(model: LTXVideoTransformer, latent: torch.Tensor, context: torc
                  check_finite: bool = True) -> torch.Tensor:
     prepared = model.prepare(context, positions)
     t0, t1 = model.sp.shard(latent.shape[1])
-    x = latent[:, t0:t1].to(model.device, torch.bfloat16).clone()
+    x = latent[:, t0:t1].to(model.device, getattr(model, "dtype", torch.bfloat16)).clone()
     values = fp32(sigmas)
     for s, n in zip(values[:-1], values[1:]):
         denoise_step(model, prepared, x, s, n)

@@ -13,13 +13,15 @@ import ctypes
 import torch
 
 from . import _lib
-from ._lib import EPI_EULER, EPI_GATED_RESIDUAL, EPI_GELU, EPI_NONE, NORM_LAYER
+from ._lib import (EPI_EULER, EPI_EULER_X0, EPI_GATED_RESIDUAL, EPI_GELU, EPI_NONE,
+                   EPI_SIGMOID2, NORM_LAYER)
 from .ops import _as3d, _need, _ptr, _stream, _timed
 
 F32 = torch.float32
 
 __all__ = [
     "adaln",
+    "add_rows",
     "attention",
     "cfg_combine",
     "euler_velocity",
@@ -44,10 +46,14 @@ def linear(
     act_col_begin: int = 0,
     dt: float = 0.0,
     sample: torch.Tensor | None = None,
+    sigma: float = 0.0,
+    ratio: float = 0.0,
 ) -> torch.Tensor:
     """out = epilogue(x @ w.T) in fp32 for x (batch, m, k) or (m, k) and an (n, k) weight.
     EPI_GELU applies to columns >= act_col_begin; EPI_GATED_RESIDUAL computes
-    residual + gate * y (gate (batch, n)); EPI_EULER computes sample + dt * y."""
+    residual + gate * y (gate (batch, n)); EPI_EULER computes sample + dt * y; EPI_SIGMOID2
+    computes 2 * sigmoid(y); EPI_EULER_X0 computes x0 = sample - sigma * y, then
+    x0 + ratio * (sample - x0)."""
     _need(x, "x", F32)
     _need(w, "w", F32)
     x3 = _as3d(x)
@@ -80,7 +86,7 @@ def linear(
         epi.bs_gate = g.stride(0) if g.shape[0] > 1 else 0
     elif kind == EPI_GELU:
         epi.act_col_begin = act_col_begin
-    elif kind == EPI_EULER:
+    elif kind in (EPI_EULER, EPI_EULER_X0):
         if sample is None:
             raise ValueError("the Euler epilogue needs the current sample")
         _need(sample, "sample", F32)
@@ -88,8 +94,9 @@ def linear(
         epi.aux = s3.data_ptr()
         epi.ld_aux = s3.stride(1)
         epi.bs_aux = s3.stride(0)
-        epi.scalar = dt
-    elif kind != EPI_NONE:
+        epi.scalar = dt if kind == EPI_EULER else sigma
+        epi.scalar2 = ratio
+    elif kind not in (EPI_NONE, EPI_SIGMOID2):
         raise ValueError(f"epilogue {kind} has no fp32 form")
     with _timed("gemm_f32", 2.0 * batch * m * n * k, 4.0 * (batch * m * k + n * k + batch * m * n)):
         _lib.call("kino_linear_f32", _ptr(x3), _ptr(w), _ptr(o3), batch, m, n, k, x3.stride(1),
@@ -99,9 +106,10 @@ def linear(
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None,
-              *, heads: int, scale: float | None = None) -> torch.Tensor:
+              *, heads: int, scale: float | None = None,
+              gate: torch.Tensor | None = None) -> torch.Tensor:
     """softmax(q k^T * scale) v with q, k, v (batch, tokens, heads * 128) token-major fp32;
-    `out` may be `q` itself."""
+    `out` may be `q` itself; `gate` (batch, q tokens, heads) multiplies each head's output."""
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
         _need(t, name, F32)
     q3, k3, v3 = _as3d(q), _as3d(k), _as3d(v)
@@ -116,11 +124,18 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tens
     o3 = _as3d(out)
     tk = k3.shape[1]
     sc = scale if scale is not None else 128**-0.5
+    g3, ld_g, bs_g = None, 0, 0
+    if gate is not None:
+        _need(gate, "gate", F32)
+        g3 = _as3d(gate)
+        if tuple(g3.shape) != (batch, tq, heads):
+            raise ValueError("attention gate must be (batch, tokens, heads)")
+        ld_g, bs_g = g3.stride(1), g3.stride(0)
     flops = 4.0 * batch * heads * tq * tk * 128
     with _timed("attention_f32", flops, 4.0 * batch * width * (2 * tq + 2 * tk)):
         _lib.call("kino_attention_f32", _ptr(q3), _ptr(k3), _ptr(v3), _ptr(o3), batch, heads, tq,
                   tk, q3.stride(1), q3.stride(0), k3.stride(1), k3.stride(0), v3.stride(1),
-                  v3.stride(0), o3.stride(1), o3.stride(0), sc, _stream())
+                  v3.stride(0), o3.stride(1), o3.stride(0), sc, _ptr(g3), ld_g, bs_g, _stream())
     return out
 
 
@@ -151,8 +166,10 @@ def adaln(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
 def qk_norm_rope(x: torch.Tensor, *, heads: int, weight: torch.Tensor | None, norm: int,
                  rope: int, cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
                  table_offset: int = 0, eps: float = 1e-6) -> torch.Tensor:
-    """In place on x (batch, tokens, heads*128) fp32: per-head RMSNorm with `weight`, then the
-    adjacent-pair RoPE from token-major (1|batch, table_tokens, 128) fp32 tables."""
+    """In place on x (batch, tokens, heads*128) fp32: per-head RMSNorm then the adjacent-pair
+    RoPE from token-major (1|batch, table_tokens, 128) tables (QKNORM_PER_HEAD / ROPE_PAIRS), or
+    full-row RMSNorm then the split-half RoPE from (1|batch, heads, table_tokens, 64) tables
+    (QKNORM_FULL_ROW / ROPE_SPLIT)."""
     _need(x, "x", F32)
     x3 = _as3d(x)
     batch, tokens, width = x3.shape
@@ -164,8 +181,8 @@ def qk_norm_rope(x: torch.Tensor, *, heads: int, weight: torch.Tensor | None, no
     if cos is not None:
         _need(cos, "cos", F32)
         _need(sin, "sin", F32)
-        if not (cos.is_contiguous() and sin.is_contiguous()) or cos.shape[-1] != 128:
-            raise ValueError("RoPE tables must be contiguous (..., tokens, 128)")
+        if not (cos.is_contiguous() and sin.is_contiguous()):
+            raise ValueError("RoPE tables must be contiguous")
         table_tokens = cos.shape[-2]
         table_batched = int(cos.dim() >= 3 and cos.shape[0] > 1)
     with _timed("qk_norm_rope_f32", 0.0, 8.0 * batch * tokens * width):
@@ -173,6 +190,24 @@ def qk_norm_rope(x: torch.Tensor, *, heads: int, weight: torch.Tensor | None, no
                   heads, _ptr(weight), norm, rope, _ptr(cos), _ptr(sin), table_batched,
                   table_tokens, table_offset, eps, _stream())
     return x
+
+
+def add_rows(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = a + b with b (n,) broadcast over the rows of a contiguous (..., n), fp32."""
+    _need(a, "a", F32)
+    _need(b, "b", F32)
+    if not a.is_contiguous() or b.numel() != a.shape[-1]:
+        raise ValueError("add_rows needs a contiguous (..., n) tensor and an (n,) row")
+    b = b.contiguous()
+    if out is None:
+        out = torch.empty_like(a)
+    _need(out, "out", F32)
+    if not out.is_contiguous() or out.shape != a.shape:
+        raise ValueError("add_rows writes a contiguous tensor shaped like a")
+    n = a.shape[-1]
+    with _timed("elementwise_f32", 0.0, 8.0 * a.numel()):
+        _lib.call("kino_add_rows_f32", _ptr(a), _ptr(b), _ptr(out), a.numel() // n, n, _stream())
+    return out
 
 
 def _unary(name: str, x: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:

@@ -238,9 +238,10 @@ def euler_step(sample, denoised, sigma: float, sigma_next: float):
 
 
 def denoise(p, latent, context, positions, sigmas, v: LTXVariant):
-    """Deterministic-Euler loop (kinomlx/models/ltx2/denoise.py:159-365)."""
+    """Deterministic-Euler loop (kinomlx/models/ltx2/denoise.py:159-365); the model dtype (which
+    the timestep features are cast to) is the latent's."""
     x = latent
     for s, n in zip(sigmas[:-1], sigmas[1:]):
-        velocity = forward(p, x, context, s, positions, v)
+        velocity = forward(p, x, context, s, positions, v, dtype=latent.dtype)
         x = euler_step(x, to_denoised(x, s, velocity), s, n)
     return x

@@ -13,13 +13,18 @@ import torch
 
 from oracle import flux2 as ref
 from oracle import fused_ops as rops
+from oracle import ltx2 as lref
 from kinomlx_b200 import _lib
 from kinomlx_b200 import ops_f32 as f
 from kinomlx_b200.flux2 import config as fcfg
 from kinomlx_b200.flux2 import sampling
 from kinomlx_b200.flux2.transformer import rotary_positions
 from kinomlx_b200.flux2.transformer_f32 import Flux2TransformerF32
-from kinomlx_b200.synthetic import flux_weights, normal
+from kinomlx_b200.ltx2 import config as lcfg
+from kinomlx_b200.ltx2 import denoise as ldn
+from kinomlx_b200.ltx2.transformer import precompute_freqs_cis
+from kinomlx_b200.ltx2.transformer_f32 import LTXVideoTransformerF32
+from kinomlx_b200.synthetic import flux_weights, ltx_weights, normal
 
 pytestmark = pytest.mark.gpu
 F32 = torch.float32
@@ -229,6 +234,104 @@ def test_denoise_f32_matches_oracle(cuda_device, cfg):
     model = Flux2TransformerF32(w, v, cuda_device)
     out = sampling.denoise(model, noise, text, ids, sigmas=sampling.linear_sigmas(3),
                            negative=negative, guidance=guidance)
+    assert out.dtype == F32
+    assert _max_rel(out, expect) <= TOL, _max_rel(out, expect)
+    assert _cos(out, expect) >= 0.999
+
+
+def test_linear_f32_ltx_epilogues(cuda_device):
+    """2 * sigmoid (the LTX head gates) and X0 + Euler (the LTX sampler update)."""
+    dev = cuda_device
+    batch, m, n, k = 2, 70, 136, 264
+    x, w, b = _r((batch, m, k), 60), _r((n, k), 61, 0.05), _r((n,), 62)
+    y = rops.linear(x, w, b)
+    got = f.linear(x.to(dev), w.to(dev), bias=b.to(dev), kind=_lib.EPI_SIGMOID2)
+    assert _max_rel(got, 2.0 * torch.sigmoid(y)) <= TOL
+    cur = _r((batch, m, n), 63)
+    sigma, nxt = lref.DISTILLED_STAGE_1_SIGMAS[6], lref.DISTILLED_STAGE_1_SIGMAS[7]
+    expect = lref.euler_step(cur, lref.to_denoised(cur, sigma, y), sigma, nxt)
+    cur_d = cur.to(dev)
+    ratio = float(torch.tensor(nxt / sigma, dtype=F32))
+    f.linear(x.to(dev), w.to(dev), cur_d, bias=b.to(dev), kind=_lib.EPI_EULER_X0,
+             sigma=float(torch.tensor(sigma, dtype=F32)), ratio=ratio, sample=cur_d)
+    assert _max_rel(cur_d, expect) <= TOL
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_qk_norm_rope_f32_full_row_split(cuda_device, rope):
+    """RMSNorm over the whole 4096-wide row with its weight, then the split-half rotation per
+    head (the LTX q/k path), on a column slice of a wider row; without RoPE, the cross-attention
+    q/k norm."""
+    v = lcfg.BASELINE_VIDEO
+    pos = lref.pixel_coords(lref.patch_grid_bounds(2, 3, 5))
+    cos, sin = precompute_freqs_cis(pos, v)
+    tokens, d = cos.shape[2], v.dim
+    x = _r((1, tokens, 3 * d), 64)
+    wt = 1 + _r((d,), 65, 0.1)
+    expect = rops.rms_norm(x[..., d : 2 * d], wt, v.eps)
+    if rope:
+        expect = lref.apply_split_rotary_emb(expect, cos, sin)
+    xd = x.to(cuda_device)
+    f.qk_norm_rope(xd[..., d : 2 * d], heads=v.heads, weight=wt.to(cuda_device),
+                   norm=_lib.QKNORM_FULL_ROW, rope=_lib.ROPE_SPLIT if rope else _lib.ROPE_NONE,
+                   cos=cos.to(cuda_device) if rope else None,
+                   sin=sin.to(cuda_device) if rope else None, eps=v.eps)
+    got = xd.cpu()
+    assert _max_rel(got[..., d : 2 * d], expect) <= TOL
+    assert torch.equal(got[..., :d], x[..., :d]) and torch.equal(got[..., 2 * d :], x[..., 2 * d :])
+
+
+def test_attention_f32_gate_and_add_rows(cuda_device):
+    """The per-head output gate of the LTX attention (cross-attention shape: 90 queries, 33
+    context keys) and the modulation-table add."""
+    dev = cuda_device
+    batch, tq, tk, heads = 2, 90, 33, 3
+    q, k, v = _r((batch, tq, heads * 128), 66), _r((batch, tk, heads * 128), 67), _r((batch, tk, heads * 128), 68)
+    gate = 2.0 * torch.sigmoid(_r((batch, tq, heads), 69))
+    sh = lambda t: t.reshape(*t.shape[:2], heads, 128).transpose(1, 2)
+    att = rops.sdpa(sh(q), sh(k), sh(v), scale=128**-0.5).transpose(1, 2)
+    expect = (att * gate[..., None]).reshape(q.shape)
+    out = f.attention(q.to(dev), k.to(dev), v.to(dev), heads=heads, gate=gate.to(dev))
+    assert _max_rel(out, expect) <= TOL
+    table, row = _r((9, 520), 70), _r((520,), 71)
+    assert torch.equal(f.add_rows(table.to(dev), row.to(dev)).cpu(), table + row)
+
+
+def _ltx_positions(f_, h, w):
+    return lref.pixel_coords(lref.patch_grid_bounds(f_, h, w))
+
+
+def test_ltx_block_velocity_f32(cuda_device):
+    """One full-width LTX-2 video block (hidden 4096, 32 heads: the q/k norm spans 4096
+    channels) with gated self- and cross-attention, in fp32: velocity within 1e-4 of the oracle."""
+    v = lcfg.BASELINE_VIDEO.with_blocks(1)
+    w = ltx_weights(v, seed=80, dtype=F32)
+    grid = (2, 4, 6)
+    latent = _r((1, grid[0] * grid[1] * grid[2], v.in_channels), 81)
+    context = _r((1, 40, v.context_dim), 82)
+    pos = _ltx_positions(*grid)
+    sigma = lref.DISTILLED_STAGE_1_SIGMAS[5]
+    expect = lref.forward(w, latent, context, sigma, pos, v, dtype=F32)
+    model = LTXVideoTransformerF32(w, v, cuda_device)
+    out = model.run(model.prepare(context, pos), latent.to(cuda_device), sigma).clone()
+    assert out.dtype == F32
+    assert _max_rel(out, expect) <= TOL, _max_rel(out, expect)
+    assert _cos(out, expect) >= 0.99999
+
+
+def test_ltx_denoise_f32(cuda_device):
+    """Two blocks at hidden 1024 / 8 heads over the last three distilled stage-1 steps with
+    X0 + Euler in the final projection, fp32 end to end, batch 2."""
+    v = lcfg.LTXVariant(dim=1024, heads=8, context_dim=1024, blocks=2)
+    w = ltx_weights(v, seed=83, dtype=F32)
+    grid = (2, 4, 4)
+    latent = _r((2, grid[0] * grid[1] * grid[2], v.in_channels), 84)
+    context = _r((2, 24, v.context_dim), 85)
+    pos = _ltx_positions(*grid)
+    sigmas = lref.DISTILLED_STAGE_1_SIGMAS[5:]
+    expect = lref.denoise(w, latent, context, pos, sigmas, v)
+    model = LTXVideoTransformerF32(w, v, cuda_device)
+    out = ldn.denoise_loop(model, latent, context, pos, sigmas)
     assert out.dtype == F32
     assert _max_rel(out, expect) <= TOL, _max_rel(out, expect)
     assert _cos(out, expect) >= 0.999
