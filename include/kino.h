@@ -30,7 +30,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (8); bumped on any signature change. */
+/* ABI version of this header (9); bumped on any signature change. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -498,6 +498,40 @@ kino_status kino_swiglu_f32(const float* x, int64_t ldx, int64_t bsx, float* out
 /* kino_timestep_embedding with fp32 features (kinomlx/models/flux2/transformer.py:238-241). */
 kino_status kino_timestep_embedding_f32(const float* t, float* out, int64_t batch, int64_t dim,
                                         void* stream);
+
+/* Video VAE decode in fp32 (same layouts as the bf16 entry points, float* tensors). */
+
+/* kino_conv3d in fp32: x (frames, height, width, in_channels) channels-last, weight (out_channels,
+ * 3, 3, 3, in_channels) OTHWI, bias (out_channels) or NULL, residual (geometry of out, no
+ * depth-to-space) or NULL; out (F, H, W, N), or with strides (st, sh, sw) in {1, 2}
+ * (F*st - (st > 1), H*sh, W*sw, N/(st*sh*sw)) with the weight rows sub-position-major.
+ * in_channels % 16 == 0. out = conv + bias, then + residual. Replaces Conv3dBlock and the
+ * depth-to-space upsample (kinomlx/models/ltx2/video_vae/blocks.py:97-139, decoder.py:80-121). */
+kino_status kino_conv3d_f32(const float* x, int64_t frames, int64_t height, int64_t width,
+                            int64_t in_channels, const float* weight, int64_t out_channels,
+                            const float* bias, const float* residual, float* out, int causal,
+                            int stride_t, int stride_h, int stride_w, void* stream);
+
+/* Stepwise PixelNorm (+ SiLU) in fp32, channels % 4 == 0 (kinomlx/kernels/fused_ops.py:460-476). */
+kino_status kino_pixel_norm_f32(const float* x, float* out, int64_t voxels, int64_t channels,
+                                float eps, int apply_silu, void* stream);
+
+/* Affine GroupNorm(32) (+ SiLU) in fp32 with two-pass statistics; needs no workspace
+ * (kinomlx/kernels/fused_ops.py:375-409). */
+kino_status kino_group_norm_f32(const float* x, const float* weight, const float* bias, float* out,
+                                int64_t voxels, int64_t channels, float eps, int apply_silu,
+                                void* stream);
+
+/* kino_latent_to_bfhwc in fp32 (kinomlx/models/ltx2/video_vae/decoder.py:227-233). */
+kino_status kino_latent_to_bfhwc_f32(const float* latent, const float* std_of_means,
+                                     const float* mean_of_means, float* out, int64_t channels,
+                                     int64_t voxels, void* stream);
+
+/* kino_tile_blend with an fp32 decoded tile (kinomlx/models/ltx2/video_vae/tiling.py:1310-1330). */
+kino_status kino_tile_blend_f32(const float* decoded, int64_t frames, int64_t height, int64_t width,
+                                int64_t channels, int64_t patch, float* canvas, float* weights,
+                                int64_t out_height, int64_t out_width, int64_t y0, int64_t x0,
+                                const float* mask_h, const float* mask_w, void* stream);
 
 /* ------------------------------------------------------------------ peer memory (NVLink)
  * Buffers that the other GPUs of a sequence-parallel group map (CUDA IPC) and write into: the

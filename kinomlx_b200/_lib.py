@@ -238,6 +238,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_euler_velocity_f32": (c_int, [P, P, F, P, I64, P]),
     "kino_swiglu_f32": (c_int, [P, I64, I64, P, I64, I64, I64, I64, I64, P]),
     "kino_timestep_embedding_f32": (c_int, [P, P, I64, I64, P]),
+    "kino_conv3d_f32": (
+        c_int,
+        [P, I64, I64, I64, I64, P, I64, P, P, P, c_int, c_int, c_int, c_int, P],
+    ),
+    "kino_pixel_norm_f32": (c_int, [P, P, I64, I64, F, c_int, P]),
+    "kino_group_norm_f32": (c_int, [P, P, P, P, I64, I64, F, c_int, P]),
+    "kino_latent_to_bfhwc_f32": (c_int, [P, P, P, P, I64, I64, P]),
+    "kino_tile_blend_f32": (c_int, [P, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, P, P, P]),
     "kino_peer_alloc": (c_int, [I64, POINTER(c_void_p), POINTER(IpcHandle)]),
     "kino_peer_free": (c_int, [P]),
     "kino_peer_open": (c_int, [POINTER(IpcHandle), POINTER(c_void_p)]),

@@ -458,7 +458,7 @@ void* group_norm_scratch_address(kino_status* status) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 8; }
+int kino_abi_version(void) { return 9; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -1271,7 +1271,7 @@ kino_status kino_tile_blend(const void* decoded, int64_t frames, int64_t height,
   int64_t blocks = nrows;
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) return KINO_OK;
-  launch_pdl(kino::tile_blend_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+  launch_pdl(kino::tile_blend_kernel<__nv_bfloat16>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(decoded), static_cast<int>(frames),
       static_cast<int>(height), static_cast<int>(width), static_cast<int>(channels),
       static_cast<int>(patch), canvas, weights, static_cast<int>(out_height),
@@ -1560,6 +1560,110 @@ kino_status kino_timestep_embedding_f32(const float* t, float* out, int64_t batc
   launch_pdl(kino::timestep_embedding_f32_kernel, dim3(static_cast<unsigned>(batch)), dim3(128),
              0, static_cast<cudaStream_t>(stream), t, out, static_cast<int>(dim));
   return check_launch("kino_timestep_embedding_f32");
+}
+
+// ---------------------------------------------------------------- video VAE, fp32 parity mode
+kino_status kino_conv3d_f32(const float* x, int64_t frames, int64_t height, int64_t width,
+                            int64_t in_channels, const float* weight, int64_t out_channels,
+                            const float* bias, const float* residual, float* out, int causal,
+                            int stride_t, int stride_h, int stride_w, void* stream) {
+  if (x == nullptr || weight == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_conv3d_f32: null operand");
+  if (frames < 1 || height < 1 || width < 1 || in_channels < 1 || out_channels < 1)
+    return fail(KINO_EINVAL, "kino_conv3d_f32: empty shape");
+  if (in_channels % 16 || !aligned16(x) || !aligned16(weight))
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d_f32: in_channels %% 16 == 0, aligned operands");
+  if (stride_t < 1 || stride_t > 2 || stride_h < 1 || stride_h > 2 || stride_w < 1 || stride_w > 2)
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d_f32: depth-to-space strides of 1 or 2");
+  const int64_t sub = static_cast<int64_t>(stride_t) * stride_h * stride_w;
+  if (out_channels % sub) return fail(KINO_EINVAL, "kino_conv3d_f32: channels do not split into the stride");
+  if (sub > 1 && residual != nullptr)
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d_f32: no residual with depth-to-space");
+  const int64_t voxels = frames * height * width;
+  if (voxels > 0x7fffffffLL || in_channels * 27 > 0x7fffffffLL || out_channels > 65535 * 128 ||
+      (voxels + kino::F32_BM - 1) / kino::F32_BM > 65535)
+    return fail(KINO_ENOTSUPPORTED, "kino_conv3d_f32: shape too large");
+  kino::Conv32Shape shape;
+  shape.F = static_cast<int>(frames);
+  shape.H = static_cast<int>(height);
+  shape.W = static_cast<int>(width);
+  shape.Cin = static_cast<int>(in_channels);
+  shape.N = static_cast<int>(out_channels);
+  shape.causal = causal ? 1 : 0;
+  shape.st = stride_t;
+  shape.sh = stride_h;
+  shape.sw = stride_w;
+  const dim3 grid(static_cast<unsigned>((out_channels + kino::F32_BN - 1) / kino::F32_BN),
+                  static_cast<unsigned>((voxels + kino::F32_BM - 1) / kino::F32_BM));
+  launch_pdl(kino::conv3d_f32_kernel, grid, dim3(kino::F32_THREADS), 0,
+             static_cast<cudaStream_t>(stream), x, weight, bias, residual, out, shape);
+  return check_launch("kino_conv3d_f32");
+}
+
+kino_status kino_pixel_norm_f32(const float* x, float* out, int64_t voxels, int64_t channels,
+                                float eps, int apply_silu, void* stream) {
+  if (x == nullptr || out == nullptr) return fail(KINO_EINVAL, "kino_pixel_norm_f32: null");
+  if (channels % 4 || channels < 4 || channels > 0x7fffffffLL || voxels < 1 || !aligned16(x) ||
+      !aligned16(out))
+    return fail(KINO_ENOTSUPPORTED, "kino_pixel_norm_f32: channels %% 4 == 0, aligned operands");
+  const int64_t blocks = (voxels * 32 + 255) / 256;
+  if (blocks > 0x7fffffffLL) return fail(KINO_ENOTSUPPORTED, "kino_pixel_norm_f32: too many voxels");
+  launch_pdl(kino::pixel_norm_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), x, out, voxels, static_cast<int>(channels), eps,
+             apply_silu);
+  return check_launch("kino_pixel_norm_f32");
+}
+
+kino_status kino_group_norm_f32(const float* x, const float* weight, const float* bias, float* out,
+                                int64_t voxels, int64_t channels, float eps, int apply_silu,
+                                void* stream) {
+  if (x == nullptr || weight == nullptr || bias == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_group_norm_f32: null operand");
+  if (channels % 32 || channels < 32 || channels > 0x7fffffffLL || voxels < 1)
+    return fail(KINO_ENOTSUPPORTED, "kino_group_norm_f32: channels must split into 32 groups");
+  launch_pdl(kino::group_norm_f32_kernel, dim3(32), dim3(kino::GN32_THREADS), 0,
+             static_cast<cudaStream_t>(stream), x, weight, bias, out, voxels,
+             static_cast<int>(channels), eps, apply_silu);
+  return check_launch("kino_group_norm_f32");
+}
+
+kino_status kino_latent_to_bfhwc_f32(const float* latent, const float* std_of_means,
+                                     const float* mean_of_means, float* out, int64_t channels,
+                                     int64_t voxels, void* stream) {
+  if (latent == nullptr || std_of_means == nullptr || mean_of_means == nullptr || out == nullptr)
+    return fail(KINO_EINVAL, "kino_latent_to_bfhwc_f32: null");
+  if (channels < 1 || channels > 0x7fffffffLL || voxels < 1)
+    return fail(KINO_EINVAL, "kino_latent_to_bfhwc_f32: shape");
+  int64_t blocks = (channels * voxels + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  launch_pdl(kino::latent_to_bfhwc_f32_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), latent, std_of_means, mean_of_means, out,
+             static_cast<int>(channels), voxels);
+  return check_launch("kino_latent_to_bfhwc_f32");
+}
+
+kino_status kino_tile_blend_f32(const float* decoded, int64_t frames, int64_t height, int64_t width,
+                                int64_t channels, int64_t patch, float* canvas, float* weights,
+                                int64_t out_height, int64_t out_width, int64_t y0, int64_t x0,
+                                const float* mask_h, const float* mask_w, void* stream) {
+  if (decoded == nullptr || canvas == nullptr || weights == nullptr || mask_h == nullptr ||
+      mask_w == nullptr)
+    return fail(KINO_EINVAL, "kino_tile_blend_f32: null");
+  if (y0 < 0 || x0 < 0 || y0 + height * patch > out_height || x0 + width * patch > out_width)
+    return fail(KINO_EINVAL, "kino_tile_blend_f32: tile outside the canvas");
+  const int64_t nrows = channels * frames * height * patch;
+  if (nrows > 0x7fffffffLL || width * patch > 0x7fffffffLL || channels * patch * patch > 0x7fffffffLL)
+    return fail(KINO_ENOTSUPPORTED, "kino_tile_blend_f32: tile too large");
+  int64_t blocks = nrows;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) return KINO_OK;
+  launch_pdl(kino::tile_blend_kernel<float>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+             static_cast<cudaStream_t>(stream), decoded, static_cast<int>(frames),
+             static_cast<int>(height), static_cast<int>(width), static_cast<int>(channels),
+             static_cast<int>(patch), canvas, weights, static_cast<int>(out_height),
+             static_cast<int>(out_width), static_cast<int>(y0), static_cast<int>(x0), mask_h,
+             mask_w);
+  return check_launch("kino_tile_blend_f32");
 }
 
 }  // extern "C"

@@ -614,4 +614,230 @@ __global__ void timestep_embedding_f32_kernel(const float* __restrict__ t, float
   }
 }
 
+// ---------------------------------------------------------------- video VAE (fp32)
+// 3x3x3 convolution as an implicit GEMM on the CUDA cores: M = voxels of the un-shuffled output
+// (F x H x W), N = output channels, K = 27 taps x Cin with the A rows gathered from the shifted
+// input voxels under the reference's padding: temporal replicate (causal: two copies of the first
+// frame in front; otherwise one at each end), spatial zero (kinomlx/models/ltx2/video_vae/
+// blocks.py:97-139). 128 x 128 tiles and 8 x 8 outputs per thread as in gemm_f32_kernel; Cin % 16
+// == 0 keeps every 16-wide k slice inside one tap. Epilogue: + bias, then + residual (separate
+// roundings, as the reference adds them); with a depth-to-space stride the weight rows are
+// sub-position-major (n = sub * C' + c) and each value is stored at its shuffled position, the
+// first output frame dropped when the temporal stride is 2 (decoder.py:80-121).
+struct Conv32Shape {
+  int F, H, W, Cin, N;
+  int causal;
+  int st, sh, sw;
+};
+
+__global__ void __launch_bounds__(F32_THREADS, 2)
+    conv3d_f32_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                      const float* __restrict__ bias, const float* residual, float* out,
+                      Conv32Shape s) {
+  __shared__ __align__(16) float As[2][F32_BK][F32_BM + F32_PAD];
+  __shared__ __align__(16) float Ws[2][F32_BK][F32_BN + F32_PAD];
+  griddep_wait();
+  griddep_launch();
+  const int tid = threadIdx.x;
+  const int M = s.F * s.H * s.W;
+  const int K = 27 * s.Cin;
+  const int row0 = blockIdx.y * F32_BM;
+  const int col0 = blockIdx.x * F32_BN;
+  const int lr = tid >> 2;
+  const int lk = (tid & 3) * 4;
+  int vf[2], vh[2], vw[2];
+  bool vok[2];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int m = row0 + lr + 64 * p;
+    vok[p] = m < M;
+    const int mm = vok[p] ? m : 0;
+    vw[p] = mm % s.W;
+    vh[p] = (mm / s.W) % s.H;
+    vf[p] = mm / (s.W * s.H);
+  }
+  float4 ra[2], rw[2];
+  auto load = [&](int k0) {
+    const int tap = k0 / s.Cin;
+    const int ci = k0 - tap * s.Cin + lk;
+    const int kt = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      int sf = s.causal ? vf[p] + kt - 2 : vf[p] + kt - 1;
+      sf = sf < 0 ? 0 : (sf > s.F - 1 ? s.F - 1 : sf);
+      const int shh = vh[p] + kh - 1, sww = vw[p] + kw - 1;
+      const bool in = vok[p] && shh >= 0 && shh < s.H && sww >= 0 && sww < s.W;
+      ra[p] = in ? *reinterpret_cast<const float4*>(
+                       x + ((static_cast<int64_t>(sf) * s.H + shh) * s.W + sww) * s.Cin + ci)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int c = col0 + lr + 64 * p;
+      rw[p] = c < s.N ? *reinterpret_cast<const float4*>(w + static_cast<int64_t>(c) * K + k0 + lk)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int r = lr + 64 * p;
+      As[buf][lk + 0][r] = ra[p].x;
+      As[buf][lk + 1][r] = ra[p].y;
+      As[buf][lk + 2][r] = ra[p].z;
+      As[buf][lk + 3][r] = ra[p].w;
+      Ws[buf][lk + 0][r] = rw[p].x;
+      Ws[buf][lk + 1][r] = rw[p].y;
+      Ws[buf][lk + 2][r] = rw[p].z;
+      Ws[buf][lk + 3][r] = rw[p].w;
+    }
+  };
+  const int ty = tid >> 4;
+  const int tx = tid & 15;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const int ktiles = K / F32_BK;
+  load(0);
+  store(0);
+  __syncthreads();
+  for (int t = 0; t < ktiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ktiles) load((t + 1) * F32_BK);
+#pragma unroll
+    for (int kk = 0; kk < F32_BK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Ws[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Ws[buf][kk][64 + tx * 4]);
+      const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], bv[j], acc[i][j]);
+    }
+    if (t + 1 < ktiles) store(buf ^ 1);
+    __syncthreads();
+  }
+  const int sub = s.st * s.sh * s.sw;
+  const int Cp = s.N / sub;
+  const int Ho = s.H * s.sh, Wo = s.W * s.sw;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = row0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (m >= M) continue;
+    const int ow0 = m % s.W, oh0 = (m / s.W) % s.H, of0 = m / (s.W * s.H);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = col0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + j - 4);
+      if (c >= s.N) continue;
+      float v = acc[i][j];
+      if (bias != nullptr) v = __fadd_rn(v, bias[c]);
+      if (sub == 1) {
+        const int64_t o = static_cast<int64_t>(m) * s.N + c;
+        if (residual != nullptr) v = __fadd_rn(v, residual[o]);
+        out[o] = v;
+      } else {
+        const int sp = c / Cp, cc = c - sp * Cp;
+        const int dt = sp / (s.sh * s.sw), dh = (sp / s.sw) % s.sh, dw = sp % s.sw;
+        const int of = of0 * s.st + dt - (s.st > 1 ? 1 : 0);
+        if (of < 0) continue;
+        out[((static_cast<int64_t>(of) * Ho + oh0 * s.sh + dh) * Wo + ow0 * s.sw + dw) * Cp + cc] = v;
+      }
+    }
+  }
+}
+
+// Stepwise PixelNorm in fp32 (square, mean, + eps, sqrt, divide: kinomlx/kernels/fused_ops.py:
+// 460-476), then optionally SiLU; one warp per voxel, channels % 4 == 0.
+__global__ void pixel_norm_f32_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                      int64_t voxels, int C, float eps, int apply_silu) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t voxel = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (voxel >= voxels) return;
+  const int lane = threadIdx.x & 31;
+  const float* row = x + voxel * C;
+  float sq = 0.f;
+  for (int c = lane * 4; c < C; c += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(row + c);
+    sq += __fmul_rn(v.x, v.x) + __fmul_rn(v.y, v.y) + __fmul_rn(v.z, v.z) + __fmul_rn(v.w, v.w);
+  }
+  sq = warp_sum_f(sq);
+  const float rms = sqrtf(__fadd_rn(__fdiv_rn(sq, static_cast<float>(C)), eps));
+  float* orow = out + voxel * C;
+  for (int c = lane * 4; c < C; c += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(row + c);
+    float y[4] = {__fdiv_rn(v.x, rms), __fdiv_rn(v.y, rms), __fdiv_rn(v.z, rms), __fdiv_rn(v.w, rms)};
+    if (apply_silu) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) y[k] = silu_exact_f32(y[k]);
+    }
+    *reinterpret_cast<float4*>(orow + c) = make_float4(y[0], y[1], y[2], y[3]);
+  }
+}
+
+// Affine GroupNorm(32) in fp32 with two-pass statistics (kinomlx/kernels/fused_ops.py:47-139,
+// 375-409), then optionally SiLU. One CTA of 1024 threads per group walks all the group's
+// elements three times (sum, squared deviations, apply); fixed-order tree reductions, so the
+// result does not depend on scheduling.
+constexpr int GN32_THREADS = 1024;
+
+__device__ __forceinline__ float block_sum_1024(float v, float* red) {
+  v = warp_sum_f(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = threadIdx.x < 32 ? red[threadIdx.x] : 0.f;
+  if (threadIdx.x < 32) t = warp_sum_f(t);
+  if (threadIdx.x == 0) red[32] = t;
+  __syncthreads();
+  const float r = red[32];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(GN32_THREADS)
+    group_norm_f32_kernel(const float* __restrict__ x, const float* __restrict__ weight,
+                          const float* __restrict__ bias, float* __restrict__ out, int64_t voxels,
+                          int C, float eps, int apply_silu) {
+  __shared__ float red[33];
+  griddep_wait();
+  griddep_launch();
+  const int g = blockIdx.x;
+  const int gc = C / 32;
+  const int64_t n = voxels * gc;
+  auto addr = [&](int64_t e) { return (e / gc) * C + g * gc + (e % gc); };
+  float s = 0.f;
+  for (int64_t e = threadIdx.x; e < n; e += GN32_THREADS) s += x[addr(e)];
+  const float mean = __fdiv_rn(block_sum_1024(s, red), static_cast<float>(n));
+  float q = 0.f;
+  for (int64_t e = threadIdx.x; e < n; e += GN32_THREADS) {
+    const float d = __fsub_rn(x[addr(e)], mean);
+    q += __fmul_rn(d, d);
+  }
+  const float rstd = rsqrtf(__fadd_rn(__fdiv_rn(block_sum_1024(q, red), static_cast<float>(n)), eps));
+  for (int64_t e = threadIdx.x; e < n; e += GN32_THREADS) {
+    const int64_t a = addr(e);
+    const int c = g * gc + static_cast<int>(e % gc);
+    float y = __fmul_rn(__fsub_rn(x[a], mean), rstd);
+    y = __fadd_rn(__fmul_rn(y, weight[c]), bias[c]);
+    out[a] = apply_silu ? silu_exact_f32(y) : y;
+  }
+}
+
+// latent (channels, voxels) -> channels-last latent * std + mean (decoder.py:227-233), fp32.
+__global__ void latent_to_bfhwc_f32_kernel(const float* __restrict__ lat, const float* __restrict__ sd,
+                                           const float* __restrict__ mu, float* __restrict__ out,
+                                           int C, int64_t voxels) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t n = voxels * C;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % C);
+    const int64_t v = i / C;
+    out[i] = __fadd_rn(__fmul_rn(lat[static_cast<int64_t>(c) * voxels + v], sd[c]), mu[c]);
+  }
+}
+
 }  // namespace kino

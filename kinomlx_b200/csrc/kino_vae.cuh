@@ -328,7 +328,12 @@ __global__ void latent_to_bfhwc_kernel(const __nv_bfloat16* __restrict__ latent,
 // c * p^2 + pw * p + ph, blocks.py:200-230), widen to fp32 and accumulate decoded * mask into the
 // fp32 BCFHW canvas at the tile's pixel offset; the first call for a tile position also adds the
 // mask to the weight canvas (tiling.py:1310-1330).
-__global__ void tile_blend_kernel(const __nv_bfloat16* __restrict__ dec, int Ft, int ht, int wt,
+__device__ __forceinline__ float tile_value(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float tile_value(float v) { return v; }
+
+// T: the decoded tile's element type (bf16, or fp32 in the fp32 parity mode).
+template <typename T>
+__global__ void tile_blend_kernel(const T* __restrict__ dec, int Ft, int ht, int wt,
                                   int channels, int patch, float* __restrict__ canvas,
                                   float* __restrict__ wcanvas, int Hout, int Wout, int y0, int x0,
                                   const float* __restrict__ mask_h, const float* __restrict__ mask_w) {
@@ -355,7 +360,7 @@ __global__ void tile_blend_kernel(const __nv_bfloat16* __restrict__ dec, int Ft,
       const int w = xx / patch, pw = xx - (xx / patch) * patch;
       const float m = mh * mask_w[xx];
       const float val =
-          __bfloat162float(dec[src_row + static_cast<int64_t>(w) * packed + pw * patch]) * m;
+          tile_value(dec[src_row + static_cast<int64_t>(w) * packed + pw * patch]) * m;
       canvas[dst_row + xx] += val;
       if (first_plane) wcanvas[static_cast<int64_t>(y0 + yy) * Wout + x0 + xx] += m;
     }

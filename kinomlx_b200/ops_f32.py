@@ -24,12 +24,17 @@ __all__ = [
     "add_rows",
     "attention",
     "cfg_combine",
+    "conv3d",
     "euler_velocity",
     "gelu_tanh",
+    "group_norm",
+    "latent_to_bfhwc",
     "linear",
+    "pixel_norm",
     "qk_norm_rope",
     "silu",
     "swiglu",
+    "tile_blend",
     "timestep_embedding",
 ]
 
@@ -283,3 +288,101 @@ def timestep_embedding(t: torch.Tensor, dim: int = 256, *,
     with _timed("elementwise_f32"):
         _lib.call("kino_timestep_embedding_f32", _ptr(t), _ptr(out), t.shape[0], dim, _stream())
     return out
+
+
+# ----------------------------------------------------------------------------- video VAE
+def conv3d(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *,
+           causal: bool, stride: tuple[int, int, int] = (1, 1, 1),
+           residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 3x3x3 conv of channels-last x (F, H, W, Cin) with an (N, 3, 3, 3, Cin) weight; with a
+    depth-to-space `stride` the weight rows must be sub-position-major (n = sub * C' + c)."""
+    _need(x, "x", F32)
+    _need(weight, "weight", F32)
+    if not x.is_contiguous() or not weight.is_contiguous():
+        raise ValueError("conv3d needs contiguous channels-last input and OTHWI weight")
+    x4 = x[0] if x.dim() == 5 else x
+    f_, h, w, cin = x4.shape
+    n = weight.shape[0]
+    if tuple(weight.shape[1:]) != (3, 3, 3, cin):
+        raise ValueError(f"weight {tuple(weight.shape)} does not match {cin} input channels")
+    st, sh, sw = stride
+    sub = st * sh * sw
+    oshape = (f_ * st - (1 if st > 1 else 0), h * sh, w * sw, n // sub)
+    if out is None:
+        out = torch.empty(oshape, device=x.device, dtype=F32)
+    if tuple(out.shape) != oshape or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous {oshape}")
+    if bias is not None:
+        _need(bias, "bias", F32)
+    if residual is not None:
+        _need(residual, "residual", F32)
+        if tuple(residual.shape[-4:]) != oshape or not residual.is_contiguous():
+            raise ValueError("residual must be contiguous with the geometry of out")
+    with _timed("conv3d_f32", 2.0 * f_ * h * w * n * 27 * cin,
+                4.0 * (x4.numel() + weight.numel() + out.numel())):
+        _lib.call("kino_conv3d_f32", _ptr(x4), f_, h, w, cin, _ptr(weight), n, _ptr(bias),
+                  _ptr(residual), _ptr(out), int(causal), st, sh, sw, _stream())
+    return out
+
+
+def pixel_norm(x: torch.Tensor, eps: float = 1e-8, *, silu: bool = False,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Stepwise fp32 PixelNorm over the last (channel) axis, optionally followed by SiLU."""
+    _need(x, "x", F32)
+    if not x.is_contiguous():
+        raise ValueError("pixel_norm needs a contiguous channels-last input")
+    if out is None:
+        out = torch.empty_like(x)
+    c = x.shape[-1]
+    with _timed("norm_f32", 0.0, 8.0 * x.numel()):
+        _lib.call("kino_pixel_norm_f32", _ptr(x), _ptr(out), x.numel() // c, c, eps, int(silu),
+                  _stream())
+    return out
+
+
+def group_norm(x: torch.Tensor, groups: int, weight: torch.Tensor, bias: torch.Tensor,
+               eps: float, *, silu: bool = False, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Affine GroupNorm(32) over channels-last fp32 x with two-pass statistics (+ SiLU)."""
+    if groups != 32:
+        raise ValueError("the GroupNorm kernel takes 32 groups")
+    _need(x, "x", F32)
+    _need(weight, "weight", F32)
+    _need(bias, "bias", F32)
+    if not x.is_contiguous():
+        raise ValueError("group_norm needs a contiguous channels-last input")
+    if out is None:
+        out = torch.empty_like(x)
+    c = x.shape[-1]
+    with _timed("norm_f32", 0.0, 16.0 * x.numel()):
+        _lib.call("kino_group_norm_f32", _ptr(x), _ptr(weight), _ptr(bias), _ptr(out),
+                  x.numel() // c, c, eps, int(silu), _stream())
+    return out
+
+
+def latent_to_bfhwc(latent: torch.Tensor, std: torch.Tensor, mean: torch.Tensor) -> torch.Tensor:
+    """(1, C, F, H, W) fp32 latent -> (F, H, W, C) of latent * std + mean."""
+    _need(latent, "latent", F32)
+    if latent.dim() != 5 or latent.shape[0] != 1 or not latent.is_contiguous():
+        raise ValueError("latent must be a contiguous (1, C, F, H, W) tensor")
+    _, c, f_, h, w = latent.shape
+    std, mean = std.float().contiguous(), mean.float().contiguous()
+    out = torch.empty((f_, h, w, c), device=latent.device, dtype=F32)
+    with _timed("elementwise_f32", 0.0, 8.0 * latent.numel()):
+        _lib.call("kino_latent_to_bfhwc_f32", _ptr(latent), _ptr(std), _ptr(mean), _ptr(out), c,
+                  f_ * h * w, _stream())
+    return out
+
+
+def tile_blend(decoded: torch.Tensor, canvas: torch.Tensor, weights: torch.Tensor, y0: int,
+               x0: int, mask_h: torch.Tensor, mask_w: torch.Tensor, patch: int = 4) -> None:
+    """Accumulate an fp32 decoded tile (F, h, w, C * patch^2) into the fp32 (1, C, F, H, W) canvas."""
+    _need(decoded, "decoded", F32)
+    if not decoded.is_contiguous():
+        raise ValueError("the decoded tile must be contiguous")
+    f_, h, w, packed = decoded.shape
+    c = packed // (patch * patch)
+    mask_h, mask_w = mask_h.float().contiguous(), mask_w.float().contiguous()
+    with _timed("elementwise_f32", 0.0, 12.0 * decoded.numel()):
+        _lib.call("kino_tile_blend_f32", _ptr(decoded), f_, h, w, c, patch, _ptr(canvas),
+                  _ptr(weights), canvas.shape[-2], canvas.shape[-1], y0, x0, _ptr(mask_h),
+                  _ptr(mask_w), _stream())

@@ -14,6 +14,7 @@ import torch
 from oracle import flux2 as ref
 from oracle import fused_ops as rops
 from oracle import ltx2 as lref
+from oracle import video_vae as vref
 from kinomlx_b200 import _lib
 from kinomlx_b200 import ops_f32 as f
 from kinomlx_b200.flux2 import config as fcfg
@@ -23,8 +24,10 @@ from kinomlx_b200.flux2.transformer_f32 import Flux2TransformerF32
 from kinomlx_b200.ltx2 import config as lcfg
 from kinomlx_b200.ltx2 import denoise as ldn
 from kinomlx_b200.ltx2.transformer import precompute_freqs_cis
+from kinomlx_b200.ltx2 import video_vae as vae
 from kinomlx_b200.ltx2.transformer_f32 import LTXVideoTransformerF32
-from kinomlx_b200.synthetic import flux_weights, ltx_weights, normal
+from kinomlx_b200.ltx2.video_vae_f32 import VideoDecoderF32
+from kinomlx_b200.synthetic import flux_weights, ltx_weights, make_weights, normal
 
 pytestmark = pytest.mark.gpu
 F32 = torch.float32
@@ -335,6 +338,90 @@ def test_ltx_denoise_f32(cuda_device):
     assert out.dtype == F32
     assert _max_rel(out, expect) <= TOL, _max_rel(out, expect)
     assert _cos(out, expect) >= 0.999
+
+
+@pytest.mark.parametrize(
+    ("f_", "h", "w", "cin", "n", "causal", "stride", "residual"),
+    [
+        (5, 9, 11, 64, 64, False, (1, 1, 1), False),
+        (5, 9, 11, 64, 64, True, (1, 1, 1), True),
+        (2, 5, 7, 16, 40, True, (1, 1, 1), True),
+        (3, 16, 16, 128, 48, True, (1, 1, 1), False),
+        (4, 6, 10, 128, 256, True, (2, 2, 2), False),
+        (3, 20, 36, 64, 128, False, (1, 2, 2), False),
+        (3, 12, 8, 64, 64, False, (2, 1, 1), False),
+    ],
+)
+def test_conv3d_f32(cuda_device, f_, h, w, cin, n, causal, stride, residual):
+    """3x3x3 conv with the reference's temporal replicate / spatial zero padding, bias, residual
+    and depth-to-space upsampling, fp32 (kinomlx/models/ltx2/video_vae/blocks.py:97-139,
+    decoder.py:80-121)."""
+    dev = cuda_device
+    x = _r((1, f_, h, w, cin), 90)
+    wt = _r((n, 3, 3, 3, cin), 91, 0.05)
+    b = _r((n,), 92, 0.1)
+    sub = stride[0] * stride[1] * stride[2]
+    if sub == 1:
+        exp = vref.conv3d(x, wt, b, causal)
+        res = _r(exp.shape, 93) if residual else None
+        if res is not None:
+            exp = exp + res
+        out = f.conv3d(x.to(dev), wt.to(dev), b.to(dev), causal=causal,
+                       residual=None if res is None else res[0].to(dev))
+    else:
+        cout = n // sub
+        exp = vref.upsample({"u.conv.weight": wt, "u.conv.bias": b}, "u", x, stride, cin // cout,
+                            vref.VaeVariant(causal=causal))
+        wd = wt.reshape(cout, sub, 3, 3, 3, cin).transpose(0, 1).reshape(wt.shape).contiguous()
+        bd = b.reshape(cout, sub).transpose(0, 1).reshape(-1).contiguous()
+        out = f.conv3d(x.to(dev), wd.to(dev), bd.to(dev), causal=causal, stride=stride)
+    exp = exp[0]
+    assert tuple(out.shape) == tuple(exp.shape)
+    assert _max_rel(out, exp) <= TOL, _max_rel(out, exp)
+
+
+@pytest.mark.parametrize("channels", [128, 96, 256])
+def test_vae_norms_f32(cuda_device, channels):
+    """Stepwise PixelNorm + SiLU and affine GroupNorm(32) + SiLU in fp32
+    (kinomlx/kernels/fused_ops.py:375-409, 460-476)."""
+    dev = cuda_device
+    x = _r((1, 5, 7, 9, channels), 94, 2.0)
+    exp = rops.silu(rops.pixel_norm(x, dim=-1, eps=1e-8))
+    assert _max_rel(f.pixel_norm(x.to(dev), 1e-8, silu=True), exp) <= TOL
+    if channels % 32 == 0:
+        wt, bs = 1 + _r((channels,), 95, 0.3), _r((channels,), 96, 0.1)
+        x1 = x.reshape(1, 5, 63, channels)
+        exp = rops.silu(rops.group_norm(x1, 32, wt, bs, 1e-6))
+        got = f.group_norm(x1.to(dev), 32, wt.to(dev), bs.to(dev), 1e-6, silu=True)
+        assert _max_rel(got, exp) <= TOL
+
+
+VAE_MINI = (("res", 1), ("d2s", (2, 2, 2), 2), ("res", 1), ("d2s", (1, 2, 2), 1), ("res", 1))
+
+
+@pytest.mark.parametrize("norm,causal", [("pixel", False), ("group32", True)])
+def test_vae_decoder_f32(cuda_device, norm, causal):
+    """A miniature decoder (top width 256, both depth-to-space kinds, residual blocks) in fp32,
+    the whole video within 1e-4 of the oracle's fp32 decode."""
+    v = vae.VaeVariant(norm=norm, causal=causal, top_width=256, blocks=VAE_MINI)
+    rv = vref.VaeVariant(norm=norm, causal=causal, top_width=256, blocks=VAE_MINI)
+    w = make_weights(vae.vae_weight_specs(v), seed=97, dtype=F32)
+    latent = _r((1, 128, 3, 4, 6), 98)
+    exp = vref.decode(w, latent, rv, dtype=F32)
+    out = VideoDecoderF32(w, v, cuda_device).decode(latent.to(cuda_device), tile=None)
+    assert tuple(out.shape) == tuple(exp.shape)
+    assert _max_rel(out, exp) <= TOL, _max_rel(out, exp)
+
+
+def test_vae_tiled_decode_f32(cuda_device):
+    """The spatial tiler with trapezoid blending in fp32 (tiling.py:1053-1386)."""
+    v = vae.VaeVariant(norm="group32", causal=True, top_width=256, blocks=VAE_MINI)
+    rv = vref.VaeVariant(norm="group32", causal=True, top_width=256, blocks=VAE_MINI)
+    w = make_weights(vae.vae_weight_specs(v), seed=99, dtype=F32)
+    latent = _r((1, 128, 2, 7, 10), 100)
+    exp = vref.decode_tiled(w, latent, rv, tile=4, overlap=1, scale=16, dtype=F32)
+    out = VideoDecoderF32(w, v, cuda_device).decode(latent.to(cuda_device), tile=4, overlap=1)
+    assert _max_rel(out, exp) <= TOL, _max_rel(out, exp)
 
 
 def test_f32_refusals(cuda_device):
