@@ -142,7 +142,7 @@ kino_status kino_gemv(const void* x, int64_t ldx, const void* w, const void* bia
 typedef struct kino_attention_args {
   int64_t batch;
   int64_t heads;
-  int64_t head_dim;        /* 128 */
+  int64_t head_dim;        /* 64 or 128 */
   float scale;             /* softmax scale, head_dim^-0.5 in the reference */
   int n_q;                 /* 1 or 2 query segments (logically concatenated) */
   const void* q[2];
@@ -180,7 +180,8 @@ kino_status kino_attention(const kino_attention_args* args, void* stream);
 
 /* The reference dense kernel's contract: q (tq, heads*dim), k and v (tk, heads*dim), out like q.
  * Replaces kinomlx.models.ltx2.kernels.dense_attention.dense_attention
- * (kinomlx/models/ltx2/kernels/dense_attention.py:107-151); dim must be 128 here. */
+ * (kinomlx/models/ltx2/kernels/dense_attention.py:107-151); dim 64 or 128, as the reference's
+ * kernel takes (dense_attention.py:87-104). */
 kino_status kino_dense_attention(const void* q, const void* k, const void* v, void* out,
                                  int64_t tq, int64_t tk, int64_t heads, int64_t dim, void* stream);
 

@@ -1,11 +1,12 @@
-// Dense attention on tcgen05 for 128-wide heads, bf16 in and out, fp32 softmax/accumulation.
+// Dense attention on tcgen05 for 128- or 64-wide heads (template D), bf16 in and out, fp32
+// softmax/accumulation.
 //
 // Restates the math of the reference's attention calls: softmax(q k^T * d^-1/2) v per head
 // (kinomlx/models/flux2/kv.py:48-54 joint attention through MLX SDPA,
 //  kinomlx/models/ltx2/kernels/dense_attention.py:107-151 token-major dense attention,
 //  kinomlx/models/ltx2/transformer/attention.py:144-161 unmasked SDPA, 364-368 head gates).
 //
-// Layout: q, k and v are token-major, (batch, tokens, heads * 128) with any row stride, which is
+// Layout: q, k and v are token-major, (batch, tokens, heads * D) with any row stride, which is
 // what the projections write. Queries and keys may each come in two segments (text tokens, then
 // image tokens) that are concatenated logically but never in memory: each 128-row query tile and
 // each 128-key block belongs to one segment.
@@ -22,7 +23,7 @@
 //               P as bf16 pairs back over the half's own scores. O is rescaled in tensor memory
 //               only when the running max grows by more than 2^8 (the stale max cancels in the
 //               final division).
-// Tensor memory (512 columns): S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512). P of
+// Tensor memory (512 columns): S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [384,384+D). P of
 // keys 0..63 sits in columns [0,32) and of keys 64..127 in [64,96) of its S. The PV product takes
 // P straight from tensor memory (the TMEM-A form of tcgen05.mma) and V in place from shared
 // memory as an MN-major operand. MMAs of one issuing thread run in order, so S(j+1) overwriting
@@ -35,7 +36,7 @@ namespace kino {
 
 constexpr int ATT_BM = 128;  // queries per tile
 constexpr int ATT_BN = 128;  // keys per block
-constexpr int ATT_D = 128;   // head dim
+constexpr int ATT_D = 128;   // widest head dim (the shared-memory layout holds 128)
 constexpr int ATT_STAGES = 2;  // K + V blocks in flight
 constexpr int ATT_THREADS = 320;
 // Key pairs i of a block whose bit (i % 8) is set take the FMA-pipe exponential
@@ -117,6 +118,7 @@ __device__ __forceinline__ QTile q_tile_of(const AttnParams& p, int global) {
   return t;
 }
 
+template <int D>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap mq0,
                         const __grid_constant__ CUtensorMap mq1,
@@ -125,6 +127,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                         const __grid_constant__ CUtensorMap mv0,
                         const __grid_constant__ CUtensorMap mv1, const AttnParams p) {
   using L = AttnSmem;
+  static_assert(D == 64 || D == 128, "heads are 64 or 128 wide");
+  constexpr int NH = D / 64;  // 64-wide halves of a head (one 128-byte swizzle row each)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -182,12 +186,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, (has_b ? 4 : 2) * L::HALF);
+      mbar_expect_tx(q_full, (has_b ? 2 : 1) * NH * L::HALF);
       for (int t = 0; t < ntile; ++t) {
         const CUtensorMap* mq = tiles[t].seg ? &mq1 : &mq0;
         uint8_t* sq = smem + L::Q_OFF + t * 2 * L::HALF;
         tma_load_4d(sq, mq, q_full, 0, tiles[t].tile * ATT_BM, head, batch);
-        tma_load_4d(sq + L::HALF, mq, q_full, 64, tiles[t].tile * ATT_BM, head, batch);
+        if (NH > 1) tma_load_4d(sq + L::HALF, mq, q_full, 64, tiles[t].tile * ATT_BM, head, batch);
       }
       int issued = 0;
       for (int j = 0; j < nblk; ++j) {
@@ -200,10 +204,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const CUtensorMap* mv = kseg ? &mv1 : &mv0;
         uint8_t* sk = smem + L::KV_OFF + stage * L::STAGE;
         uint8_t* sv = sk + 2 * L::HALF;
-        mbar_expect_tx(&kv_full[stage], 4 * L::HALF);
+        mbar_expect_tx(&kv_full[stage], 2 * NH * L::HALF);
         const int t0 = kb * ATT_BN;
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
+        for (int h2 = 0; h2 < NH; ++h2) {
           tma_load_4d(sk + h2 * L::HALF, mk, &kv_full[stage], h2 * 64, t0, head, batch);
           tma_load_4d(sv + h2 * L::HALF, mv, &kv_full[stage], h2 * 64, t0, head, batch);
         }
@@ -225,12 +229,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_bf16(ATT_BM, ATT_BN);
-      constexpr uint32_t idesc_o = idesc_bf16(ATT_BM, ATT_D) | (1u << 16);  // B (V) MN-major
+      constexpr uint32_t idesc_o = idesc_bf16(ATT_BM, D) | (1u << 16);  // B (V) MN-major
       auto s_mma = [&](int t, int j) {
         const uint32_t sq = smem_u32(smem + L::Q_OFF + t * 2 * L::HALF);
         const uint32_t sk = smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE);
 #pragma unroll
-        for (int kk = 0; kk < ATT_D / 16; ++kk) {
+        for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::HALF + (kk & 3) * 32;
           umma_bf16(tmem + t * 128, sdesc_k128(sq + off), sdesc_k128(sk + off), idesc_s,
                     kk > 0 ? 1u : 0u);
@@ -384,9 +388,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
         l_run[t] += ls.x + ls.y;
         if (rescale) {
-          const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * 64;
+          const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * (D / 2);
 #pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             uint32_t o[32];
             tmem_ld32(o_col + c * 32, o);
             tmem_wait_ld();
@@ -423,7 +427,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           const int owner = tok / p.rows_per_rank;
           const int64_t lt = tok - static_cast<int64_t>(owner) * p.rows_per_rank;
           dst = (store ? p.out_peers[owner] : p.out_peers[0]) + lt * p.ld_out[0] +
-                p.out_col_offset + head * ATT_D;
+                p.out_col_offset + head * D;
           if (p.gate_peers != nullptr) {
             gp = p.gate_peers[0];
             if (store)
@@ -432,7 +436,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           }
         } else {
           dst = p.out[qt.seg] + static_cast<int64_t>(batch) * p.bs_out[qt.seg] +
-                static_cast<int64_t>(tok) * p.ld_out[qt.seg] + head * ATT_D;
+                static_cast<int64_t>(tok) * p.ld_out[qt.seg] + head * D;
           if (gp != nullptr && store)
             gv = __bfloat162float(gp[static_cast<int64_t>(batch) * p.bs_gate[qt.seg] +
                                      static_cast<int64_t>(tok) * p.ld_gate[qt.seg] + head]);
@@ -441,9 +445,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           const float o = __uint_as_float(raw) * inv_l;
           return gp != nullptr ? bf16_round(bf16_round(o) * gv) : o;
         };
-        const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * 64;
+        const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * (D / 2);
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           uint32_t o[32];
           tmem_ld32(o_col + c * 32, o);
           tmem_wait_ld();
@@ -455,7 +459,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
               w.y = pack_bf16x2(fin(o[g * 8 + 2]), fin(o[g * 8 + 3]));
               w.z = pack_bf16x2(fin(o[g * 8 + 4]), fin(o[g * 8 + 5]));
               w.w = pack_bf16x2(fin(o[g * 8 + 6]), fin(o[g * 8 + 7]));
-              *reinterpret_cast<uint4*>(dst + half * 64 + c * 32 + g * 8) = w;
+              *reinterpret_cast<uint4*>(dst + half * (D / 2) + c * 32 + g * 8) = w;
             }
           }
         }

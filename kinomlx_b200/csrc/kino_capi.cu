@@ -645,9 +645,10 @@ kino_status kino_gemv(const void* x, int64_t ldx, const void* w, const void* bia
 
 kino_status kino_attention(const kino_attention_args* a, void* stream) {
   if (a == nullptr) return fail(KINO_EINVAL, "kino_attention: null args");
-  if (a->head_dim != 128)
-    return fail(KINO_ENOTSUPPORTED, "kino_attention: head_dim %lld (only 128)",
+  if (a->head_dim != 128 && a->head_dim != 64)
+    return fail(KINO_ENOTSUPPORTED, "kino_attention: head_dim %lld (64 or 128)",
                 (long long)a->head_dim);
+  const uint64_t hd = static_cast<uint64_t>(a->head_dim);
   if (a->n_q < 1 || a->n_q > 2 || a->n_kv < 1 || a->n_kv > 2)
     return fail(KINO_EINVAL, "kino_attention: 1 or 2 segments");
   if (a->batch < 1 || a->heads < 1 || a->batch > 65535 || a->heads > 65535)
@@ -669,9 +670,9 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
       return fail(KINO_EINVAL, "kino_attention: empty query segment");
     if (a->ld_q[qs] % 8 || a->ld_out[qs] % 8 || (a->batch > 1 && (a->bs_q[qs] % 8)))
       return fail(KINO_ENOTSUPPORTED, "kino_attention: strides must be multiples of 8");
-    const uint64_t dq[4] = {128, static_cast<uint64_t>(a->q_tokens[qs]),
+    const uint64_t dq[4] = {hd, static_cast<uint64_t>(a->q_tokens[qs]),
                             static_cast<uint64_t>(a->heads), static_cast<uint64_t>(a->batch)};
-    const uint64_t sq[3] = {static_cast<uint64_t>(a->ld_q[qs]), 128,
+    const uint64_t sq[3] = {static_cast<uint64_t>(a->ld_q[qs]), hd,
                             static_cast<uint64_t>(a->batch > 1 ? a->bs_q[qs] : 8)};
     kino_status st = make_map(&mq[s], a->q[qs], 4, dq, sq, box);
     if (st != KINO_OK) return st;
@@ -693,11 +694,11 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
     if (a->ld_k[ks] % 8 || a->ld_v[ks] % 8 ||
         (a->batch > 1 && (a->bs_k[ks] % 8 || a->bs_v[ks] % 8)))
       return fail(KINO_ENOTSUPPORTED, "kino_attention: strides must be multiples of 8");
-    const uint64_t dk[4] = {128, static_cast<uint64_t>(a->kv_tokens[ks]),
+    const uint64_t dk[4] = {hd, static_cast<uint64_t>(a->kv_tokens[ks]),
                             static_cast<uint64_t>(a->heads), static_cast<uint64_t>(a->batch)};
-    const uint64_t sk[3] = {static_cast<uint64_t>(a->ld_k[ks]), 128,
+    const uint64_t sk[3] = {static_cast<uint64_t>(a->ld_k[ks]), hd,
                             static_cast<uint64_t>(a->batch > 1 ? a->bs_k[ks] : 8)};
-    const uint64_t sv[3] = {static_cast<uint64_t>(a->ld_v[ks]), 128,
+    const uint64_t sv[3] = {static_cast<uint64_t>(a->ld_v[ks]), hd,
                             static_cast<uint64_t>(a->batch > 1 ? a->bs_v[ks] : 8)};
     st = make_map(&mk[s], a->k[ks], 4, dk, sk, kvbox);
     if (st != KINO_OK) return st;
@@ -713,7 +714,7 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
       return fail(KINO_EINVAL, "kino_attention: peer return needs batch 1, one query segment");
     if (a->world < 1 || a->world > kino::PEER_MAX_WORLD || a->rows_per_rank < 1 ||
         a->rows_per_rank * a->world < a->q_tokens[0] || a->out_col_offset < 0 ||
-        a->out_col_offset % 8 || a->out_col_offset + a->heads * 128 > a->out_cols ||
+        a->out_col_offset % 8 || a->out_col_offset + a->heads * a->head_dim > a->out_cols ||
         a->out_cols > a->ld_out[0])
       return fail(KINO_EINVAL, "kino_attention: peer return rows/columns outside the buffers");
     if (a->gate_peers != nullptr &&
@@ -727,18 +728,23 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
     p.ld_out[0] = a->ld_out[0];
     p.ld_gate[0] = a->ld_gate[0];
   }
-  kino_status st = ensure_smem(kino::attention_tc_kernel, kino::AttnSmem::TOTAL, 3);
-  if (st != KINO_OK) return st;
   dim3 grid((tiles + 1) / 2, p.heads, p.batch);  // two 128-query tiles per CTA
-  launch_pdl(kino::attention_tc_kernel, dim3(grid), dim3(kino::ATT_THREADS), kino::AttnSmem::TOTAL, static_cast<cudaStream_t>(stream), mq[0], mq[1], mk[0], mk[1],
-                                                                   mv[0], mv[1], p);
-  return check_launch("kino_attention");
+  auto run = [&](auto kernel, int slot) {
+    kino_status st = ensure_smem(kernel, kino::AttnSmem::TOTAL, slot);
+    if (st != KINO_OK) return st;
+    launch_pdl(kernel, dim3(grid), dim3(kino::ATT_THREADS), kino::AttnSmem::TOTAL,
+               static_cast<cudaStream_t>(stream), mq[0], mq[1], mk[0], mk[1], mv[0], mv[1], p);
+    return check_launch("kino_attention");
+  };
+  return a->head_dim == 64 ? run(kino::attention_tc_kernel<64>, 11)
+                           : run(kino::attention_tc_kernel<128>, 3);
 }
 
 kino_status kino_dense_attention(const void* q, const void* k, const void* v, void* out,
                                  int64_t tq, int64_t tk, int64_t heads, int64_t dim,
                                  void* stream) {
-  if (dim != 128) return fail(KINO_ENOTSUPPORTED, "kino_dense_attention: dim %lld", (long long)dim);
+  if (dim != 128 && dim != 64)
+    return fail(KINO_ENOTSUPPORTED, "kino_dense_attention: dim %lld (64 or 128)", (long long)dim);
   kino_attention_args a;
   std::memset(&a, 0, sizeof(a));
   a.batch = 1;

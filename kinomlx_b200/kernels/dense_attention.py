@@ -2,7 +2,8 @@
 (kinomlx/models/ltx2/kernels/dense_attention.py:87-151) on the tcgen05 attention kernel.
 
 bf16 in and out with fp32 softmax and accumulation (no fp16 saturation: the reference converts
-only because the M1 lacks bf16 arithmetic). Heads are 128 wide on this build.
+only because the M1 lacks bf16 arithmetic). Heads are 64 or 128 wide, as the reference's kernel
+takes (dense_attention.py:87-104).
 """
 
 from __future__ import annotations
@@ -11,7 +12,7 @@ import torch
 
 from .. import ops
 
-HEAD_DIMS = (128,)
+HEAD_DIMS = (64, 128)
 _SUPPORTED = (torch.bfloat16,)
 
 
@@ -38,7 +39,7 @@ def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, heads:
     dim = width // heads if heads > 0 and width % heads == 0 else 0
     if dim not in HEAD_DIMS or k.dim() != 2 or k.shape[1] != width or v.shape != k.shape or q.shape[0] == 0 or k.shape[0] == 0:
         raise ValueError(
-            f"dense attention needs (query_tokens, {heads} * 128) queries and matching "
+            f"dense attention needs (query_tokens, {heads} * 64 or 128) queries and matching "
             f"(key_tokens, width) keys and values, got {tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}"
         )
     out = torch.empty_like(q)

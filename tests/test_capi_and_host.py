@@ -44,10 +44,12 @@ def test_ops_refuse_cpu_tensors():
 def test_reference_surface_refusals():
     from kinomlx_b200.kernels import dense_attention, mpp_linear, split_rope
 
-    q = torch.zeros((5, 2 * 64), dtype=torch.bfloat16)
+    q = torch.zeros((5, 2 * 96), dtype=torch.bfloat16)
     with pytest.raises(ValueError):
-        dense_attention.dense_attention(q, q, q, heads=2)  # 64-wide heads are not built
+        dense_attention.dense_attention(q, q, q, heads=2)  # heads are 64 or 128 wide
     assert not dense_attention.applies(q[None], q[None], heads=2)
+    q64 = torch.zeros((1, 5, 2 * 64), dtype=torch.bfloat16)
+    assert not dense_attention.applies(q64, q64, heads=2)  # the CPU tensor is what refuses here
     v = torch.zeros((2, 5, 32), dtype=torch.bfloat16)
     cos = torch.zeros((1, 2, 5, 8))
     assert not split_rope.applies(v, cos.half(), cos.half())

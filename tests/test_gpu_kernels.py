@@ -169,6 +169,43 @@ def test_attention_two_segments_equal_concatenation(cuda_device):
     assert _rel_l2(torch.cat([out_t, out_i], dim=1), ref) < 6e-3
 
 
+@pytest.mark.parametrize(
+    ("batch", "tq", "tk", "heads"),
+    [(1, 7, 7, 2), (2, 300, 517, 3), (1, 517, 33, 2), (1, 1, 300, 4), (1, 1024, 126, 32)],
+)
+def test_attention_head_dim_64_matches_fp32_sdpa(cuda_device, batch, tq, tk, heads):
+    """64-wide heads (the reference's audio stream and its audio/video cross-attention, 32 x 64),
+    ragged query and key counts, batch 2."""
+    from kinomlx_b200 import ops
+
+    q = _randn((batch, tq, heads * 64), 31)
+    k = _randn((batch, tk, heads * 64), 32)
+    v = _randn((batch, tk, heads * 64), 33)
+    out = torch.empty_like(q).to(cuda_device)
+    ops.attention([q.to(cuda_device)], [k.to(cuda_device)], [v.to(cuda_device)], [out], heads=heads)
+    torch.cuda.synchronize()
+    assert _rel_l2(out, _sdpa_ref(q, k, v, heads)) < 6e-3
+
+
+def test_dense_attention_surface_head_dim_64(cuda_device):
+    """The reference dense-attention contract with dim 64: q (Tq, H*64), k and v (Tk, H*64)
+    (kinomlx/models/ltx2/kernels/dense_attention.py:87-151), two key segments equal to one."""
+    from kinomlx_b200 import ops
+    from kinomlx_b200.kernels import dense_attention
+
+    heads, tq, tk = 32, 300, 126
+    q, k, v = _randn((tq, heads * 64), 34), _randn((tk, heads * 64), 35), _randn((tk, heads * 64), 36)
+    dev = cuda_device
+    assert dense_attention.applies(q[None].to(dev), k[None].to(dev), heads=heads)
+    out = dense_attention.dense_attention(q.to(dev), k.to(dev), v.to(dev), heads=heads)
+    ref = _sdpa_ref(q[None], k[None], v[None], heads)[0]
+    assert _rel_l2(out, ref) < 6e-3
+    split = torch.empty((1, tq, heads * 64), dtype=BF, device=dev)
+    ops.attention([q[None].to(dev)], [k[None, :50].to(dev), k[None, 50:].to(dev)],
+                  [v[None, :50].to(dev), v[None, 50:].to(dev)], [split], heads=heads)
+    assert _rel_l2(split[0], ref) < 6e-3
+
+
 def test_attention_full_size_flux(cuda_device):
     from kinomlx_b200 import ops
 
