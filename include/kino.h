@@ -210,6 +210,9 @@ kino_status kino_rms_norm(const void* x, const void* weight, void* out, int64_t 
 #define KINO_ROPE_NONE 0
 #define KINO_ROPE_PAIRS 1   /* adjacent pairs, tables [table_batch][table_tokens][128] */
 #define KINO_ROPE_SPLIT 2   /* split halves, tables [table_batch][heads][table_tokens][64] */
+#define KINO_ROPE_SPLIT64 3 /* split halves within 64-wide heads (two per 128 columns; heads still
+                               counts 128-column groups), tables
+                               [table_batch][2 * heads][table_tokens][32]; full-row norm only */
 
 /* In place on token-major q or k (batch x tokens x heads*128, ld, bs): RMSNorm (per head or over
  * the whole row) with weight, rounded to bf16, then RoPE from fp32 tables. Token t reads table

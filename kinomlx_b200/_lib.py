@@ -44,6 +44,7 @@ QKNORM_FULL_ROW = 2
 ROPE_NONE = 0
 ROPE_PAIRS = 1
 ROPE_SPLIT = 2
+ROPE_SPLIT64 = 3
 
 
 class Epilogue(ctypes.Structure):

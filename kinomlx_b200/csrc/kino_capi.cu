@@ -823,8 +823,10 @@ kino_status kino_qk_norm_rope(void* x, int64_t ld, int64_t bs, int64_t batch, in
                               int64_t table_tokens, int64_t table_offset, float eps,
                               void* stream) {
   if (x == nullptr) return fail(KINO_EINVAL, "kino_qk_norm_rope: null");
-  if (norm_kind < 0 || norm_kind > 2 || rope_kind < 0 || rope_kind > 2)
+  if (norm_kind < 0 || norm_kind > 2 || rope_kind < 0 || rope_kind > 3)
     return fail(KINO_EINVAL, "kino_qk_norm_rope: bad kind");
+  if (rope_kind == 3 && norm_kind == 1)
+    return fail(KINO_ENOTSUPPORTED, "kino_qk_norm_rope: 64-wide heads take the full-row norm");
   if (norm_kind != 0 && (weight == nullptr || !aligned16(weight)))
     return fail(KINO_EINVAL, "kino_qk_norm_rope: norm needs an aligned weight");
   if (rope_kind != 0 && (cos_table == nullptr || sin_table == nullptr))

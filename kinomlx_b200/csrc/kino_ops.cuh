@@ -267,7 +267,10 @@ __global__ void __launch_bounds__(ADALN_THREADS)
 //   rope_kind 0: none; 1: adjacent pairs, fp32 tables (tokens, 128) with repeated entries
 //                (kinomlx/models/flux2/transformer.py:17-29);
 //             2: split halves, fp32 tables (table_batch, heads, tokens, 64)
-//                (kinomlx/kernels/split_rope.py:35-56).
+//                (kinomlx/kernels/split_rope.py:35-56);
+//             3: split halves within 64-wide heads (two per 128 columns), tables
+//                (table_batch, 2 * heads, tokens, 32) (the LTX audio stream and the
+//                audio/video cross-attention, kinomlx/models/ltx2/transformer/attention.py:343-346).
 // The normalised value is rounded to bf16 before the rotation, as the reference's separate
 // norm and rotate operations are. One CTA per token, 8 threads per head, 16 values per thread.
 __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, int64_t bs,
@@ -291,6 +294,9 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, i
   if (rope_kind == 2) {
     e0 = h * 128 + u * 8;
     e1 = e0 + 64;
+  } else if (rope_kind == 3) {
+    e0 = h * 128 + (u >> 2) * 64 + (u & 3) * 8;
+    e1 = e0 + 32;
   } else {
     e0 = h * 128 + u * 16;
     e1 = e0 + 8;
@@ -349,12 +355,16 @@ __global__ void qk_norm_rope_kernel(__nv_bfloat16* __restrict__ x, int64_t ld, i
       a[j] = ra[j];
       c[j] = rc[j];
     }
-  } else if (rope_kind == 2) {
-    // split halves: first = a (i), second = c (i + 64), table entry (b|0, h, t, i)
+  } else if (rope_kind == 2 || rope_kind == 3) {
+    // split halves: first = a (i), second = c (i + half), table entry (b|0, head, t, i); with
+    // 64-wide heads (kind 3) the 128 columns hold heads 2h and 2h + 1, half 32
     const int tt = table_offset + t;
     const int64_t base =
-        ((static_cast<int64_t>(table_batched ? b : 0) * heads + h) * table_tokens + tt) * 64 +
-        u * 8;
+        rope_kind == 2
+            ? ((static_cast<int64_t>(table_batched ? b : 0) * heads + h) * table_tokens + tt) * 64 +
+                  u * 8
+            : ((static_cast<int64_t>(table_batched ? b : 0) * 2 * heads + 2 * h + (u >> 2)) *
+                   table_tokens + tt) * 32 + (u & 3) * 8;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float cs = cos_t[base + j];

@@ -28,6 +28,7 @@ from ._lib import (
     ROPE_NONE,
     ROPE_PAIRS,
     ROPE_SPLIT,
+    ROPE_SPLIT64,
 )
 
 __all__ = [
@@ -47,6 +48,7 @@ __all__ = [
     "ROPE_NONE",
     "ROPE_PAIRS",
     "ROPE_SPLIT",
+    "ROPE_SPLIT64",
     "adaln",
     "add_rows",
     "attention",
@@ -560,8 +562,9 @@ def qk_norm_rope(
     scatter: Scatter | None = None,
 ) -> torch.Tensor:
     """In place: RMSNorm (per head or full row) then RoPE on x (batch, tokens, heads*128).
-    With `scatter` (batch 1, one segment), the result goes to the head owners' receive buffers
-    (slot scatter.slots[0]) instead."""
+    `heads` counts 128-column groups; ROPE_SPLIT64 rotates 64-wide heads (two per group) from
+    (1|batch, 2 * heads, tokens, 32) tables. With `scatter` (batch 1, one segment), the result
+    goes to the head owners' receive buffers (slot scatter.slots[0]) instead."""
     _need(x, "x")
     x3 = _as3d(x)
     batch, tokens, width = x3.shape

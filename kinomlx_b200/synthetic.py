@@ -91,6 +91,65 @@ def ltx_weight_specs(v, blocks: int | None = None):
     return specs
 
 
+def _adaln_single_specs(prefix: str, d: int, n: int):
+    return [(f"{prefix}.emb.timestep_embedder.linear_1.weight", (d, 256), "normal"),
+            (f"{prefix}.emb.timestep_embedder.linear_1.bias", (d,), "normal"),
+            (f"{prefix}.emb.timestep_embedder.linear_2.weight", (d, d), "normal"),
+            (f"{prefix}.emb.timestep_embedder.linear_2.bias", (d,), "normal"),
+            (f"{prefix}.linear.weight", (n * d, d), "normal"),
+            (f"{prefix}.linear.bias", (n * d,), "normal")]
+
+
+def _attention_specs(prefix: str, query_dim: int, context_dim: int, inner: int, heads: int):
+    specs = []
+    for name, src in (("to_q", query_dim), ("to_k", context_dim), ("to_v", context_dim)):
+        specs += [(f"{prefix}.{name}.weight", (inner, src), "normal"),
+                  (f"{prefix}.{name}.bias", (inner,), "normal")]
+    specs += [(f"{prefix}.to_out.weight", (query_dim, inner), "normal"),
+              (f"{prefix}.to_out.bias", (query_dim,), "normal"),
+              (f"{prefix}.to_gate_logits.weight", (heads, query_dim), "normal"),
+              (f"{prefix}.to_gate_logits.bias", (heads,), "normal"),
+              (f"{prefix}.q_norm.weight", (inner,), "ones"),
+              (f"{prefix}.k_norm.weight", (inner,), "ones")]
+    return specs
+
+
+def ltx_av_weight_specs(video, audio, blocks: int):
+    """(name, shape, kind) in draw order for the joint audio/video model: the video stream's specs,
+    then the audio stream, the four A/V AdaLN singles and, per block, the audio layers, the two
+    cross-modal attentions (on the audio stream's heads) and their modulation tables; names
+    follow the reference checkpoint (kinomlx/models/ltx2/transformer/model.py:205-236,
+    transformer.py:85-176)."""
+    dv, da = video.dim, audio.dim
+    specs = ltx_weight_specs(video, blocks)
+    specs += [("audio_patchify_proj.weight", (da, audio.in_channels), "normal"),
+              ("audio_patchify_proj.bias", (da,), "normal")]
+    specs += _adaln_single_specs("audio_adaln_single", da, 9)
+    specs += _adaln_single_specs("audio_prompt_adaln_single", da, 2)
+    specs += _adaln_single_specs("av_ca_video_scale_shift_adaln_single", dv, 4)
+    specs += _adaln_single_specs("av_ca_a2v_gate_adaln_single", dv, 1)
+    specs += _adaln_single_specs("av_ca_audio_scale_shift_adaln_single", da, 4)
+    specs += _adaln_single_specs("av_ca_v2a_gate_adaln_single", da, 1)
+    for i in range(blocks):
+        a = f"transformer_blocks.{i}"
+        specs += [(f"{a}.audio_scale_shift_table", (9, da), "normal"),
+                  (f"{a}.audio_prompt_scale_shift_table", (2, da), "normal")]
+        specs += _attention_specs(f"{a}.audio_attn1", da, da, da, audio.heads)
+        specs += _attention_specs(f"{a}.audio_attn2", da, audio.context_dim, da, audio.heads)
+        specs += [(f"{a}.audio_ff.project_in.proj.weight", (audio.ff_mult * da, da), "normal"),
+                  (f"{a}.audio_ff.project_in.proj.bias", (audio.ff_mult * da,), "normal"),
+                  (f"{a}.audio_ff.project_out.weight", (da, audio.ff_mult * da), "normal"),
+                  (f"{a}.audio_ff.project_out.bias", (da,), "normal")]
+        specs += _attention_specs(f"{a}.audio_to_video_attn", dv, da, da, audio.heads)
+        specs += _attention_specs(f"{a}.video_to_audio_attn", da, dv, da, audio.heads)
+        specs += [(f"{a}.scale_shift_table_a2v_ca_audio", (5, da), "normal"),
+                  (f"{a}.scale_shift_table_a2v_ca_video", (5, dv), "normal")]
+    specs += [("audio_scale_shift_table", (2, da), "normal"),
+              ("audio_proj_out.weight", (audio.out_channels, da), "normal"),
+              ("audio_proj_out.bias", (audio.out_channels,), "normal")]
+    return specs
+
+
 def ltx_weights(v, *, seed: int = 0, device="cpu", dtype=torch.bfloat16, blocks: int | None = None):
     return make_weights(ltx_weight_specs(v, blocks), seed=seed, device=device, dtype=dtype)
 

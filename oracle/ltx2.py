@@ -151,9 +151,10 @@ def adaln(value, scale, shift, eps):
 
 
 # ----------------------------------------------------------------------------- attention / FF
-def attention(p: dict, prefix: str, x: torch.Tensor, v: LTXVariant, *, context=None, pe=None):
-    """Gated attention with Q/K RMSNorm over all heads and split RoPE
-    (kinomlx/models/ltx2/transformer/attention.py:249-371)."""
+def attention(p: dict, prefix: str, x: torch.Tensor, v: LTXVariant, *, context=None, pe=None,
+              k_pe=None):
+    """Gated attention with Q/K RMSNorm over all heads and split RoPE; the keys take `k_pe` when
+    given (the A/V cross-attention), else `pe` (kinomlx/models/ltx2/transformer/attention.py:249-371)."""
     g = lambda name: p[f"{prefix}.{name}"]
     lin = _blin(v)
     gate = None
@@ -165,7 +166,7 @@ def attention(p: dict, prefix: str, x: torch.Tensor, v: LTXVariant, *, context=N
     k = rms_norm(lin(src, g("to_k.weight"), g("to_k.bias")), g("k_norm.weight"), v.eps)
     if pe is not None:
         q = apply_split_rotary_emb(q, *pe)
-        k = apply_split_rotary_emb(k, *pe)
+        k = apply_split_rotary_emb(k, *(pe if k_pe is None else k_pe))
     b, tq, _ = q.shape
     tk = k.shape[1]
     heads, d = v.heads, v.head_dim
@@ -245,3 +246,132 @@ def denoise(p, latent, context, positions, sigmas, v: LTXVariant):
         velocity = forward(p, x, context, s, positions, v, dtype=latent.dtype)
         x = euler_step(x, to_denoised(x, s, velocity), s, n)
     return x
+
+
+# ----------------------------------------------------------------------------- joint audio/video
+@dataclass(frozen=True)
+class LTXAVVariant:
+    """LTXAVModel's two streams (kinomlx/models/ltx2/transformer/model.py:137-236): the video
+    stream, the audio stream (64-wide heads, one position axis), and the A/V cross-attention,
+    which runs on the audio stream's heads (equal head counts are required, model.py:185-186)."""
+
+    video: LTXVariant
+    audio: LTXVariant
+    av_gate_scale: float = 1000.0
+
+
+# the reference's default audio stream (model.py:141-153): 32 heads x 64, context 2048, one axis
+AUDIO = LTXVariant(dim=2048, heads=32, head_dim=64, context_dim=2048, max_pos=(20,))
+
+
+def modulate(value: torch.Tensor, scale: torch.Tensor, shift: torch.Tensor) -> torch.Tensor:
+    """(value * (1 + scale) + shift) in the value's dtype (ltx2/transformer/transformer.py:33-34)."""
+    return (value * (1.0 + scale) + shift).to(value.dtype)
+
+
+def av_values(table: torch.Tensor, scale_shift: torch.Tensor, gate: torch.Tensor):
+    """_av_ada_values (transformer.py:188-199): table rows 0-3 plus the (B, 1, 4, D) scale/shift
+    timestep, row 4 plus the (B, 1, 1, D) gate timestep; returns scale_a2v, shift_a2v, scale_v2a,
+    shift_v2a, gate."""
+    ss = table[:4][None, None] + scale_shift
+    g = table[4:5][None, None] + gate
+    return ss[:, :, 0], ss[:, :, 1], ss[:, :, 2], ss[:, :, 3], g[:, :, 0]
+
+
+def _stream_self_and_text(p, a, prefix, x, context, timesteps, prompt_timestep, pe, v):
+    """The self-attention and text cross-attention of one stream (transformer.py:249-320)."""
+    table = p[f"{a}.{prefix}scale_shift_table"]
+    vals = table[None, None] + timesteps
+    attended = attention(p, f"{a}.{prefix}attn1", adaln(x, vals[:, :, 1], vals[:, :, 0], v.eps), v, pe=pe)
+    x = (x + attended * vals[:, :, 2]).to(x.dtype)
+    prompt = p[f"{a}.{prefix}prompt_scale_shift_table"][None, None] + prompt_timestep
+    query = adaln(x, vals[:, :, 7], vals[:, :, 6], v.eps)
+    ctx = modulate(context, prompt[:, :, 1], prompt[:, :, 0])
+    cross = attention(p, f"{a}.{prefix}attn2", query, v, context=ctx)
+    return (x + (cross * vals[:, :, 8]).to(x.dtype)).to(x.dtype)
+
+
+def _stream_ff(p, a, prefix, x, timesteps, v):
+    """The stream's feed-forward with its gated residual (transformer.py:373-413)."""
+    vals = p[f"{a}.{prefix}scale_shift_table"][None, None] + timesteps
+    ff = feed_forward(p, f"{a}.{prefix}ff", adaln(x, vals[:, :, 4], vals[:, :, 3], v.eps), _blin(v))
+    return (x + ff * vals[:, :, 5]).to(x.dtype)
+
+
+def av_block(p: dict, i: int, vx, ax, vctx, actx, vt, at, vprompt, aprompt, vpe, ape, vxpe,
+             axpe, vcss, vcg, acss, acg, v: LTXAVVariant):
+    """BasicAVTransformerBlock with both streams and both cross-modal attentions
+    (kinomlx/models/ltx2/transformer/transformer.py:225-413). vt/at: (B, 1, 9, D) modulations;
+    vprompt/aprompt: (B, 1, 2, D); vcss/acss: (B, 1, 4, D) cross scale/shift; vcg/acg:
+    (B, 1, 1, D) cross gates; pe tables (B|1, heads, T, half)."""
+    a = f"transformer_blocks.{i}"
+    V, A = v.video, v.audio
+    vx = _stream_self_and_text(p, a, "", vx, vctx, vt, vprompt, vpe, V)
+    ax = _stream_self_and_text(p, a, "audio_", ax, actx, at, aprompt, ape, A)
+    vbase, abase = vx, ax
+    vnorm = rms_norm(vbase, None, V.eps)
+    anorm = rms_norm(abase, None, A.eps)
+    a_sc_a2v, a_sh_a2v, a_sc_v2a, a_sh_v2a, g_v2a = av_values(
+        p[f"{a}.scale_shift_table_a2v_ca_audio"], acss, acg)
+    v_sc_a2v, v_sh_a2v, v_sc_v2a, v_sh_v2a, g_a2v = av_values(
+        p[f"{a}.scale_shift_table_a2v_ca_video"], vcss, vcg)
+    a2v = attention(p, f"{a}.audio_to_video_attn", modulate(vnorm, v_sc_a2v, v_sh_a2v), A,
+                    context=modulate(anorm, a_sc_a2v, a_sh_a2v), pe=vxpe, k_pe=axpe)
+    vx = (vbase + a2v * g_a2v).to(vbase.dtype)
+    v2a = attention(p, f"{a}.video_to_audio_attn", modulate(anorm, a_sc_v2a, a_sh_v2a), A,
+                    context=modulate(vnorm, v_sc_v2a, v_sh_v2a), pe=axpe, k_pe=vxpe)
+    ax = (abase + v2a * g_v2a).to(abase.dtype)
+    vx = _stream_ff(p, a, "", vx, vt, V)
+    ax = _stream_ff(p, a, "audio_", ax, at, A)
+    return vx, ax
+
+
+def av_forward(p: dict, vlat, alat, vctx, actx, sigma: float, vpos, apos, v: LTXAVVariant,
+               blocks: int, dtype=torch.bfloat16):
+    """LTXAVModel.__call__ with both modalities and a uniform timestep (model.py:595-635,
+    preprocessing.py:134-213): returns the (video, audio) velocities."""
+    V, A = v.video, v.audio
+    b = vlat.shape[0]
+    t = torch.full((b,), sigma, dtype=torch.float32)
+    ts = t * V.timestep_scale
+    vx = linear(vlat, p["patchify_proj.weight"], p["patchify_proj.bias"])
+    ax = linear(alat, p["audio_patchify_proj.weight"], p["audio_patchify_proj.bias"])
+    single = lambda name, scale, n, d: adaln_single(p, name, scale, dtype)[0].reshape(b, -1, n, d)
+    vmod, vemb = adaln_single(p, "adaln_single", ts, dtype)
+    amod, aemb = adaln_single(p, "audio_adaln_single", t * A.timestep_scale, dtype)
+    vt, at = vmod.reshape(b, -1, 9, V.dim), amod.reshape(b, -1, 9, A.dim)
+    vprompt = single("prompt_adaln_single", ts, 2, V.dim)
+    aprompt = single("audio_prompt_adaln_single", t * A.timestep_scale, 2, A.dim)
+    vcss = single("av_ca_video_scale_shift_adaln_single", ts, 4, V.dim)
+    acss = single("av_ca_audio_scale_shift_adaln_single", t * A.timestep_scale, 4, A.dim)
+    # each gate comes from the other modality's sigma (equal here) times av_gate_scale
+    vcg = single("av_ca_a2v_gate_adaln_single", t * v.av_gate_scale, 1, V.dim)
+    acg = single("av_ca_v2a_gate_adaln_single", t * v.av_gate_scale, 1, A.dim)
+    vpe = precompute_freqs_cis(vpos, dim=V.dim, theta=V.theta, max_pos=V.max_pos, heads=V.heads)
+    ape = precompute_freqs_cis(apos, dim=A.dim, theta=A.theta, max_pos=A.max_pos, heads=A.heads)
+    cross_max = (max(V.max_pos[0], A.max_pos[0]),)
+    vxpe = precompute_freqs_cis(vpos[:, 0:1], dim=A.dim, theta=V.theta, max_pos=cross_max, heads=V.heads)
+    axpe = precompute_freqs_cis(apos[:, 0:1], dim=A.dim, theta=A.theta, max_pos=cross_max, heads=A.heads)
+    for i in range(blocks):
+        vx, ax = av_block(p, i, vx, ax, vctx, actx, vt, at, vprompt, aprompt, vpe, ape, vxpe,
+                          axpe, vcss, vcg, acss, acg, v)
+
+    def out(x, table, emb, w, bias, eps):
+        """_output (model.py:577-593): (table + embedded timestep), LayerNorm, projection."""
+        mod = (table[None, None] + emb.reshape(b, -1, x.shape[-1])[:, :, None, :]).to(x.dtype)
+        h = (layer_norm(x, eps) * (1.0 + mod[:, :, 1]) + mod[:, :, 0]).to(x.dtype)
+        return linear(h, w, bias)
+
+    return (out(vx, p["scale_shift_table"], vemb, p["proj_out.weight"], p["proj_out.bias"], V.eps),
+            out(ax, p["audio_scale_shift_table"], aemb, p["audio_proj_out.weight"],
+                p["audio_proj_out.bias"], A.eps))
+
+
+def av_denoise(p, vlat, alat, vctx, actx, vpos, apos, sigmas, v: LTXAVVariant, blocks: int):
+    """The deterministic-Euler loop over both modalities (kinomlx/models/ltx2/denoise.py:159-365)."""
+    vx, ax = vlat, alat
+    for s, n in zip(sigmas[:-1], sigmas[1:]):
+        vv, av = av_forward(p, vx, ax, vctx, actx, s, vpos, apos, v, blocks, dtype=vlat.dtype)
+        vx = euler_step(vx, to_denoised(vx, s, vv), s, n)
+        ax = euler_step(ax, to_denoised(ax, s, av), s, n)
+    return vx, ax
