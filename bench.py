@@ -690,6 +690,9 @@ def run_kernel_case(case: str) -> None:
     elif case == "bandwidth":
         run_bandwidth_case(dev)
         return
+    elif case == "av_step":
+        run_av_step(dev)
+        return
     elif case == "f32":
         # fp32 parity mode at config 1: the image stream's FF up projection (1024 x 12288 x 3072,
         # GELU epilogue) and the joint attention over 1536 tokens x 24 heads
@@ -733,6 +736,44 @@ def run_kernel_case(case: str) -> None:
     torch.cuda.synchronize()
     ops.device_status()
     print(json.dumps({"kernel_case": case, "ok": True}))
+
+
+def run_av_step(dev: torch.device) -> None:
+    """The joint audio/video LTX-2.3 step (48 blocks, video 4096 wide with 32 x 128 heads, audio
+    2048 wide with 32 x 64 heads) at BASELINE config 4's video shape (16 x 18 x 32 = 9216 tokens,
+    256 text tokens) plus 126 audio tokens (5 s at 25 tokens/s) and 128 audio text tokens:
+    2 warm-up and 3 timed X0 + Euler steps, then one step with per-launch events."""
+    from kinomlx_b200.ltx2 import av_transformer as avm
+    from kinomlx_b200.ltx2 import config as lcfg
+    from kinomlx_b200.synthetic import ltx_av_weight_specs, make_weights, normal
+
+    video, audio = lcfg.BASELINE_VIDEO, avm.audio_variant(lcfg.BASELINE_VIDEO.blocks)
+    model = avm.LTXAVTransformer(
+        make_weights(ltx_av_weight_specs(video, audio, video.blocks), seed=0, device=dev),
+        video, audio, dev)
+    torch.cuda.empty_cache()
+    f, h, w = 16, 18, 32
+    fr, hr, wr = torch.meshgrid(torch.arange(f), torch.arange(h), torch.arange(w), indexing="ij")
+    starts = torch.stack([fr, hr, wr]).reshape(3, -1).float()
+    vpos = torch.stack([starts, starts + 1], -1)[None] * torch.tensor([8.0, 32.0, 32.0]).reshape(1, 3, 1, 1)
+    vpos[:, 0] = torch.clamp(vpos[:, 0] + 1 - 8, min=0) / 24.0
+    ta = 126
+    at = torch.arange(ta, dtype=torch.float32) * 0.04
+    apos = torch.stack([at, at + 0.04], -1)[None, None]
+    prep = model.prepare(normal((1, 256, video.dim), seed=2, device=dev),
+                         normal((1, 128, audio.dim), seed=3, device=dev), vpos, apos)
+    vlat = normal((1, f * h * w, video.in_channels), seed=1, device=dev)
+    alat = normal((1, ta, audio.in_channels), seed=4, device=dev)
+    step = lambda: model.run(prep, vlat, alat, 0.725, sigma_next=0.421875, video_out=vlat,
+                             audio_out=alat)
+    ms = _time(step, 2, 3, 1)
+    from kinomlx_b200 import ops
+
+    ops.device_status()
+    print(json.dumps({"kernel_case": "av_step", "ok": True, "ms_per_step": round(ms, 3),
+                      "video_tokens": f * h * w, "audio_tokens": ta,
+                      "video_only_step_tflop": round(ltx_step_flops() / 1e12, 1),
+                      "kernels": _kernel_shares(step)}))
 
 
 def run_bandwidth_case(dev: torch.device) -> None:
@@ -842,7 +883,7 @@ def main() -> None:
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
     ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow",
-                                              "bandwidth", "f32"],
+                                              "bandwidth", "f32", "av_step"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     args = ap.parse_args()
     if args.kernel_case:
