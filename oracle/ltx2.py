@@ -326,27 +326,42 @@ def av_block(p: dict, i: int, vx, ax, vctx, actx, vt, at, vprompt, aprompt, vpe,
     return vx, ax
 
 
+def av_modulations(p: dict, video_sigma: float, audio_sigma: float, b: int, v: LTXAVVariant,
+                   dtype=torch.bfloat16) -> dict:
+    """Every timestep-driven modulation of a joint step with uniform per-modality timesteps
+    (preprocessing.py:63-83, 134-213): each stream's AdaLN (9 rows) and prompt AdaLN (2 rows) from
+    its own sigma, its cross scale/shift (4 rows) from its own timesteps, and its cross gate (1 row)
+    from the OTHER modality's sigma times av_gate_scale; plus the embedded timesteps of the
+    outputs."""
+    V, A = v.video, v.audio
+    tv = torch.full((b,), video_sigma, dtype=torch.float32)
+    ta = torch.full((b,), audio_sigma, dtype=torch.float32)
+    single = lambda name, t, n, d: adaln_single(p, name, t, dtype)[0].reshape(b, -1, n, d)
+    vmod, vemb = adaln_single(p, "adaln_single", tv * V.timestep_scale, dtype)
+    amod, aemb = adaln_single(p, "audio_adaln_single", ta * A.timestep_scale, dtype)
+    return {
+        "vt": vmod.reshape(b, -1, 9, V.dim), "at": amod.reshape(b, -1, 9, A.dim),
+        "vemb": vemb, "aemb": aemb,
+        "vprompt": single("prompt_adaln_single", tv * V.timestep_scale, 2, V.dim),
+        "aprompt": single("audio_prompt_adaln_single", ta * A.timestep_scale, 2, A.dim),
+        "vcss": single("av_ca_video_scale_shift_adaln_single", tv * V.timestep_scale, 4, V.dim),
+        "acss": single("av_ca_audio_scale_shift_adaln_single", ta * A.timestep_scale, 4, A.dim),
+        "vcg": single("av_ca_a2v_gate_adaln_single", ta * v.av_gate_scale, 1, V.dim),
+        "acg": single("av_ca_v2a_gate_adaln_single", tv * v.av_gate_scale, 1, A.dim),
+    }
+
+
 def av_forward(p: dict, vlat, alat, vctx, actx, sigma: float, vpos, apos, v: LTXAVVariant,
                blocks: int, dtype=torch.bfloat16):
     """LTXAVModel.__call__ with both modalities and a uniform timestep (model.py:595-635,
     preprocessing.py:134-213): returns the (video, audio) velocities."""
     V, A = v.video, v.audio
     b = vlat.shape[0]
-    t = torch.full((b,), sigma, dtype=torch.float32)
-    ts = t * V.timestep_scale
     vx = linear(vlat, p["patchify_proj.weight"], p["patchify_proj.bias"])
     ax = linear(alat, p["audio_patchify_proj.weight"], p["audio_patchify_proj.bias"])
-    single = lambda name, scale, n, d: adaln_single(p, name, scale, dtype)[0].reshape(b, -1, n, d)
-    vmod, vemb = adaln_single(p, "adaln_single", ts, dtype)
-    amod, aemb = adaln_single(p, "audio_adaln_single", t * A.timestep_scale, dtype)
-    vt, at = vmod.reshape(b, -1, 9, V.dim), amod.reshape(b, -1, 9, A.dim)
-    vprompt = single("prompt_adaln_single", ts, 2, V.dim)
-    aprompt = single("audio_prompt_adaln_single", t * A.timestep_scale, 2, A.dim)
-    vcss = single("av_ca_video_scale_shift_adaln_single", ts, 4, V.dim)
-    acss = single("av_ca_audio_scale_shift_adaln_single", t * A.timestep_scale, 4, A.dim)
-    # each gate comes from the other modality's sigma (equal here) times av_gate_scale
-    vcg = single("av_ca_a2v_gate_adaln_single", t * v.av_gate_scale, 1, V.dim)
-    acg = single("av_ca_v2a_gate_adaln_single", t * v.av_gate_scale, 1, A.dim)
+    m = av_modulations(p, sigma, sigma, b, v, dtype)
+    vt, at, vprompt, aprompt = m["vt"], m["at"], m["vprompt"], m["aprompt"]
+    vcss, vcg, acss, acg, vemb, aemb = m["vcss"], m["vcg"], m["acss"], m["acg"], m["vemb"], m["aemb"]
     vpe = precompute_freqs_cis(vpos, dim=V.dim, theta=V.theta, max_pos=V.max_pos, heads=V.heads)
     ape = precompute_freqs_cis(apos, dim=A.dim, theta=A.theta, max_pos=A.max_pos, heads=A.heads)
     cross_max = (max(V.max_pos[0], A.max_pos[0]),)
