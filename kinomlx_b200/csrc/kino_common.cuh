@@ -1,7 +1,7 @@
 // Shared device helpers for the sm_100a kernels of kinomlx_b200.
 //
-// Everything here is a thin wrapper over documented PTX: mbarriers, TMA tensor copies
-// (cp.async.bulk.tensor, never with .multicast::cluster), tcgen05 tensor-memory allocation,
+// Everything here is a thin wrapper over documented PTX: mbarriers, TMA tensor copies (each CTA
+// loads its own tiles; no cross-CTA broadcast of loads), tcgen05 tensor-memory allocation,
 // MMA issue/commit and tensor-memory loads/stores. Waits are bounded: a wait that does not
 // complete within KINO_WAIT_NS nanoseconds records KINO_ETIMEOUT in a device flag that the
 // host reads through kino_device_status(), and the caller abandons its loop.
