@@ -216,7 +216,7 @@ class LTXAVTransformer:
 
     # ------------------------------------------------------------------ per step embeddings
     @staticmethod
-    def _single(p: dict, temb, h1, emb, out) -> None:
+    def _run_single(p: dict, temb, h1, emb, out) -> None:
         """AdaLayerNormSingle: linear(silu(emb)), emb = linear_2(silu(linear_1(features)))
         (timestep.py:31-85)."""
         ops.gemv(temb, p["l1w"], p["l1b"], out=h1)
@@ -231,11 +231,11 @@ class LTXAVTransformer:
         ops.timestep_embedding(wav.t, 256, out=wav.temb)
         ops.timestep_embedding(wav.tg, 256, out=wav.tgemb)
         for st, ws, css, cg in ((self.vs, wv, self.v_css, self.v_cg), (self.as_, wa, self.a_css, self.a_cg)):
-            self._single(st.adaln, wav.temb, ws.h1, ws.emb, ws.mod9)
-            self._single(st.prompt_adaln, wav.temb, ws.ph1, ws.pemb, ws.pmod)
-            self._single(css, wav.temb, ws.ph1, ws.pemb, ws.css)
+            self._run_single(st.adaln, wav.temb, ws.h1, ws.emb, ws.mod9)
+            self._run_single(st.prompt_adaln, wav.temb, ws.ph1, ws.pemb, ws.pmod)
+            self._run_single(css, wav.temb, ws.ph1, ws.pemb, ws.css)
             # each gate is driven by the other modality's sigma (equal in a joint step)
-            self._single(cg, wav.tgemb, ws.ph1, ws.pemb, ws.cg)
+            self._run_single(cg, wav.tgemb, ws.ph1, ws.pemb, ws.cg)
         for b in range(wv.x.shape[0]):
             for st, ws, t_ss, t_g in ((self.vs, wv, self.tv_ss, self.tv_g), (self.as_, wa, self.ta_ss, self.ta_g)):
                 ops.add_rows(st.tables, ws.mod9[b], out=ws.vals[b])
