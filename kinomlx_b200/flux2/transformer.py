@@ -12,6 +12,12 @@ Memory layout (one workspace per batch/token shape, allocated once):
                            contiguous (D + mlp_hidden)-wide operand of to_out
 Projections run on the tcgen05 GEMM with their epilogue fused (GELU, gated residual, Euler);
 QK RMSNorm + RoPE run in place on the projection output; attention reads token-major q/k/v.
+
+KV editing (kinomlx/models/flux2/kv.py, transformer.py:319-350): an extracting evaluation holds
+[text | reference | target] rows in `stream`; the reference rows take the modulations of
+timestep 0 (a second modulation vector, `mods_fixed`), their queries attend to reference keys
+only, and each layer's reference keys/values are kept in a ReferenceKV. A reusing evaluation
+holds [text | target] rows and attends to the kept rows as a second key segment.
 """
 
 from __future__ import annotations
@@ -23,6 +29,9 @@ import torch
 from .. import ops
 from ..sequence_parallel import SequenceParallel
 from .config import FluxVariant
+from .kv import ReferenceKV
+
+BF = torch.bfloat16
 
 
 def rotary_positions(ids: torch.Tensor, variant: FluxVariant) -> tuple[torch.Tensor, torch.Tensor]:
@@ -51,7 +60,7 @@ class _Workspace:
     def __init__(self, v: FluxVariant, batch: int, nt: int, ni: int, device: torch.device,
                  sp: SequenceParallel):
         n, d = nt + ni, v.dim
-        e = lambda *shape: torch.empty(shape, device=device, dtype=torch.bfloat16)
+        e = lambda *shape: torch.empty(shape, device=device, dtype=BF)
         self.batch, self.nt, self.ni = batch, nt, ni
         self.stream = e(batch, n, d)
         self.nrm = e(batch, n, d)
@@ -70,6 +79,7 @@ class _Workspace:
         self.emb1 = e(batch, d)
         self.emb = e(batch, d)
         self.mods = e(batch, 17 * d)
+        self.mods_fixed = e(batch, 17 * d)  # timestep-0 modulations of KV-extraction reference rows
         self.velocity = e(batch, ni, v.in_channels)
 
 
@@ -89,7 +99,7 @@ class Flux2Transformer:
         # SwiGLU up projections: gate/content rows interleaved for the fused epilogue
         self.act_kind = ops.EPI_SWIGLU if swiglu else ops.EPI_GELU
         mlp_rows = ops.swiglu_interleave if swiglu else (lambda t: t)
-        dev = lambda t: t.to(self.device, torch.bfloat16).contiguous()
+        dev = lambda t: t.to(self.device, BF).contiguous()
         w = weights
         d = variant.dim
         self.x_embedder = dev(w["x_embedder.weight"])
@@ -136,10 +146,18 @@ class Flux2Transformer:
         self.proj_out = dev(w["proj_out.weight"])
         self._ws: dict[tuple[int, int, int], _Workspace] = {}
 
+    @property
+    def dtype(self) -> torch.dtype:
+        return BF
+
+    @property
+    def layer_count(self) -> int:
+        return len(self.double) + len(self.single)
+
     # ------------------------------------------------------------------ preparation
     def prepare(self, text: torch.Tensor, ids: torch.Tensor) -> PreparedText:
         """Project the text once and build the RoPE tables for the joint [text, image] ids."""
-        text = text.to(self.device, torch.bfloat16)
+        text = text.to(self.device, BF)
         projected = ops.linear(text, self.context_embedder)
         cos, sin = rotary_positions(ids, self.v)
         if self.sp.size > 1:
@@ -151,6 +169,25 @@ class Flux2Transformer:
             cos, sin = cos[:, rows].contiguous(), sin[:, rows].contiguous()
         return PreparedText(projected, ops.RopeTables(cos.to(self.device), sin.to(self.device)))
 
+    def prepare_layouts(self, text: torch.Tensor, ids: tuple[torch.Tensor, ...]) -> tuple[PreparedText, ...]:
+        """The text projected once, with RoPE tables for each joint [text, image] id layout
+        (kinomlx/models/flux2/transformer.py:283-292): KV editing evaluates [text, reference,
+        target] rows first and [text, target] rows after that. One GPU."""
+        if self.sp.size > 1:
+            raise ValueError("several id layouts need the whole sequence on one GPU")
+        projected = ops.linear(text.to(self.device, BF), self.context_embedder)
+        out = []
+        for joint in ids:
+            cos, sin = rotary_positions(joint, self.v)
+            out.append(PreparedText(projected, ops.RopeTables(cos.to(self.device), sin.to(self.device))))
+        return tuple(out)
+
+    def new_reference_kv(self, reference_tokens: int, batch: int = 1) -> ReferenceKV:
+        """An empty reference K/V cache for one edit (kinomlx/models/flux2/transformer.py:279-282)."""
+        if self.sp.size > 1:
+            raise ValueError("reference K/V editing runs on one GPU")
+        return ReferenceKV(reference_tokens, self.layer_count, batch, self.v.dim, self.device, BF)
+
     def workspace(self, batch: int, nt: int, ni: int) -> _Workspace:
         key = (batch, nt, ni)
         if key not in self._ws:
@@ -158,9 +195,32 @@ class Flux2Transformer:
         return self._ws[key]
 
     # ------------------------------------------------------------------ blocks
-    def _double_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
+    def _attend(self, q, k, v, kv: ReferenceKV | None, layer: int) -> None:
+        """Self-attention written over q; a reusing KV edit adds the kept reference keys and
+        values as a second key segment (kinomlx/models/flux2/kv.py:69-75)."""
+        if kv is None:
+            self.sp.attention(q, k, v, q, heads=self.v.heads)
+            return
+        rk, rv = kv.tensors(layer)
+        ops.attention([q], [k, rk], [v, rv], [q], heads=self.v.heads)
+
+    def _attend_extracting(self, q, k, v, nt: int, kv: ReferenceKV, layer: int) -> None:
+        """[text | reference | target] rows: keep the reference keys/values, then text and
+        target queries attend to every key and reference queries to the reference keys only
+        (kinomlx/models/flux2/kv.py:76-80). Outputs are written over q."""
+        h = self.v.heads
+        r0, r1 = nt, nt + kv.reference_tokens
+        kv.keep(layer, k[:, r0:r1], v[:, r0:r1])
+        ops.attention([q[:, :r0], q[:, r1:]], [k], [v], [q[:, :r0], q[:, r1:]], heads=h)
+        ops.attention([q[:, r0:r1]], [k[:, r0:r1]], [v[:, r0:r1]], [q[:, r0:r1]], heads=h)
+
+    def _double_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables,
+                      kv: ReferenceKV | None = None, layer: int = 0) -> None:
+        if kv is not None and kv.extracting:
+            self._double_block_extracting(ws, p, rope, kv, layer)
+            return
         if ws.nt % 256 == 0 and ws.ni > 0:
-            self._double_block_joint(ws, p, rope)
+            self._double_block_joint(ws, p, rope, kv, layer)
             return
         d, nt, h = self.v.dim, ws.nt, self.v.heads
         txt, img = ws.stream[:, :nt], ws.stream[:, nt:]
@@ -182,7 +242,7 @@ class Flux2Transformer:
             self.sp.attention_from_peers(recv, heads=h, out_ptrs=ws.qkv_ptrs, out_ld=3 * d,
                                          out_cols=3 * d, out_col=0)
         else:
-            self.sp.attention(q, k, v, q, heads=h)
+            self._attend(q, k, v, kv, layer)
         ops.linear(q[:, nt:], p["to_out"], img, kind=ops.EPI_GATED_RESIDUAL, residual=img,
                    gate=m(0, 2))
         ops.linear(q[:, :nt], p["to_add_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
@@ -196,7 +256,8 @@ class Flux2Transformer:
         ops.linear(ws.hid[:, :nt], p["ffc_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
                    gate=m(6, 5))
 
-    def _double_block_joint(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
+    def _double_block_joint(self, ws: _Workspace, p: dict, rope: ops.RopeTables,
+                            kv: ReferenceKV | None = None, layer: int = 0) -> None:
         """The double block with each projection of the two streams in one launch over the joint
         [text | image] rows: text rows use the text stream's weights, norms and gates (lead
         rows), image rows the image stream's. The streams stay independent; only the launch
@@ -217,7 +278,7 @@ class Flux2Transformer:
             self.sp.attention_from_peers(recv, heads=h, out_ptrs=ws.qkv_ptrs, out_ld=3 * d,
                                          out_cols=3 * d, out_col=0)
         else:
-            self.sp.attention(q, k, v, q, heads=h)
+            self._attend(q, k, v, kv, layer)
         ops.linear(q, p["to_out"], ws.stream, kind=ops.EPI_GATED_RESIDUAL, residual=ws.stream,
                    gate=m(0, 2), lead_w=p["to_add_out"], lead_rows=nt, lead_gate=m(6, 2))
         ops.adaln(img, m(0, 3), m(0, 4), img_n, norm=ops.NORM_LAYER)
@@ -228,7 +289,51 @@ class Flux2Transformer:
                    residual=ws.stream, gate=m(0, 5), lead_w=p["ffc_out"], lead_rows=nt,
                    lead_gate=m(6, 5))
 
-    def _single_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables) -> None:
+    def _double_block_extracting(self, ws: _Workspace, p: dict, rope: ops.RopeTables,
+                                 kv: ReferenceKV, layer: int) -> None:
+        """The double block on [text | reference | target] rows: reference rows use the image
+        modulation of timestep 0 (kinomlx/models/flux2/transformer.py:333-339, 139-153), so
+        each image-row AdaLN and gated residual runs once per row range."""
+        d, nt = self.v.dim, ws.nt
+        r0, r1 = nt, nt + kv.reference_tokens
+        txt, img = ws.stream[:, :nt], ws.stream[:, nt:]
+        txt_n, img_n = ws.nrm[:, :nt], ws.nrm[:, nt:]
+        m = lambda base, j: ws.mods[:, (base + j) * d : (base + j + 1) * d]  # img base 0, txt 6
+        mf = lambda base, j: ws.mods_fixed[:, (base + j) * d : (base + j + 1) * d]
+        image_rows = ((r0, r1, mf), (r1, nt + ws.ni, m))
+        for a, b, mod in image_rows:
+            ops.adaln(ws.stream[:, a:b], mod(0, 0), mod(0, 1), ws.nrm[:, a:b], norm=ops.NORM_LAYER)
+        ops.adaln(txt, m(6, 0), m(6, 1), txt_n, norm=ops.NORM_LAYER)
+        ops.linear(img_n, p["img_qkv"], ws.qkv[:, nt:], qk_norm=[(0, p["norm_q"]), (d, p["norm_k"])],
+                   norm_width=d, rope=(rope, nt))
+        ops.linear(txt_n, p["txt_qkv"], ws.qkv[:, :nt],
+                   qk_norm=[(0, p["norm_added_q"]), (d, p["norm_added_k"])], norm_width=d,
+                   rope=(rope, 0))
+        q, k, v = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
+        self._attend_extracting(q, k, v, nt, kv, layer)
+        for a, b, mod in image_rows:
+            rows = ws.stream[:, a:b]
+            ops.linear(q[:, a:b], p["to_out"], rows, kind=ops.EPI_GATED_RESIDUAL, residual=rows,
+                       gate=mod(0, 2))
+        ops.linear(q[:, :nt], p["to_add_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
+                   gate=m(6, 2))
+        for a, b, mod in image_rows:
+            ops.adaln(ws.stream[:, a:b], mod(0, 3), mod(0, 4), ws.nrm[:, a:b], norm=ops.NORM_LAYER)
+        ops.linear(img_n, p["ff_in"], ws.hid[:, nt:], kind=self.act_kind)
+        for a, b, mod in image_rows:
+            rows = ws.stream[:, a:b]
+            ops.linear(ws.hid[:, a:b], p["ff_out"], rows, kind=ops.EPI_GATED_RESIDUAL,
+                       residual=rows, gate=mod(0, 5))
+        ops.adaln(txt, m(6, 3), m(6, 4), txt_n, norm=ops.NORM_LAYER)
+        ops.linear(txt_n, p["ffc_in"], ws.hid[:, :nt], kind=self.act_kind)
+        ops.linear(ws.hid[:, :nt], p["ffc_out"], txt, kind=ops.EPI_GATED_RESIDUAL, residual=txt,
+                   gate=m(6, 5))
+
+    def _single_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables,
+                      kv: ReferenceKV | None = None, layer: int = 0) -> None:
+        if kv is not None and kv.extracting:
+            self._single_block_extracting(ws, p, rope, kv, layer)
+            return
         d, h = self.v.dim, self.v.heads
         sm = lambda j: ws.mods[:, (12 + j) * d : (13 + j) * d]
         ops.adaln(ws.stream, sm(0), sm(1), ws.nrm, norm=ops.NORM_LAYER)
@@ -243,9 +348,29 @@ class Flux2Transformer:
                                          out_ld=ws.big.shape[-1], out_cols=ws.big.shape[-1],
                                          out_col=2 * d)
         else:
-            self.sp.attention(q, k, v, q, heads=h)
+            self._attend(q, k, v, kv, layer)
         ops.linear(ws.big[..., 2 * d :], p["to_out"], ws.stream, kind=ops.EPI_GATED_RESIDUAL,
                    residual=ws.stream, gate=sm(2))
+
+    def _single_block_extracting(self, ws: _Workspace, p: dict, rope: ops.RopeTables,
+                                 kv: ReferenceKV, layer: int) -> None:
+        """The single block on [text | reference | target] rows, reference rows on the single
+        modulation of timestep 0 (kinomlx/models/flux2/transformer.py:340-346, 206-220)."""
+        d, nt = self.v.dim, ws.nt
+        r0, r1 = nt, nt + kv.reference_tokens
+        sm = lambda j: ws.mods[:, (12 + j) * d : (13 + j) * d]
+        smf = lambda j: ws.mods_fixed[:, (12 + j) * d : (13 + j) * d]
+        parts = ((0, r0, sm), (r0, r1, smf), (r1, nt + ws.ni, sm))
+        for a, b, mod in parts:
+            ops.adaln(ws.stream[:, a:b], mod(0), mod(1), ws.nrm[:, a:b], norm=ops.NORM_LAYER)
+        ops.linear(ws.nrm, p["fused"], ws.big, kind=self.act_kind, act_col_begin=3 * d,
+                   qk_norm=[(0, p["norm_k"]), (2 * d, p["norm_q"])], norm_width=d, rope=(rope, 0))
+        k, v, q = ws.big[..., :d], ws.big[..., d : 2 * d], ws.big[..., 2 * d : 3 * d]
+        self._attend_extracting(q, k, v, nt, kv, layer)
+        for a, b, mod in parts:
+            rows = ws.stream[:, a:b]
+            ops.linear(ws.big[:, a:b, 2 * d :], p["to_out"], rows, kind=ops.EPI_GATED_RESIDUAL,
+                       residual=rows, gate=mod(2))
 
     def double_block(self, index: int, image: torch.Tensor, text: torch.Tensor,
                      timestep_x1000: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor):
@@ -271,8 +396,10 @@ class Flux2Transformer:
         return ws.stream.clone()
 
     # ------------------------------------------------------------------ forward
-    def _embed(self, ws: _Workspace, timestep_x1000: torch.Tensor | float) -> None:
-        """Timestep MLP and every modulation vector (kinomlx/models/flux2/transformer.py:315-318)."""
+    def _embed(self, ws: _Workspace, timestep_x1000: torch.Tensor | float,
+               mods: torch.Tensor | None = None) -> None:
+        """Timestep MLP and every modulation vector (kinomlx/models/flux2/transformer.py:315-318)
+        into `mods` (default ws.mods)."""
         if isinstance(timestep_x1000, torch.Tensor):
             ws.t.copy_(timestep_x1000, non_blocking=True)
         else:  # one value for every batch entry: a fill, no host-to-device copy
@@ -280,28 +407,60 @@ class Flux2Transformer:
         ops.timestep_embedding(ws.t, 256, out=ws.temb)
         ops.gemv(ws.temb, self.t_lin1, out=ws.emb1)
         ops.gemv(ws.emb1, self.t_lin2, silu_input=True, out=ws.emb)
-        ops.gemv(ws.emb, self.mod_all, silu_input=True, out=ws.mods)
+        ops.gemv(ws.emb, self.mod_all, silu_input=True, out=ws.mods if mods is None else mods)
 
     def run(self, prepared: PreparedText, image: torch.Tensor, timestep_x1000: torch.Tensor | float,
             *, euler_dt: float | None = None, sample: torch.Tensor | None = None,
-            out: torch.Tensor | None = None) -> torch.Tensor:
+            out: torch.Tensor | None = None, reference_kv: ReferenceKV | None = None,
+            target: tuple[int, int] | None = None) -> torch.Tensor:
         """One transformer evaluation. With `euler_dt`, the final projection's epilogue applies
         the Klein Euler update to `sample` and returns the next latent instead of the velocity
-        (kinomlx/models/flux2/sampling.py:109-113, 240)."""
+        (kinomlx/models/flux2/sampling.py:109-113, 240).
+
+        `target` = (first row, rows) of `image` whose velocity is produced (default: all; image
+        rows appended as in-context references are left out this way). With `reference_kv`
+        extracting, `image` is [reference | target] rows and the target is every row after the
+        references (kinomlx/models/flux2/transformer.py:319-358)."""
         batch, ni, _ = image.shape
         nt = prepared.text.shape[1]
+        if reference_kv is not None:
+            self._check_reference_kv(reference_kv, batch, ni)
+            if reference_kv.extracting:
+                nr = reference_kv.reference_tokens
+                target = (nr, ni - nr)
+        first, rows = (0, ni) if target is None else target
+        if first < 0 or rows < 1 or first + rows > ni:
+            raise ValueError(f"target rows {target} outside the {ni} image rows")
         ws = self.workspace(batch, nt, ni)
+        kv = reference_kv
+        if kv is not None and kv.extracting:
+            self._embed(ws, 0.0, ws.mods_fixed)
         self._embed(ws, timestep_x1000)
         ws.stream[:, :nt].copy_(prepared.text)
         ops.linear(image, self.x_embedder, ws.stream[:, nt:])
-        for p in self.double:
-            self._double_block(ws, p, prepared.rope)
-        for p in self.single:
-            self._single_block(ws, p, prepared.rope)
+        for i, p in enumerate(self.double):
+            self._double_block(ws, p, prepared.rope, kv, i)
+        for i, p in enumerate(self.single, len(self.double)):
+            self._single_block(ws, p, prepared.rope, kv, i)
         d = self.v.dim
         om = lambda j: ws.mods[:, (15 + j) * d : (16 + j) * d]  # [scale | shift]
-        ops.adaln(ws.stream[:, nt:], om(1), om(0), ws.nrm[:, nt:], norm=ops.NORM_LAYER)
+        r0, r1 = nt + first, nt + first + rows
+        ops.adaln(ws.stream[:, r0:r1], om(1), om(0), ws.nrm[:, r0:r1], norm=ops.NORM_LAYER)
         if euler_dt is None:
-            return ops.linear(ws.nrm[:, nt:], self.proj_out, ws.velocity if out is None else out)
-        return ops.linear(ws.nrm[:, nt:], self.proj_out, out, kind=ops.EPI_EULER, dt=euler_dt,
+            dst = ws.velocity[:, :rows] if out is None else out
+            return ops.linear(ws.nrm[:, r0:r1], self.proj_out, dst)
+        return ops.linear(ws.nrm[:, r0:r1], self.proj_out, out, kind=ops.EPI_EULER, dt=euler_dt,
                           sample=sample)
+
+    def _check_reference_kv(self, kv: ReferenceKV, batch: int, image_rows: int) -> None:
+        """The reference's refusals (kinomlx/models/flux2/transformer.py:321-332)."""
+        if kv.closed:
+            raise ValueError("Reference K/V belongs to a completed generation")
+        if kv.layer_count != self.layer_count:
+            raise ValueError("Reference K/V layer count does not match the transformer")
+        if kv.batch != batch:
+            raise ValueError("Reference K/V batch does not match the image batch")
+        if self.sp.size > 1:
+            raise ValueError("reference K/V editing runs on one GPU")
+        if kv.extracting and kv.reference_tokens >= image_rows:
+            raise ValueError("KV extraction requires reference tokens followed by target tokens")

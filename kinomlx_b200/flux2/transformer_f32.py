@@ -231,12 +231,16 @@ class Flux2TransformerF32:
 
     def run(self, prepared: PreparedTextF32, image: torch.Tensor, timestep_x1000: torch.Tensor | float,
             *, euler_dt: float | None = None, sample: torch.Tensor | None = None,
-            out: torch.Tensor | None = None) -> torch.Tensor:
+            out: torch.Tensor | None = None, target: tuple[int, int] | None = None) -> torch.Tensor:
         """One transformer evaluation (kinomlx/models/flux2/transformer.py:307-358). With
         `euler_dt`, the final projection's epilogue applies the Euler update to `sample` and
-        returns the next latent instead of the velocity."""
+        returns the next latent instead of the velocity. `target` = (first row, rows) of `image`
+        whose velocity is produced (default all)."""
         batch, ni, _ = image.shape
         nt = prepared.text.shape[1]
+        first, rows = (0, ni) if target is None else target
+        if first < 0 or rows < 1 or first + rows > ni:
+            raise ValueError(f"target rows {target} outside the {ni} image rows")
         ws = self.workspace(batch, nt, ni)
         self._embed(ws, timestep_x1000)
         ws.stream[:, :nt].copy_(prepared.text)
@@ -247,8 +251,9 @@ class Flux2TransformerF32:
             self._single_block(ws, p, prepared.cos, prepared.sin)
         d = self.v.dim
         om = lambda j: ws.mods[:, (15 + j) * d : (16 + j) * d]  # [scale | shift]
-        f.adaln(ws.stream[:, nt:], om(1), om(0), ws.nrm[:, nt:], norm=NORM_LAYER)
+        r0, r1 = nt + first, nt + first + rows
+        f.adaln(ws.stream[:, r0:r1], om(1), om(0), ws.nrm[:, r0:r1], norm=NORM_LAYER)
         if euler_dt is None:
-            return f.linear(ws.nrm[:, nt:], self.proj_out, ws.velocity if out is None else out)
-        return f.linear(ws.nrm[:, nt:], self.proj_out, out, kind=EPI_EULER, dt=euler_dt,
+            return f.linear(ws.nrm[:, r0:r1], self.proj_out, ws.velocity[:, :rows] if out is None else out)
+        return f.linear(ws.nrm[:, r0:r1], self.proj_out, out, kind=EPI_EULER, dt=euler_dt,
                         sample=sample)

@@ -112,14 +112,83 @@ def activation(value: torch.Tensor, variant: FluxVariant) -> torch.Tensor:
     return swiglu(value) if variant.mlp == "swiglu" else gelu_approx(value)
 
 
-def joint_attention(q, k, v, cos, sin) -> torch.Tensor:
-    """Rotate q and k, SDPA with scale d^-1/2 over (B, H, N, d), back to (B, N, H*d)
-    (kinomlx/models/flux2/transformer.py:35-53, kinomlx/models/flux2/kv.py:48-54)."""
-    q, k = rotate(q, cos, sin), rotate(k, cos, sin)
-    out = sdpa(
+def attend(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """SDPA with scale d^-1/2 on (B, N, H, d) operands (kinomlx/models/flux2/kv.py:48-54)."""
+    return sdpa(
         q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=q.shape[-1] ** -0.5
     ).transpose(1, 2)
+
+
+class ReferenceKV:
+    """Post-RoPE reference-token keys and values of every layer, owned by one denoising call
+    (kinomlx/models/flux2/kv.py:8-45): `extracting` until the first evaluation has stored them,
+    `closed` once cleared."""
+
+    def __init__(self, reference_tokens: int, layers: int):
+        if reference_tokens < 1 or layers < 1:
+            raise ValueError("Reference K/V requires positive token and layer counts")
+        self.reference_tokens = reference_tokens
+        self.layers: list[tuple[torch.Tensor, torch.Tensor] | None] = [None] * layers
+        self.extracting = True
+        self.closed = False
+
+    def store(self, layer: int, key: torch.Tensor, value: torch.Tensor, start: int, count: int) -> None:
+        self.layers[layer] = (key[:, start : start + count].clone(), value[:, start : start + count].clone())
+
+    def tensors(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
+        entry = self.layers[layer]
+        if entry is None:
+            raise ValueError("Reference K/V has not been extracted")
+        return entry
+
+    def clear(self) -> None:
+        self.layers = [None] * len(self.layers)
+        self.closed = True
+
+
+def reference_attention(q, k, v, *, text_tokens: int, state: ReferenceKV, layer: int) -> torch.Tensor:
+    """Attention with reference K/V (kinomlx/models/flux2/kv.py:57-80) on post-RoPE (B, N, H, d):
+    extracting, rows are [text, reference, target]; the reference rows' keys and values are
+    stored, text and target queries attend to every key and reference queries to the reference
+    keys only. Reusing, rows are [text, target] and the stored keys and values are inserted
+    after the text's."""
+    start = text_tokens
+    if not state.extracting:
+        rk, rv = state.tensors(layer)
+        return attend(q, torch.cat([k[:, :start], rk, k[:, start:]], 1),
+                      torch.cat([v[:, :start], rv, v[:, start:]], 1))
+    end = start + state.reference_tokens
+    state.store(layer, k, v, start, state.reference_tokens)
+    active = attend(torch.cat([q[:, :start], q[:, end:]], 1), k, v)
+    reference = attend(q[:, start:end], k[:, start:end], v[:, start:end])
+    return torch.cat([active[:, :start], reference, active[:, start:]], 1)
+
+
+def blend_modulation(current: torch.Tensor, reference: torch.Tensor, start: int, count: int,
+                     length: int) -> torch.Tensor:
+    """Per-row modulation (B, length, C): `reference` at rows [start, start + count), `current`
+    elsewhere (kinomlx/models/flux2/kv.py:83-90)."""
+    shape = (current.shape[0], length, current.shape[-1])
+    expanded = current[:, None].expand(shape)
+    fixed = reference[:, None].expand(shape[0], count, shape[-1])
+    return torch.cat([expanded[:, :start], fixed, expanded[:, start + count :]], 1)
+
+
+def joint_attention(q, k, v, cos, sin, *, text_tokens: int = 0,
+                    reference_kv: ReferenceKV | None = None, layer: int = 0) -> torch.Tensor:
+    """Rotate q and k, attend (plain, or with reference K/V), back to (B, N, H*d)
+    (kinomlx/models/flux2/transformer.py:35-53)."""
+    q, k = rotate(q, cos, sin), rotate(k, cos, sin)
+    if reference_kv is None:
+        out = attend(q, k, v)
+    else:
+        out = reference_attention(q, k, v, text_tokens=text_tokens, state=reference_kv, layer=layer)
     return out.reshape(*q.shape[:2], -1)
+
+
+def _rows(mod: torch.Tensor) -> torch.Tensor:
+    """One modulation per batch entry (B, C) or per row (B, N, C), as (B, 1|N, C)."""
+    return mod[:, None] if mod.dim() == 2 else mod
 
 
 def _heads(x: torch.Tensor, variant: FluxVariant) -> torch.Tensor:
@@ -142,10 +211,13 @@ def double_block(
     cos: torch.Tensor,
     sin: torch.Tensor,
     variant: FluxVariant,
+    reference_kv: ReferenceKV | None = None,
+    layer: int = 0,
 ) -> tuple[torch.Tensor, torch.Tensor]:
-    """DoubleBlock + DoubleAttention (kinomlx/models/flux2/transformer.py:88-167)."""
+    """DoubleBlock + DoubleAttention (kinomlx/models/flux2/transformer.py:88-167); `image_mod`
+    is (B, 6D) or per image row (B, Ni, 6D)."""
     a = f"transformer_blocks.{i}"
-    shift, scale, gate, ff_shift, ff_scale, ff_gate = torch.chunk(image_mod[:, None], 6, dim=-1)
+    shift, scale, gate, ff_shift, ff_scale, ff_gate = torch.chunk(_rows(image_mod), 6, dim=-1)
     ts, tc, tg, fs, fc, fg = torch.chunk(text_mod[:, None], 6, dim=-1)
     img_n = normalized(image, shift, scale)
     txt_n = normalized(text, ts, tc)
@@ -168,8 +240,9 @@ def double_block(
         [_heads(linear(txt_n, w("add_v_proj")), variant), _heads(linear(img_n, w("to_v")), variant)],
         dim=1,
     )
-    result = joint_attention(query, key, value, cos, sin)
     nt = text.shape[1]
+    result = joint_attention(query, key, value, cos, sin, text_tokens=nt,
+                             reference_kv=reference_kv, layer=layer)
     ai = linear(result[:, nt:], w("to_out.0"))
     at = linear(result[:, :nt], w("to_add_out"))
     image, text = image + gate * ai, text + tg * at
@@ -186,10 +259,14 @@ def single_block(
     cos: torch.Tensor,
     sin: torch.Tensor,
     variant: FluxVariant,
+    reference_kv: ReferenceKV | None = None,
+    layer: int = 0,
+    text_tokens: int = 0,
 ) -> torch.Tensor:
-    """SingleBlock + SingleAttention (kinomlx/models/flux2/transformer.py:170-220)."""
+    """SingleBlock + SingleAttention (kinomlx/models/flux2/transformer.py:170-220);
+    `modulation` is (B, 3D) or per row (B, N, 3D)."""
     a = f"single_transformer_blocks.{i}.attn"
-    shift, scale, gate = torch.chunk(modulation[:, None], 3, dim=-1)
+    shift, scale, gate = torch.chunk(_rows(modulation), 3, dim=-1)
     x = normalized(value, shift, scale)
     d = variant.dim
     fused = linear(x, p[f"{a}.to_qkv_mlp_proj.weight"])
@@ -200,6 +277,9 @@ def single_block(
         _heads(v, variant),
         cos,
         sin,
+        text_tokens=text_tokens,
+        reference_kv=reference_kv,
+        layer=layer,
     )
     out = linear(torch.cat([attention, activation(mlp, variant)], dim=-1), p[f"{a}.to_out.weight"])
     return value + gate * out
@@ -235,19 +315,41 @@ def forward(
     image: torch.Tensor,
     timestep: torch.Tensor,
     variant: FluxVariant,
+    *,
+    reference_kv: ReferenceKV | None = None,
 ) -> torch.Tensor:
-    """Flux2Transformer._forward with projected text (kinomlx/models/flux2/transformer.py:307-358)."""
+    """Flux2Transformer._forward with projected text (kinomlx/models/flux2/transformer.py:307-358).
+    With `reference_kv` extracting, `image` is [reference, target] rows: the reference rows take
+    the modulations of timestep 0 and the velocity covers the target rows only."""
     embedding = timestep_embedding(p, timestep.to(image.dtype) * 1000)
     im = modulation(p, "double_stream_modulation_img", embedding)
     tm = modulation(p, "double_stream_modulation_txt", embedding)
     sm = modulation(p, "single_stream_modulation", embedding)
+    layers = variant.double_blocks + variant.single_blocks
+    reference_tokens = 0
+    if reference_kv is not None:
+        if reference_kv.closed:
+            raise ValueError("Reference K/V belongs to a completed generation")
+        if len(reference_kv.layers) != layers:
+            raise ValueError("Reference K/V layer count does not match the transformer")
+        if reference_kv.extracting:
+            reference_tokens = reference_kv.reference_tokens
+            if reference_tokens >= image.shape[1]:
+                raise ValueError("KV extraction requires reference tokens followed by target tokens")
+            fixed = timestep_embedding(p, torch.zeros_like(timestep).to(image.dtype))
+            im = blend_modulation(im, modulation(p, "double_stream_modulation_img", fixed), 0,
+                                  reference_tokens, image.shape[1])
+            sm = blend_modulation(sm, modulation(p, "single_stream_modulation", fixed),
+                                  text.shape[1], reference_tokens, text.shape[1] + image.shape[1])
     image = linear(image, p["x_embedder.weight"])
     for i in range(variant.double_blocks):
-        image, text = double_block(p, i, image, text, im, tm, cos, sin, variant)
+        image, text = double_block(p, i, image, text, im, tm, cos, sin, variant, reference_kv, i)
     value = torch.cat([text, image], dim=1)
     for i in range(variant.single_blocks):
-        value = single_block(p, i, value, sm, cos, sin, variant)
-    return linear(output_norm(p, value[:, text.shape[1] :], embedding), p["proj_out.weight"])
+        value = single_block(p, i, value, sm, cos, sin, variant, reference_kv,
+                             variant.double_blocks + i, text.shape[1])
+    out = output_norm(p, value[:, text.shape[1] + reference_tokens :], embedding)
+    return linear(out, p["proj_out.weight"])
 
 
 def prepare(p: dict, text: torch.Tensor, ids: torch.Tensor, variant: FluxVariant):
@@ -299,23 +401,83 @@ def denoise(
     negative: torch.Tensor | None = None,
     guidance: float = 1.0,
     steps: int | None = None,
+    references: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """The Euler loop of kinomlx/models/flux2/sampling.py:116-281 with batched CFG when a
-    negative text is given (cond first, uncond second, `uncond + g * (cond - uncond)`)."""
+    negative text is given (cond first, uncond second, `uncond + g * (cond - uncond)`). With
+    `references` (1, Nr, C), every evaluation sees [target, reference] rows and `ids` holds the
+    [text, target, reference] positions; the velocity is the target rows'
+    (sampling.py:193-197, 255-281)."""
     count = len(sigmas) - 1 if steps is None else steps
     conditioned = text if negative is None else torch.cat([text, negative])
     projected, cos, sin = prepare(p, conditioned, ids, variant)
     current = noise
     for i in range(count):
         t = step_timestep(sigmas, i, noise.dtype)
+        image = current if references is None else torch.cat([current, references], 1)
         if negative is None:
-            velocity = forward(p, projected, cos, sin, current, t, variant)
+            velocity = forward(p, projected, cos, sin, image, t, variant)
         else:
-            both = forward(p, projected, cos, sin, torch.cat([current, current]), torch.cat([t, t]), variant)
+            both = forward(p, projected, cos, sin, torch.cat([image, image]), torch.cat([t, t]), variant)
             positive, uncond = torch.chunk(both, 2, dim=0)
             velocity = uncond + guidance * (positive - uncond)
+        velocity = velocity[:, : current.shape[1]]
         current = euler_step(current, velocity, sigmas[i + 1] - sigmas[i])
     return current
+
+
+def kv_loop(predict, reuse, new_cache, references: torch.Tensor, noise: torch.Tensor,
+            sigmas: torch.Tensor, *, recompute: bool = False) -> torch.Tensor:
+    """The KV-editing branch of the Euler loop (kinomlx/models/flux2/sampling.py:206-252): a
+    cache is extracted from [reference, target] rows at the first evaluation (at every one with
+    `recompute`) and reused on target rows after that; the cache is cleared when the loop ends
+    or fails. `predict`/`reuse`(image, timestep, cache) return the target velocity."""
+    current, cache = noise, None
+    try:
+        for i in range(len(sigmas) - 1):
+            t = step_timestep(sigmas, i, noise.dtype)
+            if cache is None:
+                cache = new_cache(references.shape[1])
+            if cache.extracting:
+                velocity = predict(torch.cat([references, current], 1), t, cache)
+            else:
+                velocity = reuse(current, t, cache)
+            cache.extracting = False
+            if recompute:
+                cache.clear()
+                cache = None
+            current = euler_step(current, velocity, sigmas[i + 1] - sigmas[i])
+    finally:
+        if cache is not None:
+            cache.clear()
+    return current
+
+
+def denoise_kv(
+    p: dict,
+    noise: torch.Tensor,
+    text: torch.Tensor,
+    text_ids: torch.Tensor,
+    image_ids: torch.Tensor,
+    references: torch.Tensor,
+    reference_ids: torch.Tensor,
+    sigmas: torch.Tensor,
+    variant: FluxVariant,
+    *,
+    recompute: bool = False,
+) -> torch.Tensor:
+    """Klein KV editing (kinomlx/models/flux2/sampling.py:186-190, 206-252): the text projected
+    once, RoPE tables for the [text, reference, target] extraction rows and the [text, target]
+    reuse rows."""
+    projected = linear(text, p["context_embedder.weight"])
+    cx, sx = rotary_positions(torch.cat([text_ids, reference_ids, image_ids], 1), variant)
+    cr, sr = rotary_positions(torch.cat([text_ids, image_ids], 1), variant)
+    layers = variant.double_blocks + variant.single_blocks
+    return kv_loop(
+        lambda image, t, cache: forward(p, projected, cx, sx, image, t, variant, reference_kv=cache),
+        lambda image, t, cache: forward(p, projected, cr, sr, image, t, variant, reference_kv=cache),
+        lambda count: ReferenceKV(count, layers),
+        references, noise, sigmas, recompute=recompute)
 
 
 def image_ids(height: int, width: int, axes: int) -> torch.Tensor:

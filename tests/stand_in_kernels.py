@@ -25,23 +25,54 @@ def _put(out, y):
     return out
 
 
+def _rope_rows(tables, offset: int, batch: int, rows: int):
+    """(batch, rows, 1, 128) cos/sin of ops.RopeTables: batch b, row i reads table column
+    (b * tables.rows if batched) + offset + i."""
+    idx = offset + torch.arange(rows)
+    cols = (torch.arange(batch)[:, None] * tables.rows if tables.batched else torch.zeros(batch, 1, dtype=torch.long)) + idx
+    pick = lambda t: t.T[cols][:, :, None]
+    return pick(tables.cos_t), pick(tables.sin_t)
+
+
 def linear(x, w, out=None, *, bias=None, kind=0, residual=None, gate=None, act_col_begin=0,
-           dt=0.0, sample=None, sigma=0.0, ratio=0.0, **_):
-    y = x.float() @ w.float().T
+           dt=0.0, sample=None, sigma=0.0, ratio=0.0, qk_norm=None, norm_width=0, rope=None,
+           eps=1e-6, lead_w=None, lead_rows=0, lead_qk_norm=None, lead_gate=None, **_):
+    x3 = _3(x).float()
+    y = x3 @ w.float().T
+    if lead_w is not None:  # rows [0, lead_rows) of every batch entry use the lead weight
+        y[:, :lead_rows] = x3[:, :lead_rows] @ lead_w.float().T
     if bias is not None:
         y = y + bias.float()
+    if qk_norm:  # per-head RMSNorm then adjacent-pair RoPE on each (column, weight) range
+        b, m = y.shape[:2]
+        c, s = _rope_rows(rope[0], rope[1], b, m)
+        for r, (col, wt) in enumerate(qk_norm):
+            seg = y[..., col : col + norm_width].reshape(b, m, -1, 128)
+            normed = rops.rms_norm(seg, wt.float(), eps)
+            if lead_qk_norm:
+                normed[:, :lead_rows] = rops.rms_norm(seg[:, :lead_rows], lead_qk_norm[r].float(), eps)
+            y[..., col : col + norm_width] = fref.rotate(normed, c, s).reshape(b, m, norm_width)
     if kind == 1:  # GELU on columns >= act_col_begin
         y = torch.cat([y[..., :act_col_begin], rops.gelu_approx(y[..., act_col_begin:])], -1)
+    elif kind == 6:  # SwiGLU on blocks of 16 gate + 16 content columns from act_col_begin
+        blocks = y[..., act_col_begin:].reshape(*y.shape[:-1], -1, 2, 16)
+        act = rops.silu(blocks[..., 0, :]) * blocks[..., 1, :]
+        y = torch.cat([y[..., :act_col_begin], act.reshape(*y.shape[:-1], -1)], -1)
     elif kind == 2:  # gated residual
-        g = gate.reshape(-1, gate.shape[-1]).float()
-        y = (_3(residual).float() + g[:, None] * _3(y)).reshape(residual.shape)
+        g = gate.reshape(-1, gate.shape[-1]).float()[:, None].expand(y.shape[0], y.shape[1], -1).clone()
+        if lead_gate is not None:
+            g[:, :lead_rows] = lead_gate.reshape(-1, lead_gate.shape[-1]).float()[:, None]
+        y = (_3(residual).float() + g * y).reshape(residual.shape)
     elif kind == 3:  # Euler
-        y = sample.float() + dt * y
+        y = sample.float() + dt * y.reshape(sample.shape)
     elif kind == 4:  # 2 * sigmoid
         y = 2.0 * torch.sigmoid(y)
     elif kind == 5:  # X0 + Euler
+        y = y.reshape(sample.shape)
         x0 = sample.float() - sigma * y
         y = x0 + ratio * (sample.float() - x0)
+    if out is None and x.dim() == 2 and y.dim() == 3:
+        y = y[0]
     return _put(out, y)
 
 
@@ -175,8 +206,12 @@ def blend_normalize(canvas, weights):
 
 
 def install(monkeypatch) -> None:
-    """Replace the kernel calls of kinomlx_b200.ops and kinomlx_b200.ops_f32 for one test."""
+    """Replace the kernel calls of kinomlx_b200.ops and kinomlx_b200.ops_f32 for one test, and
+    run the bf16 model classes' wiring in fp32."""
     from kinomlx_b200 import ops, ops_f32
+    from kinomlx_b200.flux2 import transformer as flux
+
+    monkeypatch.setattr(flux, "BF", torch.float32)
 
     for mod, att in ((ops, attention_list), (ops_f32, attention_tensor)):
         for name, fn in (("linear", linear), ("attention", att), ("adaln", adaln),
