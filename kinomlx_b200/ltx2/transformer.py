@@ -21,6 +21,8 @@ from ..sequence_parallel import SequenceParallel
 from . import quantization as qz
 from .config import LTXVariant
 
+BF = torch.bfloat16
+
 
 def frequency_grid(theta: float, axes: int, inner_dim: int) -> tuple[float, ...]:
     """theta^(i/(n-1)) * pi/2 on the host in double (kinomlx/models/ltx2/transformer/rope.py:75-92)."""
@@ -60,7 +62,7 @@ class _Workspace:
     def __init__(self, v: LTXVariant, batch: int, tokens: int, ctx_tokens: int, device,
                  sp: SequenceParallel):
         d = v.dim
-        e = lambda *s: torch.empty(s, device=device, dtype=torch.bfloat16)
+        e = lambda *s: torch.empty(s, device=device, dtype=BF)
         self.x = e(batch, tokens, d)
         self.nrm = e(batch, tokens, d)
         self.hid = e(batch, tokens, v.ff_mult * d)
@@ -92,6 +94,10 @@ class _Workspace:
 class LTXVideoTransformer:
     """Device LTX-2 video DiT. `weights` uses the reference checkpoint names."""
 
+    @property
+    def dtype(self) -> torch.dtype:
+        return BF
+
     def __init__(self, weights: dict[str, torch.Tensor], variant: LTXVariant,
                  device: torch.device | str = "cuda", *, sp: SequenceParallel | None = None,
                  quantize: str = "off"):
@@ -107,7 +113,7 @@ class LTXVideoTransformer:
         self.sp = sp if sp is not None else SequenceParallel.single()
         self.v = variant
         self.device = torch.device(device)
-        dev = lambda t: t.to(self.device, torch.bfloat16).contiguous()
+        dev = lambda t: t.to(self.device, BF).contiguous()
         w = weights
         self.patch_w, self.patch_b = dev(w["patchify_proj.weight"]), dev(w["patchify_proj.bias"])
 
@@ -204,7 +210,7 @@ class LTXVideoTransformer:
         self._ws: dict[tuple[int, int, int], _Workspace] = {}
         # one bf16 buffer for the packed linears' dequantised weights, reused by every GEMM on
         # the stream (each dequantisation waits for the previous GEMM to finish reading it)
-        self._dq = (torch.empty(scratch_elems, device=self.device, dtype=torch.bfloat16)
+        self._dq = (torch.empty(scratch_elems, device=self.device, dtype=BF)
                     if packed else None)
 
     def _wt(self, p: dict, name: str) -> torch.Tensor:
@@ -222,7 +228,7 @@ class LTXVideoTransformer:
         if self.sp.size > 1:
             t0, t1 = self.sp.shard(cos.shape[2])
             cos, sin = cos[:, :, t0:t1].contiguous(), sin[:, :, t0:t1].contiguous()
-        return PreparedContext(context.to(self.device, torch.bfloat16).contiguous(),
+        return PreparedContext(context.to(self.device, BF).contiguous(),
                                cos.to(self.device), sin.to(self.device))
 
     def workspace(self, batch: int, tokens: int, ctx_tokens: int) -> _Workspace:

@@ -210,8 +210,10 @@ def install(monkeypatch) -> None:
     run the bf16 model classes' wiring in fp32."""
     from kinomlx_b200 import ops, ops_f32
     from kinomlx_b200.flux2 import transformer as flux
+    from kinomlx_b200.ltx2 import transformer as ltx
 
     monkeypatch.setattr(flux, "BF", torch.float32)
+    monkeypatch.setattr(ltx, "BF", torch.float32)
 
     for mod, att in ((ops, attention_list), (ops_f32, attention_tensor)):
         for name, fn in (("linear", linear), ("attention", att), ("adaln", adaln),

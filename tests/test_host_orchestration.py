@@ -1,10 +1,12 @@
 """Host-side orchestration of the model classes on the CPU: the kernel calls are replaced by torch
 stand-ins of the same contracts (tests/stand_in_kernels.py), so these tests check only what the
 classes hand to which kernel (slices, aliasing, modulation rows, RoPE tables, step order) against
-the oracle. Covered: the fp32 Flux2 and LTX-2 transformers, the fp32 VAE decoder, the joint
-audio/video LTX-2 model and the bf16 Flux2 class (both run in fp32 here; the stand-in GEMM
-applies the fused QK-norm/RoPE, lead-row and SwiGLU epilogues the way the kernel does), with
-its CFG, in-context reference and KV-editing loops. Every kernel is tested on the GPU."""
+the oracle. Covered: the fp32 Flux2 and LTX-2 transformers, the fp32 VAE decoder, and the bf16
+Flux2, LTX-2 video and joint audio/video classes (run in fp32 here; the stand-in GEMM applies the
+fused QK-norm/RoPE, lead-row and SwiGLU epilogues the way the kernel does), with the Flux2 CFG,
+in-context reference and KV-editing loops. Weights are rescaled so that a wiring mistake moves
+the compared update by far more than the tolerance (see `_kaiming`). Every kernel is tested on
+the GPU."""
 
 from __future__ import annotations
 
@@ -22,6 +24,7 @@ from kinomlx_b200.ltx2 import av_transformer as avm
 from kinomlx_b200.ltx2 import denoise as ldn
 from kinomlx_b200.ltx2 import video_vae as vae
 from kinomlx_b200.ltx2.config import LTXVariant
+from kinomlx_b200.ltx2.transformer import LTXVideoTransformer
 from kinomlx_b200.ltx2.transformer_f32 import LTXVideoTransformerF32
 from kinomlx_b200.ltx2.video_vae_f32 import VideoDecoderF32
 from kinomlx_b200.synthetic import (flux_weights, ltx_av_weight_specs, ltx_weights, make_weights,
@@ -95,6 +98,21 @@ def test_ltx_f32_trajectory(monkeypatch):
     sigmas = lref.DISTILLED_STAGE_1_SIGMAS[5:]
     expect = lref.denoise(w, latent, context, pos, sigmas, v)
     out = ldn.denoise_loop(LTXVideoTransformerF32(w, v, CPU), latent, context, pos, sigmas)
+    assert _max_rel(out - latent, expect - latent) < TOL
+
+
+def test_ltx_bf16_class_trajectory(monkeypatch):
+    """The bf16 LTX-2 video class's wiring (run in fp32): AdaLN tables, gated self- and
+    cross-attention with full-row QK norms and split RoPE, prompt AdaLN, X0 + Euler output."""
+    stand_in.install(monkeypatch)
+    v = LTXVariant(dim=256, heads=2, context_dim=256, blocks=2)
+    w = _kaiming(ltx_weights(v, seed=120, dtype=F32))
+    latent = normal((2, 2 * 3 * 4, v.in_channels), seed=121, dtype=F32)
+    context = normal((2, 6, v.context_dim), seed=122, dtype=F32)
+    pos = lref.pixel_coords(lref.patch_grid_bounds(2, 3, 4))
+    sigmas = lref.DISTILLED_STAGE_1_SIGMAS[5:]
+    expect = lref.denoise(w, latent, context, pos, sigmas, v)
+    out = ldn.denoise_loop(LTXVideoTransformer(w, v, CPU), latent, context, pos, sigmas)
     assert _max_rel(out - latent, expect - latent) < TOL
 
 
