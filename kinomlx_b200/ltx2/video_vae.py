@@ -16,6 +16,8 @@ import torch
 
 from .. import ops
 
+BF = torch.bfloat16
+
 
 @dataclass(frozen=True)
 class VaeVariant:
@@ -107,7 +109,7 @@ class VideoDecoder:
                  device: torch.device | str = "cuda"):
         self.v = variant
         self.device = torch.device(device)
-        dev = lambda t: t.to(self.device, torch.bfloat16).contiguous()
+        dev = lambda t: t.to(self.device, BF).contiguous()
         w = weights
         self.std = w["per_channel_statistics.std_of_means"].to(self.device, torch.float32)
         self.mean = w["per_channel_statistics.mean_of_means"].to(self.device, torch.float32)
@@ -166,7 +168,7 @@ class VideoDecoder:
             self._conv_ws = ops.conv_workspace(self.device)
         st = self._stats if group else None  # every GroupNorm input is the previous conv's output
         ws = self._conv_ws
-        x = ops.latent_to_bfhwc(latent.to(self.device, torch.bfloat16).contiguous(), self.std, self.mean)
+        x = ops.latent_to_bfhwc(latent.to(self.device, BF).contiguous(), self.std, self.mean)
         x = ops.conv3d(x, *self.conv_in, causal=causal, stats=st, workspace=ws)
         for kind, payload in self.stages:
             if kind == "res":

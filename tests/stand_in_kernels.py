@@ -159,7 +159,17 @@ def euler_velocity(x, v, dt, out=None):
     return _put(out, x.float() + dt * v.float())
 
 
-def conv3d(x, weight, bias=None, *, causal, stride=(1, 1, 1), residual=None, out=None, **_):
+def _keep_stats(stats, y) -> None:
+    """The bf16 conv's GroupNorm(32) statistics, in a stand-in layout: stats[:32] the group
+    means, stats[32:64] the biased group variances of the conv output y (..., C)."""
+    if stats is not None:
+        g = y.float().reshape(-1, 32, y.shape[-1] // 32)
+        stats[:32] = g.mean(dim=(0, 2))
+        stats[32:64] = g.var(dim=(0, 2), unbiased=False)
+
+
+def conv3d(x, weight, bias=None, *, causal, stride=(1, 1, 1), residual=None, out=None, stats=None,
+           **_):
     x5 = (x if x.dim() == 5 else x[None]).float()
     sub = stride[0] * stride[1] * stride[2]
     b = torch.zeros(weight.shape[0]) if bias is None else bias.float()
@@ -167,6 +177,7 @@ def conv3d(x, weight, bias=None, *, causal, stride=(1, 1, 1), residual=None, out
         y = vref.conv3d(x5, weight.float(), b, causal)[0]
         if residual is not None:
             y = y + residual.float()
+        _keep_stats(stats, y)
         return _put(out, y)
     n, cin = weight.shape[0], weight.shape[-1]
     cout = n // sub
@@ -175,6 +186,7 @@ def conv3d(x, weight, bias=None, *, causal, stride=(1, 1, 1), residual=None, out
     bs = b.reshape(sub, cout).transpose(0, 1).reshape(-1)
     y = vref.upsample({"u.conv.weight": wt, "u.conv.bias": bs}, "u", x5, stride, cin // cout,
                       vref.VaeVariant(causal=causal))[0]
+    _keep_stats(stats, y)
     return _put(out, y)
 
 
@@ -185,6 +197,16 @@ def pixel_norm(x, eps=1e-8, *, silu=False, out=None):
 
 def group_norm(x, groups, weight, bias, eps, *, silu=False, out=None, **_):
     y = rops.group_norm(x.float()[None], 32, weight.float(), bias.float(), eps)[0]
+    return _put(out, rops.silu(y) if silu else y)
+
+
+def group_norm_from_stats(x, weight, bias, eps, stats, *, silu=False, out=None):
+    """Normalise with the statistics the producing conv kept (never recomputed from x), so a
+    norm reading another conv's statistics shows."""
+    c = x.shape[-1]
+    g = x.float().reshape(-1, 32, c // 32)
+    y = (g - stats[:32, None]) / torch.sqrt(stats[32:64, None] + eps)
+    y = y.reshape(x.shape) * weight.float() + bias.float()
     return _put(out, rops.silu(y) if silu else y)
 
 
@@ -211,9 +233,10 @@ def install(monkeypatch) -> None:
     from kinomlx_b200 import ops, ops_f32
     from kinomlx_b200.flux2 import transformer as flux
     from kinomlx_b200.ltx2 import transformer as ltx
+    from kinomlx_b200.ltx2 import video_vae as vae
 
-    monkeypatch.setattr(flux, "BF", torch.float32)
-    monkeypatch.setattr(ltx, "BF", torch.float32)
+    for mod in (flux, ltx, vae):
+        monkeypatch.setattr(mod, "BF", torch.float32)
 
     for mod, att in ((ops, attention_list), (ops_f32, attention_tensor)):
         for name, fn in (("linear", linear), ("attention", att), ("adaln", adaln),
@@ -223,6 +246,11 @@ def install(monkeypatch) -> None:
             monkeypatch.setattr(mod, name, fn, raising=False)
     monkeypatch.setattr(ops, "gemv", gemv)
     monkeypatch.setattr(ops, "device_status", lambda: None)
+    for name, fn in (("conv3d", conv3d), ("pixel_norm", pixel_norm), ("latent_to_bfhwc", latent_to_bfhwc),
+                     ("tile_blend", tile_blend), ("group_norm_from_stats", group_norm_from_stats),
+                     ("conv_stats_buffer", lambda device=None: torch.zeros(64)),
+                     ("conv_workspace", lambda device=None: torch.zeros(1, dtype=torch.uint8))):
+        monkeypatch.setattr(ops, name, fn)
     for name, fn in (("silu", unary(rops.silu)), ("gelu_tanh", unary(rops.gelu_approx)),
                      ("swiglu", swiglu), ("conv3d", conv3d), ("pixel_norm", pixel_norm),
                      ("group_norm", group_norm), ("latent_to_bfhwc", latent_to_bfhwc),

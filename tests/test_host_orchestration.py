@@ -129,6 +129,23 @@ def test_vae_f32_tiled_decode(monkeypatch):
         assert _max_rel(out, expect) < TOL
 
 
+def test_vae_bf16_class_tiled_decode(monkeypatch):
+    """The bf16 decoder's wiring (run in fp32): each GroupNorm normalises with the statistics the
+    conv that produced its input kept in its epilogue (the stand-in norm reads only those), the
+    residual conv writes over its residual, depth-to-space rows, the tiled blend."""
+    stand_in.install(monkeypatch)
+    blocks = (("res", 1), ("d2s", (2, 2, 2), 2), ("res", 2), ("d2s", (1, 2, 2), 1), ("res", 1))
+    for norm, causal in (("pixel", True), ("group32", False)):
+        v = vae.VaeVariant(norm=norm, causal=causal, top_width=64, blocks=blocks)
+        rv = vref.VaeVariant(norm=norm, causal=causal, top_width=64, blocks=blocks)
+        w = make_weights(vae.vae_weight_specs(v), seed=123, dtype=F32)
+        w = {k: (t + 0.1 * normal(t.shape, seed=124, dtype=F32) if "norm" in k else t) for k, t in w.items()}
+        latent = normal((1, 128, 2, 5, 7), seed=125, dtype=F32)
+        expect = vref.decode_tiled(w, latent, rv, tile=3, overlap=1, scale=16, dtype=F32)
+        out = vae.VideoDecoder(w, v, CPU).decode(latent, tile=3, overlap=1)
+        assert _max_rel(out, expect) < TOL
+
+
 def test_av_model_trajectory(monkeypatch):
     stand_in.install(monkeypatch)
     monkeypatch.setattr(avm, "BF", F32)  # run the bf16 model's wiring in fp32
