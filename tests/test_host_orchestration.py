@@ -40,13 +40,15 @@ def _max_rel(out, expect) -> float:
 
 
 def _kaiming(w: dict) -> dict:
-    """Projection weights rescaled to std 1/sqrt(fan_in) (modulations x4): the synthetic std
-    0.02 leaves gates near 0.02, where a wiring mistake moves the output by less than the
-    tolerance."""
+    """Projection weights rescaled to std 1/sqrt(fan_in) (modulations x4) and norm weights moved
+    off 1: the synthetic std 0.02 leaves gates near 0.02, where a wiring mistake moves the output
+    by less than the tolerance, and all-ones norm weights hide a swapped norm."""
     scaled = {}
     for name, t in w.items():
         if t.dim() == 2 and name.endswith(".weight") and "norm" not in name:
             t = t / t.std() * t.shape[1] ** -0.5 * (4.0 if "modulation" in name else 1.0)
+        elif t.dim() == 1 and "norm" in name:
+            t = t + 0.2 * normal(t.shape, seed=len(scaled), dtype=t.dtype)
         scaled[name] = t
     return scaled
 

@@ -2,24 +2,21 @@
 
 Collected after the other GPU tests, so that a failure here under `pytest -x` stops nothing else.
 
-What each check can see, measured on the oracle (bf16 against fp32 on the same inputs):
-  * kept reference keys/values, with projection weights at std 1/sqrt(fan_in) (modulations x2):
-    bf16 rounding moves them by 0.5-0.7% (relative L2), while reference rows on the current
-    modulation move the second layer's keys by 75% and reference queries that also see text and
-    target keys by 19%: gate 2e-2;
+What each check can see, measured on the oracle (bf16 against fp32 on the same inputs; the
+timestep is 500, which bf16 holds exactly: the reference rounds timestep x 1000 to the model
+dtype, so a value bf16 cannot hold would give the two precisions different inputs):
+  * with projection weights at std 1/sqrt(fan_in) (modulations x2, QK-norm weights perturbed
+    off 1), the kept reference keys/values move by 0.5-0.7% (relative L2) under bf16 rounding,
+    while reference rows on the current modulation move the second layer's keys by 72% and
+    reference queries that also see text and target keys by 19%: gate 2e-2;
+  * at the same weights the velocities of one extracting and one reusing evaluation move by
+    0.7% under bf16 rounding, while leaving the reference out moves them by 7.7% and the
+    reference rows on the current modulation by 3.6%: gate 2e-2 and cosine >= 0.999;
   * the kept rows depend on the reference rows alone, so two extractions with different
     targets, texts and timesteps keep bit-identical rows on the device (every kernel computes
     rows independently and deterministically);
-  * velocities of one extracting and one reusing evaluation at the synthetic weights (std 0.02):
-    bf16 rounding gives 2.2-2.4% relative L2, cosine 0.9997; gate 5e-2 and cosine >= 0.999
-    against the fp32 oracle on the bf16-rounded weights and inputs. At these weights the
-    reference rows move the velocity by less than bf16 rounding does (0.45% without them), so
-    this checks the numerics of both evaluations end to end; the wiring of the reusing pass
-    (kept rows as a second key segment) is checked exactly on the CPU
-    (tests/test_host_orchestration.py), the two-segment attention kernel in
-    tests/test_gpu_kernels.py;
-  * whole trajectories: final-latent cosine >= 0.999 and relative L2 <= 3e-2, the gate of the
-    other trajectory tests.
+  * whole trajectories at the synthetic weights (std 0.02): final-latent cosine >= 0.999 and
+    relative L2 <= 3e-2, the gate of the other trajectory tests.
 
 Seeds: weights S, target latents S + 1, text S + 2, references S + 3, all N(0, 1) on the CPU.
 """
@@ -46,11 +43,13 @@ def _variant(double: int = 1, single: int = 1) -> fcfg.FluxVariant:
                             context_dim=512, double_blocks=double, single_blocks=single)
 
 
-def _scaled(w: dict) -> dict:
+def _scaled(w: dict, seed: int) -> dict:
     out = {}
     for name, t in w.items():
         if t.dim() == 2 and name.endswith(".weight") and "norm" not in name:
             t = t.float() / t.float().std() * t.shape[1] ** -0.5 * (2.0 if "modulation" in name else 1.0)
+        elif t.dim() == 1 and "norm" in name:
+            t = t.float() + 0.2 * normal(t.shape, seed=seed + len(out), dtype=F32)
         out[name] = t.to(BF)
     return out
 
@@ -106,10 +105,10 @@ def test_kept_reference_rows_match_oracle(cuda_device, nt):
     """Split (40 text rows) and joint (256) double-block paths: every layer's kept keys and
     values against the oracle's at weights where a mis-wired reference row shows."""
     v = _variant()
-    w = _scaled(flux_weights(v, seed=31, dtype=F32))
+    w = _scaled(flux_weights(v, seed=31, dtype=F32), 31)
     c = _case(31, nt)
-    _, _, kept = _oracle_pair(w, c, v, 0.75)
-    _, _, got = _device_pair(Flux2Transformer(w, v, cuda_device), c, 0.75, cuda_device)
+    _, _, kept = _oracle_pair(w, c, v, 0.5)
+    _, _, got = _device_pair(Flux2Transformer(w, v, cuda_device), c, 0.5, cuda_device)
     torch.cuda.synchronize()
     for layer, ((ek, ev), (gk, gv)) in enumerate(zip(kept, got)):
         for name, e, g in (("key", ek, gk), ("value", ev, gv)):
@@ -124,7 +123,7 @@ def test_kept_rows_depend_on_the_reference_alone(cuda_device):
     model = Flux2Transformer(w, v, cuda_device)
     a, b = _case(51, 40), _case(61, 40)
     b["refs"] = a["refs"]
-    _, _, kept_a = _device_pair(model, a, 0.75, cuda_device)
+    _, _, kept_a = _device_pair(model, a, 0.5, cuda_device)
     _, _, kept_b = _device_pair(model, b, 0.25, cuda_device)
     torch.cuda.synchronize()
     for (ka, va), (kb, vb) in zip(kept_a, kept_b):
@@ -134,14 +133,14 @@ def test_kept_rows_depend_on_the_reference_alone(cuda_device):
 @pytest.mark.parametrize("nt", [40, 256])
 def test_extracting_and_reusing_velocities_match_oracle(cuda_device, nt):
     v = _variant()
-    w = flux_weights(v, seed=41)
-    c = _case(41, nt)
-    ex, ru, _ = _oracle_pair(w, c, v, 0.75)
-    gx, gr, _ = _device_pair(Flux2Transformer(w, v, cuda_device), c, 0.75, cuda_device)
+    w = _scaled(flux_weights(v, seed=21, dtype=F32), 21)
+    c = _case(21, nt)
+    ex, ru, _ = _oracle_pair(w, c, v, 0.5)
+    gx, gr, _ = _device_pair(Flux2Transformer(w, v, cuda_device), c, 0.5, cuda_device)
     torch.cuda.synchronize()
     for name, g, e in (("extracting", gx, ex), ("reusing", gr, ru)):
         rel, cos = _metrics(g, e)
-        assert rel <= 5e-2 and cos >= 0.999, (name, rel, cos)
+        assert rel <= 2e-2 and cos >= 0.999, (name, rel, cos)
 
 
 @pytest.mark.parametrize("recompute", [False, True])
