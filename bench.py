@@ -693,6 +693,9 @@ def run_kernel_case(case: str) -> None:
     elif case == "av_step":
         run_av_step(dev)
         return
+    elif case == "kv_step":
+        run_kv_step(dev)
+        return
     elif case == "f32":
         # fp32 parity mode at config 1: the image stream's FF up projection (1024 x 12288 x 3072,
         # GELU epilogue) and the joint attention over 1536 tokens x 24 heads
@@ -774,6 +777,57 @@ def run_av_step(dev: torch.device) -> None:
                       "video_tokens": f * h * w, "audio_tokens": ta,
                       "video_only_step_tflop": round(ltx_step_flops() / 1e12, 1),
                       "kernels": _kernel_shares(step)}))
+
+
+def run_kv_step(dev: torch.device) -> None:
+    """Klein KV editing at the reference's graph (4096 wide, 32 heads, 8 double + 24 single
+    blocks, SwiGLU): 512 text tokens, a 64 x 64 target and a 64 x 64 reference. Times the
+    extracting evaluation ([text | reference | target] rows, reference keys/values kept), a
+    reusing one ([text | target] rows against the kept rows) and a plain evaluation of the target
+    alone, each with its Euler update fused; 2 warm-up and 3 timed evaluations each."""
+    from kinomlx_b200 import ops
+    from kinomlx_b200.flux2 import config as fcfg
+    from kinomlx_b200.flux2.transformer import Flux2Transformer
+    from kinomlx_b200.synthetic import flux_weights, normal
+
+    v = fcfg.KLEIN
+    model = Flux2Transformer(flux_weights(v, seed=0, device=dev), v, dev)
+    torch.cuda.empty_cache()
+    nt, side = 512, 64
+    text_ids = torch.zeros((1, nt, 4), dtype=torch.int64)
+    text_ids[0, :, 3] = torch.arange(nt)
+    grid = torch.stack(torch.meshgrid(torch.arange(side), torch.arange(side), indexing="ij"), -1).reshape(1, -1, 2)
+    image_ids = torch.zeros((1, side * side, 4), dtype=torch.int64)
+    image_ids[..., 1:3] = grid
+    ref_ids = image_ids.clone()
+    ref_ids[..., 0] = 10
+    text = normal((1, nt, v.context_dim), seed=1, device=dev)
+    extract, reuse = model.prepare_layouts(
+        text, (torch.cat([text_ids, ref_ids, image_ids], 1), torch.cat([text_ids, image_ids], 1)))
+    plain = model.prepare(text, torch.cat([text_ids, image_ids], 1))
+    nr = side * side
+    image = normal((1, 2 * nr, v.in_channels), seed=2, device=dev)  # [reference | target]
+    target = image[:, nr:]
+    cache = model.new_reference_kv(nr)
+    t, dt = 500.0, -0.25
+
+    def extracting():
+        cache.extracting = True
+        model.run(extract, image, t, euler_dt=dt, sample=target, out=target, reference_kv=cache)
+
+    def reusing():
+        cache.extracting = False
+        model.run(reuse, target, t, euler_dt=dt, sample=target, out=target, reference_kv=cache)
+
+    times = {}
+    for name, fn in (("extracting", extracting), ("reusing", reusing),
+                     ("plain_target", lambda: model.run(plain, target, t, euler_dt=dt,
+                                                        sample=target, out=target))):
+        times[name] = round(_time(fn, 2, 3, 1), 3)
+    ops.device_status()
+    cache.clear()
+    print(json.dumps({"kernel_case": "kv_step", "ok": True, "ms_per_evaluation": times,
+                      "text_tokens": nt, "target_tokens": nr, "reference_tokens": nr}))
 
 
 def run_bandwidth_case(dev: torch.device) -> None:
@@ -883,7 +937,7 @@ def main() -> None:
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
     ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow",
-                                              "bandwidth", "f32", "av_step"],
+                                              "bandwidth", "f32", "av_step", "kv_step"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     args = ap.parse_args()
     if args.kernel_case:
