@@ -428,6 +428,8 @@ class Flux2Transformer:
             if reference_kv.extracting:
                 nr = reference_kv.reference_tokens
                 target = (nr, ni - nr)
+        if target is not None and self.sp.size > 1:
+            raise ValueError("target rows need the whole sequence on one GPU")
         first, rows = (0, ni) if target is None else target
         if first < 0 or rows < 1 or first + rows > ni:
             raise ValueError(f"target rows {target} outside the {ni} image rows")
