@@ -90,6 +90,26 @@ def test_flux_f32_blocks_and_cfg_trajectory(monkeypatch):
         assert _max_rel(out - noise, expect - noise) < TOL
 
 
+def test_flux_f32_in_context_references(monkeypatch):
+    """The fp32 class under the in-context reference loop: [target | reference] rows, the target
+    rows' velocity only, with and without CFG."""
+    stand_in.install(monkeypatch)
+    v, w, text_ids = _flux_case("gelu_tanh", 16, 130)
+    noise = normal((1, 12, v.in_channels), seed=131, dtype=F32)
+    refs = normal((1, 6, v.in_channels), seed=132, dtype=F32)
+    ctx, neg = normal((1, 16, v.context_dim), seed=133, dtype=F32), normal((1, 16, v.context_dim), seed=134, dtype=F32)
+    ref_ids = fref.image_ids(2, 3, 4)
+    ref_ids[..., 0] = 10
+    ids = torch.cat([text_ids, fref.image_ids(3, 4, 4), ref_ids], 1)
+    model = Flux2TransformerF32(w, v, CPU)
+    for negative, g in ((None, 1.0), (neg, 2.5)):
+        expect = fref.denoise(w, noise, ctx, ids, fref.linear_sigmas(2), v, negative=negative,
+                              guidance=g, references=refs)
+        out = sampling.denoise(model, noise, ctx, ids, sigmas=sampling.linear_sigmas(2),
+                               negative=negative, guidance=g, references=refs)
+        assert _max_rel(out - noise, expect - noise) < TOL
+
+
 def test_ltx_f32_trajectory(monkeypatch):
     stand_in.install(monkeypatch)
     v = LTXVariant(dim=256, heads=2, context_dim=256, blocks=2)
