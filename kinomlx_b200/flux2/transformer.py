@@ -29,7 +29,7 @@ import torch
 from .. import ops
 from ..sequence_parallel import SequenceParallel
 from .config import FluxVariant
-from .kv import ReferenceKV
+from .kv import ReferenceKV, attend_rows
 
 BF = torch.bfloat16
 
@@ -195,24 +195,13 @@ class Flux2Transformer:
         return self._ws[key]
 
     # ------------------------------------------------------------------ blocks
-    def _attend(self, q, k, v, kv: ReferenceKV | None, layer: int) -> None:
-        """Self-attention written over q; a reusing KV edit adds the kept reference keys and
-        values as a second key segment (kinomlx/models/flux2/kv.py:69-75)."""
+    def _attend(self, q, k, v, kv: ReferenceKV | None, layer: int, nt: int = 0) -> None:
+        """Self-attention written over q; with a reference K/V cache, its extracting or reusing
+        form (kinomlx/models/flux2/kv.py:57-80)."""
         if kv is None:
             self.sp.attention(q, k, v, q, heads=self.v.heads)
             return
-        rk, rv = kv.tensors(layer)
-        ops.attention([q], [k, rk], [v, rv], [q], heads=self.v.heads)
-
-    def _attend_extracting(self, q, k, v, nt: int, kv: ReferenceKV, layer: int) -> None:
-        """[text | reference | target] rows: keep the reference keys/values, then text and
-        target queries attend to every key and reference queries to the reference keys only
-        (kinomlx/models/flux2/kv.py:76-80). Outputs are written over q."""
-        h = self.v.heads
-        r0, r1 = nt, nt + kv.reference_tokens
-        kv.keep(layer, k[:, r0:r1], v[:, r0:r1])
-        ops.attention([q[:, :r0], q[:, r1:]], [k], [v], [q[:, :r0], q[:, r1:]], heads=h)
-        ops.attention([q[:, r0:r1]], [k[:, r0:r1]], [v[:, r0:r1]], [q[:, r0:r1]], heads=h)
+        attend_rows(q, k, v, q, heads=self.v.heads, text_tokens=nt, state=kv, layer=layer)
 
     def _double_block(self, ws: _Workspace, p: dict, rope: ops.RopeTables,
                       kv: ReferenceKV | None = None, layer: int = 0) -> None:
@@ -310,7 +299,7 @@ class Flux2Transformer:
                    qk_norm=[(0, p["norm_added_q"]), (d, p["norm_added_k"])], norm_width=d,
                    rope=(rope, 0))
         q, k, v = ws.qkv[..., :d], ws.qkv[..., d : 2 * d], ws.qkv[..., 2 * d :]
-        self._attend_extracting(q, k, v, nt, kv, layer)
+        self._attend(q, k, v, kv, layer, nt)
         for a, b, mod in image_rows:
             rows = ws.stream[:, a:b]
             ops.linear(q[:, a:b], p["to_out"], rows, kind=ops.EPI_GATED_RESIDUAL, residual=rows,
@@ -366,7 +355,7 @@ class Flux2Transformer:
         ops.linear(ws.nrm, p["fused"], ws.big, kind=self.act_kind, act_col_begin=3 * d,
                    qk_norm=[(0, p["norm_k"]), (2 * d, p["norm_q"])], norm_width=d, rope=(rope, 0))
         k, v, q = ws.big[..., :d], ws.big[..., d : 2 * d], ws.big[..., 2 * d : 3 * d]
-        self._attend_extracting(q, k, v, nt, kv, layer)
+        self._attend(q, k, v, kv, layer, nt)
         for a, b, mod in parts:
             rows = ws.stream[:, a:b]
             ops.linear(ws.big[:, a:b, 2 * d :], p["to_out"], rows, kind=ops.EPI_GATED_RESIDUAL,

@@ -125,3 +125,22 @@ def test_denoise_kv_refuses_mismatched_inputs(monkeypatch):
     with pytest.raises(ValueError, match="no reference K/V path"):
         sampling.denoise_kv(object(), c["noise"], c["text"], c["text_ids"], c["image_ids"],
                             c["references"], c["reference_ids"], sigmas=sig)
+
+
+def test_reference_attention_function_matches_oracle(monkeypatch):
+    """The reference-shaped function on the reference test's geometry (9 rows: 2 text, 3
+    reference, 4 target) with 128-wide heads: extraction against the oracle, reuse on the active
+    rows against the extraction's rows."""
+    from kinomlx_b200.flux2.kv import reference_attention
+
+    stand_in.install(monkeypatch)
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn((1, 9, 2, 128), generator=g) for _ in range(3))
+    expect = fref.reference_attention(q, k, v, text_tokens=2, state=fref.ReferenceKV(3, 1), layer=0)
+    state = ReferenceKV(3, 1, 1, 256, CPU, F32)
+    out = reference_attention(q, k, v, text_tokens=2, state=state, layer=0)
+    assert out.shape == q.shape and float((out - expect).abs().max()) < 1e-5
+    state.extracting = False
+    active = torch.tensor([0, 1, 5, 6, 7, 8])
+    again = reference_attention(q[:, active], k[:, active], v[:, active], text_tokens=2, state=state, layer=0)
+    assert float((again - out[:, active]).abs().max()) < 1e-5

@@ -172,3 +172,25 @@ def test_in_context_reference_trajectory_matches_oracle(cuda_device):
                            references=c["refs"])
     rel, cos = _metrics(out, expect)
     assert out.shape == c["noise"].shape and cos >= 0.999 and rel <= 3e-2, (rel, cos)
+
+
+def test_reference_attention_function_matches_oracle(cuda_device):
+    """The reference-shaped function on the reference test's geometry (2 text, 3 reference, 4
+    target rows; here 128-wide heads and bf16): extraction against the fp32 oracle, reuse on the
+    active rows against the extraction's rows."""
+    from kinomlx_b200.flux2.kv import ReferenceKV, reference_attention
+
+    q, k, v = (normal((1, 9, 2, 128), seed=90 + i) for i in range(3))
+    expect = ref.reference_attention(q.float(), k.float(), v.float(), text_tokens=2,
+                                     state=ref.ReferenceKV(3, 1), layer=0)
+    state = ReferenceKV(3, 1, 1, 256, cuda_device, BF)
+    out = reference_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                              text_tokens=2, state=state, layer=0)
+    rel, cos = _metrics(out, expect)
+    assert out.shape == q.shape and rel <= 1e-2 and cos >= 0.9999, (rel, cos)
+    state.extracting = False
+    active = torch.tensor([0, 1, 5, 6, 7, 8])
+    again = reference_attention(q[:, active].to(cuda_device), k[:, active].to(cuda_device),
+                                v[:, active].to(cuda_device), text_tokens=2, state=state, layer=0)
+    rel, cos = _metrics(again, out[:, active.to(cuda_device)])
+    assert rel <= 1e-2, (rel, cos)
