@@ -1,8 +1,10 @@
-"""Host logic of the device KV-editing path on the CPU (kernel calls replaced by the torch
-stand-ins of tests/stand_in_kernels.py): the cache's lifetime when the loop fails or is
-interrupted, the extraction/reuse sequence the loop drives, and the refusals of
+"""Host logic of the device reference paths on the CPU (kernel calls replaced by the torch
+stand-ins of tests/stand_in_kernels.py): for KV editing, the cache's lifetime when the loop fails
+or is interrupted, the extraction/reuse sequence the loop drives, and the refusals of
 `Flux2Transformer.run` and `sampling.denoise_kv`, which follow the reference's
-(kinomlx/models/flux2/transformer.py:321-332, sampling.py:133-165, kv.py:30-45)."""
+(kinomlx/models/flux2/transformer.py:321-332, sampling.py:133-165, kv.py:30-45); for in-context
+references, the reference sampling test's known answer (tests/models/flux2/test_sampling.py:
+150-169) and its refusal of references without positions."""
 
 from __future__ import annotations
 
@@ -144,3 +146,56 @@ def test_reference_attention_function_matches_oracle(monkeypatch):
     active = torch.tensor([0, 1, 5, 6, 7, 8])
     again = reference_attention(q[:, active], k[:, active], v[:, active], text_tokens=2, state=state, layer=0)
     assert float((again - out[:, active]).abs().max()) < 1e-5
+
+
+class _TextVelocity:
+    """The reference sampling test's stand-in model (tests/models/flux2/test_sampling.py:136-142):
+    every row's velocity is the first value of its batch entry's text; it records each image it
+    is given. Runs the `Flux2Transformer.run` contract (fused Euler, target rows)."""
+
+    device, dtype = CPU, F32
+
+    def __init__(self):
+        from kinomlx_b200.sequence_parallel import SequenceParallel
+
+        self.sp = SequenceParallel.single()
+        self.inputs = []
+
+    def prepare(self, text, ids):
+        return text
+
+    def run(self, prepared, image, t, *, euler_dt=None, sample=None, out=None, target=None):
+        self.inputs.append(image.clone())
+        first, rows = target or (0, image.shape[1])
+        velocity = torch.ones_like(image[:, first : first + rows]) * prepared[:, :1, :1]
+        if euler_dt is None:
+            return velocity
+        out.copy_(sample + euler_dt * velocity)
+        return out
+
+
+@pytest.mark.parametrize("guidance", [1.0, 4.0])
+def test_cfg_updates_only_targets_and_keeps_references_fixed(monkeypatch, guidance):
+    """The reference's known answer: with negative = -text and guidance 4 the combined velocity
+    is -1 + 4 * 2 = 7, so a schedule from 1 to 0 ends at -7 (at guidance 1, -1); the reference
+    rows every evaluation sees stay 17."""
+    stand_in.install(monkeypatch)
+    model = _TextVelocity()
+    noise, text = torch.zeros((1, 4, 32)), torch.ones((1, 2, 64))
+    ids = torch.zeros((1, 2 + 4 + 3, 4), dtype=torch.int64)
+    result = sampling.denoise(model, noise, text, ids, sigmas=sampling.schedule(4, 4),
+                              negative=-text if guidance != 1.0 else None, guidance=guidance,
+                              references=torch.full((1, 3, 32), 17.0))
+    assert result.shape == noise.shape
+    assert float((result + (7.0 if guidance != 1.0 else 1.0)).abs().max()) < 1e-6
+    assert len(model.inputs) == 4 and all(bool((seen[:, 4:] == 17).all()) for seen in model.inputs)
+
+
+def test_references_without_their_positions_fail_before_any_evaluation(monkeypatch):
+    stand_in.install(monkeypatch)
+    model = _TextVelocity()
+    with pytest.raises(ValueError, match="positions must match"):
+        sampling.denoise(model, torch.zeros((1, 4, 32)), torch.ones((1, 2, 64)),
+                         torch.zeros((1, 6, 4), dtype=torch.int64), sigmas=sampling.schedule(4, 4),
+                         references=torch.zeros((1, 1, 32)))
+    assert not model.inputs
