@@ -3,7 +3,10 @@
  * KinoMLX (the Flux2-style MMDiT, the LTX-2 video DiT block and the tiled conv VAE decoder).
  *
  * Conventions
- *   - All tensors are caller-owned device pointers; nothing here allocates device memory.
+ *   - All tensors are caller-owned device pointers. The compute entry points allocate no device
+ *     memory; the exceptions are kino_peer_alloc (cudaMalloc of a buffer shared with the other
+ *     GPUs of a sequence-parallel group, freed by kino_peer_free) and the fixed scratch array of
+ *     kino_group_norm_noalloc, which lives in the library's image rather than being allocated.
  *   - bf16 activations and weights, fp32 rope tables; "ld" is a row stride and "bs" a batch
  *     stride, both in elements. Row strides of TMA-read operands must be multiples of 8.
  *   - `stream` is a cudaStream_t (NULL = legacy default stream). Every call is asynchronous.
@@ -30,7 +33,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (9); bumped on any signature change. */
+/* ABI version of this header (10); bumped on any signature change or addition. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -263,6 +266,17 @@ kino_status kino_euler_velocity(const void* x, const void* v, float dt, void* ou
 kino_status kino_euler_x0(const void* x, const void* v, float sigma, float ratio, void* out,
                           int64_t n, void* stream);
 
+/* Deterministic Euler on a denoised prediction: out = bf16(d + ratio * (x - d)) in fp32 with
+ * ratio = fp32(sigma_next / sigma) (replaces kinomlx/samplers/steps.py:36-70 `euler_step`).
+ * n % 8 == 0, 16-byte aligned operands. */
+kino_status kino_euler_step(const void* sample, const void* denoised, float ratio, void* out,
+                            int64_t n, void* stream);
+
+/* Velocity Euler: out = bf16(x + bf16(delta * f32(v))), delta = fp32(sigma_next - sigma)
+ * (replaces kinomlx/samplers/steps.py:8-33 `euler_velocity_step`). n % 8 == 0. */
+kino_status kino_euler_velocity_step(const void* sample, const void* velocity, float delta,
+                                     void* out, int64_t n, void* stream);
+
 /* out[r, c] = bf16(a[r, c] + b[c]); a: rows x n, b: n. The per-block modulation tables plus the
  * step's timestep projection (kinomlx/models/ltx2/transformer/transformer.py:178-186). n % 8 == 0. */
 kino_status kino_add_rows(const void* a, const void* b, void* out, int64_t rows, int64_t n,
@@ -383,7 +397,10 @@ kino_status kino_group_norm_from_stats(const void* x, const void* weight, const 
  * Its statistics scratch is one fixed array inside the library (the size above), which every GPU
  * that loads the library keeps until the process exits; nothing is allocated per call. The first
  * call on each device looks up that array's device address (cudaGetSymbolAddress) with the device
- * current; make that first call before any stream capture. Every call shares the one array and
+ * current; make that first call before any stream capture. A device reset (cudaDeviceReset, or a
+ * primary context released and created again) unloads the array with the module: the next call
+ * in the new context looks the address up again, so that call, too, belongs outside a capture.
+ * Every call shares the one array and
  * leaves its contents behind: each call writes every scratch word before reading it, so no
  * clearing is needed, but calls that overlap on the GPU (for example on two streams) race on the
  * array and must be serialised by the caller. Shapes needing more scratch than the maximum are
@@ -411,6 +428,134 @@ kino_status kino_tile_blend(const void* decoded, int64_t frames, int64_t height,
 /* canvas[p, y, x] /= max(weights[y, x], 1e-8) (kinomlx/models/ltx2/video_vae/tiling.py:1369). */
 kino_status kino_blend_normalize(float* canvas, const float* weights, int64_t planes, int64_t hw,
                                  void* stream);
+
+/* ------------------------------------------------------------------ whole blocks
+ * One call per transformer block for hosts that drive the path without Python: the launch
+ * sequence of the block over the entry points above, on the caller's stream, with weights,
+ * activations, modulation vectors, RoPE tables and a scratch workspace all owned by the caller.
+ * The results are bit-identical to the same launches issued one by one. Weights are bf16
+ * (out, in) row-major, prepared once at load time as described per field. */
+#define KINO_MLP_GELU_TANH 0   /* GELU-tanh MLP (BASELINE) */
+#define KINO_MLP_SWIGLU 1      /* SwiGLU, gate rows first (Klein) */
+
+typedef struct kino_flux_block_shape {
+  int64_t batch;
+  int64_t text_tokens;   /* Nt: rows [0, Nt) of every batch entry are text */
+  int64_t image_tokens;  /* Ni: rows [Nt, Nt + Ni) are image */
+  int64_t heads;         /* D = heads * 128 */
+  int64_t mlp_hidden;    /* activation width entering the MLP down projection, % 32 == 0 */
+  int mlp;               /* KINO_MLP_* */
+  float eps;             /* LayerNorm and QK RMSNorm epsilon (1e-6 in the reference) */
+} kino_flux_block_shape;
+
+/* Pair-RoPE tables of the joint [text | image] rows, head-dim-major (128, T), T = (batched ?
+ * batch : 1) * rows: row i of batch entry b reads column (batched ? b * rows : 0) + i. */
+typedef struct kino_rope_tables {
+  const float* cos;
+  const float* sin;
+  int64_t rows;
+  int batched;
+} kino_rope_tables;
+
+typedef struct kino_flux_double_weights {
+  const void* img_qkv;       /* (3D, D): rows [attn.to_q; attn.to_k; attn.to_v] */
+  const void* txt_qkv;       /* (3D, D): rows [attn.add_q_proj; add_k_proj; add_v_proj] */
+  const void* to_out;        /* (D, D) attn.to_out.0 */
+  const void* to_add_out;    /* (D, D) attn.to_add_out */
+  const void* norm_q;        /* (128) attn.norm_q, norm_k, norm_added_q, norm_added_k */
+  const void* norm_k;
+  const void* norm_added_q;
+  const void* norm_added_k;
+  const void* ff_in;         /* (mlp_in, D) ff.linear_in (SwiGLU: rows in blocks of 16 gate +
+                                16 content, the KINO_EPI_SWIGLU order) */
+  const void* ff_out;        /* (D, mlp_hidden) ff.linear_out */
+  const void* ffc_in;        /* the text stream's ff_context.linear_in / linear_out */
+  const void* ffc_out;
+} kino_flux_double_weights;
+
+typedef struct kino_flux_single_weights {
+  const void* fused;         /* (3D + mlp_in, D): attn.to_qkv_mlp_proj with its row blocks
+                                reordered [k; v; q; mlp] (SwiGLU mlp rows interleaved as above) */
+  const void* to_out;        /* (D, D + mlp_hidden) attn.to_out */
+  const void* norm_q;        /* (128) */
+  const void* norm_k;
+} kino_flux_single_weights;
+
+/* Bytes of workspace a double or single block of this shape needs (-1 for an invalid shape). */
+int64_t kino_flux_block_workspace_size(const kino_flux_block_shape* shape);
+
+/* One Flux2 DoubleBlock in place on hidden (B, Nt + Ni, D) bf16, text rows then image rows.
+ * modulation: (B, 12 D) bf16 at batch stride bs_modulation (0: one vector for every entry),
+ * the image stream's [shift, scale, gate, ff_shift, ff_scale, ff_gate] then the text stream's.
+ * Replaces DoubleBlock / DoubleAttention (kinomlx/models/flux2/transformer.py:88-167). */
+kino_status kino_flux_double_block(const kino_flux_block_shape* shape,
+                                   const kino_flux_double_weights* weights, void* hidden,
+                                   const void* modulation, int64_t bs_modulation,
+                                   const kino_rope_tables* rope, void* workspace,
+                                   int64_t workspace_bytes, void* stream);
+
+/* One Flux2 SingleBlock in place on hidden (B, Nt + Ni, D); modulation (B, 3 D):
+ * [shift, scale, gate]. Replaces SingleBlock / SingleAttention
+ * (kinomlx/models/flux2/transformer.py:170-220). */
+kino_status kino_flux_single_block(const kino_flux_block_shape* shape,
+                                   const kino_flux_single_weights* weights, void* hidden,
+                                   const void* modulation, int64_t bs_modulation,
+                                   const kino_rope_tables* rope, void* workspace,
+                                   int64_t workspace_bytes, void* stream);
+
+typedef struct kino_ltx_block_shape {
+  int64_t batch;
+  int64_t tokens;          /* video tokens T */
+  int64_t context_tokens;  /* text tokens Tc */
+  int64_t heads;           /* D = heads * 128 */
+  int64_t context_dim;     /* width of the text context (= D) */
+  int64_t ff_hidden;       /* feed-forward width (4 D) */
+  float eps;               /* RMSNorm epsilon (1e-6) */
+} kino_ltx_block_shape;
+
+typedef struct kino_ltx_video_block_weights {
+  const void* qkv_w;       /* (3D, D): rows [attn1.to_v; attn1.to_q; attn1.to_k]; bias (3D) */
+  const void* qkv_b;
+  const void* g1_w;        /* (heads, D) attn1.to_gate_logits and its bias */
+  const void* g1_b;
+  const void* o1_w;        /* (D, D) attn1.to_out and bias */
+  const void* o1_b;
+  const void* qn1;         /* (D) attn1.q_norm / k_norm */
+  const void* kn1;
+  const void* q2_w;        /* (D, D) attn2.to_q and bias */
+  const void* q2_b;
+  const void* kv2_w;       /* (2D, context_dim): rows [attn2.to_k; attn2.to_v]; bias (2D) */
+  const void* kv2_b;
+  const void* g2_w;        /* attn2.to_gate_logits, to_out, q_norm, k_norm as above */
+  const void* g2_b;
+  const void* o2_w;
+  const void* o2_b;
+  const void* qn2;
+  const void* kn2;
+  const void* ff_in_w;     /* (ff_hidden, D) ff.project_in.proj and bias */
+  const void* ff_in_b;
+  const void* ff_out_w;    /* (D, ff_hidden) ff.project_out and bias */
+  const void* ff_out_b;
+} kino_ltx_video_block_weights;
+
+/* Bytes of workspace kino_ltx_video_block needs (-1 for an invalid shape). */
+int64_t kino_ltx_video_block_workspace_size(const kino_ltx_block_shape* shape);
+
+/* One LTX-2 video block in place on hidden (B, T, D): gated self-attention (full-row QK RMSNorm,
+ * split RoPE from the (1|B, heads, T, 64) fp32 tables rope_cos / rope_sin), gated text
+ * cross-attention on the prompt-modulated context (B, Tc, D), GELU feed-forward, AdaLN-modulated
+ * gated residuals. values: (B, 9 D) = the block's scale_shift_table plus the step's timestep
+ * projection, rows (shift, scale, gate) x {attention, feed-forward} then (shift, scale, gate) of
+ * the cross-attention query; prompt: (B, 2 D) = prompt_scale_shift_table plus the prompt
+ * timestep projection, (shift, scale). Replaces the video path of BasicAVTransformerBlock
+ * (kinomlx/models/ltx2/transformer/transformer.py:16-45, 178-276) with its Attention
+ * (attention.py:249-371) and FeedForward (feed_forward.py:11-100). */
+kino_status kino_ltx_video_block(const kino_ltx_block_shape* shape,
+                                 const kino_ltx_video_block_weights* weights, void* hidden,
+                                 const void* context, const void* values, int64_t bs_values,
+                                 const void* prompt, int64_t bs_prompt, const float* rope_cos,
+                                 const float* rope_sin, int rope_batched, void* workspace,
+                                 int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------ fp32 parity mode
  * The Flux2 block operators in single precision on the CUDA cores, for the reference's fp32
@@ -492,6 +637,10 @@ kino_status kino_cfg_combine_f32(const float* cond, const float* uncond, float g
 /* out = x + dt * v (kinomlx/models/flux2/sampling.py:109-113 with the model dtype fp32). */
 kino_status kino_euler_velocity_f32(const float* x, const float* v, float dt, float* out,
                                     int64_t n, void* stream);
+
+/* out = d + ratio * (x - d) in fp32 (kinomlx/samplers/steps.py:36-70 with an fp32 sample). */
+kino_status kino_euler_step_f32(const float* sample, const float* denoised, float ratio,
+                               float* out, int64_t n, void* stream);
 
 /* out[b, r, c] = silu(x[b, r, c]) * x[b, r, width + c], gate half first
  * (kinomlx/models/flux2/transformer.py:63-65); out may alias x. */

@@ -165,6 +165,55 @@ class EpilogueF32(ctypes.Structure):
     ]
 
 
+class FluxBlockShape(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int64),
+        ("text_tokens", c_int64),
+        ("image_tokens", c_int64),
+        ("heads", c_int64),
+        ("mlp_hidden", c_int64),
+        ("mlp", c_int),
+        ("eps", c_float),
+    ]
+
+
+class RopeTablesArgs(ctypes.Structure):
+    _fields_ = [("cos", c_void_p), ("sin", c_void_p), ("rows", c_int64), ("batched", c_int)]
+
+
+class FluxDoubleWeights(ctypes.Structure):
+    _fields_ = [(name, c_void_p) for name in (
+        "img_qkv", "txt_qkv", "to_out", "to_add_out", "norm_q", "norm_k", "norm_added_q",
+        "norm_added_k", "ff_in", "ff_out", "ffc_in", "ffc_out")]
+
+
+class FluxSingleWeights(ctypes.Structure):
+    _fields_ = [(name, c_void_p) for name in ("fused", "to_out", "norm_q", "norm_k")]
+
+
+class LTXBlockShape(ctypes.Structure):
+    _fields_ = [
+        ("batch", c_int64),
+        ("tokens", c_int64),
+        ("context_tokens", c_int64),
+        ("heads", c_int64),
+        ("context_dim", c_int64),
+        ("ff_hidden", c_int64),
+        ("eps", c_float),
+    ]
+
+
+class LTXVideoBlockWeights(ctypes.Structure):
+    _fields_ = [(name, c_void_p) for name in (
+        "qkv_w", "qkv_b", "g1_w", "g1_b", "o1_w", "o1_b", "qn1", "kn1", "q2_w", "q2_b", "kv2_w",
+        "kv2_b", "g2_w", "g2_b", "o2_w", "o2_b", "qn2", "kn2", "ff_in_w", "ff_in_b", "ff_out_w",
+        "ff_out_b")]
+
+
+MLP_GELU_TANH = 0
+MLP_SWIGLU = 1
+
+
 class IpcHandle(ctypes.Structure):
     _fields_ = [("bytes", ctypes.c_ubyte * 64)]
 
@@ -202,6 +251,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_cfg_combine": (c_int, [P, P, F, P, I64, P]),
     "kino_euler_velocity": (c_int, [P, P, F, P, I64, P]),
     "kino_euler_x0": (c_int, [P, P, F, F, P, I64, P]),
+    "kino_euler_step": (c_int, [P, P, F, P, I64, P]),
+    "kino_euler_velocity_step": (c_int, [P, P, F, P, I64, P]),
     "kino_add_rows": (c_int, [P, P, P, I64, I64, P]),
     "kino_heads_pack": (c_int, [P, I64, P, I64, I64, I64, P]),
     "kino_heads_unpack": (c_int, [P, P, I64, I64, I64, I64, P, I64, P]),
@@ -237,6 +288,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_silu_f32": (c_int, [P, P, I64, P]),
     "kino_cfg_combine_f32": (c_int, [P, P, F, P, I64, P]),
     "kino_euler_velocity_f32": (c_int, [P, P, F, P, I64, P]),
+    "kino_euler_step_f32": (c_int, [P, P, F, P, I64, P]),
     "kino_swiglu_f32": (c_int, [P, I64, I64, P, I64, I64, I64, I64, I64, P]),
     "kino_timestep_embedding_f32": (c_int, [P, P, I64, I64, P]),
     "kino_conv3d_f32": (
@@ -247,6 +299,23 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_group_norm_f32": (c_int, [P, P, P, P, I64, I64, F, c_int, P]),
     "kino_latent_to_bfhwc_f32": (c_int, [P, P, P, P, I64, I64, P]),
     "kino_tile_blend_f32": (c_int, [P, I64, I64, I64, I64, I64, P, P, I64, I64, I64, I64, P, P, P]),
+    "kino_flux_block_workspace_size": (I64, [POINTER(FluxBlockShape)]),
+    "kino_flux_double_block": (
+        c_int,
+        [POINTER(FluxBlockShape), POINTER(FluxDoubleWeights), P, P, I64, POINTER(RopeTablesArgs),
+         P, I64, P],
+    ),
+    "kino_flux_single_block": (
+        c_int,
+        [POINTER(FluxBlockShape), POINTER(FluxSingleWeights), P, P, I64, POINTER(RopeTablesArgs),
+         P, I64, P],
+    ),
+    "kino_ltx_video_block_workspace_size": (I64, [POINTER(LTXBlockShape)]),
+    "kino_ltx_video_block": (
+        c_int,
+        [POINTER(LTXBlockShape), POINTER(LTXVideoBlockWeights), P, P, P, I64, P, I64, P, P, c_int,
+         P, I64, P],
+    ),
     "kino_peer_alloc": (c_int, [I64, POINTER(c_void_p), POINTER(IpcHandle)]),
     "kino_peer_free": (c_int, [P]),
     "kino_peer_open": (c_int, [POINTER(IpcHandle), POINTER(c_void_p)]),

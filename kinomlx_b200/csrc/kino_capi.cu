@@ -429,9 +429,41 @@ int gn_parts(int64_t voxels) {
   return static_cast<int>(p < 592 ? (p < 1 ? 1 : p) : 592);
 }
 
+// The id of the calling thread's current context (cuCtxGetId through the runtime's driver entry
+// point), or 0 when there is none or the driver lacks the call. A device reset destroys the
+// primary context and the module with it, so a cached symbol address is only valid for the
+// context it was looked up in.
+unsigned long long current_context_id() {
+  using GetCurrent = int (*)(void**);
+  using GetId = int (*)(void*, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  void* ctx = nullptr;
+  if (get_current(&ctx) != 0 || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  return get_id(ctx, &id) == 0 ? id : 0;
+}
+
+// Device address of g_group_norm_scratch for the current device, looked up with that device
+// current the first time a context uses it and cached per device with the context's id; a new
+// context on the device (after cudaDeviceReset) looks it up again.
 void* group_norm_scratch_address(kino_status* status) {
   static std::mutex lock;
   static void* addresses[64] = {nullptr};
+  static unsigned long long contexts[64] = {0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) {
@@ -440,7 +472,8 @@ void* group_norm_scratch_address(kino_status* status) {
     return nullptr;
   }
   std::lock_guard<std::mutex> guard(lock);
-  if (addresses[dev] == nullptr) {
+  const unsigned long long ctx = current_context_id();
+  if (addresses[dev] == nullptr || ctx == 0 || ctx != contexts[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_group_norm_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -449,6 +482,7 @@ void* group_norm_scratch_address(kino_status* status) {
       return nullptr;
     }
     addresses[dev] = p;
+    contexts[dev] = current_context_id();  // the lookup made the primary context current
   }
   *status = KINO_OK;
   return addresses[dev];
@@ -458,7 +492,7 @@ void* group_norm_scratch_address(kino_status* status) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 9; }
+int kino_abi_version(void) { return 10; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -947,6 +981,20 @@ kino_status kino_euler_x0(const void* x, const void* v, float sigma, float ratio
                           int64_t n, void* stream) {
   if (v == nullptr) return fail(KINO_EINVAL, "kino_euler_x0: null");
   return launch_elem(kino::ELEM_EULER_X0, x, v, out, n, sigma, ratio, stream, "kino_euler_x0");
+}
+
+kino_status kino_euler_step(const void* sample, const void* denoised, float ratio, void* out,
+                            int64_t n, void* stream) {
+  if (denoised == nullptr) return fail(KINO_EINVAL, "kino_euler_step: null");
+  return launch_elem(kino::ELEM_EULER_D, sample, denoised, out, n, 0.f, ratio, stream,
+                     "kino_euler_step");
+}
+
+kino_status kino_euler_velocity_step(const void* sample, const void* velocity, float delta,
+                                     void* out, int64_t n, void* stream) {
+  if (velocity == nullptr) return fail(KINO_EINVAL, "kino_euler_velocity_step: null");
+  return launch_elem(kino::ELEM_EULER_VS, sample, velocity, out, n, delta, 0.f, stream,
+                     "kino_euler_velocity_step");
 }
 
 kino_status kino_add_rows(const void* a, const void* b, void* out, int64_t rows, int64_t n,
@@ -1544,6 +1592,13 @@ kino_status kino_euler_velocity_f32(const float* x, const float* v, float dt, fl
   return launch_elem_f32(kino::ELEM32_EULER_V, x, v, out, n, dt, stream, "kino_euler_velocity_f32");
 }
 
+kino_status kino_euler_step_f32(const float* sample, const float* denoised, float ratio,
+                               float* out, int64_t n, void* stream) {
+  if (denoised == nullptr) return fail(KINO_EINVAL, "kino_euler_step_f32: null");
+  return launch_elem_f32(kino::ELEM32_EULER_D, sample, denoised, out, n, ratio, stream,
+                         "kino_euler_step_f32");
+}
+
 kino_status kino_swiglu_f32(const float* x, int64_t ldx, int64_t bsx, float* out, int64_t ldo,
                             int64_t bso, int64_t batch, int64_t rows, int64_t width,
                             void* stream) {
@@ -1675,3 +1730,5 @@ kino_status kino_tile_blend_f32(const float* decoded, int64_t frames, int64_t he
 }
 
 }  // extern "C"
+
+#include "kino_blocks.cuh"

@@ -548,6 +548,7 @@ constexpr int ELEM32_GELU = 0;
 constexpr int ELEM32_SILU = 1;
 constexpr int ELEM32_CFG = 2;      // a = cond, b = uncond: b + s0 * (a - b)
 constexpr int ELEM32_EULER_V = 3;  // a = sample, b = velocity: a + s0 * b
+constexpr int ELEM32_EULER_D = 4;  // a = sample, b = denoised: b + s0 * (a - b)
 
 __global__ void elementwise_f32_kernel(int kind, const float* a, const float* bsrc, float* out,
                                        int64_t n, float s0) {
@@ -567,6 +568,11 @@ __global__ void elementwise_f32_kernel(int kind, const float* a, const float* bs
       case ELEM32_CFG: {
         const float u = bsrc[i];
         y = __fadd_rn(u, __fmul_rn(s0, __fsub_rn(x, u)));
+        break;
+      }
+      case ELEM32_EULER_D: {
+        const float d = bsrc[i];
+        y = __fadd_rn(d, __fmul_rn(s0, __fsub_rn(x, d)));
         break;
       }
       default:

@@ -481,6 +481,8 @@ enum ElemKind : int {
   ELEM_CFG = 2,        // flux2/sampling.py:272: u + g * (p - u), bf16 ops
   ELEM_EULER_V = 3,    // flux2/sampling.py:109-113: x + bf16(bf16(dt) * v) in fp32
   ELEM_EULER_X0 = 4,   // ltx2 wrappers.py:49-65 + samplers/steps.py:36-70
+  ELEM_EULER_D = 5,    // samplers/steps.py:36-70: d + ratio * (x - d) in fp32
+  ELEM_EULER_VS = 6,   // samplers/steps.py:8-33: x + bf16(fp32 delta * v)
 };
 
 __global__ void elementwise_kernel(int kind, const __nv_bfloat16* __restrict__ a,
@@ -516,6 +518,12 @@ __global__ void elementwise_kernel(int kind, const __nv_bfloat16* __restrict__ a
           o[j] = __fadd_rn(d, __fmul_rn(s1, __fsub_rn(x[j], d)));
           break;
         }
+        case ELEM_EULER_D:  // a = sample, b = denoised, s1 = sigma_next / sigma
+          o[j] = __fadd_rn(y[j], __fmul_rn(s1, __fsub_rn(x[j], y[j])));
+          break;
+        case ELEM_EULER_VS:  // a = sample, b = velocity, s0 = sigma_next - sigma (fp32)
+          o[j] = __fadd_rn(x[j], bf16_round(__fmul_rn(s0, y[j])));
+          break;
         default:
           o[j] = x[j];
       }

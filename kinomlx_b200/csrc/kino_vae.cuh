@@ -110,15 +110,15 @@ __global__ void __launch_bounds__(256)
 constexpr int GN_GROUPS = 32;
 constexpr int GN_THREADS = 256;
 
-// pass 0: sum(x); pass 1: sum((x - mean)^2)
+// pass 0: sum(x); pass 1: sum((x - mean)^2). Each thread's eight channel sums are staged in
+// shared memory and thread g < 32 adds group g's entries in a fixed order (rows, then
+// channels), so the statistics, and every output bit, are the same on every run.
 __global__ void __launch_bounds__(GN_THREADS)
     group_norm_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t voxels, int C,
                               float* __restrict__ ws, int parts, int pass) {
   griddep_wait();
   griddep_launch();
-  __shared__ float gsum[GN_GROUPS];
-  if (threadIdx.x < GN_GROUPS) gsum[threadIdx.x] = 0.0f;
-  __syncthreads();
+  __shared__ float part[GN_THREADS * 8];
   const int vec_per_row = C >> 3;
   const int rows_per_iter = GN_THREADS / vec_per_row;  // C <= 2048
   const int cv = threadIdx.x % vec_per_row;
@@ -142,12 +142,17 @@ __global__ void __launch_bounds__(GN_THREADS)
         acc[j] += pass ? d * d : f[j];
       }
     }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) atomicAdd(&gsum[(cv * 8 + j) / gs], acc[j]);
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) part[threadIdx.x * 8 + j] = acc[j];
   __syncthreads();
-  if (threadIdx.x < GN_GROUPS) ws[static_cast<int64_t>(blockIdx.x) * GN_GROUPS + threadIdx.x] =
-      gsum[threadIdx.x];
+  if (threadIdx.x < GN_GROUPS) {
+    const int g = threadIdx.x;
+    float s = 0.0f;
+    for (int r = 0; r < rows_per_iter; ++r)
+      for (int c = g * gs; c < (g + 1) * gs; ++c) s += part[(r * vec_per_row + (c >> 3)) * 8 + (c & 7)];
+    ws[static_cast<int64_t>(blockIdx.x) * GN_GROUPS + g] = s;
+  }
 }
 
 // One CTA of 32 threads: reduce the partials of group g; pass 0 writes mean, pass 1 rstd.

@@ -359,7 +359,7 @@ class LTXAVTransformer:
         return outs[0], outs[1]
 
 
-def denoise_loop(model: LTXAVTransformer, video_latent, audio_latent, video_context,
+def denoise_av(model: LTXAVTransformer, video_latent, audio_latent, video_context,
                  audio_context, video_positions, audio_positions, sigmas):
     """The deterministic-Euler loop over both modalities (kinomlx/models/ltx2/denoise.py:261-365)."""
     prep = model.prepare(video_context, audio_context, video_positions, audio_positions)

@@ -56,7 +56,9 @@ __all__ = [
     "cfg_combine",
     "conv3d",
     "device_status",
+    "euler_denoised",
     "euler_velocity",
+    "euler_velocity_step",
     "euler_x0",
     "gelu_tanh",
     "gemv",
@@ -689,6 +691,34 @@ def euler_x0(
     out = torch.empty_like(x)
     ratio = float(torch.tensor(sigma_next / sigma, dtype=torch.float32))
     _elementwise("kino_euler_x0", _ptr(x), _ptr(v), sigma, ratio, _ptr(out), x.numel())
+    return out
+
+
+def euler_denoised(
+    x: torch.Tensor, denoised: torch.Tensor, sigma: float, sigma_next: float,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """denoised + fp32(sigma_next / sigma) * (x - denoised) in fp32, stored as bf16."""
+    _need(x, "x")
+    _need(denoised, "denoised")
+    if out is None:
+        out = torch.empty_like(x)
+    ratio = float(torch.tensor(sigma_next / sigma, dtype=torch.float32))
+    _elementwise("kino_euler_step", _ptr(x), _ptr(denoised), ratio, _ptr(out), x.numel())
+    return out
+
+
+def euler_velocity_step(
+    x: torch.Tensor, v: torch.Tensor, sigma: float, sigma_next: float,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """x + bf16(fp32(sigma_next - sigma) * v), stored as bf16."""
+    _need(x, "x")
+    _need(v, "v")
+    if out is None:
+        out = torch.empty_like(x)
+    delta = float(torch.tensor(sigma_next - sigma, dtype=torch.float32))
+    _elementwise("kino_euler_velocity_step", _ptr(x), _ptr(v), delta, _ptr(out), x.numel())
     return out
 
 

@@ -26,6 +26,7 @@ __all__ = [
     "cfg_combine",
     "conv3d",
     "euler_velocity",
+    "euler_denoised",
     "gelu_tanh",
     "group_norm",
     "latent_to_bfhwc",
@@ -243,6 +244,22 @@ def cfg_combine(cond: torch.Tensor, uncond: torch.Tensor, guidance: float,
     with _timed("elementwise_f32"):
         _lib.call("kino_cfg_combine_f32", _ptr(cond), _ptr(uncond), guidance, _ptr(out),
                   cond.numel(), _stream())
+    return out
+
+
+def euler_denoised(x: torch.Tensor, denoised: torch.Tensor, sigma: float, sigma_next: float,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """denoised + fp32(sigma_next / sigma) * (x - denoised) in fp32."""
+    _need(x, "x", F32)
+    _need(denoised, "denoised", F32)
+    if not (x.is_contiguous() and denoised.is_contiguous()):
+        raise ValueError("euler_denoised takes contiguous tensors")
+    if out is None:
+        out = torch.empty_like(x)
+    ratio = float(torch.tensor(sigma_next / sigma, dtype=torch.float32))
+    with _timed("elementwise_f32"):
+        _lib.call("kino_euler_step_f32", _ptr(x), _ptr(denoised), ratio, _ptr(out), x.numel(),
+                  _stream())
     return out
 
 

@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     for name in names:
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.kino_abi_version() == 9
+    assert lib.kino_abi_version() == 10
     assert _lib.last_error() == ""
 
 
@@ -134,3 +134,25 @@ def test_fp32_timestep_matches_oracle():
         != float(sampling.timestep_x1000(sig, i))
         for i in range(7)
     )
+
+
+def test_block_entry_workspace_sizes():
+    """The whole-block entries' workspace sizes (host arithmetic only, no device call)."""
+    import ctypes
+
+    from kinomlx_b200 import _lib
+
+    lib = _lib.load()
+    a = lambda n: (n + 255) // 256 * 256
+    s = _lib.FluxBlockShape(1, 512, 4096, 24, 12288, _lib.MLP_GELU_TANH, 1e-6)
+    rows, d = 4608, 3072
+    expect = a(rows * d * 2) + max(a(rows * 3 * d * 2) + a(rows * 12288 * 2), a(rows * (3 * d + 12288) * 2))
+    assert lib.kino_flux_block_workspace_size(ctypes.byref(s)) == expect
+    s.mlp_hidden = 100  # not a multiple of 32
+    assert lib.kino_flux_block_workspace_size(ctypes.byref(s)) == -1
+    assert "invalid shape" in _lib.last_error()
+    t = _lib.LTXBlockShape(1, 9216, 256, 32, 4096, 16384, 1e-6)
+    d = 4096
+    expect = (a(9216 * d * 2) + a(9216 * 16384 * 2) + a(9216 * 3 * d * 2) + a(9216 * 32 * 2)
+              + a(256 * d * 2) + a(256 * 2 * d * 2))
+    assert lib.kino_ltx_video_block_workspace_size(ctypes.byref(t)) == expect

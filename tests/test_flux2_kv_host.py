@@ -183,7 +183,7 @@ def test_cfg_updates_only_targets_and_keeps_references_fixed(monkeypatch, guidan
     model = _TextVelocity()
     noise, text = torch.zeros((1, 4, 32)), torch.ones((1, 2, 64))
     ids = torch.zeros((1, 2 + 4 + 3, 4), dtype=torch.int64)
-    result = sampling.denoise(model, noise, text, ids, sigmas=sampling.schedule(4, 4),
+    result = sampling.denoise_joint(model, noise, text, ids, sigmas=sampling.schedule(4, 4),
                               negative=-text if guidance != 1.0 else None, guidance=guidance,
                               references=torch.full((1, 3, 32), 17.0))
     assert result.shape == noise.shape
@@ -195,7 +195,7 @@ def test_references_without_their_positions_fail_before_any_evaluation(monkeypat
     stand_in.install(monkeypatch)
     model = _TextVelocity()
     with pytest.raises(ValueError, match="positions must match"):
-        sampling.denoise(model, torch.zeros((1, 4, 32)), torch.ones((1, 2, 64)),
+        sampling.denoise_joint(model, torch.zeros((1, 4, 32)), torch.ones((1, 2, 64)),
                          torch.zeros((1, 6, 4), dtype=torch.int64), sigmas=sampling.schedule(4, 4),
                          references=torch.zeros((1, 1, 32)))
     assert not model.inputs

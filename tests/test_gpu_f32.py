@@ -235,7 +235,7 @@ def test_denoise_f32_matches_oracle(cuda_device, cfg):
     guidance = 4.0 if cfg else 1.0
     expect = ref.denoise(w, noise, text, ids, sigmas, v, negative=negative, guidance=guidance)
     model = Flux2TransformerF32(w, v, cuda_device)
-    out = sampling.denoise(model, noise, text, ids, sigmas=sampling.linear_sigmas(3),
+    out = sampling.denoise_joint(model, noise, text, ids, sigmas=sampling.linear_sigmas(3),
                            negative=negative, guidance=guidance)
     assert out.dtype == F32
     assert _max_rel(out, expect) <= TOL, _max_rel(out, expect)
@@ -334,7 +334,7 @@ def test_ltx_denoise_f32(cuda_device):
     sigmas = lref.DISTILLED_STAGE_1_SIGMAS[5:]
     expect = lref.denoise(w, latent, context, pos, sigmas, v)
     model = LTXVideoTransformerF32(w, v, cuda_device)
-    out = ldn.denoise_loop(model, latent, context, pos, sigmas)
+    out = ldn.denoise_video(model, latent, context, pos, sigmas)
     assert out.dtype == F32
     assert _max_rel(out, expect) <= TOL, _max_rel(out, expect)
     assert _cos(out, expect) >= 0.999

@@ -98,7 +98,7 @@ def test_denoise_schedule_matches_oracle(cuda_device, cfg):
     expect = ref.denoise(w, noise, text, ids, sigmas, v, negative=negative,
                          guidance=4.0 if cfg else 1.0)
     model = Flux2Transformer(w, v, cuda_device)
-    out = sampling.denoise(model, noise, text, ids, sigmas=sampling.linear_sigmas(steps),
+    out = sampling.denoise_joint(model, noise, text, ids, sigmas=sampling.linear_sigmas(steps),
                            negative=negative, guidance=4.0 if cfg else 1.0)
     rel_l2, max_rel, cosine = _metrics(out, expect)
     assert cosine >= 0.999, (rel_l2, max_rel, cosine)
@@ -146,6 +146,6 @@ def test_klein_swiglu_variant_matches_oracle(cuda_device):
     sigmas = ref.schedule(h * wd, 2)
     expect = ref.denoise(w, noise, text, ids, sigmas, v)
     model = Flux2Transformer(w, v, cuda_device)
-    out = sampling.denoise(model, noise, text, ids, sigmas=sampling.schedule(h * wd, 2))
+    out = sampling.denoise_joint(model, noise, text, ids, sigmas=sampling.schedule(h * wd, 2))
     rel_l2, max_rel, cosine = _metrics(out, expect)
     assert cosine >= 0.999 and rel_l2 <= 3e-2, (rel_l2, max_rel, cosine)

@@ -65,7 +65,7 @@ def test_denoise_tail_matches_oracle(cuda_device):
     sigmas = ref.DISTILLED_STAGE_1_SIGMAS[5:]
     expect = ref.denoise(w, latent, context, pos, sigmas, v)
     model = LTXVideoTransformer(w, v, cuda_device)
-    out = ldn.denoise_loop(model, latent, context, pos, sigmas)
+    out = ldn.denoise_video(model, latent, context, pos, sigmas)
     rel_l2, max_rel, cos = _metrics(out, expect)
     assert cos >= 0.999 and rel_l2 <= 3e-2, (rel_l2, max_rel, cos)
 

@@ -92,7 +92,7 @@ def test_av_denoise_matches_oracle(cuda_device):
     ev, ea = ref.av_denoise(w, vlat, alat, vctx, actx, vpos, apos, sigmas,
                             _oracle_variant(video, audio), 2)
     model = avm.LTXAVTransformer(w, video, audio, cuda_device)
-    gv, ga = avm.denoise_loop(model, vlat, alat, vctx, actx, vpos, apos, sigmas)
+    gv, ga = avm.denoise_av(model, vlat, alat, vctx, actx, vpos, apos, sigmas)
     for out, exp in ((gv, ev), (ga, ea)):
         rel_l2, max_rel, cosine = _metrics(out, exp)
         assert cosine >= 0.999 and rel_l2 <= 3e-2, (rel_l2, max_rel, cosine)

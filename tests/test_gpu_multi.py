@@ -81,7 +81,7 @@ def _run(case: str, device, sp=None):
         v, w, noise, text, ids = _flux_case()
         negative = normal(tuple(text.shape), seed=45)
         model = Flux2Transformer(w, v, device)
-        return sampling.denoise(model, noise, text, ids, sigmas=sampling.linear_sigmas(3),
+        return sampling.denoise_joint(model, noise, text, ids, sigmas=sampling.linear_sigmas(3),
                                 negative=negative, guidance=4.0)
     if case == "flux":
         from kinomlx_b200.flux2 import sampling
@@ -89,13 +89,13 @@ def _run(case: str, device, sp=None):
 
         v, w, noise, text, ids = _flux_case()
         model = Flux2Transformer(w, v, device, sp=sp)
-        return sampling.denoise(model, noise, text, ids, sigmas=sampling.linear_sigmas(3))
+        return sampling.denoise_joint(model, noise, text, ids, sigmas=sampling.linear_sigmas(3))
     from kinomlx_b200.ltx2 import denoise as ldn
     from kinomlx_b200.ltx2.transformer import LTXVideoTransformer
 
     v, w, latent, context, pos = _ltx_case()
     model = LTXVideoTransformer(w, v, device, sp=sp)
-    return ldn.denoise_loop(model, latent, context, pos, sigmas=ldn.DISTILLED_STAGE_1_SIGMAS[5:])
+    return ldn.denoise_video(model, latent, context, pos, sigmas=ldn.DISTILLED_STAGE_1_SIGMAS[5:])
 
 
 def _worker(rank: int, size: int, port: int, case: str, queue) -> None:

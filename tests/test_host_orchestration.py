@@ -85,7 +85,7 @@ def test_flux_f32_blocks_and_cfg_trajectory(monkeypatch):
         ctx, neg = normal((1, nt, v.context_dim), seed=74, dtype=F32), normal((1, nt, v.context_dim), seed=75, dtype=F32)
         sig = fref.linear_sigmas(2)
         expect = fref.denoise(w, noise, ctx, ids, sig, v, negative=neg, guidance=3.0)
-        out = sampling.denoise(model, noise, ctx, ids, sigmas=sampling.linear_sigmas(2),
+        out = sampling.denoise_joint(model, noise, ctx, ids, sigmas=sampling.linear_sigmas(2),
                                negative=neg, guidance=3.0)
         assert _max_rel(out - noise, expect - noise) < TOL
 
@@ -105,7 +105,7 @@ def test_flux_f32_in_context_references(monkeypatch):
     for negative, g in ((None, 1.0), (neg, 2.5)):
         expect = fref.denoise(w, noise, ctx, ids, fref.linear_sigmas(2), v, negative=negative,
                               guidance=g, references=refs)
-        out = sampling.denoise(model, noise, ctx, ids, sigmas=sampling.linear_sigmas(2),
+        out = sampling.denoise_joint(model, noise, ctx, ids, sigmas=sampling.linear_sigmas(2),
                                negative=negative, guidance=g, references=refs)
         assert _max_rel(out - noise, expect - noise) < TOL
 
@@ -119,7 +119,7 @@ def test_ltx_f32_trajectory(monkeypatch):
     pos = lref.pixel_coords(lref.patch_grid_bounds(2, 3, 4))
     sigmas = lref.DISTILLED_STAGE_1_SIGMAS[5:]
     expect = lref.denoise(w, latent, context, pos, sigmas, v)
-    out = ldn.denoise_loop(LTXVideoTransformerF32(w, v, CPU), latent, context, pos, sigmas)
+    out = ldn.denoise_video(LTXVideoTransformerF32(w, v, CPU), latent, context, pos, sigmas)
     assert _max_rel(out - latent, expect - latent) < TOL
 
 
@@ -134,7 +134,7 @@ def test_ltx_bf16_class_trajectory(monkeypatch):
     pos = lref.pixel_coords(lref.patch_grid_bounds(2, 3, 4))
     sigmas = lref.DISTILLED_STAGE_1_SIGMAS[5:]
     expect = lref.denoise(w, latent, context, pos, sigmas, v)
-    out = ldn.denoise_loop(LTXVideoTransformer(w, v, CPU), latent, context, pos, sigmas)
+    out = ldn.denoise_video(LTXVideoTransformer(w, v, CPU), latent, context, pos, sigmas)
     assert _max_rel(out - latent, expect - latent) < TOL
 
 
@@ -186,7 +186,7 @@ def test_av_model_trajectory(monkeypatch):
     # a gate scale apart from the timestep scale (both 1000 by default) tells the two apart
     ev, ea = lref.av_denoise(w, vlat, alat, vctx, actx, vpos, apos, sigmas,
                              lref.LTXAVVariant(pick(video), pick(audio), av_gate_scale=250.0), 2)
-    gv, ga = avm.denoise_loop(avm.LTXAVTransformer(w, video, audio, CPU, av_gate_scale=250.0),
+    gv, ga = avm.denoise_av(avm.LTXAVTransformer(w, video, audio, CPU, av_gate_scale=250.0),
                               vlat, alat, vctx, actx, vpos, apos, sigmas)
     assert _max_rel(gv - vlat, ev - vlat) < TOL and _max_rel(ga - alat, ea - alat) < TOL
 
@@ -229,7 +229,7 @@ def test_flux_bf16_class_blocks_cfg_and_references(monkeypatch):
         ctx, neg = normal((1, nt, v.context_dim), seed=104, dtype=F32), normal((1, nt, v.context_dim), seed=105, dtype=F32)
         sig = fref.linear_sigmas(2)
         expect = fref.denoise(w, noise, ctx, ids, sig, v, negative=neg, guidance=3.0)
-        out = sampling.denoise(model, noise, ctx, ids, sigmas=sampling.linear_sigmas(2),
+        out = sampling.denoise_joint(model, noise, ctx, ids, sigmas=sampling.linear_sigmas(2),
                                negative=neg, guidance=3.0)
         assert _max_rel(out - noise, expect - noise) < TOL
         refs = normal((1, 6, v.in_channels), seed=106, dtype=F32)
@@ -239,7 +239,7 @@ def test_flux_bf16_class_blocks_cfg_and_references(monkeypatch):
         for negative, g in ((None, 1.0), (neg, 2.0)):
             expect = fref.denoise(w, noise, ctx, ids_r, sig, v, negative=negative, guidance=g,
                                   references=refs)
-            out = sampling.denoise(model, noise, ctx, ids_r, sigmas=sampling.linear_sigmas(2),
+            out = sampling.denoise_joint(model, noise, ctx, ids_r, sigmas=sampling.linear_sigmas(2),
                                    negative=negative, guidance=g, references=refs)
             assert out.shape == noise.shape and _max_rel(out - noise, expect - noise) < TOL
 

@@ -168,7 +168,7 @@ def test_in_context_reference_trajectory_matches_oracle(cuda_device):
     sigmas = ref.schedule(H * W, 3)
     expect = ref.denoise(w, c["noise"], c["text"], ids, sigmas, v, references=c["refs"])
     model = Flux2Transformer(w, v, cuda_device)
-    out = sampling.denoise(model, c["noise"], c["text"], ids, sigmas=sampling.schedule(H * W, 3),
+    out = sampling.denoise_joint(model, c["noise"], c["text"], ids, sigmas=sampling.schedule(H * W, 3),
                            references=c["refs"])
     rel, cos = _metrics(out, expect)
     assert out.shape == c["noise"].shape and cos >= 0.999 and rel <= 3e-2, (rel, cos)
