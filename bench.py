@@ -195,8 +195,18 @@ def physical_gpu(local: int) -> int:
 
 
 # ----------------------------------------------------------------------------- CPU oracle sample
-def cpu_sample_ms(threads: int) -> tuple[float, str]:
-    """One double + one single block of the workload on the CPU oracle, extrapolated to a step."""
+def config_dict() -> dict:
+    """The workload description both arms print (the same keys and values)."""
+    return {
+        "workload": WORKLOAD,
+        "l2": "no flush: 9.4 GB of weights stream per step, inputs exceed the 126 MB L2",
+        "step_gflop": round(step_flops() / 1e9, 1),
+    }
+
+
+def cpu_sample_ms(threads: int) -> tuple[float, str, dict]:
+    """One double + one single block of the workload on the CPU oracle, extrapolated to a step;
+    also returns the measured parts in ms."""
     from oracle import flux2 as ref
     from kinomlx_b200.flux2 import config as fcfg
     from kinomlx_b200.synthetic import flux_weights, normal
@@ -227,7 +237,9 @@ def cpu_sample_ms(threads: int) -> tuple[float, str]:
         "CPU oracle (torch, bf16 values, fp32 matmul): timestep MLP + modulations + 1 double "
         "block + 1 single block at 4096+512 tokens, extrapolated x8 double / x24 single"
     )
-    return ms, sample
+    parts = {"modulations_ms": round(1e3 * (t1 - t0), 1), "double_block_ms": round(1e3 * (t2 - t1), 1),
+             "single_block_ms": round(1e3 * (t3 - t2), 1)}
+    return ms, sample, parts
 
 
 def run_reference(args, world: int, rank: int) -> None:
@@ -236,8 +248,9 @@ def run_reference(args, world: int, rank: int) -> None:
     threads = os.cpu_count() or 1
     for _ in range(args.warmup):
         cpu_sample_ms(threads)
-    times = [cpu_sample_ms(threads)[0] for _ in range(args.steps)]
-    ms = statistics.mean(times)
+    samples = [cpu_sample_ms(threads) for _ in range(args.steps)]
+    ms = statistics.mean(x[0] for x in samples)
+    measured = {k: round(statistics.mean(x[2][k] for x in samples), 1) for k in samples[0][2]}
     sample = (
         "CPU restatement of the reference formulas (oracle/, torch CPU): per step 1 double + 1 "
         "single block at 4096+512 tokens, extrapolated x8 / x24 (the reference's MLX path needs "
@@ -257,9 +270,10 @@ def run_reference(args, world: int, rank: int) -> None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "l2": "weights 9.4 GB per step exceed L2"},
+        "config": config_dict(),
         "cpu_baseline": {"value": round(ms, 3), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "measured": measured,
+                         "extrapolated": "value = modulations + 8 x double + 24 x single"},
         "e2e": {"value": round(ms, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -404,6 +418,15 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
         "step_tflops": round(step_flops() / (ms * 1e9), 1),
         "timing": "per-launch CUDA events over a second pass of the same K steps",
     }
+    if bound == "tensor":
+        # the same achieved rate against the burst peak, and per MHz against the sustained
+        # peak per MHz of the clock it was measured at (the bench and the peak run at different
+        # clocks under the power cap)
+        roofline["frac_of_burst"] = round(achieved / float(pk.get("bf16_tflops", peak)), 4)
+        peak_mhz = (pk.get("clocks_under_load") or {}).get("sm_mhz_median")
+        run_mhz = (clocks or {}).get("sm_mhz")
+        if peak_mhz and run_mhz:
+            roofline["frac_clock_normalised"] = round((achieved / run_mhz) / (peak / peak_mhz), 4)
 
     secondary = None
     model.sp.close()
@@ -415,9 +438,11 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu:
         threads = os.cpu_count() or 1
-        cms, sample = cpu_sample_ms(threads)
+        cpu_sample_ms(threads)  # warm-up (allocator, thread pool)
+        cms, sample, parts = cpu_sample_ms(threads)
         cpu = {"value": round(cms, 1), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": sample}
+               "sample": sample, "measured": parts,
+               "extrapolated": "value = modulations + 8 x double + 24 x single"}
 
     if rank == 0:
         line = {
@@ -433,12 +458,10 @@ def run_kino(args, world: int, rank: int, local: int) -> None:
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) latents and text, random-init N(0,0.02) weights)",
-            "config": {
-                "workload": WORKLOAD,
-                "parallelism": f"ulysses sequence parallel x{world} (NCCL all-to-all)" if world > 1 else "single GPU",
-                "l2": "no flush: 9.4 GB of weights stream per step, inputs exceed the 126 MB L2",
-                "step_gflop": round(step_flops() / 1e9, 1),
-            },
+            "config": config_dict(),
+            "parallelism": (f"ulysses sequence parallel x{world} (q/k/v and attention rows "
+                            "exchanged over NVLink peer memory inside the projection and "
+                            "attention kernels)") if world > 1 else "single GPU",
             "e2e": {"value": round(e2e_ms, 3), "unit": UNIT, "h2d_bytes_per_step": io_bytes,
                     "d2h_bytes_per_step": io_bytes},
             "roofline": roofline,

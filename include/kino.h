@@ -188,6 +188,45 @@ kino_status kino_attention(const kino_attention_args* args, void* stream);
 kino_status kino_dense_attention(const void* q, const void* k, const void* v, void* out,
                                  int64_t tq, int64_t tk, int64_t heads, int64_t dim, void* stream);
 
+/* ------------------------------------------------------------------ Sol-Attn (sparse) */
+#define KINO_DTYPE_BF16 0
+#define KINO_DTYPE_F16 1
+
+typedef struct kino_sol_attention_args {
+  const void* q;           /* (tokens, heads * 128) token-major, dtype below, row strides ld_* */
+  const void* k;
+  const void* v;
+  int64_t ld_q, ld_k, ld_v;
+  void* out;               /* (tokens, heads * 128), rows in the input order, the input dtype */
+  int64_t ld_out;
+  const void* gate;        /* optional (tokens, heads) per-head output gate, input order:
+                              out = round(round(attention) * gate), as the LTX gated heads */
+  int64_t ld_gate;
+  int64_t tokens;          /* at most 512 blocks of 64 tokens */
+  int64_t heads;
+  int dtype;               /* KINO_DTYPE_BF16 or KINO_DTYPE_F16 */
+  float tau;               /* routing threshold in standard deviations (finite) */
+  const int32_t* order;    /* device (tokens): routing position -> input row, e.g. Morton */
+  uint32_t* routes;        /* optional device (heads, blocks, ceil(blocks / 32)): receives the
+                              routing mask words (bit b of row a: key block b routed for query
+                              block a); NULL keeps them in the workspace */
+  void* workspace;         /* kino_sol_attention_workspace_size bytes, 16-byte aligned */
+  int64_t workspace_bytes;
+} kino_sol_attention_args;
+
+/* Workspace bytes of kino_sol_attention (fp16 copies of q, k, v in routing order, block means,
+ * routing words, per-CTA block lists); -1 for invalid sizes. */
+int64_t kino_sol_attention_workspace_size(int64_t tokens, int64_t heads);
+
+/* Sol-Attn routed sparse attention (128-wide heads): tokens in 64-token blocks along `order`;
+ * each query block attends exactly to the key blocks whose mean-key score exceeds the row's
+ * mean + tau standard deviations (plus itself and both neighbours) and to every other block
+ * through its mean key (score + log2 of its length) and mean value, in one softmax; operands
+ * converted to fp16 (saturating), fp32 scores and accumulation. Replaces
+ * kinomlx.models.ltx2.kernels.sol_attention.sol_attention
+ * (kinomlx/models/ltx2/kernels/sol_attention.py:219-272, route_blocks :181-216). */
+kino_status kino_sol_attention(const kino_sol_attention_args* args, void* stream);
+
 /* ------------------------------------------------------------------ norms and rotary */
 #define KINO_NORM_RMS 0
 #define KINO_NORM_LAYER 1

@@ -210,6 +210,31 @@ class LTXVideoBlockWeights(ctypes.Structure):
         "ff_out_b")]
 
 
+class SolAttentionArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p),
+        ("k", c_void_p),
+        ("v", c_void_p),
+        ("ld_q", c_int64),
+        ("ld_k", c_int64),
+        ("ld_v", c_int64),
+        ("out", c_void_p),
+        ("ld_out", c_int64),
+        ("gate", c_void_p),
+        ("ld_gate", c_int64),
+        ("tokens", c_int64),
+        ("heads", c_int64),
+        ("dtype", c_int),
+        ("tau", c_float),
+        ("order", c_void_p),
+        ("routes", c_void_p),
+        ("workspace", c_void_p),
+        ("workspace_bytes", c_int64),
+    ]
+
+
+DTYPE_BF16 = 0
+DTYPE_F16 = 1
 MLP_GELU_TANH = 0
 MLP_SWIGLU = 1
 
@@ -235,6 +260,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_gemv": (c_int, [P, I64, P, P, P, I64, I64, I64, I64, c_int, P]),
     "kino_attention": (c_int, [POINTER(AttentionArgs), P]),
     "kino_dense_attention": (c_int, [P, P, P, P, I64, I64, I64, I64, P]),
+    "kino_sol_attention_workspace_size": (I64, [I64, I64]),
+    "kino_sol_attention": (c_int, [POINTER(SolAttentionArgs), P]),
     "kino_adaln": (c_int, [P, I64, I64, P, P, I64, P, I64, I64, I64, I64, I64, c_int, F, P]),
     "kino_rms_norm": (c_int, [P, P, P, I64, I64, F, F, P]),
     "kino_qk_norm_rope": (

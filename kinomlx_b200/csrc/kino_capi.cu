@@ -15,6 +15,7 @@
 #include "kino_conv3d.cuh"
 #include "kino_ops.cuh"
 #include "kino_peer.cuh"
+#include "kino_sol.cuh"
 #include "kino_vae.cuh"
 #include "kino_quant.cuh"
 #include "kino_f32.cuh"
@@ -490,6 +491,42 @@ void* group_norm_scratch_address(kino_status* status) {
 
 }  // namespace
 
+// Sol-Attn workspace sections (all 256-byte aligned), in order.
+namespace {
+
+struct SolLayout {
+  int64_t nb, words, ncta, width;
+  int64_t q16, k16, v16, qmean, kmean, vmean, bits, lists, counts, total;
+};
+
+SolLayout sol_layout(int64_t tokens, int64_t heads) {
+  SolLayout l;
+  l.nb = (tokens + kino::SOL_BLOCK - 1) / kino::SOL_BLOCK;
+  l.words = (l.nb + 31) / 32;
+  l.ncta = (l.nb + kino::SOL_QBLOCKS - 1) / kino::SOL_QBLOCKS;
+  l.width = heads * 128;
+  auto up = [](int64_t v) { return (v + 255) / 256 * 256; };
+  int64_t at = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t here = at;
+    at += up(bytes);
+    return here;
+  };
+  l.q16 = take(tokens * l.width * 2);
+  l.k16 = take(tokens * l.width * 2);
+  l.v16 = take(tokens * l.width * 2);
+  l.qmean = take(heads * l.nb * 128 * 4);
+  l.kmean = take(heads * l.nb * 128 * 2);
+  l.vmean = take(heads * l.nb * 128 * 2);
+  l.bits = take(heads * l.nb * l.words * 4);
+  l.lists = take(heads * l.ncta * l.nb * 4);
+  l.counts = take(heads * l.ncta * 4);
+  l.total = at;
+  return l;
+}
+
+}  // namespace
+
 extern "C" {
 
 int kino_abi_version(void) { return 10; }
@@ -507,7 +544,8 @@ kino_status kino_device_status(void* stream) {
   if (flag != 0) {
     const int zero = 0;
     cudaMemcpyToSymbol(kino::g_device_error, &zero, sizeof(int));
-    return fail(flag, "a kernel wait timed out (device status %d)", flag);
+    if (flag == KINO_ETIMEOUT) return fail(flag, "a kernel wait timed out (device status %d)", flag);
+    return fail(flag, "a kernel skipped an out-of-range index (device status %d)", flag);
   }
   return KINO_OK;
 }
@@ -772,6 +810,112 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
   };
   return a->head_dim == 64 ? run(kino::attention_tc_kernel<64>, 11)
                            : run(kino::attention_tc_kernel<128>, 3);
+}
+
+// ---------------------------------------------------------------- Sol-Attn
+int64_t kino_sol_attention_workspace_size(int64_t tokens, int64_t heads) {
+  if (tokens < 1 || heads < 1 || tokens > (int64_t{1} << 30) || heads > 256) {
+    fail(KINO_EINVAL, "kino_sol_attention_workspace_size: tokens/heads");
+    return -1;
+  }
+  return sol_layout(tokens, heads).total;
+}
+
+kino_status kino_sol_attention(const kino_sol_attention_args* a, void* stream) {
+  if (a == nullptr || a->q == nullptr || a->k == nullptr || a->v == nullptr ||
+      a->out == nullptr || a->order == nullptr || a->workspace == nullptr)
+    return fail(KINO_EINVAL, "kino_sol_attention: null argument");
+  if (a->tokens < 1 || a->heads < 1 || a->heads > 256)
+    return fail(KINO_EINVAL, "kino_sol_attention: tokens/heads");
+  if (a->dtype != KINO_DTYPE_BF16 && a->dtype != KINO_DTYPE_F16)
+    return fail(KINO_EINVAL, "kino_sol_attention: dtype must be KINO_DTYPE_BF16 or KINO_DTYPE_F16");
+  if (!(a->tau == a->tau) || a->tau > 3.0e38f || a->tau < -3.0e38f)
+    return fail(KINO_EINVAL, "kino_sol_attention: tau must be finite");
+  const SolLayout l = sol_layout(a->tokens, a->heads);
+  if (l.nb > kino::SOL_MAX_WORDS * 32)
+    return fail(KINO_ENOTSUPPORTED, "kino_sol_attention: at most %d blocks of 64 tokens",
+                kino::SOL_MAX_WORDS * 32);
+  if (a->workspace_bytes < l.total || !aligned16(a->workspace))
+    return fail(KINO_EINVAL, "kino_sol_attention: workspace below %lld bytes or unaligned",
+                (long long)l.total);
+  if (a->ld_q < l.width || a->ld_k < l.width || a->ld_v < l.width || a->ld_out < l.width ||
+      a->ld_q % 8 || a->ld_k % 8 || a->ld_v % 8 || a->ld_out % 8 || !aligned16(a->q) ||
+      !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->out))
+    return fail(KINO_ENOTSUPPORTED,
+                "kino_sol_attention: row strides >= heads * 128, multiples of 8, aligned rows");
+  if (a->gate != nullptr && a->ld_gate < a->heads)
+    return fail(KINO_EINVAL, "kino_sol_attention: gate stride below heads");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+  __half* q16 = reinterpret_cast<__half*>(ws + l.q16);
+  __half* k16 = reinterpret_cast<__half*>(ws + l.k16);
+  __half* v16 = reinterpret_cast<__half*>(ws + l.v16);
+  float* qmean = reinterpret_cast<float*>(ws + l.qmean);
+  __half* kmean = reinterpret_cast<__half*>(ws + l.kmean);
+  __half* vmean = reinterpret_cast<__half*>(ws + l.vmean);
+  uint32_t* bits = a->routes != nullptr ? a->routes : reinterpret_cast<uint32_t*>(ws + l.bits);
+  int* lists = reinterpret_cast<int*>(ws + l.lists);
+  int* counts = reinterpret_cast<int*>(ws + l.counts);
+  const int tokens = static_cast<int>(a->tokens), heads = static_cast<int>(a->heads);
+  const dim3 grid_bh(static_cast<unsigned>(l.nb), static_cast<unsigned>(heads));
+  if (a->dtype == KINO_DTYPE_F16)
+    launch_pdl(kino::sol_prepare_kernel<__half>, grid_bh, dim3(128), 0, st,
+               static_cast<const __half*>(a->q), static_cast<const __half*>(a->k),
+               static_cast<const __half*>(a->v), a->ld_q, a->ld_k, a->ld_v, a->order, tokens,
+               heads, q16, k16, v16, qmean, kmean, vmean);
+  else
+    launch_pdl(kino::sol_prepare_kernel<__nv_bfloat16>, grid_bh, dim3(128), 0, st,
+               static_cast<const __nv_bfloat16*>(a->q), static_cast<const __nv_bfloat16*>(a->k),
+               static_cast<const __nv_bfloat16*>(a->v), a->ld_q, a->ld_k, a->ld_v, a->order,
+               tokens, heads, q16, k16, v16, qmean, kmean, vmean);
+  kino_status s = check_launch("kino_sol_attention (prepare)");
+  if (s != KINO_OK) return s;
+  const double ls = 1.4426950408889634 / sqrt(128.0);
+  launch_pdl(kino::sol_route_kernel, grid_bh, dim3(128), 0, st, qmean, kmean,
+             static_cast<int>(l.words), static_cast<float>(ls), static_cast<float>(ls * ls),
+             a->tau, bits);
+  s = check_launch("kino_sol_attention (route)");
+  if (s != KINO_OK) return s;
+  launch_pdl(kino::sol_union_kernel, dim3(static_cast<unsigned>(l.ncta), heads), dim3(32), 0, st,
+             bits, static_cast<int>(l.nb), static_cast<int>(l.words), lists, counts);
+  s = check_launch("kino_sol_attention (union)");
+  if (s != KINO_OK) return s;
+  CUtensorMap mq, mk, mv, mkc, mvc;
+  const uint64_t dq[4] = {128, static_cast<uint64_t>(tokens), static_cast<uint64_t>(heads), 1};
+  const uint64_t sq[3] = {static_cast<uint64_t>(l.width), 128, 8};
+  const uint32_t qbox[4] = {64, 128, 1, 1};
+  const uint32_t kbox[4] = {64, 64, 1, 1};
+  if ((s = make_map(&mq, q16, 4, dq, sq, qbox)) != KINO_OK) return s;
+  if ((s = make_map(&mk, k16, 4, dq, sq, kbox)) != KINO_OK) return s;
+  if ((s = make_map(&mv, v16, 4, dq, sq, kbox)) != KINO_OK) return s;
+  const uint64_t dc[3] = {128, static_cast<uint64_t>(l.nb), static_cast<uint64_t>(heads)};
+  const uint64_t sc[2] = {128, static_cast<uint64_t>(l.nb * 128)};
+  const uint32_t cbox[3] = {64, 64, 1};
+  if ((s = make_map(&mkc, kmean, 3, dc, sc, cbox)) != KINO_OK) return s;
+  if ((s = make_map(&mvc, vmean, 3, dc, sc, cbox)) != KINO_OK) return s;
+  kino::SolParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.tokens = tokens;
+  p.heads = heads;
+  p.nb = static_cast<int>(l.nb);
+  p.words = static_cast<int>(l.words);
+  p.ncta = static_cast<int>(l.ncta);
+  p.scale_log2 = static_cast<float>(ls);
+  p.last_log2 = static_cast<float>(log2(static_cast<double>(tokens - (l.nb - 1) * kino::SOL_BLOCK)));
+  p.bits = bits;
+  p.lists = lists;
+  p.counts = counts;
+  p.order = a->order;
+  p.out = a->out;
+  p.ld_out = a->ld_out;
+  p.out_f16 = a->dtype == KINO_DTYPE_F16 ? 1 : 0;
+  p.gate = a->gate;
+  p.ld_gate = a->ld_gate;
+  constexpr int smem = kino::AttnSmem::TOTAL + 256;  // + the CTA's routing words
+  if ((s = ensure_smem(kino::sol_attention_kernel, smem, 12)) != KINO_OK) return s;
+  launch_pdl(kino::sol_attention_kernel, dim3(static_cast<unsigned>(l.ncta), heads),
+             dim3(kino::ATT_THREADS), smem, st, mq, mk, mv, mkc, mvc, p);
+  return check_launch("kino_sol_attention");
 }
 
 kino_status kino_dense_attention(const void* q, const void* k, const void* v, void* out,

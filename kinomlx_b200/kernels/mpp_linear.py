@@ -92,8 +92,31 @@ def linear(value, weight, bias, *, transposed: bool, operand: Operand | None = N
     return ops.linear(flat, w.contiguous(), bias=bias).reshape(*value.shape[:-1], w.shape[0])
 
 
+_ONES: dict[tuple, torch.Tensor] = {}
+
+
 def linear_rows(value, weight, bias=None, *, residual=None):
     """residual + addmm(bias, value, weight.T) with the product rounded before the residual add
-    (kinomlx/kernels/mpp_linear.py:592-611)."""
-    out = linear(value, weight, bias, transposed=True)
-    return out if residual is None else out + residual
+    (kinomlx/kernels/mpp_linear.py:592-611). The add runs in the GEMM's epilogue: the gated
+    residual form with a gate of ones, residual + round(1 * round(acc + bias)), rounded once
+    more at the store, is that sum."""
+    if residual is None:
+        return linear(value, weight, bias, transposed=True)
+    w = _weight(weight)
+    n = w.shape[0]
+    if residual.dtype != value.dtype or tuple(residual.shape) != (*value.shape[:-1], n):
+        raise ValueError(f"the residual must be a {value.dtype} {(*value.shape[:-1], n)} tensor")
+    rows = math.prod(value.shape[:-1])
+    if w.dtype != value.dtype or not supports(rows, value.shape[-1], n, transposed=True,
+                                              dtype=value.dtype):
+        raise ValueError(
+            f"the B200 GEMM does not take a {rows} x {value.shape[-1]} by {value.shape[-1]} x "
+            f"{n} {value.dtype} product")
+    key = (value.device, n, value.dtype)
+    if key not in _ONES:
+        _ONES[key] = torch.ones((1, n), device=value.device, dtype=value.dtype)
+    res = residual.reshape(rows, n).contiguous()
+    out = torch.empty_like(res)
+    ops.linear(value.reshape(rows, value.shape[-1]), w.contiguous(), out, bias=bias,
+               kind=ops.EPI_GATED_RESIDUAL, residual=res, gate=_ONES[key])
+    return out.reshape(*value.shape[:-1], n)

@@ -11,10 +11,11 @@ Two layers:
 Each step is one X0 transformer evaluation with the Euler update fused into the final
 projection's epilogue (x0 = x - sigma v, then x0 + (sigma'/sigma)(x - x0), both in fp32).
 
-Supported here: uniform denoise masks (every token at the step's sigma), dense self-attention,
-no context masks or keyframes, the deterministic-Euler step. The reference's other options
-(per-token masks from image/keyframe conditioning, padded text masks, Sol-Attn sparse steps, the
-RF-ancestral step) are refused with a ValueError naming the option, never silently ignored.
+Supported here: uniform denoise masks (every token at the step's sigma), dense or Sol-Attn
+sparse video self-attention (per step, video-only transformer on one GPU), no context masks or
+keyframes, the deterministic-Euler step. The reference's other options (per-token masks from
+image/keyframe conditioning, padded text masks, the RF-ancestral step) are refused with a
+ValueError naming the option, never silently ignored.
 """
 
 from __future__ import annotations
@@ -108,8 +109,8 @@ def _refuse_unsupported(video_state: LatentState, audio_state: LatentState | Non
         raise ValueError("padded text masks are not supported by the device loop")
     if video_keyframes_mask is not None:
         raise ValueError("keyframe masks are not supported by the device loop")
-    if video_sparse_attention is not None:
-        raise ValueError("sparse video self-attention is not supported by the device loop")
+    if video_sparse_attention is not None and audio_state is not None:
+        raise ValueError("sparse video self-attention runs on the video-only transformer")
     if not video_enabled or not audio_enabled:
         raise ValueError("the device loop denoises every supplied modality")
 
@@ -140,7 +141,7 @@ class _Prepared:
 
 
 def _step(transformer, prepared: _Prepared, video_state: LatentState,
-          audio_state: LatentState | None, sigma: float, sigma_next: float):
+          audio_state: LatentState | None, sigma: float, sigma_next: float, sparse=None):
     dtype = getattr(transformer, "dtype", torch.bfloat16)
     video = video_state.latent.to(transformer.device, dtype)
     video_out = torch.empty_like(video)
@@ -159,7 +160,8 @@ def _step(transformer, prepared: _Prepared, video_state: LatentState,
         transformer.run(prepared.prep, shard, sigma, sigma_next=sigma_next, out=shard)
         video_out = sp.all_gather_tokens(shard)
     else:
-        transformer.run(prepared.prep, video, sigma, sigma_next=sigma_next, out=video_out)
+        kw = {} if sparse is None else {"sparse": sparse}
+        transformer.run(prepared.prep, video, sigma, sigma_next=sigma_next, out=video_out, **kw)
     _check_finite([("video", video_out)])
     return replace(video_state, latent=video_out), audio_state
 
@@ -197,7 +199,7 @@ def denoise_step(
         raise ValueError(f"current sigma must be positive and finite, got {sigma!r}")
     prepared = _Prepared(transformer, video_state, audio_state, video_context, audio_context)
     return _step(transformer, prepared, video_state, audio_state, fp32([sigma])[0],
-                 fp32([sigma_next])[0])
+                 fp32([sigma_next])[0], video_sparse_attention)
 
 
 def denoise_loop(
@@ -238,14 +240,14 @@ def denoise_loop(
     if video_sparse_attention and len(video_sparse_attention) != total:
         raise ValueError(f"sparse attention lists {len(video_sparse_attention)} steps for a "
                          f"{total}-step schedule")
-    if any(step is not None for step in video_sparse_attention):
-        raise ValueError("sparse video self-attention is not supported by the device loop")
+    sparse_steps = tuple(video_sparse_attention) or (None,) * total
     _refuse_unsupported(video_state, audio_state, step_kind=step_kind,
                         video_context_mask=video_context_mask,
                         audio_context_mask=audio_context_mask,
                         video_keyframes_mask=video_keyframes_mask, video_noise=None,
-                        audio_noise=None, video_sparse_attention=None, video_enabled=True,
-                        audio_enabled=True)
+                        audio_noise=None,
+                        video_sparse_attention=next((x for x in sparse_steps if x is not None), None),
+                        video_enabled=True, audio_enabled=True)
     sink = reporter if reporter is not None else _NullReporter()
     prepared = _Prepared(transformer, video_state, audio_state, video_context, audio_context)
     schedule = fp32(values)
@@ -254,7 +256,8 @@ def denoise_loop(
         for index in range(1, total + 1):
             try:
                 video_state, audio_state = _step(transformer, prepared, video_state, audio_state,
-                                                 schedule[index - 1], schedule[index])
+                                                 schedule[index - 1], schedule[index],
+                                                 sparse_steps[index - 1])
             except LTX2DenoiseError as error:
                 location = f"stage {stage}" if stage is not None else phase
                 message = f"{location}, step {index}: {error}"

@@ -254,7 +254,8 @@ class LTXVideoTransformer:
             ops.add_rows(self.out_table, ws.emb[b], out=ws.outmod[b].view(2, -1))
 
     # ------------------------------------------------------------------ block
-    def _block(self, ws: _Workspace, i: int, p: dict, prepared: PreparedContext) -> None:
+    def _block(self, ws: _Workspace, i: int, p: dict, prepared: PreparedContext,
+               sparse=None) -> None:
         v, d, h = self.v, self.v.dim, self.v.heads
         val = lambda j: ws.vals[:, i, j * d : (j + 1) * d]
         x, nrm = ws.x, ws.nrm
@@ -281,7 +282,15 @@ class LTXVideoTransformer:
                              rope=ops.ROPE_SPLIT, cos=prepared.cos, sin=prepared.sin, eps=v.eps)
             ops.qk_norm_rope(k, heads=h, weight=p["kn1"], norm=ops.QKNORM_FULL_ROW,
                              rope=ops.ROPE_SPLIT, cos=prepared.cos, sin=prepared.sin, eps=v.eps)
-            self.sp.attention(q, k, vv, q, heads=h, gate=ws.gates)
+            if sparse is not None and sparse.applies_to(i):
+                # Sol-Attn on this layer (kinomlx/models/ltx2/transformer/attention.py:210-226,
+                # 344-346); the output rows land over q, with the head gate
+                order = self._sparse_order(sparse, q.shape[1])
+                for b in range(q.shape[0]):
+                    ops.sol_attention(q[b], k[b], vv[b], heads=h, tau=sparse.tau, order=order,
+                                      out=q[b], gate=ws.gates[b])
+            else:
+                self.sp.attention(q, k, vv, q, heads=h, gate=ws.gates)
         self._lin(q, p, "o1_w", x, bias=p["o1_b"], kind=ops.EPI_GATED_RESIDUAL,
                    residual=x, gate=val(2))
         # text cross-attention with the prompt-modulated context
@@ -305,18 +314,31 @@ class LTXVideoTransformer:
         self._lin(ws.hid, p, "ff_out_w", x, bias=p["ff_out_b"],
                    kind=ops.EPI_GATED_RESIDUAL, residual=x, gate=val(5))
 
+    def _sparse_order(self, sparse, tokens: int) -> torch.Tensor:
+        """The step's routing order on the device, converted once per order tensor."""
+        cached = getattr(self, "_order_cache", None)
+        if cached is None or cached[0] is not sparse.order:
+            if sparse.order.numel() != tokens:
+                raise ValueError("the sparse step's token order must hold one index per video token")
+            self._order_cache = (sparse.order, sparse.order.to(self.device, torch.int32).contiguous())
+        return self._order_cache[1]
+
     # ------------------------------------------------------------------ forward
     def run(self, prepared: PreparedContext, latent: torch.Tensor, sigma: float, *,
             sigma_next: float | None = None, out: torch.Tensor | None = None,
-            blocks: range | None = None) -> torch.Tensor:
+            blocks: range | None = None, sparse=None) -> torch.Tensor:
         """Velocity for `latent` (B, T, C) at `sigma`; with `sigma_next`, the next latent of the
-        deterministic Euler step (X0 + Euler fused into the final projection)."""
+        deterministic Euler step (X0 + Euler fused into the final projection). `sparse` (a
+        SparseAttentionStep) computes the video self-attention of the layers it applies to with
+        Sol-Attn; it needs the whole sequence on one GPU."""
+        if sparse is not None and self.sp.size > 1:
+            raise ValueError("sparse video self-attention runs with the whole sequence on one GPU")
         batch, tokens, _ = latent.shape
         ws = self.workspace(batch, tokens, prepared.context.shape[1])
         self._embed(ws, sigma)
         ops.linear(latent, self.patch_w, ws.x, bias=self.patch_b)
         for i in blocks if blocks is not None else range(self.v.blocks):
-            self._block(ws, i, self.blocks[i], prepared)
+            self._block(ws, i, self.blocks[i], prepared, sparse)
         d = self.v.dim
         ops.adaln(ws.x, ws.outmod[:, :d], ws.outmod[:, d:], ws.nrm, norm=ops.NORM_LAYER,
                   eps=self.v.eps)

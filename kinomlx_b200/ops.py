@@ -70,6 +70,7 @@ __all__ = [
     "qk_norm_rope",
     "rms_norm",
     "silu",
+    "sol_attention",
     "split_rope",
     "tile_blend",
     "timestep_embedding",
@@ -459,6 +460,62 @@ def attention(
     flops = 4.0 * args.batch * heads * nq * nk * args.head_dim
     with _timed("attention", flops, 2.0 * args.batch * heads * args.head_dim * (2 * nq + 2 * nk)):
         _lib.call("kino_attention", ctypes.byref(args), _stream())
+    return out
+
+
+_SOL_WORKSPACES: dict[tuple, torch.Tensor] = {}
+
+
+def sol_attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    heads: int,
+    tau: float,
+    order: torch.Tensor,
+    out: torch.Tensor | None = None,
+    gate: torch.Tensor | None = None,
+    routes: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Sol-Attn of (tokens, heads * 128) q, k, v (bf16 or fp16, any row stride) routed in
+    `order` (a device int32 permutation); the output rows come back in input order, in the
+    input dtype, optionally times a (tokens, heads) gate. `routes` (int32 (heads, blocks,
+    words)) receives the routing mask words."""
+    dtype = q.dtype
+    if dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError("Sol attention needs float16 or bfloat16 q, k and v")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _need(t, name, dtype)
+    tokens = q.shape[0]
+    if out is None:
+        out = torch.empty((tokens, heads * 128), device=q.device, dtype=dtype)
+    _need(out, "out", dtype)
+    if order.dtype != torch.int32 or not order.is_cuda or order.numel() != tokens:
+        raise ValueError("the routing order must be a device int32 tensor of one index per token")
+    lib = _lib.load()
+    need = int(lib.kino_sol_attention_workspace_size(tokens, heads))
+    key = (q.device, tokens, heads)
+    ws = _SOL_WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = _SOL_WORKSPACES[key] = torch.empty(need, device=q.device, dtype=torch.uint8)
+    args = _lib.SolAttentionArgs()
+    args.q, args.k, args.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    args.ld_q, args.ld_k, args.ld_v = q.stride(0), k.stride(0), v.stride(0)
+    args.out, args.ld_out = out.data_ptr(), out.stride(0)
+    if gate is not None:
+        _need(gate, "gate", dtype)
+        args.gate, args.ld_gate = gate.data_ptr(), gate.stride(0)
+    args.tokens, args.heads = tokens, heads
+    args.dtype = _lib.DTYPE_F16 if dtype == torch.float16 else _lib.DTYPE_BF16
+    args.tau = tau
+    args.order = order.data_ptr()
+    if routes is not None:
+        _need(routes, "routes", torch.int32)
+        args.routes = routes.data_ptr()
+    args.workspace, args.workspace_bytes = ws.data_ptr(), ws.numel()
+    with _timed("sol_attention", 0.0, 0.0):
+        _lib.call("kino_sol_attention", ctypes.byref(args), _stream())
     return out
 
 

@@ -142,3 +142,71 @@ def test_two_gloo_ranks_ulysses_attention_equals_full_attention():
     expect = (o * gate[..., None]).reshape(1, tokens, heads * 128)
     for r in range(size):
         assert torch.equal(torch.tensor(results[r]).to(torch.bfloat16), expect)
+
+
+def _qkv(branch: int, heads: int, tokens: int):
+    import torch
+
+    gen = torch.Generator().manual_seed(40 + branch)
+    return tuple(torch.randn((1, tokens, heads * 128), generator=gen).to(torch.bfloat16)
+                 for _ in range(3))
+
+
+def _cfg_worker(rank: int, size: int, port: int, queue) -> None:
+    """One rank of the CFG split: the branch's Ulysses attention over its half of the ranks,
+    then the pair combine u + g (p - u) of the two branches' shards."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(size),
+                      RANK=str(rank), LOCAL_RANK=str(rank))
+    import torch
+    import torch.distributed as tdist
+
+    from kinomlx_b200 import dist, multi_gpu, sequence_parallel
+
+    sequence_parallel.ops = _CpuOps
+    multi_gpu.ops = type("CpuCfg", (), {
+        "cfg_combine": staticmethod(lambda p, u, g: (u.float() + g * (p.float() - u.float())).to(p.dtype))})
+    dist.init("gloo", timeout_s=60)
+    cfg = multi_gpu.CfgSplit()
+    heads, tokens = 4, 8
+    q, k, v = _qkv(cfg.branch, heads, tokens)
+    t0, t1 = cfg.sp.shard(tokens)
+    out = torch.zeros((1, t1 - t0, heads * 128), dtype=torch.bfloat16)
+    cfg.sp.attention(q[:, t0:t1], k[:, t0:t1], v[:, t0:t1], out, heads=heads)
+    combined = cfg.combine(out, 3.0)
+    full = cfg.sp.all_gather_tokens(combined)
+    pair = tdist.get_process_group_ranks(cfg.pair)
+    tdist.destroy_process_group()
+    queue.put((rank, cfg.branch, cfg.sp.size, pair, full.float().numpy().tolist()))
+
+
+@pytest.mark.parametrize("size", [2, 4])
+def test_gloo_ranks_cfg_split_with_ulysses_branches(size):
+    """CFG split on 2 ranks (one branch each) and 4 ranks (each branch on a Ulysses group of 2,
+    BASELINE config 3's layout at 4 GPUs): every rank ends with u + g (p - u) of the whole
+    sequence, p and u the two branches' full attention outputs."""
+    import torch
+
+    from oracle.fused_ops import sdpa
+
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_cfg_worker, args=(r, size, port, queue)) for r in range(size)]
+    for p in procs:
+        p.start()
+    results = {r: rest for r, *rest in (queue.get(timeout=240) for _ in range(size))}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    heads, tokens, half = 4, 8, size // 2
+    outs = []
+    for branch in (0, 1):
+        q, k, v = _qkv(branch, heads, tokens)
+        split = lambda x: x.reshape(1, tokens, heads, 128).transpose(1, 2)
+        o = sdpa(split(q), split(k), split(v), 128 ** -0.5).transpose(1, 2).reshape(1, tokens, -1)
+        outs.append(o.to(torch.bfloat16))
+    expect = (outs[1].float() + 3.0 * (outs[0].float() - outs[1].float())).to(torch.bfloat16)
+    for rank, (branch, sp_size, pair, full) in results.items():
+        assert branch == (0 if rank < half else 1) and sp_size == half
+        assert pair == [rank % half, rank % half + half]
+        assert torch.equal(torch.tensor(full).to(torch.bfloat16), expect)

@@ -130,3 +130,18 @@ def test_ltx_state_loop_matches_bare_loop(cuda_device):
     m = metrics(video.latent - latent.to(cuda_device),
                 lref.denoise(w, latent, context, pos, sigmas, v) - latent)
     assert m["cos"] >= 0.999, show("LTX state loop update vs oracle", m)
+
+
+def test_linear_rows_residual_in_the_epilogue(cuda_device):
+    """mpp_linear.linear_rows (kinomlx/kernels/mpp_linear.py:592-611): residual + the rounded
+    product, the add done in the GEMM epilogue, equals the product rounded then added."""
+    from kinomlx_b200.kernels import mpp_linear
+
+    x = normal((3, 70, 256), seed=51).to(cuda_device)
+    w = normal((384, 256), seed=52, std=0.05).to(cuda_device)
+    b = normal((384,), seed=53).to(cuda_device)
+    r = normal((3, 70, 384), seed=54).to(cuda_device)
+    got = mpp_linear.linear_rows(x, w, b, residual=r)
+    plain = mpp_linear.linear(x, w, b, transposed=True)
+    assert torch.equal(got, (plain.float() + r.float()).to(torch.bfloat16))
+    assert torch.equal(mpp_linear.linear_rows(x, w, b), plain)
