@@ -636,13 +636,10 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
     sp = SequenceParallel(peer=True) if world > 1 else None
     lmodel = LTXVideoTransformer(ltx_weights(lv, seed=0, device=device), lv, device, sp=sp)
     torch.cuda.empty_cache()
+    from kinomlx_b200.ltx2.patchifier import latent_positions
+
     f, h, w = 16, 18, 32
-    fr, hr, wr = torch.meshgrid(torch.arange(f), torch.arange(h), torch.arange(w), indexing="ij")
-    starts = torch.stack([fr, hr, wr]).reshape(3, -1).float()
-    bounds = torch.stack([starts, starts + 1], -1)[None]
-    scale = torch.tensor([8.0, 32.0, 32.0]).reshape(1, 3, 1, 1)
-    pix = bounds * scale
-    pix[:, 0] = torch.clamp(pix[:, 0] + 1 - 8, min=0) / 24.0
+    pix = latent_positions(f, h, w)
     context = normal((1, 256, lv.context_dim), seed=2, device=device)
     lprep = lmodel.prepare(context, pix)
     t0, t1 = lmodel.sp.shard(f * h * w)
@@ -718,6 +715,12 @@ def run_kernel_case(case: str) -> None:
         return
     elif case == "kv_step":
         run_kv_step(dev)
+        return
+    elif case == "sol":
+        run_sol_case(dev)
+        return
+    elif case == "sol_step":
+        run_sol_step(dev)
         return
     elif case == "f32":
         # fp32 parity mode at config 1: the image stream's FF up projection (1024 x 12288 x 3072,
@@ -800,6 +803,106 @@ def run_av_step(dev: torch.device) -> None:
                       "video_tokens": f * h * w, "audio_tokens": ta,
                       "video_only_step_tflop": round(ltx_step_flops() / 1e12, 1),
                       "kernels": _kernel_shares(step)}))
+
+
+def run_sol_case(dev: torch.device) -> None:
+    """Sol-Attn at config 4's video self-attention (9216 tokens on a 16 x 18 x 32 Morton grid,
+    32 heads of 128) against the dense kernel on the same q, k, v, for the published taus. The
+    algorithmic work counts the exact (query, routed key) pairs and the (query, centroid) pairs,
+    4 x 128 FLOP each."""
+    from kinomlx_b200 import ops
+    from kinomlx_b200.kernels import sol_attention as sol
+    from kinomlx_b200.synthetic import normal
+
+    tokens, heads, d = 9216, 32, 4096
+    grid = (16, 18, 32)
+    out = torch.empty((tokens, d), device=dev, dtype=torch.bfloat16)
+    order = sol.morton_order(*grid).to(dev)
+    # input families: i.i.d. N(0, 1) q, k, v (routing uncorrelated between neighbouring query
+    # blocks: the worst case for a CTA's shared block list), and smooth fields over the latent
+    # grid plus noise (32 random low-frequency cosine modes mixed into each head, N(0, 0.3^2) on
+    # top), without and with the block's 3-D RoPE on q and k
+    gen = torch.Generator(device=dev).manual_seed(11)
+    f_, h_, w_ = torch.meshgrid(*(torch.arange(n, device=dev, dtype=torch.float32) / n for n in grid),
+                                indexing="ij")
+    pos = torch.stack([f_, h_, w_], -1).reshape(-1, 3)
+    freq = torch.rand((3, 32), generator=gen, device=dev) * 3.0
+    phase = torch.rand((32,), generator=gen, device=dev) * 6.283
+    modes = torch.cos(6.283 * pos @ freq + phase)  # (tokens, 32)
+    smooth = lambda: (modes @ torch.randn((32, d), generator=gen, device=dev) / 4.0
+                      + 0.3 * torch.randn((tokens, d), generator=gen, device=dev)).to(torch.bfloat16)
+    from kinomlx_b200.ltx2 import config as lcfg
+    from kinomlx_b200.ltx2.patchifier import latent_positions
+    from kinomlx_b200.ltx2.transformer import precompute_freqs_cis
+
+    cos, sin = (t.to(dev) for t in precompute_freqs_cis(latent_positions(*grid), lcfg.BASELINE_VIDEO))
+    rope = lambda x: ops.split_rope(x[None], cos, sin)[0]
+    inputs = {"iid": normal((tokens, 3 * d), seed=3, device=dev).split(d, 1),
+              "smooth": (smooth(), smooth(), smooth()),
+              # the same kind of fields after the video block's 3-D rotary embedding, as q and k
+              # reach the self-attention
+              "smooth_rope": (rope(smooth()), rope(smooth()), smooth())}
+    dense_flop = 4.0 * heads * tokens * tokens * 128
+    q, k, v = inputs["iid"]
+    dense_ms = _time(lambda: ops.attention([q[None]], [k[None]], [v[None]], [out[None]], heads=heads),
+                     3, 10, 1)
+    rows = []
+    for (family, (q, k, v)), tau in ((fam_t, tau) for fam_t in inputs.items()
+                                     for tau in (0.5, 1.0, 1.25, 1.5)):
+        ms = _time(lambda: ops.sol_attention(q, k, v, heads=heads, tau=tau, order=order, out=out),
+                   3, 10, 1)
+        routes = sol.routed_blocks(q, k, v, heads=heads, tau=tau, order=order)
+        nb = routes.shape[-1]
+        lengths = torch.clamp(tokens - torch.arange(nb, device=dev) * 64, max=64).float()
+        exact_keys = (routes.float() * lengths).sum(-1)  # (heads, blocks): keys per query row
+        rows_per_block = lengths[None, :]
+        exact = float((exact_keys * rows_per_block).sum())
+        centroid = float(((nb - routes.sum(-1)).float() * rows_per_block).sum())
+        flop = 4.0 * 128 * (exact + centroid)
+        pad = (-nb) % 4
+        union = torch.nn.functional.pad(routes, (0, 0, 0, pad)).reshape(heads, -1, 4, nb).any(2)
+        rows.append({"inputs": family, "tau": tau, "ms": round(ms, 3),
+                     "speedup_vs_dense": round(dense_ms / ms, 2),
+                     "routed_fraction": round(float(routes.float().mean()), 4),
+                     "cta_block_union_fraction": round(float(union.float().mean()), 4),
+                     "algorithmic_tflop": round(flop / 1e12, 3),
+                     "tflops": round(flop / (ms * 1e9), 1)})
+    ops.device_status()
+    print(json.dumps({"kernel_case": "sol", "ok": True, "tokens": tokens, "heads": heads,
+                      "dense_ms": round(dense_ms, 3),
+                      "dense_tflops": round(dense_flop / (dense_ms * 1e9), 1), "sol": rows}))
+
+
+def run_sol_step(dev: torch.device) -> None:
+    """The 48-block LTX-2 video step at config 4 with a Sol-Attn step (tau 1, layer 0 dense)
+    against the dense step, X0 + Euler fused, 2 warm-up and 3 timed steps each."""
+    from kinomlx_b200 import ops
+    from kinomlx_b200.kernels import sol_attention as sol
+    from kinomlx_b200.ltx2 import config as lcfg
+    from kinomlx_b200.ltx2.patchifier import latent_positions
+    from kinomlx_b200.ltx2.sparse_attention import SparseAttentionStep
+    from kinomlx_b200.ltx2.transformer import LTXVideoTransformer
+    from kinomlx_b200.synthetic import ltx_weights, normal
+
+    grid = (16, 18, 32)
+    tokens = grid[0] * grid[1] * grid[2]
+    v4 = lcfg.BASELINE_VIDEO
+    model = LTXVideoTransformer(ltx_weights(v4, seed=0, device=dev), v4, dev)
+    torch.cuda.empty_cache()
+    prep = model.prepare(normal((1, 256, v4.context_dim), seed=5, device=dev), latent_positions(*grid))
+    latent = normal((1, tokens, v4.in_channels), seed=4, device=dev)
+    nxt = latent.clone()
+    steps = {}
+    for name, sparse in (("dense", None),
+                         ("sol_tau1_layer0_dense", SparseAttentionStep(1.0, frozenset({0}),
+                                                                       sol.morton_order(*grid))),
+                         ("sol_tau1.5_layer0_dense", SparseAttentionStep(1.5, frozenset({0}),
+                                                                         sol.morton_order(*grid)))):
+        steps[name] = round(_time(lambda: model.run(prep, latent, 0.725, sigma_next=0.421875,
+                                                    out=nxt, sparse=sparse), 2, 3, 1), 3)
+    ops.device_status()
+    print(json.dumps({"kernel_case": "sol_step", "ok": True, "tokens": tokens,
+                      "ltx_step_ms": steps}))
 
 
 def run_kv_step(dev: torch.device) -> None:
@@ -959,7 +1062,7 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
-    ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow",
+    ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow", "sol", "sol_step",
                                               "bandwidth", "f32", "av_step", "kv_step"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     args = ap.parse_args()

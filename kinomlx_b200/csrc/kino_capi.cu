@@ -871,9 +871,11 @@ kino_status kino_sol_attention(const kino_sol_attention_args* a, void* stream) {
   kino_status s = check_launch("kino_sol_attention (prepare)");
   if (s != KINO_OK) return s;
   const double ls = 1.4426950408889634 / sqrt(128.0);
-  launch_pdl(kino::sol_route_kernel, grid_bh, dim3(128), 0, st, qmean, kmean,
-             static_cast<int>(l.words), static_cast<float>(ls), static_cast<float>(ls * ls),
-             a->tau, bits);
+  const dim3 grid_route(static_cast<unsigned>((l.nb + kino::SOL_ROUTE_ROWS - 1) / kino::SOL_ROUTE_ROWS),
+                        static_cast<unsigned>(heads));
+  launch_pdl(kino::sol_route_kernel, grid_route, dim3(256), 0, st, qmean, kmean,
+             static_cast<int>(l.nb), static_cast<int>(l.words), static_cast<float>(ls),
+             static_cast<float>(ls * ls), a->tau, bits);
   s = check_launch("kino_sol_attention (route)");
   if (s != KINO_OK) return s;
   launch_pdl(kino::sol_union_kernel, dim3(static_cast<unsigned>(l.ncta), heads), dim3(32), 0, st,
@@ -911,7 +913,8 @@ kino_status kino_sol_attention(const kino_sol_attention_args* a, void* stream) {
   p.out_f16 = a->dtype == KINO_DTYPE_F16 ? 1 : 0;
   p.gate = a->gate;
   p.ld_gate = a->ld_gate;
-  constexpr int smem = kino::AttnSmem::TOTAL + 256;  // + the CTA's routing words
+  // + the CTA's routing words (4 x 16 words) and its block list (at most 512 entries)
+  constexpr int smem = kino::AttnSmem::TOTAL + 256 + kino::SOL_MAX_WORDS * 32 * 4;
   if ((s = ensure_smem(kino::sol_attention_kernel, smem, 12)) != KINO_OK) return s;
   launch_pdl(kino::sol_attention_kernel, dim3(static_cast<unsigned>(l.ncta), heads),
              dim3(kino::ATT_THREADS), smem, st, mq, mk, mv, mkc, mvc, p);

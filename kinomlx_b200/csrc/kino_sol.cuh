@@ -132,57 +132,80 @@ __global__ void __launch_bounds__(128)
   vmean[m] = __float2half_rn(sol_sat(sol_round_in<In>(sum[2])));
 }
 
-// grid (blocks, heads), 128 threads (one per head dimension): routing row of query block a.
-// Scores are log2-scaled mean-query . mean-key products; the limit is the row's mean plus tau
-// standard deviations of those scores under a diagonal key covariance
-// (kinomlx/models/ltx2/kernels/sol_attention.py:181-216).
-__global__ void __launch_bounds__(128)
-    sol_route_kernel(const float* __restrict__ qmean, const __half* __restrict__ kmean,
+// grid (ceil(blocks / 8), heads), 256 threads: the routing rows of eight query blocks, one per
+// warp. The key-mean center and per-dimension variance over the blocks come first (thread d < 128
+// for dimension d); then each warp forms its row's limit, the row's mean score plus tau standard
+// deviations under a diagonal key covariance, and scores 32 key blocks at a time (lane l takes
+// block 32 i + l: a 128-long dot product against its mean key), a ballot turning the comparisons
+// into mask word i (kinomlx/models/ltx2/kernels/sol_attention.py:181-216).
+constexpr int SOL_ROUTE_ROWS = 8;
+
+__global__ void __launch_bounds__(256)
+    sol_route_kernel(const float* __restrict__ qmean, const __half* __restrict__ kmean, int nb,
                      int words, float log2_scale, float log2_scale_sq, float tau,
                      uint32_t* __restrict__ bits) {
   griddep_wait();
   griddep_launch();
-  __shared__ float qs[128];
-  __shared__ float red[2][4];
-  __shared__ uint32_t wsm[SOL_MAX_WORDS];
-  const int a = blockIdx.x, h = blockIdx.y, nb = gridDim.x;
-  const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
+  __shared__ float center[128], var[128];
+  __shared__ float qs[SOL_ROUTE_ROWS][128];
+  const int h = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __half* kh = kmean + static_cast<int64_t>(h) * nb * 128;
-  float s = 0.0f;
-  for (int b = 0; b < nb; ++b) s += __half2float(kh[b * 128 + d]);
-  const float center = s / static_cast<float>(nb);
-  float s2 = 0.0f;
-  for (int b = 0; b < nb; ++b) {
-    const float dl = __half2float(kh[b * 128 + d]) - center;
-    s2 += dl * dl;
+  if (tid < 128) {
+    float s = 0.0f;
+    for (int b = 0; b < nb; ++b) s += __half2float(kh[b * 128 + tid]);
+    const float c = s / static_cast<float>(nb);
+    float s2 = 0.0f;
+    for (int b = 0; b < nb; ++b) {
+      const float dl = __half2float(kh[b * 128 + tid]) - c;
+      s2 += dl * dl;
+    }
+    center[tid] = c;
+    var[tid] = s2 / static_cast<float>(nb);
   }
-  const float var = s2 / static_cast<float>(nb);
-  const float qm = qmean[(static_cast<int64_t>(h) * nb + a) * 128 + d];
-  qs[d] = qm;
-  if (d < SOL_MAX_WORDS) wsm[d] = 0u;
-  const float rm = warp_sum_f(qm * center);
-  const float rv = warp_sum_f(qm * qm * var);
-  if (lane == 0) {
-    red[0][warp] = rm;
-    red[1][warp] = rv;
+  const int a0 = blockIdx.x * SOL_ROUTE_ROWS;
+  for (int i = tid; i < SOL_ROUTE_ROWS * 128; i += 256) {
+    const int r = i >> 7, a = a0 + r;
+    qs[r][i & 127] = a < nb ? qmean[(static_cast<int64_t>(h) * nb + a) * 128 + (i & 127)] : 0.0f;
   }
   __syncthreads();
-  const float raw_mean = red[0][0] + red[0][1] + red[0][2] + red[0][3];
-  const float raw_var = red[1][0] + red[1][1] + red[1][2] + red[1][3];
+  const int a = a0 + warp;
+  if (a >= nb) return;
+  const float* q = qs[warp];
+  float rm = 0.0f, rv = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int d = lane + 32 * k;
+    rm += q[d] * center[d];
+    rv += q[d] * q[d] * var[d];
+  }
+  const float raw_mean = warp_sum_f(rm);
+  const float raw_var = warp_sum_f(rv);
   const float variance = fmaxf(raw_var, 0.0f) * log2_scale_sq;
   const float limit = raw_mean * log2_scale + tau * sqrtf(variance + 1.0e-6f);
-  for (int b = warp; b < nb; b += 4) {
-    const __half* kr = kh + b * 128 + lane * 4;
-    float dot = qs[lane * 4] * __half2float(kr[0]) + qs[lane * 4 + 1] * __half2float(kr[1]) +
-                qs[lane * 4 + 2] * __half2float(kr[2]) + qs[lane * 4 + 3] * __half2float(kr[3]);
-    dot = warp_sum_f(dot);
-    if (lane == 0) {
-      const bool routed = (b >= a - 1 && b <= a + 1) || dot * log2_scale > limit;
-      if (routed) atomicOr(&wsm[b >> 5], 1u << (b & 31));
+  uint32_t* row = bits + (static_cast<int64_t>(h) * nb + a) * words;
+  for (int w = 0; w < words; ++w) {
+    const int b = w * 32 + lane;
+    bool routed = false;
+    if (b < nb) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kh + b * 128);
+      float dot = 0.0f;
+#pragma unroll 4
+      for (int c = 0; c < 16; ++c) {
+        const uint4 raw = kr[c];
+        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 kv = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+          dot = fmaf(q[c * 8 + 2 * e], kv.x, dot);
+          dot = fmaf(q[c * 8 + 2 * e + 1], kv.y, dot);
+        }
+      }
+      routed = (b >= a - 1 && b <= a + 1) || dot * log2_scale > limit;
     }
+    const uint32_t word = __ballot_sync(0xffffffffu, routed);
+    if (lane == 0) row[w] = word;
   }
-  __syncthreads();
-  if (d < words) bits[(static_cast<int64_t>(h) * nb + a) * words + d] = wsm[d];
 }
 
 // grid (CTAs per head, heads), 32 threads: the union of the routing rows of query blocks
@@ -264,8 +287,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   float* xsum = reinterpret_cast<float*>(smem + L::L_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // routing words of the CTA's four query blocks, after the barrier block
+  // routing words of the CTA's four query blocks and its block list, after the barrier block
   uint32_t* rwords = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBAR * 8 + 16);
+  int* slist = reinterpret_cast<int*>(rwords + SOL_QBLOCKS * SOL_MAX_WORDS);
 
   const int warp = warp_id();
   const uint32_t lane = lane_id();
@@ -302,6 +326,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                               : 0u;
   }
   const int count = p.counts[head * p.ncta + cta];
+  for (int i = threadIdx.x; i < count; i += blockDim.x) slist[i] = list[i];
   const int ns = (count + 1) / 2;               // exact stages: two 64-key blocks each
   const int nblk = ns + (p.nb + 127) / 128;     // then the centroid stages
   if (warp == 1) {
@@ -331,8 +356,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         uint8_t* sv = sk + 2 * L::HALF;
         mbar_expect_tx(&kv_full[stage], 2 * NH * L::HALF);
         if (j < ns) {
-          const int kb0 = list[2 * j];
-          const int kb1 = 2 * j + 1 < count ? list[2 * j + 1] : kb0;  // a masked stand-in
+          const int kb0 = slist[2 * j];
+          const int kb1 = 2 * j + 1 < count ? slist[2 * j + 1] : kb0;  // a masked stand-in
 #pragma unroll
           for (int h2 = 0; h2 < NH; ++h2) {
             tma_load_4d(sk + h2 * L::HALF, &mk, &kv_full[stage], h2 * 64, kb0 * 64, head, 0);
@@ -433,13 +458,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     float m_run[2] = {-INFINITY, -INFINITY};
     float l_run[2] = {0.0f, 0.0f};
     bool ok = true;
-    for (int j = 0; j < nblk && ok; ++j) {
-      // this warp's 64 keys: exact block kb (or none), or centroids c0 .. c0 + 63
-      const bool exact = j < ns;
+    // one stage of this warp: 64 keys, an exact block kb (or none) or centroids c0 .. c0 + 63;
+    // instantiated once per kind so that each loop's body stays compact
+    auto stage = [&](const int j, auto kind) {
+      constexpr bool exact = decltype(kind)::value;
       int kb = -1, nk = 0, c0 = 0;
-      if (exact) {
+      if constexpr (exact) {
         const int li = 2 * j + half;
-        kb = li < count ? list[li] : -1;
+        kb = li < count ? slist[li] : -1;
         nk = kb >= 0 ? min(SOL_BLOCK, p.tokens - kb * SOL_BLOCK) : 0;
       } else {
         c0 = (j - ns) * 128 + half * 64;
@@ -456,16 +482,36 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tmem_ld32(s_col, sr[0]);
         tmem_ld32(s_col + 32, sr[1]);
         tmem_wait_ld();
-        // log2-domain logits with the routing applied; -inf where a key does not take part
-        if (exact) {
-          const bool routed = kb >= 0 && ((rw[kb >> 5] >> (kb & 31)) & 1u);
+        // An exact block is all or nothing for a row: its logits are s * scale - m, folded into
+        // one packed FMA per pair with a per-row (scale, offset) = (sl2, -m), or (0, -inf) when
+        // the row does not route the block. Centroid logits carry a per-key bias (log2 of the
+        // block's length) or -inf; they are formed here, already scaled.
+        bool routed_row = true;
+        float mine;
+        if constexpr (exact) {
+          routed_row = kb >= 0 && ((rw[kb >> 5] >> (kb & 31)) & 1u);
+          if (nk < SOL_BLOCK) {  // the last, partial block (warp-uniform): finite sentinel
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
+            for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              sr[c][i] = __float_as_uint((routed && c * 32 + i < nk)
-                                             ? __uint_as_float(sr[c][i]) * sl2
-                                             : -INFINITY);
+              for (int i = 0; i < 32; ++i)
+                if (c * 32 + i >= nk) sr[c][i] = __float_as_uint(-1.0e30f);
+          }
+          float mq[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
+            float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+            a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
+            a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
+            a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
+            a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
+            a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
+            a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
+            mq[q] = fmaxf(a, __uint_as_float(v[15]));
+          }
+          const float raw = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+          mine = routed_row ? raw * sl2 : -INFINITY;
         } else {
           const int w0 = c0 >> 5;
           const uint32_t words[2] = {w0 < p.words ? rw[w0] : ~0u,
@@ -480,21 +526,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
               sr[c][i] = __float_as_uint(take ? fmaf(__uint_as_float(sr[c][i]), sl2, bias)
                                               : -INFINITY);
             }
-        }
-        float mq[4];
+          float mq[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
-          float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
-          a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
-          a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
-          a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
-          a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
-          a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
-          a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
-          mq[q] = fmaxf(a, __uint_as_float(v[15]));
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
+            float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+            a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
+            a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
+            a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
+            a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
+            a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
+            a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
+            mq[q] = fmaxf(a, __uint_as_float(v[15]));
+          }
+          mine = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
         }
-        const float mine = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
         float* xm = xmax + (t * 2 + (j & 1)) * 256;
         xm[half * 128 + row] = mine;
         uint64_t* xb = &xbar[(quarter * 2 + t) * 2 + (j & 1)];
@@ -519,7 +565,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         // a row with no logit so far subtracts 0: its exponentials are all 0 (or 2^-126)
         const float msub = m_run[t] == -INFINITY ? 0.0f : m_run[t];
-        const uint64_t negm = f2_pack(-msub, -msub);
+        const float scl = exact ? (routed_row ? sl2 : 0.0f) : 1.0f;
+        const float off = (exact && !routed_row) ? -INFINITY : -msub;
+        const uint64_t sc2 = f2_pack(scl, scl);
+        const uint64_t negm = f2_pack(off, off);
         uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {
@@ -529,7 +578,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             const int i = q8 * 8 + u;
             const uint32_t* v = sr[i >> 4];
             const int e = (2 * i) & 31;
-            const uint64_t xs = f2_add(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), negm);
+            const uint64_t xs =
+                f2_fma(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2, negm);
             uint64_t ev;
             if ((ATT_EMU_MASK >> (i & 7)) & 1) {
               ev = exp2_poly_x2(xs);
@@ -562,7 +612,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[t]);
       }
-    }
+    };
+    for (int j = 0; j < ns && ok; ++j) stage(j, std::true_type{});
+    for (int j = ns; j < nblk && ok; ++j) stage(j, std::false_type{});
     if (ok && nblk > 0) {
       for (int t = 0; t < ntile; ++t) xsum[(t * 2 + half) * 128 + row] = l_run[t];
       mbar_arrive(&lbar[quarter]);
