@@ -873,7 +873,11 @@ kino_status kino_sol_attention(const kino_sol_attention_args* a, void* stream) {
   const double ls = 1.4426950408889634 / sqrt(128.0);
   const dim3 grid_route(static_cast<unsigned>((l.nb + kino::SOL_ROUTE_ROWS - 1) / kino::SOL_ROUTE_ROWS),
                         static_cast<unsigned>(heads));
-  launch_pdl(kino::sol_route_kernel, grid_route, dim3(256), 0, st, qmean, kmean,
+  const int route_smem = kino::sol_route_smem(static_cast<int>(l.nb));
+  if ((s = ensure_smem(kino::sol_route_kernel, kino::sol_route_smem(kino::SOL_MAX_WORDS * 32), 13)) !=
+      KINO_OK)
+    return s;
+  launch_pdl(kino::sol_route_kernel, grid_route, dim3(256), route_smem, st, qmean, kmean,
              static_cast<int>(l.nb), static_cast<int>(l.words), static_cast<float>(ls),
              static_cast<float>(ls * ls), a->tau, bits);
   s = check_launch("kino_sol_attention (route)");
@@ -913,8 +917,7 @@ kino_status kino_sol_attention(const kino_sol_attention_args* a, void* stream) {
   p.out_f16 = a->dtype == KINO_DTYPE_F16 ? 1 : 0;
   p.gate = a->gate;
   p.ld_gate = a->ld_gate;
-  // + the CTA's routing words (4 x 16 words) and its block list (at most 512 entries)
-  constexpr int smem = kino::AttnSmem::TOTAL + 256 + kino::SOL_MAX_WORDS * 32 * 4;
+  constexpr int smem = kino::SolSmem::TOTAL;
   if ((s = ensure_smem(kino::sol_attention_kernel, smem, 12)) != KINO_OK) return s;
   launch_pdl(kino::sol_attention_kernel, dim3(static_cast<unsigned>(l.ncta), heads),
              dim3(kino::ATT_THREADS), smem, st, mq, mk, mv, mkc, mvc, p);

@@ -32,7 +32,7 @@ namespace kino {
 
 constexpr int SOL_BLOCK = 64;
 constexpr int SOL_MAX_WORDS = 16;  // mask words per query block: at most 512 blocks
-constexpr int SOL_QBLOCKS = 4;     // query blocks per attention CTA (two 128-row tiles)
+constexpr int SOL_QBLOCKS = 2;     // query blocks per attention CTA (one 128-row tile)
 
 __device__ __forceinline__ float sol_sat(float x) { return fminf(fmaxf(x, -65504.0f), 65504.0f); }
 
@@ -132,13 +132,19 @@ __global__ void __launch_bounds__(128)
   vmean[m] = __float2half_rn(sol_sat(sol_round_in<In>(sum[2])));
 }
 
-// grid (ceil(blocks / 8), heads), 256 threads: the routing rows of eight query blocks, one per
-// warp. The key-mean center and per-dimension variance over the blocks come first (thread d < 128
-// for dimension d); then each warp forms its row's limit, the row's mean score plus tau standard
-// deviations under a diagonal key covariance, and scores 32 key blocks at a time (lane l takes
-// block 32 i + l: a 128-long dot product against its mean key), a ballot turning the comparisons
-// into mask word i (kinomlx/models/ltx2/kernels/sol_attention.py:181-216).
-constexpr int SOL_ROUTE_ROWS = 8;
+// grid (ceil(blocks / 32), heads), 256 threads: the routing rows of 32 query blocks, four per
+// warp (kinomlx/models/ltx2/kernels/sol_attention.py:181-216). The head's key means are staged in
+// shared memory once (16-byte loads, all in flight), their center and per-dimension variance
+// reduced in a fixed order; each row's limit is its mean score plus tau standard deviations
+// under a diagonal key covariance. Scores: for 32 key blocks at a time every lane keeps the
+// partial products of its 4 dimensions with each of the 32 keys, and a butterfly
+// (reduce-scatter over the lanes, 31 shuffles) leaves lane l with the full score of key block
+// base + l; a ballot turns the 32 comparisons into one mask word.
+constexpr int SOL_ROUTE_ROWS = 32;
+
+__host__ __device__ constexpr int sol_route_smem(int nb) {
+  return nb * 128 * 2 + (16 * 128 + 128 + 128 + SOL_ROUTE_ROWS * 128) * 4;
+}
 
 __global__ void __launch_bounds__(256)
     sol_route_kernel(const float* __restrict__ qmean, const __half* __restrict__ kmean, int nb,
@@ -146,70 +152,107 @@ __global__ void __launch_bounds__(256)
                      uint32_t* __restrict__ bits) {
   griddep_wait();
   griddep_launch();
-  __shared__ float center[128], var[128];
-  __shared__ float qs[SOL_ROUTE_ROWS][128];
+  extern __shared__ __align__(16) uint8_t rsm[];
+  __half* ks = reinterpret_cast<__half*>(rsm);
+  float* part = reinterpret_cast<float*>(rsm + nb * 256);
+  float* center = part + 16 * 128;
+  float* var = center + 128;
+  float* qs = var + 128;  // [SOL_ROUTE_ROWS][128]
   const int h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __half* kh = kmean + static_cast<int64_t>(h) * nb * 128;
-  if (tid < 128) {
-    float s = 0.0f;
-    for (int b = 0; b < nb; ++b) s += __half2float(kh[b * 128 + tid]);
-    const float c = s / static_cast<float>(nb);
-    float s2 = 0.0f;
-    for (int b = 0; b < nb; ++b) {
-      const float dl = __half2float(kh[b * 128 + tid]) - c;
-      s2 += dl * dl;
-    }
-    center[tid] = c;
-    var[tid] = s2 / static_cast<float>(nb);
-  }
+  for (int i = tid; i < nb * 16; i += 256)
+    reinterpret_cast<uint4*>(ks)[i] = reinterpret_cast<const uint4*>(kh)[i];
   const int a0 = blockIdx.x * SOL_ROUTE_ROWS;
   for (int i = tid; i < SOL_ROUTE_ROWS * 128; i += 256) {
     const int r = i >> 7, a = a0 + r;
-    qs[r][i & 127] = a < nb ? qmean[(static_cast<int64_t>(h) * nb + a) * 128 + (i & 127)] : 0.0f;
+    qs[i] = a < nb ? qmean[(static_cast<int64_t>(h) * nb + a) * 128 + (i & 127)] : 0.0f;
   }
   __syncthreads();
-  const int a = a0 + warp;
-  if (a >= nb) return;
-  const float* q = qs[warp];
-  float rm = 0.0f, rv = 0.0f;
+  const int rg = tid >> 4, cv = tid & 15;
+  for (int pass = 0; pass < 2; ++pass) {
+    float acc[8];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int d = lane + 32 * k;
-    rm += q[d] * center[d];
-    rv += q[d] * q[d] * var[d];
-  }
-  const float raw_mean = warp_sum_f(rm);
-  const float raw_var = warp_sum_f(rv);
-  const float variance = fmaxf(raw_var, 0.0f) * log2_scale_sq;
-  const float limit = raw_mean * log2_scale + tau * sqrtf(variance + 1.0e-6f);
-  uint32_t* row = bits + (static_cast<int64_t>(h) * nb + a) * words;
-  for (int w = 0; w < words; ++w) {
-    const int b = w * 32 + lane;
-    bool routed = false;
-    if (b < nb) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kh + b * 128);
-      float dot = 0.0f;
-#pragma unroll 4
-      for (int c = 0; c < 16; ++c) {
-        const uint4 raw = kr[c];
-        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+    for (int b = rg; b < nb; b += 16) {
+      const uint4 raw = reinterpret_cast<const uint4*>(ks + b * 128)[cv];
+      const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 kv = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
-          dot = fmaf(q[c * 8 + 2 * e], kv.x, dot);
-          dot = fmaf(q[c * 8 + 2 * e + 1], kv.y, dot);
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+        if (pass == 0) {
+          acc[2 * e] += f.x;
+          acc[2 * e + 1] += f.y;
+        } else {
+          const float d0 = f.x - center[cv * 8 + 2 * e], d1 = f.y - center[cv * 8 + 2 * e + 1];
+          acc[2 * e] += d0 * d0;
+          acc[2 * e + 1] += d1 * d1;
         }
       }
-      routed = (b >= a - 1 && b <= a + 1) || dot * log2_scale > limit;
     }
-    const uint32_t word = __ballot_sync(0xffffffffu, routed);
-    if (lane == 0) row[w] = word;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[rg * 128 + cv * 8 + e] = acc[e];
+    __syncthreads();
+    if (tid < 128) {
+      float t = 0.0f;
+      for (int r = 0; r < 16; ++r) t += part[r * 128 + tid];
+      (pass == 0 ? center : var)[tid] = t / static_cast<float>(nb);
+    }
+    __syncthreads();
+  }
+  for (int rr = 0; rr < SOL_ROUTE_ROWS / 8; ++rr) {
+    const int r = warp * (SOL_ROUTE_ROWS / 8) + rr;
+    const int a = a0 + r;
+    if (a >= nb) break;  // warp-uniform
+    const float* q = qs + r * 128;
+    float rm = 0.0f, rv = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int d = lane + 32 * k;
+      rm += q[d] * center[d];
+      rv += q[d] * q[d] * var[d];
+    }
+    const float raw_mean = warp_sum_f(rm);
+    const float raw_var = warp_sum_f(rv);
+    const float variance = fmaxf(raw_var, 0.0f) * log2_scale_sq;
+    const float limit = raw_mean * log2_scale + tau * sqrtf(variance + 1.0e-6f);
+    const float q0 = q[lane * 4], q1 = q[lane * 4 + 1], q2 = q[lane * 4 + 2], q3 = q[lane * 4 + 3];
+    uint32_t* row = bits + (static_cast<int64_t>(h) * nb + a) * words;
+    for (int w = 0; w < words; ++w) {
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int b = w * 32 + i;
+        float dot = 0.0f;
+        if (b < nb) {  // uniform across the warp
+          const uint2 raw = reinterpret_cast<const uint2*>(ks + b * 128)[lane];
+          const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+          const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+          dot = fmaf(q0, k01.x, fmaf(q1, k01.y, fmaf(q2, k23.x, q3 * k23.y)));
+        }
+        v[i] = dot;
+      }
+#pragma unroll
+      for (int sh = 16; sh >= 1; sh >>= 1) {
+        const bool upper = (lane & sh) != 0;
+#pragma unroll
+        for (int i = 0; i < sh; ++i) {
+          const float send = upper ? v[i] : v[i + sh];
+          const float keep = upper ? v[i + sh] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, sh);
+        }
+      }
+      const int b = w * 32 + lane;
+      const bool routed = b < nb && ((b >= a - 1 && b <= a + 1) || v[0] * log2_scale > limit);
+      const uint32_t word = __ballot_sync(0xffffffffu, routed);
+      if (lane == 0) row[w] = word;
+    }
   }
 }
 
-// grid (CTAs per head, heads), 32 threads: the union of the routing rows of query blocks
-// 4c .. 4c + 3 as an ascending block list and its length.
+// grid (CTAs per head, heads), 32 threads: the union of the routing rows of the CTA's query
+// blocks (SOL_QBLOCKS c .. SOL_QBLOCKS c + SOL_QBLOCKS - 1) as an ascending block list and its
+// length.
 __global__ void __launch_bounds__(32)
     sol_union_kernel(const uint32_t* __restrict__ bits, int nb, int words,
                      int* __restrict__ lists, int* __restrict__ counts) {
@@ -260,13 +303,38 @@ struct SolParams {
   int64_t ld_gate;
 };
 
+// Shared memory of sol_attention_kernel: one 128-row query tile, two 128-key K/V stages, the
+// softmax exchange areas and barriers of the dense kernel, then the CTA's routing words and
+// block list.
+struct SolSmem {
+  static constexpr int HALF = AttnSmem::HALF;
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = 2 * HALF;
+  static constexpr int STAGE = 4 * HALF;
+  static constexpr int X_OFF = KV_OFF + ATT_STAGES * STAGE;
+  static constexpr int L_OFF = X_OFF + 2 * 2 * 2 * 128 * 4;
+  static constexpr int BAR_OFF = L_OFF + 2 * 2 * 128 * 4;
+  static constexpr int NBAR = AttnSmem::NBAR;
+  static constexpr int W_OFF = BAR_OFF + NBAR * 8 + 16;
+  static constexpr int LIST_OFF = W_OFF + SOL_QBLOCKS * SOL_MAX_WORDS * 4;
+  static constexpr int TOTAL = LIST_OFF + SOL_MAX_WORDS * 32 * 4 + 1024;
+};
+
+// One CTA: query blocks 2c and 2c + 1 (one 128-row tile) against the ascending list of key
+// blocks either of them routes, then the centroids. The stages (two 64-key blocks, or 128
+// centroids) alternate between two key streams, A taking stages 0, 2, 4, ... and B stages
+// 1, 3, 5, ...: each stream has its own S and O in tensor memory and its own running row
+// maxima and sums, so the MMA warp works on one stream while the softmax warps work on the
+// other (the dense kernel's ping-pong, over key halves of one query tile instead of over two
+// query tiles), and the epilogue merges the two streams by their row statistics. Stage i
+// lives in K/V slot i % 2, so each stream owns a slot.
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     sol_attention_kernel(const __grid_constant__ CUtensorMap mq,
                          const __grid_constant__ CUtensorMap mk,
                          const __grid_constant__ CUtensorMap mv,
                          const __grid_constant__ CUtensorMap mkc,
                          const __grid_constant__ CUtensorMap mvc, const SolParams p) {
-  using L = AttnSmem;
+  using L = SolSmem;
   constexpr int D = 128;
   constexpr int NH = 2;
   constexpr int SUB = 64 * 128;  // one 64-row box of a 64-wide swizzled half: 8 KB
@@ -277,27 +345,24 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + ATT_STAGES;
-  uint64_t* s_full = kv_empty + ATT_STAGES;
-  uint64_t* p_full = s_full + 2;
+  uint64_t* s_full = kv_empty + ATT_STAGES;  // [stream]
+  uint64_t* p_full = s_full + 2;             // [stream]
   uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 1;
-  uint64_t* xbar = drain + 1;
-  uint64_t* lbar = xbar + 16;
+  uint64_t* xbar = drain + 1;                // [quarter][stream][parity]
+  uint64_t* lbar = xbar + 16;                // [quarter]
   float* xmax = reinterpret_cast<float*>(smem + L::X_OFF);
   float* xsum = reinterpret_cast<float*>(smem + L::L_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // routing words of the CTA's four query blocks and its block list, after the barrier block
-  uint32_t* rwords = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBAR * 8 + 16);
-  int* slist = reinterpret_cast<int*>(rwords + SOL_QBLOCKS * SOL_MAX_WORDS);
+  uint32_t* rwords = reinterpret_cast<uint32_t*>(smem + L::W_OFF);
+  int* slist = reinterpret_cast<int*>(smem + L::LIST_OFF);
 
   const int warp = warp_id();
   const uint32_t lane = lane_id();
   const int cta = blockIdx.x;
   const int head = blockIdx.y;
-  const int row0 = cta * 256;  // tile t covers routed rows [row0 + 128 t, row0 + 128 t + 128)
-  const bool has_b = row0 + 128 < p.tokens;
-  const int ntile = has_b ? 2 : 1;
+  const int row0 = cta * 128;
   const int* list = p.lists + (static_cast<int64_t>(head) * p.ncta + cta) * p.nb;
 
   if (threadIdx.x == 0) {
@@ -327,8 +392,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   }
   const int count = p.counts[head * p.ncta + cta];
   for (int i = threadIdx.x; i < count; i += blockDim.x) slist[i] = list[i];
-  const int ns = (count + 1) / 2;               // exact stages: two 64-key blocks each
-  const int nblk = ns + (p.nb + 127) / 128;     // then the centroid stages
+  const int ns = (count + 1) / 2;            // exact stages: two 64-key blocks each
+  const int nst = ns + (p.nb + 127) / 128;   // then the centroid stages
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -341,38 +406,35 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, ntile * NH * L::HALF);
-      for (int t = 0; t < ntile; ++t) {
-        uint8_t* sq = smem + L::Q_OFF + t * 2 * L::HALF;
-        tma_load_4d(sq, &mq, q_full, 0, row0 + t * 128, head, 0);
-        tma_load_4d(sq + L::HALF, &mq, q_full, 64, row0 + t * 128, head, 0);
-      }
+      mbar_expect_tx(q_full, NH * L::HALF);
+      tma_load_4d(smem + L::Q_OFF, &mq, q_full, 0, row0, head, 0);
+      tma_load_4d(smem + L::Q_OFF + L::HALF, &mq, q_full, 64, row0, head, 0);
       int issued = 0;
-      for (int j = 0; j < nblk; ++j) {
-        const int stage = j % ATT_STAGES;
-        const uint32_t parity = (j / ATT_STAGES) & 1;
-        if (!mbar_wait(&kv_empty[stage], parity ^ 1u, abort_flag)) break;
-        uint8_t* sk = smem + L::KV_OFF + stage * L::STAGE;
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i & 1;
+        const uint32_t parity = (i >> 1) & 1;
+        if (!mbar_wait(&kv_empty[slot], parity ^ 1u, abort_flag)) break;
+        uint8_t* sk = smem + L::KV_OFF + slot * L::STAGE;
         uint8_t* sv = sk + 2 * L::HALF;
-        mbar_expect_tx(&kv_full[stage], 2 * NH * L::HALF);
-        if (j < ns) {
-          const int kb0 = slist[2 * j];
-          const int kb1 = 2 * j + 1 < count ? slist[2 * j + 1] : kb0;  // a masked stand-in
+        mbar_expect_tx(&kv_full[slot], 2 * NH * L::HALF);
+        if (i < ns) {
+          const int kb0 = slist[2 * i];
+          const int kb1 = 2 * i + 1 < count ? slist[2 * i + 1] : kb0;  // a masked stand-in
 #pragma unroll
           for (int h2 = 0; h2 < NH; ++h2) {
-            tma_load_4d(sk + h2 * L::HALF, &mk, &kv_full[stage], h2 * 64, kb0 * 64, head, 0);
-            tma_load_4d(sk + h2 * L::HALF + SUB, &mk, &kv_full[stage], h2 * 64, kb1 * 64, head, 0);
-            tma_load_4d(sv + h2 * L::HALF, &mv, &kv_full[stage], h2 * 64, kb0 * 64, head, 0);
-            tma_load_4d(sv + h2 * L::HALF + SUB, &mv, &kv_full[stage], h2 * 64, kb1 * 64, head, 0);
+            tma_load_4d(sk + h2 * L::HALF, &mk, &kv_full[slot], h2 * 64, kb0 * 64, head, 0);
+            tma_load_4d(sk + h2 * L::HALF + SUB, &mk, &kv_full[slot], h2 * 64, kb1 * 64, head, 0);
+            tma_load_4d(sv + h2 * L::HALF, &mv, &kv_full[slot], h2 * 64, kb0 * 64, head, 0);
+            tma_load_4d(sv + h2 * L::HALF + SUB, &mv, &kv_full[slot], h2 * 64, kb1 * 64, head, 0);
           }
         } else {
-          const int c0 = (j - ns) * 128;
+          const int c0 = (i - ns) * 128;
 #pragma unroll
           for (int h2 = 0; h2 < NH; ++h2) {
-            tma_load_3d(sk + h2 * L::HALF, &mkc, &kv_full[stage], h2 * 64, c0, head);
-            tma_load_3d(sk + h2 * L::HALF + SUB, &mkc, &kv_full[stage], h2 * 64, c0 + 64, head);
-            tma_load_3d(sv + h2 * L::HALF, &mvc, &kv_full[stage], h2 * 64, c0, head);
-            tma_load_3d(sv + h2 * L::HALF + SUB, &mvc, &kv_full[stage], h2 * 64, c0 + 64, head);
+            tma_load_3d(sk + h2 * L::HALF, &mkc, &kv_full[slot], h2 * 64, c0, head);
+            tma_load_3d(sk + h2 * L::HALF + SUB, &mkc, &kv_full[slot], h2 * 64, c0 + 64, head);
+            tma_load_3d(sv + h2 * L::HALF, &mvc, &kv_full[slot], h2 * 64, c0, head);
+            tma_load_3d(sv + h2 * L::HALF + SUB, &mvc, &kv_full[slot], h2 * 64, c0 + 64, head);
           }
         }
         ++issued;
@@ -381,9 +443,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const uint64_t t0 = global_ns();
         while (!mbar_try_wait(q_full, 0) && global_ns() - t0 < 200000000ull) {
         }
-        for (int j = issued - 1; j >= 0 && j >= issued - ATT_STAGES; --j) {
+        for (int i = issued - 1; i >= 0 && i >= issued - ATT_STAGES; --i) {
           const uint64_t t1 = global_ns();
-          while (!mbar_try_wait(&kv_full[j % ATT_STAGES], (j / ATT_STAGES) & 1) &&
+          while (!mbar_try_wait(&kv_full[i & 1], (i >> 1) & 1) &&
                  global_ns() - t1 < 200000000ull) {
           }
         }
@@ -393,9 +455,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(ATT_BM, ATT_BN);
       constexpr uint32_t idesc_o = idesc_f16(ATT_BM, D) | (1u << 16);  // B (V) MN-major
-      auto s_mma = [&](int t, int j) {
-        const uint32_t sq = smem_u32(smem + L::Q_OFF + t * 2 * L::HALF);
-        const uint32_t sk = smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE);
+      const uint32_t sq = smem_u32(smem + L::Q_OFF);
+      auto s_mma = [&](int t) {  // S_t = Q K^T of the stage in slot t
+        const uint32_t sk = smem_u32(smem + L::KV_OFF + t * L::STAGE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::HALF + (kk & 3) * 32;
@@ -404,42 +466,41 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         umma_commit(&s_full[t]);
       };
-      auto pv_mma = [&](int t, int j) {
-        const uint32_t sv =
-            smem_u32(smem + L::KV_OFF + (j % ATT_STAGES) * L::STAGE + 2 * L::HALF);
+      auto pv_mma = [&](int t, bool first) {  // O_t += P_t V of the stage in slot t
+        const uint32_t sv = smem_u32(smem + L::KV_OFF + t * L::STAGE + 2 * L::HALF);
 #pragma unroll
         for (int kk = 0; kk < ATT_BN / 16; ++kk) {
           umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8 + (kk >= 4 ? 32 : 0),
                        sdesc_mn128(sv + kk * 2048, L::HALF), idesc_o,
-                       (j > 0 || kk > 0) ? 1u : 0u);
+                       (!first || kk > 0) ? 1u : 0u);
         }
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag) && nblk > 0;
-      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < ntile; ++t) s_mma(t, 0);
+      bool ok = mbar_wait(q_full, 0, abort_flag) && nst > 0;
+      for (int t = 0; ok && t < 2 && t < nst; ++t) {
+        ok = mbar_wait(&kv_full[t], 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          s_mma(t);
+        }
       }
-      for (int j = 0; ok && j < nblk; ++j) {
-        const bool more = j + 1 < nblk;
-        for (int t = 0; t < ntile && ok; ++t) {
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag)) {
+      for (int k = 0; ok && 2 * k < nst; ++k) {
+        for (int t = 0; t < 2 && ok; ++t) {
+          const int i = 2 * k + t;
+          if (i >= nst) break;
+          if (!mbar_wait(&p_full[t], k & 1, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          pv_mma(t, j);
-          if (t == ntile - 1) umma_commit(&kv_empty[j % ATT_STAGES]);
-          if (more) {
-            if (t == 0) {
-              if (!mbar_wait(&kv_full[(j + 1) % ATT_STAGES], ((j + 1) / ATT_STAGES) & 1,
-                             abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
+          pv_mma(t, k == 0);
+          umma_commit(&kv_empty[t]);
+          if (i + 2 < nst) {
+            if (!mbar_wait(&kv_full[t], (k + 1) & 1, abort_flag)) {
+              ok = false;
+              break;
             }
-            s_mma(t, j + 1);
+            tc_fence_after();
+            s_mma(t);
           }
         }
       }
@@ -455,219 +516,214 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int row = quarter * 32 + static_cast<int>(lane);
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = p.scale_log2;
+    const uint32_t* rw = rwords + (row >> 6) * SOL_MAX_WORDS;  // this row's query block
     float m_run[2] = {-INFINITY, -INFINITY};
     float l_run[2] = {0.0f, 0.0f};
     bool ok = true;
-    // one stage of this warp: 64 keys, an exact block kb (or none) or centroids c0 .. c0 + 63;
-    // instantiated once per kind so that each loop's body stays compact
-    auto stage = [&](const int j, auto kind) {
+    // stage i (the k-th of stream t) for this warp's 64 keys: an exact block kb (or none) or
+    // centroids c0 .. c0 + 63; instantiated once per kind so each loop's body stays compact
+    auto stage = [&](const int i, const int t, const int k, auto kind) {
       constexpr bool exact = decltype(kind)::value;
       int kb = -1, nk = 0, c0 = 0;
       if constexpr (exact) {
-        const int li = 2 * j + half;
+        const int li = 2 * i + half;
         kb = li < count ? slist[li] : -1;
         nk = kb >= 0 ? min(SOL_BLOCK, p.tokens - kb * SOL_BLOCK) : 0;
       } else {
-        c0 = (j - ns) * 128 + half * 64;
+        c0 = (i - ns) * 128 + half * 64;
       }
-      for (int t = 0; t < ntile; ++t) {
-        if (!mbar_wait(&s_full[t], j & 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t* rw = rwords + (2 * t + (row >> 6)) * SOL_MAX_WORDS;
-        const uint32_t s_col = tmem + lane_base + t * 128 + half * 64;
-        uint32_t sr[2][32];
-        tmem_ld32(s_col, sr[0]);
-        tmem_ld32(s_col + 32, sr[1]);
-        tmem_wait_ld();
-        // An exact block is all or nothing for a row: its logits are s * scale - m, folded into
-        // one packed FMA per pair with a per-row (scale, offset) = (sl2, -m), or (0, -inf) when
-        // the row does not route the block. Centroid logits carry a per-key bias (log2 of the
-        // block's length) or -inf; they are formed here, already scaled.
-        bool routed_row = true;
-        float mine;
-        if constexpr (exact) {
-          routed_row = kb >= 0 && ((rw[kb >> 5] >> (kb & 31)) & 1u);
-          if (nk < SOL_BLOCK) {  // the last, partial block (warp-uniform): finite sentinel
-#pragma unroll
-            for (int c = 0; c < 2; ++c)
-#pragma unroll
-              for (int i = 0; i < 32; ++i)
-                if (c * 32 + i >= nk) sr[c][i] = __float_as_uint(-1.0e30f);
-          }
-          float mq[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
-            float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
-            a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
-            a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
-            a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
-            a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
-            a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
-            a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
-            mq[q] = fmaxf(a, __uint_as_float(v[15]));
-          }
-          const float raw = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-          mine = routed_row ? raw * sl2 : -INFINITY;
-        } else {
-          const int w0 = c0 >> 5;
-          const uint32_t words[2] = {w0 < p.words ? rw[w0] : ~0u,
-                                     w0 + 1 < p.words ? rw[w0 + 1] : ~0u};
+      if (!mbar_wait(&s_full[t], k & 1, abort_flag)) {
+        ok = false;
+        return;
+      }
+      tc_fence_after();
+      const uint32_t s_col = tmem + lane_base + t * 128 + half * 64;
+      uint32_t sr[2][32];
+      tmem_ld32(s_col, sr[0]);
+      tmem_ld32(s_col + 32, sr[1]);
+      tmem_wait_ld();
+      // An exact block is all or nothing for a row: its logits are s * scale - m, folded into
+      // one packed FMA per pair with a per-row (scale, offset) = (sl2, -m), or (0, -inf) when
+      // the row does not route the block. Centroid logits carry a per-key bias (log2 of the
+      // block's length) or -inf; they are formed here, already scaled.
+      bool routed_row = true;
+      float mine;
+      if constexpr (exact) {
+        routed_row = kb >= 0 && ((rw[kb >> 5] >> (kb & 31)) & 1u);
+        if (nk < SOL_BLOCK) {  // the last, partial block (warp-uniform): finite sentinel
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int b = c0 + c * 32 + i;
-              const float bias = b == p.nb - 1 ? p.last_log2 : 6.0f;
-              const bool take = b < p.nb && !((words[c] >> i) & 1u);
-              sr[c][i] = __float_as_uint(take ? fmaf(__uint_as_float(sr[c][i]), sl2, bias)
-                                              : -INFINITY);
-            }
-          float mq[4];
+            for (int j = 0; j < 32; ++j)
+              if (c * 32 + j >= nk) sr[c][j] = __float_as_uint(-1.0e30f);
+        }
+      } else {
+        const int w0 = c0 >> 5;
+        const uint32_t words[2] = {w0 < p.words ? rw[w0] : ~0u,
+                                   w0 + 1 < p.words ? rw[w0 + 1] : ~0u};
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
-            float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
-            a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
-            a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
-            a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
-            a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
-            a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
-            a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
-            mq[q] = fmaxf(a, __uint_as_float(v[15]));
-          }
-          mine = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-        }
-        float* xm = xmax + (t * 2 + (j & 1)) * 256;
-        xm[half * 128 + row] = mine;
-        uint64_t* xb = &xbar[(quarter * 2 + t) * 2 + (j & 1)];
-        mbar_arrive(xb);
-        if (!mbar_wait(xb, (j >> 1) & 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        const float m_blk = fmaxf(mine, xm[(1 - half) * 128 + row]);
-        float alpha = 1.0f;
-        bool rescale = false;
-        if (j > 0) {
-          const bool need = m_blk > m_run[t] + 8.0f;
-          rescale = __any_sync(0xffffffffu, need);
-          if (need) {
-            alpha = ex2_approx(m_run[t] - m_blk);  // 0 while the row had no logit yet
-            m_run[t] = m_blk;
-            l_run[t] *= alpha;
-          }
-        } else {
-          m_run[t] = m_blk;
-        }
-        // a row with no logit so far subtracts 0: its exponentials are all 0 (or 2^-126)
-        const float msub = m_run[t] == -INFINITY ? 0.0f : m_run[t];
-        const float scl = exact ? (routed_row ? sl2 : 0.0f) : 1.0f;
-        const float off = (exact && !routed_row) ? -INFINITY : -msub;
-        const uint64_t sc2 = f2_pack(scl, scl);
-        const uint64_t negm = f2_pack(off, off);
-        uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          uint32_t packed[8];
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int i = q8 * 8 + u;
-            const uint32_t* v = sr[i >> 4];
-            const int e = (2 * i) & 31;
-            const uint64_t xs =
-                f2_fma(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2, negm);
-            uint64_t ev;
-            if ((ATT_EMU_MASK >> (i & 7)) & 1) {
-              ev = exp2_poly_x2(xs);
-            } else {
-              const float2 xv = f2_unpack(xs);
-              ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
-            }
-            lsum2[u & 1] = f2_add(lsum2[u & 1], ev);
-            const float2 e2 = f2_unpack(ev);
-            packed[u] = pack_f16x2(e2.x, e2.y);
+          for (int j = 0; j < 32; ++j) {
+            const int b = c0 + c * 32 + j;
+            const float bias = b == p.nb - 1 ? p.last_log2 : 6.0f;
+            const bool take = b < p.nb && !((words[c] >> j) & 1u);
+            sr[c][j] = __float_as_uint(take ? fmaf(__uint_as_float(sr[c][j]), sl2, bias)
+                                            : -INFINITY);
           }
-          tmem_st8(s_col + q8 * 8, packed);
-        }
-        const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
-        l_run[t] += ls.x + ls.y;
-        if (rescale) {
-          const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * (D / 2);
-#pragma unroll 1
-          for (int c = 0; c < D / 64; ++c) {
-            uint32_t o[32];
-            tmem_ld32(o_col + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(o_col + c * 32, o);
-          }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[t]);
       }
-    };
-    for (int j = 0; j < ns && ok; ++j) stage(j, std::true_type{});
-    for (int j = ns; j < nblk && ok; ++j) stage(j, std::false_type{});
-    if (ok && nblk > 0) {
-      for (int t = 0; t < ntile; ++t) xsum[(t * 2 + half) * 128 + row] = l_run[t];
-      mbar_arrive(&lbar[quarter]);
-      ok = mbar_wait(&lbar[quarter], 0, abort_flag);
-    }
-    if (ok && nblk > 0 && mbar_wait(o_done, 0, abort_flag)) {
-      tc_fence_after();
-      for (int t = 0; t < ntile; ++t) {
-        const int tok = row0 + t * 128 + row;
-        bool store = tok < p.tokens;
-        const float inv_l = 1.0f / (l_run[t] + xsum[(t * 2 + 1 - half) * 128 + row]);
-        const int64_t dst_row = store ? p.order[tok] : 0;
-        if (store && (dst_row < 0 || dst_row >= p.tokens)) {
-          atomicExch(&g_device_error, 1);
-          store = false;
+      float mq[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
+        float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+        a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
+        a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
+        a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
+        a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
+        a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
+        a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
+        mq[q] = fmaxf(a, __uint_as_float(v[15]));
+      }
+      const float raw = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      if constexpr (exact)
+        mine = routed_row ? raw * sl2 : -INFINITY;
+      else
+        mine = raw;
+      float* xm = xmax + (t * 2 + (k & 1)) * 256;
+      xm[half * 128 + row] = mine;
+      uint64_t* xb = &xbar[(quarter * 2 + t) * 2 + (k & 1)];
+      mbar_arrive(xb);
+      if (!mbar_wait(xb, (k >> 1) & 1, abort_flag)) {
+        ok = false;
+        return;
+      }
+      const float m_blk = fmaxf(mine, xm[(1 - half) * 128 + row]);
+      float alpha = 1.0f;
+      bool rescale = false;
+      if (k > 0) {
+        const bool need = m_blk > m_run[t] + 8.0f;
+        rescale = __any_sync(0xffffffffu, need);
+        if (need) {
+          alpha = ex2_approx(m_run[t] - m_blk);  // 0 while the row had no logit yet
+          m_run[t] = m_blk;
+          l_run[t] *= alpha;
         }
-        float gv = 1.0f;
-        if (p.gate != nullptr && store) {
-          const int64_t gi = dst_row * p.ld_gate + head;
-          gv = p.out_f16 ? __half2float(static_cast<const __half*>(p.gate)[gi])
-                         : __bfloat162float(static_cast<const __nv_bfloat16*>(p.gate)[gi]);
+      } else {
+        m_run[t] = m_blk;
+      }
+      // a row with no logit so far subtracts 0: its exponentials are all 0 (or 2^-126)
+      const float msub = m_run[t] == -INFINITY ? 0.0f : m_run[t];
+      const float scl = exact ? (routed_row ? sl2 : 0.0f) : 1.0f;
+      const float off = (exact && !routed_row) ? -INFINITY : -msub;
+      const uint64_t sc2 = f2_pack(scl, scl);
+      const uint64_t negm = f2_pack(off, off);
+      uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+#pragma unroll
+      for (int q8 = 0; q8 < 4; ++q8) {
+        uint32_t packed[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = q8 * 8 + u;
+          const uint32_t* v = sr[j >> 4];
+          const int e = (2 * j) & 31;
+          const uint64_t xs =
+              f2_fma(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2, negm);
+          uint64_t ev;
+          if ((ATT_EMU_MASK >> (j & 7)) & 1) {
+            ev = exp2_poly_x2(xs);
+          } else {
+            const float2 xv = f2_unpack(xs);
+            ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
+          }
+          lsum2[u & 1] = f2_add(lsum2[u & 1], ev);
+          const float2 e2 = f2_unpack(ev);
+          packed[u] = pack_f16x2(e2.x, e2.y);
         }
-        auto fin = [&](uint32_t raw) -> float {
-          const float o = __uint_as_float(raw) * inv_l;
-          if (p.gate == nullptr) return o;
-          const float r = p.out_f16 ? __half2float(__float2half_rn(o)) : bf16_round(o);
-          return r * gv;
-        };
+        tmem_st8(s_col + q8 * 8, packed);
+      }
+      const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
+      l_run[t] += ls.x + ls.y;
+      if (rescale) {
         const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * (D / 2);
 #pragma unroll 1
         for (int c = 0; c < D / 64; ++c) {
           uint32_t o[32];
           tmem_ld32(o_col + c * 32, o);
           tmem_wait_ld();
-          if (store) {
-            uint8_t* base = static_cast<uint8_t*>(p.out) +
-                            (dst_row * p.ld_out + head * D + half * (D / 2) + c * 32) * 2;
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              uint4 w;
-              if (p.out_f16) {
-                w.x = pack_f16x2(fin(o[g * 8 + 0]), fin(o[g * 8 + 1]));
-                w.y = pack_f16x2(fin(o[g * 8 + 2]), fin(o[g * 8 + 3]));
-                w.z = pack_f16x2(fin(o[g * 8 + 4]), fin(o[g * 8 + 5]));
-                w.w = pack_f16x2(fin(o[g * 8 + 6]), fin(o[g * 8 + 7]));
-              } else {
-                w.x = pack_bf16x2(fin(o[g * 8 + 0]), fin(o[g * 8 + 1]));
-                w.y = pack_bf16x2(fin(o[g * 8 + 2]), fin(o[g * 8 + 3]));
-                w.z = pack_bf16x2(fin(o[g * 8 + 4]), fin(o[g * 8 + 5]));
-                w.w = pack_bf16x2(fin(o[g * 8 + 6]), fin(o[g * 8 + 7]));
-              }
-              *reinterpret_cast<uint4*>(base + g * 16) = w;
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+          tmem_st32(o_col + c * 32, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    };
+    // the exact stages, then the centroid stages, each alternating between the streams
+    for (int i = 0; i < ns && ok; ++i) stage(i, i & 1, i >> 1, std::true_type{});
+    for (int i = ns; i < nst && ok; ++i) stage(i, i & 1, i >> 1, std::false_type{});
+    if (ok && nst > 0) {
+      for (int t = 0; t < 2; ++t) xsum[(t * 2 + half) * 128 + row] = l_run[t];
+      mbar_arrive(&lbar[quarter]);
+      ok = mbar_wait(&lbar[quarter], 0, abort_flag);
+    }
+    if (ok && nst > 0 && mbar_wait(o_done, 0, abort_flag)) {
+      tc_fence_after();
+      const int tok = row0 + row;
+      bool store = tok < p.tokens;
+      // merge the streams: O = (O_A 2^(m_A - m) + O_B 2^(m_B - m)) / (l_A 2^(m_A - m) + ...)
+      const float la = l_run[0] + xsum[(0 * 2 + 1 - half) * 128 + row];
+      const float lb = l_run[1] + xsum[(1 * 2 + 1 - half) * 128 + row];
+      const float m = fmaxf(m_run[0], m_run[1]);
+      const bool has_b = nst > 1;
+      const float sa = m_run[0] == -INFINITY ? 0.0f : ex2_approx(m_run[0] - m);
+      const float sb = (!has_b || m_run[1] == -INFINITY) ? 0.0f : ex2_approx(m_run[1] - m);
+      const float inv_l = 1.0f / (la * sa + lb * sb);
+      const int64_t dst_row = store ? p.order[tok] : 0;
+      if (store && (dst_row < 0 || dst_row >= p.tokens)) {
+        atomicExch(&g_device_error, 1);
+        store = false;
+      }
+      float gv = 1.0f;
+      if (p.gate != nullptr && store) {
+        const int64_t gi = dst_row * p.ld_gate + head;
+        gv = p.out_f16 ? __half2float(static_cast<const __half*>(p.gate)[gi])
+                       : __bfloat162float(static_cast<const __nv_bfloat16*>(p.gate)[gi]);
+      }
+      auto fin = [&](uint32_t ra, uint32_t rb) -> float {
+        const float o = (__uint_as_float(ra) * sa + (has_b ? __uint_as_float(rb) * sb : 0.0f)) * inv_l;
+        if (p.gate == nullptr) return o;
+        const float r = p.out_f16 ? __half2float(__float2half_rn(o)) : bf16_round(o);
+        return r * gv;
+      };
+      const uint32_t oa_col = tmem + lane_base + 256 + half * (D / 2);
+      const uint32_t ob_col = oa_col + 128;
+#pragma unroll 1
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t oa[32], ob[32];
+        tmem_ld32(oa_col + c * 32, oa);
+        tmem_ld32(ob_col + c * 32, ob);
+        tmem_wait_ld();
+        if (store) {
+          uint8_t* base = static_cast<uint8_t*>(p.out) +
+                          (dst_row * p.ld_out + head * D + half * (D / 2) + c * 32) * 2;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 w;
+            if (p.out_f16) {
+              w.x = pack_f16x2(fin(oa[g * 8 + 0], ob[g * 8 + 0]), fin(oa[g * 8 + 1], ob[g * 8 + 1]));
+              w.y = pack_f16x2(fin(oa[g * 8 + 2], ob[g * 8 + 2]), fin(oa[g * 8 + 3], ob[g * 8 + 3]));
+              w.z = pack_f16x2(fin(oa[g * 8 + 4], ob[g * 8 + 4]), fin(oa[g * 8 + 5], ob[g * 8 + 5]));
+              w.w = pack_f16x2(fin(oa[g * 8 + 6], ob[g * 8 + 6]), fin(oa[g * 8 + 7], ob[g * 8 + 7]));
+            } else {
+              w.x = pack_bf16x2(fin(oa[g * 8 + 0], ob[g * 8 + 0]), fin(oa[g * 8 + 1], ob[g * 8 + 1]));
+              w.y = pack_bf16x2(fin(oa[g * 8 + 2], ob[g * 8 + 2]), fin(oa[g * 8 + 3], ob[g * 8 + 3]));
+              w.z = pack_bf16x2(fin(oa[g * 8 + 4], ob[g * 8 + 4]), fin(oa[g * 8 + 5], ob[g * 8 + 5]));
+              w.w = pack_bf16x2(fin(oa[g * 8 + 6], ob[g * 8 + 6]), fin(oa[g * 8 + 7], ob[g * 8 + 7]));
             }
+            *reinterpret_cast<uint4*>(base + g * 16) = w;
           }
         }
       }
