@@ -671,7 +671,7 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
     return out
 
 
-def run_kernel_case(case: str) -> None:
+def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | None = None) -> None:
     """Three launches of one kernel at a workload shape (for ncu captures). `gemm`: the single
     block's fused projection, 4608 x 21504 x 3072, with its in-step epilogue (per-head RMSNorm +
     RoPE on k and q, GELU on the MLP columns); `attention`: the joint attention over 4608 tokens
@@ -717,7 +717,7 @@ def run_kernel_case(case: str) -> None:
         run_kv_step(dev)
         return
     elif case == "sol":
-        run_sol_case(dev)
+        run_sol_case(dev, tau=sol_tau, family=sol_inputs)
         return
     elif case == "sol_step":
         run_sol_step(dev)
@@ -805,11 +805,12 @@ def run_av_step(dev: torch.device) -> None:
                       "kernels": _kernel_shares(step)}))
 
 
-def run_sol_case(dev: torch.device) -> None:
+def run_sol_case(dev: torch.device, tau: float | None = None, family: str | None = None) -> None:
     """Sol-Attn at config 4's video self-attention (9216 tokens on a 16 x 18 x 32 Morton grid,
-    32 heads of 128) against the dense kernel on the same q, k, v, for the published taus. The
-    algorithmic work counts the exact (query, routed key) pairs and the (query, centroid) pairs,
-    4 x 128 FLOP each."""
+    32 heads of 128) against the dense kernel on the same q, k, v, for the published taus (or
+    one `tau` and one input `family`, for a launch list: 3 warm-up calls, then the timed ones).
+    The algorithmic work counts the exact (query, routed key) pairs and the (query, centroid)
+    pairs, 4 x 128 FLOP each."""
     from kinomlx_b200 import ops
     from kinomlx_b200.kernels import sol_attention as sol
     from kinomlx_b200.synthetic import normal
@@ -847,8 +848,9 @@ def run_sol_case(dev: torch.device) -> None:
     dense_ms = _time(lambda: ops.attention([q[None]], [k[None]], [v[None]], [out[None]], heads=heads),
                      3, 10, 1)
     rows = []
-    for (family, (q, k, v)), tau in ((fam_t, tau) for fam_t in inputs.items()
-                                     for tau in (0.5, 1.0, 1.25, 1.5)):
+    taus = (0.5, 1.0, 1.25, 1.5) if tau is None else (tau,)
+    chosen = [(name, t) for name, t in inputs.items() if family is None or name == family]
+    for (family, (q, k, v)), tau in ((fam_t, t) for fam_t in chosen for t in taus):
         ms = _time(lambda: ops.sol_attention(q, k, v, heads=heads, tau=tau, order=order, out=out),
                    3, 10, 1)
         routes = sol.routed_blocks(q, k, v, heads=heads, tau=tau, order=order)
@@ -859,8 +861,9 @@ def run_sol_case(dev: torch.device) -> None:
         exact = float((exact_keys * rows_per_block).sum())
         centroid = float(((nb - routes.sum(-1)).float() * rows_per_block).sum())
         flop = 4.0 * 128 * (exact + centroid)
-        pad = (-nb) % 4
-        union = torch.nn.functional.pad(routes, (0, 0, 0, pad)).reshape(heads, -1, 4, nb).any(2)
+        pad = (-nb) % sol.QUERY_BLOCKS_PER_CTA
+        union = torch.nn.functional.pad(routes, (0, 0, 0, pad)).reshape(
+            heads, -1, sol.QUERY_BLOCKS_PER_CTA, nb).any(2)
         rows.append({"inputs": family, "tau": tau, "ms": round(ms, 3),
                      "speedup_vs_dense": round(dense_ms / ms, 2),
                      "routed_fraction": round(float(routes.float().mean()), 4),
@@ -1065,9 +1068,12 @@ def main() -> None:
     ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow", "sol", "sol_step",
                                               "bandwidth", "f32", "av_step", "kv_step"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
+    ap.add_argument("--sol-tau", type=float, help="--kernel-case sol: this tau only")
+    ap.add_argument("--sol-inputs", choices=["iid", "smooth", "smooth_rope"],
+                    help="--kernel-case sol: this input family only")
     args = ap.parse_args()
     if args.kernel_case:
-        run_kernel_case(args.kernel_case)
+        run_kernel_case(args.kernel_case, args.sol_tau, args.sol_inputs)
         return
     if args.warmup < 3:
         log("warm-up raised to 3 steps (timing rule)")

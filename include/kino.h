@@ -33,7 +33,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (10); bumped on any signature change or addition. */
+/* ABI version of this header (11); bumped on any signature change or addition. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -173,6 +173,15 @@ typedef struct kino_attention_args {
   int64_t out_col_offset;
   int64_t out_cols;
   int64_t gate_head_offset;
+  /* Optional additive key bias (one key segment, no peer return): key_bias[b * ld_key_bias + j]
+   * (fp32, natural-log units) is added to q_i . k_j * scale before the softmax, as the
+   * reference's additive attention masks are (kinomlx/models/ltx2/transformer/attention.py:164-186;
+   * a padded text mask becomes 0 / -3.39e38, kinomlx/models/ltx2/transformer/preprocessing.py:85-96).
+   * Rows 16-byte aligned, ld_key_bias a multiple of 4 covering kv_tokens rounded up to 4 (the
+   * kernel reads whole float4s; entries past kv_tokens are ignored). Biases below -1e30 / log2(e)
+   * are raised to it, so a row whose keys are all masked averages them uniformly. */
+  const float* key_bias;
+  int64_t ld_key_bias;
 } kino_attention_args;
 
 /* softmax(q k^T * scale) v over all key segments, per head, token-major operands.
@@ -630,9 +639,11 @@ kino_status kino_linear_f32(const float* x, const float* w, float* out, int64_t 
                             int64_t n, int64_t k, int64_t ldx, int64_t bsx, int64_t ldw,
                             int64_t ldo, int64_t bso, const kino_epilogue_f32* epi, void* stream);
 
-/* softmax(q k^T * scale) v per (batch, head), head_dim 128, token-major q (q_tokens rows),
- * k and v (kv_tokens rows); out like q and may alias it. With `gate` (batch, q_tokens, heads)
- * at row stride ld_gate and batch stride bs_gate, each head's output is multiplied by its gate.
+/* softmax(q k^T * scale + key_bias) v per (batch, head), head_dim 128, token-major q (q_tokens
+ * rows), k and v (kv_tokens rows); out like q and may alias it. With `gate` (batch, q_tokens,
+ * heads) at row stride ld_gate and batch stride bs_gate, each head's output is multiplied by its
+ * gate. `key_bias` (optional, fp32, row b at b * ld_key_bias) is an additive mask over the keys
+ * (kinomlx/models/ltx2/transformer/attention.py:164-186).
  * Replaces MLX SDPA in fp32 (kinomlx/models/flux2/kv.py:48-54, kinomlx/models/flux2/
  * transformer.py:35-53, kinomlx/models/ltx2/transformer/attention.py:144-161, 364-368). */
 kino_status kino_attention_f32(const float* q, const float* k, const float* v, float* out,
@@ -640,7 +651,7 @@ kino_status kino_attention_f32(const float* q, const float* k, const float* v, f
                                int64_t ld_q, int64_t bs_q, int64_t ld_k, int64_t bs_k,
                                int64_t ld_v, int64_t bs_v, int64_t ld_out, int64_t bs_out,
                                float scale, const float* gate, int64_t ld_gate, int64_t bs_gate,
-                               void* stream);
+                               const float* key_bias, int64_t ld_key_bias, void* stream);
 
 /* kino_adaln in fp32: out = norm(x) * (1 + scale[b]) + shift[b], dim <= 8192
  * (kinomlx/models/flux2/transformer.py:56-60). */

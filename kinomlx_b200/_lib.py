@@ -121,6 +121,8 @@ class AttentionArgs(ctypes.Structure):
         ("out_col_offset", c_int64),
         ("out_cols", c_int64),
         ("gate_head_offset", c_int64),
+        ("key_bias", c_void_p),
+        ("ld_key_bias", c_int64),
     ]
 
 
@@ -303,7 +305,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "kino_attention_f32": (
         c_int,
-        [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, F, P, I64, I64, P],
+        [P, P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, F, P, I64, I64,
+         P, I64, P],
     ),
     "kino_adaln_f32": (c_int, [P, I64, I64, P, P, I64, P, I64, I64, I64, I64, I64, c_int, F, P]),
     "kino_qk_norm_rope_f32": (

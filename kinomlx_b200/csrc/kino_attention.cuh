@@ -65,6 +65,11 @@ struct AttnParams {
   int rows_per_rank;
   int64_t out_col_offset;
   int gate_head_offset;
+  // Optional additive key bias (the BIAS instantiation, one key segment): key_bias[batch *
+  // ld_key_bias + key] is added to q k^T * scale (natural-log units), as an additive attention
+  // mask is (kinomlx/models/ltx2/transformer/attention.py:164-186).
+  const float* key_bias;
+  int64_t ld_key_bias;
 };
 
 struct AttnSmem {
@@ -118,7 +123,7 @@ __device__ __forceinline__ QTile q_tile_of(const AttnParams& p, int global) {
   return t;
 }
 
-template <int D>
+template <int D, bool BIAS = false>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap mq0,
                         const __grid_constant__ CUtensorMap mq1,
@@ -301,6 +306,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const int kseg = (j < p.kv_blocks[0]) ? 0 : 1;
       const int kb = j - (kseg ? p.kv_blocks[0] : 0);
       const int valid = min(ATT_BN, p.kv_tokens[kseg] - kb * ATT_BN) - half * 64;
+      // BIAS: this half block's key biases in log2 units, floored at -1e30 so that a row whose
+      // keys are all masked averages them uniformly, as a finite additive mask does
+      float kbias[BIAS ? 64 : 1];
+      if constexpr (BIAS) {
+        const float4* bp = reinterpret_cast<const float4*>(
+            p.key_bias + static_cast<int64_t>(batch) * p.ld_key_bias + kb * ATT_BN + half * 64);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float4 b4 = c * 4 < valid ? bp[c] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          kbias[c * 4 + 0] = fmaxf(b4.x * 1.4426950408889634f, -1.0e30f);
+          kbias[c * 4 + 1] = fmaxf(b4.y * 1.4426950408889634f, -1.0e30f);
+          kbias[c * 4 + 2] = fmaxf(b4.z * 1.4426950408889634f, -1.0e30f);
+          kbias[c * 4 + 3] = fmaxf(b4.w * 1.4426950408889634f, -1.0e30f);
+        }
+      }
       for (int t = 0; t < ntile; ++t) {
         if (!mbar_wait(&s_full[t], j & 1, abort_flag)) {
           ok = false;
@@ -319,6 +339,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             for (int i = 0; i < 32; ++i)
               if (c * 32 + i >= valid) sr[c][i] = __float_as_uint(-INFINITY);
           }
+        }
+        if constexpr (BIAS) {  // logits in log2 units from here on
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              sr[c][i] = __float_as_uint(fmaf(__uint_as_float(sr[c][i]), sl2, kbias[c * 32 + i]));
         }
         float mq[4];
 #pragma unroll
@@ -343,7 +370,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           ok = false;
           break;
         }
-        const float m_blk = fmaxf(mine, xm[(1 - half) * 128 + row]) * sl2;
+        const float m_blk = fmaxf(mine, xm[(1 - half) * 128 + row]) * (BIAS ? 1.0f : sl2);
         // Lazy rescale, decided identically by both halves of a row. O of this tile holds PV(j-1)
         // (completed before S(j) was signalled).
         float alpha = 1.0f;
@@ -359,7 +386,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         } else {
           m_run[t] = m_blk;
         }
-        const uint64_t sl2x2 = f2_pack(sl2, sl2);
+        const float mult = BIAS ? 1.0f : sl2;
+        const uint64_t sl2x2 = f2_pack(mult, mult);
         const uint64_t negm = f2_pack(-m_run[t], -m_run[t]);
         uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
 #pragma unroll

@@ -529,7 +529,7 @@ SolLayout sol_layout(int64_t tokens, int64_t heads) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 10; }
+int kino_abi_version(void) { return 11; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -808,6 +808,20 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
                static_cast<cudaStream_t>(stream), mq[0], mq[1], mk[0], mk[1], mv[0], mv[1], p);
     return check_launch("kino_attention");
   };
+  if (a->key_bias != nullptr) {
+    if (a->n_kv != 1 || a->out_peers != nullptr)
+      return fail(KINO_EINVAL, "kino_attention: a key bias takes one key segment, no peer return");
+    const int64_t padded = (a->kv_tokens[0] + 3) / 4 * 4;
+    if (!aligned16(a->key_bias) || a->ld_key_bias % 4 ||
+        (a->batch > 1 && a->ld_key_bias < padded))
+      return fail(KINO_EINVAL,
+                  "kino_attention: key bias rows 16-byte aligned, stride a multiple of 4 floats "
+                  "covering the keys rounded up to 4");
+    p.key_bias = a->key_bias;
+    p.ld_key_bias = a->ld_key_bias;
+    return a->head_dim == 64 ? run(kino::attention_tc_kernel<64, true>, 14)
+                             : run(kino::attention_tc_kernel<128, true>, 15);
+  }
   return a->head_dim == 64 ? run(kino::attention_tc_kernel<64>, 11)
                            : run(kino::attention_tc_kernel<128>, 3);
 }
@@ -1602,9 +1616,11 @@ kino_status kino_attention_f32(const float* q, const float* k, const float* v, f
                                int64_t ld_q, int64_t bs_q, int64_t ld_k, int64_t bs_k,
                                int64_t ld_v, int64_t bs_v, int64_t ld_out, int64_t bs_out,
                                float scale, const float* gate, int64_t ld_gate, int64_t bs_gate,
-                               void* stream) {
+                               const float* key_bias, int64_t ld_key_bias, void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr)
     return fail(KINO_EINVAL, "kino_attention_f32: null operand");
+  if (key_bias != nullptr && batch > 1 && ld_key_bias < kv_tokens)
+    return fail(KINO_EINVAL, "kino_attention_f32: key bias rows shorter than the keys");
   if (gate != nullptr && ld_gate < heads)
     return fail(KINO_EINVAL, "kino_attention_f32: gate rows shorter than heads");
   if (batch < 1 || heads < 1 || q_tokens < 1 || kv_tokens < 1)
@@ -1625,7 +1641,7 @@ kino_status kino_attention_f32(const float* q, const float* k, const float* v, f
   launch_pdl(kino::attention_f32_kernel, grid, dim3(kino::FA32_THREADS), smem,
              static_cast<cudaStream_t>(stream), q, k, v, out, static_cast<int>(q_tokens),
              static_cast<int>(kv_tokens), ld_q, bs_q, ld_k, bs_k, ld_v, bs_v, ld_out, bs_out,
-             scale, gate, ld_gate, bs_gate);
+             scale, gate, ld_gate, bs_gate, key_bias, ld_key_bias);
   return check_launch("kino_attention_f32");
 }
 

@@ -193,7 +193,8 @@ __global__ void __launch_bounds__(FA32_THREADS, 1)
                          const float* __restrict__ vv, float* out, int tq, int tk, int64_t ld_q,
                          int64_t bs_q, int64_t ld_k, int64_t bs_k, int64_t ld_v, int64_t bs_v,
                          int64_t ld_o, int64_t bs_o, float scale, const float* __restrict__ gate,
-                         int64_t ld_g, int64_t bs_g) {
+                         int64_t ld_g, int64_t bs_g, const float* __restrict__ key_bias,
+                         int64_t ld_bias) {
   extern __shared__ __align__(16) unsigned char fa32_raw[];
   Fa32Smem& s = *reinterpret_cast<Fa32Smem*>(fa32_raw);
   griddep_wait();
@@ -282,10 +283,15 @@ __global__ void __launch_bounds__(FA32_THREADS, 1)
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const bool valid = k0 + tx * 4 + j < tk;
+      const int key = k0 + tx * 4 + j;
+      const bool valid = key < tk;
+      // an additive key bias (a text mask) joins the scaled score, as the reference adds it
+      const float bias = (valid && key_bias != nullptr)
+                             ? key_bias[static_cast<int64_t>(b) * ld_bias + key] : 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i)
-        s.pt[tx * 4 + j][ty * 4 + i] = valid ? __fmul_rn(sacc[i][j], scale) : -CUDART_INF_F;
+        s.pt[tx * 4 + j][ty * 4 + i] =
+            valid ? __fadd_rn(__fmul_rn(sacc[i][j], scale), bias) : -CUDART_INF_F;
     }
     __syncthreads();
 

@@ -132,18 +132,19 @@ __global__ void __launch_bounds__(128)
   vmean[m] = __float2half_rn(sol_sat(sol_round_in<In>(sum[2])));
 }
 
-// grid (ceil(blocks / 32), heads), 256 threads: the routing rows of 32 query blocks, four per
-// warp (kinomlx/models/ltx2/kernels/sol_attention.py:181-216). The head's key means are staged in
-// shared memory once (16-byte loads, all in flight), their center and per-dimension variance
-// reduced in a fixed order; each row's limit is its mean score plus tau standard deviations
-// under a diagonal key covariance. Scores: for 32 key blocks at a time every lane keeps the
-// partial products of its 4 dimensions with each of the 32 keys, and a butterfly
-// (reduce-scatter over the lanes, 31 shuffles) leaves lane l with the full score of key block
-// base + l; a ballot turns the 32 comparisons into one mask word.
-constexpr int SOL_ROUTE_ROWS = 32;
+// grid (ceil(blocks / 16), heads), 256 threads: the routing rows of 16 query blocks
+// (kinomlx/models/ltx2/kernels/sol_attention.py:181-216). The head's key means are staged in
+// shared memory once (rows padded to 272 bytes, so a warp's 16-byte loads of 32 different rows
+// meet no bank conflict), their center and per-dimension variance reduced in a fixed order, and
+// each row's limit is its mean score plus tau standard deviations under a diagonal key
+// covariance. Scores: a warp owns eight query rows and a 32-block word of keys, lane l key block
+// 32 w + l; the eight query rows are read as broadcasts, so every lane runs 8 x 128 FMAs with no
+// shuffles and a ballot per row turns the comparisons into the mask word.
+constexpr int SOL_ROUTE_ROWS = 16;
+constexpr int SOL_KEY_PAD = 136;  // halves per staged key-mean row
 
 __host__ __device__ constexpr int sol_route_smem(int nb) {
-  return nb * 128 * 2 + (16 * 128 + 128 + 128 + SOL_ROUTE_ROWS * 128) * 4;
+  return nb * SOL_KEY_PAD * 2 + (16 * 128 + 128 + 128 + SOL_ROUTE_ROWS * 128 + SOL_ROUTE_ROWS) * 4;
 }
 
 __global__ void __launch_bounds__(256)
@@ -154,19 +155,23 @@ __global__ void __launch_bounds__(256)
   griddep_launch();
   extern __shared__ __align__(16) uint8_t rsm[];
   __half* ks = reinterpret_cast<__half*>(rsm);
-  float* part = reinterpret_cast<float*>(rsm + nb * 256);
+  float* part = reinterpret_cast<float*>(rsm + nb * SOL_KEY_PAD * 2);
   float* center = part + 16 * 128;
   float* var = center + 128;
-  float* qs = var + 128;  // [SOL_ROUTE_ROWS][128]
+  float* qs = var + 128;                      // [SOL_ROUTE_ROWS][128]
+  float* limit = qs + SOL_ROUTE_ROWS * 128;  // [SOL_ROUTE_ROWS]
   const int h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const __half* kh = kmean + static_cast<int64_t>(h) * nb * 128;
+  const uint4* kh = reinterpret_cast<const uint4*>(kmean + static_cast<int64_t>(h) * nb * 128);
   for (int i = tid; i < nb * 16; i += 256)
-    reinterpret_cast<uint4*>(ks)[i] = reinterpret_cast<const uint4*>(kh)[i];
+    *reinterpret_cast<uint4*>(ks + (i >> 4) * SOL_KEY_PAD + (i & 15) * 8) = kh[i];
   const int a0 = blockIdx.x * SOL_ROUTE_ROWS;
-  for (int i = tid; i < SOL_ROUTE_ROWS * 128; i += 256) {
-    const int r = i >> 7, a = a0 + r;
-    qs[i] = a < nb ? qmean[(static_cast<int64_t>(h) * nb + a) * 128 + (i & 127)] : 0.0f;
+  for (int i = tid; i < SOL_ROUTE_ROWS * 32; i += 256) {
+    const int r = i >> 5, a = a0 + r;
+    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    reinterpret_cast<float4*>(qs)[i] =
+        a < nb ? reinterpret_cast<const float4*>(qmean + (static_cast<int64_t>(h) * nb + a) * 128)[i & 31]
+               : z;
   }
   __syncthreads();
   const int rg = tid >> 4, cv = tid & 15;
@@ -175,7 +180,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
     for (int b = rg; b < nb; b += 16) {
-      const uint4 raw = reinterpret_cast<const uint4*>(ks + b * 128)[cv];
+      const uint4 raw = *reinterpret_cast<const uint4*>(ks + b * SOL_KEY_PAD + cv * 8);
       const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -200,10 +205,7 @@ __global__ void __launch_bounds__(256)
     }
     __syncthreads();
   }
-  for (int rr = 0; rr < SOL_ROUTE_ROWS / 8; ++rr) {
-    const int r = warp * (SOL_ROUTE_ROWS / 8) + rr;
-    const int a = a0 + r;
-    if (a >= nb) break;  // warp-uniform
+  for (int r = warp; r < SOL_ROUTE_ROWS; r += 8) {
     const float* q = qs + r * 128;
     float rm = 0.0f, rv = 0.0f;
 #pragma unroll
@@ -215,37 +217,48 @@ __global__ void __launch_bounds__(256)
     const float raw_mean = warp_sum_f(rm);
     const float raw_var = warp_sum_f(rv);
     const float variance = fmaxf(raw_var, 0.0f) * log2_scale_sq;
-    const float limit = raw_mean * log2_scale + tau * sqrtf(variance + 1.0e-6f);
-    const float q0 = q[lane * 4], q1 = q[lane * 4 + 1], q2 = q[lane * 4 + 2], q3 = q[lane * 4 + 3];
-    uint32_t* row = bits + (static_cast<int64_t>(h) * nb + a) * words;
-    for (int w = 0; w < words; ++w) {
-      float v[32];
+    if (lane == 0) limit[r] = raw_mean * log2_scale + tau * sqrtf(variance + 1.0e-6f);
+  }
+  __syncthreads();
+  const int r0 = (warp & 1) * 8;
+  for (int w = warp >> 1; w < words; w += 4) {
+    const int b = w * 32 + lane;
+    const __half* kr = ks + min(b, nb - 1) * SOL_KEY_PAD;
+    float acc[8];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int b = w * 32 + i;
-        float dot = 0.0f;
-        if (b < nb) {  // uniform across the warp
-          const uint2 raw = reinterpret_cast<const uint2*>(ks + b * 128)[lane];
-          const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-          const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-          dot = fmaf(q0, k01.x, fmaf(q1, k01.y, fmaf(q2, k23.x, q3 * k23.y)));
-        }
-        v[i] = dot;
+    for (int r = 0; r < 8; ++r) acc[r] = 0.0f;
+#pragma unroll 2
+    for (int c = 0; c < 16; ++c) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(kr + c * 8);
+      const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+      float kf[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&wv[e]));
+        kf[2 * e] = f.x;
+        kf[2 * e + 1] = f.y;
       }
 #pragma unroll
-      for (int sh = 16; sh >= 1; sh >>= 1) {
-        const bool upper = (lane & sh) != 0;
-#pragma unroll
-        for (int i = 0; i < sh; ++i) {
-          const float send = upper ? v[i] : v[i + sh];
-          const float keep = upper ? v[i + sh] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, sh);
-        }
+      for (int r = 0; r < 8; ++r) {
+        const float4 qa = reinterpret_cast<const float4*>(qs + (r0 + r) * 128 + c * 8)[0];
+        const float4 qb = reinterpret_cast<const float4*>(qs + (r0 + r) * 128 + c * 8)[1];
+        acc[r] = fmaf(qa.x, kf[0], acc[r]);
+        acc[r] = fmaf(qa.y, kf[1], acc[r]);
+        acc[r] = fmaf(qa.z, kf[2], acc[r]);
+        acc[r] = fmaf(qa.w, kf[3], acc[r]);
+        acc[r] = fmaf(qb.x, kf[4], acc[r]);
+        acc[r] = fmaf(qb.y, kf[5], acc[r]);
+        acc[r] = fmaf(qb.z, kf[6], acc[r]);
+        acc[r] = fmaf(qb.w, kf[7], acc[r]);
       }
-      const int b = w * 32 + lane;
-      const bool routed = b < nb && ((b >= a - 1 && b <= a + 1) || v[0] * log2_scale > limit);
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int a = a0 + r0 + r;
+      const bool routed =
+          b < nb && ((b >= a - 1 && b <= a + 1) || acc[r] * log2_scale > limit[r0 + r]);
       const uint32_t word = __ballot_sync(0xffffffffu, routed);
-      if (lane == 0) row[w] = word;
+      if (lane == 0 && a < nb) bits[(static_cast<int64_t>(h) * nb + a) * words + w] = word;
     }
   }
 }

@@ -19,6 +19,7 @@ HEAD_DIM = 128
 _WORD_BITS = 32
 _SUPPORTED_DTYPES = (torch.float16, torch.bfloat16)
 MAX_BLOCKS = 512  # the device kernel keeps each query block's routing row in 16 mask words
+QUERY_BLOCKS_PER_CTA = 2  # the attention kernel's 128-row query tile covers two blocks
 
 
 def block_count(tokens: int) -> int:

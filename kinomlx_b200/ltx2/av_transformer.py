@@ -19,7 +19,7 @@ import torch
 
 from .. import ops
 from .config import LTXVariant
-from .transformer import precompute_freqs_cis
+from .transformer import context_key_bias, precompute_freqs_cis
 
 BF = torch.bfloat16
 
@@ -45,6 +45,8 @@ class PreparedAV:
     audio_pe: Tables  # audio self-attention (B|1, heads, Ta, 32)
     video_cross_pe: Tables  # A/V attention, video side (B|1, heads, Tv, 32)
     audio_cross_pe: Tables  # A/V attention, audio side (B|1, heads, Ta, 32)
+    video_key_bias: torch.Tensor | None = None  # text-mask biases of the two text contexts
+    audio_key_bias: torch.Tensor | None = None
 
 
 class _Stream:
@@ -189,10 +191,13 @@ class LTXAVTransformer:
 
     # ------------------------------------------------------------------ preparation
     def prepare(self, video_context: torch.Tensor, audio_context: torch.Tensor,
-                video_positions: torch.Tensor, audio_positions: torch.Tensor) -> PreparedAV:
+                video_positions: torch.Tensor, audio_positions: torch.Tensor,
+                video_context_mask: torch.Tensor | None = None,
+                audio_context_mask: torch.Tensor | None = None) -> PreparedAV:
         """RoPE tables of both streams and of the A/V attention (preprocessing.py:108-121,
         170-200: the cross tables take the time axis only, on the audio width, with the larger
-        of the two temporal max_pos)."""
+        of the two temporal max_pos), and the key biases of optional padded text masks
+        (preprocessing.py:85-96)."""
         v, a = self.video, self.audio
         vpos, apos = video_positions.cpu(), audio_positions.cpu()
         cross_max = (max(v.max_pos[0], a.max_pos[0]),)
@@ -203,6 +208,10 @@ class LTXAVTransformer:
             tab(vpos, v), tab(apos, a),
             tab(vpos[:, 0:1], replace(v, dim=a.dim, max_pos=cross_max)),
             tab(apos[:, 0:1], replace(a, max_pos=cross_max)),
+            context_key_bias(video_context_mask, video_context.shape[0], video_context.shape[1],
+                             self.device),
+            context_key_bias(audio_context_mask, audio_context.shape[0], audio_context.shape[1],
+                             self.device),
         )
 
     def _workspace(self, batch, tv, ta, cv, ca):
@@ -245,7 +254,8 @@ class LTXAVTransformer:
                 ops.add_rows(t_g, ws.cg[b], out=ws.gv[b])
 
     # ------------------------------------------------------------------ blocks
-    def _self_and_text(self, st: _Stream, ws: _StreamWS, i: int, ctx: torch.Tensor, pe: Tables):
+    def _self_and_text(self, st: _Stream, ws: _StreamWS, i: int, ctx: torch.Tensor, pe: Tables,
+                       key_bias: torch.Tensor | None = None):
         """transformer.py:249-320 for one stream."""
         v, p = st.v, st.blocks[i]
         d, h = v.dim, v.heads
@@ -271,7 +281,7 @@ class LTXAVTransformer:
         for t, wn in ((q, p["qn2"]), (k2, p["kn2"])):
             ops.qk_norm_rope(t, heads=st.qk_heads, weight=wn, norm=ops.QKNORM_FULL_ROW,
                              rope=ops.ROPE_NONE, eps=v.eps)
-        ops.attention([q], [k2], [v2], [q], heads=h, gate=[ws.gates])
+        ops.attention([q], [k2], [v2], [q], heads=h, gate=[ws.gates], key_bias=key_bias)
         ops.linear(q, p["o2_w"], x, bias=p["o2_b"], kind=ops.EPI_GATED_RESIDUAL, residual=x,
                    gate=val(8))
 
@@ -307,8 +317,8 @@ class LTXAVTransformer:
 
     def _block(self, i: int, wv: _StreamWS, wa: _StreamWS, wav: _AVWS, prep: PreparedAV) -> None:
         """BasicAVTransformerBlock (transformer.py:225-413)."""
-        self._self_and_text(self.vs, wv, i, prep.video_context, prep.video_pe)
-        self._self_and_text(self.as_, wa, i, prep.audio_context, prep.audio_pe)
+        self._self_and_text(self.vs, wv, i, prep.video_context, prep.video_pe, prep.video_key_bias)
+        self._self_and_text(self.as_, wa, i, prep.audio_context, prep.audio_pe, prep.audio_key_bias)
         dv, da = self.video.dim, self.audio.dim
         # rows: scale_a2v, shift_a2v, scale_v2a, shift_v2a (transformer.py:188-199, 322-371)
         vr = lambda j: wv.ssv[:, i, j * dv : (j + 1) * dv]
@@ -360,9 +370,13 @@ class LTXAVTransformer:
 
 
 def denoise_av(model: LTXAVTransformer, video_latent, audio_latent, video_context,
-                 audio_context, video_positions, audio_positions, sigmas):
-    """The deterministic-Euler loop over both modalities (kinomlx/models/ltx2/denoise.py:261-365)."""
-    prep = model.prepare(video_context, audio_context, video_positions, audio_positions)
+                 audio_context, video_positions, audio_positions, sigmas, *,
+                 video_context_mask=None, audio_context_mask=None):
+    """The deterministic-Euler loop over both modalities (kinomlx/models/ltx2/denoise.py:261-365),
+    with optional padded text masks per stream."""
+    prep = model.prepare(video_context, audio_context, video_positions, audio_positions,
+                         video_context_mask=video_context_mask,
+                         audio_context_mask=audio_context_mask)
     vx = video_latent.to(model.device, BF).clone()
     ax = audio_latent.to(model.device, BF).clone()
     values = tuple(float(torch.tensor(s, dtype=torch.float32)) for s in sigmas)

@@ -11,11 +11,11 @@ Two layers:
 Each step is one X0 transformer evaluation with the Euler update fused into the final
 projection's epilogue (x0 = x - sigma v, then x0 + (sigma'/sigma)(x - x0), both in fp32).
 
-Supported here: uniform denoise masks (every token at the step's sigma), dense or Sol-Attn
-sparse video self-attention (per step, video-only transformer on one GPU), no context masks or
-keyframes, the deterministic-Euler step. The reference's other options (per-token masks from
-image/keyframe conditioning, padded text masks, the RF-ancestral step) are refused with a
-ValueError naming the option, never silently ignored.
+Supported here: uniform denoise masks (every token at the step's sigma), padded text masks on
+the bf16 transformers (an additive key bias in the cross-attention), dense or Sol-Attn sparse
+video self-attention (per step, video-only transformer on one GPU), the deterministic-Euler step.
+The reference's other options (per-token masks from image/keyframe conditioning, keyframe masks,
+the RF-ancestral step) are refused with a ValueError naming the option, never silently ignored.
 """
 
 from __future__ import annotations
@@ -65,8 +65,9 @@ def denoise_video_step(model: LTXVideoTransformer, prepared: PreparedContext, la
 
 def denoise_video(model: LTXVideoTransformer, latent: torch.Tensor, context: torch.Tensor,
                   positions: torch.Tensor, sigmas=DISTILLED_STAGE_1_SIGMAS,
-                  check_finite: bool = True) -> torch.Tensor:
-    prepared = model.prepare(context, positions)
+                  check_finite: bool = True, context_mask=None) -> torch.Tensor:
+    prepared = (model.prepare(context, positions) if context_mask is None
+                else model.prepare(context, positions, context_mask=context_mask))
     t0, t1 = model.sp.shard(latent.shape[1])
     x = latent[:, t0:t1].to(model.device, getattr(model, "dtype", torch.bfloat16)).clone()
     values = fp32(sigmas)
@@ -105,8 +106,8 @@ def _refuse_unsupported(video_state: LatentState, audio_state: LatentState | Non
     for state, name in ((video_state, "video"), (audio_state, "audio")):
         if state is not None and not state.uniform_mask:
             raise ValueError(f"the device loop takes uniform {name} denoise masks only")
-    if video_context_mask is not None or audio_context_mask is not None:
-        raise ValueError("padded text masks are not supported by the device loop")
+    if audio_context_mask is not None and audio_state is None:
+        raise ValueError("an audio text mask needs an audio latent state")
     if video_keyframes_mask is not None:
         raise ValueError("keyframe masks are not supported by the device loop")
     if video_sparse_attention is not None and audio_state is not None:
@@ -127,7 +128,8 @@ class _Prepared:
     """The once-per-loop preparation: context and RoPE tables for the transformer in use."""
 
     def __init__(self, transformer, video_state: LatentState, audio_state: LatentState | None,
-                 video_context: torch.Tensor, audio_context: torch.Tensor | None):
+                 video_context: torch.Tensor, audio_context: torch.Tensor | None,
+                 video_context_mask=None, audio_context_mask=None):
         self.av = audio_state is not None
         if self.av:
             if audio_context is None:
@@ -135,7 +137,12 @@ class _Prepared:
             if not hasattr(transformer, "as_"):
                 raise ValueError("an audio latent state needs the joint audio/video transformer")
             self.prep = transformer.prepare(video_context, audio_context, video_state.positions,
-                                            audio_state.positions)
+                                            audio_state.positions,
+                                            video_context_mask=video_context_mask,
+                                            audio_context_mask=audio_context_mask)
+        elif video_context_mask is not None:
+            self.prep = transformer.prepare(video_context, video_state.positions,
+                                            context_mask=video_context_mask)
         else:
             self.prep = transformer.prepare(video_context, video_state.positions)
 
@@ -197,7 +204,8 @@ def denoise_step(
                         video_enabled=video_enabled, audio_enabled=audio_enabled)
     if not math.isfinite(sigma) or sigma <= 0.0:
         raise ValueError(f"current sigma must be positive and finite, got {sigma!r}")
-    prepared = _Prepared(transformer, video_state, audio_state, video_context, audio_context)
+    prepared = _Prepared(transformer, video_state, audio_state, video_context, audio_context,
+                         video_context_mask, audio_context_mask)
     return _step(transformer, prepared, video_state, audio_state, fp32([sigma])[0],
                  fp32([sigma_next])[0], video_sparse_attention)
 
@@ -249,7 +257,8 @@ def denoise_loop(
                         video_sparse_attention=next((x for x in sparse_steps if x is not None), None),
                         video_enabled=True, audio_enabled=True)
     sink = reporter if reporter is not None else _NullReporter()
-    prepared = _Prepared(transformer, video_state, audio_state, video_context, audio_context)
+    prepared = _Prepared(transformer, video_state, audio_state, video_context, audio_context,
+                         video_context_mask, audio_context_mask)
     schedule = fp32(values)
     sink.phase_start(phase, total=total, unit="step")
     try:

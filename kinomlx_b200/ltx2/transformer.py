@@ -56,6 +56,45 @@ class PreparedContext:
     context: torch.Tensor  # (B, Tc, D) text after the connector
     cos: torch.Tensor  # (1|B, heads, T, 64) fp32
     sin: torch.Tensor
+    key_bias: torch.Tensor | None = None  # (B, Tc rounded up to 4) fp32 text-mask bias
+
+
+# the most negative finite bf16: a padded text token's additive bias
+# (kinomlx/models/ltx2/transformer/preprocessing.py:14-17)
+_BF16_MINIMUM = -3.3895313892515355e38
+
+
+def context_key_bias(mask, batch: int, tokens: int, device,
+                     dtype: torch.dtype = torch.bfloat16) -> torch.Tensor | None:
+    """The additive bias a text context mask puts on the cross-attention's keys
+    (kinomlx/models/ltx2/transformer/preprocessing.py:85-96): a floating-point mask is the bias
+    itself, in the model's compute dtype; a boolean or integer mask of 1 (token) / 0 (padding)
+    becomes (mask - 1) * 3.3895313892515355e38, i.e. 0 or -3.39e38 (bf16 and fp32 models alike).
+    Returned as fp32 (batch, tokens rounded up to 4), the attention kernels' key-bias operand.
+    Masks broadcast over the queries only: (B, Tc) or (B, 1, Tc); a per-query (B, Tq, Tc) mask
+    is refused."""
+    if mask is None:
+        return None
+    m = torch.as_tensor(mask)
+    if m.dim() == 3 and m.shape[1] == 1:
+        m = m[:, 0]
+    if m.dim() == 1:
+        m = m[None]
+    if m.dim() != 2:
+        raise ValueError("text context masks must be (batch, text tokens); per-query masks are "
+                         "not supported by the device attention")
+    if m.shape[-1] != tokens or m.shape[0] not in (1, batch):
+        raise ValueError(f"text context mask of shape {tuple(m.shape)} does not match "
+                         f"{batch} x {tokens} text tokens")
+    if m.dtype in (torch.float16, torch.bfloat16, torch.float32):
+        bias = m.to(dtype).float()
+    else:
+        if not bool(((m == 0) | (m == 1)).all()):
+            raise ValueError("boolean or integer text masks hold 1 (token) and 0 (padding)")
+        bias = torch.where(m.bool(), 0.0, _BF16_MINIMUM).float()
+    out = torch.zeros((batch, (tokens + 3) // 4 * 4), dtype=torch.float32)
+    out[:, :tokens] = bias.expand(batch, tokens)
+    return out.to(device)
 
 
 class _Workspace:
@@ -223,13 +262,17 @@ class LTXVideoTransformer:
         reference's quantised linears do (weights/quantization.py:32-43)."""
         return ops.linear(x, self._wt(p, name), out, bias_after_round=self.quantize != "off", **kw)
 
-    def prepare(self, context: torch.Tensor, positions: torch.Tensor) -> PreparedContext:
+    def prepare(self, context: torch.Tensor, positions: torch.Tensor,
+                context_mask: torch.Tensor | None = None) -> PreparedContext:
+        """The context on the device, the RoPE tables of the video tokens (this rank's shard) and
+        the key bias of an optional text mask (padded prompts)."""
         cos, sin = precompute_freqs_cis(positions.cpu(), self.v)
         if self.sp.size > 1:
             t0, t1 = self.sp.shard(cos.shape[2])
             cos, sin = cos[:, :, t0:t1].contiguous(), sin[:, :, t0:t1].contiguous()
+        bias = context_key_bias(context_mask, context.shape[0], context.shape[1], self.device)
         return PreparedContext(context.to(self.device, BF).contiguous(),
-                               cos.to(self.device), sin.to(self.device))
+                               cos.to(self.device), sin.to(self.device), bias)
 
     def workspace(self, batch: int, tokens: int, ctx_tokens: int) -> _Workspace:
         key = (batch, tokens, ctx_tokens)
@@ -305,7 +348,7 @@ class LTXVideoTransformer:
                          eps=v.eps)
         ops.qk_norm_rope(k2, heads=h, weight=p["kn2"], norm=ops.QKNORM_FULL_ROW, rope=ops.ROPE_NONE,
                          eps=v.eps)
-        ops.attention([q], [k2], [v2], [q], heads=h, gate=[ws.gates])
+        ops.attention([q], [k2], [v2], [q], heads=h, gate=[ws.gates], key_bias=prepared.key_bias)
         self._lin(q, p, "o2_w", x, bias=p["o2_b"], kind=ops.EPI_GATED_RESIDUAL,
                    residual=x, gate=val(8))
         # feed-forward

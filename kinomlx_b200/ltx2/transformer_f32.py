@@ -22,7 +22,7 @@ from .._lib import (EPI_EULER_X0, EPI_GATED_RESIDUAL, EPI_GELU, EPI_SIGMOID2, NO
                     NORM_NONE, NORM_RMS, QKNORM_FULL_ROW, ROPE_NONE, ROPE_SPLIT)
 from ..sequence_parallel import SequenceParallel
 from .config import LTXVariant
-from .transformer import PreparedContext, precompute_freqs_cis
+from .transformer import PreparedContext, context_key_bias, precompute_freqs_cis
 
 F32 = torch.float32
 
@@ -121,10 +121,13 @@ class LTXVideoTransformerF32:
         self.proj_w, self.proj_b = dev(w["proj_out.weight"]), dev(w["proj_out.bias"])
         self._ws: dict[tuple[int, int, int], _Workspace] = {}
 
-    def prepare(self, context: torch.Tensor, positions: torch.Tensor) -> PreparedContext:
+    def prepare(self, context: torch.Tensor, positions: torch.Tensor,
+                context_mask: torch.Tensor | None = None) -> PreparedContext:
         cos, sin = precompute_freqs_cis(positions.cpu(), self.v)
+        bias = context_key_bias(context_mask, context.shape[0], context.shape[1], self.device,
+                                dtype=F32)
         return PreparedContext(context.to(self.device, F32).contiguous(), cos.to(self.device),
-                               sin.to(self.device))
+                               sin.to(self.device), bias)
 
     def workspace(self, batch: int, tokens: int, ctx_tokens: int) -> _Workspace:
         key = (batch, tokens, ctx_tokens)
@@ -175,7 +178,7 @@ class LTXVideoTransformerF32:
         k2, v2 = ws.ctxkv[..., :d], ws.ctxkv[..., d:]
         f.qk_norm_rope(q, heads=h, weight=p["qn2"], norm=QKNORM_FULL_ROW, rope=ROPE_NONE, eps=v.eps)
         f.qk_norm_rope(k2, heads=h, weight=p["kn2"], norm=QKNORM_FULL_ROW, rope=ROPE_NONE, eps=v.eps)
-        f.attention(q, k2, v2, q, heads=h, gate=ws.gates)
+        f.attention(q, k2, v2, q, heads=h, gate=ws.gates, key_bias=prepared.key_bias)
         f.linear(q, p["o2_w"], x, bias=p["o2_b"], kind=EPI_GATED_RESIDUAL, residual=x, gate=val(8))
         # feed-forward
         f.adaln(x, val(3), val(4), nrm, norm=NORM_RMS, eps=v.eps)

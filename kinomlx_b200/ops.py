@@ -396,10 +396,13 @@ def attention(
     scale: float | None = None,
     gate: list[torch.Tensor | None] | None = None,
     peer_return: PeerReturn | None = None,
+    key_bias: torch.Tensor | None = None,
 ) -> list[torch.Tensor]:
     """Attention over logically concatenated segments; each tensor (batch, tokens, heads*128).
     `gate[s]` (batch, tokens, heads), if given, multiplies segment s's output per head. With
-    `peer_return`, output rows go to their owner GPUs instead of `out`."""
+    `peer_return`, output rows go to their owner GPUs instead of `out`. `key_bias` (fp32,
+    (batch, >= keys rounded up to 4), unit column stride; one key segment) is added to the
+    scaled scores of every query row: an additive attention mask over the keys."""
     if not 1 <= len(q) <= 2 or len(out) != len(q) or not 1 <= len(k) <= 2 or len(v) != len(k):
         raise ValueError("attention takes 1 or 2 query and key/value segments")
     args = _lib.AttentionArgs()
@@ -443,6 +446,17 @@ def attention(
         args.bs_k[s] = k3.stride(0)
         args.ld_v[s] = v3.stride(1)
         args.bs_v[s] = v3.stride(0)
+    if key_bias is not None:
+        tk = int(args.kv_tokens[0])
+        if len(k) != 1 or peer_return is not None:
+            raise ValueError("a key bias takes one key segment and no peer return")
+        if (key_bias.dtype != torch.float32 or key_bias.dim() != 2 or key_bias.device != q0.device
+                or key_bias.shape[0] != args.batch or key_bias.shape[1] < (tk + 3) // 4 * 4
+                or key_bias.stride(1) != 1):
+            raise ValueError("key_bias must be fp32 (batch, keys rounded up to 4) with unit "
+                             "column stride, on the queries' device")
+        args.key_bias = key_bias.data_ptr()
+        args.ld_key_bias = key_bias.stride(0)
     if peer_return is not None:
         r = peer_return
         args.out_peers = r.out_ptrs.data_ptr()

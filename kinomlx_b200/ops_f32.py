@@ -113,9 +113,11 @@ def linear(
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor | None = None,
               *, heads: int, scale: float | None = None,
-              gate: torch.Tensor | None = None) -> torch.Tensor:
+              gate: torch.Tensor | None = None,
+              key_bias: torch.Tensor | None = None) -> torch.Tensor:
     """softmax(q k^T * scale) v with q, k, v (batch, tokens, heads * 128) token-major fp32;
-    `out` may be `q` itself; `gate` (batch, q tokens, heads) multiplies each head's output."""
+    `out` may be `q` itself; `gate` (batch, q tokens, heads) multiplies each head's output;
+    `key_bias` (batch, >= k tokens) fp32 is added to every row's scaled scores."""
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
         _need(t, name, F32)
     q3, k3, v3 = _as3d(q), _as3d(k), _as3d(v)
@@ -137,11 +139,20 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tens
         if tuple(g3.shape) != (batch, tq, heads):
             raise ValueError("attention gate must be (batch, tokens, heads)")
         ld_g, bs_g = g3.stride(1), g3.stride(0)
+    ld_b = 0
+    if key_bias is not None:
+        if (key_bias.dtype != F32 or key_bias.dim() != 2 or key_bias.shape[0] != batch
+                or key_bias.shape[1] < tk or key_bias.stride(1) != 1
+                or key_bias.device != q.device):
+            raise ValueError("key_bias must be fp32 (batch, >= k tokens) with unit column "
+                             "stride, on the queries' device")
+        ld_b = key_bias.stride(0)
     flops = 4.0 * batch * heads * tq * tk * 128
     with _timed("attention_f32", flops, 4.0 * batch * width * (2 * tq + 2 * tk)):
         _lib.call("kino_attention_f32", _ptr(q3), _ptr(k3), _ptr(v3), _ptr(o3), batch, heads, tq,
                   tk, q3.stride(1), q3.stride(0), k3.stride(1), k3.stride(0), v3.stride(1),
-                  v3.stride(0), o3.stride(1), o3.stride(0), sc, _ptr(g3), ld_g, bs_g, _stream())
+                  v3.stride(0), o3.stride(1), o3.stride(0), sc, _ptr(g3), ld_g, bs_g,
+                  _ptr(key_bias), ld_b, _stream())
     return out
 
 

@@ -96,8 +96,13 @@ def linear_then_bias(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = 
     return y
 
 
-def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> torch.Tensor:
+def sdpa(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+         mask: torch.Tensor | None = None) -> torch.Tensor:
     """Scaled dot-product attention on (B, H, T, D) in fp32, one rounding
-    (mx.fast.scaled_dot_product_attention at kinomlx/models/flux2/kv.py:48-54)."""
+    (mx.fast.scaled_dot_product_attention at kinomlx/models/flux2/kv.py:48-54); an additive
+    `mask` broadcastable to (B, H, Tq, Tk) is added to the scaled scores
+    (kinomlx/models/ltx2/transformer/attention.py:164-186)."""
     s = (q.float() @ k.float().transpose(-1, -2)) * scale
+    if mask is not None:
+        s = s + mask.float()
     return (torch.softmax(s, dim=-1) @ v.float()).to(q.dtype)

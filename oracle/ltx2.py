@@ -151,10 +151,29 @@ def adaln(value, scale, shift, eps):
 
 
 # ----------------------------------------------------------------------------- attention / FF
+def context_mask_bias(mask, dtype=torch.bfloat16):
+    """ModalityPreprocessor._context_mask (kinomlx/models/ltx2/transformer/preprocessing.py:85-96):
+    a floating-point text mask is an additive bias, cast to the compute dtype and shaped
+    (B, 1, 1|Tq, Tk); any other mask becomes (mask - 1) * -min(dtype), with min -65504 for fp16
+    and -3.3895313892515355e38 otherwise (preprocessing.py:14-17)."""
+    if mask is None:
+        return None
+    if mask.dtype in (torch.float16, torch.bfloat16, torch.float32):
+        if mask.dim() == 2:
+            mask = mask[:, None, None, :]
+        elif mask.dim() == 3:
+            mask = mask[:, None, :, :]
+        return mask.to(dtype)
+    minimum = -65504.0 if dtype == torch.float16 else -3.3895313892515355e38
+    bias = (mask.to(dtype) - 1.0) * -minimum
+    return bias.to(dtype).reshape(mask.shape[0], 1, -1, mask.shape[-1])
+
+
 def attention(p: dict, prefix: str, x: torch.Tensor, v: LTXVariant, *, context=None, pe=None,
-              k_pe=None):
+              k_pe=None, mask=None):
     """Gated attention with Q/K RMSNorm over all heads and split RoPE; the keys take `k_pe` when
-    given (the A/V cross-attention), else `pe` (kinomlx/models/ltx2/transformer/attention.py:249-371)."""
+    given (the A/V cross-attention), else `pe`; `mask` is an additive bias over the keys
+    (kinomlx/models/ltx2/transformer/attention.py:249-371)."""
     g = lambda name: p[f"{prefix}.{name}"]
     lin = _blin(v)
     gate = None
@@ -171,7 +190,7 @@ def attention(p: dict, prefix: str, x: torch.Tensor, v: LTXVariant, *, context=N
     tk = k.shape[1]
     heads, d = v.heads, v.head_dim
     out = sdpa(q.reshape(b, tq, heads, d).transpose(1, 2), k.reshape(b, tk, heads, d).transpose(1, 2),
-               value.reshape(b, tk, heads, d).transpose(1, 2), d ** -0.5)
+               value.reshape(b, tk, heads, d).transpose(1, 2), d ** -0.5, mask)
     out = out.transpose(1, 2)
     if gate is not None:
         out = out * gate[..., None]
@@ -185,9 +204,11 @@ def feed_forward(p: dict, prefix: str, x: torch.Tensor, lin=linear) -> torch.Ten
     return lin(h, p[f"{prefix}.project_out.weight"], p[f"{prefix}.project_out.bias"])
 
 
-def video_block(p: dict, i: int, x, context, timesteps, prompt_timestep, pe, v: LTXVariant):
+def video_block(p: dict, i: int, x, context, timesteps, prompt_timestep, pe, v: LTXVariant,
+                context_mask=None):
     """BasicAVTransformerBlock, video stream without audio (ltx2/transformer/transformer.py:178-392).
-    timesteps: (B, 1, 9, D) modulation; prompt_timestep: (B, 1, 2, D)."""
+    timesteps: (B, 1, 9, D) modulation; prompt_timestep: (B, 1, 2, D); context_mask: the
+    additive bias of context_mask_bias."""
     a = f"transformer_blocks.{i}"
     table = p[f"{a}.scale_shift_table"]
     vals = (table[None, None] + timesteps)  # bf16 op
@@ -200,16 +221,19 @@ def video_block(p: dict, i: int, x, context, timesteps, prompt_timestep, pe, v: 
     shift_ctx, scale_ctx = prompt[:, :, 0], prompt[:, :, 1]
     query = adaln(x, scale_q, shift_q, v.eps)
     ctx = (context * (1.0 + scale_ctx) + shift_ctx).to(context.dtype)
-    cross = attention(p, f"{a}.attn2", query, v, context=ctx)
+    cross = attention(p, f"{a}.attn2", query, v, context=ctx, mask=context_mask)
     x = (x + (cross * gate_c).to(x.dtype)).to(x.dtype)
     shift, scale, gate = vals[:, :, 3], vals[:, :, 4], vals[:, :, 5]
     normalized = adaln(x, scale, shift, v.eps)
     return (x + feed_forward(p, f"{a}.ff", normalized, _blin(v)) * gate).to(x.dtype)
 
 
-def forward(p: dict, latent, context, sigma: float, positions, v: LTXVariant, dtype=torch.bfloat16):
+def forward(p: dict, latent, context, sigma: float, positions, v: LTXVariant, dtype=torch.bfloat16,
+            context_mask=None):
     """LTXAVModel.__call__ for the video modality with a uniform timestep
-    (ltx2/transformer/model.py:577-635, preprocessing.py:134-213)."""
+    (ltx2/transformer/model.py:577-635, preprocessing.py:134-213); `context_mask` is the raw
+    text mask (padded prompts)."""
+    bias = context_mask_bias(context_mask, dtype)
     b = latent.shape[0]
     hidden = linear(latent, p["patchify_proj.weight"], p["patchify_proj.bias"])
     t = torch.full((b,), sigma, dtype=torch.float32)
@@ -220,7 +244,7 @@ def forward(p: dict, latent, context, sigma: float, positions, v: LTXVariant, dt
     prompt = pmod.reshape(b, -1, 2, v.dim)
     pe = precompute_freqs_cis(positions, dim=v.dim, theta=v.theta, max_pos=v.max_pos, heads=v.heads)
     for i in range(v.blocks):
-        hidden = video_block(p, i, hidden, context, timesteps, prompt, pe, v)
+        hidden = video_block(p, i, hidden, context, timesteps, prompt, pe, v, bias)
     modulation = (p["scale_shift_table"][None, None] + emb[:, :, None, :]).to(hidden.dtype)
     shift, scale = modulation[:, :, 0], modulation[:, :, 1]
     hidden = (layer_norm(hidden, v.eps) * (1.0 + scale) + shift).to(hidden.dtype)
@@ -238,12 +262,13 @@ def euler_step(sample, denoised, sigma: float, sigma_next: float):
     return (denoised.float() + ratio * (sample.float() - denoised.float())).to(sample.dtype)
 
 
-def denoise(p, latent, context, positions, sigmas, v: LTXVariant):
+def denoise(p, latent, context, positions, sigmas, v: LTXVariant, context_mask=None):
     """Deterministic-Euler loop (kinomlx/models/ltx2/denoise.py:159-365); the model dtype (which
     the timestep features are cast to) is the latent's."""
     x = latent
     for s, n in zip(sigmas[:-1], sigmas[1:]):
-        velocity = forward(p, x, context, s, positions, v, dtype=latent.dtype)
+        velocity = forward(p, x, context, s, positions, v, dtype=latent.dtype,
+                           context_mask=context_mask)
         x = euler_step(x, to_denoised(x, s, velocity), s, n)
     return x
 
@@ -278,7 +303,7 @@ def av_values(table: torch.Tensor, scale_shift: torch.Tensor, gate: torch.Tensor
     return ss[:, :, 0], ss[:, :, 1], ss[:, :, 2], ss[:, :, 3], g[:, :, 0]
 
 
-def _stream_self_and_text(p, a, prefix, x, context, timesteps, prompt_timestep, pe, v):
+def _stream_self_and_text(p, a, prefix, x, context, timesteps, prompt_timestep, pe, v, mask=None):
     """The self-attention and text cross-attention of one stream (transformer.py:249-320)."""
     table = p[f"{a}.{prefix}scale_shift_table"]
     vals = table[None, None] + timesteps
@@ -287,7 +312,7 @@ def _stream_self_and_text(p, a, prefix, x, context, timesteps, prompt_timestep, 
     prompt = p[f"{a}.{prefix}prompt_scale_shift_table"][None, None] + prompt_timestep
     query = adaln(x, vals[:, :, 7], vals[:, :, 6], v.eps)
     ctx = modulate(context, prompt[:, :, 1], prompt[:, :, 0])
-    cross = attention(p, f"{a}.{prefix}attn2", query, v, context=ctx)
+    cross = attention(p, f"{a}.{prefix}attn2", query, v, context=ctx, mask=mask)
     return (x + (cross * vals[:, :, 8]).to(x.dtype)).to(x.dtype)
 
 
@@ -299,15 +324,15 @@ def _stream_ff(p, a, prefix, x, timesteps, v):
 
 
 def av_block(p: dict, i: int, vx, ax, vctx, actx, vt, at, vprompt, aprompt, vpe, ape, vxpe,
-             axpe, vcss, vcg, acss, acg, v: LTXAVVariant):
+             axpe, vcss, vcg, acss, acg, v: LTXAVVariant, vmask=None, amask=None):
     """BasicAVTransformerBlock with both streams and both cross-modal attentions
     (kinomlx/models/ltx2/transformer/transformer.py:225-413). vt/at: (B, 1, 9, D) modulations;
     vprompt/aprompt: (B, 1, 2, D); vcss/acss: (B, 1, 4, D) cross scale/shift; vcg/acg:
     (B, 1, 1, D) cross gates; pe tables (B|1, heads, T, half)."""
     a = f"transformer_blocks.{i}"
     V, A = v.video, v.audio
-    vx = _stream_self_and_text(p, a, "", vx, vctx, vt, vprompt, vpe, V)
-    ax = _stream_self_and_text(p, a, "audio_", ax, actx, at, aprompt, ape, A)
+    vx = _stream_self_and_text(p, a, "", vx, vctx, vt, vprompt, vpe, V, vmask)
+    ax = _stream_self_and_text(p, a, "audio_", ax, actx, at, aprompt, ape, A, amask)
     vbase, abase = vx, ax
     vnorm = rms_norm(vbase, None, V.eps)
     anorm = rms_norm(abase, None, A.eps)
@@ -352,9 +377,12 @@ def av_modulations(p: dict, video_sigma: float, audio_sigma: float, b: int, v: L
 
 
 def av_forward(p: dict, vlat, alat, vctx, actx, sigma: float, vpos, apos, v: LTXAVVariant,
-               blocks: int, dtype=torch.bfloat16):
+               blocks: int, dtype=torch.bfloat16, video_context_mask=None, audio_context_mask=None):
     """LTXAVModel.__call__ with both modalities and a uniform timestep (model.py:595-635,
-    preprocessing.py:134-213): returns the (video, audio) velocities."""
+    preprocessing.py:134-213): returns the (video, audio) velocities. The text masks are the
+    raw per-stream masks (padded prompts)."""
+    vmask = context_mask_bias(video_context_mask, dtype)
+    amask = context_mask_bias(audio_context_mask, dtype)
     V, A = v.video, v.audio
     b = vlat.shape[0]
     vx = linear(vlat, p["patchify_proj.weight"], p["patchify_proj.bias"])
@@ -369,7 +397,7 @@ def av_forward(p: dict, vlat, alat, vctx, actx, sigma: float, vpos, apos, v: LTX
     axpe = precompute_freqs_cis(apos[:, 0:1], dim=A.dim, theta=A.theta, max_pos=cross_max, heads=A.heads)
     for i in range(blocks):
         vx, ax = av_block(p, i, vx, ax, vctx, actx, vt, at, vprompt, aprompt, vpe, ape, vxpe,
-                          axpe, vcss, vcg, acss, acg, v)
+                          axpe, vcss, vcg, acss, acg, v, vmask, amask)
 
     def out(x, table, emb, w, bias, eps):
         """_output (model.py:577-593): (table + embedded timestep), LayerNorm, projection."""
@@ -382,11 +410,14 @@ def av_forward(p: dict, vlat, alat, vctx, actx, sigma: float, vpos, apos, v: LTX
                 p["audio_proj_out.bias"], A.eps))
 
 
-def av_denoise(p, vlat, alat, vctx, actx, vpos, apos, sigmas, v: LTXAVVariant, blocks: int):
+def av_denoise(p, vlat, alat, vctx, actx, vpos, apos, sigmas, v: LTXAVVariant, blocks: int,
+               video_context_mask=None, audio_context_mask=None):
     """The deterministic-Euler loop over both modalities (kinomlx/models/ltx2/denoise.py:159-365)."""
     vx, ax = vlat, alat
     for s, n in zip(sigmas[:-1], sigmas[1:]):
-        vv, av = av_forward(p, vx, ax, vctx, actx, s, vpos, apos, v, blocks, dtype=vlat.dtype)
+        vv, av = av_forward(p, vx, ax, vctx, actx, s, vpos, apos, v, blocks, dtype=vlat.dtype,
+                            video_context_mask=video_context_mask,
+                            audio_context_mask=audio_context_mask)
         vx = euler_step(vx, to_denoised(vx, s, vv), s, n)
         ax = euler_step(ax, to_denoised(ax, s, av), s, n)
     return vx, ax

@@ -76,14 +76,16 @@ def linear(x, w, out=None, *, bias=None, kind=0, residual=None, gate=None, act_c
     return _put(out, y)
 
 
-def attention_list(q, k, v, out, *, heads, scale=None, gate=None, peer_return=None):
-    """ops.attention: lists of query and key/value segments."""
+def attention_list(q, k, v, out, *, heads, scale=None, gate=None, peer_return=None,
+                   key_bias=None):
+    """ops.attention: lists of query and key/value segments, an optional additive key bias."""
     q3 = torch.cat([_3(t) for t in q], 1)
     k3 = torch.cat([_3(t) for t in k], 1)
     v3 = torch.cat([_3(t) for t in v], 1)
     d = q3.shape[-1] // heads
     sh = lambda t: t.float().reshape(*t.shape[:2], heads, d).transpose(1, 2)
-    o = rops.sdpa(sh(q3), sh(k3), sh(v3), scale=d ** -0.5).transpose(1, 2)
+    mask = None if key_bias is None else key_bias[:, None, None, : k3.shape[1]]
+    o = rops.sdpa(sh(q3), sh(k3), sh(v3), scale=d ** -0.5, mask=mask).transpose(1, 2)
     if gate is not None and gate[0] is not None:
         o = o * torch.cat([_3(g) for g in gate], 1).float()[..., None]
     o = o.reshape(q3.shape)
@@ -95,10 +97,10 @@ def attention_list(q, k, v, out, *, heads, scale=None, gate=None, peer_return=No
     return out
 
 
-def attention_tensor(q, k, v, out=None, *, heads, scale=None, gate=None):
+def attention_tensor(q, k, v, out=None, *, heads, scale=None, gate=None, key_bias=None):
     """ops_f32.attention: one segment each."""
     res = attention_list([q], [k], [v], [torch.empty_like(q) if out is None else out],
-                         heads=heads, gate=None if gate is None else [gate])
+                         heads=heads, gate=None if gate is None else [gate], key_bias=key_bias)
     return res[0]
 
 

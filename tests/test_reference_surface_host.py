@@ -226,8 +226,10 @@ def test_ltx_denoise_refusals_and_nonfinite_step(monkeypatch):
         loop((0.9, 0.0), step_kind="ancestral-rf", stage=1)
     with pytest.raises(ValueError, match="uniform video denoise masks"):
         loop((0.9, 0.0), state=ldn.LatentState(latent, torch.ones(1, 24), pos, latent, False))
-    with pytest.raises(ValueError, match="padded text masks"):
-        loop((0.9, 0.0), video_context_mask=torch.ones(1, 6))
+    with pytest.raises(ValueError, match="audio text mask needs an audio latent state"):
+        loop((0.9, 0.0), audio_context_mask=torch.ones(1, 6))
+    with pytest.raises(ValueError, match="per-query masks"):
+        loop((0.9, 0.0), video_context_mask=torch.ones(1, 3, 6))
     with pytest.raises(ValueError, match="audio context is required"):
         ldn.denoise_step(state, state, sigma=0.9, sigma_next=0.5, transformer=model,
                          video_context=context)
