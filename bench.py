@@ -722,6 +722,9 @@ def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | N
     elif case == "sol_step":
         run_sol_step(dev)
         return
+    elif case == "packed_block":
+        run_packed_block(dev)
+        return
     elif case == "f32":
         # fp32 parity mode at config 1: the image stream's FF up projection (1024 x 12288 x 3072,
         # GELU epilogue) and the joint attention over 1536 tokens x 24 heads
@@ -803,6 +806,52 @@ def run_av_step(dev: torch.device) -> None:
                       "video_tokens": f * h * w, "audio_tokens": ta,
                       "video_only_step_tflop": round(ltx_step_flops() / 1e12, 1),
                       "kernels": _kernel_shares(step)}))
+
+
+def run_packed_block(dev: torch.device) -> None:
+    """Packed (mxfp8) LTX-2 block linears against bf16 ones at config 4's shapes: one transformer
+    forward over 2 blocks at 9216 video + 256 text tokens, in each `transformer_quantize` mode,
+    and the mxfp8 dequantisation of the largest weight (16384 x 4096) alone. The packed modes
+    dequantise each block linear into a bf16 scratch right before its GEMM."""
+    from kinomlx_b200 import ops
+    from kinomlx_b200.ltx2 import config as lcfg
+    from kinomlx_b200.ltx2.patchifier import latent_positions
+    from kinomlx_b200.ltx2.transformer import LTXVideoTransformer
+    from kinomlx_b200.synthetic import ltx_weights, normal
+
+    v = lcfg.BASELINE_VIDEO.with_blocks(2)
+    grid = (16, 18, 32)
+    w = ltx_weights(v, seed=0)
+    latent = normal((1, grid[0] * grid[1] * grid[2], v.in_channels), seed=1, device=dev)
+    context = normal((1, 256, v.context_dim), seed=2)
+    pos = latent_positions(*grid)
+    rows = {}
+    for mode in ("off", "mxfp8-blocks", "mxfp8-blocks-pretranspose"):
+        model = LTXVideoTransformer(w, v, dev, quantize=mode)
+        prep = model.prepare(context, pos)
+        ms = _time(lambda: model.run(prep, latent, 0.725), 3, 10, 1)
+        rows[mode] = {"ms_per_forward": round(ms, 3), "ms_per_block": round(ms / v.blocks, 3)}
+        del model, prep
+        torch.cuda.empty_cache()
+    base = rows["off"]["ms_per_forward"]
+    for mode in rows:
+        rows[mode]["vs_bf16"] = round(rows[mode]["ms_per_forward"] / base, 3)
+    from kinomlx_b200.ltx2 import quantization as qz
+
+    packed = qz.pack_linear(normal((16384, 4096), seed=3, device=dev, std=0.02), transposed=False,
+                            device=dev)
+    scratch = torch.empty((16384, 4096), device=dev, dtype=torch.bfloat16)
+    dq = {}
+    for transposed in (False, True):
+        pw = packed if not transposed else qz.pack_linear(
+            normal((16384, 4096), seed=3, device=dev, std=0.02), transposed=True, device=dev)
+        ms = _time(lambda: pw.dequantize_into(scratch), 3, 20, 1)
+        nbytes = pw.words.numel() * 4 + pw.scales.numel() + scratch.numel() * 2
+        dq["pretransposed" if transposed else "packed"] = {
+            "us": round(ms * 1e3, 1), "gbs": round(nbytes / (ms * 1e6), 1)}
+    ops.device_status()
+    print(json.dumps({"kernel_case": "packed_block", "ok": True, "tokens": latent.shape[1],
+                      "blocks": v.blocks, "modes": rows, "dequant_16384x4096": dq}))
 
 
 def run_sol_case(dev: torch.device, tau: float | None = None, family: str | None = None) -> None:
@@ -1066,7 +1115,7 @@ def main() -> None:
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
     ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow", "sol", "sol_step",
-                                              "bandwidth", "f32", "av_step", "kv_step"],
+                                              "packed_block", "bandwidth", "f32", "av_step", "kv_step"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     ap.add_argument("--sol-tau", type=float, help="--kernel-case sol: this tau only")
     ap.add_argument("--sol-inputs", choices=["iid", "smooth", "smooth_rope"],

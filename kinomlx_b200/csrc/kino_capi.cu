@@ -161,7 +161,7 @@ int device_sms() {
 // Opt a kernel into its dynamic shared memory once per device.
 template <typename K>
 kino_status ensure_smem(K kernel, int bytes, int slot) {
-  static bool done[16][64] = {{false}};
+  static bool done[32][64] = {{false}};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && done[slot][dev]) return KINO_OK;
@@ -933,7 +933,9 @@ kino_status kino_sol_attention(const kino_sol_attention_args* a, void* stream) {
   p.ld_gate = a->ld_gate;
   constexpr int smem = kino::SolSmem::TOTAL;
   if ((s = ensure_smem(kino::sol_attention_kernel, smem, 12)) != KINO_OK) return s;
-  launch_pdl(kino::sol_attention_kernel, dim3(static_cast<unsigned>(l.ncta), heads),
+  const int64_t items = l.ncta * heads;  // (head, query tile) work items, one CTA per SM
+  const unsigned persistent = static_cast<unsigned>(std::min<int64_t>(items, device_sms()));
+  launch_pdl(kino::sol_attention_kernel, dim3(persistent),
              dim3(kino::ATT_THREADS), smem, st, mq, mk, mv, mkc, mvc, p);
   return check_launch("kino_sol_attention");
 }
@@ -975,23 +977,31 @@ kino_status kino_adaln(const void* x, int64_t ldx, int64_t bsx, const void* shif
     return fail(KINO_EINVAL, "kino_adaln: rows/batch");
   if (norm_kind < 0 || norm_kind > 2) return fail(KINO_EINVAL, "kino_adaln: norm kind");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // warp per row where the width is a multiple of 256 the kernel is instantiated for
-  auto warp_form = [&](auto kernel) {
-    dim3 wgrid(static_cast<unsigned>((rows + kino::ADALN_WARPS - 1) / kino::ADALN_WARPS),
-               static_cast<unsigned>(batch));
-    launch_pdl(kernel, dim3(wgrid), dim3(kino::ADALN_WARPS * 32), 0, st,
+  // warp per row where the width is a multiple of 256 the kernel is instantiated for: a
+  // grid-stride kernel with as many CTAs as fit on the SMs at once (two row slots per warp in
+  // shared memory), or fewer when the rows run out
+  auto warp_form = [&](auto kernel, int vpl, int slot) {
+    const int smem = kino::adaln_stream_smem(vpl);
+    kino_status s = ensure_smem(kernel, smem, slot);
+    if (s != KINO_OK) return s;
+    const int static_bytes = vpl * 256 * 4;  // shift and bf16(1 + scale)
+    const int per_sm = std::max(1, std::min(4, (227 * 1024) / (smem + static_bytes + 1024)));
+    const int64_t need = (rows + kino::ADALN_WARPS - 1) / kino::ADALN_WARPS;
+    const int64_t fit = std::max<int64_t>(1, int64_t{per_sm} * device_sms() / batch);
+    dim3 wgrid(static_cast<unsigned>(std::min(need, fit)), static_cast<unsigned>(batch));
+    launch_pdl(kernel, dim3(wgrid), dim3(kino::ADALN_WARPS * 32), smem, st,
         static_cast<const __nv_bfloat16*>(x), ldx, bsx, static_cast<const __nv_bfloat16*>(shift),
         static_cast<const __nv_bfloat16*>(scale), bs_mod, static_cast<__nv_bfloat16*>(out), ldo,
         bso, static_cast<int>(rows), norm_kind, eps);
     return check_launch("kino_adaln");
   };
   switch (dim) {
-    case 256: return warp_form(kino::adaln_warp_kernel<1>);
-    case 512: return warp_form(kino::adaln_warp_kernel<2>);
-    case 1024: return warp_form(kino::adaln_warp_kernel<4>);
-    case 2048: return warp_form(kino::adaln_warp_kernel<8>);
-    case 3072: return warp_form(kino::adaln_warp_kernel<12>);
-    case 4096: return warp_form(kino::adaln_warp_kernel<16>);
+    case 256: return warp_form(kino::adaln_warp_kernel<1>, 1, 16);
+    case 512: return warp_form(kino::adaln_warp_kernel<2>, 2, 17);
+    case 1024: return warp_form(kino::adaln_warp_kernel<4>, 4, 18);
+    case 2048: return warp_form(kino::adaln_warp_kernel<8>, 8, 19);
+    case 3072: return warp_form(kino::adaln_warp_kernel<12>, 12, 20);
+    case 4096: return warp_form(kino::adaln_warp_kernel<16>, 16, 21);
     default: break;
   }
   dim3 grid(static_cast<unsigned>(rows), static_cast<unsigned>(batch));
@@ -1444,9 +1454,24 @@ kino_status kino_dequantize(const void* words, const void* scales, const void* b
                                     "and of 16 (and rows of 16 for a transposed output)");
   if (!aligned16(words) || !aligned16(out))
     return fail(KINO_EINVAL, "kino_dequantize: words and out must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (mode == KINO_QUANT_MXFP8) {
+    // whole 32-code groups, grid-stride over 148 SMs x 8 CTAs
+    const int64_t groups = rows * (cols / 32);
+    const int64_t want = (groups + kino::DQ8_THREADS - 1) / kino::DQ8_THREADS;
+    const unsigned blocks = static_cast<unsigned>(want < 148 * 8 ? want : 148 * 8);
+    if (!transpose_out)
+      launch_pdl(kino::dequant_mxfp8_rows_kernel, dim3(blocks), dim3(kino::DQ8_THREADS), 0, s,
+                 static_cast<const uint2*>(words), static_cast<const uint8_t*>(scales),
+                 static_cast<uint4*>(out), groups * 4);
+    else  // rows is a multiple of 16 here
+      launch_pdl(kino::dequant_mxfp8_cols_kernel, dim3(blocks), dim3(kino::DQ8_THREADS), 0, s,
+                 static_cast<const uint4*>(words), static_cast<const uint8_t*>(scales),
+                 static_cast<uint32_t*>(out), rows, cols);
+    return check_launch("kino_dequantize");
+  }
   const dim3 grid(static_cast<unsigned>((cols + kino::DQ_TILE - 1) / kino::DQ_TILE),
                   static_cast<unsigned>((rows + kino::DQ_TILE - 1) / kino::DQ_TILE));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint32_t* w = static_cast<const uint32_t*>(words);
   const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(biases);
   __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);

@@ -120,11 +120,24 @@ __global__ void __launch_bounds__(ADALN_THREADS)
   }
 }
 
-// Warp-per-row form of the same modulated norm for dim = 256 * VPL: a warp holds its row in
-// registers as packed bf16 (VPL 16-byte vectors per lane), reduces with shuffles only, and reads
-// shift and bf16(1 + scale) from shared memory, filled once per CTA. Same rounding points as
-// adaln_kernel.
+// Warp-per-row form of the same modulated norm for dim = 256 * VPL, as a streaming kernel: each
+// warp walks rows grid-stride (a few CTAs per SM), and every row arrives by cp.async into the
+// warp's two shared-memory row slots, the next row's copy in flight while the current one is
+// reduced, so the loads of a whole launch are issued up front without holding registers. A lane
+// copies and later reads only its own 16-byte chunks (chunk i * 32 + lane), so the per-thread
+// cp.async wait is the only synchronisation a row needs. The row is then held in registers as
+// packed bf16 (VPL vectors per lane), reduced with shuffles only, and modulated with shift and
+// bf16(1 + scale) from shared memory, filled once per CTA. Same rounding points as adaln_kernel.
 constexpr int ADALN_WARPS = 8;
+
+__host__ __device__ constexpr int adaln_stream_smem(int vpl) {
+  return ADALN_WARPS * 2 * vpl * 32 * 16;  // two row slots per warp
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
 
 template <int VPL>
 __global__ void __launch_bounds__(ADALN_WARPS * 32)
@@ -133,12 +146,27 @@ __global__ void __launch_bounds__(ADALN_WARPS * 32)
                       const __nv_bfloat16* __restrict__ scale, int64_t bs_mod,
                       __nv_bfloat16* __restrict__ out, int64_t ld_out, int64_t bs_out, int rows,
                       int norm_kind, float eps) {
-  griddep_wait();
-  griddep_launch();
   constexpr int DIM = VPL * 256;
   __shared__ uint4 s_shift[DIM / 8];
   __shared__ uint4 s_onep[DIM / 8];  // bf16(1 + scale)
+  extern __shared__ uint4 s_rows[];  // [warp][slot][VPL * 32]
+  griddep_wait();
+  griddep_launch();
   const int b = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  uint4* slots = s_rows + warp * 2 * VPL * 32;
+  const int step = gridDim.x * ADALN_WARPS;
+  const __nv_bfloat16* xb = x + b * bs_x;
+  auto issue = [&](int row, int slot) {
+    const __nv_bfloat16* xr = xb + static_cast<int64_t>(row) * ld_x;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+      cp_async16(slots + slot * VPL * 32 + i * 32 + lane, xr + (i * 32 + lane) * 8);
+  };
+  int row = blockIdx.x * ADALN_WARPS + warp;
+  if (row < rows) issue(row, 0);
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
   const __nv_bfloat16* sh = shift + b * bs_mod;
   const __nv_bfloat16* sc = scale + b * bs_mod;
   for (int c = threadIdx.x; c < DIM / 8; c += ADALN_WARPS * 32) {
@@ -155,63 +183,73 @@ __global__ void __launch_bounds__(ADALN_WARPS * 32)
     s_onep[c] = w;
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * ADALN_WARPS + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const __nv_bfloat16* xr = x + b * bs_x + static_cast<int64_t>(row) * ld_x;
-  __nv_bfloat16* orow = out + b * bs_out + static_cast<int64_t>(row) * ld_out;
-  uint4 raw[VPL];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) raw[i] = *reinterpret_cast<const uint4*>(xr + (i * 32 + lane) * 8);
-  auto unpack = [](const uint4& r, float (&f)[8]) {
-    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 t = unpack_bf16x2(w[k]);
-      f[2 * k] = t.x;
-      f[2 * k + 1] = t.y;
-    }
-  };
-  float mean = 0.0f, rstd = 1.0f;
-  if (norm_kind != 2) {
-    if (norm_kind == 1) {
-      float s = 0.0f;
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        float f[8];
-        unpack(raw[i], f);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s += f[j];
-      }
-      mean = warp_sum(s) / static_cast<float>(DIM);
-    }
-    float q = 0.0f;
+  // a bf16 pair as an fp32 pair (exact)
+  auto widen = [](uint32_t w) { return f2_pack(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u)); };
+  for (int k = 0; row < rows; row += step, ++k) {
+    if (row + step < rows) issue(row + step, (k + 1) & 1);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // this row's copies have landed
+    const uint4* mine = slots + (k & 1) * VPL * 32;
+    uint32_t wv[VPL][4];
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
-      float f[8];
-      unpack(raw[i], f);
+      const uint4 r = mine[i * 32 + lane];
+      wv[i][0] = r.x;
+      wv[i][1] = r.y;
+      wv[i][2] = r.z;
+      wv[i][3] = r.w;
+    }
+    __nv_bfloat16* orow = out + b * bs_out + static_cast<int64_t>(row) * ld_out;
+    // statistics on fp32 pairs (sm_100 f32x2 arithmetic), reduced over the warp in fp32
+    float mean = 0.0f, rstd = 1.0f;
+    if (norm_kind != 2) {
+      if (norm_kind == 1) {
+        uint64_t s2 = f2_pack(0.0f, 0.0f);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float d = f[j] - mean;
-        q += d * d;
+        for (int i = 0; i < VPL; ++i)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) s2 = f2_add(s2, widen(wv[i][e]));
+        const float2 sv = f2_unpack(s2);
+        mean = warp_sum(sv.x + sv.y) / static_cast<float>(DIM);
       }
-    }
-    rstd = rsqrtf(warp_sum(q) / static_cast<float>(DIM) + eps);
-  }
+      const uint64_t nm2 = f2_pack(-mean, -mean);
+      uint64_t q2 = f2_pack(0.0f, 0.0f);
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int c = i * 32 + lane;
-    float f[8], fs[8], op[8], o[8];
-    unpack(raw[i], f);
-    unpack(s_shift[c], fs);
-    unpack(s_onep[c], op);
+      for (int i = 0; i < VPL; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float n = norm_kind == 2 ? f[j] : bf16_round((f[j] - mean) * rstd);
-      o[j] = bf16_round(n * op[j]) + fs[j];
+        for (int e = 0; e < 4; ++e) {
+          const uint64_t d = f2_add(widen(wv[i][e]), nm2);
+          q2 = f2_fma(d, d, q2);
+        }
+      const float2 qv = f2_unpack(q2);
+      rstd = rsqrtf(warp_sum(qv.x + qv.y) / static_cast<float>(DIM) + eps);
     }
-    store8(orow + c * 8, o);
+    // n = bf16((x - mean) * rstd) on fp32 pairs, then bf16(bf16(n * (1 + scale)) + shift) as
+    // two bf16x2 operations, each the single rounding of an exact product or sum
+    const uint64_t nm2 = f2_pack(-mean, -mean), rs2 = f2_pack(rstd, rstd);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = i * 32 + lane;
+      const uint4 shv = s_shift[c], opv = s_onep[c];
+      const uint32_t sw[4] = {shv.x, shv.y, shv.z, shv.w};
+      const uint32_t ow[4] = {opv.x, opv.y, opv.z, opv.w};
+      uint32_t res[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        uint32_t nb = wv[i][e];
+        if (norm_kind != 2) {
+          const float2 nv = f2_unpack(f2_mul(f2_add(widen(wv[i][e]), nm2), rs2));
+          nb = pack_bf16x2(nv.x, nv.y);
+        }
+        const __nv_bfloat162 prod = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&nb),
+                                            *reinterpret_cast<const __nv_bfloat162*>(&ow[e]));
+        const __nv_bfloat162 sum = __hadd2(prod, *reinterpret_cast<const __nv_bfloat162*>(&sw[e]));
+        res[e] = *reinterpret_cast<const uint32_t*>(&sum);
+      }
+      *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(res[0], res[1], res[2], res[3]);
+    }
   }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 }
 
 // ----------------------------------------------------------------------------- RMSNorm

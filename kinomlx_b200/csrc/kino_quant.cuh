@@ -120,4 +120,90 @@ __global__ void __launch_bounds__(DQ_THREADS)
   }
 }
 
+// Two E4M3 codes (the low byte first) to two f16 values: exact, E4M3 being a subset of f16.
+__device__ __forceinline__ float2 dq_e4m3x2(uint32_t two_codes) {
+  uint32_t h;
+  const uint16_t a = static_cast<uint16_t>(two_codes);
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(a));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+constexpr int DQ8_THREADS = 256;
+
+// mxfp8 in the packed orientation (codes along each output row, the GEMM's K): the matrix as
+// one flat sequence of 8-code chunks (the rows are contiguous, groups of 32 never straddle
+// them); lane l of a warp takes chunk l of each 32-chunk run, so every load (8 bytes of codes)
+// and store (16 bytes of bf16) instruction of the warp is one contiguous segment. Four chunks
+// per thread are in flight at a time, grid-stride. Codes go through the hardware E4M3 -> f16
+// conversion (exact), then the same fp32 product with the group's power-of-two scale and the
+// single bf16 rounding as dequant_kernel.
+__device__ __forceinline__ uint4 dq8_chunk(uint2 c, float sc) {
+  const float2 a = dq_e4m3x2(c.x & 0xFFFFu), b = dq_e4m3x2(c.x >> 16);
+  const float2 d = dq_e4m3x2(c.y & 0xFFFFu), e = dq_e4m3x2(c.y >> 16);
+  return make_uint4(pack_bf16x2(a.x * sc, a.y * sc), pack_bf16x2(b.x * sc, b.y * sc),
+                    pack_bf16x2(d.x * sc, d.y * sc), pack_bf16x2(e.x * sc, e.y * sc));
+}
+
+__global__ void __launch_bounds__(DQ8_THREADS)
+    dequant_mxfp8_rows_kernel(const uint2* __restrict__ codes, const uint8_t* __restrict__ scales,
+                              uint4* __restrict__ out, int64_t chunks) {
+  griddep_wait();
+  griddep_launch();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * DQ8_THREADS;
+  int64_t e = static_cast<int64_t>(blockIdx.x) * DQ8_THREADS + threadIdx.x;
+  for (; e + 3 * stride < chunks; e += 4 * stride) {
+    uint2 c[4];
+    float sc[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      c[u] = __ldg(codes + e + u * stride);
+      sc[u] = dq_e8m0(__ldg(scales + (e + u * stride) / 4));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) out[e + u * stride] = dq8_chunk(c[u], sc[u]);
+  }
+  for (; e < chunks; e += stride) out[e] = dq8_chunk(__ldg(codes + e), dq_e8m0(__ldg(scales + e / 4)));
+}
+
+// mxfp8 packed from weight.T (the reference's pretransposed weights: codes along the output
+// dimension, `rows` = input features) into the GEMM's (out, in) bf16 rows, without a shared-
+// memory pass: a warp takes 64 code rows x 32 code columns; lane l decodes its two rows' 32-code
+// groups (full 32-byte sectors) and writes, for each of the 32 columns, the bf16 pair of its two
+// rows, so each store instruction of the warp fills one contiguous 128-byte output segment.
+__global__ void __launch_bounds__(DQ8_THREADS)
+    dequant_mxfp8_cols_kernel(const uint4* __restrict__ codes, const uint8_t* __restrict__ scales,
+                              uint32_t* __restrict__ out, int64_t rows, int64_t cols) {
+  griddep_wait();
+  griddep_launch();
+  const int lane = threadIdx.x & 31;
+  const int64_t col_tasks = cols / 32;
+  const int64_t tasks = (rows + 63) / 64 * col_tasks;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (DQ8_THREADS / 32);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (DQ8_THREADS / 32) + (threadIdx.x >> 5);
+       t < tasks; t += warps) {
+    const int64_t c0 = (t % col_tasks) * 32;
+    const int64_t r = (t / col_tasks) * 64 + 2 * lane;  // rows r, r + 1 (rows is even)
+    if (r >= rows) continue;
+    const int64_t g0 = r * col_tasks + c0 / 32, g1 = g0 + col_tasks;
+    const uint4 a0 = __ldg(codes + 2 * g0), b0 = __ldg(codes + 2 * g0 + 1);
+    const uint4 a1 = __ldg(codes + 2 * g1), b1 = __ldg(codes + 2 * g1 + 1);
+    const float s0 = dq_e8m0(__ldg(scales + g0)), s1 = dq_e8m0(__ldg(scales + g1));
+    const uint32_t w0[8] = {a0.x, a0.y, a0.z, a0.w, b0.x, b0.y, b0.z, b0.w};
+    const uint32_t w1[8] = {a1.x, a1.y, a1.z, a1.w, b1.x, b1.y, b1.z, b1.w};
+    uint32_t* dst = out + (c0 * rows + r) / 2;  // out[c0][r .. r + 1] as one bf16 pair
+    const int64_t col_stride = rows / 2;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float2 x = dq_e4m3x2((w0[i] >> (16 * h)) & 0xFFFFu);
+        const float2 y = dq_e4m3x2((w1[i] >> (16 * h)) & 0xFFFFu);
+        const int j = 4 * i + 2 * h;
+        dst[j * col_stride] = pack_bf16x2(x.x * s0, y.x * s1);
+        dst[(j + 1) * col_stride] = pack_bf16x2(x.y * s0, y.y * s1);
+      }
+    }
+  }
+}
+
 }  // namespace kino

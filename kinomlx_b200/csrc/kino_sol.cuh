@@ -6,23 +6,24 @@
 // plus itself and both neighbours; routed blocks are attended exactly, every other block through
 // its mean key (score + log2 of the block's length) and mean value, all in one softmax.
 //
-// Three launches:
+// Four launches:
 //   sol_prepare_kernel   gather q, k, v into routing order as fp16 (saturating at 65504, as the
 //                        reference's kernel converts them), and the 64-token block means: fp32
 //                        query means, key / value means rounded to the input dtype, then fp16
 //   sol_route_kernel     per (head, query block): the routing row as 32-bit mask words
-//   sol_union_kernel     per (head, CTA): the ascending list of key blocks routed by any of the
-//                        CTA's four query blocks
-//   sol_attention_kernel the attention: attention_tc_kernel's pipeline (two 128-query tiles =
-//                        four Sol blocks per CTA in ping-pong, TMA / MMA / eight softmax warps,
-//                        S and O in tensor memory, P back over S) on fp16 operands, with the K/V
-//                        producer walking the CTA's block list (two 64-key blocks per 128-key
-//                        stage) and then the centroid keys (every key block's mean, 128 per
-//                        stage). Each softmax warp covers one 64-key block per stage, so routing
-//                        is one mask bit per (row, stage half) for exact blocks and one per
-//                        (row, key) for centroids (a row's routed blocks are excluded there).
-//                        Output rows go back to their input positions, in the input dtype, with
-//                        the optional per-head gate.
+//   sol_union_kernel     per (head, query tile): the ascending list of key blocks routed by any
+//                        of the tile's two query blocks
+//   sol_attention_kernel the attention: a persistent CTA per SM walks (head, query tile) items;
+//                        attention_tc_kernel's roles (TMA / MMA / eight softmax warps, S and O in
+//                        tensor memory, P back over S) on fp16 operands, one 128-row query tile
+//                        per item whose key stages alternate between two streams (own S, O and
+//                        row statistics each, merged at the end). The K/V producer walks the
+//                        item's block list (two 64-key blocks per 128-key stage) and then the
+//                        centroid keys (every key block's mean, 128 per stage). Each softmax warp
+//                        covers one 64-key block per stage, so routing is one mask bit per (row,
+//                        stage half) for exact blocks and one per (row, key) for centroids (a
+//                        row's routed blocks are excluded there). Output rows go back to their
+//                        input positions, in the input dtype, with the optional per-head gate.
 #pragma once
 #include <cuda_fp16.h>
 
@@ -316,31 +317,40 @@ struct SolParams {
   int64_t ld_gate;
 };
 
-// Shared memory of sol_attention_kernel: one 128-row query tile, two 128-key K/V stages, the
-// softmax exchange areas and barriers of the dense kernel, then the CTA's routing words and
-// block list.
+// Shared memory of sol_attention_kernel: two 128-row query tiles (the current work item's and the
+// next one's), two 128-key K/V stages (one per key stream), the softmax exchange areas and
+// barriers of the dense kernel, then two copies of the work item's routing words, block list
+// and block count.
 struct SolSmem {
   static constexpr int HALF = AttnSmem::HALF;
-  static constexpr int Q_OFF = 0;
-  static constexpr int KV_OFF = 2 * HALF;
+  static constexpr int Q_OFF = 0;                      // buffer b at Q_OFF + b * 2 * HALF
+  static constexpr int KV_OFF = 4 * HALF;
   static constexpr int STAGE = 4 * HALF;
   static constexpr int X_OFF = KV_OFF + ATT_STAGES * STAGE;
   static constexpr int L_OFF = X_OFF + 2 * 2 * 2 * 128 * 4;
   static constexpr int BAR_OFF = L_OFF + 2 * 2 * 128 * 4;
-  static constexpr int NBAR = AttnSmem::NBAR;
+  // q_full[2], q_empty[2], meta_full[2], meta_empty[2], kv_full[2], kv_empty[2], s_full[2],
+  // p_full[2], o_done, drain, xbar[4][2][2], lbar[4]
+  static constexpr int NBAR = 16 + 2 + 16 + 4;
   static constexpr int W_OFF = BAR_OFF + NBAR * 8 + 16;
-  static constexpr int LIST_OFF = W_OFF + SOL_QBLOCKS * SOL_MAX_WORDS * 4;
-  static constexpr int TOTAL = LIST_OFF + SOL_MAX_WORDS * 32 * 4 + 1024;
+  static constexpr int WORDS = SOL_QBLOCKS * SOL_MAX_WORDS;  // routing words of one item
+  static constexpr int LIST_OFF = W_OFF + 2 * WORDS * 4;
+  static constexpr int COUNT_OFF = LIST_OFF + 2 * SOL_MAX_WORDS * 32 * 4;
+  static constexpr int TOTAL = COUNT_OFF + 16 + 1024;
 };
 
-// One CTA: query blocks 2c and 2c + 1 (one 128-row tile) against the ascending list of key
-// blocks either of them routes, then the centroids. The stages (two 64-key blocks, or 128
-// centroids) alternate between two key streams, A taking stages 0, 2, 4, ... and B stages
-// 1, 3, 5, ...: each stream has its own S and O in tensor memory and its own running row
-// maxima and sums, so the MMA warp works on one stream while the softmax warps work on the
-// other (the dense kernel's ping-pong, over key halves of one query tile instead of over two
-// query tiles), and the epilogue merges the two streams by their row statistics. Stage i
-// lives in K/V slot i % 2, so each stream owns a slot.
+// A persistent CTA per SM walks work items it = blockIdx.x, blockIdx.x + gridDim.x, ... (head
+// it / ncta, query tile it % ncta: query blocks 2c and 2c + 1). An item is the tile against the
+// ascending list of key blocks either of its query blocks routes, then the centroids. The stages
+// (two 64-key blocks, or 128 centroids) alternate between two key streams, A taking stages
+// 0, 2, 4, ... and B stages 1, 3, 5, ...: each stream has its own S and O in tensor memory and
+// its own running row maxima and sums, so the MMA warp works on one stream while the softmax
+// warps work on the other, and the epilogue merges the two streams by their row statistics.
+// Stream t owns K/V slot t. Across items the ring and barrier phases run on (per-stream stage
+// counts carried from item to item), the next item's Q tile, block list and first products are
+// under way while the softmax warps finish the current item's epilogue, and the tensor memory
+// is allocated once. The next item's first PV product overwrites O only after the softmax warps
+// signal that item's first P, which they do after their epilogue has read O.
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     sol_attention_kernel(const __grid_constant__ CUtensorMap mq,
                          const __grid_constant__ CUtensorMap mk,
@@ -355,38 +365,41 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + ATT_STAGES;
-  uint64_t* s_full = kv_empty + ATT_STAGES;  // [stream]
-  uint64_t* p_full = s_full + 2;             // [stream]
-  uint64_t* o_done = p_full + 2;
-  uint64_t* drain = o_done + 1;
-  uint64_t* xbar = drain + 1;                // [quarter][stream][parity]
-  uint64_t* lbar = xbar + 16;                // [quarter]
+  uint64_t* q_full = bars;            // [buffer]
+  uint64_t* q_empty = bars + 2;       // [buffer]
+  uint64_t* meta_full = bars + 4;     // [buffer]
+  uint64_t* meta_empty = bars + 6;    // [buffer]
+  uint64_t* kv_full = bars + 8;       // [stream]
+  uint64_t* kv_empty = bars + 10;     // [stream]
+  uint64_t* s_full = bars + 12;       // [stream]
+  uint64_t* p_full = bars + 14;       // [stream]
+  uint64_t* o_done = bars + 16;
+  uint64_t* drain = bars + 17;
+  uint64_t* xbar = bars + 18;         // [quarter][stream][parity]
+  uint64_t* lbar = xbar + 16;         // [quarter]
   float* xmax = reinterpret_cast<float*>(smem + L::X_OFF);
   float* xsum = reinterpret_cast<float*>(smem + L::L_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  uint32_t* rwords = reinterpret_cast<uint32_t*>(smem + L::W_OFF);
-  int* slist = reinterpret_cast<int*>(smem + L::LIST_OFF);
+  uint32_t* rwords_all = reinterpret_cast<uint32_t*>(smem + L::W_OFF);  // [buffer][WORDS]
+  int* slist_all = reinterpret_cast<int*>(smem + L::LIST_OFF);         // [buffer][512]
+  int* mcount = reinterpret_cast<int*>(smem + L::COUNT_OFF);           // [buffer]
 
   const int warp = warp_id();
   const uint32_t lane = lane_id();
-  const int cta = blockIdx.x;
-  const int head = blockIdx.y;
-  const int row0 = cta * 128;
-  const int* list = p.lists + (static_cast<int64_t>(head) * p.ncta + cta) * p.nb;
+  const int items = p.ncta * p.heads;
+  const int ncent = (p.nb + 127) / 128;  // centroid stages
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < ATT_STAGES; ++i) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&meta_full[i], 1);
+      mbar_init(&meta_empty[i], 9);  // the eight softmax warps and the MMA warp
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-    }
-    for (int t = 0; t < 2; ++t) {
-      mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 8);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 8);
     }
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
@@ -395,18 +408,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  griddep_wait();
-  if (threadIdx.x < SOL_QBLOCKS * SOL_MAX_WORDS) {
-    const int qb = cta * SOL_QBLOCKS + threadIdx.x / SOL_MAX_WORDS;
-    const int w = threadIdx.x % SOL_MAX_WORDS;
-    rwords[threadIdx.x] = (qb < p.nb && w < p.words)
-                              ? p.bits[(static_cast<int64_t>(head) * p.nb + qb) * p.words + w]
-                              : 0u;
+  if (warp == 0 && lane == 0) {
+    tma_prefetch(&mq);
+    tma_prefetch(&mk);
+    tma_prefetch(&mv);
+    tma_prefetch(&mkc);
+    tma_prefetch(&mvc);
   }
-  const int count = p.counts[head * p.ncta + cta];
-  for (int i = threadIdx.x; i < count; i += blockDim.x) slist[i] = list[i];
-  const int ns = (count + 1) / 2;            // exact stages: two 64-key blocks each
-  const int nst = ns + (p.nb + 127) / 128;   // then the centroid stages
+  griddep_wait();
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -418,106 +427,144 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   griddep_launch();
 
   if (warp == 0) {
-    if (lane == 0) {
-      mbar_expect_tx(q_full, NH * L::HALF);
-      tma_load_4d(smem + L::Q_OFF, &mq, q_full, 0, row0, head, 0);
-      tma_load_4d(smem + L::Q_OFF + L::HALF, &mq, q_full, 64, row0, head, 0);
-      int issued = 0;
-      for (int i = 0; i < nst; ++i) {
-        const int slot = i & 1;
-        const uint32_t parity = (i >> 1) & 1;
-        if (!mbar_wait(&kv_empty[slot], parity ^ 1u, abort_flag)) break;
-        uint8_t* sk = smem + L::KV_OFF + slot * L::STAGE;
-        uint8_t* sv = sk + 2 * L::HALF;
-        mbar_expect_tx(&kv_full[slot], 2 * NH * L::HALF);
-        if (i < ns) {
-          const int kb0 = slist[2 * i];
-          const int kb1 = 2 * i + 1 < count ? slist[2 * i + 1] : kb0;  // a masked stand-in
-#pragma unroll
-          for (int h2 = 0; h2 < NH; ++h2) {
-            tma_load_4d(sk + h2 * L::HALF, &mk, &kv_full[slot], h2 * 64, kb0 * 64, head, 0);
-            tma_load_4d(sk + h2 * L::HALF + SUB, &mk, &kv_full[slot], h2 * 64, kb1 * 64, head, 0);
-            tma_load_4d(sv + h2 * L::HALF, &mv, &kv_full[slot], h2 * 64, kb0 * 64, head, 0);
-            tma_load_4d(sv + h2 * L::HALF + SUB, &mv, &kv_full[slot], h2 * 64, kb1 * 64, head, 0);
-          }
+    // the work items' block lists and routing words (all lanes), Q tiles and K/V stages (lane 0)
+    int kcount[2] = {0, 0};  // stages issued per stream, over all items
+    int j = 0;
+    for (int it = blockIdx.x; it < items; it += gridDim.x, ++j) {
+      const int buf = j & 1;
+      const uint32_t use = static_cast<uint32_t>(j >> 1) & 1u;
+      const int head = it / p.ncta, cta = it % p.ncta;
+      if (!mbar_wait(&meta_empty[buf], use ^ 1u, abort_flag)) break;
+      const int count = p.counts[head * p.ncta + cta];
+      const int qb = cta * SOL_QBLOCKS + static_cast<int>(lane) / SOL_MAX_WORDS;
+      const int w = static_cast<int>(lane) % SOL_MAX_WORDS;
+      rwords_all[buf * L::WORDS + lane] =
+          (qb < p.nb && w < p.words) ? p.bits[(static_cast<int64_t>(head) * p.nb + qb) * p.words + w]
+                                     : 0u;
+      const int* list = p.lists + (static_cast<int64_t>(head) * p.ncta + cta) * p.nb;
+      for (int i = static_cast<int>(lane); i < count; i += 32) slist_all[buf * 512 + i] = list[i];
+      if (lane == 0) mcount[buf] = count;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&meta_full[buf]);
+        if (!mbar_wait(&q_empty[buf], use ^ 1u, abort_flag)) {
+          *abort_flag = 1;
         } else {
-          const int c0 = (i - ns) * 128;
+          uint8_t* sq = smem + L::Q_OFF + buf * 2 * L::HALF;
+          mbar_expect_tx(&q_full[buf], NH * L::HALF);
+          tma_load_4d(sq, &mq, &q_full[buf], 0, cta * 128, head, 0);
+          tma_load_4d(sq + L::HALF, &mq, &q_full[buf], 64, cta * 128, head, 0);
+          const int* sl = slist_all + buf * 512;
+          const int ns = (count + 1) / 2;
+          const int nst = ns + ncent;
+          for (int i = 0; i < nst; ++i) {
+            const int t = i & 1;
+            const uint32_t parity = static_cast<uint32_t>(kcount[t]) & 1u;
+            if (!mbar_wait(&kv_empty[t], parity ^ 1u, abort_flag)) break;
+            ++kcount[t];
+            uint8_t* sk = smem + L::KV_OFF + t * L::STAGE;
+            uint8_t* sv = sk + 2 * L::HALF;
+            mbar_expect_tx(&kv_full[t], 2 * NH * L::HALF);
+            if (i < ns) {
+              const int kb0 = sl[2 * i];
+              const int kb1 = 2 * i + 1 < count ? sl[2 * i + 1] : kb0;  // a masked stand-in
 #pragma unroll
-          for (int h2 = 0; h2 < NH; ++h2) {
-            tma_load_3d(sk + h2 * L::HALF, &mkc, &kv_full[slot], h2 * 64, c0, head);
-            tma_load_3d(sk + h2 * L::HALF + SUB, &mkc, &kv_full[slot], h2 * 64, c0 + 64, head);
-            tma_load_3d(sv + h2 * L::HALF, &mvc, &kv_full[slot], h2 * 64, c0, head);
-            tma_load_3d(sv + h2 * L::HALF + SUB, &mvc, &kv_full[slot], h2 * 64, c0 + 64, head);
+              for (int h2 = 0; h2 < NH; ++h2) {
+                tma_load_4d(sk + h2 * L::HALF, &mk, &kv_full[t], h2 * 64, kb0 * 64, head, 0);
+                tma_load_4d(sk + h2 * L::HALF + SUB, &mk, &kv_full[t], h2 * 64, kb1 * 64, head, 0);
+                tma_load_4d(sv + h2 * L::HALF, &mv, &kv_full[t], h2 * 64, kb0 * 64, head, 0);
+                tma_load_4d(sv + h2 * L::HALF + SUB, &mv, &kv_full[t], h2 * 64, kb1 * 64, head, 0);
+              }
+            } else {
+              const int c0 = (i - ns) * 128;
+#pragma unroll
+              for (int h2 = 0; h2 < NH; ++h2) {
+                tma_load_3d(sk + h2 * L::HALF, &mkc, &kv_full[t], h2 * 64, c0, head);
+                tma_load_3d(sk + h2 * L::HALF + SUB, &mkc, &kv_full[t], h2 * 64, c0 + 64, head);
+                tma_load_3d(sv + h2 * L::HALF, &mvc, &kv_full[t], h2 * 64, c0, head);
+                tma_load_3d(sv + h2 * L::HALF + SUB, &mvc, &kv_full[t], h2 * 64, c0 + 64, head);
+              }
+            }
           }
         }
-        ++issued;
       }
-      if (*abort_flag) {
-        const uint64_t t0 = global_ns();
-        while (!mbar_try_wait(q_full, 0) && global_ns() - t0 < 200000000ull) {
-        }
-        for (int i = issued - 1; i >= 0 && i >= issued - ATT_STAGES; --i) {
-          const uint64_t t1 = global_ns();
-          while (!mbar_try_wait(&kv_full[i & 1], (i >> 1) & 1) &&
-                 global_ns() - t1 < 200000000ull) {
-          }
-        }
+      __syncwarp();
+      if (*abort_flag) break;
+    }
+    if (lane == 0 && *abort_flag) {
+      // after a timeout, give copies still in flight a bounded moment to land
+      const uint64_t t0 = global_ns();
+      while (global_ns() - t0 < 100000000ull) {
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_f16(ATT_BM, ATT_BN);
       constexpr uint32_t idesc_o = idesc_f16(ATT_BM, D) | (1u << 16);  // B (V) MN-major
-      const uint32_t sq = smem_u32(smem + L::Q_OFF);
-      auto s_mma = [&](int t) {  // S_t = Q K^T of the stage in slot t
-        const uint32_t sk = smem_u32(smem + L::KV_OFF + t * L::STAGE);
+      int fk[2] = {0, 0};  // K/V stages consumed per stream, over all items
+      int pk[2] = {0, 0};  // P signals consumed per stream
+      bool ok = true;
+      int j = 0;
+      for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++j) {
+        const int buf = j & 1;
+        const uint32_t use = static_cast<uint32_t>(j >> 1) & 1u;
+        if (!mbar_wait(&meta_full[buf], use, abort_flag)) break;
+        const int count = mcount[buf];
+        mbar_arrive(&meta_empty[buf]);
+        const int nst = (count + 1) / 2 + ncent;
+        if (!mbar_wait(&q_full[buf], use, abort_flag)) break;
+        const uint32_t sq = smem_u32(smem + L::Q_OFF + buf * 2 * L::HALF);
+        auto s_mma = [&](int t) {  // S_t = Q K^T of the stage in slot t
+          const uint32_t sk = smem_u32(smem + L::KV_OFF + t * L::STAGE);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * L::HALF + (kk & 3) * 32;
-          umma_bf16(tmem + t * 128, sdesc_k128(sq + off), sdesc_k128(sk + off), idesc_s,
-                    kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[t]);
-      };
-      auto pv_mma = [&](int t, bool first) {  // O_t += P_t V of the stage in slot t
-        const uint32_t sv = smem_u32(smem + L::KV_OFF + t * L::STAGE + 2 * L::HALF);
-#pragma unroll
-        for (int kk = 0; kk < ATT_BN / 16; ++kk) {
-          umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8 + (kk >= 4 ? 32 : 0),
-                       sdesc_mn128(sv + kk * 2048, L::HALF), idesc_o,
-                       (!first || kk > 0) ? 1u : 0u);
-        }
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag) && nst > 0;
-      for (int t = 0; ok && t < 2 && t < nst; ++t) {
-        ok = mbar_wait(&kv_full[t], 0, abort_flag);
-        if (ok) {
-          tc_fence_after();
-          s_mma(t);
-        }
-      }
-      for (int k = 0; ok && 2 * k < nst; ++k) {
-        for (int t = 0; t < 2 && ok; ++t) {
-          const int i = 2 * k + t;
-          if (i >= nst) break;
-          if (!mbar_wait(&p_full[t], k & 1, abort_flag)) {
-            ok = false;
-            break;
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * L::HALF + (kk & 3) * 32;
+            umma_bf16(tmem + t * 128, sdesc_k128(sq + off), sdesc_k128(sk + off), idesc_s,
+                      kk > 0 ? 1u : 0u);
           }
-          tc_fence_after();
-          pv_mma(t, k == 0);
-          umma_commit(&kv_empty[t]);
-          if (i + 2 < nst) {
-            if (!mbar_wait(&kv_full[t], (k + 1) & 1, abort_flag)) {
+          umma_commit(&s_full[t]);
+        };
+        auto pv_mma = [&](int t, bool first) {  // O_t += P_t V of the stage in slot t
+          const uint32_t sv = smem_u32(smem + L::KV_OFF + t * L::STAGE + 2 * L::HALF);
+#pragma unroll
+          for (int kk = 0; kk < ATT_BN / 16; ++kk) {
+            umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8 + (kk >= 4 ? 32 : 0),
+                         sdesc_mn128(sv + kk * 2048, L::HALF), idesc_o,
+                         (!first || kk > 0) ? 1u : 0u);
+          }
+        };
+        auto next_kv = [&](int t) {
+          const bool got = mbar_wait(&kv_full[t], static_cast<uint32_t>(fk[t]) & 1u, abort_flag);
+          ++fk[t];
+          if (got) tc_fence_after();
+          return got;
+        };
+        for (int t = 0; ok && t < 2 && t < nst; ++t) {
+          ok = next_kv(t);
+          if (ok) s_mma(t);
+        }
+        for (int k = 0; ok && 2 * k < nst; ++k) {
+          for (int t = 0; t < 2 && ok; ++t) {
+            const int i = 2 * k + t;
+            if (i >= nst) break;
+            if (!mbar_wait(&p_full[t], static_cast<uint32_t>(pk[t]) & 1u, abort_flag)) {
               ok = false;
               break;
             }
+            ++pk[t];
             tc_fence_after();
-            s_mma(t);
+            pv_mma(t, k == 0);
+            umma_commit(&kv_empty[t]);
+            if (i + 2 < nst) {
+              ok = next_kv(t);
+              if (ok) s_mma(t);
+            }
           }
         }
+        if (!ok) break;
+        umma_commit(&q_empty[buf]);
+        umma_commit(o_done);
       }
-      umma_commit(o_done);
       umma_commit(drain);
       const uint64_t t0 = global_ns();
       while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 200000000ull) {
@@ -529,160 +576,177 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int row = quarter * 32 + static_cast<int>(lane);
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const float sl2 = p.scale_log2;
-    const uint32_t* rw = rwords + (row >> 6) * SOL_MAX_WORDS;  // this row's query block
-    float m_run[2] = {-INFINITY, -INFINITY};
-    float l_run[2] = {0.0f, 0.0f};
+    int sk[2] = {0, 0};  // stages seen per stream, over all items (barrier and buffer phases)
     bool ok = true;
-    // stage i (the k-th of stream t) for this warp's 64 keys: an exact block kb (or none) or
-    // centroids c0 .. c0 + 63; instantiated once per kind so each loop's body stays compact
-    auto stage = [&](const int i, const int t, const int k, auto kind) {
-      constexpr bool exact = decltype(kind)::value;
-      int kb = -1, nk = 0, c0 = 0;
-      if constexpr (exact) {
-        const int li = 2 * i + half;
-        kb = li < count ? slist[li] : -1;
-        nk = kb >= 0 ? min(SOL_BLOCK, p.tokens - kb * SOL_BLOCK) : 0;
-      } else {
-        c0 = (i - ns) * 128 + half * 64;
-      }
-      if (!mbar_wait(&s_full[t], k & 1, abort_flag)) {
-        ok = false;
-        return;
-      }
-      tc_fence_after();
-      const uint32_t s_col = tmem + lane_base + t * 128 + half * 64;
-      uint32_t sr[2][32];
-      tmem_ld32(s_col, sr[0]);
-      tmem_ld32(s_col + 32, sr[1]);
-      tmem_wait_ld();
-      // An exact block is all or nothing for a row: its logits are s * scale - m, folded into
-      // one packed FMA per pair with a per-row (scale, offset) = (sl2, -m), or (0, -inf) when
-      // the row does not route the block. Centroid logits carry a per-key bias (log2 of the
-      // block's length) or -inf; they are formed here, already scaled.
-      bool routed_row = true;
-      float mine;
-      if constexpr (exact) {
-        routed_row = kb >= 0 && ((rw[kb >> 5] >> (kb & 31)) & 1u);
-        if (nk < SOL_BLOCK) {  // the last, partial block (warp-uniform): finite sentinel
+    int j = 0;
+    for (int it = blockIdx.x; ok && it < items; it += gridDim.x, ++j) {
+      const int buf = j & 1;
+      const uint32_t use = static_cast<uint32_t>(j >> 1) & 1u;
+      const int head = it / p.ncta, cta = it % p.ncta;
+      const int row0 = cta * 128;
+      if (!mbar_wait(&meta_full[buf], use, abort_flag)) break;
+      const int count = mcount[buf];
+      const int* slist = slist_all + buf * 512;
+      const uint32_t* rw = rwords_all + buf * L::WORDS + (row >> 6) * SOL_MAX_WORDS;
+      const int ns = (count + 1) / 2;  // exact stages: two 64-key blocks each
+      const int nst = ns + ncent;      // then the centroid stages
+      float m_run[2] = {-INFINITY, -INFINITY};
+      float l_run[2] = {0.0f, 0.0f};
+      // stage i (the k-th of stream t in this item, g-th over all items) for this warp's 64 keys:
+      // an exact block kb (or none) or centroids c0 .. c0 + 63; instantiated once per kind so
+      // each loop's body stays compact
+      auto stage = [&](const int i, const int t, const int k, auto kind) {
+        constexpr bool exact = decltype(kind)::value;
+        const int g = sk[t]++;
+        int kb = -1, nk = 0, c0 = 0;
+        if constexpr (exact) {
+          const int li = 2 * i + half;
+          kb = li < count ? slist[li] : -1;
+          nk = kb >= 0 ? min(SOL_BLOCK, p.tokens - kb * SOL_BLOCK) : 0;
+        } else {
+          c0 = (i - ns) * 128 + half * 64;
+        }
+        if (!mbar_wait(&s_full[t], static_cast<uint32_t>(g) & 1u, abort_flag)) {
+          ok = false;
+          return;
+        }
+        tc_fence_after();
+        const uint32_t s_col = tmem + lane_base + t * 128 + half * 64;
+        uint32_t sr[2][32];
+        tmem_ld32(s_col, sr[0]);
+        tmem_ld32(s_col + 32, sr[1]);
+        tmem_wait_ld();
+        // An exact block is all or nothing for a row: its logits are s * scale - m, folded into
+        // one packed FMA per pair with a per-row (scale, offset) = (sl2, -m), or (0, -inf) when
+        // the row does not route the block. Centroid logits carry a per-key bias (log2 of the
+        // block's length) or -inf; they are formed here, already scaled.
+        bool routed_row = true;
+        float mine;
+        if constexpr (exact) {
+          routed_row = kb >= 0 && ((rw[kb >> 5] >> (kb & 31)) & 1u);
+          if (nk < SOL_BLOCK) {  // the last, partial block (warp-uniform): finite sentinel
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj)
+                if (c * 32 + jj >= nk) sr[c][jj] = __float_as_uint(-1.0e30f);
+          }
+        } else {
+          const int w0 = c0 >> 5;
+          const uint32_t words[2] = {w0 < p.words ? rw[w0] : ~0u,
+                                     w0 + 1 < p.words ? rw[w0 + 1] : ~0u};
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (c * 32 + j >= nk) sr[c][j] = __float_as_uint(-1.0e30f);
+            for (int jj = 0; jj < 32; ++jj) {
+              const int b = c0 + c * 32 + jj;
+              const float bias = b == p.nb - 1 ? p.last_log2 : 6.0f;
+              const bool take = b < p.nb && !((words[c] >> jj) & 1u);
+              sr[c][jj] = __float_as_uint(take ? fmaf(__uint_as_float(sr[c][jj]), sl2, bias)
+                                               : -INFINITY);
+            }
         }
-      } else {
-        const int w0 = c0 >> 5;
-        const uint32_t words[2] = {w0 < p.words ? rw[w0] : ~0u,
-                                   w0 + 1 < p.words ? rw[w0 + 1] : ~0u};
+        float mq[4];
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int b = c0 + c * 32 + j;
-            const float bias = b == p.nb - 1 ? p.last_log2 : 6.0f;
-            const bool take = b < p.nb && !((words[c] >> j) & 1u);
-            sr[c][j] = __float_as_uint(take ? fmaf(__uint_as_float(sr[c][j]), sl2, bias)
-                                            : -INFINITY);
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
+          float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+          a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
+          a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
+          a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
+          a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
+          a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
+          a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
+          mq[q] = fmaxf(a, __uint_as_float(v[15]));
+        }
+        const float raw = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+        if constexpr (exact)
+          mine = routed_row ? raw * sl2 : -INFINITY;
+        else
+          mine = raw;
+        float* xm = xmax + (t * 2 + (g & 1)) * 256;
+        xm[half * 128 + row] = mine;
+        uint64_t* xb = &xbar[(quarter * 2 + t) * 2 + (g & 1)];
+        mbar_arrive(xb);
+        if (!mbar_wait(xb, static_cast<uint32_t>(g >> 1) & 1u, abort_flag)) {
+          ok = false;
+          return;
+        }
+        const float m_blk = fmaxf(mine, xm[(1 - half) * 128 + row]);
+        float alpha = 1.0f;
+        bool rescale = false;
+        if (k > 0) {
+          const bool need = m_blk > m_run[t] + 8.0f;
+          rescale = __any_sync(0xffffffffu, need);
+          if (need) {
+            alpha = ex2_approx(m_run[t] - m_blk);  // 0 while the row had no logit yet
+            m_run[t] = m_blk;
+            l_run[t] *= alpha;
           }
-      }
-      float mq[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t* v = sr[q >> 1] + (q & 1) * 16;
-        float a = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
-        a = max3f(a, __uint_as_float(v[3]), __uint_as_float(v[4]));
-        a = max3f(a, __uint_as_float(v[5]), __uint_as_float(v[6]));
-        a = max3f(a, __uint_as_float(v[7]), __uint_as_float(v[8]));
-        a = max3f(a, __uint_as_float(v[9]), __uint_as_float(v[10]));
-        a = max3f(a, __uint_as_float(v[11]), __uint_as_float(v[12]));
-        a = max3f(a, __uint_as_float(v[13]), __uint_as_float(v[14]));
-        mq[q] = fmaxf(a, __uint_as_float(v[15]));
-      }
-      const float raw = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      if constexpr (exact)
-        mine = routed_row ? raw * sl2 : -INFINITY;
-      else
-        mine = raw;
-      float* xm = xmax + (t * 2 + (k & 1)) * 256;
-      xm[half * 128 + row] = mine;
-      uint64_t* xb = &xbar[(quarter * 2 + t) * 2 + (k & 1)];
-      mbar_arrive(xb);
-      if (!mbar_wait(xb, (k >> 1) & 1, abort_flag)) {
-        ok = false;
-        return;
-      }
-      const float m_blk = fmaxf(mine, xm[(1 - half) * 128 + row]);
-      float alpha = 1.0f;
-      bool rescale = false;
-      if (k > 0) {
-        const bool need = m_blk > m_run[t] + 8.0f;
-        rescale = __any_sync(0xffffffffu, need);
-        if (need) {
-          alpha = ex2_approx(m_run[t] - m_blk);  // 0 while the row had no logit yet
+        } else {
           m_run[t] = m_blk;
-          l_run[t] *= alpha;
         }
-      } else {
-        m_run[t] = m_blk;
-      }
-      // a row with no logit so far subtracts 0: its exponentials are all 0 (or 2^-126)
-      const float msub = m_run[t] == -INFINITY ? 0.0f : m_run[t];
-      const float scl = exact ? (routed_row ? sl2 : 0.0f) : 1.0f;
-      const float off = (exact && !routed_row) ? -INFINITY : -msub;
-      const uint64_t sc2 = f2_pack(scl, scl);
-      const uint64_t negm = f2_pack(off, off);
-      uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+        // a row with no logit so far subtracts 0: its exponentials are all 0 (or 2^-126)
+        const float msub = m_run[t] == -INFINITY ? 0.0f : m_run[t];
+        const float scl = exact ? (routed_row ? sl2 : 0.0f) : 1.0f;
+        const float off = (exact && !routed_row) ? -INFINITY : -msub;
+        const uint64_t sc2 = f2_pack(scl, scl);
+        const uint64_t negm = f2_pack(off, off);
+        uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
 #pragma unroll
-      for (int q8 = 0; q8 < 4; ++q8) {
-        uint32_t packed[8];
+        for (int q8 = 0; q8 < 4; ++q8) {
+          uint32_t packed[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int j = q8 * 8 + u;
-          const uint32_t* v = sr[j >> 4];
-          const int e = (2 * j) & 31;
-          const uint64_t xs =
-              f2_fma(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2, negm);
-          uint64_t ev;
-          if ((ATT_EMU_MASK >> (j & 7)) & 1) {
-            ev = exp2_poly_x2(xs);
-          } else {
-            const float2 xv = f2_unpack(xs);
-            ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
+          for (int u = 0; u < 8; ++u) {
+            const int jj = q8 * 8 + u;
+            const uint32_t* v = sr[jj >> 4];
+            const int e = (2 * jj) & 31;
+            const uint64_t xs =
+                f2_fma(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2, negm);
+            uint64_t ev;
+            if ((ATT_EMU_MASK >> (jj & 7)) & 1) {
+              ev = exp2_poly_x2(xs);
+            } else {
+              const float2 xv = f2_unpack(xs);
+              ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
+            }
+            lsum2[u & 1] = f2_add(lsum2[u & 1], ev);
+            const float2 e2 = f2_unpack(ev);
+            packed[u] = pack_f16x2(e2.x, e2.y);
           }
-          lsum2[u & 1] = f2_add(lsum2[u & 1], ev);
-          const float2 e2 = f2_unpack(ev);
-          packed[u] = pack_f16x2(e2.x, e2.y);
+          tmem_st8(s_col + q8 * 8, packed);
         }
-        tmem_st8(s_col + q8 * 8, packed);
-      }
-      const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
-      l_run[t] += ls.x + ls.y;
-      if (rescale) {
-        const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * (D / 2);
+        const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
+        l_run[t] += ls.x + ls.y;
+        if (rescale) {
+          const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * (D / 2);
 #pragma unroll 1
-        for (int c = 0; c < D / 64; ++c) {
-          uint32_t o[32];
-          tmem_ld32(o_col + c * 32, o);
-          tmem_wait_ld();
+          for (int c = 0; c < D / 64; ++c) {
+            uint32_t o[32];
+            tmem_ld32(o_col + c * 32, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
-          tmem_st32(o_col + c * 32, o);
+            for (int jj = 0; jj < 32; ++jj) o[jj] = __float_as_uint(__uint_as_float(o[jj]) * alpha);
+            tmem_st32(o_col + c * 32, o);
+          }
         }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
-    };
-    // the exact stages, then the centroid stages, each alternating between the streams
-    for (int i = 0; i < ns && ok; ++i) stage(i, i & 1, i >> 1, std::true_type{});
-    for (int i = ns; i < nst && ok; ++i) stage(i, i & 1, i >> 1, std::false_type{});
-    if (ok && nst > 0) {
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[t]);
+      };
+      // the exact stages, then the centroid stages, each alternating between the streams
+      for (int i = 0; i < ns && ok; ++i) stage(i, i & 1, i >> 1, std::true_type{});
+      for (int i = ns; i < nst && ok; ++i) stage(i, i & 1, i >> 1, std::false_type{});
+      if (!ok) break;
+      if (lane == 0) mbar_arrive(&meta_empty[buf]);  // done with the item's words and list
       for (int t = 0; t < 2; ++t) xsum[(t * 2 + half) * 128 + row] = l_run[t];
       mbar_arrive(&lbar[quarter]);
-      ok = mbar_wait(&lbar[quarter], 0, abort_flag);
-    }
-    if (ok && nst > 0 && mbar_wait(o_done, 0, abort_flag)) {
+      if (!mbar_wait(&lbar[quarter], static_cast<uint32_t>(j) & 1u, abort_flag) ||
+          !mbar_wait(o_done, static_cast<uint32_t>(j) & 1u, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const int tok = row0 + row;
       bool store = tok < p.tokens;
