@@ -6,8 +6,10 @@
   (kinomlx/models/flux2/sampling.py:264-280 combines the branches as `u + g * (p - u)`) and both
   apply the same Euler update.
 - VAE tile scatter (config 5): the spatial tiles go round-robin to the ranks; each rank blends its
-  tiles into a full-size fp32 canvas and the canvases and weight maps are summed by one NCCL
-  all-reduce before the normalisation (kinomlx/models/ltx2/video_vae/tiling.py:1310-1369).
+  tiles into a full-size fp32 canvas and the canvases and weight maps are summed before the
+  normalisation (kinomlx/models/ltx2/video_vae/tiling.py:1310-1369): onto one owner rank (an
+  NCCL reduce, half the bytes an all-reduce moves) when only that rank needs the video, or onto
+  every rank (all-reduce).
 """
 
 from __future__ import annotations
@@ -56,9 +58,27 @@ def cfg_split_step(model, prepared, current: torch.Tensor, sigmas: torch.Tensor,
     return ops.euler_velocity(current, combined, step_delta(sigmas, index), out=current)
 
 
+def combine_canvases(canvas: torch.Tensor, weights: torch.Tensor, *, group=None,
+                     dst: int | None = None) -> bool:
+    """Sum every rank's blended canvas and weight map: onto rank `dst` of `group` (NCCL reduce),
+    or, with `dst` None, onto every rank (all-reduce). Returns whether this rank holds the sums."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return True
+    if dst is None:
+        dist.all_reduce(canvas, group=group)
+        dist.all_reduce(weights, group=group)
+        return True
+    root = dist.get_global_rank(group, dst) if group is not None else dst
+    dist.reduce(canvas, root, group=group)
+    dist.reduce(weights, root, group=group)
+    return dist.get_rank(group) == dst
+
+
 def decode_tiles_distributed(decoder, latent: torch.Tensor, *, tile: int = 8, overlap: int = 2,
-                             group=None) -> torch.Tensor:
-    """Tiled VAE decode with the tiles spread round-robin over the ranks of `group`."""
+                             group=None, dst: int | None = None) -> torch.Tensor | None:
+    """Tiled VAE decode with the tiles spread round-robin over the ranks of `group`. With `dst`
+    the decoded video is assembled on that rank only (the others return None); without it, on
+    every rank."""
     from .ltx2.video_vae import tile_plan
 
     world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -77,7 +97,6 @@ def decode_tiles_distributed(decoder, latent: torch.Tensor, *, tile: int = 8, ov
     if mine:
         decoder.decode_tiled(latent, tile=tile, overlap=overlap, tiles=mine,
                              canvas=canvas, weights=weights)
-    if world > 1:
-        dist.all_reduce(canvas, group=group)
-        dist.all_reduce(weights, group=group)
+    if not combine_canvases(canvas, weights, group=group, dst=dst):
+        return None
     return ops.blend_normalize(canvas, weights)

@@ -210,3 +210,44 @@ def test_gloo_ranks_cfg_split_with_ulysses_branches(size):
         assert branch == (0 if rank < half else 1) and sp_size == half
         assert pair == [rank % half, rank % half + half]
         assert torch.equal(torch.tensor(full).to(torch.bfloat16), expect)
+
+
+def _canvas_worker(rank: int, size: int, port: int, queue) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), WORLD_SIZE=str(size),
+                      RANK=str(rank), LOCAL_RANK=str(rank))
+    import torch
+
+    from kinomlx_b200 import dist
+    from kinomlx_b200.multi_gpu import combine_canvases
+
+    dist.init("gloo", timeout_s=30)
+    out = {}
+    for dst in (None, 1):
+        canvas = torch.full((1, 3, 2, 4, 5), float(rank + 1))
+        weights = torch.full((4, 5), 0.5 * (rank + 1))
+        holds = combine_canvases(canvas, weights, dst=dst)
+        out[dst] = (holds, float(canvas.max()) if holds else None, float(weights.max()) if holds else None)
+    import torch.distributed as tdist
+
+    tdist.destroy_process_group()
+    queue.put((rank, out))
+
+
+def test_gloo_ranks_combine_tile_canvases():
+    """The VAE tile canvases: summed onto every rank (all-reduce) or onto one owner rank
+    (reduce), which alone reports that it holds the sums."""
+    size = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_canvas_worker, args=(r, size, port, queue)) for r in range(size)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in range(size))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank in range(size):
+        assert results[rank][None] == (True, 3.0, 1.5)
+    assert results[1][1] == (True, 3.0, 1.5)
+    assert results[0][1] == (False, None, None)

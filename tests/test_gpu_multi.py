@@ -123,11 +123,13 @@ def _worker(rank: int, size: int, port: int, case: str, queue) -> None:
         for i in range(3):
             cfg_split_step(model, prepared, current, sig, i, 4.0, cfg)
         out = cfg.sp.all_gather_tokens(current)
-    elif case == "vae":
+    elif case in ("vae", "vae_root"):
         from kinomlx_b200.multi_gpu import decode_tiles_distributed
 
         dec, latent = _vae_case(device)
-        out = decode_tiles_distributed(dec, latent, tile=4, overlap=1)
+        # vae_root: the video assembled on rank 1 only (NCCL reduce); rank 0 returns None
+        out = decode_tiles_distributed(dec, latent, tile=4, overlap=1,
+                                       dst=1 if case == "vae_root" else None)
     else:
         sp = SequenceParallel(peer=case.endswith("_peer"))
         out = _run(case.removesuffix("_peer"), device, sp)
@@ -137,15 +139,16 @@ def _worker(rank: int, size: int, port: int, case: str, queue) -> None:
     import torch.distributed as tdist
 
     tdist.destroy_process_group()
-    queue.put((rank, out.float().cpu().numpy().tolist()))
+    queue.put((rank, None if out is None else out.float().cpu().numpy().tolist()))
 
 
-@pytest.mark.parametrize("case", ["flux", "ltx", "flux_peer", "ltx_peer", "cfg", "vae"])
+@pytest.mark.parametrize("case", ["flux", "ltx", "flux_peer", "ltx_peer", "cfg", "vae", "vae_root"])
 def test_two_gpus_match_one_gpu(cuda_device, case):
     """flux/ltx: Ulysses over 2 ranks through NCCL all-to-alls; *_peer: the same through the
     peer transport (projection epilogues and attention store into the other GPU's buffers over
     NVLink, device barriers); cfg: conditional and unconditional branch on different GPUs with
-    the velocity exchange; vae: tiles split over 2 ranks, canvases all-reduced."""
+    the velocity exchange; vae: tiles split over 2 ranks, canvases all-reduced; vae_root: the
+    canvases reduced onto rank 1 only."""
     size, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
@@ -156,8 +159,11 @@ def test_two_gpus_match_one_gpu(cuda_device, case):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    expect = _run(case.removesuffix("_peer"), cuda_device).float().cpu()
+    expect = _run(case.removesuffix("_peer").removesuffix("_root"), cuda_device).float().cpu()
     for r in range(size):
+        if case == "vae_root" and r == 0:
+            assert results[r] is None
+            continue
         got = torch.tensor(results[r])
         cos = float(torch.nn.functional.cosine_similarity(got.flatten(), expect.flatten(), dim=0))
         max_rel = float((got - expect).abs().max() / expect.abs().max())
