@@ -726,6 +726,9 @@ def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | N
     elif case == "packed_block":
         run_packed_block(dev)
         return
+    elif case == "neighborhood":
+        run_neighborhood_case(dev)
+        return
     elif case == "f32":
         # fp32 parity mode at config 1: the image stream's FF up projection (1024 x 12288 x 3072,
         # GELU epilogue) and the joint attention over 1536 tokens x 24 heads
@@ -807,6 +810,37 @@ def run_av_step(dev: torch.device) -> None:
                       "video_tokens": f * h * w, "audio_tokens": ta,
                       "video_only_step_tflop": round(ltx_step_flops() / 1e12, 1),
                       "kernels": _kernel_shares(step)}))
+
+
+def run_neighborhood_case(dev: torch.device) -> None:
+    """The LTX-2.5 diffusion decoder's neighborhood attention at its final-stage call (121 x 112 x
+    192 queries, four 64-wide heads, 11 x 11 x 11 windows: the call the reference documents at
+    632 ms on an M1 Max, kinomlx/models/ltx2/kernels/neighborhood_attention.py:21-25) and the
+    3 x 7 x 7 and 3 x 5 x 5 windows on the same grid. Algorithmic work: 4 x 64 FLOP per (query,
+    window key) pair; the MMAs also score the keys of each query tile's window union that lie
+    outside a query's window."""
+    from kinomlx_b200 import ops
+
+    grid, heads = (121, 112, 192), 4
+    shape = (1, *grid, heads, 64)
+    g = torch.Generator(device=dev).manual_seed(5)
+    q = (torch.randn(shape, generator=g, device=dev) * 0.125).half()
+    k = torch.randn(shape, generator=g, device=dev).half()
+    v = torch.randn(shape, generator=g, device=dev).half()
+    out = torch.empty_like(q)
+    tokens = grid[0] * grid[1] * grid[2]
+    rows = []
+    for window in ((11, 11, 11), (3, 7, 7), (3, 5, 5)):
+        ms = _time(lambda: ops.neighborhood_attention(q, k, v, window=window, out=out), 3, 10, 1)
+        keys = window[0] * window[1] * window[2]
+        flop = 4.0 * 64 * tokens * heads * keys
+        rows.append({"window": list(window), "ms": round(ms, 3),
+                     "algorithmic_tflop": round(flop / 1e12, 3),
+                     "tflops": round(flop / (ms * 1e9), 1)})
+    ops.device_status()
+    print(json.dumps({"kernel_case": "neighborhood", "ok": True, "grid": list(grid),
+                      "heads": heads, "calls": rows,
+                      "reference_m1_max_ms_final_stage": 632.0}))
 
 
 def run_packed_block(dev: torch.device) -> None:
@@ -1116,7 +1150,7 @@ def main() -> None:
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
     ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow", "sol", "sol_step",
-                                              "packed_block", "bandwidth", "f32", "av_step", "kv_step"],
+                                              "packed_block", "neighborhood", "bandwidth", "f32", "av_step", "kv_step"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     ap.add_argument("--sol-tau", type=float, help="--kernel-case sol: this tau only")
     ap.add_argument("--sol-inputs", choices=["iid", "smooth", "smooth_rope"],

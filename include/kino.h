@@ -33,7 +33,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (11); bumped on any signature change or addition. */
+/* ABI version of this header (12); bumped on any signature change or addition. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -235,6 +235,20 @@ int64_t kino_sol_attention_workspace_size(int64_t tokens, int64_t heads);
  * kinomlx.models.ltx2.kernels.sol_attention.sol_attention
  * (kinomlx/models/ltx2/kernels/sol_attention.py:219-272, route_blocks :181-216). */
 kino_status kino_sol_attention(const kino_sol_attention_args* args, void* stream);
+
+/* ------------------------------------------------------------------ neighborhood attention */
+/* Exact 3-D neighborhood attention of the LTX-2.5 diffusion video decoder: q, k, v and out are
+ * contiguous (batch, frames, height, width, heads, 64) fp16, the queries already scaled; every
+ * query attends to the window[0] x window[1] x window[2] keys around it, each window shifted
+ * inward to stay whole at the grid's edges (on an axis of length L the window of position i
+ * starts at clamp(i - K / 2, 0, L - K)); fp32 scores and softmax, the output rounded to fp16.
+ * Windows odd and no larger than the grid. Replaces
+ * kinomlx.models.ltx2.kernels.neighborhood_attention.neighborhood_attention
+ * (kinomlx/models/ltx2/kernels/neighborhood_attention.py:170-221). */
+kino_status kino_neighborhood_attention(const void* q, const void* k, const void* v, void* out,
+                                        int64_t batch, int64_t frames, int64_t height,
+                                        int64_t width, int64_t heads, const int32_t* window,
+                                        void* stream);
 
 /* ------------------------------------------------------------------ norms and rotary */
 #define KINO_NORM_RMS 0

@@ -264,6 +264,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_dense_attention": (c_int, [P, P, P, P, I64, I64, I64, I64, P]),
     "kino_sol_attention_workspace_size": (I64, [I64, I64]),
     "kino_sol_attention": (c_int, [POINTER(SolAttentionArgs), P]),
+    "kino_neighborhood_attention": (c_int, [P, P, P, P, I64, I64, I64, I64, I64, P, P]),
     "kino_adaln": (c_int, [P, I64, I64, P, P, I64, P, I64, I64, I64, I64, I64, c_int, F, P]),
     "kino_rms_norm": (c_int, [P, P, P, I64, I64, F, F, P]),
     "kino_qk_norm_rope": (

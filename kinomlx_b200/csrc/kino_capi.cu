@@ -16,6 +16,7 @@
 #include "kino_ops.cuh"
 #include "kino_peer.cuh"
 #include "kino_sol.cuh"
+#include "kino_na.cuh"
 #include "kino_vae.cuh"
 #include "kino_quant.cuh"
 #include "kino_f32.cuh"
@@ -529,7 +530,7 @@ SolLayout sol_layout(int64_t tokens, int64_t heads) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 11; }
+int kino_abi_version(void) { return 12; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -938,6 +939,61 @@ kino_status kino_sol_attention(const kino_sol_attention_args* a, void* stream) {
   launch_pdl(kino::sol_attention_kernel, dim3(persistent),
              dim3(kino::ATT_THREADS), smem, st, mq, mk, mv, mkc, mvc, p);
   return check_launch("kino_sol_attention");
+}
+
+kino_status kino_neighborhood_attention(const void* q, const void* k, const void* v, void* out,
+                                        int64_t batch, int64_t frames, int64_t height,
+                                        int64_t width, int64_t heads, const int32_t* window,
+                                        void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || window == nullptr)
+    return fail(KINO_EINVAL, "kino_neighborhood_attention: null argument");
+  if (batch < 1 || frames < 1 || height < 1 || width < 1 || heads < 1 || heads > 4096 ||
+      batch * frames > 0x7fffffff || height > 0x7fffffff || width > 0x7fffffff)
+    return fail(KINO_EINVAL, "kino_neighborhood_attention: empty or oversized grid");
+  const int64_t ext[3] = {frames, height, width};
+  for (int a = 0; a < 3; ++a)
+    if (window[a] < 1 || window[a] % 2 == 0 || window[a] > ext[a])
+      return fail(KINO_EINVAL, "kino_neighborhood_attention: window %d on axis %d must be odd "
+                  "and no larger than the grid (%lld)", window[a], a, (long long)ext[a]);
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(KINO_EINVAL, "kino_neighborhood_attention: operands must be 16-byte aligned");
+  kino::NaParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.batch = static_cast<int>(batch);
+  p.frames = static_cast<int>(frames);
+  p.height = static_cast<int>(height);
+  p.width = static_cast<int>(width);
+  p.heads = static_cast<int>(heads);
+  p.kt = window[0];
+  p.kh = window[1];
+  p.kw = window[2];
+  p.boxes_t = static_cast<int>((frames + kino::NA_QT - 1) / kino::NA_QT);
+  p.boxes_h = static_cast<int>((height + kino::NA_QH - 1) / kino::NA_QH);
+  p.boxes_w = static_cast<int>((width + kino::NA_QW - 1) / kino::NA_QW);
+  p.scale_log2 = 1.4426950408889634f;  // the queries arrive scaled: softmax(q k^T)
+  p.out = static_cast<__half*>(out);
+  const int64_t items = batch * heads * p.boxes_t * p.boxes_h * p.boxes_w;
+  if (items > 0x7fffffff)
+    return fail(KINO_ENOTSUPPORTED, "kino_neighborhood_attention: too many query tiles");
+  // (head dim, head, width, height, batch * frames), strides in elements
+  const uint64_t dims[5] = {64, static_cast<uint64_t>(heads), static_cast<uint64_t>(width),
+                            static_cast<uint64_t>(height), static_cast<uint64_t>(batch * frames)};
+  const uint64_t strides[4] = {64, static_cast<uint64_t>(heads * 64),
+                               static_cast<uint64_t>(width * heads * 64),
+                               static_cast<uint64_t>(height * width * heads * 64)};
+  const uint32_t qbox[5] = {64, 1, kino::NA_QW, kino::NA_QH, kino::NA_TILE_T};  // one tile
+  const uint32_t kbox[5] = {64, 1, kino::NA_KW, kino::NA_KH, 1};
+  CUtensorMap mq, mk, mv;
+  kino_status s;
+  if ((s = make_map(&mq, q, 5, dims, strides, qbox)) != KINO_OK) return s;
+  if ((s = make_map(&mk, k, 5, dims, strides, kbox)) != KINO_OK) return s;
+  if ((s = make_map(&mv, v, 5, dims, strides, kbox)) != KINO_OK) return s;
+  constexpr int smem = kino::NaSmem::TOTAL;
+  if ((s = ensure_smem(kino::na_attention_kernel, smem, 22)) != KINO_OK) return s;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(items, device_sms()));
+  launch_pdl(kino::na_attention_kernel, dim3(grid), dim3(kino::ATT_THREADS), smem,
+             static_cast<cudaStream_t>(stream), mq, mk, mv, p);
+  return check_launch("kino_neighborhood_attention");
 }
 
 kino_status kino_dense_attention(const void* q, const void* k, const void* v, void* out,

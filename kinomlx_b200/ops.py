@@ -477,6 +477,37 @@ def attention(
     return out
 
 
+def neighborhood_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+                           window: tuple[int, int, int],
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """Exact 3-D neighborhood attention: q, k, v contiguous (batch, T, H, W, heads, 64) fp16 on
+    the GPU, the queries already scaled; each query attends to the window's keys around it, the
+    window shifted inward at the grid's edges. Any odd window no larger than the grid."""
+    for t, name in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t, name, torch.float16)
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if q.dim() != 6 or q.shape[-1] != 64 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("neighborhood attention takes matching (batch, T, H, W, heads, 64) operands")
+    if len(window) != 3:
+        raise ValueError("the window has three sizes (frames, height, width)")
+    if out is None:
+        out = torch.empty_like(q)
+    _need(out, "out", torch.float16)
+    if out.shape != q.shape or not out.is_contiguous():
+        raise ValueError("out must be contiguous and shaped like q")
+    b, gt, gh, gw, heads, dim = q.shape
+    win = (ctypes.c_int32 * 3)(*(int(x) for x in window))
+    keys = 1
+    for x in window:
+        keys *= int(x)
+    with _timed("neighborhood_attention", 4.0 * b * gt * gh * gw * heads * keys * dim,
+                4.0 * q.numel() * 2):
+        _lib.call("kino_neighborhood_attention", _ptr(q), _ptr(k), _ptr(v), _ptr(out), b, gt, gh,
+                  gw, heads, ctypes.cast(win, ctypes.c_void_p), _stream())
+    return out
+
+
 _SOL_WORKSPACES: dict[tuple, torch.Tensor] = {}
 
 
