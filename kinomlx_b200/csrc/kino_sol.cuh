@@ -692,32 +692,40 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const float off = (exact && !routed_row) ? -INFINITY : -msub;
         const uint64_t sc2 = f2_pack(scl, scl);
         const uint64_t negm = f2_pack(off, off);
-        uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+        // an exact block is routed or not for a whole warp (its 32 rows lie in one query block):
+        // a warp that does not route it writes P = 0 without exponentials
+        if (!exact || routed_row) {
+          uint64_t lsum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
 #pragma unroll
-        for (int q8 = 0; q8 < 4; ++q8) {
-          uint32_t packed[8];
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint32_t packed[8];
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int jj = q8 * 8 + u;
-            const uint32_t* v = sr[jj >> 4];
-            const int e = (2 * jj) & 31;
-            const uint64_t xs =
-                f2_fma(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2, negm);
-            uint64_t ev;
-            if ((ATT_EMU_MASK >> (jj & 7)) & 1) {
-              ev = exp2_poly_x2(xs);
-            } else {
-              const float2 xv = f2_unpack(xs);
-              ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
+            for (int u = 0; u < 8; ++u) {
+              const int jj = q8 * 8 + u;
+              const uint32_t* v = sr[jj >> 4];
+              const int e = (2 * jj) & 31;
+              const uint64_t xs =
+                  f2_fma(f2_pack(__uint_as_float(v[e]), __uint_as_float(v[e + 1])), sc2, negm);
+              uint64_t ev;
+              if ((ATT_EMU_MASK >> (jj & 7)) & 1) {
+                ev = exp2_poly_x2(xs);
+              } else {
+                const float2 xv = f2_unpack(xs);
+                ev = f2_pack(ex2_approx(xv.x), ex2_approx(xv.y));
+              }
+              lsum2[u & 1] = f2_add(lsum2[u & 1], ev);
+              const float2 e2 = f2_unpack(ev);
+              packed[u] = pack_f16x2(e2.x, e2.y);
             }
-            lsum2[u & 1] = f2_add(lsum2[u & 1], ev);
-            const float2 e2 = f2_unpack(ev);
-            packed[u] = pack_f16x2(e2.x, e2.y);
+            tmem_st8(s_col + q8 * 8, packed);
           }
-          tmem_st8(s_col + q8 * 8, packed);
+          const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
+          l_run[t] += ls.x + ls.y;
+        } else {
+          const uint32_t zeros[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) tmem_st8(s_col + q8 * 8, zeros);
         }
-        const float2 ls = f2_unpack(f2_add(lsum2[0], lsum2[1]));
-        l_run[t] += ls.x + ls.y;
         if (rescale) {
           const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * (D / 2);
 #pragma unroll 1
