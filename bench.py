@@ -708,6 +708,13 @@ def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | N
         bias = normal((256,), seed=9, device=dev)
         for _ in range(3):
             ops.conv3d(x, w, bias, causal=True)
+        ms = _time(lambda: ops.conv3d(x, w, bias, causal=True), 0, 10, 1)
+        flop = 2.0 * 25 * 96 * 128 * 256 * 27 * 256
+        torch.cuda.synchronize()
+        ops.device_status()
+        print(json.dumps({"kernel_case": case, "ok": True, "ms": round(ms, 4),
+                          "tflops": round(flop / (ms * 1e9), 1)}))
+        return
     elif case == "bandwidth":
         run_bandwidth_case(dev)
         return
@@ -769,6 +776,13 @@ def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | N
         stats = ops.conv_stats_buffer(dev)
         for _ in range(3):
             ops.conv3d(x, w, bias, causal=True, residual=res, stats=stats)
+        ms = _time(lambda: ops.conv3d(x, w, bias, causal=True, residual=res, stats=stats), 0, 10, 1)
+        flop = 2.0 * 49 * 96 * 128 * 128 * 27 * 128
+        torch.cuda.synchronize()
+        ops.device_status()
+        print(json.dumps({"kernel_case": case, "ok": True, "ms": round(ms, 4),
+                          "tflops": round(flop / (ms * 1e9), 1)}))
+        return
     torch.cuda.synchronize()
     ops.device_status()
     print(json.dumps({"kernel_case": case, "ok": True}))

@@ -282,16 +282,18 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   return check_launch("kino_conv3d");
 }
 
-template <int BN, int STAGES, int KSUB>
+template <int BN, int STAGES, int KSUB, bool HALO = false>
 kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0,
                             cudaStream_t stream, int slot) {
-  using L = kino::ConvPairSmem<BN, STAGES, KSUB>;
+  using L = kino::ConvPairSmem<BN, STAGES, KSUB, HALO>;
   CUtensorMap mx, mw;
   const uint64_t dx[4] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W),
                           static_cast<uint64_t>(s0.H), static_cast<uint64_t>(s0.F)};
   const uint64_t sx[3] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W) * s0.Cin,
                           static_cast<uint64_t>(s0.H) * s0.W * s0.Cin};
-  const uint32_t bx[4] = {64, static_cast<uint32_t>(s0.tw), static_cast<uint32_t>(s0.th), 1};
+  // HALO: one 128-voxel row plus a voxel on each side per load
+  const uint32_t bx[4] = {64, static_cast<uint32_t>(HALO ? kino::CONV_HALO_ROWS : s0.tw),
+                          static_cast<uint32_t>(s0.th), 1};
   kino_status st = make_map(&mx, a->x, 4, dx, sx, bx);
   if (st != KINO_OK) return st;
   const uint64_t k = 27ull * s0.Cin;
@@ -306,7 +308,7 @@ kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0
   s.num_tiles = s.tiles_m * s.tiles_n;
   s.splits = 1;
   s.kper = s.kblocks;
-  auto kernel = kino::conv3d_2sm_kernel<BN, STAGES, KSUB>;
+  auto kernel = kino::conv3d_2sm_kernel<BN, STAGES, KSUB, HALO>;
   st = ensure_smem(kernel, L::TOTAL, slot);
   if (st != KINO_OK) return st;
   const int max_pairs = device_sms() / 2;
@@ -1289,6 +1291,9 @@ kino_status kino_timestep_embedding(const float* t, void* out, int64_t batch, in
 #ifndef KINO_CONV_CTA_PAIRS
 #define KINO_CONV_CTA_PAIRS 1
 #endif
+#ifndef KINO_CONV_HALO
+#define KINO_CONV_HALO 1  // CTA-pair convs on W >= 128: one input row per (kt, kh) for three taps
+#endif
 #ifndef KINO_CONV_NARROW_STAGES
 #define KINO_CONV_NARROW_STAGES 2
 #endif
@@ -1365,15 +1370,40 @@ kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
   const int64_t pair_tiles = ((s.boxes + 1) / 2) * ((s.N + 255) / 256);
   const int64_t narrow_pair_tiles = ((s.boxes + 1) / 2) * ((s.N + 127) / 128);
   if (a->out_channels <= 128) {
-    if (KINO_CONV_CTA_PAIRS && gemm_pairs_enabled() && narrow_pair_tiles >= device_sms() / 2)
+    if (KINO_CONV_CTA_PAIRS && gemm_pairs_enabled() && narrow_pair_tiles >= device_sms() / 2) {
+      if (KINO_CONV_HALO && s.W >= 128) {
+        // boxes of one 128-voxel row: each input row (with its halo) serves the three kw taps
+        kino::ConvShape r = s;
+        r.tw = 128;
+        r.th = 1;
+        r.tf = 1;
+        r.fb = r.F;
+        r.hb = r.H;
+        r.wb = (r.W + 127) / 128;
+        r.boxes = r.fb * r.hb * r.wb;
+        return launch_conv_2sm<128, 2, 2, true>(a, r, strm, 23);
+      }
       return launch_conv_2sm<128, KINO_CONV_NARROW_STAGES, KINO_CONV_NARROW_KSUB>(a, s, strm, 8);
+    }
     // narrow outputs: two boxes per tile share the weight block when that still fills the GPU
     if (KINO_CONV_PAIR_BOXES && s.boxes >= 2 * device_sms())
       return launch_conv<128, 4, 2>(a, s, strm, 7);
     return launch_conv<128, 6, 1>(a, s, strm, 4);
   }
-  if (KINO_CONV_CTA_PAIRS && gemm_pairs_enabled() && pair_tiles >= device_sms() / 2)
+  if (KINO_CONV_CTA_PAIRS && gemm_pairs_enabled() && pair_tiles >= device_sms() / 2) {
+    if (KINO_CONV_HALO && s.W >= 128) {
+      kino::ConvShape r = s;  // as for 128 channels: one 128-voxel row per box
+      r.tw = 128;
+      r.th = 1;
+      r.tf = 1;
+      r.fb = r.F;
+      r.hb = r.H;
+      r.wb = (r.W + 127) / 128;
+      r.boxes = r.fb * r.hb * r.wb;
+      return launch_conv_2sm<256, 3, 1, true>(a, r, strm, 24);
+    }
     return launch_conv_2sm<256, KINO_CONV_WIDE_STAGES, KINO_CONV_WIDE_KSUB>(a, s, strm, 9);
+  }
   return launch_conv<256, 4, 1>(a, s, strm, 5);
 }
 

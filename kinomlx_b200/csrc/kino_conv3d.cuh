@@ -467,11 +467,22 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 // A stage holds KSUB consecutive K blocks (each: this CTA's box and its half of the weight
 // rows), so that one barrier round trip covers KSUB x 4 MMAs: with BN = 128 an MMA is only 64
 // tensor cycles and the per-stage wait would otherwise show between the groups.
-template <int BN, int STAGES, int KSUB>
+// HALO: the box is one 128-voxel row (tw = 128) and a K sub-block is one (kt, kh, channel block)
+// triple: its input row is loaded once with a one-voxel halo on each side (130 rows) and serves
+// the three kw taps as A operands starting 0, 1 and 2 rows in, each with its own weight block.
+// The 128-byte swizzle is a function of the absolute shared-memory address (measured: the MMA
+// reads the TMA's swizzled rows correctly from a start 1 or 2 rows into a 1024-byte atom with the
+// descriptor's base-offset field left at 0, and wrongly with it set to the row phase), so the
+// shifted operands are plain descriptors of the shifted addresses.
+constexpr int CONV_HALO_ROWS = GEMM_BM + 2;
+template <int BN, int STAGES, int KSUB, bool HALO = false>
 struct ConvPairSmem {
-  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;      // 16 KB: this CTA's box
-  static constexpr int B_BYTES = (BN / 2) * GEMM_BK * 2;     // this CTA's half of the weights
+  static constexpr int A_BYTES = HALO ? 17 * 1024 : GEMM_BM * GEMM_BK * 2;  // this CTA's box
+  static constexpr int B1_BYTES = (BN / 2) * GEMM_BK * 2;  // this CTA's half of one tap's weights
+  static constexpr int B_BYTES = (HALO ? 3 : 1) * B1_BYTES;
   static constexpr int SUB_BYTES = A_BYTES + B_BYTES;
+  // bytes the TMA delivers per sub-block (the halo row is 130 rows of 128 bytes)
+  static constexpr int TX_BYTES = (HALO ? CONV_HALO_ROWS * 128 : A_BYTES) + B_BYTES;
   static constexpr int STAGE_BYTES = KSUB * SUB_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int XCH_BYTES = 4 * 32 * 3 * 4;  // GroupNorm statistics handed between halves
@@ -479,12 +490,14 @@ struct ConvPairSmem {
   static constexpr int TOTAL = TILE_BYTES + XCH_BYTES + BAR_BYTES + 1024;
 };
 
-template <int BN, int STAGES, int KSUB>
+template <int BN, int STAGES, int KSUB, bool HALO = false>
 __global__ void __launch_bounds__(CONV_PAIR_THREADS, 1)
     conv3d_2sm_kernel(const __grid_constant__ CUtensorMap map_x,
                       const __grid_constant__ CUtensorMap map_w, __nv_bfloat16* __restrict__ out,
                       const ConvShape s, const ConvEpi e) {
-  using L = ConvPairSmem<BN, STAGES, KSUB>;
+  using L = ConvPairSmem<BN, STAGES, KSUB, HALO>;
+  // K sub-blocks: one per (tap, channel block), or per (kt, kh, channel block) with HALO
+  const int ksub_blocks = HALO ? 9 * s.cblocks : s.kblocks;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -547,26 +560,41 @@ __global__ void __launch_bounds__(CONV_PAIR_THREADS, 1)
         // a box past the last one loads zero fill (width coordinate out of range)
         const int f0 = fbi * s.tf, h0 = hbi * s.th;
         const int w0 = box < s.boxes ? wbi * s.tw : s.W + 64;
-        for (int kb0 = 0; kb0 < s.kblocks; kb0 += KSUB) {
-          const int nsub = s.kblocks - kb0 < KSUB ? s.kblocks - kb0 : KSUB;
+        for (int kb0 = 0; kb0 < ksub_blocks; kb0 += KSUB) {
+          const int nsub = ksub_blocks - kb0 < KSUB ? ksub_blocks - kb0 : KSUB;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
           const uint32_t leader_full = smem_u32(&full[stage]) & kPairLeaderMask;
-          if (rank == 0) mbar_expect_tx(&full[stage], 2 * nsub * L::SUB_BYTES);
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * nsub * L::TX_BYTES);
           for (int j = 0; j < nsub; ++j) {
             const int kb = kb0 + j;
-            const int tap = kb / s.cblocks;
-            const int cb = kb - tap * s.cblocks;
-            const int kt = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
             uint8_t* sa = smem + stage * L::STAGE_BYTES + j * L::SUB_BYTES;
             uint8_t* sb = sa + L::A_BYTES;
-            for (int fi = 0; fi < s.tf; ++fi) {
-              int fs = f0 + fi + kt - s.pad_front;
+            if constexpr (HALO) {
+              // the row w0 - 1 .. w0 + 128 of frame f0 + kt, row h0 + kh (tf = th = 1)
+              const int tri = kb / s.cblocks;
+              const int cb = kb - tri * s.cblocks;
+              const int kt = tri / 3, kh = tri % 3;
+              int fs = f0 + kt - s.pad_front;
               fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
-              tma_load_4d_pair(sa + fi * box_rows * 128, &map_x, leader_full, cb * 64,
-                               w0 + kw - 1, h0 + kh - 1, fs);
+              tma_load_4d_pair(sa, &map_x, leader_full, cb * 64, w0 - 1, h0 + kh - 1, fs);
+#pragma unroll
+              for (int kw = 0; kw < 3; ++kw)
+                tma_load_2d_pair(sb + kw * L::B1_BYTES, &map_w, leader_full,
+                                 ((kt * 9 + kh * 3 + kw) * s.cblocks + cb) * GEMM_BK,
+                                 nt * BN + static_cast<int>(rank) * (BN / 2));
+            } else {
+              const int tap = kb / s.cblocks;
+              const int cb = kb - tap * s.cblocks;
+              const int kt = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+              for (int fi = 0; fi < s.tf; ++fi) {
+                int fs = f0 + fi + kt - s.pad_front;
+                fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
+                tma_load_4d_pair(sa + fi * box_rows * 128, &map_x, leader_full, cb * 64,
+                                 w0 + kw - 1, h0 + kh - 1, fs);
+              }
+              tma_load_2d_pair(sb, &map_w, leader_full, kb * GEMM_BK,
+                               nt * BN + static_cast<int>(rank) * (BN / 2));
             }
-            tma_load_2d_pair(sb, &map_w, leader_full, kb * GEMM_BK,
-                             nt * BN + static_cast<int>(rank) * (BN / 2));
           }
           ++issued;
           if (++stage == STAGES) {
@@ -596,7 +624,7 @@ __global__ void __launch_bounds__(CONV_PAIR_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb0 = 0; kb0 < s.kblocks; kb0 += KSUB) {
+        for (int kb0 = 0; kb0 < ksub_blocks; kb0 += KSUB) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) {
             ok = false;
             break;
@@ -604,13 +632,25 @@ __global__ void __launch_bounds__(CONV_PAIR_THREADS, 1)
           tc_fence_after();
 #pragma unroll
           for (int j = 0; j < KSUB; ++j) {
-            if (kb0 + j < s.kblocks) {
+            if (kb0 + j < ksub_blocks) {
               const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES + j * L::SUB_BYTES);
               const uint32_t sb = sa + L::A_BYTES;
+              if constexpr (HALO) {
 #pragma unroll
-              for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
-                umma_bf16_pair(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32), idesc,
-                               (kb0 + j > 0 || kk > 0) ? 1u : 0u);
+                for (int kw = 0; kw < 3; ++kw) {
+#pragma unroll
+                  for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+                    umma_bf16_pair(d_tmem, sdesc_k128(sa + kw * 128 + kk * 32),
+                                   sdesc_k128(sb + kw * L::B1_BYTES + kk * 32), idesc,
+                                   (kb0 + j > 0 || kw > 0 || kk > 0) ? 1u : 0u);
+                  }
+                }
+              } else {
+#pragma unroll
+                for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+                  umma_bf16_pair(d_tmem, sdesc_k128(sa + kk * 32), sdesc_k128(sb + kk * 32),
+                                 idesc, (kb0 + j > 0 || kk > 0) ? 1u : 0u);
+                }
               }
             }
           }

@@ -47,6 +47,12 @@ def _metrics(out, expect):
         (7, 44, 76, 128, 96, False, (1, 1, 1), False),
         (6, 40, 64, 64, 320, True, (1, 1, 1), False),
         (8, 64, 64, 128, 48, True, (1, 1, 1), False),  # the decoder's conv_out width, in pairs
+        # 128-channel pairs on rows of >= 128 voxels: one input row per (kt, kh) serving the
+        # three kw taps (a full row, and a row of 200 with a partial second box)
+        (5, 24, 200, 128, 128, False, (1, 1, 1), True),
+        (6, 32, 128, 128, 128, True, (1, 1, 1), False),
+        (4, 40, 128, 128, 256, True, (1, 1, 1), True),  # the same for 256 channels
+        (3, 32, 128, 256, 512, True, (1, 2, 2), False),  # and under depth-to-space
     ],
 )
 def test_conv3d_matches_oracle(cuda_device, f, h, w, cin, n, causal, stride, residual):
