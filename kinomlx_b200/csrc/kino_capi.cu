@@ -282,7 +282,7 @@ kino_status launch_conv(const kino_conv3d_args* a, const kino::ConvShape& s0, cu
   return check_launch("kino_conv3d");
 }
 
-template <int BN, int STAGES, int KSUB, bool HALO = false>
+template <int BN, int STAGES, int KSUB, int HALO = 0>
 kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0,
                             cudaStream_t stream, int slot) {
   using L = kino::ConvPairSmem<BN, STAGES, KSUB, HALO>;
@@ -291,9 +291,9 @@ kino_status launch_conv_2sm(const kino_conv3d_args* a, const kino::ConvShape& s0
                           static_cast<uint64_t>(s0.H), static_cast<uint64_t>(s0.F)};
   const uint64_t sx[3] = {static_cast<uint64_t>(s0.Cin), static_cast<uint64_t>(s0.W) * s0.Cin,
                           static_cast<uint64_t>(s0.H) * s0.W * s0.Cin};
-  // HALO: one 128-voxel row plus a voxel on each side per load
-  const uint32_t bx[4] = {64, static_cast<uint32_t>(HALO ? kino::CONV_HALO_ROWS : s0.tw),
-                          static_cast<uint32_t>(s0.th), 1};
+  // HALO 1: one 128-voxel row plus a voxel on each side per load; 2: th + 2 rows of tw
+  const uint32_t bx[4] = {64, static_cast<uint32_t>(HALO == 1 ? kino::CONV_HALO_ROWS : s0.tw),
+                          static_cast<uint32_t>(HALO == 2 ? s0.th + 2 : s0.th), 1};
   kino_status st = make_map(&mx, a->x, 4, dx, sx, bx);
   if (st != KINO_OK) return st;
   const uint64_t k = 27ull * s0.Cin;
@@ -1381,8 +1381,10 @@ kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
         r.hb = r.H;
         r.wb = (r.W + 127) / 128;
         r.boxes = r.fb * r.hb * r.wb;
-        return launch_conv_2sm<128, 2, 2, true>(a, r, strm, 23);
+        return launch_conv_2sm<128, 2, 2, 1>(a, r, strm, 23);
       }
+      if (KINO_CONV_HALO && s.tf == 1 && s.th > 1)
+        return launch_conv_2sm<128, 2, 2, 2>(a, s, strm, 25);
       return launch_conv_2sm<128, KINO_CONV_NARROW_STAGES, KINO_CONV_NARROW_KSUB>(a, s, strm, 8);
     }
     // narrow outputs: two boxes per tile share the weight block when that still fills the GPU
@@ -1400,8 +1402,10 @@ kino_status kino_conv3d(const kino_conv3d_args* a, void* stream) {
       r.hb = r.H;
       r.wb = (r.W + 127) / 128;
       r.boxes = r.fb * r.hb * r.wb;
-      return launch_conv_2sm<256, 3, 1, true>(a, r, strm, 24);
+      return launch_conv_2sm<256, 3, 1, 1>(a, r, strm, 24);
     }
+    if (KINO_CONV_HALO && s.tf == 1 && s.th > 1)
+      return launch_conv_2sm<256, 3, 1, 2>(a, s, strm, 26);
     return launch_conv_2sm<256, KINO_CONV_WIDE_STAGES, KINO_CONV_WIDE_KSUB>(a, s, strm, 9);
   }
   return launch_conv<256, 4, 1>(a, s, strm, 5);

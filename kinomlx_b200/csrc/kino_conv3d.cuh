@@ -467,22 +467,27 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
 // A stage holds KSUB consecutive K blocks (each: this CTA's box and its half of the weight
 // rows), so that one barrier round trip covers KSUB x 4 MMAs: with BN = 128 an MMA is only 64
 // tensor cycles and the per-stage wait would otherwise show between the groups.
-// HALO: the box is one 128-voxel row (tw = 128) and a K sub-block is one (kt, kh, channel block)
-// triple: its input row is loaded once with a one-voxel halo on each side (130 rows) and serves
-// the three kw taps as A operands starting 0, 1 and 2 rows in, each with its own weight block.
-// The 128-byte swizzle is a function of the absolute shared-memory address (measured: the MMA
-// reads the TMA's swizzled rows correctly from a start 1 or 2 rows into a 1024-byte atom with the
-// descriptor's base-offset field left at 0, and wrongly with it set to the row phase), so the
-// shifted operands are plain descriptors of the shifted addresses.
+// HALO (input rows loaded once for three taps):
+//   1 (along W) the box is one 128-voxel row and a K sub-block one (kt, kh, channel block)
+//     triple: its input row is loaded with a voxel of halo on each side (130 rows) and serves the
+//     kw = 0, 1, 2 taps as A operands starting 0, 1 and 2 rows in;
+//   2 (along H) the box is th rows of tw voxels of one frame and a K sub-block one (kt, kw,
+//     channel block) triple: th + 2 input rows (a row of halo above and below) serve the
+//     kh = 0, 1, 2 taps as A operands starting 0, tw and 2 tw rows in (whole 1024-byte swizzle
+//     atoms, tw >= 8);
+//   each tap with its own weight block, so the input crosses from L2 9 times per voxel instead
+//   of 27. The 128-byte swizzle is a function of the absolute shared-memory address (measured:
+//   the MMA reads the TMA's swizzled rows correctly from a start 1 or 2 rows into a 1024-byte
+//   atom with the descriptor's base-offset field left at 0, and wrongly with it set to the row
+//   phase), so the shifted operands are plain descriptors of the shifted addresses.
 constexpr int CONV_HALO_ROWS = GEMM_BM + 2;
-template <int BN, int STAGES, int KSUB, bool HALO = false>
+template <int BN, int STAGES, int KSUB, int HALO = 0>
 struct ConvPairSmem {
-  static constexpr int A_BYTES = HALO ? 17 * 1024 : GEMM_BM * GEMM_BK * 2;  // this CTA's box
+  // this CTA's input: a box, a halo row (130 rows), or th + 2 rows of tw (at most 6 x 32)
+  static constexpr int A_BYTES = HALO == 1 ? 17 * 1024 : (HALO == 2 ? 24 * 1024 : GEMM_BM * GEMM_BK * 2);
   static constexpr int B1_BYTES = (BN / 2) * GEMM_BK * 2;  // this CTA's half of one tap's weights
   static constexpr int B_BYTES = (HALO ? 3 : 1) * B1_BYTES;
   static constexpr int SUB_BYTES = A_BYTES + B_BYTES;
-  // bytes the TMA delivers per sub-block (the halo row is 130 rows of 128 bytes)
-  static constexpr int TX_BYTES = (HALO ? CONV_HALO_ROWS * 128 : A_BYTES) + B_BYTES;
   static constexpr int STAGE_BYTES = KSUB * SUB_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int XCH_BYTES = 4 * 32 * 3 * 4;  // GroupNorm statistics handed between halves
@@ -490,14 +495,18 @@ struct ConvPairSmem {
   static constexpr int TOTAL = TILE_BYTES + XCH_BYTES + BAR_BYTES + 1024;
 };
 
-template <int BN, int STAGES, int KSUB, bool HALO = false>
+template <int BN, int STAGES, int KSUB, int HALO = 0>
 __global__ void __launch_bounds__(CONV_PAIR_THREADS, 1)
     conv3d_2sm_kernel(const __grid_constant__ CUtensorMap map_x,
                       const __grid_constant__ CUtensorMap map_w, __nv_bfloat16* __restrict__ out,
                       const ConvShape s, const ConvEpi e) {
   using L = ConvPairSmem<BN, STAGES, KSUB, HALO>;
-  // K sub-blocks: one per (tap, channel block), or per (kt, kh, channel block) with HALO
+  // K sub-blocks: one per (tap, channel block), or per (kt, kh | kw, channel block) with HALO
   const int ksub_blocks = HALO ? 9 * s.cblocks : s.kblocks;
+  // bytes the TMA delivers per sub-block
+  const int a_tx = HALO == 1 ? CONV_HALO_ROWS * 128
+                             : (HALO == 2 ? (s.th + 2) * s.tw * 128 : L::A_BYTES);
+  const int sub_tx = a_tx + L::B_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -564,12 +573,25 @@ __global__ void __launch_bounds__(CONV_PAIR_THREADS, 1)
           const int nsub = ksub_blocks - kb0 < KSUB ? ksub_blocks - kb0 : KSUB;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) goto producer_done;
           const uint32_t leader_full = smem_u32(&full[stage]) & kPairLeaderMask;
-          if (rank == 0) mbar_expect_tx(&full[stage], 2 * nsub * L::TX_BYTES);
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * nsub * sub_tx);
           for (int j = 0; j < nsub; ++j) {
             const int kb = kb0 + j;
             uint8_t* sa = smem + stage * L::STAGE_BYTES + j * L::SUB_BYTES;
             uint8_t* sb = sa + L::A_BYTES;
-            if constexpr (HALO) {
+            if constexpr (HALO == 2) {
+              // rows h0 - 1 .. h0 + th of frame f0 + kt, columns shifted by kw (tf = 1)
+              const int tri = kb / s.cblocks;
+              const int cb = kb - tri * s.cblocks;
+              const int kt = tri / 3, kw = tri % 3;
+              int fs = f0 + kt - s.pad_front;
+              fs = fs < 0 ? 0 : (fs > s.F - 1 ? s.F - 1 : fs);
+              tma_load_4d_pair(sa, &map_x, leader_full, cb * 64, w0 + kw - 1, h0 - 1, fs);
+#pragma unroll
+              for (int kh = 0; kh < 3; ++kh)
+                tma_load_2d_pair(sb + kh * L::B1_BYTES, &map_w, leader_full,
+                                 ((kt * 9 + kh * 3 + kw) * s.cblocks + cb) * GEMM_BK,
+                                 nt * BN + static_cast<int>(rank) * (BN / 2));
+            } else if constexpr (HALO == 1) {
               // the row w0 - 1 .. w0 + 128 of frame f0 + kt, row h0 + kh (tf = th = 1)
               const int tri = kb / s.cblocks;
               const int cb = kb - tri * s.cblocks;
@@ -635,7 +657,18 @@ __global__ void __launch_bounds__(CONV_PAIR_THREADS, 1)
             if (kb0 + j < ksub_blocks) {
               const uint32_t sa = smem_u32(smem + stage * L::STAGE_BYTES + j * L::SUB_BYTES);
               const uint32_t sb = sa + L::A_BYTES;
-              if constexpr (HALO) {
+              if constexpr (HALO == 2) {
+                const uint32_t pitch = static_cast<uint32_t>(s.tw) * 128;  // one input row
+#pragma unroll
+                for (int kh = 0; kh < 3; ++kh) {
+#pragma unroll
+                  for (int kk = 0; kk < GEMM_BK / 16; ++kk) {
+                    umma_bf16_pair(d_tmem, sdesc_k128(sa + kh * pitch + kk * 32),
+                                   sdesc_k128(sb + kh * L::B1_BYTES + kk * 32), idesc,
+                                   (kb0 + j > 0 || kh > 0 || kk > 0) ? 1u : 0u);
+                  }
+                }
+              } else if constexpr (HALO == 1) {
 #pragma unroll
                 for (int kw = 0; kw < 3; ++kw) {
 #pragma unroll
