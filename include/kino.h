@@ -33,7 +33,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (12); bumped on any signature change or addition. */
+/* ABI version of this header (13); bumped on any signature change or addition. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -182,7 +182,19 @@ typedef struct kino_attention_args {
    * are raised to it, so a row whose keys are all masked averages them uniformly. */
   const float* key_bias;
   int64_t ld_key_bias;
+  /* Optional key split (kv_splits > 1, no key bias): each CTA takes one share of the key blocks
+   * and a merge launch combines the shares' outputs by their row maxima and sums, so that a
+   * call with few query tiles (sequence-parallel ranks, small batches) still fills the GPU.
+   * Needs kino_attention_workspace_size(args, kv_splits) bytes of 16-byte aligned workspace. */
+  int64_t kv_splits;
+  void* workspace;
+  int64_t workspace_bytes;
 } kino_attention_args;
+
+/* Workspace bytes kino_attention needs for `kv_splits` key shares (0 for one share; -1 for
+ * invalid arguments): the shares' fp32 outputs and row statistics. No counterpart in the
+ * reference (its attention is one MLX call). */
+int64_t kino_attention_workspace_size(const kino_attention_args* args, int64_t kv_splits);
 
 /* softmax(q k^T * scale) v over all key segments, per head, token-major operands.
  * Replaces MLX SDPA in the joint attention (kinomlx/models/flux2/kv.py:48-54,

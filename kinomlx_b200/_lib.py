@@ -123,6 +123,9 @@ class AttentionArgs(ctypes.Structure):
         ("gate_head_offset", c_int64),
         ("key_bias", c_void_p),
         ("ld_key_bias", c_int64),
+        ("kv_splits", c_int64),
+        ("workspace", c_void_p),
+        ("workspace_bytes", c_int64),
     ]
 
 
@@ -264,6 +267,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_dense_attention": (c_int, [P, P, P, P, I64, I64, I64, I64, P]),
     "kino_sol_attention_workspace_size": (I64, [I64, I64]),
     "kino_sol_attention": (c_int, [POINTER(SolAttentionArgs), P]),
+    "kino_attention_workspace_size": (I64, [POINTER(AttentionArgs), I64]),
     "kino_neighborhood_attention": (c_int, [P, P, P, P, I64, I64, I64, I64, I64, P, P]),
     "kino_adaln": (c_int, [P, I64, I64, P, P, I64, P, I64, I64, I64, I64, I64, c_int, F, P]),
     "kino_rms_norm": (c_int, [P, P, P, I64, I64, F, F, P]),

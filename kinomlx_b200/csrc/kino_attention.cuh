@@ -70,6 +70,15 @@ struct AttnParams {
   // mask is (kinomlx/models/ltx2/transformer/attention.py:164-186).
   const float* key_bias;
   int64_t ld_key_bias;
+  // Split keys (kv_splits > 1, no key bias): CTA x covers tile pair x / kv_splits and the
+  // kv_splits-th share x % kv_splits of the key blocks, and writes its unnormalised output and
+  // row statistics instead of `out`: part_o[((split * batch + b) * heads + h) * rows + r][D]
+  // (fp32; r = global tile index * 128 + row over both query segments) and part_ml[...][2]
+  // (row maximum in log2 units, row sum); attention_combine_kernel merges the shares.
+  int kv_splits;
+  int64_t part_rows;
+  float* part_o;
+  float* part_ml;
 };
 
 struct AttnSmem {
@@ -156,10 +165,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t lane = lane_id();
   const int head = blockIdx.y;
   const int batch = blockIdx.z;
-  const QTile tiles[2] = {q_tile_of(p, 2 * blockIdx.x), q_tile_of(p, 2 * blockIdx.x + 1)};
+  const int splits = p.kv_splits > 1 ? p.kv_splits : 1;
+  const int pair = blockIdx.x / splits, split = blockIdx.x % splits;
+  const QTile tiles[2] = {q_tile_of(p, 2 * pair), q_tile_of(p, 2 * pair + 1)};
   const bool has_b = tiles[1].valid;
   const int ntile = has_b ? 2 : 1;
-  const int nblk = p.kv_blocks[0] + (p.nkv_seg > 1 ? p.kv_blocks[1] : 0);
+  // this CTA's key blocks [b0, b0 + nblk) of all segments' blocks
+  const int nblk_all = p.kv_blocks[0] + (p.nkv_seg > 1 ? p.kv_blocks[1] : 0);
+  const int b0 = split * nblk_all / splits;
+  const int nblk = (split + 1) * nblk_all / splits - b0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -203,8 +217,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const int stage = j % ATT_STAGES;
         const uint32_t parity = (j / ATT_STAGES) & 1;
         if (!mbar_wait(&kv_empty[stage], parity ^ 1u, abort_flag)) break;
-        const int kseg = (j < p.kv_blocks[0]) ? 0 : 1;
-        const int kb = j - (kseg ? p.kv_blocks[0] : 0);
+        const int kseg = (b0 + j < p.kv_blocks[0]) ? 0 : 1;
+        const int kb = b0 + j - (kseg ? p.kv_blocks[0] : 0);
         const CUtensorMap* mk = kseg ? &mk1 : &mk0;
         const CUtensorMap* mv = kseg ? &mv1 : &mv0;
         uint8_t* sk = smem + L::KV_OFF + stage * L::STAGE;
@@ -303,8 +317,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     float l_run[2] = {0.0f, 0.0f};            // per tile: this half's share of the row sum
     bool ok = true;
     for (int j = 0; j < nblk && ok; ++j) {
-      const int kseg = (j < p.kv_blocks[0]) ? 0 : 1;
-      const int kb = j - (kseg ? p.kv_blocks[0] : 0);
+      const int kseg = (b0 + j < p.kv_blocks[0]) ? 0 : 1;
+      const int kb = b0 + j - (kseg ? p.kv_blocks[0] : 0);
       const int valid = min(ATT_BN, p.kv_tokens[kseg] - kb * ATT_BN) - half * 64;
       // BIAS: this half block's key biases in log2 units, floored at -1e30 so that a row whose
       // keys are all masked averages them uniformly, as a finite additive mask does
@@ -439,7 +453,35 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_arrive(&lbar[quarter]);
       ok = mbar_wait(&lbar[quarter], 0, abort_flag);
     }
-    if (ok && nblk > 0 && mbar_wait(o_done, 0, abort_flag)) {
+    if (ok && nblk > 0 && splits > 1 && mbar_wait(o_done, 0, abort_flag)) {
+      // one share of the keys: the unnormalised output and the row statistics
+      tc_fence_after();
+      for (int t = 0; t < ntile; ++t) {
+        const QTile qt = tiles[t];
+        const bool store = qt.tile * ATT_BM + row < p.q_tokens[qt.seg];
+        const int64_t r = static_cast<int64_t>(2 * pair + t) * ATT_BM + row;
+        const int64_t slot = ((static_cast<int64_t>(split) * p.batch + batch) * p.heads + head) *
+                                 p.part_rows + r;
+        if (store && half == 0) {
+          p.part_ml[slot * 2] = m_run[t];
+          p.part_ml[slot * 2 + 1] = l_run[t] + xsum[(t * 2 + 1) * 128 + row];
+        }
+        float* dst = p.part_o + slot * D + half * (D / 2);
+        const uint32_t o_col = tmem + lane_base + 256 + t * 128 + half * (D / 2);
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_col + c * 32, o);
+          tmem_wait_ld();
+          if (store) {
+#pragma unroll
+            for (int g = 0; g < 8; ++g)
+              *reinterpret_cast<uint4*>(dst + c * 32 + g * 4) =
+                  make_uint4(o[g * 4], o[g * 4 + 1], o[g * 4 + 2], o[g * 4 + 3]);
+          }
+        }
+      }
+    } else if (ok && nblk > 0 && mbar_wait(o_done, 0, abort_flag)) {
       tc_fence_after();
       for (int t = 0; t < ntile; ++t) {
         const QTile qt = tiles[t];
@@ -503,6 +545,76 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// Merge of the key shares of a split attention (AttnParams::kv_splits > 1): one thread per 8
+// output columns of a (batch, head, query row): O = sum_i O_i 2^(m_i - m) / sum_i l_i 2^(m_i - m)
+// over the shares i, then the one-pass kernel's gate and store (local rows, or the owner GPU's
+// rows under the sequence-parallel return).
+template <int D>
+__global__ void __launch_bounds__(256) attention_combine_kernel(const AttnParams p) {
+  griddep_wait();
+  griddep_launch();
+  constexpr int CH = D / 8;
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  const int c = static_cast<int>(gid % CH);
+  const int64_t r = (gid / CH) % p.part_rows;
+  const int64_t bh = gid / (CH * p.part_rows);
+  if (bh >= static_cast<int64_t>(p.batch) * p.heads) return;
+  const int batch = static_cast<int>(bh / p.heads), head = static_cast<int>(bh % p.heads);
+  const QTile qt = q_tile_of(p, static_cast<int>(r / ATT_BM));
+  const int tok = qt.tile * ATT_BM + static_cast<int>(r % ATT_BM);
+  if (!qt.valid || tok >= p.q_tokens[qt.seg]) return;
+  const int64_t stride = static_cast<int64_t>(p.batch) * p.heads * p.part_rows;  // per share
+  const int64_t slot0 = bh * p.part_rows + r;
+  float m = -INFINITY;
+  for (int i = 0; i < p.kv_splits; ++i) m = fmaxf(m, p.part_ml[(slot0 + i * stride) * 2]);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float l = 0.0f;
+  for (int i = 0; i < p.kv_splits; ++i) {
+    const int64_t slot = slot0 + i * stride;
+    const float w = ex2_approx(p.part_ml[slot * 2] - m);
+    l += p.part_ml[slot * 2 + 1] * w;
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + slot * D + c * 8);
+    const float4 a = src[0], b = src[1];
+    acc[0] += a.x * w;
+    acc[1] += a.y * w;
+    acc[2] += a.z * w;
+    acc[3] += a.w * w;
+    acc[4] += b.x * w;
+    acc[5] += b.y * w;
+    acc[6] += b.z * w;
+    acc[7] += b.w * w;
+  }
+  const float inv_l = 1.0f / l;
+  const __nv_bfloat16* gp = p.gate[qt.seg];
+  __nv_bfloat16* dst;
+  float gv = 1.0f;
+  if (p.out_peers != nullptr) {
+    const int owner = tok / p.rows_per_rank;
+    const int64_t lt = tok - static_cast<int64_t>(owner) * p.rows_per_rank;
+    dst = p.out_peers[owner] + lt * p.ld_out[0] + p.out_col_offset + head * D;
+    if (p.gate_peers != nullptr) {
+      gp = p.gate_peers[0];
+      gv = __bfloat162float(p.gate_peers[owner][lt * p.ld_gate[0] + p.gate_head_offset + head]);
+    }
+  } else {
+    dst = p.out[qt.seg] + static_cast<int64_t>(batch) * p.bs_out[qt.seg] +
+          static_cast<int64_t>(tok) * p.ld_out[qt.seg] + head * D;
+    if (gp != nullptr)
+      gv = __bfloat162float(gp[static_cast<int64_t>(batch) * p.bs_gate[qt.seg] +
+                               static_cast<int64_t>(tok) * p.ld_gate[qt.seg] + head]);
+  }
+  float o[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    o[e] = acc[e] * inv_l;
+    if (gp != nullptr) o[e] = bf16_round(bf16_round(o[e]) * gv);
+  }
+  *reinterpret_cast<uint4*>(dst + c * 8) =
+      make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                 pack_bf16x2(o[6], o[7]));
+  if (p.out_peers != nullptr) __threadfence_system();
 }
 
 }  // namespace kino

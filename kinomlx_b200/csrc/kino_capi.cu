@@ -532,7 +532,7 @@ SolLayout sol_layout(int64_t tokens, int64_t heads) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 12; }
+int kino_abi_version(void) { return 13; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -718,6 +718,17 @@ kino_status kino_gemv(const void* x, int64_t ldx, const void* w, const void* bia
   return check_launch("kino_gemv");
 }
 
+int64_t kino_attention_workspace_size(const kino_attention_args* a, int64_t kv_splits) {
+  if (a == nullptr || kv_splits < 1 || a->n_q < 1 || a->n_q > 2 || a->batch < 1 || a->heads < 1)
+    return -1;
+  if (kv_splits == 1) return 0;
+  int64_t tiles = 0;
+  for (int s = 0; s < a->n_q; ++s) tiles += (a->q_tokens[s] + 127) / 128;
+  const int64_t rows = (tiles + 1) / 2 * 2 * 128;
+  const int64_t n = kv_splits * a->batch * a->heads * rows;
+  return n * a->head_dim * 4 + n * 2 * 4;
+}
+
 kino_status kino_attention(const kino_attention_args* a, void* stream) {
   if (a == nullptr) return fail(KINO_EINVAL, "kino_attention: null args");
   if (a->head_dim != 128 && a->head_dim != 64)
@@ -803,13 +814,41 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
     p.ld_out[0] = a->ld_out[0];
     p.ld_gate[0] = a->ld_gate[0];
   }
-  dim3 grid((tiles + 1) / 2, p.heads, p.batch);  // two 128-query tiles per CTA
+  const int splits = a->kv_splits > 1 ? static_cast<int>(a->kv_splits) : 1;
+  if (splits > 1) {
+    const int nblk_all = p.kv_blocks[0] + (a->n_kv > 1 ? p.kv_blocks[1] : 0);
+    if (a->key_bias != nullptr)
+      return fail(KINO_EINVAL, "kino_attention: a key bias takes no key split");
+    if (splits > nblk_all || splits > 16)
+      return fail(KINO_EINVAL, "kino_attention: kv_splits %d outside 1 .. min(16, %d key blocks)",
+                  splits, nblk_all);
+    const int64_t need = kino_attention_workspace_size(a, splits);
+    if (a->workspace == nullptr || a->workspace_bytes < need || !aligned16(a->workspace))
+      return fail(KINO_EINVAL, "kino_attention: a %d-way key split needs %lld bytes of 16-byte "
+                  "aligned workspace", splits, (long long)need);
+    p.kv_splits = splits;
+    p.part_rows = static_cast<int64_t>((tiles + 1) / 2) * 2 * kino::ATT_BM;
+    p.part_o = static_cast<float*>(a->workspace);
+    p.part_ml = p.part_o + static_cast<int64_t>(splits) * p.batch * p.heads * p.part_rows * hd;
+  }
+  // two 128-query tiles per CTA, each CTA on one share of the keys when they are split
+  dim3 grid(static_cast<unsigned>((tiles + 1) / 2 * splits), p.heads, p.batch);
   auto run = [&](auto kernel, int slot) {
     kino_status st = ensure_smem(kernel, kino::AttnSmem::TOTAL, slot);
     if (st != KINO_OK) return st;
     launch_pdl(kernel, dim3(grid), dim3(kino::ATT_THREADS), kino::AttnSmem::TOTAL,
                static_cast<cudaStream_t>(stream), mq[0], mq[1], mk[0], mk[1], mv[0], mv[1], p);
-    return check_launch("kino_attention");
+    st = check_launch("kino_attention");
+    if (st != KINO_OK || splits == 1) return st;
+    const int64_t threads = static_cast<int64_t>(p.batch) * p.heads * p.part_rows * (hd / 8);
+    const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+    if (hd == 64)
+      launch_pdl(kino::attention_combine_kernel<64>, dim3(blocks), dim3(256), 0,
+                 static_cast<cudaStream_t>(stream), p);
+    else
+      launch_pdl(kino::attention_combine_kernel<128>, dim3(blocks), dim3(256), 0,
+                 static_cast<cudaStream_t>(stream), p);
+    return check_launch("kino_attention (combine)");
   };
   if (a->key_bias != nullptr) {
     if (a->n_kv != 1 || a->out_peers != nullptr)

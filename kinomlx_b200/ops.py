@@ -386,6 +386,37 @@ def gemv(
     return out
 
 
+_SPLIT_WORKSPACES: dict[torch.device, torch.Tensor] = {}
+_SM_COUNTS: dict[int, int] = {}
+
+
+def _split_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A byte buffer of at least `nbytes` on `device`, grown as needed and reused by every split
+    attention on the stream."""
+    ws = _SPLIT_WORKSPACES.get(device)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _SPLIT_WORKSPACES[device] = ws
+    return ws
+
+
+def attention_splits(args, device: torch.device) -> int:
+    """Key shares for an attention call: 1 when its CTAs (two 128-query tiles each) fill two
+    waves of the SMs, else enough shares for about two waves, at most 4 and at most one per key
+    block. Attention over few query tiles (sequence-parallel ranks, small batches) otherwise
+    leaves most SMs idle."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if index not in _SM_COUNTS:
+        _SM_COUNTS[index] = torch.cuda.get_device_properties(index).multi_processor_count
+    sms = _SM_COUNTS[index]
+    tiles = sum((int(args.q_tokens[i]) + 127) // 128 for i in range(args.n_q))
+    ctas = (tiles + 1) // 2 * int(args.heads) * int(args.batch)
+    if ctas >= 2 * sms:
+        return 1
+    blocks = sum((int(args.kv_tokens[i]) + 127) // 128 for i in range(args.n_kv))
+    return max(1, min(4, blocks, -(-2 * sms // ctas)))
+
+
 def attention(
     q: list[torch.Tensor],
     k: list[torch.Tensor],
@@ -397,12 +428,16 @@ def attention(
     gate: list[torch.Tensor | None] | None = None,
     peer_return: PeerReturn | None = None,
     key_bias: torch.Tensor | None = None,
+    kv_splits: int | str = 1,
 ) -> list[torch.Tensor]:
     """Attention over logically concatenated segments; each tensor (batch, tokens, heads*128).
     `gate[s]` (batch, tokens, heads), if given, multiplies segment s's output per head. With
     `peer_return`, output rows go to their owner GPUs instead of `out`. `key_bias` (fp32,
     (batch, >= keys rounded up to 4), unit column stride; one key segment) is added to the
-    scaled scores of every query row: an additive attention mask over the keys."""
+    scaled scores of every query row: an additive attention mask over the keys. `kv_splits`
+    shares the keys among that many CTAs per tile pair (merged by row statistics); "auto" splits
+    the calls whose tile pairs fill less than two waves of the SMs (`attention_splits`), which
+    the sequence-parallel ranks use."""
     if not 1 <= len(q) <= 2 or len(out) != len(q) or not 1 <= len(k) <= 2 or len(v) != len(k):
         raise ValueError("attention takes 1 or 2 query and key/value segments")
     args = _lib.AttentionArgs()
@@ -469,6 +504,15 @@ def attention(
             args.gate_peers = r.gate_ptrs.data_ptr()
             args.ld_gate[0] = r.ld_gate
             args.gate_head_offset = r.gate_head_offset
+    splits = attention_splits(args, q0.device) if kv_splits == "auto" else int(kv_splits)
+    if key_bias is not None:
+        splits = 1
+    if splits > 1:
+        need = int(_lib.load().kino_attention_workspace_size(ctypes.byref(args), splits))
+        ws = _split_workspace(q0.device, need)
+        args.kv_splits = splits
+        args.workspace = ws.data_ptr()
+        args.workspace_bytes = ws.numel()
     nq = sum(int(args.q_tokens[i]) for i in range(args.n_q))
     nk = sum(int(args.kv_tokens[i]) for i in range(args.n_kv))
     flops = 4.0 * args.batch * heads * nq * nk * args.head_dim

@@ -75,7 +75,8 @@ class SequenceParallel:
             ops.heads_pack(src[0], p, out=send)
             dist.all_to_all_single(recv, send, group=self.group)
         full = lambda t: t.view(1, p * tokens, width // p)
-        ops.attention([full(rq)], [full(rk)], [full(rv)], [full(att)], heads=heads // p)
+        ops.attention([full(rq)], [full(rk)], [full(rv)], [full(att)], heads=heads // p,
+                      kv_splits="auto")
         dist.all_to_all_single(ro, att, group=self.group)
         ops.heads_unpack(ro, out[0], gate=None if gate is None else gate[0])
 
@@ -120,7 +121,8 @@ class SequenceParallel:
                              gate_ptrs=None if gate is None else gate[0],
                              ld_gate=0 if gate is None else gate[1],
                              gate_head_offset=self.rank * (heads // p))
-        ops.attention([q], [k], [v], [q], heads=heads // p, peer_return=ret)
+        # H / P heads of the whole sequence: few query tiles, so the keys are split among CTAs
+        ops.attention([q], [k], [v], [q], heads=heads // p, peer_return=ret, kv_splits="auto")
         self.peer.barrier()
 
     def close(self) -> None:

@@ -77,7 +77,7 @@ def linear(x, w, out=None, *, bias=None, kind=0, residual=None, gate=None, act_c
 
 
 def attention_list(q, k, v, out, *, heads, scale=None, gate=None, peer_return=None,
-                   key_bias=None):
+                   key_bias=None, kv_splits=1):
     """ops.attention: lists of query and key/value segments, an optional additive key bias."""
     q3 = torch.cat([_3(t) for t in q], 1)
     k3 = torch.cat([_3(t) for t in k], 1)

@@ -82,7 +82,7 @@ class _CpuOps:
         return out
 
     @staticmethod
-    def attention(q, k, v, out, heads, gate=None):
+    def attention(q, k, v, out, heads, gate=None, kv_splits=1):
         from oracle.fused_ops import sdpa
 
         b, t, w = q[0].shape
