@@ -132,7 +132,7 @@ __device__ __forceinline__ QTile q_tile_of(const AttnParams& p, int global) {
   return t;
 }
 
-template <int D, bool BIAS = false>
+template <int D, bool BIAS = false, bool SPLIT = false>
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap mq0,
                         const __grid_constant__ CUtensorMap mq1,
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const uint32_t lane = lane_id();
   const int head = blockIdx.y;
   const int batch = blockIdx.z;
-  const int splits = p.kv_splits > 1 ? p.kv_splits : 1;
+  const int splits = SPLIT ? p.kv_splits : 1;
   const int pair = blockIdx.x / splits, split = blockIdx.x % splits;
   const QTile tiles[2] = {q_tile_of(p, 2 * pair), q_tile_of(p, 2 * pair + 1)};
   const bool has_b = tiles[1].valid;
@@ -453,7 +453,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_arrive(&lbar[quarter]);
       ok = mbar_wait(&lbar[quarter], 0, abort_flag);
     }
-    if (ok && nblk > 0 && splits > 1 && mbar_wait(o_done, 0, abort_flag)) {
+    if (SPLIT && ok && nblk > 0 && mbar_wait(o_done, 0, abort_flag)) {
       // one share of the keys: the unnormalised output and the row statistics
       tc_fence_after();
       for (int t = 0; t < ntile; ++t) {

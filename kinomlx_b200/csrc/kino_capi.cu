@@ -864,6 +864,9 @@ kino_status kino_attention(const kino_attention_args* a, void* stream) {
     return a->head_dim == 64 ? run(kino::attention_tc_kernel<64, true>, 14)
                              : run(kino::attention_tc_kernel<128, true>, 15);
   }
+  if (splits > 1)
+    return a->head_dim == 64 ? run(kino::attention_tc_kernel<64, false, true>, 27)
+                             : run(kino::attention_tc_kernel<128, false, true>, 28);
   return a->head_dim == 64 ? run(kino::attention_tc_kernel<64>, 11)
                            : run(kino::attention_tc_kernel<128>, 3);
 }
