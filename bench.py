@@ -702,6 +702,22 @@ def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | N
         out = torch.empty((1, n, d), device=dev, dtype=torch.bfloat16)
         for _ in range(3):
             ops.attention([q], [k], [v], [out], heads=24)
+        # timed after the captured launches: the image step's 4608 x 24 heads and the video
+        # step's 9216 x 32 heads (CUDA events, 20 launches each after 3 warm ones)
+        res = {}
+        for name, tokens, heads in (("4608x24", n, 24), ("9216x32", 9216, 32)):
+            width = heads * 128
+            qkv = normal((1, tokens, 3 * width), seed=3, device=dev)
+            q, k, v = qkv[..., :width], qkv[..., width : 2 * width], qkv[..., 2 * width :]
+            out = torch.empty((1, tokens, width), device=dev, dtype=torch.bfloat16)
+            fn = lambda: ops.attention([q], [k], [v], [out], heads=heads)
+            ms = _time(fn, 3, 20, 1)
+            flop = 4.0 * tokens * tokens * heads * 128
+            res[name] = {"us": round(ms * 1e3, 1), "tflops": round(flop / (ms * 1e9), 1)}
+        torch.cuda.synchronize()
+        ops.device_status()
+        print(json.dumps({"kernel_case": case, "ok": True, **res}))
+        return
     elif case == "conv3d":
         x = normal((25, 96, 128, 256), seed=7, device=dev)
         w = normal((256, 3, 3, 3, 256), seed=8, device=dev, std=0.02)
