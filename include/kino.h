@@ -33,7 +33,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (13); bumped on any signature change or addition. */
+/* ABI version of this header (14); bumped on any signature change or addition. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -212,6 +212,7 @@ kino_status kino_dense_attention(const void* q, const void* k, const void* v, vo
 /* ------------------------------------------------------------------ Sol-Attn (sparse) */
 #define KINO_DTYPE_BF16 0
 #define KINO_DTYPE_F16 1
+#define KINO_DTYPE_F32 2  /* kino_strided_copy only */
 
 typedef struct kino_sol_attention_args {
   const void* q;           /* (tokens, heads * 128) token-major, dtype below, row strides ld_* */
@@ -261,6 +262,35 @@ kino_status kino_neighborhood_attention(const void* q, const void* k, const void
                                         int64_t batch, int64_t frames, int64_t height,
                                         int64_t width, int64_t heads, const int32_t* window,
                                         void* stream);
+
+/* ------------------------------------------------------------------ diffusion video decoder */
+/* The qkv projection rows of a diffusion-decoder attention -> the neighborhood attention's
+ * operands. qkv: (batch * frames * height * width, >= 3 * heads * 64) bf16 rows [q | k | v]
+ * (bias already added) with row stride ld; q, k, v: contiguous (tokens, heads, 64) fp16. q and
+ * k get a per-head RMSNorm (eps, learned bf16 weights of 64) and the decoder's absolute 3-D
+ * RoPE on adjacent pairs: pairs [0, s0) rotate by the frame index, [s0, s0 + s1) by the row,
+ * [s0 + s1, 32) by the column (section_pairs = host {s0, s1, s2}); q is also multiplied by
+ * q_scale (head_dim^-1/2). rope_tables (fp32, device): cos_t (frames, s0), sin_t, cos_h
+ * (height, s1), sin_h, cos_w (width, s2), sin_w, back to back. fp32 arithmetic, fp16 results.
+ * Replaces the q/k half of NeighborhoodAttention3D._project_temporal_partition and
+ * diffusion_passes.qk_norm_rope (kinomlx/models/ltx2/video_vae/diffusion_decoder.py:492-517,
+ * kinomlx/models/ltx2/kernels/diffusion_passes.py:298-420). */
+kino_status kino_na_qkv_prepare(const void* qkv, int64_t ld, void* q, void* k, void* v,
+                                const void* q_norm_weight, const void* k_norm_weight,
+                                const float* rope_tables, int64_t batch, int64_t frames,
+                                int64_t height, int64_t width, int64_t heads,
+                                const int32_t* section_pairs, float q_scale, float eps,
+                                void* stream);
+
+/* dst[i] = convert(src[i]) over an ndim-D index space (1 <= ndim <= 8, dimension ndim - 1
+ * fastest): element offsets sum_d i_d * strides[d] on each side (a zero source stride
+ * broadcasts), dtypes KINO_DTYPE_BF16 / _F16 / _F32 (round to nearest even on narrowing). The
+ * decoder's pixel shuffles, spatial patchify / unpatchify, edge padding and dtype hand-offs
+ * (kinomlx/models/ltx2/video_vae/diffusion_decoder.py:49-91, 283-308, 928-971). Destination
+ * elements must not overlap each other or the source. */
+kino_status kino_strided_copy(const void* src, int src_dtype, const int64_t* src_strides,
+                              void* dst, int dst_dtype, const int64_t* dst_strides,
+                              const int64_t* sizes, int ndim, void* stream);
 
 /* ------------------------------------------------------------------ norms and rotary */
 #define KINO_NORM_RMS 0

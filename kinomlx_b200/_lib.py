@@ -269,6 +269,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_sol_attention": (c_int, [POINTER(SolAttentionArgs), P]),
     "kino_attention_workspace_size": (I64, [POINTER(AttentionArgs), I64]),
     "kino_neighborhood_attention": (c_int, [P, P, P, P, I64, I64, I64, I64, I64, P, P]),
+    "kino_na_qkv_prepare": (
+        c_int,
+        [P, I64, P, P, P, P, P, P, I64, I64, I64, I64, I64, P, F, F, P],
+    ),
+    "kino_strided_copy": (c_int, [P, c_int, P, P, c_int, P, P, c_int, P]),
     "kino_adaln": (c_int, [P, I64, I64, P, P, I64, P, I64, I64, I64, I64, I64, c_int, F, P]),
     "kino_rms_norm": (c_int, [P, P, P, I64, I64, F, F, P]),
     "kino_qk_norm_rope": (

@@ -17,6 +17,7 @@
 #include "kino_peer.cuh"
 #include "kino_sol.cuh"
 #include "kino_na.cuh"
+#include "kino_diffusion.cuh"
 #include "kino_vae.cuh"
 #include "kino_quant.cuh"
 #include "kino_f32.cuh"
@@ -532,7 +533,7 @@ SolLayout sol_layout(int64_t tokens, int64_t heads) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 13; }
+int kino_abi_version(void) { return 14; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -1038,6 +1039,96 @@ kino_status kino_neighborhood_attention(const void* q, const void* k, const void
   launch_pdl(kino::na_attention_kernel, dim3(grid), dim3(kino::ATT_THREADS), smem,
              static_cast<cudaStream_t>(stream), mq, mk, mv, p);
   return check_launch("kino_neighborhood_attention");
+}
+
+kino_status kino_na_qkv_prepare(const void* qkv, int64_t ld, void* q, void* k, void* v,
+                                const void* q_norm_weight, const void* k_norm_weight,
+                                const float* rope_tables, int64_t batch, int64_t frames,
+                                int64_t height, int64_t width, int64_t heads,
+                                const int32_t* section_pairs, float q_scale, float eps,
+                                void* stream) {
+  if (qkv == nullptr || q == nullptr || k == nullptr || v == nullptr ||
+      q_norm_weight == nullptr || k_norm_weight == nullptr || rope_tables == nullptr ||
+      section_pairs == nullptr)
+    return fail(KINO_EINVAL, "kino_na_qkv_prepare: null operand");
+  if (batch < 1 || frames < 1 || height < 1 || width < 1 || heads < 1 || heads > 1024)
+    return fail(KINO_EINVAL, "kino_na_qkv_prepare: empty or oversized shape");
+  const int64_t tokens = batch * frames * height * width;
+  if (tokens > (int64_t(1) << 31) || ld < 3 * heads * 64 || ld % 8)
+    return fail(KINO_EINVAL, "kino_na_qkv_prepare: row stride below 3 * heads * 64 or unaligned");
+  const int pt = section_pairs[0], ph = section_pairs[1], pw = section_pairs[2];
+  if (pt < 0 || ph < 0 || pw < 0 || pt + ph + pw != 32)
+    return fail(KINO_EINVAL, "kino_na_qkv_prepare: the t, h, w sections must hold 32 pairs");
+  if (!aligned16(qkv) || !aligned16(v) || !aligned16(q) || !aligned16(k) ||
+      !aligned16(q_norm_weight) || !aligned16(k_norm_weight))
+    return fail(KINO_EINVAL, "kino_na_qkv_prepare: operands must be 16-byte aligned");
+  kino::NaPrepParams p;
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.ld = ld;
+  p.q = static_cast<__half*>(q);
+  p.k = static_cast<__half*>(k);
+  p.v = static_cast<__half*>(v);
+  p.wq = static_cast<const __nv_bfloat16*>(q_norm_weight);
+  p.wk = static_cast<const __nv_bfloat16*>(k_norm_weight);
+  p.tables = rope_tables;
+  p.tokens = tokens;
+  p.heads = static_cast<int>(heads);
+  p.gt = static_cast<int>(frames);
+  p.gh = static_cast<int>(height);
+  p.gw = static_cast<int>(width);
+  p.pt = pt;
+  p.ph = ph;
+  p.pw = pw;
+  p.q_scale = q_scale;
+  p.eps = eps;
+  const int64_t jobs = tokens * heads * 2;
+  const int64_t blocks = (jobs + kino::NAP_THREADS / 32 - 1) / (kino::NAP_THREADS / 32);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(blocks, 32LL * device_sms()));
+  launch_pdl(kino::na_qkv_prepare_kernel, dim3(grid), dim3(kino::NAP_THREADS), 0,
+             static_cast<cudaStream_t>(stream), p);
+  return check_launch("kino_na_qkv_prepare");
+}
+
+kino_status kino_strided_copy(const void* src, int src_dtype, const int64_t* src_strides,
+                              void* dst, int dst_dtype, const int64_t* dst_strides,
+                              const int64_t* sizes, int ndim, void* stream) {
+  if (src == nullptr || dst == nullptr || src_strides == nullptr || dst_strides == nullptr ||
+      sizes == nullptr)
+    return fail(KINO_EINVAL, "kino_strided_copy: null operand");
+  if (ndim < 1 || ndim > kino::COPY_MAX_DIMS)
+    return fail(KINO_EINVAL, "kino_strided_copy: 1..%d dimensions", kino::COPY_MAX_DIMS);
+  if (src_dtype < KINO_DTYPE_BF16 || src_dtype > KINO_DTYPE_F32 || dst_dtype < KINO_DTYPE_BF16 ||
+      dst_dtype > KINO_DTYPE_F32)
+    return fail(KINO_EINVAL, "kino_strided_copy: dtypes are KINO_DTYPE_BF16, _F16 or _F32");
+  kino::CopyParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.src = src;
+  p.dst = dst;
+  p.ndim = ndim;
+  p.src_type = src_dtype;
+  p.dst_type = dst_dtype;
+  int64_t total = 1;
+  int64_t largest = 1;
+  for (int d = 0; d < kino::COPY_MAX_DIMS; ++d) p.size[d] = 1;
+  for (int d = 0; d < ndim; ++d) {
+    if (sizes[d] < 0) return fail(KINO_EINVAL, "kino_strided_copy: negative size");
+    if (dst_strides[d] < 0) return fail(KINO_EINVAL, "kino_strided_copy: negative destination stride");
+    p.size[d] = sizes[d];
+    p.src_stride[d] = src_strides[d];
+    p.dst_stride[d] = dst_strides[d];
+    total *= sizes[d];
+    largest = std::max(largest, sizes[d]);
+  }
+  if (total == 0) return KINO_OK;
+  p.total = total;
+  const int64_t blocks = (total + kino::COPY_THREADS - 1) / kino::COPY_THREADS;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(blocks, 16LL * device_sms()));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (total <= 0xffffffffLL && largest <= 0xffffffffLL)
+    launch_pdl(kino::strided_copy_kernel<uint32_t>, dim3(grid), dim3(kino::COPY_THREADS), 0, st, p);
+  else
+    launch_pdl(kino::strided_copy_kernel<uint64_t>, dim3(grid), dim3(kino::COPY_THREADS), 0, st, p);
+  return check_launch("kino_strided_copy");
 }
 
 kino_status kino_dense_attention(const void* q, const void* k, const void* v, void* out,

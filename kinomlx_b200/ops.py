@@ -552,6 +552,83 @@ def neighborhood_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     return out
 
 
+def na_qkv_prepare(qkv: torch.Tensor, q_norm_weight: torch.Tensor, k_norm_weight: torch.Tensor,
+                   rope_tables: torch.Tensor, grid: tuple[int, int, int], *, batch: int,
+                   heads: int, section_pairs: tuple[int, int, int], q_scale: float,
+                   eps: float = 1e-6,
+                   out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None,
+                   ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """qkv (tokens, >= 3 * heads * 64) bf16 rows [q | k | v] of a (batch, T, H, W) volume ->
+    fp16 (batch, T, H, W, heads, 64) q, k, v for `neighborhood_attention`: per-head RMSNorm of
+    q and k with their learned weights, q times `q_scale`, the decoder's 3-D RoPE on adjacent
+    pairs ([t | h | w] sections of `section_pairs` pairs, from `rope_tables`)."""
+    _need(qkv, "qkv")
+    _need(q_norm_weight, "q_norm_weight")
+    _need(k_norm_weight, "k_norm_weight")
+    _need(rope_tables, "rope_tables", torch.float32)
+    if qkv.dim() != 2 or qkv.stride(1) != 1:
+        raise ValueError("qkv must be (tokens, width) rows with unit column stride")
+    gt, gh, gw = (int(x) for x in grid)
+    tokens = batch * gt * gh * gw
+    if qkv.shape[0] != tokens or qkv.shape[1] < 3 * heads * 64:
+        raise ValueError(f"qkv {tuple(qkv.shape)} does not hold {tokens} rows of 3 x {heads} heads")
+    shape = (batch, gt, gh, gw, heads, 64)
+    if out is None:
+        out = tuple(torch.empty(shape, device=qkv.device, dtype=torch.float16) for _ in range(3))
+    for t, name in zip(out, "qkv"):
+        _need(t, name, torch.float16)
+        if tuple(t.shape) != shape or not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous {shape}")
+    sec = (ctypes.c_int32 * 3)(*(int(x) for x in section_pairs))
+    with _timed("na_qkv_prepare", 0.0, tokens * heads * 64 * (6.0 + 6.0)):
+        _lib.call("kino_na_qkv_prepare", _ptr(qkv), qkv.stride(0), _ptr(out[0]), _ptr(out[1]),
+                  _ptr(out[2]), _ptr(q_norm_weight), _ptr(k_norm_weight), _ptr(rope_tables),
+                  batch, gt, gh, gw, heads, ctypes.cast(sec, ctypes.c_void_p), q_scale, eps,
+                  _stream())
+    return out
+
+
+_COPY_TYPES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+
+def copy_view(src: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
+    """dst[...] = src[...] for two same-shaped device views of any strides (a zero source stride
+    broadcasts) and dtypes bf16 / fp16 / fp32, in one `kino_strided_copy` launch: permutations,
+    slices, broadcasts and dtype changes without a torch kernel. Returns dst."""
+    if src.shape != dst.shape:
+        raise ValueError(f"copy_view shapes differ: {tuple(src.shape)} vs {tuple(dst.shape)}")
+    if src.dtype not in _COPY_TYPES or dst.dtype not in _COPY_TYPES:
+        raise ValueError("copy_view takes bf16, fp16 or fp32 tensors")
+    if src.device != dst.device or src.device.type != "cuda":
+        raise ValueError("copy_view runs on one CUDA device")
+    dims = [(int(n), int(a), int(b)) for n, a, b in zip(src.shape, src.stride(), dst.stride())
+            if n != 1]
+    # merge neighbours that are contiguous in both views, so most copies stay within 8 dims
+    merged: list[list[int]] = []
+    for n, a, b in dims:
+        if merged and merged[-1][1] == a * n and merged[-1][2] == b * n:
+            merged[-1] = [merged[-1][0] * n, a, b]
+        else:
+            merged.append([n, a, b])
+    if not merged:
+        merged = [[1, 0, 0]]
+    if len(merged) > 8:
+        raise ValueError(f"copy_view supports up to 8 non-mergeable dimensions, got {len(merged)}")
+    nd = len(merged)
+    sizes = (ctypes.c_int64 * nd)(*(m[0] for m in merged))
+    sst = (ctypes.c_int64 * nd)(*(m[1] for m in merged))
+    dstr = (ctypes.c_int64 * nd)(*(m[2] for m in merged))
+    elems = 1
+    for m in merged:
+        elems *= m[0]
+    with _timed("copy", 0.0, elems * (src.element_size() + dst.element_size())):
+        _lib.call("kino_strided_copy", _ptr(src), _COPY_TYPES[src.dtype],
+                  ctypes.cast(sst, ctypes.c_void_p), _ptr(dst), _COPY_TYPES[dst.dtype],
+                  ctypes.cast(dstr, ctypes.c_void_p), ctypes.cast(sizes, ctypes.c_void_p), nd,
+                  _stream())
+    return dst
+
+
 _SOL_WORKSPACES: dict[tuple, torch.Tensor] = {}
 
 

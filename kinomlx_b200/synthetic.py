@@ -155,6 +155,8 @@ def ltx_weights(v, *, seed: int = 0, device="cpu", dtype=torch.bfloat16, blocks:
 
 
 def make_weights(specs, *, seed: int = 0, device="cpu", dtype=torch.bfloat16, std: float = 0.02):
+    """Kinds: "ones", "zeros", "normal" (N(0, std)), "scale" (1 + N(0, 0.1): learned norm
+    scales away from one), "wide" (N(0, 0.2): modulation tables, latent statistics)."""
     gen = torch.Generator(device=device).manual_seed(seed)
     out: dict[str, torch.Tensor] = {}
     for name, shape, kind in specs:
@@ -164,8 +166,80 @@ def make_weights(specs, *, seed: int = 0, device="cpu", dtype=torch.bfloat16, st
             out[name] = torch.zeros(shape, device=device, dtype=dtype)
         else:
             t = torch.randn(shape, generator=gen, device=device, dtype=torch.float32)
-            out[name] = (t * std).to(dtype)
+            if kind == "scale":
+                out[name] = (1.0 + 0.1 * t).to(dtype)
+            elif kind == "wide":
+                out[name] = (0.2 * t).to(dtype)
+            else:
+                out[name] = (t * std).to(dtype)
     return out
+
+
+def diffusion_decoder_weight_specs(cfg):
+    """(name, shape, kind) of the LTX-2.5 diffusion video decoder in draw order; names follow the
+    reference's parameter tree (kinomlx/models/ltx2/video_vae/diffusion_decoder.py:1026-1093)."""
+    specs = [("conv_in.weight", (cfg.stage_channels[0], cfg.latent_channels), "normal"),
+             ("conv_in.bias", (cfg.stage_channels[0],), "normal")]
+
+    def block(pre: str, c: int, diffusion: bool) -> None:
+        hidden = (int(c * 4.0) + 15) // 16 * 16
+        if diffusion:
+            specs.extend([(pre + "context_proj.weight", (c, c), "normal"),
+                          (pre + "context_proj.bias", (c,), "normal"),
+                          (pre + "scale_shift_table", (7, c), "wide")])
+        specs.extend([
+            (pre + "norm1.weight", (c,), "scale"),
+            (pre + "attn.qkv.weight", (3 * c, c), "normal"),
+            (pre + "attn.qkv.bias", (3 * c,), "normal"),
+            (pre + "attn.proj.weight", (c, c), "normal"),
+            (pre + "attn.proj.bias", (c,), "normal"),
+            (pre + "attn.q_norm.weight", (cfg.head_dim,), "scale"),
+            (pre + "attn.k_norm.weight", (cfg.head_dim,), "scale"),
+            (pre + "norm2.weight", (c,), "scale"),
+            (pre + "mlp.w_up.weight", (hidden, c), "normal"),
+            (pre + "mlp.w_gate.weight", (hidden, c), "normal"),
+            (pre + "mlp.w_down.weight", (c, hidden), "normal"),
+        ])
+
+    for s, stride in enumerate(cfg.upsample_strides):
+        c = cfg.stage_channels[s]
+        for i in range(cfg.stage_depths[s]):
+            block(f"det_stages.{s}.{i}.", c, False)
+        prod = stride[0] * stride[1] * stride[2]
+        out = prod * c // cfg.upsample_channel_reductions[s]
+        specs.extend([(f"upsamples.{s}.proj.weight", (out, c), "normal"),
+                      (f"upsamples.{s}.proj.bias", (out,), "normal")])
+    c5 = cfg.stage_channels[-1]
+    pixels = cfg.out_channels * cfg.patch_size ** 2
+    specs.extend([
+        ("t_embedder.linear_1.weight", (cfg.t_emb_dim, 256), "normal"),
+        ("t_embedder.linear_1.bias", (cfg.t_emb_dim,), "normal"),
+        ("t_embedder.linear_2.weight", (cfg.t_emb_dim, cfg.t_emb_dim), "normal"),
+        ("t_embedder.linear_2.bias", (cfg.t_emb_dim,), "normal"),
+        ("conv_in_x_t.weight", (c5, pixels), "normal"),
+        ("conv_in_x_t.bias", (c5,), "normal"),
+        ("shared_adaln.proj.weight", (7 * c5, cfg.t_emb_dim), "normal"),
+        ("shared_adaln.proj.bias", (7 * c5,), "normal"),
+    ])
+    for i in range(cfg.stage_depths[4]):
+        block(f"diff_blocks.{i}.", c5, True)
+    specs.extend([("norm_out.weight", (c5,), "scale"),
+                  ("conv_out.weight", (pixels, c5), "normal"),
+                  ("conv_out.bias", (pixels,), "normal")])
+    return specs
+
+
+def diffusion_decoder_weights(cfg, *, seed: int = 0, device="cpu", dtype=torch.bfloat16,
+                              std: float = 0.02):
+    """Seeded decoder weights (bf16, as a checkpoint binds them) plus the fp32 per-channel latent
+    statistics (std 1 + N(0, 0.1), mean N(0, 0.2))."""
+    w = make_weights(diffusion_decoder_weight_specs(cfg), seed=seed, device=device, dtype=dtype,
+                     std=std)
+    stats = make_weights([("per_channel_statistics.std_of_means", (cfg.latent_channels,), "scale"),
+                          ("per_channel_statistics.mean_of_means", (cfg.latent_channels,), "wide")],
+                         seed=seed + 1, device=device, dtype=torch.float32)
+    w.update(stats)
+    return w
 
 
 def flux_weights(v: FluxVariant, *, seed: int = 0, device="cpu", dtype=torch.bfloat16,
