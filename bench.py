@@ -752,6 +752,9 @@ def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | N
     elif case == "neighborhood":
         run_neighborhood_case(dev)
         return
+    elif case == "diffusion_decoder":
+        run_diffusion_decoder_case(dev)
+        return
     elif case == "f32":
         # fp32 parity mode at config 1: the image stream's FF up projection (1024 x 12288 x 3072,
         # GELU epilogue) and the joint attention over 1536 tokens x 24 heads
@@ -871,6 +874,39 @@ def run_neighborhood_case(dev: torch.device) -> None:
     print(json.dumps({"kernel_case": "neighborhood", "ok": True, "grid": list(grid),
                       "heads": heads, "calls": rows,
                       "reference_m1_max_ms_final_stage": 632.0}))
+
+
+def run_diffusion_decoder_case(dev: torch.device) -> None:
+    """One LTX-2.5 diffusion-decoder decode of a (128, 16, 14, 24) latent into 121 frames of
+    448 x 768 (the video of the reference's documented final-stage attention call: 121 x 112 x
+    192 pixel-patch tokens, four 64-wide heads, 11 x 11 x 11 windows). The other stage widths,
+    depths and windows are a synthetic choice (the reference takes them from a checkpoint):
+    widths 1024 / 512 / 512 / 256 / 256, two blocks per stage, windows 3 x 5 x 5 (stages 1-2) and
+    3 x 7 x 7 (stages 3-4), seeded random weights, one x0 step."""
+    from kinomlx_b200 import ops
+    from kinomlx_b200.ltx2.diffusion_decoder import DiffusionDecoderConfig, DiffusionVideoDecoder
+    from kinomlx_b200.synthetic import diffusion_decoder_weights, normal
+
+    cfg = DiffusionDecoderConfig(
+        head_dim=64, stage_channels=(1024, 512, 512, 256, 256), stage_depths=(2, 2, 2, 2, 2),
+        stage_kernels=((3, 5, 5), (3, 5, 5), (3, 7, 7), (3, 7, 7)),
+        upsample_strides=((1, 2, 2), (2, 1, 1), (2, 2, 2), (2, 2, 2)),
+        upsample_channel_reductions=(2, 1, 2, 1), stage5_kernel=(11, 11, 11))
+    model = DiffusionVideoDecoder(diffusion_decoder_weights(cfg, seed=0, device=dev), cfg, dev)
+    shape = (1, 128, 16, 14, 24)
+    latent = normal(shape, seed=1, device=dev)
+    noise = normal(cfg.working_pixel_shape(shape), seed=2, device=dev)
+    fn = lambda: model(latent, noise)
+    ms = _time(fn, 1, 3, 1)
+    shares = _kernel_shares(fn)
+    video = fn()
+    torch.cuda.synchronize()
+    ops.device_status()
+    frames = video.shape[2]
+    print(json.dumps({"kernel_case": "diffusion_decoder", "ok": True,
+                      "video": list(video.shape), "ms_per_decode": round(ms, 2),
+                      "frames_per_s": round(frames / (ms / 1e3), 1), "kernels": shares,
+                      "finite": bool(torch.isfinite(video.float()).all())}))
 
 
 def run_packed_block(dev: torch.device) -> None:
@@ -1180,7 +1216,7 @@ def main() -> None:
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the configs 3-5 measurements (CFG, video DiT, VAE decode)")
     ap.add_argument("--kernel-case", choices=["gemm", "attention", "conv3d", "conv3d_narrow", "sol", "sol_step",
-                                              "packed_block", "neighborhood", "bandwidth", "f32", "av_step", "kv_step"],
+                                              "packed_block", "neighborhood", "diffusion_decoder", "bandwidth", "f32", "av_step", "kv_step"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     ap.add_argument("--sol-tau", type=float, help="--kernel-case sol: this tau only")
     ap.add_argument("--sol-inputs", choices=["iid", "smooth", "smooth_rope"],

@@ -1081,8 +1081,7 @@ kino_status kino_na_qkv_prepare(const void* qkv, int64_t ld, void* q, void* k, v
   p.pw = pw;
   p.q_scale = q_scale;
   p.eps = eps;
-  const int64_t jobs = tokens * heads * 2;
-  const int64_t blocks = (jobs + kino::NAP_THREADS / 32 - 1) / (kino::NAP_THREADS / 32);
+  const int64_t blocks = (tokens + kino::NAP_THREADS / 32 - 1) / (kino::NAP_THREADS / 32);
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(blocks, 32LL * device_sms()));
   launch_pdl(kino::na_qkv_prepare_kernel, dim3(grid), dim3(kino::NAP_THREADS), 0,
              static_cast<cudaStream_t>(stream), p);
@@ -1121,13 +1120,20 @@ kino_status kino_strided_copy(const void* src, int src_dtype, const int64_t* src
   }
   if (total == 0) return KINO_OK;
   p.total = total;
-  const int64_t blocks = (total + kino::COPY_THREADS - 1) / kino::COPY_THREADS;
+  const bool vec = sizes[ndim - 1] % 8 == 0;
+  const int64_t blocks = (total / (vec ? 8 : 1) + kino::COPY_THREADS - 1) / kino::COPY_THREADS;
   const unsigned grid = static_cast<unsigned>(std::min<int64_t>(blocks, 16LL * device_sms()));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (total <= 0xffffffffLL && largest <= 0xffffffffLL)
-    launch_pdl(kino::strided_copy_kernel<uint32_t>, dim3(grid), dim3(kino::COPY_THREADS), 0, st, p);
+  const bool narrow = total <= 0xffffffffLL && largest <= 0xffffffffLL;
+  const dim3 g(grid), b(kino::COPY_THREADS);
+  if (narrow && vec)
+    launch_pdl(kino::strided_copy_kernel<uint32_t, 8>, g, b, 0, st, p);
+  else if (narrow)
+    launch_pdl(kino::strided_copy_kernel<uint32_t, 1>, g, b, 0, st, p);
+  else if (vec)
+    launch_pdl(kino::strided_copy_kernel<uint64_t, 8>, g, b, 0, st, p);
   else
-    launch_pdl(kino::strided_copy_kernel<uint64_t>, dim3(grid), dim3(kino::COPY_THREADS), 0, st, p);
+    launch_pdl(kino::strided_copy_kernel<uint64_t, 1>, g, b, 0, st, p);
   return check_launch("kino_strided_copy");
 }
 
@@ -1210,6 +1216,23 @@ kino_status kino_rms_norm(const void* x, const void* weight, void* out, int64_t 
       (weight != nullptr && !aligned16(weight)))
     return fail(KINO_ENOTSUPPORTED, "kino_rms_norm: dim %% 8, dim <= 8192, aligned operands");
   if (rows < 1 || rows > 0x7fffffff) return fail(KINO_EINVAL, "kino_rms_norm: rows");
+  if (dim <= 1024) {  // a warp per row
+    const int64_t blocks = (rows + kino::RMS_WARP_THREADS / 32 - 1) / (kino::RMS_WARP_THREADS / 32);
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(blocks, 16LL * device_sms()));
+    auto run = [&](auto kernel) {
+      launch_pdl(kernel, dim3(grid), dim3(kino::RMS_WARP_THREADS), 0,
+                 static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+                 static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out), rows,
+                 static_cast<int>(dim), eps, weight_offset);
+    };
+    if (dim <= 256)
+      run(kino::rms_norm_warp_kernel<1>);
+    else if (dim <= 512)
+      run(kino::rms_norm_warp_kernel<2>);
+    else
+      run(kino::rms_norm_warp_kernel<4>);
+    return check_launch("kino_rms_norm");
+  }
   launch_pdl(kino::rms_norm_kernel, dim3(static_cast<unsigned>(rows)), dim3(kino::ADALN_THREADS), 0, static_cast<cudaStream_t>(stream),
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
       static_cast<__nv_bfloat16*>(out), static_cast<int>(dim), eps, weight_offset);

@@ -8,15 +8,17 @@
 //                          (diffusion_decoder.py:492-517), and the decoder's absolute 3-D RoPE
 //                          on adjacent pairs, the head's pairs split into t, h and w sections
 //                          (RotaryPosition3D, diffusion_decoder.py:322-397). One warp per
-//                          (token, head) of q or k, one pair per lane, fp32 arithmetic, the
-//                          rotation from host-made fp32 cos / sin tables.
+//                          token, one pair per lane, fp32 arithmetic, the rotation from host-made
+//                          fp32 cos / sin tables.
 //   strided_copy_kernel    an N-D copy (N <= 8) with any source and destination strides, zero
 //                          for a broadcast, and a dtype change among bf16, f16 and fp32: the
 //                          decoder's linear pixel shuffles (diffusion_decoder.py:928-971),
 //                          spatial patchify / unpatchify (:49-91), edge and trailing-frame
 //                          padding (:260-308, :1161-1168) and the fp16 <-> bf16 hand-offs
-//                          around the attention. Bandwidth-bound; one element per thread with
-//                          32-bit index arithmetic when the element count allows it.
+//                          around the attention. Bandwidth-bound: eight consecutive elements of
+//                          the innermost dimension per thread where its size allows (16-byte
+//                          loads / stores on a unit-stride side), 32-bit index arithmetic when
+//                          the element count allows it.
 #pragma once
 #include <cuda_fp16.h>
 
@@ -24,7 +26,7 @@
 
 namespace kino {
 
-constexpr int NAP_THREADS = 256;  // 8 warps, each on (token, head) jobs of q then k
+constexpr int NAP_THREADS = 256;  // 8 warps, one token each at a time
 
 struct NaPrepParams {
   const __nv_bfloat16* qkv;  // (tokens, >= 3 * heads * 64): [q | k | v]
@@ -42,14 +44,15 @@ struct NaPrepParams {
   float q_scale, eps;
 };
 
+// One warp per token (32-bit index arithmetic: the host keeps tokens below 2^31): the token's
+// volume position and this lane's rotation are found once, then the warp walks q and k head by
+// head (lane = pair) and copies the token's v row, 16 bytes per lane.
 __global__ void __launch_bounds__(NAP_THREADS) na_qkv_prepare_kernel(const NaPrepParams p) {
   griddep_wait();
   griddep_launch();
   const int lane = static_cast<int>(threadIdx.x & 31);
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (NAP_THREADS / 32);
-  const int64_t jobs = p.tokens * p.heads * 2;
   const int width = p.heads * 64;
-  // this lane's pair: section and index within it (the same for every job)
+  // this lane's pair: section and index within it (the same for every token)
   int sec, idx;
   if (lane < p.pt) {
     sec = 0;
@@ -63,61 +66,59 @@ __global__ void __launch_bounds__(NAP_THREADS) na_qkv_prepare_kernel(const NaPre
   }
   const float* cos_tab = p.tables;
   int tab_pairs = p.pt;
-  if (sec >= 1) cos_tab += 2 * static_cast<int64_t>(p.gt) * p.pt;
-  if (sec == 1) tab_pairs = p.ph;
+  int axis_len = p.gt;
+  if (sec >= 1) cos_tab += 2 * p.gt * p.pt;
+  if (sec == 1) {
+    tab_pairs = p.ph;
+    axis_len = p.gh;
+  }
   if (sec == 2) {
-    cos_tab += 2 * static_cast<int64_t>(p.gh) * p.ph;
+    cos_tab += 2 * p.gh * p.ph;
     tab_pairs = p.pw;
+    axis_len = p.gw;
   }
-  const int64_t axis_len = sec == 0 ? p.gt : (sec == 1 ? p.gh : p.gw);
   const float* sin_tab = cos_tab + axis_len * tab_pairs;
-  for (int64_t job = static_cast<int64_t>(blockIdx.x) * (NAP_THREADS / 32) + (threadIdx.x >> 5);
-       job < jobs; job += warps) {
-    const int which = static_cast<int>(job & 1);  // 0: q, 1: k
-    const int64_t th = job >> 1;
-    const int head = static_cast<int>(th % p.heads);
-    const int64_t tok = th / p.heads;
-    const int64_t in_vol = tok % (static_cast<int64_t>(p.gt) * p.gh * p.gw);
-    const int w = static_cast<int>(in_vol % p.gw);
-    const int h = static_cast<int>((in_vol / p.gw) % p.gh);
-    const int t = static_cast<int>(in_vol / (static_cast<int64_t>(p.gw) * p.gh));
-    const __nv_bfloat16* src = p.qkv + tok * p.ld + which * width + head * 64 + 2 * lane;
-    const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src));
-    float ss = x.x * x.x + x.y * x.y;
+  const float2 wq = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(p.wq + 2 * lane));
+  const float2 wk = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(p.wk + 2 * lane));
+  const int vol = p.gt * p.gh * p.gw;
+  const int tokens = static_cast<int>(p.tokens);
+  const int warps = static_cast<int>(gridDim.x) * (NAP_THREADS / 32);
+  for (int tok = static_cast<int>(blockIdx.x) * (NAP_THREADS / 32) + (threadIdx.x >> 5);
+       tok < tokens; tok += warps) {
+    const int in_vol = tok % vol;
+    const int pos = sec == 0 ? in_vol / (p.gh * p.gw)
+                             : (sec == 1 ? (in_vol / p.gw) % p.gh : in_vol % p.gw);
+    const float c = cos_tab[pos * tab_pairs + idx];
+    const float s = sin_tab[pos * tab_pairs + idx];
+    const __nv_bfloat16* row = p.qkv + static_cast<int64_t>(tok) * p.ld;
+    const int64_t orow = static_cast<int64_t>(tok) * width;
+    for (int j = 0; j < 2 * p.heads; ++j) {
+      const int which = j >= p.heads ? 1 : 0;  // 0: q, 1: k
+      const int col = j * 64 + 2 * lane;       // q heads then k heads, back to back
+      const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(row + col));
+      float ss = x.x * x.x + x.y * x.y;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = rsqrtf(ss * (1.0f / 64.0f) + p.eps);
-    const float2 wv =
-        unpack_bf16x2(*reinterpret_cast<const uint32_t*>((which ? p.wk : p.wq) + 2 * lane));
-    float e = x.x * inv * wv.x;
-    float o = x.y * inv * wv.y;
-    if (which == 0) {
-      e *= p.q_scale;
-      o *= p.q_scale;
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = rsqrtf(ss * (1.0f / 64.0f) + p.eps);
+      const float2 wv = which ? wk : wq;
+      const float scale = which ? 1.0f : p.q_scale;
+      const float e = x.x * inv * wv.x * scale;
+      const float o = x.y * inv * wv.y * scale;
+      const __half2 r = __floats2half2_rn(e * c - o * s, e * s + o * c);
+      *reinterpret_cast<__half2*>((which ? p.k : p.q) + orow + (col - which * width)) = r;
     }
-    const int pos = sec == 0 ? t : (sec == 1 ? h : w);
-    const float c = cos_tab[static_cast<int64_t>(pos) * tab_pairs + idx];
-    const float s = sin_tab[static_cast<int64_t>(pos) * tab_pairs + idx];
-    const __half2 r = __floats2half2_rn(e * c - o * s, e * s + o * c);
-    __half* dst = (which ? p.k : p.q) + tok * width + head * 64 + 2 * lane;
-    *reinterpret_cast<__half2*>(dst) = r;
-  }
-  // v: 8 columns per thread
-  const int64_t vchunks = p.tokens * (width / 8);
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * NAP_THREADS + threadIdx.x; i < vchunks;
-       i += static_cast<int64_t>(gridDim.x) * NAP_THREADS) {
-    const int64_t tok = i / (width / 8);
-    const int col = static_cast<int>(i % (width / 8)) * 8;
-    const uint4 raw = *reinterpret_cast<const uint4*>(p.qkv + tok * p.ld + 2 * width + col);
-    const uint32_t r4[4] = {raw.x, raw.y, raw.z, raw.w};
-    uint32_t h4[4];
+    for (int ch = lane; ch < width / 8; ch += 32) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(row + 2 * width + ch * 8);
+      const uint32_t r4[4] = {raw.x, raw.y, raw.z, raw.w};
+      uint32_t h4[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack_bf16x2(r4[j]);
-      const __half2 hv = __floats2half2_rn(f.x, f.y);
-      h4[j] = *reinterpret_cast<const uint32_t*>(&hv);
+      for (int jj = 0; jj < 4; ++jj) {
+        const float2 f = unpack_bf16x2(r4[jj]);
+        const __half2 hv = __floats2half2_rn(f.x, f.y);
+        h4[jj] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+      *reinterpret_cast<uint4*>(p.v + orow + ch * 8) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
     }
-    *reinterpret_cast<uint4*>(p.v + tok * width + col) = make_uint4(h4[0], h4[1], h4[2], h4[3]);
   }
 }
 
@@ -152,29 +153,108 @@ __device__ __forceinline__ void copy_store(void* base, int type, int64_t i, floa
     static_cast<float*>(base)[i] = v;
 }
 
+template <int VEC>
+__device__ __forceinline__ void copy_load_run(const void* base, int type, int64_t off,
+                                              int64_t stride, float (&v)[VEC]) {
+  if (VEC == 8 && stride == 1) {
+    if (type != COPY_F32) {
+      const void* ptr = static_cast<const uint16_t*>(base) + off;
+      if ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0) {
+        const uint4 raw = *static_cast<const uint4*>(ptr);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f;
+          if (type == COPY_BF16) {
+            f = unpack_bf16x2(w[j]);
+          } else {
+            f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+          }
+          v[2 * j] = f.x;
+          v[2 * j + 1] = f.y;
+        }
+        return;
+      }
+    } else {
+      const float* ptr = static_cast<const float*>(base) + off;
+      if ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0) {
+        const float4 a = reinterpret_cast<const float4*>(ptr)[0];
+        const float4 b = reinterpret_cast<const float4*>(ptr)[1];
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+        v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+        return;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) v[j] = copy_load(base, type, off + j * stride);
+}
+
+template <int VEC>
+__device__ __forceinline__ void copy_store_run(void* base, int type, int64_t off, int64_t stride,
+                                               const float (&v)[VEC]) {
+  if (VEC == 8 && stride == 1) {
+    if (type != COPY_F32) {
+      void* ptr = static_cast<uint16_t*>(base) + off;
+      if ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (type == COPY_BF16) {
+            w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+          } else {
+            const __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+            w[j] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+        }
+        *static_cast<uint4*>(ptr) = make_uint4(w[0], w[1], w[2], w[3]);
+        return;
+      }
+    } else {
+      float* ptr = static_cast<float*>(base) + off;
+      if ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0) {
+        reinterpret_cast<float4*>(ptr)[0] = make_float4(v[0], v[1], v[2], v[3]);
+        reinterpret_cast<float4*>(ptr)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        return;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) copy_store(base, type, off + j * stride, v[j]);
+}
+
 // Idx: uint32_t when every size and the element count fit 32 bits, else uint64_t. Dimension
-// ndim - 1 is the fastest-varying one of the element order.
-template <typename Idx>
+// ndim - 1 is the fastest-varying one of the element order; each thread moves VEC consecutive
+// elements of it (VEC divides its size).
+template <typename Idx, int VEC>
 __global__ void __launch_bounds__(COPY_THREADS) strided_copy_kernel(const CopyParams p) {
   griddep_wait();
   griddep_launch();
+  const int last = p.ndim - 1;
   Idx size[COPY_MAX_DIMS];
 #pragma unroll
   for (int d = 0; d < COPY_MAX_DIMS; ++d) size[d] = static_cast<Idx>(p.size[d]);
-  for (Idx e = static_cast<Idx>(blockIdx.x) * COPY_THREADS + threadIdx.x;
-       e < static_cast<Idx>(p.total); e += static_cast<Idx>(gridDim.x) * COPY_THREADS) {
-    Idx rest = e;
-    int64_t so = 0, dof = 0;
+  const Idx inner = static_cast<Idx>(p.size[last] / VEC);
+  const int64_t s_last = p.src_stride[last], d_last = p.dst_stride[last];
+  const Idx runs = static_cast<Idx>(p.total / VEC);
+  for (Idx e = static_cast<Idx>(blockIdx.x) * COPY_THREADS + threadIdx.x; e < runs;
+       e += static_cast<Idx>(gridDim.x) * COPY_THREADS) {
+    Idx rest = e / inner;
+    const int64_t c_last = static_cast<int64_t>(e - rest * inner) * VEC;
+    int64_t so = c_last * s_last, dof = c_last * d_last;
 #pragma unroll
-    for (int d = COPY_MAX_DIMS - 1; d >= 0; --d) {
-      if (d < p.ndim) {
-        const Idx c = rest % size[d];
-        rest /= size[d];
+    for (int d = COPY_MAX_DIMS - 2; d >= 0; --d) {
+      if (d < last) {
+        const Idx q = rest / size[d];
+        const Idx c = rest - q * size[d];
+        rest = q;
         so += static_cast<int64_t>(c) * p.src_stride[d];
         dof += static_cast<int64_t>(c) * p.dst_stride[d];
       }
     }
-    copy_store(p.dst, p.dst_type, dof, copy_load(p.src, p.src_type, so));
+    float v[VEC];
+    copy_load_run<VEC>(p.src, p.src_type, so, s_last, v);
+    copy_store_run<VEC>(p.dst, p.dst_type, dof, d_last, v);
   }
 }
 

@@ -297,6 +297,53 @@ __global__ void __launch_bounds__(ADALN_THREADS)
   }
 }
 
+// RMSNorm of rows no wider than 1024: one warp per row, NCH 16-byte chunks per lane (the
+// block-per-row form above leaves most of its threads idle on narrow rows); same fp32 math.
+constexpr int RMS_WARP_THREADS = 256;
+template <int NCH>
+__global__ void __launch_bounds__(RMS_WARP_THREADS)
+    rms_norm_warp_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                         __nv_bfloat16* __restrict__ out, int64_t rows, int dim, float eps,
+                         float offset) {
+  griddep_wait();
+  griddep_launch();
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const int nvec = dim >> 3;
+  const int64_t wpb = RMS_WARP_THREADS / 32;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * wpb + (threadIdx.x >> 5); row < rows;
+       row += static_cast<int64_t>(gridDim.x) * wpb) {
+    const __nv_bfloat16* xr = x + row * dim;
+    float v[NCH][8];
+    float q = 0.0f;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int i = lane + c * 32;
+      if (i < nvec) {
+        load8(xr + i * 8, v[c]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q = fmaf(v[c][j], v[c][j], q);
+      }
+    }
+    const float inv = rsqrtf(warp_sum(q) / static_cast<float>(dim) + eps);
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int i = lane + c * 32;
+      if (i < nvec) {
+        float fw[8];
+        if (w != nullptr) load8(w + i * 8, fw);
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float r = v[c][j] * inv;
+          if (w != nullptr) r *= fw[j] + offset;
+          o[j] = r;
+        }
+        store8(out + row * dim + i * 8, o);
+      }
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------- QK norm + RoPE
 // In place on token-major projections (batch, tokens, heads * 128) with row stride ld:
 //   norm_kind 0: none; 1: RMSNorm per head (weight[128], kinomlx/models/flux2/transformer.py:68-75);

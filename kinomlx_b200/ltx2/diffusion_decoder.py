@@ -134,6 +134,32 @@ def rope_tables(head_dim: int, grid: tuple[int, int, int], base: float = 10_000.
     return torch.cat(parts)
 
 
+def patchify_spatial(x: torch.Tensor, patch_size: int) -> torch.Tensor:
+    """Space-to-depth of (B, C, F, H, W) into (B, C * p * p, F, H / p, W / p) with the LTX
+    channel packing c * p * p + pw * p + ph (diffusion_decoder.py:49-72), one strided copy."""
+    b, c, f, h, w = x.shape
+    p = patch_size
+    if h % p or w % p:
+        raise ValueError(f"pixel dimensions {h}x{w} are not divisible by patch size {p}")
+    out = torch.empty((b, c * p * p, f, h // p, w // p), device=x.device, dtype=x.dtype)
+    src = x.view(b, c, f, h // p, p, w // p, p).permute(0, 1, 6, 4, 2, 3, 5)
+    ops.copy_view(src, out.view(b, c, p, p, f, h // p, w // p))
+    return out
+
+
+def unpatchify_spatial(x: torch.Tensor, patch_size: int) -> torch.Tensor:
+    """Depth-to-space inverse of `patchify_spatial` (diffusion_decoder.py:75-91)."""
+    b, pc, f, h, w = x.shape
+    p = patch_size
+    if pc % (p * p):
+        raise ValueError(f"packed channel count {pc} is not divisible by {p * p}")
+    c = pc // (p * p)
+    out = torch.empty((b, c, f, h * p, w * p), device=x.device, dtype=x.dtype)
+    src = x.view(b, c, p, p, f, h, w).permute(0, 1, 4, 5, 3, 6, 2)
+    ops.copy_view(src, out.view(b, c, f, h, p, w, p))
+    return out
+
+
 class DiffusionVideoDecoder:
     """Device weights and the decode of the reference's DiffusionVideoDecoder."""
 

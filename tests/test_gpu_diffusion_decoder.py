@@ -16,7 +16,7 @@ import torch
 from oracle import diffusion_decoder as dref
 from kinomlx_b200 import ops
 from kinomlx_b200.ltx2.diffusion_decoder import (DiffusionDecoderConfig, DiffusionVideoDecoder,
-                                                 rope_tables)
+                                                 patchify_spatial, rope_tables, unpatchify_spatial)
 from kinomlx_b200.synthetic import diffusion_decoder_weights, normal
 from parity_metrics import metrics, show
 
@@ -82,6 +82,13 @@ def test_copy_view_matches_torch(cuda_device):
     ops.copy_view(row.expand(3, 4, 3, 6, 7, 2), big[:, :, 1:])
     assert torch.equal(big[:, :, 1:], row.expand(3, 4, 3, 6, 7, 2))
     assert not big[:, :, 0].any()
+
+
+def test_patchify_matches_oracle(cuda_device):
+    x = normal((2, 3, 5, 16, 24), seed=8)
+    packed = patchify_spatial(x.to(cuda_device), 4)
+    assert torch.equal(packed.cpu(), dref.patchify_spatial(x, 4))
+    assert torch.equal(unpatchify_spatial(packed, 4).cpu(), x)
 
 
 def test_context_stages_match_oracle(model_and_weights):
