@@ -672,7 +672,8 @@ def run_secondary(world: int, rank: int, local: int) -> dict:
     return out
 
 
-def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | None = None) -> None:
+def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | None = None,
+                    na_grid: tuple[int, int, int] = (121, 112, 192)) -> None:
     """Three launches of one kernel at a workload shape (for ncu captures). `gemm`: the single
     block's fused projection, 4608 x 21504 x 3072, with its in-step epilogue (per-head RMSNorm +
     RoPE on k and q, GELU on the MLP columns); `attention`: the joint attention over 4608 tokens
@@ -750,7 +751,7 @@ def run_kernel_case(case: str, sol_tau: float | None = None, sol_inputs: str | N
         run_packed_block(dev)
         return
     elif case == "neighborhood":
-        run_neighborhood_case(dev)
+        run_neighborhood_case(dev, na_grid)
         return
     elif case == "diffusion_decoder":
         run_diffusion_decoder_case(dev)
@@ -845,7 +846,7 @@ def run_av_step(dev: torch.device) -> None:
                       "kernels": _kernel_shares(step)}))
 
 
-def run_neighborhood_case(dev: torch.device) -> None:
+def run_neighborhood_case(dev: torch.device, grid: tuple[int, int, int] = (121, 112, 192)) -> None:
     """The LTX-2.5 diffusion decoder's neighborhood attention at its final-stage call (121 x 112 x
     192 queries, four 64-wide heads, 11 x 11 x 11 windows: the call the reference documents at
     632 ms on an M1 Max, kinomlx/models/ltx2/kernels/neighborhood_attention.py:21-25) and the
@@ -854,7 +855,7 @@ def run_neighborhood_case(dev: torch.device) -> None:
     outside a query's window."""
     from kinomlx_b200 import ops
 
-    grid, heads = (121, 112, 192), 4
+    heads = 4
     shape = (1, *grid, heads, 64)
     g = torch.Generator(device=dev).manual_seed(5)
     q = (torch.randn(shape, generator=g, device=dev) * 0.125).half()
@@ -1219,11 +1220,14 @@ def main() -> None:
                                               "packed_block", "neighborhood", "diffusion_decoder", "bandwidth", "f32", "av_step", "kv_step"],
                     help="run 3 launches of one kernel and exit (for ncu captures)")
     ap.add_argument("--sol-tau", type=float, help="--kernel-case sol: this tau only")
+    ap.add_argument("--na-grid", default="121,112,192",
+                    help="--kernel-case neighborhood: the T,H,W token grid")
     ap.add_argument("--sol-inputs", choices=["iid", "smooth", "smooth_rope"],
                     help="--kernel-case sol: this input family only")
     args = ap.parse_args()
     if args.kernel_case:
-        run_kernel_case(args.kernel_case, args.sol_tau, args.sol_inputs)
+        run_kernel_case(args.kernel_case, args.sol_tau, args.sol_inputs,
+                        tuple(int(x) for x in args.na_grid.split(",")))
         return
     if args.warmup < 3:
         log("warm-up raised to 3 steps (timing rule)")
