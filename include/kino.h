@@ -33,7 +33,7 @@ typedef int kino_status;
 #define KINO_ECUDA 3
 #define KINO_ETIMEOUT 4
 
-/* ABI version of this header (14); bumped on any signature change or addition. */
+/* ABI version of this header (15); bumped on any signature change or addition. */
 int kino_abi_version(void);
 
 /* One-line description of the last error on the calling thread ("" if none). */
@@ -262,6 +262,13 @@ kino_status kino_neighborhood_attention(const void* q, const void* k, const void
                                         int64_t batch, int64_t frames, int64_t height,
                                         int64_t width, int64_t heads, const int32_t* window,
                                         void* stream);
+
+/* The same with the output written as KINO_DTYPE_F16 or KINO_DTYPE_BF16 (rounded once from the
+ * fp32 result): the diffusion decoder hands the attention straight to its bf16 proj product. */
+kino_status kino_neighborhood_attention_ex(const void* q, const void* k, const void* v, void* out,
+                                           int out_dtype, int64_t batch, int64_t frames,
+                                           int64_t height, int64_t width, int64_t heads,
+                                           const int32_t* window, void* stream);
 
 /* ------------------------------------------------------------------ diffusion video decoder */
 /* The qkv projection rows of a diffusion-decoder attention -> the neighborhood attention's

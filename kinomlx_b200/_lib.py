@@ -269,6 +269,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "kino_sol_attention": (c_int, [POINTER(SolAttentionArgs), P]),
     "kino_attention_workspace_size": (I64, [POINTER(AttentionArgs), I64]),
     "kino_neighborhood_attention": (c_int, [P, P, P, P, I64, I64, I64, I64, I64, P, P]),
+    "kino_neighborhood_attention_ex": (c_int, [P, P, P, P, c_int, I64, I64, I64, I64, I64, P, P]),
     "kino_na_qkv_prepare": (
         c_int,
         [P, I64, P, P, P, P, P, P, I64, I64, I64, I64, I64, P, F, F, P],

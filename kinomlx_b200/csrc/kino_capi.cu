@@ -533,7 +533,7 @@ SolLayout sol_layout(int64_t tokens, int64_t heads) {
 
 extern "C" {
 
-int kino_abi_version(void) { return 14; }
+int kino_abi_version(void) { return 15; }
 
 const char* kino_last_error(void) { return g_err; }
 
@@ -990,8 +990,18 @@ kino_status kino_neighborhood_attention(const void* q, const void* k, const void
                                         int64_t batch, int64_t frames, int64_t height,
                                         int64_t width, int64_t heads, const int32_t* window,
                                         void* stream) {
+  return kino_neighborhood_attention_ex(q, k, v, out, KINO_DTYPE_F16, batch, frames, height, width,
+                                        heads, window, stream);
+}
+
+kino_status kino_neighborhood_attention_ex(const void* q, const void* k, const void* v, void* out,
+                                           int out_dtype, int64_t batch, int64_t frames,
+                                           int64_t height, int64_t width, int64_t heads,
+                                           const int32_t* window, void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || window == nullptr)
     return fail(KINO_EINVAL, "kino_neighborhood_attention: null argument");
+  if (out_dtype != KINO_DTYPE_F16 && out_dtype != KINO_DTYPE_BF16)
+    return fail(KINO_EINVAL, "kino_neighborhood_attention: out_dtype is KINO_DTYPE_F16 or _BF16");
   if (batch < 1 || frames < 1 || height < 1 || width < 1 || heads < 1 || heads > 4096 ||
       batch * frames > 0x7fffffff || height > 0x7fffffff || width > 0x7fffffff)
     return fail(KINO_EINVAL, "kino_neighborhood_attention: empty or oversized grid");
@@ -1017,6 +1027,7 @@ kino_status kino_neighborhood_attention(const void* q, const void* k, const void
   p.boxes_w = static_cast<int>((width + kino::NA_QW - 1) / kino::NA_QW);
   p.scale_log2 = 1.4426950408889634f;  // the queries arrive scaled: softmax(q k^T)
   p.out = static_cast<__half*>(out);
+  p.out_bf16 = out_dtype == KINO_DTYPE_BF16 ? 1 : 0;
   const int64_t items = batch * heads * p.boxes_t * p.boxes_h * p.boxes_w;
   if (items > 0x7fffffff)
     return fail(KINO_ENOTSUPPORTED, "kino_neighborhood_attention: too many query tiles");

@@ -400,6 +400,14 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
                : "memory");
 }
+// The same arrive without release ordering, for the tensor-memory-free signal of an epilogue
+// warp: its tcgen05.ld reads have completed (tcgen05.wait::ld) before it arrives, and it has no
+// memory writes the waiting MMA thread depends on, so the arrive need not wait for the warp's
+// global stores to be acknowledged the way a cluster-scope release does.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
 // The even CTA of a pair owns the barriers that 2-SM TMA loads complete on: clearing this bit of a
 // shared-memory address gives the same offset in the pair's even CTA.
 constexpr uint32_t kPairLeaderMask = 0xFEFFFFFFu;

@@ -92,20 +92,37 @@ __global__ void __launch_bounds__(NAP_THREADS) na_qkv_prepare_kernel(const NaPre
     const float s = sin_tab[pos * tab_pairs + idx];
     const __nv_bfloat16* row = p.qkv + static_cast<int64_t>(tok) * p.ld;
     const int64_t orow = static_cast<int64_t>(tok) * width;
-    for (int j = 0; j < 2 * p.heads; ++j) {
-      const int which = j >= p.heads ? 1 : 0;  // 0: q, 1: k
-      const int col = j * 64 + 2 * lane;       // q heads then k heads, back to back
-      const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(row + col));
-      float ss = x.x * x.x + x.y * x.y;
+    // q heads then k heads, back to back: four (head, q/k) segments at a time, their loads and
+    // shuffle reductions interleaved
+    const int jobs = 2 * p.heads;
+    for (int j0 = 0; j0 < jobs; j0 += 4) {
+      float2 x[4];
+      float ss[4];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float inv = rsqrtf(ss * (1.0f / 64.0f) + p.eps);
-      const float2 wv = which ? wk : wq;
-      const float scale = which ? 1.0f : p.q_scale;
-      const float e = x.x * inv * wv.x * scale;
-      const float o = x.y * inv * wv.y * scale;
-      const __half2 r = __floats2half2_rn(e * c - o * s, e * s + o * c);
-      *reinterpret_cast<__half2*>((which ? p.k : p.q) + orow + (col - which * width)) = r;
+      for (int u = 0; u < 4; ++u) {
+        const int j = min(j0 + u, jobs - 1);
+        x[u] = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(row + j * 64 + 2 * lane));
+        ss[u] = x[u].x * x[u].x + x[u].y * x[u].y;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = j0 + u;
+        if (j < jobs) {
+          const int which = j >= p.heads ? 1 : 0;  // 0: q, 1: k
+          const float inv = rsqrtf(ss[u] * (1.0f / 64.0f) + p.eps);
+          const float2 wv = which ? wk : wq;
+          const float scale = which ? 1.0f : p.q_scale;
+          const float e = x[u].x * inv * wv.x * scale;
+          const float o = x[u].y * inv * wv.y * scale;
+          const __half2 r = __floats2half2_rn(e * c - o * s, e * s + o * c);
+          *reinterpret_cast<__half2*>((which ? p.k : p.q) + orow + (j - which * p.heads) * 64 +
+                                      2 * lane) = r;
+        }
+      }
     }
     for (int ch = lane; ch < width / 8; ch += 32) {
       const uint4 raw = *reinterpret_cast<const uint4*>(row + 2 * width + ch * 8);

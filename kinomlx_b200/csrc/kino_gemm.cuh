@@ -706,7 +706,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                         tmem_base + ((quarter * 32) << 16) + acc * BN + half * (BN / 2), BN / 2);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(leader_tempty0 + acc * 8);
+      if (lane == 0) mbar_arrive_cluster_relaxed(leader_tempty0 + acc * 8);
     }
     // scattered rows went to other GPUs: make them visible before the next kernel signals
     if (e.scatter_ptrs != nullptr) __threadfence_system();

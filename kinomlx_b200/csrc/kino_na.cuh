@@ -31,7 +31,8 @@ struct NaParams {
   int kt, kh, kw;                // window
   int boxes_t, boxes_h, boxes_w;  // query boxes per axis
   float scale_log2;               // log2(e): the queries arrive scaled
-  __half* out;
+  __half* out;                    // fp16, or bf16 bits when out_bf16
+  int out_bf16;
 };
 
 // Shared memory: Q tiles [buffer][tile] (16 KB each), the K/V ring [slot] (16 + 16 KB), the
@@ -438,7 +439,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int c = g4 * 8 + 2 * e;
-              w4[e] = pack_f16x2(__uint_as_float(ov[c]) * inv_l, __uint_as_float(ov[c + 1]) * inv_l);
+              const float o0 = __uint_as_float(ov[c]) * inv_l;
+              const float o1 = __uint_as_float(ov[c + 1]) * inv_l;
+              w4[e] = p.out_bf16 ? pack_bf16x2(o0, o1) : pack_f16x2(o0, o1);
             }
             reinterpret_cast<uint4*>(dst)[g4] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }

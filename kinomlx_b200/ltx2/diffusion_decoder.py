@@ -6,7 +6,8 @@ followed by a linear pixel shuffle (the context), then a pixel-space diffusion s
 add the projected context and modulate their norms by a shared timestep AdaLN, one x0 step by
 default. Every product runs on tcgen05 GEMMs with fused epilogues (bias, residual add, SwiGLU),
 every attention on the exact windowed kernel `kino_neighborhood_attention`; the q/k RMSNorm, q
-scale and 3-D RoPE run in `kino_na_qkv_prepare`, which also hands q, k, v over in fp16; norms,
+scale and 3-D RoPE run in `kino_na_qkv_prepare`, which also hands q, k, v over in fp16 (the
+attention writes bf16 back for the proj product); norms,
 modulation and the layout moves (pixel shuffles, spatial patchify / unpatchify, edge padding)
 run in the library's own bandwidth kernels. Activations are bf16 (the reference's default
 compute dtype), the attention operands fp16 with fp32 scores, as on the reference's kernel
@@ -225,12 +226,10 @@ class DiffusionVideoDecoder:
                                      batch=1, heads=heads, section_pairs=self.sections,
                                      q_scale=self.cfg.head_dim ** -0.5, eps=1e-6)
         del qkv
-        o = ops.neighborhood_attention(q, k, v, window=tuple(window))
-        del k, v
-        o16 = torch.empty((x.shape[0], c), device=self.device, dtype=BF16)
-        ops.copy_view(o.view(x.shape[0], c), o16)
-        del o, q
-        return self._linear(o16, pre + "proj", residual=x)
+        o = torch.empty(q.shape, device=self.device, dtype=BF16)
+        ops.neighborhood_attention(q, k, v, window=tuple(window), out=o)
+        del q, k, v
+        return self._linear(o.view(x.shape[0], c), pre + "proj", residual=x)
 
     def _mlp(self, x: torch.Tensor, normed: torch.Tensor, pre: str) -> torch.Tensor:
         """x += w_down(silu(w_gate(n)) * w_up(n)) (TiledSwiGLU, :715-737)."""

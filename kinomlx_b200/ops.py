@@ -526,7 +526,8 @@ def neighborhood_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                            out: torch.Tensor | None = None) -> torch.Tensor:
     """Exact 3-D neighborhood attention: q, k, v contiguous (batch, T, H, W, heads, 64) fp16 on
     the GPU, the queries already scaled; each query attends to the window's keys around it, the
-    window shifted inward at the grid's edges. Any odd window no larger than the grid."""
+    window shifted inward at the grid's edges. Any odd window no larger than the grid. `out`
+    fp16 (default) or bf16."""
     for t, name in ((q, "q"), (k, "k"), (v, "v")):
         _need(t, name, torch.float16)
         if not t.is_contiguous():
@@ -537,7 +538,9 @@ def neighborhood_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         raise ValueError("the window has three sizes (frames, height, width)")
     if out is None:
         out = torch.empty_like(q)
-    _need(out, "out", torch.float16)
+    if out.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("out is fp16 or bf16")
+    _need(out, "out", out.dtype)
     if out.shape != q.shape or not out.is_contiguous():
         raise ValueError("out must be contiguous and shaped like q")
     b, gt, gh, gw, heads, dim = q.shape
@@ -547,8 +550,9 @@ def neighborhood_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         keys *= int(x)
     with _timed("neighborhood_attention", 4.0 * b * gt * gh * gw * heads * keys * dim,
                 4.0 * q.numel() * 2):
-        _lib.call("kino_neighborhood_attention", _ptr(q), _ptr(k), _ptr(v), _ptr(out), b, gt, gh,
-                  gw, heads, ctypes.cast(win, ctypes.c_void_p), _stream())
+        _lib.call("kino_neighborhood_attention_ex", _ptr(q), _ptr(k), _ptr(v), _ptr(out),
+                  _COPY_TYPES[out.dtype], b, gt, gh, gw, heads, ctypes.cast(win, ctypes.c_void_p),
+                  _stream())
     return out
 
 

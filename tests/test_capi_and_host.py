@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     for name in names:
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
-    assert lib.kino_abi_version() == 14
+    assert lib.kino_abi_version() == 15
     assert _lib.last_error() == ""
 
 

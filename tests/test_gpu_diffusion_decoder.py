@@ -84,6 +84,19 @@ def test_copy_view_matches_torch(cuda_device):
     assert not big[:, :, 0].any()
 
 
+def test_neighborhood_attention_bf16_output(cuda_device):
+    """The decoder's form of the attention: the same fp32 result rounded to bf16 once."""
+    shape = (1, 5, 9, 17, 2, 64)
+    q, k, v = (normal(shape, seed=s, dtype=torch.float16).to(cuda_device) for s in (51, 52, 53))
+    q = q * 0.125
+    half = ops.neighborhood_attention(q, k, v, window=(3, 5, 5))
+    bf = torch.empty(shape, device=cuda_device, dtype=torch.bfloat16)
+    ops.neighborhood_attention(q, k, v, window=(3, 5, 5), out=bf)
+    torch.cuda.synchronize()
+    diff = (bf.float() - half.float()).abs()
+    assert float((diff / half.float().abs().clamp_min(1e-3)).max()) <= 2 ** -8
+
+
 def test_patchify_matches_oracle(cuda_device):
     x = normal((2, 3, 5, 16, 24), seed=8)
     packed = patchify_spatial(x.to(cuda_device), 4)
