@@ -125,6 +125,34 @@ __device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int t, int&
   mt = rem - b * s.tiles_m;
 }
 
+// 16 bf16 (32 bytes) of one row: one 256-bit store where the address is 32-byte aligned (every
+// L1 -> L2 sector then arrives whole), else two 16-byte stores.
+__device__ __forceinline__ void store_16(__nv_bfloat16* dst, const uint32_t (&w)[8]) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]),
+                 "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+  } else {
+    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+// The first min(32, limit) of 32 packed bf16 columns of one row (limit a multiple of 8).
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (&w)[16],
+                                            int limit) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (h * 16 + 16 <= limit) {
+      const uint32_t (&part)[8] = *reinterpret_cast<const uint32_t(*)[8]>(w + h * 8);
+      store_16(dst + h * 16, part);
+    } else if (h * 16 + 8 <= limit) {
+      reinterpret_cast<uint4*>(dst + h * 16)[0] =
+          make_uint4(w[h * 8], w[h * 8 + 1], w[h * 8 + 2], w[h * 8 + 3]);
+    }
+  }
+}
+
 // Apply the epilogue to 32 consecutive columns [col0, col0 + 32) of one output row and store.
 __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const GemmEpi& e,
                                                     __nv_bfloat16* out, int b, int row,
@@ -165,15 +193,10 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j] = bf16_round(silu_fast_f32(v[j])) * v[16 + j];
     __nv_bfloat16* dst = out + out_off + e.act_col_begin + (col0 - e.act_col_begin) / 2;
+    uint32_t w[8];
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      uint4 w;
-      w.x = pack_bf16x2(o[g * 8 + 0], o[g * 8 + 1]);
-      w.y = pack_bf16x2(o[g * 8 + 2], o[g * 8 + 3]);
-      w.z = pack_bf16x2(o[g * 8 + 4], o[g * 8 + 5]);
-      w.w = pack_bf16x2(o[g * 8 + 6], o[g * 8 + 7]);
-      *reinterpret_cast<uint4*>(dst + g * 8) = w;
-    }
+    for (int j = 0; j < 8; ++j) w[j] = pack_bf16x2(o[2 * j], o[2 * j + 1]);
+    store_16(dst, w);
     return;
   }
   if (e.kind == EPI_GELU) {
@@ -250,17 +273,10 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const Ge
     }
   }
   __nv_bfloat16* dst = gemm_dst(e, out, out_off, row, col0);
+  uint32_t packed[16];
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    if (col0 + g * 8 < s.n) {
-      uint4 w;
-      w.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-      w.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-      w.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-      w.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-      *reinterpret_cast<uint4*>(dst + g * 8) = w;
-    }
-  }
+  for (int j = 0; j < 16; ++j) packed[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+  store_row32(dst, packed, s.n - col0);
 }
 
 // Which norm range (0/1) holds the 128-column group starting at col, or -1.
