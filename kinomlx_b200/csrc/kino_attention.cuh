@@ -522,15 +522,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           tmem_ld32(o_col + c * 32, o);
           tmem_wait_ld();
           if (store) {
+            uint32_t w16[16];
 #pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              uint4 w;
-              w.x = pack_bf16x2(fin(o[g * 8 + 0]), fin(o[g * 8 + 1]));
-              w.y = pack_bf16x2(fin(o[g * 8 + 2]), fin(o[g * 8 + 3]));
-              w.z = pack_bf16x2(fin(o[g * 8 + 4]), fin(o[g * 8 + 5]));
-              w.w = pack_bf16x2(fin(o[g * 8 + 6]), fin(o[g * 8 + 7]));
-              *reinterpret_cast<uint4*>(dst + half * (D / 2) + c * 32 + g * 8) = w;
-            }
+            for (int j = 0; j < 16; ++j) w16[j] = pack_bf16x2(fin(o[2 * j]), fin(o[2 * j + 1]));
+            store_row32(dst + half * (D / 2) + c * 32, w16, 32);
           }
         }
       }

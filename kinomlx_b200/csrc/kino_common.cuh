@@ -339,6 +339,34 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// 16 bf16 (32 bytes) of one row: one 256-bit store where the address is 32-byte aligned (every
+// L1 -> L2 sector then arrives whole), else two 16-byte stores.
+__device__ __forceinline__ void store_16(__nv_bfloat16* dst, const uint32_t (&w)[8]) {
+  if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]),
+                 "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+                 : "memory");
+  } else {
+    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  }
+}
+
+// The first min(32, limit) of 32 packed bf16 columns of one row (limit a multiple of 8).
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (&w)[16],
+                                            int limit) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (h * 16 + 16 <= limit) {
+      const uint32_t (&part)[8] = *reinterpret_cast<const uint32_t(*)[8]>(w + h * 8);
+      store_16(dst + h * 16, part);
+    } else if (h * 16 + 8 <= limit) {
+      reinterpret_cast<uint4*>(dst + h * 16)[0] =
+          make_uint4(w[h * 8], w[h * 8 + 1], w[h * 8 + 2], w[h * 8 + 3]);
+    }
+  }
+}
+
 __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
   __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
   return __bfloat1622float2(b);

@@ -184,13 +184,13 @@ __device__ __forceinline__ void conv_store_box(const ConvShape& s, const ConvEpi
             v[g * 8 + 2 * q + 1] += fr.y;
           }
         }
-        uint4 o;
-        o.x = pack_bf16x2(v[g * 8 + 0], v[g * 8 + 1]);
-        o.y = pack_bf16x2(v[g * 8 + 2], v[g * 8 + 3]);
-        o.z = pack_bf16x2(v[g * 8 + 4], v[g * 8 + 5]);
-        o.w = pack_bf16x2(v[g * 8 + 6], v[g * 8 + 7]);
-        if (live) *reinterpret_cast<uint4*>(out + off + g * 8) = o;
       }
+    }
+    if (live) {
+      uint32_t o16[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o16[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+      store_row32(out + off, o16, s.N - n0);
     }
     if (e.stats != nullptr) {
       // the stored (bf16) values of this chunk, group by group: the warp's 32 voxels give

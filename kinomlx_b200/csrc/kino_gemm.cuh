@@ -125,34 +125,6 @@ __device__ __forceinline__ void gemm_tile_coords(const GemmShape& s, int t, int&
   mt = rem - b * s.tiles_m;
 }
 
-// 16 bf16 (32 bytes) of one row: one 256-bit store where the address is 32-byte aligned (every
-// L1 -> L2 sector then arrives whole), else two 16-byte stores.
-__device__ __forceinline__ void store_16(__nv_bfloat16* dst, const uint32_t (&w)[8]) {
-  if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
-    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]),
-                 "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
-                 : "memory");
-  } else {
-    reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-  }
-}
-
-// The first min(32, limit) of 32 packed bf16 columns of one row (limit a multiple of 8).
-__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const uint32_t (&w)[16],
-                                            int limit) {
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    if (h * 16 + 16 <= limit) {
-      const uint32_t (&part)[8] = *reinterpret_cast<const uint32_t(*)[8]>(w + h * 8);
-      store_16(dst + h * 16, part);
-    } else if (h * 16 + 8 <= limit) {
-      reinterpret_cast<uint4*>(dst + h * 16)[0] =
-          make_uint4(w[h * 8], w[h * 8 + 1], w[h * 8 + 2], w[h * 8 + 3]);
-    }
-  }
-}
-
 // Apply the epilogue to 32 consecutive columns [col0, col0 + 32) of one output row and store.
 __device__ __forceinline__ void gemm_epilogue_store(const GemmShape& s, const GemmEpi& e,
                                                     __nv_bfloat16* out, int b, int row,
@@ -347,11 +319,11 @@ __device__ __forceinline__ void gemm_epilogue_head(const GemmShape& s, const Gem
     if (!live) continue;
     const float* cs = e.rope_cos + trow + static_cast<int64_t>(c * 32) * tstride;
     const float* sn = e.rope_sin + trow + static_cast<int64_t>(c * 32) * tstride;
+    uint32_t o16[16];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const uint4 raw = *reinterpret_cast<const uint4*>(w + c * 32 + g * 8);
       const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-      uint32_t o4[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int j = g * 8 + 2 * q;
@@ -360,11 +332,11 @@ __device__ __forceinline__ void gemm_epilogue_head(const GemmShape& s, const Gem
         const float x1 = bf16_round(v[j + 1] * inv * t.y);
         const float c0 = __ldg(cs + j * tstride), c1 = __ldg(cs + (j + 1) * tstride);
         const float s0 = __ldg(sn + j * tstride), s1 = __ldg(sn + (j + 1) * tstride);
-        o4[q] = pack_bf16x2(__fadd_rn(__fmul_rn(x0, c0), __fmul_rn(-x1, s0)),
-                            __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1)));
+        o16[g * 4 + q] = pack_bf16x2(__fadd_rn(__fmul_rn(x0, c0), __fmul_rn(-x1, s0)),
+                                     __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(x0, s1)));
       }
-      *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
     }
+    store_row32(dst + c * 32, o16, 32);
   }
 }
 
