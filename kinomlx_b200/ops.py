@@ -400,21 +400,35 @@ def _split_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     return ws
 
 
+# Wave model of the key split, in units of one 128-key block of a CTA: a CTA costs its blocks
+# plus a fixed set-up and epilogue; a split call adds the merge of the shares.
+_SPLIT_CTA_OVERHEAD = 4
+_SPLIT_MERGE_COST = 3
+
+
 def attention_splits(args, device: torch.device) -> int:
-    """Key shares for an attention call: 1 when its CTAs (two 128-query tiles each) fill two
-    waves of the SMs, else enough shares for about two waves, at most 4 and at most one per key
-    block. Attention over few query tiles (sequence-parallel ranks, small batches) otherwise
-    leaves most SMs idle."""
+    """Key shares for an attention call (1 to 4, at most one per key block): the count whose
+    waves of CTAs (two 128-query tiles each, `kv_splits` per tile pair) finish first, counting
+    each wave as its CTAs' blocks plus a fixed per-CTA cost and a split call's merge. Attention
+    over few query tiles (sequence-parallel ranks, small batches) otherwise leaves SMs idle,
+    while a call that already fills the SMs once (config 4's 4 heads x 9216 tokens per rank at 8
+    GPUs: 144 CTAs on 148 SMs) only pays for splitting."""
     index = device.index if device.index is not None else torch.cuda.current_device()
     if index not in _SM_COUNTS:
         _SM_COUNTS[index] = torch.cuda.get_device_properties(index).multi_processor_count
     sms = _SM_COUNTS[index]
     tiles = sum((int(args.q_tokens[i]) + 127) // 128 for i in range(args.n_q))
     ctas = (tiles + 1) // 2 * int(args.heads) * int(args.batch)
-    if ctas >= 2 * sms:
-        return 1
     blocks = sum((int(args.kv_tokens[i]) + 127) // 128 for i in range(args.n_kv))
-    return max(1, min(4, blocks, -(-2 * sms // ctas)))
+    best, best_cost = 1, None
+    for splits in range(1, max(1, min(4, blocks)) + 1):
+        waves = -(-ctas * splits // sms)
+        cost = waves * (-(-blocks // splits) + _SPLIT_CTA_OVERHEAD)
+        if splits > 1:
+            cost += _SPLIT_MERGE_COST
+        if best_cost is None or cost < best_cost:
+            best, best_cost = splits, cost
+    return best
 
 
 def attention(

@@ -122,6 +122,7 @@ class SequenceParallel:
                              ld_gate=0 if gate is None else gate[1],
                              gate_head_offset=self.rank * (heads // p))
         # H / P heads of the whole sequence: few query tiles, so the keys are split among CTAs
+        # where that finishes sooner (ops.attention_splits)
         ops.attention([q], [k], [v], [q], heads=heads // p, peer_return=ret, kv_splits="auto")
         self.peer.barrier()
 
