@@ -156,3 +156,26 @@ def test_block_entry_workspace_sizes():
     expect = (a(9216 * d * 2) + a(9216 * 16384 * 2) + a(9216 * 3 * d * 2) + a(9216 * 32 * 2)
               + a(256 * d * 2) + a(256 * 2 * d * 2))
     assert lib.kino_ltx_video_block_workspace_size(ctypes.byref(t)) == expect
+
+
+def test_attention_key_split_policy():
+    """The wave model of ops.attention_splits on a 148-SM B200: calls that fill the SMs once stay
+    whole (config 4's per-rank 4 heads x 9216 at 8 GPUs), calls over few tiles split (config 2's
+    per-rank 12 heads at 2 GPUs and 3 heads at 8 GPUs), never beyond the key blocks."""
+    from types import SimpleNamespace
+
+    from kinomlx_b200 import ops
+
+    ops._SM_COUNTS[0] = 148
+    dev = torch.device("cuda", 0)
+
+    def splits(tokens, heads, keys=None, batch=1):
+        args = SimpleNamespace(q_tokens=[tokens], n_q=1, heads=heads, batch=batch,
+                               kv_tokens=[keys or tokens], n_kv=1)
+        return ops.attention_splits(args, dev)
+
+    assert splits(4608, 24) == 1 and splits(9216, 32) == 1
+    assert splits(9216, 4) == 1 and splits(9216, 8) == 1 and splits(9216, 16) == 1
+    assert splits(4608, 12) == 2 and splits(4608, 3) == 2
+    assert splits(128, 1, keys=256) <= 2  # at most one share per key block
+    assert splits(256, 1, keys=128) == 1
