@@ -55,6 +55,7 @@ __all__ = [
     "blend_normalize",
     "cfg_combine",
     "conv3d",
+    "copy_view",
     "device_status",
     "euler_denoised",
     "euler_velocity",
@@ -65,6 +66,8 @@ __all__ = [
     "group_norm",
     "latent_to_bfhwc",
     "linear",
+    "na_qkv_prepare",
+    "neighborhood_attention",
     "pixel_norm",
     "RopeTables",
     "qk_norm_rope",
