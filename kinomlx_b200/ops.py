@@ -612,6 +612,22 @@ def na_qkv_prepare(qkv: torch.Tensor, q_norm_weight: torch.Tensor, k_norm_weight
 _COPY_TYPES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 
 
+def _copy_dims(shape, src_strides, dst_strides) -> list[list[int]]:
+    """[size, source stride, destination stride] per dimension of a copy, outermost first, with
+    size-1 dimensions dropped and neighbours that are contiguous on both sides merged (so most
+    layout moves stay within the kernel's 8 dimensions)."""
+    merged: list[list[int]] = []
+    for n, a, b in zip(shape, src_strides, dst_strides):
+        n, a, b = int(n), int(a), int(b)
+        if n == 1:
+            continue
+        if merged and merged[-1][1] == a * n and merged[-1][2] == b * n:
+            merged[-1] = [merged[-1][0] * n, a, b]
+        else:
+            merged.append([n, a, b])
+    return merged or [[1, 0, 0]]
+
+
 def copy_view(src: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
     """dst[...] = src[...] for two same-shaped device views of any strides (a zero source stride
     broadcasts) and dtypes bf16 / fp16 / fp32, in one `kino_strided_copy` launch: permutations,
@@ -622,17 +638,7 @@ def copy_view(src: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
         raise ValueError("copy_view takes bf16, fp16 or fp32 tensors")
     if src.device != dst.device or src.device.type != "cuda":
         raise ValueError("copy_view runs on one CUDA device")
-    dims = [(int(n), int(a), int(b)) for n, a, b in zip(src.shape, src.stride(), dst.stride())
-            if n != 1]
-    # merge neighbours that are contiguous in both views, so most copies stay within 8 dims
-    merged: list[list[int]] = []
-    for n, a, b in dims:
-        if merged and merged[-1][1] == a * n and merged[-1][2] == b * n:
-            merged[-1] = [merged[-1][0] * n, a, b]
-        else:
-            merged.append([n, a, b])
-    if not merged:
-        merged = [[1, 0, 0]]
+    merged = _copy_dims(src.shape, src.stride(), dst.stride())
     if len(merged) > 8:
         raise ValueError(f"copy_view supports up to 8 non-mergeable dimensions, got {len(merged)}")
     nd = len(merged)

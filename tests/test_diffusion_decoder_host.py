@@ -86,3 +86,33 @@ def test_rope3d_rotates_each_section_by_its_axis():
     assert not torch.equal(y[0, 0, 1, 1, 0, 16:], x[0, 0, 1, 1, 0, 16:])
     assert not torch.equal(y[0, 2, 0, 0, 0, :16], x[0, 2, 0, 0, 0, :16])
     assert torch.equal(y[0, 2, 0, 0, 0, 16:], x[0, 2, 0, 0, 0, 16:])
+
+
+def test_copy_dims_merge_and_order():
+    """The strided copy's host-side dimension list (ops._copy_dims): contiguous runs merge on
+    both sides, size-1 dimensions vanish, broadcasts keep a zero source stride, and applying the
+    list element by element reproduces the permuted copy."""
+    from kinomlx_b200.ops import _copy_dims
+
+    x = torch.arange(2 * 3 * 4 * 5).reshape(2, 3, 4, 5)
+    assert _copy_dims(x.shape, x.stride(), x.stride()) == [[120, 1, 1]]
+    p = x.permute(0, 2, 1, 3)  # (2, 4, 3, 5) view
+    out = torch.empty(p.shape, dtype=x.dtype)
+    dims = _copy_dims(p.shape, p.stride(), out.stride())
+    assert dims == [[2, 60, 60], [4, 5, 15], [3, 20, 5], [5, 1, 1]]
+    flat_src, flat_dst = x.reshape(-1), out.reshape(-1)
+    sizes = [d[0] for d in dims]
+    for e in range(p.numel()):
+        rest, so, do = e, 0, 0
+        for (n, a, b) in reversed(dims):
+            c = rest % n
+            rest //= n
+            so += c * a
+            do += c * b
+        flat_dst[do] = flat_src[so]
+    assert torch.equal(out, p.contiguous()) and sizes == [2, 4, 3, 5]
+    row = x[1:2, :, 2:3].expand(2, 3, 4, 5)  # a broadcast along two axes
+    dst = torch.empty(row.shape, dtype=x.dtype)
+    assert _copy_dims(row.shape, row.stride(), dst.stride()) == [[2, 0, 60], [3, 20, 20],
+                                                                  [4, 0, 5], [5, 1, 1]]
+    assert _copy_dims((1, 1), (0, 0), (1, 1)) == [[1, 0, 0]]
