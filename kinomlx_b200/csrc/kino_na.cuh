@@ -433,18 +433,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           const int64_t tok = ((static_cast<int64_t>(m.b) * p.frames + qt[t]) * p.height + qh) *
                                   p.width + qw;
           __half* dst = p.out + (tok * p.heads + m.head) * D + half * (D / 2);
+          uint32_t w16[16];
 #pragma unroll
-          for (int g4 = 0; g4 < 4; ++g4) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int c = g4 * 8 + 2 * e;
-              const float o0 = __uint_as_float(ov[c]) * inv_l;
-              const float o1 = __uint_as_float(ov[c + 1]) * inv_l;
-              w4[e] = p.out_bf16 ? pack_bf16x2(o0, o1) : pack_f16x2(o0, o1);
-            }
-            reinterpret_cast<uint4*>(dst)[g4] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+          for (int e = 0; e < 16; ++e) {
+            const float o0 = __uint_as_float(ov[2 * e]) * inv_l;
+            const float o1 = __uint_as_float(ov[2 * e + 1]) * inv_l;
+            w16[e] = p.out_bf16 ? pack_bf16x2(o0, o1) : pack_f16x2(o0, o1);
           }
+          store_row32(reinterpret_cast<__nv_bfloat16*>(dst), w16, 32);
         }
       }
     }

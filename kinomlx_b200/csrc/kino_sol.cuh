@@ -794,22 +794,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (store) {
           uint8_t* base = static_cast<uint8_t*>(p.out) +
                           (dst_row * p.ld_out + head * D + half * (D / 2) + c * 32) * 2;
+          uint32_t w16[16];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 w;
-            if (p.out_f16) {
-              w.x = pack_f16x2(fin(oa[g * 8 + 0], ob[g * 8 + 0]), fin(oa[g * 8 + 1], ob[g * 8 + 1]));
-              w.y = pack_f16x2(fin(oa[g * 8 + 2], ob[g * 8 + 2]), fin(oa[g * 8 + 3], ob[g * 8 + 3]));
-              w.z = pack_f16x2(fin(oa[g * 8 + 4], ob[g * 8 + 4]), fin(oa[g * 8 + 5], ob[g * 8 + 5]));
-              w.w = pack_f16x2(fin(oa[g * 8 + 6], ob[g * 8 + 6]), fin(oa[g * 8 + 7], ob[g * 8 + 7]));
-            } else {
-              w.x = pack_bf16x2(fin(oa[g * 8 + 0], ob[g * 8 + 0]), fin(oa[g * 8 + 1], ob[g * 8 + 1]));
-              w.y = pack_bf16x2(fin(oa[g * 8 + 2], ob[g * 8 + 2]), fin(oa[g * 8 + 3], ob[g * 8 + 3]));
-              w.z = pack_bf16x2(fin(oa[g * 8 + 4], ob[g * 8 + 4]), fin(oa[g * 8 + 5], ob[g * 8 + 5]));
-              w.w = pack_bf16x2(fin(oa[g * 8 + 6], ob[g * 8 + 6]), fin(oa[g * 8 + 7], ob[g * 8 + 7]));
-            }
-            *reinterpret_cast<uint4*>(base + g * 16) = w;
+          for (int e = 0; e < 16; ++e) {
+            const float o0 = fin(oa[2 * e], ob[2 * e]), o1 = fin(oa[2 * e + 1], ob[2 * e + 1]);
+            w16[e] = p.out_f16 ? pack_f16x2(o0, o1) : pack_bf16x2(o0, o1);
           }
+          store_row32(reinterpret_cast<__nv_bfloat16*>(base), w16, 32);
         }
       }
     }
