@@ -387,12 +387,15 @@ bool gemm_pairs_enabled() {
 // 3 = one SM with 128 x 128 tiles. The persistent kernels run ceil(tiles / slots) waves of
 // equal-length tiles, so the estimate is waves x tile time, the tile time relative to the
 // CTA-pair kernel's per-SM share (128 x 256) with the single-SM kernels' measured throughput
-// ratios (per mille).
+// ratios (per mille). The 128 x 128 ratio comes from the small-row products of the
+// sequence-parallel ranks (576 and 1152 rows, K = 3072 to 15360, each tiling timed): at 770 the
+// estimate picks the fastest tiling for all twelve shapes timed (at 860 it gave 1152 x 9216 to
+// the 128 x 128 tiles, 60.7 us, against the pairs' 56.0).
 #ifndef KINO_GEMM_E1
 #define KINO_GEMM_E1 930
 #endif
 #ifndef KINO_GEMM_E1B
-#define KINO_GEMM_E1B 860
+#define KINO_GEMM_E1B 770
 #endif
 #ifndef KINO_GEMM_FORCE
 #define KINO_GEMM_FORCE 0
