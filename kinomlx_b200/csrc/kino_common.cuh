@@ -399,6 +399,28 @@ __device__ __forceinline__ float gelu_tanh_f32(float x) {
 // formula's (the standalone op and the VAE norms, which are bandwidth-bound anyway).
 __device__ __forceinline__ float silu_f32(float x) { return x / (1.0f + expf(-x)); }
 
+// bf16(fp32(a / b)) without a division on most elements: q = a * r, r within 1 ulp of 1 / b, is
+// within 3 fp32 ulps of the correctly rounded quotient, and rounding fp32 to bf16 (to nearest,
+// ties to even) only depends on which side of the half-way pattern 0x8000 the low 16 bits fall
+// (a carry past 0xFFFF rounds the same way on both sides). So q rounds like the exact quotient
+// unless its low half lies within `window` of 0x8000; those elements (about 1 in 4000 for a
+// window of 8) take the IEEE division.
+__device__ __forceinline__ float div_round_bf16(float a, float b, float r, uint32_t window) {
+  const float q = a * r;
+  const uint32_t low = __float_as_uint(q) & 0xFFFFu;
+  if (low - (0x8000u - window) <= 2u * window) return bf16_round(__fdiv_rn(a, b));
+  return bf16_round(q);
+}
+
+// bf16(x / (1 + exp(-x))) with the fp32 exponential and quotient of silu_f32, rounded once, the
+// quotient through div_round_bf16.
+__device__ __forceinline__ float silu_round_bf16(float x) {
+  const float d = 1.0f + expf(-x);
+  float r;
+  asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return div_round_bf16(x, d, r, 8u);
+}
+
 // SiLU for GEMM epilogues: x * rcp(1 + 2^(-x log2 e)) on the special-function unit.
 __device__ __forceinline__ float silu_fast_f32(float x) {
   return x * rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * x));

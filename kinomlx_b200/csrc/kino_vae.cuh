@@ -35,6 +35,7 @@ __global__ void pixel_norm_silu_kernel(const __nv_bfloat16* __restrict__ x,
   const float mean = bf16_round(s / static_cast<float>(C));
   const float shifted = bf16_round(mean + eps);
   const float rms = bf16_round(sqrtf(shifted));
+  const float rrms = __frcp_rn(rms);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int c = lane + i * 32;
@@ -42,8 +43,8 @@ __global__ void pixel_norm_silu_kernel(const __nv_bfloat16* __restrict__ x,
       float o[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float y = bf16_round(__fdiv_rn(v[i][j], rms));
-        o[j] = apply_silu ? silu_f32(y) : y;
+        const float y = div_round_bf16(v[i][j], rms, rrms, 4u);
+        o[j] = apply_silu ? silu_round_bf16(y) : y;
       }
       store8(orow + c * 8, o);
     }
@@ -88,14 +89,15 @@ __global__ void __launch_bounds__(256)
   const float mean = bf16_round(s / static_cast<float>(C));
   const float shifted = bf16_round(mean + eps);
   const float rms = bf16_round(sqrtf(shifted));
+  const float rrms = __frcp_rn(rms);
   __nv_bfloat16* orow = out + voxel * C;
 #pragma unroll
   for (int k = 0; k < K; ++k) {
     float o[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float y = bf16_round(__fdiv_rn(v[k][j], rms));
-      o[j] = apply_silu ? silu_f32(y) : y;
+      const float y = div_round_bf16(v[k][j], rms, rrms, 4u);
+      o[j] = apply_silu ? silu_round_bf16(y) : y;
     }
     store8(orow + (k * T + sub) * 8, o);
   }
