@@ -116,3 +116,28 @@ def test_copy_dims_merge_and_order():
     assert _copy_dims(row.shape, row.stride(), dst.stride()) == [[2, 0, 60], [3, 20, 20],
                                                                   [4, 0, 5], [5, 1, 1]]
     assert _copy_dims((1, 1), (0, 0), (1, 1)) == [[1, 0, 0]]
+
+
+@pytest.mark.parametrize("latent_shape", [(1, 8, 1, 1, 1), (2, 8, 3, 2, 4), (1, 8, 4, 5, 3)])
+def test_working_shape_matches_the_oracle_decode(latent_shape):
+    """x_t's working shape for latents that need no, some and all of the padding: the oracle
+    decodes them and crops to (B, 3, 1 + (F - 1) * 8, H * 16, W * 16)."""
+    cfg = mini_config()
+    w = diffusion_decoder_weights(cfg, seed=5)
+    latent = normal(latent_shape, seed=6, dtype=torch.float32)
+    noise = normal(cfg.working_pixel_shape(latent_shape), seed=7)
+    out = dref.decode(latent, noise, w, cfg)
+    b, _, f, h, wd = latent_shape
+    assert tuple(out.shape) == (b, 3, 1 + (f - 1) * 8, h * 16, wd * 16)
+
+
+def test_copy_view_refusals():
+    from kinomlx_b200 import ops
+
+    a = torch.zeros((2, 3), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="shapes differ"):
+        ops.copy_view(a, torch.zeros((3, 2), dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="bf16, fp16 or fp32"):
+        ops.copy_view(a.to(torch.int32), torch.zeros((2, 3), dtype=torch.int32))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.copy_view(a, torch.zeros((2, 3), dtype=torch.float16))
